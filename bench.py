@@ -1,0 +1,378 @@
+"""Benchmark of the W4A8 decode step on B200 (driver contract: one JSON line from rank 0).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload gemv]
+
+Workload `gemv` (the W4A8 GEMV HBM GB/s part of the metric): one step is a batch
+of 64 verify-row linears (M = 8 tree rows, bf16 x [8, 4096] -> per-token int8 quant -> GPTQ W4A8 GEMV
+4096 -> 12288 -> bf16 [8, 12288]) that cycle through 8 distinct weight copies (208 MB, more than the 126 MB
+L2, so every linear streams its weights from HBM). value = algorithmic bytes / device time (CUDA graph
+replay of the K steps, CUDA events, max over ranks). e2e = the same through the public op calls
+(mono_b200._C) with pinned host inputs copied in and outputs read back every linear.
+
+Multi-GPU: every rank runs its own replica (independent decode streams, no collective): scaling "weak".
+--impl reference: the reference's arithmetic on the host cores (the CPU oracle restatement; the reference
+itself is SYCL for Intel GPUs and cannot run here), on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "comfy-mono-decode-xpu_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "decode tok/s (1 stream, 1 B200) + aggregate tok/s at 2/4/8; W4A8 GEMV HBM GB/s"
+N_OUT, K_IN, M_ROWS = 12288, 4096, 8
+COPIES, PER_STEP = 8, 64
+L2_BYTES = 126 * 2 ** 20
+
+
+def gemv_bytes(M, N, K, x_bf16=True):
+    """Algorithmic HBM bytes of one W4A8 linear: int4 weights + fp16 scales + activation in + bf16 out."""
+    return N * K // 2 + N * (K // 128) * 2 + M * K * (2 if x_bf16 else 1) + M * N * 2 + (0 if x_bf16 else M * 4)
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profile_traffic(name):
+    """Per-launch DRAM bytes of a kernel from its committed ncu summary (profiles/<name>.md line
+    `traffic_bytes_per_launch: N`), or None."""
+    path = os.path.join(ROOT, "profiles", name + ".md")
+    try:
+        for line in open(path):
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1].strip().split()[0]))
+    except Exception:
+        pass
+    return None
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.proc, self.lines = index, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        for l in self.lines:
+            f = [x.strip() for x in l.split(",")]
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except Exception:
+                continue
+            for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(n):
+    rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    if world != n and n > 1 and "RANK" not in os.environ:
+        raise SystemExit("bench.py --gpus N>1 must run under torch.distributed.run (one rank per GPU)")
+    return rank, world, int(os.environ.get("LOCAL_RANK", 0))
+
+
+# ---- our implementation ---------------------------------------------------------------------------------
+
+def run_ours(args):
+    import datetime
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from mono_b200 import _C
+    from oracle import w4a8 as ow  # seeded weight generator + the cpu_baseline leg (test infrastructure)
+
+    rank, world, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    # weights: 8 distinct copies (tile-major), seeded like BASELINE configs[0]
+    packed, scales = ow.gen_gptq(N_OUT, K_IN, seed=0x5EED + 0)
+    pk0, sc0 = torch.from_numpy(packed).to(dev), torch.from_numpy(scales).to(dev)
+    ws = []
+    for c in range(COPIES):
+        # distinct bytes per copy (flip the low nibble of every byte of copy c when c is odd): same shapes
+        pk = pk0 ^ c if c else pk0.clone()
+        qt, st = _C.w4_repack(0, pk.contiguous(), sc0, N_OUT, K_IN)
+        ws.append((qt, st))
+    assert COPIES * ws[0][0].numel() > L2_BYTES
+    g = torch.Generator().manual_seed(0x5EED + rank)
+    xs_host = [torch.randn(M_ROWS, K_IN, generator=g).to(torch.bfloat16) for _ in range(COPIES)]
+    xs_dev = [x.to(dev) for x in xs_host]
+    outs = [torch.empty(M_ROWS, N_OUT, dtype=torch.bfloat16, device=dev) for _ in range(COPIES)]
+
+    stream = torch.cuda.Stream(dev)
+
+    def linear(i):
+        c = i % COPIES
+        xq, s = _C.act_quant(xs_dev[c])
+        return _C.w4a8_gptq_linear(xq, s.view(-1), ws[c][0], ws[c][1], tiled=True)
+
+    def step():
+        for i in range(PER_STEP):
+            linear(i)
+
+    def gemv_only(i, xq, s):
+        c = i % COPIES
+        return _C.w4a8_gptq_linear(xq, s, ws[c][0], ws[c][1], tiled=True)
+
+    # correctness gate on this box: one linear against the oracle
+    with torch.cuda.stream(stream):
+        out0 = linear(0)
+    stream.synchronize()
+    rq, rs = ow.act_quant(xs_host[0].view(torch.int16).numpy().view(np.uint16))
+    ok = np.array_equal(out0.cpu().view(torch.int16).numpy().view(np.uint16), ow.gptq_linear(rq, rs, packed, scales))
+
+    # capture K steps into one CUDA graph (warm-up replays first)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            step()
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with Clocks(local) as clk:
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(stream)
+        stream.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    step_bytes = PER_STEP * gemv_bytes(M_ROWS, N_OUT, K_IN)
+    value = world * args.steps * step_bytes / (ms * 1e-3) / 1e9
+
+    # the dominant kernel alone: a graph of GEMV launches (same rotating weights), averaged per launch
+    with torch.cuda.stream(stream):
+        xq_s, s_s = _C.act_quant(xs_dev[0])
+        s_s = s_s.view(-1)
+        for i in range(3):
+            gemv_only(i, xq_s, s_s)
+    stream.synchronize()
+    g2 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g2, stream=stream):
+        for i in range(PER_STEP):
+            gemv_only(i, xq_s, s_s)
+    for _ in range(3):
+        g2.replay()
+    torch.cuda.synchronize()
+    reps = max(20, args.steps // 4)
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        k0.record(stream)
+        for _ in range(reps):
+            g2.replay()
+        k1.record(stream)
+    stream.synchronize()
+    kern_us = k0.elapsed_time(k1) * 1e3 / (reps * PER_STEP)
+    kbytes = gemv_bytes(M_ROWS, N_OUT, K_IN, x_bf16=False)
+    hbm, src = peaks()
+    achieved = kbytes / (kern_us * 1e-6) / 1e9
+
+    # e2e through the public op calls with host buffers (pinned), per linear: H2D x, quant, GEMV, D2H out
+    host_x = [x.pin_memory() for x in xs_host]
+    host_o = torch.empty(M_ROWS, N_OUT, dtype=torch.bfloat16).pin_memory()
+    e2e_linears = max(PER_STEP, args.steps * PER_STEP // 50)
+
+    def e2e_once(i):
+        c = i % COPIES
+        xd = host_x[c].to(dev, non_blocking=True)
+        xq, s = _C.act_quant(xd)
+        o = _C.w4a8_gptq_linear(xq, s.view(-1), ws[c][0], ws[c][1], tiled=True)
+        host_o.copy_(o, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for i in range(8):
+            e2e_once(i)
+    stream.synchronize()
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        f0.record(stream)
+        for i in range(e2e_linears):
+            e2e_once(i)
+        f1.record(stream)
+    stream.synchronize()
+    e2e_ms = f0.elapsed_time(f1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * e2e_linears * gemv_bytes(M_ROWS, N_OUT, K_IN) / (e2e_ms * 1e-3) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(ow, packed, scales)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 1),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "int8",
+            "data": "synthetic (seeded, BASELINE configs[0] distributions)",
+            "config": {"workload": "W4A8 GPTQ verify linear 4096->12288, M=8 rows (configs[0])",
+                       "linears_per_step": PER_STEP, "weight_copies": COPIES,
+                       "l2": "inputs larger than L2 (8 weight copies = 208 MB cycled)", "parallelism": f"replicas x{world}",
+                       "layout": "tile-major (mono_w4_repack)", "parity_gate": bool(ok)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(achieved / hbm, 4), "peak_source": src,
+                         "traffic": profile_traffic("w4a8_gemv_gptq_m8_4096x12288"),
+                         "kernel": "w4a8_gemv_kernel<GPTQ,TILED,1>", "us_per_launch": round(kern_us, 3),
+                         "algorithmic_bytes_per_launch": kbytes},
+            "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": PER_STEP * M_ROWS * K_IN * 2,
+                    "d2h_bytes_per_step": PER_STEP * M_ROWS * N_OUT * 2},
+            "gpu_launches": args.steps * PER_STEP * 2,
+            "clocks": clk.summary(),
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_baseline(ow, packed, scales, rows=None):
+    """The oracle's eager chain (act quant + GPTQ linear) on the host cores, on a bounded sample."""
+    import numpy as np
+    import torch
+    torch.set_num_threads(os.cpu_count() or 1)
+    rows = rows or N_OUT // 4
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(M_ROWS, K_IN, generator=g).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    times = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        q, s = ow.act_quant(x)
+        ow.gptq_linear(q, s, packed[:rows], scales[:rows])
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": round(gemv_bytes(M_ROWS, rows, K_IN) / t / 1e9, 3), "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"one act-quant + GPTQ linear, {rows} of {N_OUT} output rows, M=8, K=4096; "
+                                      f"median of 3 ({t:.2f} s)"}
+
+
+def run_reference(args):
+    rank, world, _ = dist_setup(args.gpus)
+    if rank != 0:
+        return
+    from oracle import w4a8 as ow
+    packed, scales = ow.gen_gptq(N_OUT, K_IN, seed=0x5EED)
+    rows = 1024
+    import numpy as np
+    import torch
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(M_ROWS, K_IN, generator=g).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+
+    def step():
+        q, s = ow.act_quant(x)
+        ow.gptq_linear(q, s, packed[:rows], scales[:rows])
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    t = time.perf_counter() - t0
+    value = args.steps * gemv_bytes(M_ROWS, rows, K_IN) / t / 1e9
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3 / args.steps, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (seeded, BASELINE configs[0] distributions)",
+            "config": {"workload": "W4A8 GPTQ verify linear 4096->12288, M=8 rows (configs[0])"},
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": f"per step one act-quant + GPTQ linear over {rows} of {N_OUT} output rows"},
+            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="gemv", choices=["gemv"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,152 @@
+// extern "C" entry points: host-side validation, then the launchers.
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "abi_internal.h"
+#include "w4a8_gemv.cuh"
+
+namespace mono {
+
+namespace {
+thread_local std::string g_last_error;
+}
+
+int fail(int code, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int sm_count() {
+    static int counts[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (counts[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        counts[dev] = n;
+    }
+    return counts[dev];
+}
+
+int launch_gemv(int fmt, int layout, const GemvParams& p, cudaStream_t stream);
+int launch_repack(int fmt, const void* q, const void* s, int N, int K, void* qt, void* st, cudaStream_t stream);
+int launch_pair_table(const float* codebook, uint16_t* tab, cudaStream_t stream);
+int launch_act_quant(const void* x, int M, int K, int8_t* q, float* xs, cudaStream_t stream);
+size_t rot_quant_workspace(int M, int K);
+int launch_rot_quant(const void* x, const void* h, int M, int K, int8_t* q, float* s, void* ws, cudaStream_t stream);
+
+static int check_linear_common(const int8_t* x, const float* xs, const void* packed, const void* scales,
+                               const void* out, int64_t M, int64_t N, int64_t K, int out_dtype_code, int layout) {
+    MONO_CHECK(x && xs && packed && scales && out, "null operand");
+    MONO_CHECK(M >= 1 && M <= 16, "1 <= M <= 16 (got %lld)", (long long)M);
+    MONO_CHECK(K >= kChunkK && K % kChunkK == 0 && K <= kChunkK * kMaxChunks, "K must be a multiple of 1024 in [1024, 16384] (got %lld)",
+               (long long)K);
+    MONO_CHECK(N >= 16 && N % 16 == 0 && N <= (1 << 24), "N must be a positive multiple of 16 (got %lld)", (long long)N);
+    MONO_CHECK(out_dtype_code == MONO_OUT_F32 || out_dtype_code == MONO_OUT_BF16, "out dtype fp32 (0) or bf16 (2)");
+    MONO_CHECK(layout == MONO_LAYOUT_ROW || layout == MONO_LAYOUT_TILED, "layout ROW (0) or TILED (1)");
+    MONO_CHECK(aligned(x, 16), "x must be 16-byte aligned");
+    MONO_CHECK(aligned(packed, 16), "packed weights must be 16-byte aligned");
+    MONO_CHECK(aligned(scales, 16), "scales must be 16-byte aligned");
+    return MONO_OK;
+}
+
+}  // namespace mono
+
+using namespace mono;
+
+extern "C" {
+
+const char* mono_last_error(void) { return g_last_error.c_str(); }
+
+int mono_abi_version(void) { return 1; }
+
+int mono_device_status(int* code, int reset) {
+    int v = 0;
+    CUDA_TRY(cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)));
+    if (code) *code = v;
+    if (reset && v) {
+        const int zero = 0;
+        CUDA_TRY(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)));
+    }
+    return v ? fail(MONO_EDEVICE, "device error word = %d", v) : MONO_OK;
+}
+
+int mono_w4a8_decode_linear(const int8_t* x, const float* x_scale, const void* packed, const void* s_rel,
+                            int s_rel_dtype, const float* s_channel, const uint16_t* pair_table,
+                            const void* residual, int64_t M, int64_t N, int64_t K, int64_t group_size,
+                            int out_dtype_code, int layout, void* out, mono_stream_t stream) {
+    int rc = check_linear_common(x, x_scale, packed, s_rel, out, M, N, K, out_dtype_code, layout);
+    if (rc) return rc;
+    MONO_CHECK(group_size == 16, "group_size must be 16 (G16 FP8 relative scales)");
+    MONO_CHECK(s_rel_dtype == MONO_SCALE_FP8_E4M3, "s_rel must be FP8 e4m3");
+    MONO_CHECK(s_channel && pair_table, "s_channel and pair_table are required");
+    GemvParams p{};
+    p.q = static_cast<const uint8_t*>(packed);
+    p.scales = static_cast<const uint8_t*>(s_rel);
+    p.s_channel = s_channel;
+    p.pair_tab = pair_table;
+    p.x = x;
+    p.xs = x_scale;
+    p.residual = residual;
+    p.out = out;
+    p.M = int(M); p.N = int(N); p.K = int(K);
+    p.out_bf16 = out_dtype_code == MONO_OUT_BF16;
+    return launch_gemv(FMT_REF, layout, p, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int mono_w4_pair_table(const float* codebook, uint16_t* table, mono_stream_t stream) {
+    MONO_CHECK(table, "null table");
+    return launch_pair_table(codebook, table, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int mono_w4a8_gptq_linear(const int8_t* x, const float* x_scale, const void* packed, const void* scales,
+                          const void* residual, int64_t M, int64_t N, int64_t K, int out_dtype_code, int layout,
+                          void* out, mono_stream_t stream) {
+    int rc = check_linear_common(x, x_scale, packed, scales, out, M, N, K, out_dtype_code, layout);
+    if (rc) return rc;
+    GemvParams p{};
+    p.q = static_cast<const uint8_t*>(packed);
+    p.scales = static_cast<const uint8_t*>(scales);
+    p.x = x;
+    p.xs = x_scale;
+    p.residual = residual;
+    p.out = out;
+    p.M = int(M); p.N = int(N); p.K = int(K);
+    p.out_bf16 = out_dtype_code == MONO_OUT_BF16;
+    return launch_gemv(FMT_GPTQ, layout, p, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int mono_w4_repack(int fmt, const void* packed, const void* scales, int64_t N, int64_t K, void* packed_tiled,
+                   void* scales_tiled, mono_stream_t stream) {
+    MONO_CHECK(fmt == MONO_FMT_GPTQ || fmt == MONO_FMT_REF, "fmt GPTQ (0) or REF (1)");
+    MONO_CHECK(packed && scales && packed_tiled && scales_tiled, "null operand");
+    MONO_CHECK(N >= 16 && N % 16 == 0 && K >= 256 && K % 256 == 0, "N % 16 == 0 and K % 256 == 0");
+    MONO_CHECK(aligned(packed, 16) && aligned(packed_tiled, 16), "weights must be 16-byte aligned");
+    return launch_repack(fmt, packed, scales, int(N), int(K), packed_tiled, scales_tiled,
+                         reinterpret_cast<cudaStream_t>(stream));
+}
+
+int mono_act_quant(const void* x_bf16, int64_t M, int64_t K, int8_t* q, float* scale, mono_stream_t stream) {
+    MONO_CHECK(x_bf16 && q && scale, "null operand");
+    MONO_CHECK(M >= 1 && M <= 65535 && K >= 8 && K % 8 == 0, "M in [1, 65535], K % 8 == 0");
+    MONO_CHECK(aligned(x_bf16, 16) && aligned(q, 8), "x must be 16-byte and q 8-byte aligned");
+    return launch_act_quant(x_bf16, int(M), int(K), q, scale, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t mono_rot_quant_workspace(int64_t M, int64_t K) { return rot_quant_workspace(int(M), int(K)); }
+
+int mono_rot_quant(const void* x_bf16, const void* h_bf16, int64_t M, int64_t K, int8_t* q, float* scale,
+                   void* workspace, mono_stream_t stream) {
+    MONO_CHECK(x_bf16 && h_bf16 && q && scale && workspace, "null operand");
+    MONO_CHECK(M >= 1 && M <= 65535 && K >= 256 && K % 256 == 0, "M in [1, 65535], K % 256 == 0");
+    MONO_CHECK(aligned(workspace, 16), "workspace must be 16-byte aligned");
+    return launch_rot_quant(x_bf16, h_bf16, int(M), int(K), q, scale, workspace, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,168 @@
+"""The reference's native op surface (comfy_mono_decode_xpu._C, csrc/bindings.cpp:70-104) over torch CUDA
+tensors, implemented by the C ABI of libmono_b200.so.
+
+Same op names, argument order and meaning; outputs are allocated here with torch (the C ABI never
+allocates) and every call is enqueued on torch's current CUDA stream. Argument errors raise RuntimeError
+before anything is launched, as the reference's TORCH_CHECKs do.
+"""
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from . import _lib
+
+_tables = {}
+_tables_lock = threading.Lock()
+
+
+def _check(cond, msg):
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _cuda(*ts):
+    for t in ts:
+        _check(t is not None and t.is_cuda, "operands must be CUDA tensors")
+    dev = ts[0].device
+    for t in ts:
+        _check(t.device == dev, "operands must be on one device")
+
+
+def _stream(dev):
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def pair_table(codebook, device):
+    """REF decode table for `codebook` (None = float(i - 8)), cached per (device, storage, version)."""
+    dev = torch.device(device)
+    key = (dev, None) if codebook is None else (dev, codebook.data_ptr(), codebook._version)
+    with _tables_lock:
+        tab = _tables.get(key)
+    if tab is None:
+        if codebook is not None:
+            _check(codebook.dtype == torch.float32 and codebook.numel() == 16 and codebook.is_contiguous(),
+                   "codebook f32 [16]")
+            _cuda(codebook)
+        tab = torch.empty(65536, dtype=torch.int16, device=dev)
+        with torch.cuda.device(dev):
+            _lib.call("mono_w4_pair_table", _p(codebook), tab.data_ptr(), _stream(dev))
+        with _tables_lock:
+            _tables[key] = tab
+    return tab
+
+
+def w4a8_decode_linear(x, x_scale, packed, s_rel, s_channel, codebook=None, residual=None, group_size=16,
+                       out_dtype_code=2, cols=0, fast=False, tiled=False):
+    """out[m, n] = cast(float(int32 dot(x[m], decode(w[n]))) * x_scale[m] * s_channel[n]) (+ residual).
+    Reference: csrc/w4a8_decode.sycl:325-370. `cols` and `fast` are the reference's tuning knobs and are
+    accepted for signature compatibility; `tiled` selects mono_w4_repack's tile-major weights."""
+    _cuda(x, x_scale, packed, s_rel, s_channel)
+    _check(x.dtype == torch.int8 and x.dim() == 2 and x.is_contiguous(), "x must be contiguous int8 [M, K]")
+    M, K = x.shape
+    N = packed.shape[0]
+    _check(packed.dtype in (torch.int8, torch.uint8) and packed.is_contiguous() and packed.dim() == 2
+           and packed.shape[1] * 2 == K, "packed must be contiguous int8 [N, K/2]")
+    _check(s_rel.is_contiguous() and s_rel.numel() == N * (K // group_size), "s_rel must be contiguous [N, K/G]")
+    _check(s_rel.dtype == torch.float8_e4m3fn, "s_rel must be fp8 e4m3")
+    _check(x_scale.dtype == torch.float32 and x_scale.is_contiguous() and x_scale.numel() == M, "x_scale f32 [M]")
+    _check(s_channel.dtype == torch.float32 and s_channel.is_contiguous() and s_channel.numel() == N,
+           "s_channel f32 [N]")
+    _check(out_dtype_code in (0, 2), "out dtype fp32 or bf16")
+    dtype = torch.float32 if out_dtype_code == 0 else torch.bfloat16
+    out = torch.empty((M, N), dtype=dtype, device=x.device)
+    if residual is not None:
+        _check(residual.dtype == dtype and residual.is_contiguous() and residual.numel() == M * N,
+               "residual must match output")
+    tab = pair_table(codebook, x.device)
+    with torch.cuda.device(x.device):
+        _lib.call("mono_w4a8_decode_linear", _p(x), _p(x_scale), _p(packed), _p(s_rel), _lib.SCALE_FP8,
+                  _p(s_channel), _p(tab), _p(residual), M, N, K, group_size, out_dtype_code,
+                  _lib.LAYOUT_TILED if tiled else _lib.LAYOUT_ROW, _p(out), _stream(x.device))
+    return out
+
+
+def w4a8_gptq_linear(x, x_scale, packed, scales, residual=None, out_dtype_code=2, tiled=False):
+    """GPTQ W4A8 linear (BASELINE configs[0] format): int4 nibbles v + 8 [N, K/2], fp16 scales [N, K/128]."""
+    _cuda(x, x_scale, packed, scales)
+    _check(x.dtype == torch.int8 and x.dim() == 2 and x.is_contiguous(), "x must be contiguous int8 [M, K]")
+    M, K = x.shape
+    N = packed.shape[0]
+    _check(packed.dtype in (torch.int8, torch.uint8, torch.int32) and packed.is_contiguous()
+           and packed.numel() * packed.element_size() == N * K // 2, "packed must be contiguous [N, K/2] bytes")
+    _check(scales.dtype == torch.float16 and scales.is_contiguous() and scales.numel() == N * (K // 128),
+           "scales must be contiguous fp16 [N, K/128]")
+    _check(x_scale.dtype == torch.float32 and x_scale.numel() == M, "x_scale f32 [M]")
+    dtype = torch.float32 if out_dtype_code == 0 else torch.bfloat16
+    out = torch.empty((M, N), dtype=dtype, device=x.device)
+    if residual is not None:
+        _check(residual.dtype == dtype and residual.is_contiguous() and residual.numel() == M * N,
+               "residual must match output")
+    with torch.cuda.device(x.device):
+        _lib.call("mono_w4a8_gptq_linear", _p(x), _p(x_scale), _p(packed), _p(scales), _p(residual), M, N, K,
+                  out_dtype_code, _lib.LAYOUT_TILED if tiled else _lib.LAYOUT_ROW, _p(out), _stream(x.device))
+    return out
+
+
+def w4_repack(fmt, packed, scales, N, K):
+    """Tile-major copies (packed, scales) of a W4 weight for the TILED layout."""
+    _cuda(packed, scales)
+    _check(packed.is_contiguous() and scales.is_contiguous(), "contiguous operands")
+    qt = torch.empty_like(packed)
+    st = torch.empty_like(scales)
+    with torch.cuda.device(packed.device):
+        _lib.call("mono_w4_repack", fmt, _p(packed), _p(scales), N, K, _p(qt), _p(st), _stream(packed.device))
+    return qt, st
+
+
+def act_quant(x):
+    """GPTQ per-token int8 quantization of bf16 rows: (q int8 [..., K], scale f32 [..., 1])."""
+    _cuda(x)
+    _check(x.dtype == torch.bfloat16 and x.is_contiguous(), "x bf16 contiguous")
+    K = x.shape[-1]
+    M = x.numel() // K
+    q = torch.empty(x.shape, dtype=torch.int8, device=x.device)
+    s = torch.empty((*x.shape[:-1], 1), dtype=torch.float32, device=x.device)
+    if M:
+        with torch.cuda.device(x.device):
+            _lib.call("mono_act_quant", _p(x), M, K, _p(q), _p(s), _stream(x.device))
+    return q, s
+
+
+_rot_ws = {}
+
+
+def rot_quant(x, h, order=0):
+    """ConvRot rotation + row-wise INT8 quantization (csrc/act_prep.sycl:97-110): (q, scale [..., 1])."""
+    _cuda(x, h)
+    _check(x.dtype == torch.bfloat16 and x.is_contiguous(), "x bf16 contiguous")
+    _check(h.dtype == torch.bfloat16 and h.is_contiguous() and h.numel() == 65536, "H bf16 [256,256]")
+    K = x.shape[-1]
+    M = x.numel() // K
+    _check(K % 256 == 0, "K must be a multiple of 256")
+    q = torch.empty(x.shape, dtype=torch.int8, device=x.device)
+    s = torch.empty((*x.shape[:-1], 1), dtype=torch.float32, device=x.device)
+    if M == 0:
+        return q, s
+    need = _lib.load().mono_rot_quant_workspace(M, K)
+    key = x.device
+    ws = _rot_ws.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.zeros(need, dtype=torch.uint8, device=x.device)
+        _rot_ws[key] = ws
+    with torch.cuda.device(x.device):
+        _lib.call("mono_rot_quant", _p(x), _p(h), M, K, _p(q), _p(s), _p(ws), _stream(x.device))
+    return q, s
+
+
+def device_status(reset=True):
+    """The device error word (0 = no bounded wait has given up)."""
+    import ctypes
+    code = ctypes.c_int(0)
+    _lib.load().mono_device_status(ctypes.byref(code), 1 if reset else 0)
+    return code.value

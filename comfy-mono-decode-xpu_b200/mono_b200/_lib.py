@@ -1,0 +1,79 @@
+"""ctypes binding of libmono_b200.so (the C ABI declared in include/mono_b200.h).
+
+The library is built in-tree (csrc/build.py) and loaded from this directory. A missing or unloadable
+library raises ImportError: there is no CPU or eager fallback behind these entry points.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libmono_b200.so")
+
+P = ctypes.c_void_p
+I = ctypes.c_int
+I64 = ctypes.c_int64
+SZ = ctypes.c_size_t
+
+# name -> (restype, argtypes); every int-returning entry returns a MONO_* status
+SIGNATURES = {
+    "mono_last_error": (ctypes.c_char_p, []),
+    "mono_abi_version": (I, []),
+    "mono_device_status": (I, [ctypes.POINTER(I), I]),
+    "mono_w4a8_decode_linear": (I, [P, P, P, P, I, P, P, P, I64, I64, I64, I64, I, I, P, P]),
+    "mono_w4_pair_table": (I, [P, P, P]),
+    "mono_w4a8_gptq_linear": (I, [P, P, P, P, P, I64, I64, I64, I, I, P, P]),
+    "mono_w4_repack": (I, [I, P, P, I64, I64, P, P, P]),
+    "mono_act_quant": (I, [P, I64, I64, P, P, P]),
+    "mono_rot_quant_workspace": (SZ, [I64, I64]),
+    "mono_rot_quant": (I, [P, P, I64, I64, P, P, P, P]),
+}
+
+MONO_OK, MONO_EINVAL, MONO_ECUDA, MONO_ETIMEOUT, MONO_EDEVICE = 0, 1, 2, 3, 4
+OUT_F32, OUT_BF16 = 0, 2
+FMT_GPTQ, FMT_REF = 0, 1
+LAYOUT_ROW, LAYOUT_TILED = 0, 1
+SCALE_FP8, SCALE_F32 = 0, 1
+
+_lock = threading.Lock()
+_lib = None
+
+
+class MonoError(RuntimeError):
+    """A C-ABI call returned a non-zero status (message from mono_last_error())."""
+
+    def __init__(self, name, status, message):
+        super().__init__(f"{name}: status {status}: {message}")
+        self.status = status
+
+
+def load():
+    """Load the library once and declare every signature of SIGNATURES."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.isfile(LIB_PATH):
+                raise ImportError(f"{LIB_PATH} is not built: run python csrc/build.py (or __graft_entry__.build())")
+            lib = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def call(name, *args):
+    """Call an int-status entry point; a non-zero status raises MonoError (a RuntimeError)."""
+    lib = load()
+    status = getattr(lib, name)(*args)
+    if status != MONO_OK:
+        msg = lib.mono_last_error()
+        raise MonoError(name, status, msg.decode() if msg else "")
+    return status
+
+
+def exported_symbols():
+    return list(SIGNATURES)

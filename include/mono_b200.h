@@ -1,0 +1,106 @@
+/* mono_b200: C ABI of the B200 (sm_100a) W4A8 decode-step kernels.
+ *
+ * One entry point per operation of the reference's native module (comfy-mono-decode-xpu
+ * csrc/bindings.cpp), with torch::Tensor arguments replaced by device pointers, sizes and a CUDA stream.
+ * Conventions:
+ *   - every pointer is device memory owned by the caller (outputs included), unless noted;
+ *   - shapes and alignment are validated on the host before any launch; a rejected call launches nothing;
+ *   - the return value is a status (MONO_OK = 0); mono_last_error() gives the calling thread's last message;
+ *   - work is enqueued on `stream` (NULL = the legacy default stream) and nothing synchronizes;
+ *   - bounded device-side waits never trap: they record a code that mono_device_status() reads.
+ */
+#ifndef MONO_B200_H
+#define MONO_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define MONO_API __attribute__((visibility("default")))
+#else
+#define MONO_API
+#endif
+
+typedef struct CUstream_st* mono_stream_t; /* the same handle as cudaStream_t */
+
+enum {
+    MONO_OK = 0,
+    MONO_EINVAL = 1,   /* argument rejected before launch */
+    MONO_ECUDA = 2,    /* a CUDA runtime call failed */
+    MONO_ETIMEOUT = 3, /* a device-side bounded wait gave up */
+    MONO_EDEVICE = 4   /* the device error word is set */
+};
+
+/* output dtype codes, as the reference's out_dtype_code (csrc/w4a8_decode.sycl:360-361) */
+enum { MONO_OUT_F32 = 0, MONO_OUT_BF16 = 2 };
+/* relative-scale dtypes of the REF weight format */
+enum { MONO_SCALE_FP8_E4M3 = 0, MONO_SCALE_F32 = 1 };
+/* W4 weight formats: GPTQ = int4 symmetric, fp16 scale per (row, 128-group);
+ * REF = the reference's AsymW4A8Int8Layout codes + codebook + FP8 G16 + channel scale */
+enum { MONO_FMT_GPTQ = 0, MONO_FMT_REF = 1 };
+/* W4 weight layouts: ROW = the checkpoint's [N][K/2] bytes; TILED = mono_w4_repack's B200 tile-major copy */
+enum { MONO_LAYOUT_ROW = 0, MONO_LAYOUT_TILED = 1 };
+
+MONO_API const char* mono_last_error(void);
+MONO_API int mono_abi_version(void);
+/* Reads (and with reset != 0 clears) the device error word of the current device. Synchronizes. */
+MONO_API int mono_device_status(int* code, int reset);
+
+/* ---- W4A8 linear ----------------------------------------------------------------------------------- */
+
+/* Replaces _C.w4a8_decode_linear (csrc/bindings.cpp:71-74; csrc/w4a8_decode.sycl:325-370).
+ *   out[m, n] = cast(float(int32 sum_k x[m, k] * w_i8[n, k]) * x_scale[m] * s_channel[n]) (+ residual)
+ *   w_i8 = isnan(r) ? 0 : clamp(r, -127, 127), r = rint(codebook[code] * s_rel[n, k / 16])
+ * x int8 [M, K] (16 B aligned), x_scale f32 [M], packed [N, K/2] bytes (low nibble = even k) or its TILED
+ * copy, s_rel FP8 e4m3 [N, K/16] (G16) or its TILED copy, s_channel f32 [N], pair_table from
+ * mono_w4_pair_table(codebook), residual [M, N] in the output dtype or NULL, out [M, N].
+ * 1 <= M <= 16, K % 1024 == 0, K <= 16384, N % 16 == 0, group_size == 16. */
+MONO_API int mono_w4a8_decode_linear(const int8_t* x, const float* x_scale, const void* packed, const void* s_rel,
+                            int s_rel_dtype, const float* s_channel, const uint16_t* pair_table,
+                            const void* residual, int64_t M, int64_t N, int64_t K, int64_t group_size,
+                            int out_dtype_code, int layout, void* out, mono_stream_t stream);
+
+/* The REF decode table of one codebook (NULL = the reference's default float(i - 8)): 65536 uint16
+ * entries (scale byte << 8 | code byte) -> int8 value of the low code | int8 value of the high code << 8.
+ * Stands in for the per-element decode of csrc/w4a8_decode.sycl:35-45 and the pair table of
+ * csrc/mono_common.hpp:94-141 (which covers scale bytes < 0x80 only; this one covers all 256). */
+MONO_API int mono_w4_pair_table(const float* codebook, uint16_t* table, mono_stream_t stream);
+
+/* GPTQ W4A8 linear (the reference has no GPTQ entry, its W4A8 linear above is the
+ * closest): int4 v in [-8, 7] stored as nibble v + 8 (8 per int32 along K, i.e. [N, K/2] bytes),
+ * fp16 scales [N, K/128] (or TILED copies);
+ *   acc_g = int32 sum over group g of x * v;  F_c = sum_{g in 1024-chunk c} float(acc_g) * float(s[n, g]);
+ *   out = cast((sum_c F_c) * x_scale[m])  (fp32, sequential sums from +0, no fused multiply-add). */
+MONO_API int mono_w4a8_gptq_linear(const int8_t* x, const float* x_scale, const void* packed, const void* scales,
+                          const void* residual, int64_t M, int64_t N, int64_t K, int out_dtype_code, int layout,
+                          void* out, mono_stream_t stream);
+
+/* Tile-major copy of a W4 weight for the TILED layout (the role of tiles.py tile_major,
+ * comfy_mono_decode_xpu/tiles.py:45-48): packed [N, K/2] -> [N/16][K/128][2][32][16] bytes (GPTQ nibbles
+ * re-coded as two's complement), scales -> [N/16][K/256][16][4 or 16 bytes]. Outputs are the same sizes as
+ * the inputs. N % 16 == 0, K % 256 == 0. */
+MONO_API int mono_w4_repack(int fmt, const void* packed, const void* scales, int64_t N, int64_t K, void* packed_tiled,
+                   void* scales_tiled, mono_stream_t stream);
+
+/* ---- activation quantization ----------------------------------------------------------------------- */
+
+/* GPTQ activation quant: per row s = amax / 127, q = clamp(rint(x / s), -127, 127).
+ * x bf16 [M, K] (16 B aligned), q int8 [M, K], scale f32 [M]. K % 8 == 0. */
+MONO_API int mono_act_quant(const void* x_bf16, int64_t M, int64_t K, int8_t* q, float* scale, mono_stream_t stream);
+
+/* Replaces _C.rot_quant (csrc/bindings.cpp:104; csrc/act_prep.sycl:97-110): ConvRot rotation by H
+ * (bf16 [256, 256]) per 256-group, then row-wise int8 quantization. x bf16 [M, K], q int8 [M, K],
+ * scale f32 [M]. K % 256 == 0. workspace: mono_rot_quant_workspace(M, K) bytes, zero-filled before its
+ * first use (the kernels leave it reusable). */
+MONO_API size_t mono_rot_quant_workspace(int64_t M, int64_t K);
+MONO_API int mono_rot_quant(const void* x_bf16, const void* h_bf16, int64_t M, int64_t K, int8_t* q, float* scale,
+                   void* workspace, mono_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MONO_B200_H */
