@@ -4,7 +4,7 @@
 #include <string>
 
 #include "abi_internal.h"
-#include "w4a8_gemv.cuh"
+#include "engine.cuh"
 
 namespace mono {
 
@@ -34,12 +34,39 @@ int sm_count() {
     return counts[dev];
 }
 
-int launch_gemv(int fmt, int layout, const GemvParams& p, cudaStream_t stream);
+struct LinearEpi {
+    const float* xs;
+    const float* s_channel;
+    const void* residual;
+    void* out;
+    int out_bf16;
+    int max_items;
+};
+int launch_linear(int fmt, int layout, Program& P, LinearEpi& E, cudaStream_t stream);
 int launch_repack(int fmt, const void* q, const void* s, int N, int K, void* qt, void* st, cudaStream_t stream);
 int launch_pair_table(const float* codebook, uint16_t* tab, cudaStream_t stream);
 int launch_act_quant(const void* x, int M, int K, int8_t* q, float* xs, cudaStream_t stream);
 size_t rot_quant_workspace(int M, int K);
 int launch_rot_quant(const void* x, const void* h, int M, int K, int8_t* q, float* s, void* ws, cudaStream_t stream);
+
+struct MlpArgs {
+    const uint16_t* x;
+    const uint16_t* norm_w;
+    const uint16_t* lut;
+    uint16_t* out;
+    float eps;
+    int H, I, residual, max_items;
+    uint16_t* xn;
+    int8_t* q1;
+    float* s1;
+    uint16_t* h;
+    unsigned* amax2;
+    int8_t* q2;
+    float* s2;
+    unsigned* bar;
+};
+int launch_mlp(Program& P, MlpArgs& A, cudaStream_t stream);
+size_t mlp_workspace_bytes(int H, int I);
 
 static int check_linear_common(const int8_t* x, const float* xs, const void* packed, const void* scales,
                                const void* out, int64_t M, int64_t N, int64_t K, int out_dtype_code, int layout) {
@@ -86,18 +113,16 @@ int mono_w4a8_decode_linear(const int8_t* x, const float* x_scale, const void* p
     MONO_CHECK(group_size == 16, "group_size must be 16 (G16 FP8 relative scales)");
     MONO_CHECK(s_rel_dtype == MONO_SCALE_FP8_E4M3, "s_rel must be FP8 e4m3");
     MONO_CHECK(s_channel && pair_table, "s_channel and pair_table are required");
-    GemvParams p{};
-    p.q = static_cast<const uint8_t*>(packed);
-    p.scales = static_cast<const uint8_t*>(s_rel);
-    p.s_channel = s_channel;
-    p.pair_tab = pair_table;
-    p.x = x;
-    p.xs = x_scale;
-    p.residual = residual;
-    p.out = out;
-    p.M = int(M); p.N = int(N); p.K = int(K);
-    p.out_bf16 = out_dtype_code == MONO_OUT_BF16;
-    return launch_gemv(FMT_REF, layout, p, reinterpret_cast<cudaStream_t>(stream));
+    Program P{};
+    P.nph = 1;
+    P.M = int(M);
+    P.pair_tab = pair_table;
+    P.ph[0].m[0] = MatDesc{static_cast<const uint8_t*>(packed), static_cast<const uint8_t*>(s_rel), int(N)};
+    P.ph[0].nm = 1;
+    P.ph[0].K = int(K);
+    P.ph[0].x = x;
+    LinearEpi E{x_scale, s_channel, residual, out, out_dtype_code == MONO_OUT_BF16, 0};
+    return launch_linear(FMT_REF, layout, P, E, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int mono_w4_pair_table(const float* codebook, uint16_t* table, mono_stream_t stream) {
@@ -110,16 +135,15 @@ int mono_w4a8_gptq_linear(const int8_t* x, const float* x_scale, const void* pac
                           void* out, mono_stream_t stream) {
     int rc = check_linear_common(x, x_scale, packed, scales, out, M, N, K, out_dtype_code, layout);
     if (rc) return rc;
-    GemvParams p{};
-    p.q = static_cast<const uint8_t*>(packed);
-    p.scales = static_cast<const uint8_t*>(scales);
-    p.x = x;
-    p.xs = x_scale;
-    p.residual = residual;
-    p.out = out;
-    p.M = int(M); p.N = int(N); p.K = int(K);
-    p.out_bf16 = out_dtype_code == MONO_OUT_BF16;
-    return launch_gemv(FMT_GPTQ, layout, p, reinterpret_cast<cudaStream_t>(stream));
+    Program P{};
+    P.nph = 1;
+    P.M = int(M);
+    P.ph[0].m[0] = MatDesc{static_cast<const uint8_t*>(packed), static_cast<const uint8_t*>(scales), int(N)};
+    P.ph[0].nm = 1;
+    P.ph[0].K = int(K);
+    P.ph[0].x = x;
+    LinearEpi E{x_scale, nullptr, residual, out, out_dtype_code == MONO_OUT_BF16, 0};
+    return launch_linear(FMT_GPTQ, layout, P, E, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int mono_w4_repack(int fmt, const void* packed, const void* scales, int64_t N, int64_t K, void* packed_tiled,
@@ -147,6 +171,59 @@ int mono_rot_quant(const void* x_bf16, const void* h_bf16, int64_t M, int64_t K,
     MONO_CHECK(M >= 1 && M <= 65535 && K >= 256 && K % 256 == 0, "M in [1, 65535], K % 256 == 0");
     MONO_CHECK(aligned(workspace, 16), "workspace must be 16-byte aligned");
     return launch_rot_quant(x_bf16, h_bf16, int(M), int(K), q, scale, workspace, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t mono_mlp_gptq_workspace(int64_t H, int64_t I) { return mlp_workspace_bytes(int(H), int(I)); }
+
+int mono_mlp_gptq(const void* x, const void* norm_w, float eps, const void* gate_q, const void* gate_s,
+                  const void* up_q, const void* up_s, const void* down_q, const void* down_s, const void* silu_lut,
+                  int64_t M, int64_t H, int64_t I, int residual, void* out, void* workspace, size_t workspace_bytes,
+                  mono_stream_t stream) {
+    MONO_CHECK(x && gate_q && gate_s && up_q && up_s && down_q && down_s && silu_lut && out && workspace, "null operand");
+    MONO_CHECK(M >= 1 && M <= 16, "1 <= M <= 16 (got %lld)", (long long)M);
+    MONO_CHECK(H >= kChunkK && H % kChunkK == 0 && H <= kChunkK * kMaxChunks, "H must be a multiple of 1024 up to 16384");
+    MONO_CHECK(I >= kChunkK && I % kChunkK == 0 && I <= kChunkK * kMaxChunks, "I must be a multiple of 1024 up to 16384");
+    MONO_CHECK(workspace_bytes >= mlp_workspace_bytes(int(H), int(I)), "workspace too small (%zu < %zu)", workspace_bytes,
+               mlp_workspace_bytes(int(H), int(I)));
+    MONO_CHECK(aligned(x, 16) && aligned(out, 16) && aligned(workspace, 256), "x/out 16-byte, workspace 256-byte aligned");
+    for (const void* p : {gate_q, gate_s, up_q, up_s, down_q, down_s}) MONO_CHECK(aligned(p, 16), "weights 16-byte aligned");
+    auto al = [](size_t b) { return (b + 255) / 256 * 256; };
+    uint8_t* w = static_cast<uint8_t*>(workspace);
+    MlpArgs A{};
+    A.x = static_cast<const uint16_t*>(x);
+    A.norm_w = static_cast<const uint16_t*>(norm_w);
+    A.lut = static_cast<const uint16_t*>(silu_lut);
+    A.out = static_cast<uint16_t*>(out);
+    A.eps = eps;
+    A.H = int(H);
+    A.I = int(I);
+    A.residual = residual != 0;
+    A.xn = reinterpret_cast<uint16_t*>(w);
+    w += al(16 * size_t(H) * 2);
+    A.q1 = reinterpret_cast<int8_t*>(w);
+    w += al(16 * size_t(H));
+    A.h = reinterpret_cast<uint16_t*>(w);
+    w += al(16 * size_t(I) * 2);
+    A.q2 = reinterpret_cast<int8_t*>(w);
+    w += al(16 * size_t(I));
+    A.s1 = reinterpret_cast<float*>(w);
+    A.s2 = reinterpret_cast<float*>(w + 256);
+    A.amax2 = reinterpret_cast<unsigned*>(w + 512);
+    A.bar = reinterpret_cast<unsigned*>(w + 768);
+    Program P{};
+    P.nph = 2;
+    P.M = int(M);
+    P.ph[0].m[0] = MatDesc{static_cast<const uint8_t*>(gate_q), static_cast<const uint8_t*>(gate_s), int(I)};
+    P.ph[0].m[1] = MatDesc{static_cast<const uint8_t*>(up_q), static_cast<const uint8_t*>(up_s), int(I)};
+    P.ph[0].nm = 2;
+    P.ph[0].paired = 1;
+    P.ph[0].K = int(H);
+    P.ph[0].x = A.q1;
+    P.ph[1].m[0] = MatDesc{static_cast<const uint8_t*>(down_q), static_cast<const uint8_t*>(down_s), int(H)};
+    P.ph[1].nm = 1;
+    P.ph[1].K = int(I);
+    P.ph[1].x = A.q2;
+    return launch_mlp(P, A, reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -153,14 +153,17 @@ int launch_act_quant(const void* x, int M, int K, int8_t* q, float* xs, cudaStre
     return MONO_OK;
 }
 
-// workspace: xr bf16 [M][K], then amax words [M] and done counters [M] (zero on first use; the kernels
-// leave them zero again)
-size_t rot_quant_workspace(int M, int K) { return size_t(M) * K * 2 + size_t(M) * 8; }
+// workspace: amax words [kRotMaxRows] and done counters [kRotMaxRows] at fixed offsets (zero on first use;
+// the kernels leave them zero again), then xr bf16 [M][K]. The fixed offsets keep the counters clear of
+// the rotated rows of any earlier call with another shape.
+constexpr int kRotMaxRows = 256;
+size_t rot_quant_workspace(int M, int K) { return size_t(kRotMaxRows) * 8 + size_t(M) * K * 2; }
 
 int launch_rot_quant(const void* x, const void* h, int M, int K, int8_t* q, float* s, void* ws, cudaStream_t stream) {
-    auto* xr = static_cast<uint16_t*>(ws);
-    auto* amax = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + size_t(M) * K * 2);
-    auto* done = amax + M;
+    if (M > kRotMaxRows) return fail(MONO_EINVAL, "rot_quant: at most %d rows (got %d)", kRotMaxRows, M);
+    auto* amax = static_cast<unsigned*>(ws);
+    auto* done = amax + kRotMaxRows;
+    auto* xr = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(ws) + size_t(kRotMaxRows) * 8);
     rot_kernel<<<dim3(K / 256, M), 256, 0, stream>>>(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(h),
                                                       K, xr, amax);
     CUDA_TRY(cudaGetLastError());

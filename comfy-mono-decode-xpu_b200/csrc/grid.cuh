@@ -1,0 +1,54 @@
+// Grid-wide barrier of a cooperative launch (the role of csrc/mono_common.hpp:54-73 grid_sync), bounded.
+//
+// counter[0] counts arrivals (epoch * gridDim.x after the epoch-th barrier), counter[1] counts exits; the
+// last CTA to exit resets both, so the workspace is reusable by the next launch and by graph replays.
+// After kGridSpinLimit polls a waiting CTA records DEV_GRID_TIMEOUT and carries on: no trap, no hang.
+#pragma once
+#include "common.cuh"
+
+namespace mono {
+
+constexpr uint32_t kGridSpinLimit = 1u << 24;
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Returns false if the wait gave up. flag: one int of shared memory.
+__device__ __forceinline__ bool grid_barrier(unsigned* counter, unsigned& epoch, int* flag) {
+    __syncthreads();
+    ++epoch;
+    if (threadIdx.x == 0) {
+        const unsigned target = epoch * gridDim.x;
+        __threadfence();
+        atomicAdd(counter, 1u);
+        bool ok = true;
+        uint32_t spins = 0;
+        while (ld_acquire_gpu(counter) < target) {
+            if (++spins > kGridSpinLimit) {
+                set_device_error(DEV_GRID_TIMEOUT);
+                ok = false;
+                break;
+            }
+            __nanosleep(32);
+        }
+        *flag = ok;
+    }
+    __syncthreads();
+    return *flag != 0;
+}
+
+__device__ __forceinline__ void grid_exit(unsigned* counter) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(counter + 1, 1u) == gridDim.x - 1) {
+            atomicExch(counter, 0u);
+            atomicExch(counter + 1, 0u);
+        }
+    }
+}
+
+}  // namespace mono

@@ -1,9 +1,9 @@
-// W4A8 linear: launchers for the GEMV kernel, the tile-major repack and the REF pair table.
+// W4A8 weight preparation: the tile-major repack and the REF pair table; the device error word.
 #include <cstdio>
 #include <mutex>
 
 #include "abi_internal.h"
-#include "w4a8_gemv.cuh"
+#include "engine.cuh"
 
 namespace mono {
 
@@ -56,55 +56,6 @@ __global__ void pair_table_kernel(const float* __restrict__ cb, uint16_t* __rest
     const float scale = fp8e4m3_to_f32(uint8_t(i >> 8));
     const float lo = cb ? cb[byte & 15] : float((byte & 15) - 8), hi = cb ? cb[byte >> 4] : float((byte >> 4) - 8);
     tab[i] = uint16_t(ref_grid(lo, scale) | (ref_grid(hi, scale) << 8));
-}
-
-template <int FMT, int LAYOUT, int MT>
-static int launch_gemv_t(const GemvParams& p, cudaStream_t stream) {
-    auto kern = w4a8_gemv_kernel<FMT, LAYOUT, MT>;
-    const int C = p.K / kChunkK;
-    const size_t smem = gemv_smem_bytes<FMT>(C);
-    // the dynamic shared memory opt-in and the occupancy query, once per (kernel, size)
-    static std::mutex mu;
-    static size_t done_smem[kMaxChunks + 1] = {};
-    static int done_per_sm[kMaxChunks + 1] = {};
-    int per_sm = 0;
-    {
-        std::lock_guard<std::mutex> lock(mu);
-        if (done_smem[C] != smem) {
-            CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-            CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&done_per_sm[C], kern, kGemvWarps * 32, smem));
-            done_smem[C] = smem;
-        }
-        per_sm = done_per_sm[C];
-    }
-    const int sms = sm_count();
-    if (per_sm < 1) return fail(MONO_EINVAL, "w4a8 gemv: shared memory requirement %zu B does not fit an SM", smem);
-    const int tiles = p.N / 16;
-    const int grid = tiles < sms * per_sm ? tiles : sms * per_sm;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kGemvWarps * 32);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p));
-    return MONO_OK;
-}
-
-int launch_gemv(int fmt, int layout, const GemvParams& p, cudaStream_t stream) {
-    const bool two = p.M > 8;
-#define MONO_GEMV_CASE(F, L)                                                                    \
-    if (fmt == F && layout == L) return two ? launch_gemv_t<F, L, 2>(p, stream) : launch_gemv_t<F, L, 1>(p, stream);
-    MONO_GEMV_CASE(FMT_GPTQ, LAYOUT_ROW)
-    MONO_GEMV_CASE(FMT_GPTQ, LAYOUT_TILED)
-    MONO_GEMV_CASE(FMT_REF, LAYOUT_ROW)
-    MONO_GEMV_CASE(FMT_REF, LAYOUT_TILED)
-#undef MONO_GEMV_CASE
-    return fail(MONO_EINVAL, "w4a8 gemv: unknown format %d / layout %d", fmt, layout);
 }
 
 int launch_repack(int fmt, const void* q, const void* s, int N, int K, void* qt, void* st, cudaStream_t stream) {

@@ -166,3 +166,53 @@ def device_status(reset=True):
     code = ctypes.c_int(0)
     _lib.load().mono_device_status(ctypes.byref(code), 1 if reset else 0)
     return code.value
+
+
+# ---- constants of the fused kernels -------------------------------------------------------------------
+
+_luts = {}
+
+
+def act_luts(device):
+    """(silu, sigmoid) of every bf16 bit pattern as bf16 [65536], from torch's own F.silu / torch.sigmoid on
+    the device (as comfy_mono_decode_xpu/layer.py:100-102 builds them)."""
+    dev = torch.device(device)
+    c = _luts.get(dev)
+    if c is None:
+        allbf = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16).to(dev)
+        c = _luts[dev] = (torch.nn.functional.silu(allbf).contiguous(), torch.sigmoid(allbf).contiguous())
+    return c
+
+
+_mlp_ws = {}
+
+
+def _workspace(table, key, nbytes, device):
+    ws = table.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=device)  # zero-filled: barrier words start at 0
+        table[key] = ws
+    return ws
+
+
+def mlp_gptq(x, norm_w, eps, gate, up, down, silu_lut=None, residual=True, out=None):
+    """Fused GPTQ MLP block (include/mono_b200.h mono_mlp_gptq). gate/up/down: (tiled packed, tiled fp16
+    scales) from w4_repack. x bf16 [..., H]; returns bf16 [..., H] (out may be x: in place)."""
+    _cuda(x)
+    _check(x.dtype == torch.bfloat16 and x.is_contiguous(), "x bf16 contiguous")
+    H = x.shape[-1]
+    M = x.numel() // H
+    I = gate[0].numel() * 2 // H
+    if silu_lut is None:
+        silu_lut = act_luts(x.device)[0]
+    if norm_w is not None:
+        _check(norm_w.dtype == torch.bfloat16 and norm_w.numel() == H and norm_w.is_contiguous(), "norm_w bf16 [H]")
+    if out is None:
+        out = torch.empty_like(x)
+    need = _lib.load().mono_mlp_gptq_workspace(H, I)
+    ws = _workspace(_mlp_ws, (x.device, H, I), need, x.device)
+    with torch.cuda.device(x.device):
+        _lib.call("mono_mlp_gptq", _p(x), _p(norm_w), float(eps), _p(gate[0]), _p(gate[1]), _p(up[0]), _p(up[1]),
+                  _p(down[0]), _p(down[1]), _p(silu_lut), M, H, I, 1 if residual else 0, _p(out), _p(ws), need,
+                  _stream(x.device))
+    return out

@@ -94,11 +94,30 @@ MONO_API int mono_act_quant(const void* x_bf16, int64_t M, int64_t K, int8_t* q,
 
 /* Replaces _C.rot_quant (csrc/bindings.cpp:104; csrc/act_prep.sycl:97-110): ConvRot rotation by H
  * (bf16 [256, 256]) per 256-group, then row-wise int8 quantization. x bf16 [M, K], q int8 [M, K],
- * scale f32 [M]. K % 256 == 0. workspace: mono_rot_quant_workspace(M, K) bytes, zero-filled before its
- * first use (the kernels leave it reusable). */
+ * scale f32 [M]. 1 <= M <= 256, K % 256 == 0. workspace: mono_rot_quant_workspace(M, K) bytes, zero-filled
+ * before its first use (the kernels leave it reusable); one call at a time per workspace. */
 MONO_API size_t mono_rot_quant_workspace(int64_t M, int64_t K);
 MONO_API int mono_rot_quant(const void* x_bf16, const void* h_bf16, int64_t M, int64_t K, int8_t* q, float* scale,
                    void* workspace, mono_stream_t stream);
+
+/* ---- fused MLP block --------------------------------------------------------------------------------- */
+
+/* GPTQ MLP block in one cooperative launch (the GPTQ counterpart of _C.mono_mlp, csrc/bindings.cpp:75-77;
+ * csrc/mono_mlp.sycl:34-180, and of layer_post's MLP phases, csrc/mono_layer.sycl:272-313):
+ *   xn = RMSNorm(x; norm_w, eps)  (norm_w NULL: xn = x)        q1, s1 = act_quant(xn)
+ *   g, u = GPTQ linear (gate, up)(q1)  h = bf16(silu_lut[g] * u)  q2, s2 = act_quant(h)
+ *   out = bf16(x + bf16(GPTQ down(q2)))  (residual != 0)  or  bf16(GPTQ down(q2))
+ * RMSNorm order: P[v] = sum_j x[v + 256 j]^2 (v < 256), butterfly within each 32, the 8 partial sums in
+ * order, r = 1 / sqrt(total / H + eps), out = bf16((x * r) * w) (IEEE fp32 ops, no fused multiply-add).
+ * x, out bf16 [M, H] (out may alias x); gate/up TILED [I, H/2] + fp16 scales; down TILED [H, I/2] + scales;
+ * silu_lut bf16 [65536] (SiLU of every bf16 bit pattern). 1 <= M <= 16, H and I multiples of 1024 up to
+ * 16384. workspace: mono_mlp_gptq_workspace(H, I) bytes, zero-filled before its first use (the kernel
+ * leaves it reusable); one call at a time per workspace. */
+MONO_API size_t mono_mlp_gptq_workspace(int64_t H, int64_t I);
+MONO_API int mono_mlp_gptq(const void* x, const void* norm_w, float eps, const void* gate_q, const void* gate_s,
+                           const void* up_q, const void* up_s, const void* down_q, const void* down_s,
+                           const void* silu_lut, int64_t M, int64_t H, int64_t I, int residual, void* out,
+                           void* workspace, size_t workspace_bytes, mono_stream_t stream);
 
 #ifdef __cplusplus
 }
