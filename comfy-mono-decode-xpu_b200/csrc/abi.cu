@@ -43,7 +43,8 @@ struct LinearEpi {
     int max_items;
 };
 int launch_linear(int fmt, int layout, Program& P, LinearEpi& E, cudaStream_t stream);
-int launch_repack(int fmt, const void* q, const void* s, int N, int K, void* qt, void* st, cudaStream_t stream);
+int launch_repack(int fmt, const void* q, const void* s, int N, int K, void* out, cudaStream_t stream);
+size_t tiled_bytes(int fmt, int64_t N, int64_t K);
 int launch_pair_table(const float* codebook, uint16_t* tab, cudaStream_t stream);
 int launch_act_quant(const void* x, int M, int K, int8_t* q, float* xs, cudaStream_t stream);
 size_t rot_quant_workspace(int M, int K);
@@ -70,7 +71,7 @@ size_t mlp_workspace_bytes(int H, int I);
 
 static int check_linear_common(const int8_t* x, const float* xs, const void* packed, const void* scales,
                                const void* out, int64_t M, int64_t N, int64_t K, int out_dtype_code, int layout) {
-    MONO_CHECK(x && xs && packed && scales && out, "null operand");
+    MONO_CHECK(x && xs && packed && out && (scales || layout == MONO_LAYOUT_TILED), "null operand");
     MONO_CHECK(M >= 1 && M <= 16, "1 <= M <= 16 (got %lld)", (long long)M);
     MONO_CHECK(K >= kChunkK && K % kChunkK == 0 && K <= kChunkK * kMaxChunks, "K must be a multiple of 1024 in [1024, 16384] (got %lld)",
                (long long)K);
@@ -79,7 +80,7 @@ static int check_linear_common(const int8_t* x, const float* xs, const void* pac
     MONO_CHECK(layout == MONO_LAYOUT_ROW || layout == MONO_LAYOUT_TILED, "layout ROW (0) or TILED (1)");
     MONO_CHECK(aligned(x, 16), "x must be 16-byte aligned");
     MONO_CHECK(aligned(packed, 16), "packed weights must be 16-byte aligned");
-    MONO_CHECK(aligned(scales, 16), "scales must be 16-byte aligned");
+    MONO_CHECK(layout == MONO_LAYOUT_TILED || aligned(scales, 16), "scales must be 16-byte aligned");
     return MONO_OK;
 }
 
@@ -102,6 +103,15 @@ int mono_device_status(int* code, int reset) {
         CUDA_TRY(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)));
     }
     return v ? fail(MONO_EDEVICE, "device error word = %d", v) : MONO_OK;
+}
+
+size_t mono_trace_bytes(void) { return size_t(kTraceCtas) * kTracePhases * 8; }
+
+int mono_trace_enable(void* buffer, size_t bytes) {
+    MONO_CHECK(buffer == nullptr || bytes >= size_t(kTraceCtas) * kTracePhases * 8, "trace buffer too small");
+    unsigned long long* p = static_cast<unsigned long long*>(buffer);
+    CUDA_TRY(cudaMemcpyToSymbol(g_trace, &p, sizeof(p)));
+    return MONO_OK;
 }
 
 int mono_w4a8_decode_linear(const int8_t* x, const float* x_scale, const void* packed, const void* s_rel,
@@ -146,14 +156,15 @@ int mono_w4a8_gptq_linear(const int8_t* x, const float* x_scale, const void* pac
     return launch_linear(FMT_GPTQ, layout, P, E, reinterpret_cast<cudaStream_t>(stream));
 }
 
-int mono_w4_repack(int fmt, const void* packed, const void* scales, int64_t N, int64_t K, void* packed_tiled,
-                   void* scales_tiled, mono_stream_t stream) {
+size_t mono_w4_tiled_bytes(int fmt, int64_t N, int64_t K) { return tiled_bytes(fmt, N, K); }
+
+int mono_w4_repack(int fmt, const void* packed, const void* scales, int64_t N, int64_t K, void* tiled,
+                   mono_stream_t stream) {
     MONO_CHECK(fmt == MONO_FMT_GPTQ || fmt == MONO_FMT_REF, "fmt GPTQ (0) or REF (1)");
-    MONO_CHECK(packed && scales && packed_tiled && scales_tiled, "null operand");
-    MONO_CHECK(N >= 16 && N % 16 == 0 && K >= 256 && K % 256 == 0, "N % 16 == 0 and K % 256 == 0");
-    MONO_CHECK(aligned(packed, 16) && aligned(packed_tiled, 16), "weights must be 16-byte aligned");
-    return launch_repack(fmt, packed, scales, int(N), int(K), packed_tiled, scales_tiled,
-                         reinterpret_cast<cudaStream_t>(stream));
+    MONO_CHECK(packed && scales && tiled, "null operand");
+    MONO_CHECK(N >= 16 && N % 16 == 0 && K >= kChunkK && K % kChunkK == 0, "N % 16 == 0 and K % 1024 == 0");
+    MONO_CHECK(aligned(packed, 16) && aligned(scales, 16) && aligned(tiled, 16), "operands must be 16-byte aligned");
+    return launch_repack(fmt, packed, scales, int(N), int(K), tiled, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int mono_act_quant(const void* x_bf16, int64_t M, int64_t K, int8_t* q, float* scale, mono_stream_t stream) {
@@ -175,18 +186,18 @@ int mono_rot_quant(const void* x_bf16, const void* h_bf16, int64_t M, int64_t K,
 
 size_t mono_mlp_gptq_workspace(int64_t H, int64_t I) { return mlp_workspace_bytes(int(H), int(I)); }
 
-int mono_mlp_gptq(const void* x, const void* norm_w, float eps, const void* gate_q, const void* gate_s,
-                  const void* up_q, const void* up_s, const void* down_q, const void* down_s, const void* silu_lut,
+int mono_mlp_gptq(const void* x, const void* norm_w, float eps, const void* gate_q, const void* up_q,
+                  const void* down_q, const void* silu_lut,
                   int64_t M, int64_t H, int64_t I, int residual, void* out, void* workspace, size_t workspace_bytes,
                   mono_stream_t stream) {
-    MONO_CHECK(x && gate_q && gate_s && up_q && up_s && down_q && down_s && silu_lut && out && workspace, "null operand");
+    MONO_CHECK(x && gate_q && up_q && down_q && silu_lut && out && workspace, "null operand");
     MONO_CHECK(M >= 1 && M <= 16, "1 <= M <= 16 (got %lld)", (long long)M);
-    MONO_CHECK(H >= kChunkK && H % kChunkK == 0 && H <= kChunkK * kMaxChunks, "H must be a multiple of 1024 up to 16384");
+    MONO_CHECK(H >= kChunkK && H % kChunkK == 0 && H <= 4096, "H must be a multiple of 1024 up to 4096");
     MONO_CHECK(I >= kChunkK && I % kChunkK == 0 && I <= kChunkK * kMaxChunks, "I must be a multiple of 1024 up to 16384");
     MONO_CHECK(workspace_bytes >= mlp_workspace_bytes(int(H), int(I)), "workspace too small (%zu < %zu)", workspace_bytes,
                mlp_workspace_bytes(int(H), int(I)));
     MONO_CHECK(aligned(x, 16) && aligned(out, 16) && aligned(workspace, 256), "x/out 16-byte, workspace 256-byte aligned");
-    for (const void* p : {gate_q, gate_s, up_q, up_s, down_q, down_s}) MONO_CHECK(aligned(p, 16), "weights 16-byte aligned");
+    for (const void* p : {gate_q, up_q, down_q}) MONO_CHECK(aligned(p, 16), "weights 16-byte aligned");
     auto al = [](size_t b) { return (b + 255) / 256 * 256; };
     uint8_t* w = static_cast<uint8_t*>(workspace);
     MlpArgs A{};
@@ -213,16 +224,18 @@ int mono_mlp_gptq(const void* x, const void* norm_w, float eps, const void* gate
     Program P{};
     P.nph = 2;
     P.M = int(M);
-    P.ph[0].m[0] = MatDesc{static_cast<const uint8_t*>(gate_q), static_cast<const uint8_t*>(gate_s), int(I)};
-    P.ph[0].m[1] = MatDesc{static_cast<const uint8_t*>(up_q), static_cast<const uint8_t*>(up_s), int(I)};
+    P.ph[0].m[0] = MatDesc{static_cast<const uint8_t*>(gate_q), nullptr, int(I)};
+    P.ph[0].m[1] = MatDesc{static_cast<const uint8_t*>(up_q), nullptr, int(I)};
     P.ph[0].nm = 2;
     P.ph[0].paired = 1;
     P.ph[0].K = int(H);
     P.ph[0].x = A.q1;
-    P.ph[1].m[0] = MatDesc{static_cast<const uint8_t*>(down_q), static_cast<const uint8_t*>(down_s), int(H)};
+    P.ph[0].xperm = 1;
+    P.ph[1].m[0] = MatDesc{static_cast<const uint8_t*>(down_q), nullptr, int(H)};
     P.ph[1].nm = 1;
     P.ph[1].K = int(I);
     P.ph[1].x = A.q2;
+    P.ph[1].xperm = 1;
     return launch_mlp(P, A, reinterpret_cast<cudaStream_t>(stream));
 }
 

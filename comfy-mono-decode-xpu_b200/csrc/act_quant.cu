@@ -45,6 +45,9 @@ constexpr int kAqThreads = 256;
 __global__ void __launch_bounds__(kAqThreads) act_quant_kernel(const uint16_t* __restrict__ x, int K,
                                                                int8_t* __restrict__ q, float* __restrict__ xs) {
     __shared__ float red[kAqThreads / 32];
+    // The next kernel may launch right away (its weight prefetch overlaps this one); its own dependency
+    // wait covers this kernel's output. This kernel's wait makes its completion imply the predecessor's.
+    pdl_launch_dependents();
     pdl_wait();
     const int r = blockIdx.x;
     const uint16_t* xr = x + size_t(r) * K;
@@ -79,7 +82,6 @@ __global__ void __launch_bounds__(kAqThreads) act_quant_kernel(const uint16_t* _
         }
         *reinterpret_cast<uint2*>(qr + i) = make_uint2(out[0], out[1]);
     }
-    pdl_launch_dependents();
 }
 
 // ---- REF rot_quant ----------------------------------------------------------------------------------

@@ -21,6 +21,25 @@ extern __device__ int g_device_error;
 
 __device__ __forceinline__ void set_device_error(int code) { atomicCAS(&g_device_error, 0, code); }
 
+// ---- phase trace ------------------------------------------------------------------------------------
+// Off unless mono_trace_enable() set a buffer: thread 0 of every CTA of the traced kernels stores
+// %globaltimer (ns) at each phase boundary into slot [blockIdx.x][phase] of a [kTraceCtas][kTracePhases]
+// table. One global load per stamp when off.
+constexpr int kTracePhases = 16;
+constexpr int kTraceCtas = 1024;
+extern __device__ unsigned long long* g_trace;
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void trace_stamp(int phase) {
+    unsigned long long* tr = g_trace;
+    if (tr != nullptr && threadIdx.x == 0 && blockIdx.x < kTraceCtas && phase < kTracePhases)
+        tr[blockIdx.x * kTracePhases + phase] = globaltimer();
+}
+
 // ---- shared-memory addresses ---------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -120,6 +139,16 @@ __device__ __forceinline__ void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t 
         "{%0,%1,%2,%3};"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// D = A * B (+ 0): the zero accumulator comes from registers the caller keeps zero for the whole kernel
+__device__ __forceinline__ void mma_s8_16832_z(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1, uint32_t z) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(z));
 }
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {

@@ -12,20 +12,25 @@
 // Work: a program of GEMV phases. A phase multiplies the activation rows x [M][K] by up to three
 // matrices that share K, with tiles concatenated (q | k | v), or by a gate/up pair whose tiles are
 // processed together. Tile = 16 output rows; its K is cut into 1024-wide chunks (items). A CTA holds
-// kGroups warp-groups of 4 warps; each warp-group is a virtual CTA that takes tiles round-robin, its
-// warps take a tile's items round-robin, and the chunk partials meet in shared memory where one thread
-// per output sums them in chunk order. Every warp streams its items through a private ring of 2-group
-// stages (2 KB of weights + scales): TMA bulk copies for tile-major weights, cp.async for the
-// checkpoint's row-major weights. The producer cursor walks the warp's stages across all phases, so the
-// next phase's weights are in flight while the CTA waits at a grid barrier. Activations of a phase are
-// staged once per CTA in shared memory (pitch K + 16 bytes: the fragment reads are conflict-free) when
-// they fit, otherwise read from L2.
+// warp-groups of 4 warps; each warp-group is a virtual CTA (interleaved over the SMs) that takes tiles
+// round-robin, its warps take a tile's items round-robin, and the chunk partials meet in shared memory
+// where one thread per output sums them in chunk order.
+//
+// Streaming: one item = 8 KB of weights + its scales, one TMA bulk copy from the tile-major layout
+// (mono_w4_repack: per (tile, chunk) the weights then the scales, contiguous), or 16-byte cp.async
+// pieces from the checkpoint's row-major layout. Every warp owns a 2-deep ring of item stages; its
+// producer cursor walks the warp's items across all phases of the program, so the next phase's weights
+// are in flight while the CTA waits at a grid barrier. (Measured on B200: 8 KB copies, 2 stages, 8 warps
+// per SM stream at ~6.3 TB/s; 2 KB copies plus separate scale copies were capped by the per-copy cost of
+// the TMA unit.) Activations of a phase are staged once per CTA in shared memory by vector loads (pitch
+// K + 16: conflict-free fragment reads) when they fit, else read through L1.
 //
 // mma fragment mapping (swap-AB: weights are the 16-row A operand, activations the 8-column B operand).
 // Inside a 128-group lane (g, t) owns bytes [16t, 16t + 16) of rows g and g + 8, i.e. packed words
 // 4t + s (s = 0..3). At k-step s its word's even nibbles are A columns 4t..4t+3 and its odd nibbles A
 // columns 16 + 4t..; the activation bytes of those columns are x[8(4t + s) + {0,2,4,6}] and
-// x[8(4t + s) + {1,3,5,7}] of the group: 32 contiguous bytes per lane and group.
+// x[8(4t + s) + {1,3,5,7}] of the group: 32 contiguous bytes per lane and group, stored permuted
+// (bytes 0 2 4 6 1 3 5 7 of every 8) so each B register is one 32-bit word.
 #pragma once
 #include "common.cuh"
 
@@ -34,30 +39,29 @@ namespace mono {
 enum W4Format : int { FMT_GPTQ = 0, FMT_REF = 1 };
 enum W4Layout : int { LAYOUT_ROW = 0, LAYOUT_TILED = 1 };
 
-constexpr int kGroupWarps = 4;   // warps per warp-group
-constexpr int kStages = 4;       // ring depth per warp
-constexpr int kStageW = 2048;    // weight bytes per stage (2 groups x 16 rows x 64 B)
-constexpr int kChunkK = 1024;    // K per item
-constexpr int kMaxChunks = 16;   // K <= 16384
+constexpr int kGroupWarps = 4;     // warps per warp-group
+constexpr int kMaxStages = 2;      // deepest ring per warp (item stages)
+constexpr int kStageW = 8192;      // weight bytes per item (8 groups x 16 rows x 64 B)
+constexpr int kChunkK = 1024;      // K per item
+constexpr int kMaxChunks = 16;     // K <= 16384
 constexpr int kMaxPhases = 4;
-constexpr int kXStageMax = 98304;  // largest activation block staged in shared memory (M * K bytes)
 
 template <int FMT>
 struct Fmt;
 template <>
 struct Fmt<FMT_GPTQ> {
-    static constexpr int SB = 64;  // scale bytes per stage: [16 rows][2 groups] fp16
+    static constexpr int SB = 256;  // item scales: [16 rows][8 groups] fp16
 };
 template <>
 struct Fmt<FMT_REF> {
-    static constexpr int SB = 256;  // [16 rows][16 fp8] (2 groups x 8 G16 scales)
+    static constexpr int SB = 1024;  // item scales: [16 rows][8 groups x 8 G16] fp8
 };
 template <int FMT>
 __host__ __device__ constexpr int stage_bytes() { return kStageW + Fmt<FMT>::SB; }
 
 struct MatDesc {
-    const uint8_t* q;  // TILED: [N/16][K/128][2][32][16]; ROW: [N][K/2] bytes (low nibble = even k)
-    const uint8_t* s;  // GPTQ fp16 / REF fp8 scales, TILED [N/16][K/256][16][SB/16] or ROW [N][K/g]
+    const uint8_t* q;  // TILED: [N/16][K/1024][8 KB weights | scales]; ROW: [N][K/2] bytes (low nibble = even k)
+    const uint8_t* s;  // ROW only: GPTQ fp16 [N][K/128] / REF fp8 [N][K/16]
     int n;
 };
 
@@ -66,6 +70,7 @@ struct PhaseDesc {
     int nm, paired, K;
     const int8_t* x;  // activation rows [M][K] (row stride K)
     int xsmem;        // 1: staged in shared memory
+    int xperm;        // 1: x is already in the permuted byte order
 };
 
 struct Program {
@@ -103,84 +108,109 @@ __host__ __device__ inline void resolve(const PhaseDesc& p, int T, int sub, int&
 }
 
 struct Cursor {
-    int ph, ti, it, pair;
+    int ph, ti, it;  // phase, k-th own tile, k-th own item of the tile
+    int sub, chunk;  // item = warp + 4 it -> (subtile, chunk)
     bool done;
 };
 
-// The stage sequence of one warp: virtual CTA vc of nvc, warp `warp` of its group.
+// The item sequence of one warp: virtual CTA vc of nvc, warp `warp` of its group. Per-phase counts are
+// computed from the kernel parameters when needed (no per-phase arrays: those would live in local memory).
 struct Seq {
     int warp, vc, nvc;
-    __device__ int my_tiles(const Program& P, int ph) const {
-        const int t = phase_tiles(P.ph[ph]);
+    const Program* prog;
+    __device__ void init(const Program& P, int warp_, int vc_, int nvc_) {
+        warp = warp_;
+        vc = vc_;
+        nvc = nvc_;
+        prog = &P;
+    }
+    __device__ int my_tiles(int ph) const {
+        const int t = phase_tiles(prog->ph[ph]);
         return vc < t ? (t - 1 - vc) / nvc + 1 : 0;
     }
-    __device__ int my_items(const Program& P, int ph) const {
-        const int it = phase_items(P.ph[ph]);
-        return warp < it ? (it - 1 - warp) / kGroupWarps + 1 : 0;
+    __device__ int my_items(int ph) const {
+        const int it = phase_items(prog->ph[ph]);
+        return warp < it ? ((it - 1 - warp) >> 2) + 1 : 0;
+    }
+    __device__ int chunks(int ph) const { return prog->ph[ph].K >> 10; }
+    __device__ void first_item(Cursor& c) const {
+        const int C = chunks(c.ph);
+        c.chunk = warp;
+        c.sub = 0;
+        while (c.chunk >= C) {
+            c.chunk -= C;
+            ++c.sub;
+        }
     }
     __device__ Cursor start(const Program& P, int ph) const {
-        Cursor c{ph, 0, 0, 0, false};
-        while (c.ph < P.nph && (my_tiles(P, c.ph) == 0 || my_items(P, c.ph) == 0)) ++c.ph;
+        Cursor c{ph, 0, 0, 0, 0, false};
+        while (c.ph < P.nph && (my_tiles(c.ph) == 0 || my_items(c.ph) == 0)) ++c.ph;
         c.done = c.ph >= P.nph;
+        if (!c.done) first_item(c);
         return c;
     }
     __device__ void advance(const Program& P, Cursor& c) const {
-        if (++c.pair < 4) return;
-        c.pair = 0;
-        if (++c.it < my_items(P, c.ph)) return;
+        if (++c.it < my_items(c.ph)) {
+            const int C = chunks(c.ph);
+            c.chunk += kGroupWarps;
+            while (c.chunk >= C) {
+                c.chunk -= C;
+                ++c.sub;
+            }
+            return;
+        }
         c.it = 0;
-        if (++c.ti < my_tiles(P, c.ph)) return;
+        if (++c.ti < my_tiles(c.ph)) {
+            first_item(c);
+            return;
+        }
         c = start(P, c.ph + 1);
     }
 };
 
 template <int FMT, int LAYOUT>
-__device__ __forceinline__ void issue_stage(const Program& P, const Seq& sq, const Cursor& c, uint8_t* stage,
-                                            uint64_t* bar, int lane) {
+__device__ __forceinline__ void issue_item(const Program& P, const Seq& sq, const Cursor& c, uint8_t* stage,
+                                           uint64_t* bar, int lane) {
     constexpr int SB = Fmt<FMT>::SB;
     const PhaseDesc& p = P.ph[c.ph];
     const int T = sq.vc + c.ti * sq.nvc;
-    const int item = sq.warp + c.it * kGroupWarps;
-    const int C = phase_chunks(p);
-    const int sub = item / C, chunk = item - sub * C;
     int mat, lt;
-    resolve(p, T, sub, mat, lt);
+    resolve(p, T, c.sub, mat, lt);
     const MatDesc& w = p.m[mat];
-    const int G = p.K >> 7;
-    const int g0 = chunk * 8 + c.pair * 2;
+    const int C = p.K >> 10;
     if constexpr (LAYOUT == LAYOUT_TILED) {
         if (lane == 0) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            // The slot's previous contents were consumed into registers before the warp's __syncwarp in
+            // Ring::release: the bulk copy may overwrite it without a proxy fence.
             mbar_arrive_expect_tx(bar, kStageW + SB);
-            bulk_g2s(stage, w.q + (size_t(lt) * G + g0) * 1024, kStageW, bar);
-            bulk_g2s(stage + kStageW, w.s + (size_t(lt) * (G >> 1) + (g0 >> 1)) * SB, SB, bar);
+            bulk_g2s(stage, w.q + (size_t(lt) * C + c.chunk) * (kStageW + SB), kStageW + SB, bar);
         }
     } else {
         const int g = lane >> 2, t = lane & 3;
         const size_t rowb = size_t(p.K) >> 1;
-        const uint8_t* r0 = w.q + size_t(lt * 16 + g) * rowb + size_t(g0) * 64 + t * 16;
+        const uint8_t* r0 = w.q + size_t(lt * 16 + g) * rowb + size_t(c.chunk) * 512 + t * 16;
         const uint8_t* r1 = r0 + 8 * rowb;
 #pragma unroll
-        for (int gi = 0; gi < 2; ++gi) {
+        for (int gi = 0; gi < 8; ++gi) {
             cp_async16(stage + gi * 1024 + lane * 16, r0 + gi * 64);
             cp_async16(stage + gi * 1024 + 512 + lane * 16, r1 + gi * 64);
         }
-        if (lane < 16) {
-            const int row = lt * 16 + lane;
-            if constexpr (FMT == FMT_GPTQ) {
-                const uint8_t* s = w.s + (size_t(row) * G + g0) * 2;
-                asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(stage + kStageW + lane * 4)),
-                             "l"(s)
-                             : "memory");
-            } else {
-                cp_async16(stage + kStageW + lane * 16, w.s + size_t(row) * (p.K >> 4) + g0 * 8);
+        if constexpr (FMT == FMT_GPTQ) {
+            // [16 rows][8 groups] fp16: 16 bytes per row
+            if (lane < 16) cp_async16(stage + kStageW + lane * 16, w.s + (size_t(lt * 16 + lane) * (p.K >> 7) + c.chunk * 8) * 2);
+        } else {
+            // [16 rows][64 bytes]: 4 pieces per row, 2 per lane
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int piece = lane + 32 * h, row = piece >> 2, part = piece & 3;
+                cp_async16(stage + kStageW + row * 64 + part * 16, w.s + size_t(lt * 16 + row) * (p.K >> 4) + c.chunk * 64 + part * 16);
             }
         }
         cp_async_commit();
     }
 }
 
-template <int FMT, int LAYOUT>
+template <int FMT, int LAYOUT, int kStages>
 struct Ring {
     uint8_t* buf;
     uint64_t* bars;
@@ -199,8 +229,8 @@ struct Ring {
         ok = true;
         for (int i = 0; i < kStages; ++i) {
             if (!prod.done) {
-                issue_stage<FMT, LAYOUT>(P, sq, prod, buf + (issued % kStages) * stage_bytes<FMT>(),
-                                         &bars[issued % kStages], lane);
+                issue_item<FMT, LAYOUT>(P, sq, prod, buf + (issued % kStages) * stage_bytes<FMT>(), &bars[issued % kStages],
+                                        lane);
                 ++issued;
                 sq.advance(P, prod);
             } else if (LAYOUT == LAYOUT_ROW) {
@@ -223,7 +253,7 @@ struct Ring {
         const int slot = consumed % kStages;
         ++consumed;
         if (!prod.done && ok) {
-            issue_stage<FMT, LAYOUT>(P, sq, prod, buf + slot * stage_bytes<FMT>(), &bars[slot], lane);
+            issue_item<FMT, LAYOUT>(P, sq, prod, buf + slot * stage_bytes<FMT>(), &bars[slot], lane);
             ++issued;
             sq.advance(P, prod);
         } else if (LAYOUT == LAYOUT_ROW) {
@@ -241,6 +271,49 @@ struct Ring {
     }
 };
 
+// ---- L2 prefetch of upcoming tiles ------------------------------------------------------------------
+// A warp-group's tiles in a tile-major layout are contiguous runs (all chunk items of a 16-row tile, for
+// each subtile). Lane 0 of the group's first warp keeps kPrefetchTiles tiles requested into L2 ahead of the
+// tile being consumed, across phase boundaries, so HBM keeps streaming through row phases and grid
+// barriers (the role of the reference's prefetch_stream, csrc/mono_common.hpp:318-340).
+constexpr int kPrefetchTiles = 2;
+
+struct TileCursor {
+    int ph, ti;
+    bool done;
+};
+
+__device__ __forceinline__ TileCursor tile_start(const Program& P, const Seq& sq, int ph) {
+    TileCursor c{ph, 0, false};
+    while (c.ph < P.nph && sq.my_tiles(c.ph) == 0) ++c.ph;
+    c.done = c.ph >= P.nph;
+    return c;
+}
+__device__ __forceinline__ void tile_advance(const Program& P, const Seq& sq, TileCursor& c) {
+    if (++c.ti < sq.my_tiles(c.ph)) return;
+    c = tile_start(P, sq, c.ph + 1);
+}
+template <int FMT>
+__device__ __forceinline__ void prefetch_tile(const Program& P, const Seq& sq, const TileCursor& c) {
+    const PhaseDesc& p = P.ph[c.ph];
+    const int T = sq.vc + c.ti * sq.nvc, C = p.K >> 10;
+    const uint32_t bytes = uint32_t(C) * stage_bytes<FMT>();
+    for (int sub = 0; sub < (p.paired ? 2 : 1); ++sub) {
+        int mat, lt;
+        resolve(p, T, sub, mat, lt);
+        bulk_prefetch_l2(p.m[mat].q + size_t(lt) * bytes, bytes);
+    }
+}
+// Called by the group's lane 0 (tiled layouts only): at kernel start with `first` = true (requests the
+// first kPrefetchTiles tiles), then once per consumed tile (requests one more).
+template <int FMT>
+__device__ __forceinline__ void prefetch_ahead(const Program& P, const Seq& sq, TileCursor& c, bool first) {
+    for (int i = 0; i < (first ? kPrefetchTiles : 1) && !c.done; ++i) {
+        prefetch_tile<FMT>(P, sq, c);
+        tile_advance(P, sq, c);
+    }
+}
+
 // REF decode of one packed word (8 codes sharing one fp8 scale byte) into the even / odd A registers.
 __device__ __forceinline__ void ref_decode(const uint16_t* __restrict__ tab, uint32_t word, uint32_t sb,
                                            uint32_t& even, uint32_t& odd) {
@@ -252,17 +325,18 @@ __device__ __forceinline__ void ref_decode(const uint16_t* __restrict__ tab, uin
     odd = prmt(r01, r23, 0x7531);
 }
 
-// Activation source of a phase: shared (pitch K + 16) or global (pitch K).
+// Activation source of a phase: shared (pitch K + 16) or global through L1 (pitch K); perm: permuted bytes.
 struct XSrc {
     const int8_t* p;
     int pitch;
-    bool smem;
+    bool smem, perm;
 };
 
-// Consume one item (4 stages = 8 groups). R = the chunk partial per fragment element: fp32 bits (GPTQ)
-// or the int32 dot (REF). Fragment element i of m-tile mt: (row g + 8 (i >> 1), activation 2t + (i & 1)).
-template <int FMT, int LAYOUT, int MT>
-__device__ __forceinline__ void consume_item(Ring<FMT, LAYOUT>& r, const Program& P, const Seq& sq, const XSrc& xs,
+// Consume one item (8 groups). R = the chunk partial per fragment element: fp32 bits (GPTQ, carrying a
+// factor 16, see below) or the int32 dot (REF). Fragment element i of m-tile mt: (row g + 8 (i >> 1),
+// activation 2t + (i & 1)).
+template <int FMT, int LAYOUT, int MT, int ST>
+__device__ __forceinline__ void consume_item(Ring<FMT, LAYOUT, ST>& r, const Program& P, const Seq& sq, const XSrc& xs,
                                              int M, int chunk, int lane, uint32_t (&R)[MT][4]) {
     const int g = lane >> 2, t = lane & 3;
     float F[MT][4];
@@ -274,84 +348,94 @@ __device__ __forceinline__ void consume_item(Ring<FMT, LAYOUT>& r, const Program
             F[mt][i] = 0.f;
             A[mt][i] = 0;
         }
-    for (int pair = 0; pair < 4; ++pair) {
-        uint8_t* stage = r.wait();
+    uint8_t* stage = r.wait();
+    // GPTQ item scales: [16 rows][8 groups] fp16
+    const __half* sc16 = reinterpret_cast<const __half*>(stage + kStageW);
+    const uint32_t zero = 0;
+    const int8_t* xrow[MT];
 #pragma unroll
-        for (int gi = 0; gi < 2; ++gi) {
-            const int grp = chunk * 8 + pair * 2 + gi;
-            const uint4 wa = lds_v4(stage + gi * 1024 + lane * 16);
-            const uint4 wb = lds_v4(stage + gi * 1024 + 512 + lane * 16);
-            const uint32_t wA[4] = {wa.x, wa.y, wa.z, wa.w}, wB[4] = {wb.x, wb.y, wb.z, wb.w};
-            uint4 xv[MT][2];
+    for (int mt = 0; mt < MT; ++mt) xrow[mt] = xs.p + size_t(g + 8 * mt) * xs.pitch + chunk * kChunkK + 32 * t;
+#pragma unroll 2
+    for (int gi = 0; gi < 8; ++gi) {
+        const uint4 wa = lds_v4(stage + gi * 1024 + lane * 16);
+        const uint4 wb = lds_v4(stage + gi * 1024 + 512 + lane * 16);
+        const uint32_t wA[4] = {wa.x, wa.y, wa.z, wa.w}, wB[4] = {wb.x, wb.y, wb.z, wb.w};
+        uint4 xv[MT][2];
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+            if (g + 8 * mt < M) {
+                const int8_t* xr = xrow[mt] + gi * 128;
+                if (xs.smem) {
+                    xv[mt][0] = lds_v4(xr);
+                    xv[mt][1] = lds_v4(xr + 16);
+                } else {
+                    xv[mt][0] = __ldg(reinterpret_cast<const uint4*>(xr));
+                    xv[mt][1] = __ldg(reinterpret_cast<const uint4*>(xr + 16));
+                }
+            } else {
+                xv[mt][0] = make_uint4(0, 0, 0, 0);
+                xv[mt][1] = make_uint4(0, 0, 0, 0);
+            }
+        }
+        uint32_t sbA = 0, sbB = 0;
+        if constexpr (FMT == FMT_REF) {
+            const uint8_t* sc = stage + kStageW;
+            sbA = *reinterpret_cast<const uint16_t*>(sc + g * 64 + gi * 8 + 2 * t);
+            sbB = *reinterpret_cast<const uint16_t*>(sc + (g + 8) * 64 + gi * 8 + 2 * t);
+        }
+        // two mma chains of depth 2 (k-steps 0,1 and 2,3), each started from the zero register
+        int c0[MT][4], c1[MT][4];
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            uint32_t a0, a1, a2, a3;
+            if constexpr (FMT == FMT_GPTQ) {
+                // two's complement nibbles (tile-major copies are re-coded by the repack; row-major
+                // nibbles v + 8 are re-coded here) moved into the high half of each byte: 16 * v
+                const uint32_t xa = LAYOUT == LAYOUT_ROW ? (wA[s] ^ 0x88888888u) : wA[s];
+                const uint32_t xb = LAYOUT == LAYOUT_ROW ? (wB[s] ^ 0x88888888u) : wB[s];
+                a0 = (xa << 4) & 0xF0F0F0F0u;
+                a1 = (xb << 4) & 0xF0F0F0F0u;
+                a2 = xa & 0xF0F0F0F0u;
+                a3 = xb & 0xF0F0F0F0u;
+            } else {
+                ref_decode(P.pair_tab, wA[s], (sbA >> (8 * (s >> 1))) & 0xFF, a0, a2);
+                ref_decode(P.pair_tab, wB[s], (sbB >> (8 * (s >> 1))) & 0xFF, a1, a3);
+            }
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) {
-                const int m = g + 8 * mt;
-                if (m < M) {
-                    const int8_t* xr = xs.p + size_t(m) * xs.pitch + grp * 128 + 32 * t;
-                    if (xs.smem) {
-                        xv[mt][0] = lds_v4(xr);
-                        xv[mt][1] = lds_v4(xr + 16);
-                    } else {
-                        xv[mt][0] = __ldcg(reinterpret_cast<const uint4*>(xr));
-                        xv[mt][1] = __ldcg(reinterpret_cast<const uint4*>(xr + 16));
-                    }
-                } else {
-                    xv[mt][0] = make_uint4(0, 0, 0, 0);
-                    xv[mt][1] = make_uint4(0, 0, 0, 0);
+                uint32_t b0 = (s < 2) ? (s == 0 ? xv[mt][0].x : xv[mt][0].z) : (s == 2 ? xv[mt][1].x : xv[mt][1].z);
+                uint32_t b1 = (s < 2) ? (s == 0 ? xv[mt][0].y : xv[mt][0].w) : (s == 2 ? xv[mt][1].y : xv[mt][1].w);
+                if (!xs.perm) {
+                    const uint32_t lo = b0, hi = b1;
+                    b0 = prmt(lo, hi, 0x6420);
+                    b1 = prmt(lo, hi, 0x7531);
                 }
+                int(&c)[4] = (s < 2) ? c0[mt] : c1[mt];
+                if ((s & 1) == 0)
+                    mma_s8_16832_z(c, a0, a1, a2, a3, b0, b1, zero);
+                else
+                    mma_s8_16832(c, a0, a1, a2, a3, b0, b1);
             }
-            int acc[MT][4];
+        }
+        if constexpr (FMT == FMT_GPTQ) {
+            const float sa = __half2float(sc16[g * 8 + gi]), sb = __half2float(sc16[(g + 8) * 8 + gi]);
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                // The dots carry the factor 16 of the shifted nibbles, and so do these products and sums:
+                // scaling by 16 is exact in every step (|acc| < 2^21, no overflow, no subnormal), so the
+                // partial is 16 * F bit for bit; tile_total() removes the factor.
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    F[mt][i] = __fadd_rn(F[mt][i], __fmul_rn(__int2float_rn(c0[mt][i] + c1[mt][i]), i < 2 ? sa : sb));
+            }
+        } else {
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-                for (int i = 0; i < 4; ++i) acc[mt][i] = 0;
-            uint32_t sbA = 0, sbB = 0;
-            if constexpr (FMT == FMT_REF) {
-                const uint8_t* sc = stage + kStageW;
-                sbA = *reinterpret_cast<const uint16_t*>(sc + g * 16 + gi * 8 + 2 * t);
-                sbB = *reinterpret_cast<const uint16_t*>(sc + (g + 8) * 16 + gi * 8 + 2 * t);
-            }
-#pragma unroll
-            for (int s = 0; s < 4; ++s) {
-                uint32_t a0, a1, a2, a3;
-                if constexpr (FMT == FMT_GPTQ) {
-                    // two's complement nibbles (tile-major copies are re-coded by the repack; row-major
-                    // nibbles v + 8 are re-coded here) moved into the high half of each byte: 16 * v
-                    const uint32_t xa = LAYOUT == LAYOUT_ROW ? (wA[s] ^ 0x88888888u) : wA[s];
-                    const uint32_t xb = LAYOUT == LAYOUT_ROW ? (wB[s] ^ 0x88888888u) : wB[s];
-                    a0 = (xa << 4) & 0xF0F0F0F0u;
-                    a1 = (xb << 4) & 0xF0F0F0F0u;
-                    a2 = xa & 0xF0F0F0F0u;
-                    a3 = xb & 0xF0F0F0F0u;
-                } else {
-                    ref_decode(P.pair_tab, wA[s], (sbA >> (8 * (s >> 1))) & 0xFF, a0, a2);
-                    ref_decode(P.pair_tab, wB[s], (sbB >> (8 * (s >> 1))) & 0xFF, a1, a3);
-                }
-#pragma unroll
-                for (int mt = 0; mt < MT; ++mt) {
-                    const uint32_t lo = (s < 2) ? (s == 0 ? xv[mt][0].x : xv[mt][0].z) : (s == 2 ? xv[mt][1].x : xv[mt][1].z);
-                    const uint32_t hi = (s < 2) ? (s == 0 ? xv[mt][0].y : xv[mt][0].w) : (s == 2 ? xv[mt][1].y : xv[mt][1].w);
-                    if constexpr (FMT == FMT_GPTQ)
-                        mma_s8_16832(acc[mt], a0, a1, a2, a3, prmt(lo, hi, 0x6420), prmt(lo, hi, 0x7531));
-                    else
-                        mma_s8_16832(A[mt], a0, a1, a2, a3, prmt(lo, hi, 0x6420), prmt(lo, hi, 0x7531));
-                }
-            }
-            if constexpr (FMT == FMT_GPTQ) {
-                const __half* sc = reinterpret_cast<const __half*>(stage + kStageW);
-                const float sa = __half2float(sc[g * 2 + gi]), sb = __half2float(sc[(g + 8) * 2 + gi]);
-#pragma unroll
-                for (int mt = 0; mt < MT; ++mt) {
-                    // the int32 dots carry the factor 16 of the shifted nibbles: exact >> 4
-                    F[mt][0] = __fadd_rn(F[mt][0], __fmul_rn(__int2float_rn(acc[mt][0] >> 4), sa));
-                    F[mt][1] = __fadd_rn(F[mt][1], __fmul_rn(__int2float_rn(acc[mt][1] >> 4), sa));
-                    F[mt][2] = __fadd_rn(F[mt][2], __fmul_rn(__int2float_rn(acc[mt][2] >> 4), sb));
-                    F[mt][3] = __fadd_rn(F[mt][3], __fmul_rn(__int2float_rn(acc[mt][3] >> 4), sb));
-                }
-            }
+                for (int i = 0; i < 4; ++i) A[mt][i] += c0[mt][i] + c1[mt][i];
         }
-        r.release(P, sq, lane);
     }
+    r.release(P, sq, lane);
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -373,13 +457,14 @@ __device__ __forceinline__ void store_partial(uint32_t* part, int item, int lane
     }
 }
 
-// Total of subtile `sub` at (m, nl) over the C chunk partials, in chunk order.
+// Total of subtile `sub` at (m, nl) over the C chunk partials, in chunk order (GPTQ: the factor 16 of the
+// partials is removed exactly at the end).
 template <int FMT, int MT>
 __device__ __forceinline__ uint32_t tile_total(const uint32_t* part, int C, int sub, int m, int nl) {
     if constexpr (FMT == FMT_GPTQ) {
         float tot = 0.f;
         for (int c = 0; c < C; ++c) tot = __fadd_rn(tot, __uint_as_float(part[(sub * C + c) * (MT * 128) + m * 16 + nl]));
-        return __float_as_uint(tot);
+        return __float_as_uint(__fmul_rn(tot, 0.0625f));
     } else {
         uint32_t tot = 0;
         for (int c = 0; c < C; ++c) tot += part[(sub * C + c) * (MT * 128) + m * 16 + nl];
@@ -391,22 +476,43 @@ __device__ __forceinline__ void group_sync(int wg) {
     asm volatile("bar.sync %0, %1;" ::"r"(1 + wg), "r"(kGroupWarps * 32) : "memory");
 }
 
-// Stage the activation block x [M][K] of a phase into shared memory (pitch K + 16): one bulk copy per row.
-__device__ __forceinline__ void stage_x(const PhaseDesc& p, int M, int8_t* xsm, uint64_t* xbar) {
+// Stage the activation block x [M][K] of a phase into shared memory (pitch K + 16): thread 0 issues one
+// TMA bulk copy per row (measured on B200: 8 row copies stage 96 KB from L2 in ~1 us, about twice as fast
+// as vector loads by 256 threads); every thread waits (bounded) on xbar with the given parity, then the
+// bytes are permuted in place unless x is permuted already. Returns false if the wait gave up.
+// CTA-uniform result (the callers' tile loops hold warp-group barriers).
+__device__ __forceinline__ bool stage_x(const PhaseDesc& p, int M, int8_t* xsm, uint64_t* xbar, int parity) {
     if (threadIdx.x == 0) {
+        // earlier generic accesses of the buffer (fragment reads, the permutation) before the async writes
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("fence.proxy.async.global;" ::: "memory");
         mbar_arrive_expect_tx(xbar, uint32_t(M) * p.K);
-        for (int m = 0; m < M; ++m) bulk_g2s(xsm + size_t(m) * (p.K + 16), p.x + size_t(m) * p.K, p.K, xbar);
+        for (int i = 0; i < M; ++i) {
+            const int m = (i + int(blockIdx.x)) % M;  // CTAs start at different rows
+            bulk_g2s(xsm + size_t(m) * (p.K + 16), p.x + size_t(m) * p.K, p.K, xbar);
+        }
     }
+    const bool ok = __syncthreads_and(mbar_wait(xbar, parity));
+    if (!p.xperm) {
+        const int words = p.K >> 4, total = M * words;  // 16-byte pieces
+        for (int i = threadIdx.x; i < total; i += blockDim.x) {
+            const int m = i / words, c = i - m * words;
+            uint4* q = reinterpret_cast<uint4*>(xsm + size_t(m) * (p.K + 16)) + c;
+            const uint4 v = *q;
+            *q = make_uint4(prmt(v.x, v.y, 0x6420), prmt(v.x, v.y, 0x7531), prmt(v.z, v.w, 0x6420), prmt(v.z, v.w, 0x7531));
+        }
+        __syncthreads();
+    }
+    return ok;
 }
 
-// Shared-memory plan of an engine kernel (bytes): rings, ring barriers, the x barrier, partials, x.
+// Shared-memory plan of an engine kernel (bytes): rings, ring barriers, partials, staged activations.
 template <int FMT, int MT>
 struct SmemPlan {
     size_t rings, bars, part, x, total;
-    __host__ __device__ SmemPlan(int groups, int max_items, int x_bytes) {
-        rings = size_t(groups) * kGroupWarps * kStages * stage_bytes<FMT>();
-        bars = size_t(groups) * kGroupWarps * kStages * 8 + 16;
+    __host__ __device__ SmemPlan(int groups, int stages, int max_items, int x_bytes) {
+        rings = size_t(groups) * kGroupWarps * stages * stage_bytes<FMT>();
+        bars = (size_t(groups) * kGroupWarps * stages * 8 + 8 + 127) / 128 * 128;  // ring barriers + xbar
         part = size_t(groups) * 2 * max_items * MT * 128 * 4;
         x = size_t(x_bytes + 127) / 128 * 128;
         total = rings + bars + part + x;

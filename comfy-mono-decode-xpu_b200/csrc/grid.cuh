@@ -22,8 +22,9 @@ __device__ __forceinline__ bool grid_barrier(unsigned* counter, unsigned& epoch,
     ++epoch;
     if (threadIdx.x == 0) {
         const unsigned target = epoch * gridDim.x;
-        __threadfence();
-        atomicAdd(counter, 1u);
+        // one release-add publishes this CTA's writes (ordered by the __syncthreads above); the polls
+        // acquire the other CTAs' writes
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
         bool ok = true;
         uint32_t spins = 0;
         while (ld_acquire_gpu(counter) < target) {
@@ -32,7 +33,6 @@ __device__ __forceinline__ bool grid_barrier(unsigned* counter, unsigned& epoch,
                 ok = false;
                 break;
             }
-            __nanosleep(32);
         }
         *flag = ok;
     }

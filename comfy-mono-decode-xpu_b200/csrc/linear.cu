@@ -1,6 +1,7 @@
 // Standalone W4A8 linear (GPTQ or REF, row-major or tile-major weights) on the stream engine.
 //   GPTQ: out = cast(total * x_scale[m]);   REF: out = cast(float(acc) * x_scale[m] * s_channel[n])
 //   residual: out = cast(float(residual) + float(cast(f)))  (csrc/w4a8_decode.sycl:155-160)
+#include <cstdlib>
 #include <mutex>
 
 #include "abi_internal.h"
@@ -17,46 +18,58 @@ struct LinearEpi {
     int max_items;
 };
 
-template <int FMT, int LAYOUT, int MT, int GROUPS>
-__global__ void __launch_bounds__(GROUPS * 128) linear_kernel(const Program P, const LinearEpi E) {
+template <int FMT, int LAYOUT, int MT, int GROUPS, int ST>
+__global__ void __launch_bounds__(GROUPS * 128, GROUPS == 1 ? 2 : 1) linear_kernel(const Program P, const LinearEpi E) {
     extern __shared__ __align__(128) uint8_t smem[];
     const PhaseDesc& ph = P.ph[0];
     const int wg = threadIdx.x >> 7, tig = threadIdx.x & 127, warp = tig >> 5, lane = threadIdx.x & 31;
     const int M = P.M, K = ph.K, C = phase_chunks(ph), items = phase_items(ph);
-    const SmemPlan<FMT, MT> plan(GROUPS, E.max_items, ph.xsmem ? M * (K + 16) : 0);
+    const SmemPlan<FMT, MT> plan(GROUPS, ST, E.max_items, ph.xsmem ? M * (K + 16) : 0);
     constexpr int SBY = stage_bytes<FMT>();
     const int wid = wg * kGroupWarps + warp;
     uint64_t* bar_base = reinterpret_cast<uint64_t*>(smem + plan.rings);
-    uint64_t* xbar = bar_base + GROUPS * kGroupWarps * kStages;
+    uint64_t* xbar = bar_base + GROUPS * kGroupWarps * ST;
     uint32_t* part = reinterpret_cast<uint32_t*>(smem + plan.rings + plan.bars) + wg * 2 * E.max_items * MT * 128;
     int8_t* xsm = reinterpret_cast<int8_t*>(smem + plan.rings + plan.bars + plan.part);
 
-    Ring<FMT, LAYOUT> ring;
-    ring.buf = smem + size_t(wid) * kStages * SBY;
-    ring.bars = bar_base + wid * kStages;
-    const Seq sq{warp, int(blockIdx.x) * GROUPS + wg, int(gridDim.x) * GROUPS};
-    if (threadIdx.x == 0 && ph.xsmem) {
+    Ring<FMT, LAYOUT, ST> ring;
+    ring.buf = smem + size_t(wid) * ST * SBY;
+    ring.bars = bar_base + wid * ST;
+    Seq sq;
+    sq.init(P, warp, wg * int(gridDim.x) + int(blockIdx.x), int(gridDim.x) * GROUPS);
+    if (threadIdx.x == 0) {
         mbar_init(xbar, 1);
         fence_mbar_init();
     }
     __syncthreads();
+    trace_stamp(0);
     // weights do not depend on the preceding kernel: stream them before the dependency wait
+    TileCursor pf = tile_start(P, sq, 0);
+    const bool pf_lane = LAYOUT == LAYOUT_TILED && tig == 0;
+    if (pf_lane) {
+        tile_advance(P, sq, pf);  // the first tile is in the rings
+        prefetch_ahead<FMT>(P, sq, pf, true);
+    }
     ring.init(P, sq, lane);
+    // let the next kernel in the stream launch now: its CTAs take SMs as ours exit and start streaming
+    // their weights; its dependency wait still covers all of this kernel's memory effects
+    pdl_launch_dependents();
     pdl_wait();
-    XSrc xs{ph.x, K, false};
+    XSrc xs{ph.x, K, false, ph.xperm != 0};
     bool ok = true;
     if (ph.xsmem) {
-        stage_x(ph, M, xsm, xbar);
-        ok = __syncthreads_and(mbar_wait(xbar, 0));  // uniform: the tile loop holds warp-group barriers
-        xs = XSrc{xsm, K + 16, true};
+        ok = stage_x(ph, M, xsm, xbar, 0);
+        xs = XSrc{xsm, K + 16, true, true};
     }
-    const int ntiles = sq.my_tiles(P, 0);
+    trace_stamp(1);
+    const int ntiles = sq.my_tiles(0);
     for (int ti = 0; ti < ntiles && ok; ++ti) {
         const int T = sq.vc + ti * sq.nvc;
         uint32_t* pt = part + (ti & 1) * E.max_items * MT * 128;
+        if (pf_lane) prefetch_ahead<FMT>(P, sq, pf, false);
         for (int item = warp; item < items; item += kGroupWarps) {
             uint32_t R[MT][4];
-            consume_item<FMT, LAYOUT, MT>(ring, P, sq, xs, M, item % C, lane, R);
+            consume_item<FMT, LAYOUT, MT, ST>(ring, P, sq, xs, M, item % C, lane, R);
             store_partial<MT>(pt, item, lane, R);
         }
         group_sync(wg);
@@ -84,13 +97,13 @@ __global__ void __launch_bounds__(GROUPS * 128) linear_kernel(const Program P, c
             }
         }
     }
+    trace_stamp(2);
     ring.drain(lane);
-    pdl_launch_dependents();
 }
 
-template <int FMT, int LAYOUT, int MT, int GROUPS>
-static int launch_linear_t(const Program& P, const LinearEpi& E, size_t smem, cudaStream_t stream) {
-    auto kern = linear_kernel<FMT, LAYOUT, MT, GROUPS>;
+template <int FMT, int LAYOUT, int MT, int GROUPS, int ST>
+static int launch_linear_t(const Program& P, const LinearEpi& E, size_t smem, int ctas_per_sm, cudaStream_t stream) {
+    auto kern = linear_kernel<FMT, LAYOUT, MT, GROUPS, ST>;
     static std::mutex mu;
     static size_t opt_in = 0;
     {
@@ -102,7 +115,8 @@ static int launch_linear_t(const Program& P, const LinearEpi& E, size_t smem, cu
     }
     const int tiles = phase_tiles(P.ph[0]);
     const int vctas = (tiles + GROUPS - 1) / GROUPS;
-    const int grid = vctas < sm_count() ? vctas : sm_count();
+    const int slots = sm_count() * ctas_per_sm;
+    const int grid = vctas < slots ? vctas : slots;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(GROUPS * 128);
@@ -117,19 +131,36 @@ static int launch_linear_t(const Program& P, const LinearEpi& E, size_t smem, cu
     return MONO_OK;
 }
 
-constexpr size_t kSmemLimit = 227 * 1024;
+constexpr size_t kSmemLimit = 227 * 1024;     // one CTA per SM
+constexpr size_t kSmemHalf = 113 * 1024;      // two CTAs per SM (the next kernel's CTAs can co-reside)
+
+// Launch plans (warp-groups x ring depth per warp): 16 warps with single-stage rings (the most compute
+// in flight), 8 warps with 2-stage rings, or 2 CTAs of 4 warps per SM (the next kernel's CTAs can then
+// co-reside). MONO_B200_PLAN=a|b|c forces one (for measurements); the default takes the first that fits.
+static char plan_override() {
+    static char c = [] {
+        const char* v = getenv("MONO_B200_PLAN");
+        return (v && (v[0] == 'a' || v[0] == 'b' || v[0] == 'c')) ? v[0] : '0';
+    }();
+    return c;
+}
 
 template <int FMT, int LAYOUT, int MT>
 static int launch_linear_mt(Program& P, LinearEpi& E, cudaStream_t stream) {
     PhaseDesc& ph = P.ph[0];
     E.max_items = phase_items(ph);
-    ph.xsmem = P.M * ph.K <= kXStageMax;
-    for (int attempt = 0; attempt < 2; ++attempt) {
-        const int xb = ph.xsmem ? P.M * (ph.K + 16) : 0;
-        const SmemPlan<FMT, MT> p4(4, E.max_items, xb), p2(2, E.max_items, xb);
-        if (p4.total <= kSmemLimit) return launch_linear_t<FMT, LAYOUT, MT, 4>(P, E, p4.total, stream);
-        if (p2.total <= kSmemLimit) return launch_linear_t<FMT, LAYOUT, MT, 2>(P, E, p2.total, stream);
-        ph.xsmem = 0;  // activations too large to stage next to the rings: read them from L2
+    const char force = plan_override();
+    for (int staged = 1; staged >= 0; --staged) {
+        ph.xsmem = staged;
+        const int xb = staged ? P.M * (ph.K + 16) : 0;
+        const SmemPlan<FMT, MT> pa(4, 1, E.max_items, xb), pb(2, 2, E.max_items, xb), pc(1, 2, E.max_items, xb);
+        if constexpr (MT == 1)  // (two m-tiles need more than the 128 registers a 16-warp CTA allows)
+            if ((force == '0' || force == 'a') && pa.total <= kSmemLimit)
+                return launch_linear_t<FMT, LAYOUT, MT, 4, 1>(P, E, pa.total, 1, stream);
+        if ((force == '0' || force == 'b') && pb.total <= kSmemLimit)
+            return launch_linear_t<FMT, LAYOUT, MT, 2, 2>(P, E, pb.total, 1, stream);
+        if ((force == '0' || force == 'c') && pc.total <= kSmemHalf)
+            return launch_linear_t<FMT, LAYOUT, MT, 1, 2>(P, E, pc.total, 2, stream);
     }
     return fail(MONO_EINVAL, "w4a8 linear: no shared-memory plan fits (M=%d K=%d)", P.M, ph.K);
 }

@@ -35,7 +35,7 @@ struct MlpArgs {
     unsigned* bar;    // [2] grid barrier words (zero between launches)
 };
 
-template <int MT, int GROUPS>
+template <int MT, int GROUPS, int ST>
 __global__ void __launch_bounds__(GROUPS * 128) mlp_kernel(const Program P, const MlpArgs A) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float red[GROUPS][16];
@@ -45,64 +45,71 @@ __global__ void __launch_bounds__(GROUPS * 128) mlp_kernel(const Program P, cons
     int xbytes = 0;
     for (int i = 0; i < P.nph; ++i)
         if (P.ph[i].xsmem && M * (P.ph[i].K + 16) > xbytes) xbytes = M * (P.ph[i].K + 16);
-    const SmemPlan<FMT_GPTQ, MT> plan(GROUPS, A.max_items, xbytes);
+    const SmemPlan<FMT_GPTQ, MT> plan(GROUPS, ST, A.max_items, xbytes);
     constexpr int SBY = stage_bytes<FMT_GPTQ>();
     const int wid = wg * kGroupWarps + warp;
     uint64_t* bar_base = reinterpret_cast<uint64_t*>(smem + plan.rings);
-    uint64_t* xbar = bar_base + GROUPS * kGroupWarps * kStages;
+    uint64_t* xbar = bar_base + GROUPS * kGroupWarps * ST;
     uint32_t* part = reinterpret_cast<uint32_t*>(smem + plan.rings + plan.bars) + wg * 2 * A.max_items * MT * 128;
     int8_t* xsm = reinterpret_cast<int8_t*>(smem + plan.rings + plan.bars + plan.part);
 
-    Ring<FMT_GPTQ, LAYOUT_TILED> ring;
-    ring.buf = smem + size_t(wid) * kStages * SBY;
-    ring.bars = bar_base + wid * kStages;
-    const Seq sq{warp, int(blockIdx.x) * GROUPS + wg, int(gridDim.x) * GROUPS};
+    Ring<FMT_GPTQ, LAYOUT_TILED, ST> ring;
+    ring.buf = smem + size_t(wid) * ST * SBY;
+    ring.bars = bar_base + wid * ST;
+    Seq sq;
+    sq.init(P, warp, wg * int(gridDim.x) + int(blockIdx.x), int(gridDim.x) * GROUPS);
     if (threadIdx.x == 0) {
         mbar_init(xbar, 1);
         fence_mbar_init();
     }
     __syncthreads();
+    trace_stamp(0);
+    TileCursor pf = tile_start(P, sq, 0);
+    const bool pf_lane = tig == 0;
+    if (pf_lane) {
+        tile_advance(P, sq, pf);  // the first tile is in the rings
+        prefetch_ahead<FMT_GPTQ>(P, sq, pf, true);
+    }
     ring.init(P, sq, lane);
+    pdl_launch_dependents();  // the next kernel may launch and stream its weights as our CTAs exit
     pdl_wait();
+    trace_stamp(1);
     unsigned epoch = 0;
     bool ok = true;
 
     // ---- P1: norm + quant of the rows (one warp-group per row) ----
     if (blockIdx.x == 0 && threadIdx.x < 16) A.amax2[threadIdx.x] = 0u;
-    for (int m = sq.vc; m < M; m += sq.nvc) {
-        const uint16_t* src = A.x + size_t(m) * A.H;
-        if (A.norm_w) {
-            rmsnorm_row(src, A.norm_w, A.xn + size_t(m) * A.H, A.H, A.eps, red[wg], tig, wg);
-            src = A.xn + size_t(m) * A.H;
-        }
-        quant_row(src, A.H, A.q1 + size_t(m) * A.H, A.s1 + m, red[wg], tig, wg);
-    }
+    for (int m = sq.vc; m < M; m += sq.nvc)
+        norm_quant_row(A.x + size_t(m) * A.H, A.norm_w, A.eps, A.H, nullptr, A.q1 + size_t(m) * A.H, A.s1 + m, red[wg],
+                       tig, wg);
+    trace_stamp(2);
     ok = grid_barrier(A.bar, epoch, &flag);
+    trace_stamp(3);
 
-    // ---- P2: gate / up, h = silu(g) * u ----
     int xpar = 0;
     auto phase_x = [&](int ph) {
         const PhaseDesc& p = P.ph[ph];
-        if (!p.xsmem) return XSrc{p.x, p.K, false};
-        if (threadIdx.x == 0) asm volatile("fence.proxy.async.global;" ::: "memory");
-        stage_x(p, M, xsm, xbar);
-        // uniform over the CTA: the tile loops hold warp-group barriers
-        ok = __syncthreads_and(mbar_wait(xbar, xpar) && ok);
+        if (!p.xsmem) return XSrc{p.x, p.K, false, true};
+        ok = stage_x(p, M, xsm, xbar, xpar) && ok;
         xpar ^= 1;
-        return XSrc{xsm, p.K + 16, true};
+        return XSrc{xsm, p.K + 16, true, true};
     };
+
+    // ---- P2: gate / up, h = silu(g) * u ----
     {
         const XSrc xs = phase_x(0);
+        trace_stamp(4);
         const PhaseDesc& ph = P.ph[0];
         const int C = phase_chunks(ph), items = phase_items(ph);
         float rmax0 = 0.f, rmax1 = 0.f;  // running |h| max of rows tig >> 4 and (tig >> 4) + 8
-        const int ntiles = sq.my_tiles(P, 0);
+        const int ntiles = sq.my_tiles(0);
         for (int ti = 0; ti < ntiles && ok; ++ti) {
             const int T = sq.vc + ti * sq.nvc;
             uint32_t* pt = part + (ti & 1) * A.max_items * MT * 128;
+            if (pf_lane) prefetch_ahead<FMT_GPTQ>(P, sq, pf, false);
             for (int item = warp; item < items; item += kGroupWarps) {
                 uint32_t R[MT][4];
-                consume_item<FMT_GPTQ, LAYOUT_TILED, MT>(ring, P, sq, xs, M, item % C, lane, R);
+                consume_item<FMT_GPTQ, LAYOUT_TILED, MT, ST>(ring, P, sq, xs, M, item % C, lane, R);
                 store_partial<MT>(pt, item, lane, R);
             }
             group_sync(wg);
@@ -131,33 +138,45 @@ __global__ void __launch_bounds__(GROUPS * 128) mlp_kernel(const Program P, cons
             if (m + 8 < M) atomicMax(A.amax2 + m + 8, __float_as_uint(rmax1));
         }
     }
+    trace_stamp(5);
     ok = grid_barrier(A.bar, epoch, &flag) && ok;
+    trace_stamp(6);
 
     // ---- P3: q2 = quant(h) ----
     {
-        const size_t total = size_t(M) * A.I;
-        const size_t stride = size_t(gridDim.x) * blockDim.x;
-        for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
-            const int m = int(i / A.I);
+        // 8-element pieces: one 16-byte load of h, one 8-byte store of permuted q2
+        const int ppr = A.I >> 3, pieces = M * ppr;
+        const int stride = int(gridDim.x * blockDim.x);
+        for (int i = int(blockIdx.x * blockDim.x + threadIdx.x); i < pieces; i += stride) {
+            const int m = i / ppr;
             const float s = __fdiv_rn(__uint_as_float(__ldcg(A.amax2 + m)), 127.f);
-            A.q2[i] = quant_one(bf16_bits_to_f32(__ldcg(A.h + i)), s);
+            const uint4 hv = __ldcg(reinterpret_cast<const uint4*>(A.h) + i);
+            const uint32_t u[4] = {hv.x, hv.y, hv.z, hv.w};
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = __uint_as_float((e & 1) ? (u[e >> 1] & 0xFFFF0000u) : (u[e >> 1] << 16));
+            reinterpret_cast<uint2*>(A.q2)[i] = quant8_perm(v, s);
         }
         if (blockIdx.x == 0 && threadIdx.x < M) A.s2[threadIdx.x] = __fdiv_rn(__uint_as_float(__ldcg(A.amax2 + threadIdx.x)), 127.f);
     }
+    trace_stamp(7);
     ok = grid_barrier(A.bar, epoch, &flag) && ok;
+    trace_stamp(8);
 
     // ---- P4: down (+ residual) ----
     {
         const XSrc xs = phase_x(1);
+        trace_stamp(9);
         const PhaseDesc& ph = P.ph[1];
         const int C = phase_chunks(ph), items = phase_items(ph);
-        const int ntiles = sq.my_tiles(P, 1);
+        const int ntiles = sq.my_tiles(1);
         for (int ti = 0; ti < ntiles && ok; ++ti) {
             const int T = sq.vc + ti * sq.nvc;
             uint32_t* pt = part + (ti & 1) * A.max_items * MT * 128;
+            if (pf_lane) prefetch_ahead<FMT_GPTQ>(P, sq, pf, false);
             for (int item = warp; item < items; item += kGroupWarps) {
                 uint32_t R[MT][4];
-                consume_item<FMT_GPTQ, LAYOUT_TILED, MT>(ring, P, sq, xs, M, item % C, lane, R);
+                consume_item<FMT_GPTQ, LAYOUT_TILED, MT, ST>(ring, P, sq, xs, M, item % C, lane, R);
                 store_partial<MT>(pt, item, lane, R);
             }
             group_sync(wg);
@@ -172,6 +191,7 @@ __global__ void __launch_bounds__(GROUPS * 128) mlp_kernel(const Program P, cons
             }
         }
     }
+    trace_stamp(10);
     ring.drain(lane);
     grid_exit(A.bar);
 }
@@ -182,9 +202,9 @@ size_t mlp_workspace_bytes(int H, int I) {
     return al(16 * size_t(H) * 2) + al(16 * size_t(H)) + al(16 * size_t(I) * 2) + al(16 * size_t(I)) + 4 * 256;
 }
 
-template <int MT, int GROUPS>
+template <int MT, int GROUPS, int ST>
 static int launch_mlp_t(const Program& P, const MlpArgs& A, size_t smem, cudaStream_t stream) {
-    auto kern = mlp_kernel<MT, GROUPS>;
+    auto kern = mlp_kernel<MT, GROUPS, ST>;
     static std::mutex mu;
     static size_t opt_in = 0;
     static int per_sm = 0;
@@ -222,18 +242,21 @@ int launch_mlp(Program& P, MlpArgs& A, cudaStream_t stream) {
     // stage each phase's activations when they fit next to the rings (largest phase first)
     for (int i = 0; i < P.nph; ++i) P.ph[i].xsmem = 1;
     const bool two = M > 8;
+    // plans in order: 16 warps x 1 stage, 8 warps x 2 stages, 4 warps x 2 stages, with every activation
+    // block staged; then the same with the largest block read through L1
     for (int attempt = 0; attempt < 3; ++attempt) {
         int xb = 0;
         for (int i = 0; i < P.nph; ++i)
             if (P.ph[i].xsmem) xb = M * (P.ph[i].K + 16) > xb ? M * (P.ph[i].K + 16) : xb;
-        if (two) {
-            const SmemPlan<FMT_GPTQ, 2> p2(2, A.max_items, xb);
-            if (p2.total <= kMlpSmemLimit) return launch_mlp_t<2, 2>(P, A, p2.total, stream);
-        } else {
-            const SmemPlan<FMT_GPTQ, 1> p2(2, A.max_items, xb);
-            if (p2.total <= kMlpSmemLimit) return launch_mlp_t<1, 2>(P, A, p2.total, stream);
-        }
-        // drop the staging of the phase with the largest activation block
+#define MONO_MLP_TRY(MTV)                                                                              \
+    {                                                                                                  \
+        const SmemPlan<FMT_GPTQ, MTV> a(4, 1, A.max_items, xb), b(2, 2, A.max_items, xb), c(1, 2, A.max_items, xb); \
+        if (MTV == 1 && a.total <= kMlpSmemLimit) return launch_mlp_t<1, 4, 1>(P, A, a.total, stream); \
+        if (b.total <= kMlpSmemLimit) return launch_mlp_t<MTV, 2, 2>(P, A, b.total, stream);          \
+        if (c.total <= kMlpSmemLimit) return launch_mlp_t<MTV, 1, 2>(P, A, c.total, stream);          \
+    }
+        if (two) MONO_MLP_TRY(2) else MONO_MLP_TRY(1)
+#undef MONO_MLP_TRY
         int big = -1;
         for (int i = 0; i < P.nph; ++i)
             if (P.ph[i].xsmem && (big < 0 || P.ph[i].K > P.ph[big].K)) big = i;

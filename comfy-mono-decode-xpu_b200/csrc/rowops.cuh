@@ -1,57 +1,27 @@
 // Row-local device operations of the fused kernels, run by one warp-group (128 threads, named barrier),
 // with a pinned reduction order so the CPU oracle reproduces every bit.
 //
-// RMSNorm of one row of H bf16 values (the role of csrc/mono_common.hpp:452-505 rms_norm_row; the order is
-// this build's own, every op IEEE fp32 RNE, no fused multiply-add):
-//   sq[i]   = x[i] * x[i]
-//   P[v]    = sum_j sq[v + 256 j]              v = 0..255, sequential in j from +0
-//   W[w]    = butterfly sum of P[32 w .. 32 w + 31] (lanes l and l ^ 16, then ^ 8, ^ 4, ^ 2, ^ 1)
-//   total   = sum_{w=0..7} W[w]                 sequential from +0
-//   r       = 1 / sqrt(total / H + eps)         (IEEE division and square root)
-//   out[i]  = bf16((x[i] * r) * w[i])
-// Per-token GPTQ quantization of a bf16 row: s = amax / 127, q = clamp(rint(x / s), -127, 127), s = 0 -> q = 0.
+// A row of H bf16 values (H % 1024 == 0, H <= 4096) is held in registers: thread t owns the 8-element
+// pieces c = t + 128 j (j = 0 .. H/1024 - 1), loaded with all requests in flight.
+//
+// RMSNorm (the role of csrc/mono_common.hpp:452-505 rms_norm_row; this order is this build's own, every op
+// IEEE fp32 RNE, no fused multiply-add):
+//   P[t]   = sum over j, then over e = 0..7, of x[8 (t + 128 j) + e]^2      sequential from +0
+//   W[w]   = butterfly sum of P[32 w .. 32 w + 31] (lanes l and l ^ 16, then ^ 8, ^ 4, ^ 2, ^ 1)
+//   total  = W[0] + W[1] + W[2] + W[3]                                        sequential from +0
+//   r      = 1 / sqrt(total / H + eps)                                        (IEEE division, square root)
+//   out[i] = bf16((x[i] * r) * w[i])
+// Per-token GPTQ quantization: s = amax / 127, q = clamp(rint(x / s), -127, 127), s = 0 -> q = 0; q is
+// written in the engine's permuted activation layout (bytes 0 2 4 6 1 3 5 7 of every 8).
 #pragma once
 #include "common.cuh"
 
 namespace mono {
 
+constexpr int kRowMaxPieces = 4;  // H <= 4096
+
 __device__ __forceinline__ void wg_sync(int wg) {
     asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");
-}
-
-// red: >= 16 floats of shared memory owned by the warp-group. H % 256 == 0.
-__device__ __forceinline__ void rmsnorm_row(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
-                                            uint16_t* __restrict__ out, int H, float eps, float* red, int tig, int wg) {
-    const int lane = tig & 31, warp = tig >> 5;
-    float pa = 0.f, pb = 0.f;  // virtual threads tig and tig + 128
-    for (int j = 0; j * 256 < H; ++j) {
-        const float a = bf16_bits_to_f32(x[tig + 256 * j]);
-        const float b = bf16_bits_to_f32(x[tig + 128 + 256 * j]);
-        pa = __fadd_rn(pa, __fmul_rn(a, a));
-        pb = __fadd_rn(pb, __fmul_rn(b, b));
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-        pa = __fadd_rn(pa, __shfl_xor_sync(0xffffffffu, pa, o));
-        pb = __fadd_rn(pb, __shfl_xor_sync(0xffffffffu, pb, o));
-    }
-    if (lane == 0) {
-        red[warp] = pa;
-        red[4 + warp] = pb;
-    }
-    wg_sync(wg);
-    if (tig == 0) {
-        float tot = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) tot = __fadd_rn(tot, red[i]);
-        const float v = __fadd_rn(__fdiv_rn(tot, float(H)), eps);
-        red[8] = __fdiv_rn(1.f, __fsqrt_rn(v));
-    }
-    wg_sync(wg);
-    const float r = red[8];
-    for (int i = tig; i < H; i += 128)
-        out[i] = f32_to_bf16_bits(__fmul_rn(__fmul_rn(bf16_bits_to_f32(x[i]), r), bf16_bits_to_f32(w[i])));
-    wg_sync(wg);
 }
 
 __device__ __forceinline__ int8_t quant_one(float v, float s) {
@@ -61,19 +31,86 @@ __device__ __forceinline__ int8_t quant_one(float v, float s) {
     return int8_t(q);
 }
 
-// red: >= 8 floats of the warp-group's shared memory.
-__device__ __forceinline__ void quant_row(const uint16_t* __restrict__ x, int K, int8_t* __restrict__ q,
-                                          float* __restrict__ s_out, float* red, int tig, int wg) {
+// Position of byte i in the engine's permuted activation layout (bytes 0 2 4 6 1 3 5 7 of every 8).
+__device__ __forceinline__ int perm8(int i) { return (i & ~7) | ((i & 1) ? 4 + ((i & 7) >> 1) : ((i & 7) >> 1)); }
+
+// 8 quantized values -> the permuted 8-byte word
+__device__ __forceinline__ uint2 quant8_perm(const float (&v)[8], float s) {
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        const uint32_t q = uint32_t(uint8_t(quant_one(v[e], s)));
+        if (e & 1) hi |= q << (8 * (e >> 1));
+        else lo |= q << (8 * (e >> 1));
+    }
+    return make_uint2(lo, hi);
+}
+
+// Optional RMSNorm (w != null) and per-token quantization of one row. xn_out (optional): the normalized
+// bf16 row. q: int8 [H] permuted; s_out: the row scale. red: >= 16 floats of the warp-group's shared memory.
+__device__ __forceinline__ void norm_quant_row(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, float eps,
+                                               int H, uint16_t* __restrict__ xn_out, int8_t* __restrict__ q,
+                                               float* __restrict__ s_out, float* red, int tig, int wg) {
+    const int lane = tig & 31, warp = tig >> 5, J = H >> 10;
+    uint4 xv[kRowMaxPieces], wv[kRowMaxPieces];
+#pragma unroll
+    for (int j = 0; j < kRowMaxPieces; ++j)
+        if (j < J) {
+            xv[j] = __ldcg(reinterpret_cast<const uint4*>(x) + tig + 128 * j);
+            if (w) wv[j] = __ldg(reinterpret_cast<const uint4*>(w) + tig + 128 * j);
+        }
+    float vals[kRowMaxPieces][8];
+#pragma unroll
+    for (int j = 0; j < kRowMaxPieces; ++j)
+        if (j < J) {
+            const uint32_t u[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) vals[j][e] = __uint_as_float((e & 1) ? (u[e >> 1] & 0xFFFF0000u) : (u[e >> 1] << 16));
+        }
+    if (w) {
+        float p = 0.f;
+#pragma unroll
+        for (int j = 0; j < kRowMaxPieces; ++j)
+            if (j < J)
+#pragma unroll
+                for (int e = 0; e < 8; ++e) p = __fadd_rn(p, __fmul_rn(vals[j][e], vals[j][e]));
+#pragma unroll
+        for (int o = 16; o; o >>= 1) p = __fadd_rn(p, __shfl_xor_sync(0xffffffffu, p, o));
+        if (lane == 0) red[warp] = p;
+        wg_sync(wg);
+        const float tot = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.f, red[0]), red[1]), red[2]), red[3]);
+        const float r = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, float(H)), eps)));
+#pragma unroll
+        for (int j = 0; j < kRowMaxPieces; ++j)
+            if (j < J) {
+                const uint32_t u[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
+                uint32_t o[4] = {0, 0, 0, 0};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float wf = __uint_as_float((e & 1) ? (u[e >> 1] & 0xFFFF0000u) : (u[e >> 1] << 16));
+                    const uint16_t b = f32_to_bf16_bits(__fmul_rn(__fmul_rn(vals[j][e], r), wf));
+                    vals[j][e] = bf16_bits_to_f32(b);
+                    o[e >> 1] |= uint32_t(b) << (16 * (e & 1));
+                }
+                if (xn_out) reinterpret_cast<uint4*>(xn_out)[tig + 128 * j] = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+    }
     float amax = 0.f;
-    for (int i = tig; i < K; i += 128) amax = fmaxf(amax, fabsf(bf16_bits_to_f32(x[i])));
+#pragma unroll
+    for (int j = 0; j < kRowMaxPieces; ++j)
+        if (j < J)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(vals[j][e]));
 #pragma unroll
     for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    if ((tig & 31) == 0) red[tig >> 5] = amax;
+    if (lane == 0) red[8 + warp] = amax;
     wg_sync(wg);
-    const float m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    const float m = fmaxf(fmaxf(red[8], red[9]), fmaxf(red[10], red[11]));
     const float s = __fdiv_rn(m, 127.f);
     if (tig == 0) *s_out = s;
-    for (int i = tig; i < K; i += 128) q[i] = quant_one(bf16_bits_to_f32(x[i]), s);
+#pragma unroll
+    for (int j = 0; j < kRowMaxPieces; ++j)
+        if (j < J) reinterpret_cast<uint2*>(q)[tig + 128 * j] = quant8_perm(vals[j], s);
     wg_sync(wg);
 }
 

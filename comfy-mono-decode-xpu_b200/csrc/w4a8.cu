@@ -7,39 +7,46 @@
 
 namespace mono {
 
-__device__ int g_device_error = 0;  // declared in common.cuh
+__device__ int g_device_error = 0;                   // declared in common.cuh
+__device__ unsigned long long* g_trace = nullptr;  // declared in common.cuh
 
 // ---- tile-major repack ------------------------------------------------------------------------------
-// q:  row-major [N][K/2] bytes -> [N/16][K/128][2][32][16]: 16-byte piece (half h, lane 4 g + t) of the
-//     (tile, group) block is row 16 tile + g + 8 h, bytes [64 group + 16 t, +16). GPTQ nibbles v + 8 are
-//     stored as two's complement (XOR 8) so the GEMV unpacks them with one mask.
-__global__ void repack_q_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int N, int K,
-                                uint32_t xor_mask) {
-    const int G = K >> 7;
-    const int64_t pieces = int64_t(N / 16) * G * 64;
+// Row-major [N][K/2] weights + scales -> one buffer of items [N/16][K/1024][8192 weight bytes | SB scale
+// bytes]: piece (group gi, half h, lane 4 g + t) of an item's weights is row 16 tile + g + 8 h, bytes
+// [64 (8 chunk + gi) + 16 t, +16) of that row; the scales follow as [16 rows][8 groups] fp16 (GPTQ) or
+// [16 rows][8 groups x 8] fp8 (REF). GPTQ nibbles v + 8 are stored as two's complement (XOR 8) so the
+// engine unpacks them with one mask.
+__global__ void repack_kernel(const uint8_t* __restrict__ q, const uint8_t* __restrict__ s, uint8_t* __restrict__ dst,
+                              int N, int K, int fmt) {
+    const int C = K >> 10;
+    const int sb = fmt == FMT_GPTQ ? Fmt<FMT_GPTQ>::SB : Fmt<FMT_REF>::SB;
+    const int per_unit = (kStageW + sb) >> 4;  // 16-byte pieces per item
+    const int64_t pieces = int64_t(N >> 4) * C * per_unit;
+    const uint32_t xm = fmt == FMT_GPTQ ? 0x88888888u : 0u;
     for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < pieces; i += int64_t(gridDim.x) * blockDim.x) {
-        const int piece = int(i & 63);
-        const int64_t blk = i >> 6;  // tile * G + group
-        const int tile = int(blk / G), grp = int(blk - int64_t(tile) * G);
-        const int h = piece >> 5, lane = piece & 31, g = lane >> 2, t = lane & 3;
-        const int row = tile * 16 + g + 8 * h;
-        uint4 v = *reinterpret_cast<const uint4*>(src + int64_t(row) * (K / 2) + grp * 64 + t * 16);
-        v.x ^= xor_mask; v.y ^= xor_mask; v.z ^= xor_mask; v.w ^= xor_mask;
+        const int64_t unit = i / per_unit;
+        const int p = int(i - unit * per_unit);
+        const int tile = int(unit / C), chunk = int(unit - int64_t(tile) * C);
+        uint4 v;
+        if (p < 512) {
+            const int gi = p >> 6, r = p & 63, h = r >> 5, lane = r & 31, g = lane >> 2, t = lane & 3;
+            const int row = tile * 16 + g + 8 * h;
+            v = *reinterpret_cast<const uint4*>(q + int64_t(row) * (K >> 1) + (chunk * 8 + gi) * 64 + t * 16);
+            v.x ^= xm; v.y ^= xm; v.z ^= xm; v.w ^= xm;
+        } else if (fmt == FMT_GPTQ) {
+            const int row = tile * 16 + (p - 512);
+            v = *reinterpret_cast<const uint4*>(s + (int64_t(row) * (K >> 7) + chunk * 8) * 2);
+        } else {
+            const int r = p - 512, row = tile * 16 + (r >> 2), part = r & 3;
+            v = *reinterpret_cast<const uint4*>(s + int64_t(row) * (K >> 4) + chunk * 64 + part * 16);
+        }
         *reinterpret_cast<uint4*>(dst + i * 16) = v;
     }
 }
 
-// scales: GPTQ fp16 [N][K/128] -> [N/16][K/256][16][2]; REF fp8 [N][K/16] -> [N/16][K/256][16][16]
-__global__ void repack_s_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int N, int K, int fmt) {
-    const int pairs = K >> 8;                 // 256-wide group pairs per row
-    const int eb = fmt == FMT_GPTQ ? 4 : 16;  // bytes per (row, pair)
-    const int64_t items = int64_t(N) * pairs;
-    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < items; i += int64_t(gridDim.x) * blockDim.x) {
-        const int row = int(i / pairs), pr = int(i - int64_t(row) * pairs);
-        const uint8_t* s = src + int64_t(row) * pairs * eb + int64_t(pr) * eb;
-        uint8_t* d = dst + ((int64_t(row >> 4) * pairs + pr) * 16 + (row & 15)) * eb;
-        for (int b = 0; b < eb; ++b) d[b] = s[b];
-    }
+size_t tiled_bytes(int fmt, int64_t N, int64_t K) {
+    const int sb = fmt == FMT_GPTQ ? Fmt<FMT_GPTQ>::SB : Fmt<FMT_REF>::SB;
+    return size_t(N / 16) * size_t(K / 1024) * size_t(kStageW + sb);
 }
 
 // REF pair table: entry (s << 8 | byte) = int8 grid values of the byte's low and high code at FP8 scale s,
@@ -58,15 +65,11 @@ __global__ void pair_table_kernel(const float* __restrict__ cb, uint16_t* __rest
     tab[i] = uint16_t(ref_grid(lo, scale) | (ref_grid(hi, scale) << 8));
 }
 
-int launch_repack(int fmt, const void* q, const void* s, int N, int K, void* qt, void* st, cudaStream_t stream) {
-    const int64_t pieces = int64_t(N / 16) * (K / 128) * 64;
-    const int blocks = int((pieces + 255) / 256 < 4096 ? (pieces + 255) / 256 : 4096);
-    repack_q_kernel<<<blocks, 256, 0, stream>>>(static_cast<const uint8_t*>(q), static_cast<uint8_t*>(qt), N, K,
-                                                fmt == FMT_GPTQ ? 0x88888888u : 0u);
-    CUDA_TRY(cudaGetLastError());
-    const int64_t items = int64_t(N) * (K / 256);
-    const int sblocks = int((items + 255) / 256 < 4096 ? (items + 255) / 256 : 4096);
-    repack_s_kernel<<<sblocks, 256, 0, stream>>>(static_cast<const uint8_t*>(s), static_cast<uint8_t*>(st), N, K, fmt);
+int launch_repack(int fmt, const void* q, const void* s, int N, int K, void* out, cudaStream_t stream) {
+    const int64_t pieces = int64_t(tiled_bytes(fmt, N, K) / 16);
+    const int blocks = int((pieces + 255) / 256 < 8192 ? (pieces + 255) / 256 : 8192);
+    repack_kernel<<<blocks, 256, 0, stream>>>(static_cast<const uint8_t*>(q), static_cast<const uint8_t*>(s),
+                                              static_cast<uint8_t*>(out), N, K, fmt);
     CUDA_TRY(cudaGetLastError());
     return MONO_OK;
 }

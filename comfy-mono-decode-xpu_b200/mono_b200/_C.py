@@ -58,18 +58,22 @@ def pair_table(codebook, device):
 
 
 def w4a8_decode_linear(x, x_scale, packed, s_rel, s_channel, codebook=None, residual=None, group_size=16,
-                       out_dtype_code=2, cols=0, fast=False, tiled=False):
+                       out_dtype_code=2, cols=0, fast=False, tiled=False, N=None):
     """out[m, n] = cast(float(int32 dot(x[m], decode(w[n]))) * x_scale[m] * s_channel[n]) (+ residual).
     Reference: csrc/w4a8_decode.sycl:325-370. `cols` and `fast` are the reference's tuning knobs and are
     accepted for signature compatibility; `tiled` selects mono_w4_repack's tile-major weights."""
-    _cuda(x, x_scale, packed, s_rel, s_channel)
+    _cuda(x, x_scale, packed, s_channel)
     _check(x.dtype == torch.int8 and x.dim() == 2 and x.is_contiguous(), "x must be contiguous int8 [M, K]")
     M, K = x.shape
-    N = packed.shape[0]
-    _check(packed.dtype in (torch.int8, torch.uint8) and packed.is_contiguous() and packed.dim() == 2
-           and packed.shape[1] * 2 == K, "packed must be contiguous int8 [N, K/2]")
-    _check(s_rel.is_contiguous() and s_rel.numel() == N * (K // group_size), "s_rel must be contiguous [N, K/G]")
-    _check(s_rel.dtype == torch.float8_e4m3fn, "s_rel must be fp8 e4m3")
+    if tiled:
+        N = s_channel.numel()
+        _check(packed.numel() == _lib.load().mono_w4_tiled_bytes(1, N, K), "tiled weight size")
+    else:
+        N = packed.shape[0]
+        _check(packed.dtype in (torch.int8, torch.uint8) and packed.is_contiguous() and packed.dim() == 2
+               and packed.shape[1] * 2 == K, "packed must be contiguous int8 [N, K/2]")
+        _check(s_rel.is_contiguous() and s_rel.numel() == N * (K // group_size), "s_rel must be contiguous [N, K/G]")
+        _check(s_rel.dtype == torch.float8_e4m3fn, "s_rel must be fp8 e4m3")
     _check(x_scale.dtype == torch.float32 and x_scale.is_contiguous() and x_scale.numel() == M, "x_scale f32 [M]")
     _check(s_channel.dtype == torch.float32 and s_channel.is_contiguous() and s_channel.numel() == N,
            "s_channel f32 [N]")
@@ -87,16 +91,20 @@ def w4a8_decode_linear(x, x_scale, packed, s_rel, s_channel, codebook=None, resi
     return out
 
 
-def w4a8_gptq_linear(x, x_scale, packed, scales, residual=None, out_dtype_code=2, tiled=False):
-    """GPTQ W4A8 linear (BASELINE configs[0] format): int4 nibbles v + 8 [N, K/2], fp16 scales [N, K/128]."""
-    _cuda(x, x_scale, packed, scales)
+def w4a8_gptq_linear(x, x_scale, packed, scales, residual=None, out_dtype_code=2, tiled=False, N=None):
+    """GPTQ W4A8 linear (BASELINE configs[0] format): int4 nibbles v + 8 [N, K/2], fp16 scales [N, K/128];
+    tiled=True: `packed` is the w4_repack copy (pass N; `scales` is ignored)."""
+    _cuda(x, x_scale, packed)
     _check(x.dtype == torch.int8 and x.dim() == 2 and x.is_contiguous(), "x must be contiguous int8 [M, K]")
     M, K = x.shape
-    N = packed.shape[0]
-    _check(packed.dtype in (torch.int8, torch.uint8, torch.int32) and packed.is_contiguous()
-           and packed.numel() * packed.element_size() == N * K // 2, "packed must be contiguous [N, K/2] bytes")
-    _check(scales.dtype == torch.float16 and scales.is_contiguous() and scales.numel() == N * (K // 128),
-           "scales must be contiguous fp16 [N, K/128]")
+    if tiled:
+        _check(N is not None and packed.numel() == _lib.load().mono_w4_tiled_bytes(0, N, K), "tiled weight size")
+    else:
+        N = packed.shape[0]
+        _check(packed.dtype in (torch.int8, torch.uint8, torch.int32) and packed.is_contiguous()
+               and packed.numel() * packed.element_size() == N * K // 2, "packed must be contiguous [N, K/2] bytes")
+        _check(scales.dtype == torch.float16 and scales.is_contiguous() and scales.numel() == N * (K // 128),
+               "scales must be contiguous fp16 [N, K/128]")
     _check(x_scale.dtype == torch.float32 and x_scale.numel() == M, "x_scale f32 [M]")
     dtype = torch.float32 if out_dtype_code == 0 else torch.bfloat16
     out = torch.empty((M, N), dtype=dtype, device=x.device)
@@ -110,14 +118,13 @@ def w4a8_gptq_linear(x, x_scale, packed, scales, residual=None, out_dtype_code=2
 
 
 def w4_repack(fmt, packed, scales, N, K):
-    """Tile-major copies (packed, scales) of a W4 weight for the TILED layout."""
+    """The tile-major copy (one uint8 tensor: weights and scales per chunk item) of a W4 weight."""
     _cuda(packed, scales)
     _check(packed.is_contiguous() and scales.is_contiguous(), "contiguous operands")
-    qt = torch.empty_like(packed)
-    st = torch.empty_like(scales)
+    out = torch.empty(_lib.load().mono_w4_tiled_bytes(fmt, N, K), dtype=torch.uint8, device=packed.device)
     with torch.cuda.device(packed.device):
-        _lib.call("mono_w4_repack", fmt, _p(packed), _p(scales), N, K, _p(qt), _p(st), _stream(packed.device))
-    return qt, st
+        _lib.call("mono_w4_repack", fmt, _p(packed), _p(scales), N, K, _p(out), _stream(packed.device))
+    return out
 
 
 def act_quant(x):
@@ -195,14 +202,15 @@ def _workspace(table, key, nbytes, device):
     return ws
 
 
-def mlp_gptq(x, norm_w, eps, gate, up, down, silu_lut=None, residual=True, out=None):
-    """Fused GPTQ MLP block (include/mono_b200.h mono_mlp_gptq). gate/up/down: (tiled packed, tiled fp16
-    scales) from w4_repack. x bf16 [..., H]; returns bf16 [..., H] (out may be x: in place)."""
+def mlp_gptq(x, norm_w, eps, gate, up, down, silu_lut=None, residual=True, out=None, I=None):
+    """Fused GPTQ MLP block (include/mono_b200.h mono_mlp_gptq). gate/up/down: tile-major copies from
+    w4_repack. x bf16 [..., H]; returns bf16 [..., H] (out may be x: in place)."""
     _cuda(x)
     _check(x.dtype == torch.bfloat16 and x.is_contiguous(), "x bf16 contiguous")
     H = x.shape[-1]
     M = x.numel() // H
-    I = gate[0].numel() * 2 // H
+    if I is None:  # the tiled GPTQ copy holds N * K / 2 weight bytes + N * K / 64 scale bytes
+        I = gate.numel() * 64 // (33 * H)
     if silu_lut is None:
         silu_lut = act_luts(x.device)[0]
     if norm_w is not None:
@@ -212,7 +220,6 @@ def mlp_gptq(x, norm_w, eps, gate, up, down, silu_lut=None, residual=True, out=N
     need = _lib.load().mono_mlp_gptq_workspace(H, I)
     ws = _workspace(_mlp_ws, (x.device, H, I), need, x.device)
     with torch.cuda.device(x.device):
-        _lib.call("mono_mlp_gptq", _p(x), _p(norm_w), float(eps), _p(gate[0]), _p(gate[1]), _p(up[0]), _p(up[1]),
-                  _p(down[0]), _p(down[1]), _p(silu_lut), M, H, I, 1 if residual else 0, _p(out), _p(ws), need,
-                  _stream(x.device))
+        _lib.call("mono_mlp_gptq", _p(x), _p(norm_w), float(eps), _p(gate), _p(up), _p(down), _p(silu_lut), M, H, I,
+                  1 if residual else 0, _p(out), _p(ws), need, _stream(x.device))
     return out

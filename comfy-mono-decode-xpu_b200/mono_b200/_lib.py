@@ -22,15 +22,18 @@ SIGNATURES = {
     "mono_last_error": (ctypes.c_char_p, []),
     "mono_abi_version": (I, []),
     "mono_device_status": (I, [ctypes.POINTER(I), I]),
+    "mono_trace_bytes": (SZ, []),
+    "mono_trace_enable": (I, [P, SZ]),
     "mono_w4a8_decode_linear": (I, [P, P, P, P, I, P, P, P, I64, I64, I64, I64, I, I, P, P]),
     "mono_w4_pair_table": (I, [P, P, P]),
     "mono_w4a8_gptq_linear": (I, [P, P, P, P, P, I64, I64, I64, I, I, P, P]),
-    "mono_w4_repack": (I, [I, P, P, I64, I64, P, P, P]),
+    "mono_w4_tiled_bytes": (SZ, [I, I64, I64]),
+    "mono_w4_repack": (I, [I, P, P, I64, I64, P, P]),
     "mono_act_quant": (I, [P, I64, I64, P, P, P]),
     "mono_rot_quant_workspace": (SZ, [I64, I64]),
     "mono_rot_quant": (I, [P, P, I64, I64, P, P, P, P]),
     "mono_mlp_gptq_workspace": (SZ, [I64, I64]),
-    "mono_mlp_gptq": (I, [P, P, ctypes.c_float, P, P, P, P, P, P, P, I64, I64, I64, I, P, P, SZ, P]),
+    "mono_mlp_gptq": (I, [P, P, ctypes.c_float, P, P, P, P, I64, I64, I64, I, P, P, SZ, P]),
 }
 
 MONO_OK, MONO_EINVAL, MONO_ECUDA, MONO_ETIMEOUT, MONO_EDEVICE = 0, 1, 2, 3, 4

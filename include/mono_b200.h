@@ -50,13 +50,20 @@ MONO_API int mono_abi_version(void);
 /* Reads (and with reset != 0 clears) the device error word of the current device. Synchronizes. */
 MONO_API int mono_device_status(int* code, int reset);
 
+/* Phase trace (the role of the reference's per-phase clock stamps, csrc/mono_mlp.sycl:108-169): with a
+ * device buffer of mono_trace_bytes() set, thread 0 of every CTA of the fused kernels writes %globaltimer
+ * (ns) at each phase boundary to [cta][phase] (uint64, 1024 x 16). NULL turns it off (the default).
+ * Synchronous; not for use while kernels run. */
+MONO_API size_t mono_trace_bytes(void);
+MONO_API int mono_trace_enable(void* buffer, size_t bytes);
+
 /* ---- W4A8 linear ----------------------------------------------------------------------------------- */
 
 /* Replaces _C.w4a8_decode_linear (csrc/bindings.cpp:71-74; csrc/w4a8_decode.sycl:325-370).
  *   out[m, n] = cast(float(int32 sum_k x[m, k] * w_i8[n, k]) * x_scale[m] * s_channel[n]) (+ residual)
  *   w_i8 = isnan(r) ? 0 : clamp(r, -127, 127), r = rint(codebook[code] * s_rel[n, k / 16])
- * x int8 [M, K] (16 B aligned), x_scale f32 [M], packed [N, K/2] bytes (low nibble = even k) or its TILED
- * copy, s_rel FP8 e4m3 [N, K/16] (G16) or its TILED copy, s_channel f32 [N], pair_table from
+ * x int8 [M, K] (16 B aligned), x_scale f32 [M], packed [N, K/2] bytes (low nibble = even k) with s_rel
+ * FP8 e4m3 [N, K/16] (G16), or packed = the TILED copy (s_rel unused), s_channel f32 [N], pair_table from
  * mono_w4_pair_table(codebook), residual [M, N] in the output dtype or NULL, out [M, N].
  * 1 <= M <= 16, K % 1024 == 0, K <= 16384, N % 16 == 0, group_size == 16. */
 MONO_API int mono_w4a8_decode_linear(const int8_t* x, const float* x_scale, const void* packed, const void* s_rel,
@@ -72,7 +79,7 @@ MONO_API int mono_w4_pair_table(const float* codebook, uint16_t* table, mono_str
 
 /* GPTQ W4A8 linear (the reference has no GPTQ entry, its W4A8 linear above is the
  * closest): int4 v in [-8, 7] stored as nibble v + 8 (8 per int32 along K, i.e. [N, K/2] bytes),
- * fp16 scales [N, K/128] (or TILED copies);
+ * fp16 scales [N, K/128] (or packed = the TILED copy, scales unused);
  *   acc_g = int32 sum over group g of x * v;  F_c = sum_{g in 1024-chunk c} float(acc_g) * float(s[n, g]);
  *   out = cast((sum_c F_c) * x_scale[m])  (fp32, sequential sums from +0, no fused multiply-add). */
 MONO_API int mono_w4a8_gptq_linear(const int8_t* x, const float* x_scale, const void* packed, const void* scales,
@@ -80,11 +87,14 @@ MONO_API int mono_w4a8_gptq_linear(const int8_t* x, const float* x_scale, const 
                           void* out, mono_stream_t stream);
 
 /* Tile-major copy of a W4 weight for the TILED layout (the role of tiles.py tile_major,
- * comfy_mono_decode_xpu/tiles.py:45-48): packed [N, K/2] -> [N/16][K/128][2][32][16] bytes (GPTQ nibbles
- * re-coded as two's complement), scales -> [N/16][K/256][16][4 or 16 bytes]. Outputs are the same sizes as
- * the inputs. N % 16 == 0, K % 256 == 0. */
-MONO_API int mono_w4_repack(int fmt, const void* packed, const void* scales, int64_t N, int64_t K, void* packed_tiled,
-                   void* scales_tiled, mono_stream_t stream);
+ * comfy_mono_decode_xpu/tiles.py:45-48, in this build's own layout): one buffer of
+ * mono_w4_tiled_bytes(fmt, N, K) bytes holding, per (16-row tile, 1024-wide chunk), the chunk's weights in
+ * mma fragment order (GPTQ nibbles re-coded as two's complement) followed by its scales, so the kernels
+ * fetch a whole chunk with one bulk copy. packed [N, K/2], scales GPTQ fp16 [N, K/128] / REF fp8
+ * [N, K/16]. N % 16 == 0, K % 1024 == 0. */
+MONO_API size_t mono_w4_tiled_bytes(int fmt, int64_t N, int64_t K);
+MONO_API int mono_w4_repack(int fmt, const void* packed, const void* scales, int64_t N, int64_t K, void* tiled,
+                            mono_stream_t stream);
 
 /* ---- activation quantization ----------------------------------------------------------------------- */
 
@@ -107,17 +117,17 @@ MONO_API int mono_rot_quant(const void* x_bf16, const void* h_bf16, int64_t M, i
  *   xn = RMSNorm(x; norm_w, eps)  (norm_w NULL: xn = x)        q1, s1 = act_quant(xn)
  *   g, u = GPTQ linear (gate, up)(q1)  h = bf16(silu_lut[g] * u)  q2, s2 = act_quant(h)
  *   out = bf16(x + bf16(GPTQ down(q2)))  (residual != 0)  or  bf16(GPTQ down(q2))
- * RMSNorm order: P[v] = sum_j x[v + 256 j]^2 (v < 256), butterfly within each 32, the 8 partial sums in
- * order, r = 1 / sqrt(total / H + eps), out = bf16((x * r) * w) (IEEE fp32 ops, no fused multiply-add).
- * x, out bf16 [M, H] (out may alias x); gate/up TILED [I, H/2] + fp16 scales; down TILED [H, I/2] + scales;
- * silu_lut bf16 [65536] (SiLU of every bf16 bit pattern). 1 <= M <= 16, H and I multiples of 1024 up to
- * 16384. workspace: mono_mlp_gptq_workspace(H, I) bytes, zero-filled before its first use (the kernel
+ * RMSNorm order: P[t] = sum over the 8-element pieces t + 128 j (j outer, element inner) of x^2 (t < 128),
+ * butterfly within each 32, the 4 partial sums in order, r = 1 / sqrt(total / H + eps),
+ * out = bf16((x * r) * w) (IEEE fp32 ops, no fused multiply-add).
+ * x, out bf16 [M, H] (out may alias x); gate/up: TILED copies of [I, H/2] weights; down: of [H, I/2];
+ * silu_lut bf16 [65536] (SiLU of every bf16 bit pattern). 1 <= M <= 16, H a multiple of 1024 up to
+ * 4096, I a multiple of 1024 up to 16384. workspace: mono_mlp_gptq_workspace(H, I) bytes, zero-filled before its first use (the kernel
  * leaves it reusable); one call at a time per workspace. */
 MONO_API size_t mono_mlp_gptq_workspace(int64_t H, int64_t I);
-MONO_API int mono_mlp_gptq(const void* x, const void* norm_w, float eps, const void* gate_q, const void* gate_s,
-                           const void* up_q, const void* up_s, const void* down_q, const void* down_s,
-                           const void* silu_lut, int64_t M, int64_t H, int64_t I, int residual, void* out,
-                           void* workspace, size_t workspace_bytes, mono_stream_t stream);
+MONO_API int mono_mlp_gptq(const void* x, const void* norm_w, float eps, const void* gate, const void* up,
+                           const void* down, const void* silu_lut, int64_t M, int64_t H, int64_t I, int residual,
+                           void* out, void* workspace, size_t workspace_bytes, mono_stream_t stream);
 
 #ifdef __cplusplus
 }

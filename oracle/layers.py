@@ -18,18 +18,20 @@ def _butterfly32(a: np.ndarray) -> np.ndarray:
 
 
 def rmsnorm(x_bits: np.ndarray, w_bits: np.ndarray, eps: float) -> np.ndarray:
-    """RMSNorm with the pinned order of include/mono_b200.h (mono_mlp_gptq): P[v] = sum_j x[v + 256 j]^2,
-    butterfly within each 32, the 8 partials in order, r = 1 / sqrt(total / H + eps),
-    out = bf16((x * r) * w). The role of csrc/mono_common.hpp:452-505 (whose order is the Intel build's)."""
+    """RMSNorm with the pinned order of the fused kernels (include/mono_b200.h mono_mlp_gptq): thread t of 128
+    sums the squares of its 8-element pieces t + 128 j (j outer, element inner, from +0), butterfly within
+    each 32, the 4 warp sums in order, r = 1 / sqrt(total / H + eps), out = bf16((x * r) * w).
+    The role of csrc/mono_common.hpp:452-505 (whose reduction order is the Intel build's)."""
     x = bf16_bits_to_f32(x_bits).astype(F32)
     M, H = x.shape
-    sq = (x * x).astype(F32)
-    P = np.zeros((M, 256), dtype=F32)
-    for j in range(H // 256):
-        P = (P + sq[:, j * 256:(j + 1) * 256]).astype(F32)
-    W = _butterfly32(P.reshape(M, 8, 32))  # [M, 8]
+    sq = (x * x).astype(F32).reshape(M, H // 1024, 128, 8)  # [m, j, t, e]
+    P = np.zeros((M, 128), dtype=F32)
+    for j in range(H // 1024):
+        for e in range(8):
+            P = (P + sq[:, j, :, e]).astype(F32)
+    W = _butterfly32(P.reshape(M, 4, 32))  # [M, 4]
     tot = np.zeros(M, dtype=F32)
-    for w in range(8):
+    for w in range(4):
         tot = (tot + W[:, w]).astype(F32)
     v = ((tot / F32(H)).astype(F32) + F32(eps)).astype(F32)
     r = (F32(1.0) / np.sqrt(v).astype(F32)).astype(F32)

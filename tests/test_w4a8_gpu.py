@@ -10,7 +10,7 @@ from oracle import w4a8 as ow
 
 pytestmark = pytest.mark.gpu
 
-SHAPES = [(12288, 4096), (4096, 12288), (1024, 4096), (4096, 1024), (48, 3072)]
+SHAPES = [(12288, 4096), (4096, 12288), (1024, 4096), (4096, 1024), (48, 3072), (8192 + 2048, 4096)]
 
 
 def _bf16_t(bits, dev):
@@ -25,13 +25,13 @@ def test_gptq_linear_bit_exact(cuda, N, K, tiled):
     pk = torch.from_numpy(packed).to(cuda)
     sc = torch.from_numpy(scales).to(cuda)
     if tiled:
-        pk, sc = _C.w4_repack(0, pk, sc, N, K)
+        pk, sc = _C.w4_repack(0, pk, sc, N, K), None
     g = torch.Generator().manual_seed(N * 3 + K)
     for M in (1, 2, 4, 8, 9, 16):
         x = torch.randn(M, K, generator=g).to(torch.bfloat16)
         xq, xs = ow.act_quant(x.view(torch.int16).numpy().view(np.uint16))
         ref = ow.gptq_linear(xq, xs, packed, scales)
-        out = _C.w4a8_gptq_linear(torch.from_numpy(xq).to(cuda), torch.from_numpy(xs).to(cuda), pk, sc, tiled=tiled)
+        out = _C.w4a8_gptq_linear(torch.from_numpy(xq).to(cuda), torch.from_numpy(xs).to(cuda), pk, sc, tiled=tiled, N=N)
         assert bits_equal(bf16_bits(out), ref), (M, N, K, tiled)
 
 
@@ -63,8 +63,9 @@ def test_ref_decode_linear_bit_exact(cuda, N, K, tiled):
     pk = torch.from_numpy(packed).to(cuda)
     sr = torch.from_numpy(s_rel).to(cuda)
     if tiled:
-        pk, sr = _C.w4_repack(1, pk, sr, N, K)
-    sr = sr.view(torch.float8_e4m3fn)
+        pk, sr = _C.w4_repack(1, pk, sr, N, K), None
+    else:
+        sr = sr.view(torch.float8_e4m3fn)
     for M in (1, 2, 3, 8, 16):
         x = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8)
         xs = torch.rand(M, generator=g) * 0.05 + 1e-3
