@@ -49,6 +49,7 @@ int launch_pair_table(const float* codebook, uint16_t* tab, cudaStream_t stream)
 int launch_act_quant(const void* x, int M, int K, int8_t* q, float* xs, cudaStream_t stream);
 size_t rot_quant_workspace(int M, int K);
 int launch_rot_quant(const void* x, const void* h, int M, int K, int8_t* q, float* s, void* ws, cudaStream_t stream);
+int launch_rot_quant_noalloc(const void* x, const void* h, int M, int K, int8_t* q, float* s, cudaStream_t stream);
 
 struct MlpArgs {
     const uint16_t* x;
@@ -182,6 +183,13 @@ int mono_rot_quant(const void* x_bf16, const void* h_bf16, int64_t M, int64_t K,
     MONO_CHECK(M >= 1 && M <= 65535 && K >= 256 && K % 256 == 0, "M in [1, 65535], K % 256 == 0");
     MONO_CHECK(aligned(workspace, 16), "workspace must be 16-byte aligned");
     return launch_rot_quant(x_bf16, h_bf16, int(M), int(K), q, scale, workspace, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int mono_rot_quant_noalloc(const void* x_bf16, const void* h_bf16, int64_t M, int64_t K, int8_t* q, float* scale,
+                           mono_stream_t stream) {
+    MONO_CHECK(x_bf16 && h_bf16 && q && scale, "null operand");
+    MONO_CHECK(M >= 1 && M <= 65535 && K >= 256 && K <= (1 << 20), "M in [1, 65535], K in [256, 2^20]");
+    return launch_rot_quant_noalloc(x_bf16, h_bf16, int(M), int(K), q, scale, reinterpret_cast<cudaStream_t>(stream));
 }
 
 size_t mono_mlp_gptq_workspace(int64_t H, int64_t I) { return mlp_workspace_bytes(int(H), int(I)); }

@@ -12,6 +12,8 @@
 // The reference accumulates the rotation in fp32 on its matrix engine; wherever those fp32 partial sums
 // are exact (bounded exponent spread inside a group, the normal case) both give the correctly rounded
 // value, which the fp64 sum here gives for every input whose group spans at most 2^37 in magnitude.
+#include <mutex>
+
 #include "abi_internal.h"
 #include "common.cuh"
 
@@ -172,6 +174,47 @@ int launch_rot_quant(const void* x, const void* h, int M, int K, int8_t* q, floa
     rot_quant_kernel<<<dim3(K / 256, M), 256, 0, stream>>>(xr, K, amax, done, q, s);
     CUDA_TRY(cudaGetLastError());
     return MONO_OK;
+}
+
+// ---- rot_quant without allocation ------------------------------------------------------------------
+// Scratch of mono_rot_quant_noalloc: the same layout as the caller-provided workspace of mono_rot_quant
+// (kRotMaxRows amax words and done counters, then the rotated rows), sized for at most
+// kNoAllocRows x kNoAllocK. Every GPU that loads the library holds these ~386 KB until the process exits.
+constexpr int kNoAllocRows = 16;
+constexpr int kNoAllocK = 12288;
+constexpr size_t kNoAllocBytes = size_t(kRotMaxRows) * 8 + size_t(kNoAllocRows) * kNoAllocK * 2;
+static __device__ __align__(256) uint8_t g_rot_scratch[kNoAllocBytes];
+
+// Device address of g_rot_scratch on the current device, looked up once per device. In host code the
+// symbol names a host-side stand-in, never the device memory: only this address may reach a kernel.
+static int rot_scratch_address(void** out) {
+    static std::mutex mu;
+    static void* addr[64] = {};
+    int dev = 0;
+    CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(MONO_EINVAL, "rot_quant_noalloc: device ordinal %d out of range", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (addr[dev] == nullptr) {
+        void* p = nullptr;
+        CUDA_TRY(cudaGetSymbolAddress(&p, g_rot_scratch));
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return MONO_OK;
+}
+
+int launch_rot_quant_noalloc(const void* x, const void* h, int M, int K, int8_t* q, float* s, cudaStream_t stream) {
+    if (M < 1 || M > kNoAllocRows || K < 256 || K > kNoAllocK || K % 256)
+        return fail(MONO_EINVAL,
+                    "rot_quant_noalloc: shape [%d, %d] exceeds the fixed scratch (1 <= M <= %d rows, K <= %d, K %% 256 "
+                    "== 0); use mono_rot_quant with a workspace",
+                    M, K, kNoAllocRows, kNoAllocK);
+    void* ws = nullptr;
+    const int rc = rot_scratch_address(&ws);
+    if (rc) return rc;
+    // the amax words and done counters must start at zero: clear them (the rows need no clearing)
+    CUDA_TRY(cudaMemsetAsync(ws, 0, size_t(kRotMaxRows) * 8, stream));
+    return launch_rot_quant(x, h, M, K, q, s, ws, stream);
 }
 
 }  // namespace mono

@@ -32,6 +32,7 @@ SIGNATURES = {
     "mono_act_quant": (I, [P, I64, I64, P, P, P]),
     "mono_rot_quant_workspace": (SZ, [I64, I64]),
     "mono_rot_quant": (I, [P, P, I64, I64, P, P, P, P]),
+    "mono_rot_quant_noalloc": (I, [P, P, I64, I64, P, P, P]),
     "mono_mlp_gptq_workspace": (SZ, [I64, I64]),
     "mono_mlp_gptq": (I, [P, P, ctypes.c_float, P, P, P, P, I64, I64, I64, I, P, P, SZ, P]),
 }
