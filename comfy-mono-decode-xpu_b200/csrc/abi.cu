@@ -3,8 +3,7 @@
 #include <mutex>
 #include <string>
 
-#include "abi_internal.h"
-#include "engine.cuh"
+#include "launch.h"
 
 namespace mono {
 
@@ -33,42 +32,6 @@ int sm_count() {
     }
     return counts[dev];
 }
-
-struct LinearEpi {
-    const float* xs;
-    const float* s_channel;
-    const void* residual;
-    void* out;
-    int out_bf16;
-    int max_items;
-};
-int launch_linear(int fmt, int layout, Program& P, LinearEpi& E, cudaStream_t stream);
-int launch_repack(int fmt, const void* q, const void* s, int N, int K, void* out, cudaStream_t stream);
-size_t tiled_bytes(int fmt, int64_t N, int64_t K);
-int launch_pair_table(const float* codebook, uint16_t* tab, cudaStream_t stream);
-int launch_act_quant(const void* x, int M, int K, int8_t* q, float* xs, cudaStream_t stream);
-size_t rot_quant_workspace(int M, int K);
-int launch_rot_quant(const void* x, const void* h, int M, int K, int8_t* q, float* s, void* ws, cudaStream_t stream);
-int launch_rot_quant_noalloc(const void* x, const void* h, int M, int K, int8_t* q, float* s, cudaStream_t stream);
-
-struct MlpArgs {
-    const uint16_t* x;
-    const uint16_t* norm_w;
-    const uint16_t* lut;
-    uint16_t* out;
-    float eps;
-    int H, I, residual, max_items;
-    uint16_t* xn;
-    int8_t* q1;
-    float* s1;
-    uint16_t* h;
-    unsigned* amax2;
-    int8_t* q2;
-    float* s2;
-    unsigned* bar;
-};
-int launch_mlp(Program& P, MlpArgs& A, cudaStream_t stream);
-size_t mlp_workspace_bytes(int H, int I);
 
 static int check_linear_common(const int8_t* x, const float* xs, const void* packed, const void* scales,
                                const void* out, int64_t M, int64_t N, int64_t K, int out_dtype_code, int layout) {
@@ -132,7 +95,7 @@ int mono_w4a8_decode_linear(const int8_t* x, const float* x_scale, const void* p
     P.ph[0].nm = 1;
     P.ph[0].K = int(K);
     P.ph[0].x = x;
-    LinearEpi E{x_scale, s_channel, residual, out, out_dtype_code == MONO_OUT_BF16, 0};
+    LinearEpi E{nullptr, x_scale, s_channel, residual, out, out_dtype_code == MONO_OUT_BF16, 0};
     return launch_linear(FMT_REF, layout, P, E, reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -153,7 +116,25 @@ int mono_w4a8_gptq_linear(const int8_t* x, const float* x_scale, const void* pac
     P.ph[0].nm = 1;
     P.ph[0].K = int(K);
     P.ph[0].x = x;
-    LinearEpi E{x_scale, nullptr, residual, out, out_dtype_code == MONO_OUT_BF16, 0};
+    LinearEpi E{nullptr, x_scale, nullptr, residual, out, out_dtype_code == MONO_OUT_BF16, 0};
+    return launch_linear(FMT_GPTQ, layout, P, E, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int mono_w4a8_gptq_linear_bf16(const void* x, const void* packed, const void* scales, const void* residual, int64_t M,
+                               int64_t N, int64_t K, int out_dtype_code, int layout, void* out, mono_stream_t stream) {
+    // the int8 checks with x standing in for both activation operands (x_scale is produced in the kernel)
+    int rc = check_linear_common(static_cast<const int8_t*>(x), static_cast<const float*>(x), packed, scales, out, M, N,
+                                 K, out_dtype_code, layout);
+    if (rc) return rc;
+    Program P{};
+    P.nph = 1;
+    P.M = int(M);
+    P.ph[0].m[0] = MatDesc{static_cast<const uint8_t*>(packed), static_cast<const uint8_t*>(scales), int(N)};
+    P.ph[0].nm = 1;
+    P.ph[0].K = int(K);
+    P.ph[0].x = nullptr;
+    P.ph[0].xperm = 1;
+    LinearEpi E{static_cast<const uint16_t*>(x), nullptr, nullptr, residual, out, out_dtype_code == MONO_OUT_BF16, 0};
     return launch_linear(FMT_GPTQ, layout, P, E, reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -14,8 +14,7 @@
 // value, which the fp64 sum here gives for every input whose group spans at most 2^37 in magnitude.
 #include <mutex>
 
-#include "abi_internal.h"
-#include "common.cuh"
+#include "launch.h"
 
 namespace mono {
 

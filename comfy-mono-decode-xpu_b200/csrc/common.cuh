@@ -67,11 +67,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait: returns false (and records DEV_MBAR_TIMEOUT) if the phase never completes.
-constexpr uint32_t kMbarSpinLimit = 1u << 22;
+// Bounded wait: returns false (and records DEV_MBAR_TIMEOUT) if the phase has not completed after
+// kWaitLimitNs of %globaltimer time (checked every 256 polls) or kMbarSpinLimit polls. Plain try_wait
+// polls (try_wait itself parks the warp for a short, hardware-chosen time): measured on B200, a suspend-time
+// hint or __nanosleep back-off between polls delayed the wake-up of a producer warp waiting for a freed
+// ring slot by a microsecond or more, which serialized the refills.
+constexpr uint32_t kMbarSpinLimit = 1u << 26;
+constexpr unsigned long long kWaitLimitNs = 1000000000ull;  // 1 s
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kMbarSpinLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer();
+    for (uint32_t i = 1; i < kMbarSpinLimit; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255) == 0 && globaltimer() - t0 > kWaitLimitNs) break;
+    }
     set_device_error(DEV_MBAR_TIMEOUT);
     return false;
 }

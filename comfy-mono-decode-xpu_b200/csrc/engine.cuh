@@ -168,6 +168,16 @@ struct Seq {
     }
 };
 
+// The tile-major source of an item (weights followed by scales, stage_bytes<FMT>() contiguous bytes).
+template <int FMT>
+__device__ __forceinline__ const uint8_t* item_src(const Program& P, const Seq& sq, const Cursor& c) {
+    const PhaseDesc& p = P.ph[c.ph];
+    const int T = sq.vc + c.ti * sq.nvc;
+    int mat, lt;
+    resolve(p, T, c.sub, mat, lt);
+    return p.m[mat].q + (size_t(lt) * (p.K >> 10) + c.chunk) * stage_bytes<FMT>();
+}
+
 template <int FMT, int LAYOUT>
 __device__ __forceinline__ void issue_item(const Program& P, const Seq& sq, const Cursor& c, uint8_t* stage,
                                            uint64_t* bar, int lane) {
@@ -214,11 +224,14 @@ template <int FMT, int LAYOUT, int kStages>
 struct Ring {
     uint8_t* buf;
     uint64_t* bars;
-    Cursor prod;
+    Cursor prod;  // next item to copy into the ring
+    Cursor pfc;   // next item to request into L2 (tiled layouts): pf_dist items ahead of prod
     int issued, consumed;
     bool ok;
 
-    __device__ void init(const Program& P, const Seq& sq, int lane) {
+    // Issue the first kStages copies and L2 prefetches of the pf_dist items after them. The copies go
+    // through this SM's TMA unit in order: callers issue them after any urgent activation loads.
+    __device__ void init(const Program& P, const Seq& sq, int lane, int pf_dist) {
         if (LAYOUT == LAYOUT_TILED && lane == 0) {
             for (int i = 0; i < kStages; ++i) mbar_init(&bars[i], 1);
             fence_mbar_init();
@@ -237,6 +250,13 @@ struct Ring {
                 cp_async_commit();
             }
         }
+        pfc = prod;
+        if constexpr (LAYOUT == LAYOUT_TILED)
+            for (int i = 0; i < pf_dist && !pfc.done; ++i) prefetch_next(P, sq, lane);
+    }
+    __device__ void prefetch_next(const Program& P, const Seq& sq, int lane) {
+        if (lane == 0) bulk_prefetch_l2(item_src<FMT>(P, sq, pfc), stage_bytes<FMT>());
+        sq.advance(P, pfc);
     }
     __device__ uint8_t* wait() {
         const int slot = consumed % kStages;
@@ -256,6 +276,8 @@ struct Ring {
             issue_item<FMT, LAYOUT>(P, sq, prod, buf + slot * stage_bytes<FMT>(), &bars[slot], lane);
             ++issued;
             sq.advance(P, prod);
+            if constexpr (LAYOUT == LAYOUT_TILED)
+                if (!pfc.done) prefetch_next(P, sq, lane);
         } else if (LAYOUT == LAYOUT_ROW) {
             cp_async_commit();
         }
@@ -270,49 +292,6 @@ struct Ring {
         }
     }
 };
-
-// ---- L2 prefetch of upcoming tiles ------------------------------------------------------------------
-// A warp-group's tiles in a tile-major layout are contiguous runs (all chunk items of a 16-row tile, for
-// each subtile). Lane 0 of the group's first warp keeps kPrefetchTiles tiles requested into L2 ahead of the
-// tile being consumed, across phase boundaries, so HBM keeps streaming through row phases and grid
-// barriers (the role of the reference's prefetch_stream, csrc/mono_common.hpp:318-340).
-constexpr int kPrefetchTiles = 2;
-
-struct TileCursor {
-    int ph, ti;
-    bool done;
-};
-
-__device__ __forceinline__ TileCursor tile_start(const Program& P, const Seq& sq, int ph) {
-    TileCursor c{ph, 0, false};
-    while (c.ph < P.nph && sq.my_tiles(c.ph) == 0) ++c.ph;
-    c.done = c.ph >= P.nph;
-    return c;
-}
-__device__ __forceinline__ void tile_advance(const Program& P, const Seq& sq, TileCursor& c) {
-    if (++c.ti < sq.my_tiles(c.ph)) return;
-    c = tile_start(P, sq, c.ph + 1);
-}
-template <int FMT>
-__device__ __forceinline__ void prefetch_tile(const Program& P, const Seq& sq, const TileCursor& c) {
-    const PhaseDesc& p = P.ph[c.ph];
-    const int T = sq.vc + c.ti * sq.nvc, C = p.K >> 10;
-    const uint32_t bytes = uint32_t(C) * stage_bytes<FMT>();
-    for (int sub = 0; sub < (p.paired ? 2 : 1); ++sub) {
-        int mat, lt;
-        resolve(p, T, sub, mat, lt);
-        bulk_prefetch_l2(p.m[mat].q + size_t(lt) * bytes, bytes);
-    }
-}
-// Called by the group's lane 0 (tiled layouts only): at kernel start with `first` = true (requests the
-// first kPrefetchTiles tiles), then once per consumed tile (requests one more).
-template <int FMT>
-__device__ __forceinline__ void prefetch_ahead(const Program& P, const Seq& sq, TileCursor& c, bool first) {
-    for (int i = 0; i < (first ? kPrefetchTiles : 1) && !c.done; ++i) {
-        prefetch_tile<FMT>(P, sq, c);
-        tile_advance(P, sq, c);
-    }
-}
 
 // REF decode of one packed word (8 codes sharing one fp8 scale byte) into the even / odd A registers.
 __device__ __forceinline__ void ref_decode(const uint16_t* __restrict__ tab, uint32_t word, uint32_t sb,
@@ -335,9 +314,10 @@ struct XSrc {
 // Consume one item (8 groups). R = the chunk partial per fragment element: fp32 bits (GPTQ, carrying a
 // factor 16, see below) or the int32 dot (REF). Fragment element i of m-tile mt: (row g + 8 (i >> 1),
 // activation 2t + (i & 1)).
-template <int FMT, int LAYOUT, int MT, int ST>
-__device__ __forceinline__ void consume_item(Ring<FMT, LAYOUT, ST>& r, const Program& P, const Seq& sq, const XSrc& xs,
-                                             int M, int chunk, int lane, uint32_t (&R)[MT][4]) {
+// XMODE: 0 = global, natural byte order; 1 = global, permuted; 2 = shared (pitch K + 16), permuted.
+template <int FMT, int LAYOUT, int MT, int XMODE>
+__device__ __forceinline__ void compute_item(const uint8_t* __restrict__ stage, const uint16_t* __restrict__ pair_tab,
+                                             const XSrc& xs, int M, int chunk, int lane, uint32_t (&R)[MT][4]) {
     const int g = lane >> 2, t = lane & 3;
     float F[MT][4];
     int A[MT][4];
@@ -348,7 +328,6 @@ __device__ __forceinline__ void consume_item(Ring<FMT, LAYOUT, ST>& r, const Pro
             F[mt][i] = 0.f;
             A[mt][i] = 0;
         }
-    uint8_t* stage = r.wait();
     // GPTQ item scales: [16 rows][8 groups] fp16
     const __half* sc16 = reinterpret_cast<const __half*>(stage + kStageW);
     const uint32_t zero = 0;
@@ -365,7 +344,7 @@ __device__ __forceinline__ void consume_item(Ring<FMT, LAYOUT, ST>& r, const Pro
         for (int mt = 0; mt < MT; ++mt) {
             if (g + 8 * mt < M) {
                 const int8_t* xr = xrow[mt] + gi * 128;
-                if (xs.smem) {
+                if (XMODE == 2) {
                     xv[mt][0] = lds_v4(xr);
                     xv[mt][1] = lds_v4(xr + 16);
                 } else {
@@ -398,14 +377,14 @@ __device__ __forceinline__ void consume_item(Ring<FMT, LAYOUT, ST>& r, const Pro
                 a2 = xa & 0xF0F0F0F0u;
                 a3 = xb & 0xF0F0F0F0u;
             } else {
-                ref_decode(P.pair_tab, wA[s], (sbA >> (8 * (s >> 1))) & 0xFF, a0, a2);
-                ref_decode(P.pair_tab, wB[s], (sbB >> (8 * (s >> 1))) & 0xFF, a1, a3);
+                ref_decode(pair_tab, wA[s], (sbA >> (8 * (s >> 1))) & 0xFF, a0, a2);
+                ref_decode(pair_tab, wB[s], (sbB >> (8 * (s >> 1))) & 0xFF, a1, a3);
             }
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) {
                 uint32_t b0 = (s < 2) ? (s == 0 ? xv[mt][0].x : xv[mt][0].z) : (s == 2 ? xv[mt][1].x : xv[mt][1].z);
                 uint32_t b1 = (s < 2) ? (s == 0 ? xv[mt][0].y : xv[mt][0].w) : (s == 2 ? xv[mt][1].y : xv[mt][1].w);
-                if (!xs.perm) {
+                if (XMODE == 0) {
                     const uint32_t lo = b0, hi = b1;
                     b0 = prmt(lo, hi, 0x6420);
                     b1 = prmt(lo, hi, 0x7531);
@@ -435,11 +414,30 @@ __device__ __forceinline__ void consume_item(Ring<FMT, LAYOUT, ST>& r, const Pro
                 for (int i = 0; i < 4; ++i) A[mt][i] += c0[mt][i] + c1[mt][i];
         }
     }
-    r.release(P, sq, lane);
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) R[mt][i] = FMT == FMT_GPTQ ? __float_as_uint(F[mt][i]) : uint32_t(A[mt][i]);
+}
+
+template <int FMT, int LAYOUT, int MT, int ST, int XMODE>
+__device__ __forceinline__ void consume_item_x(Ring<FMT, LAYOUT, ST>& r, const Program& P, const Seq& sq, const XSrc& xs,
+                                               int M, int chunk, int lane, uint32_t (&R)[MT][4]) {
+    const uint8_t* stage = r.wait();
+    compute_item<FMT, LAYOUT, MT, XMODE>(stage, P.pair_tab, xs, M, chunk, lane, R);
+    r.release(P, sq, lane);
+}
+
+template <int FMT, int LAYOUT, int MT, int ST>
+__device__ __forceinline__ void consume_item(Ring<FMT, LAYOUT, ST>& r, const Program& P, const Seq& sq, const XSrc& xs,
+                                             int M, int chunk, int lane, uint32_t (&R)[MT][4]) {
+    // one warp-uniform branch per item; each body has only its own activation path
+    if (xs.smem)
+        consume_item_x<FMT, LAYOUT, MT, ST, 2>(r, P, sq, xs, M, chunk, lane, R);
+    else if (xs.perm)
+        consume_item_x<FMT, LAYOUT, MT, ST, 1>(r, P, sq, xs, M, chunk, lane, R);
+    else
+        consume_item_x<FMT, LAYOUT, MT, ST, 0>(r, P, sq, xs, M, chunk, lane, R);
 }
 
 // Partials of one warp-group tile: [item][MT * 8 rows][16 columns] 32-bit words.
@@ -476,12 +474,63 @@ __device__ __forceinline__ void group_sync(int wg) {
     asm volatile("bar.sync %0, %1;" ::"r"(1 + wg), "r"(kGroupWarps * 32) : "memory");
 }
 
-// Stage the activation block x [M][K] of a phase into shared memory (pitch K + 16): thread 0 issues one
-// TMA bulk copy per row (measured on B200: 8 row copies stage 96 KB from L2 in ~1 us, about twice as fast
-// as vector loads by 256 threads); every thread waits (bounded) on xbar with the given parity, then the
-// bytes are permuted in place unless x is permuted already. Returns false if the wait gave up.
-// CTA-uniform result (the callers' tile loops hold warp-group barriers).
-__device__ __forceinline__ bool stage_x(const PhaseDesc& p, int M, int8_t* xsm, uint64_t* xbar, int parity) {
+// Stage the activation block x [M][K] of a phase into shared memory (pitch K + 16), permuting the bytes
+// unless x is permuted already. Two paths:
+//  * vector loads by all threads (L2, every load of a batch in flight before any store) when the block is at
+//    most 16 pieces of 16 bytes per thread: these bypass the TMA unit, whose queue is full of weight copies
+//    while a phase starts (measured on B200: row copies queued behind the rings' and the L2 prefetches'
+//    requests landed 1.5-2.5 us after issue; vector loads take one L2 round trip);
+//  * otherwise one TMA bulk copy per row by thread 0, waited on (bounded) through xbar with `parity` (flipped
+//    for the barrier's next phase), and the permutation in place.
+// Returns false if a wait gave up. CTA-uniform result (the callers' tile loops hold warp-group barriers).
+__device__ __forceinline__ uint4 perm16(uint4 v) {
+    return make_uint4(prmt(v.x, v.y, 0x6420), prmt(v.x, v.y, 0x7531), prmt(v.z, v.w, 0x6420), prmt(v.z, v.w, 0x7531));
+}
+
+// One-batch vector staging split in two, so that other requests (the weight rings) can be issued while the
+// activation loads are in flight: fits when the block is at most 8 pieces of 16 bytes per thread.
+__device__ __forceinline__ bool stage_x_lsu_fits(const PhaseDesc& p, int M) { return M * (p.K >> 4) <= 8 * int(blockDim.x); }
+__device__ __forceinline__ void stage_x_lsu_load(const PhaseDesc& p, int M, uint4 (&v)[8]) {
+    const int T = blockDim.x, total = M * (p.K >> 4);
+    const uint4* src = reinterpret_cast<const uint4*>(p.x);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        if (int(threadIdx.x) + j * T < total) v[j] = __ldcg(src + threadIdx.x + j * T);
+}
+__device__ __forceinline__ void stage_x_lsu_store(const PhaseDesc& p, int M, int8_t* xsm, const uint4 (&v)[8]) {
+    const int T = blockDim.x, words = p.K >> 4, total = M * words;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int i = threadIdx.x + j * T;
+        if (i < total) {
+            const int m = i / words, c = i - m * words;
+            reinterpret_cast<uint4*>(xsm + size_t(m) * (p.K + 16))[c] = p.xperm ? v[j] : perm16(v[j]);
+        }
+    }
+    __syncthreads();
+}
+
+__device__ __forceinline__ bool stage_x(const PhaseDesc& p, int M, int8_t* xsm, uint64_t* xbar, int& parity) {
+    const int T = blockDim.x, words = p.K >> 4, total = M * words;
+    if (total <= 16 * T) {
+        const uint4* src = reinterpret_cast<const uint4*>(p.x);  // rows contiguous: piece i = (i / words, i % words)
+        for (int base = threadIdx.x; base < total; base += 8 * T) {
+            uint4 v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (base + j * T < total) v[j] = __ldcg(src + base + j * T);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = base + j * T;
+                if (i < total) {
+                    const int m = i / words, c = i - m * words;
+                    reinterpret_cast<uint4*>(xsm + size_t(m) * (p.K + 16))[c] = p.xperm ? v[j] : perm16(v[j]);
+                }
+            }
+        }
+        __syncthreads();
+        return true;
+    }
     if (threadIdx.x == 0) {
         // earlier generic accesses of the buffer (fragment reads, the permutation) before the async writes
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -493,13 +542,11 @@ __device__ __forceinline__ bool stage_x(const PhaseDesc& p, int M, int8_t* xsm, 
         }
     }
     const bool ok = __syncthreads_and(mbar_wait(xbar, parity));
+    parity ^= 1;
     if (!p.xperm) {
-        const int words = p.K >> 4, total = M * words;  // 16-byte pieces
-        for (int i = threadIdx.x; i < total; i += blockDim.x) {
-            const int m = i / words, c = i - m * words;
-            uint4* q = reinterpret_cast<uint4*>(xsm + size_t(m) * (p.K + 16)) + c;
-            const uint4 v = *q;
-            *q = make_uint4(prmt(v.x, v.y, 0x6420), prmt(v.x, v.y, 0x7531), prmt(v.z, v.w, 0x6420), prmt(v.z, v.w, 0x7531));
+        for (int m = 0; m < M; ++m) {
+            uint4* row = reinterpret_cast<uint4*>(xsm + size_t(m) * (p.K + 16));
+            for (int c = threadIdx.x; c < words; c += T) row[c] = perm16(row[c]);
         }
         __syncthreads();
     }

@@ -27,8 +27,11 @@ __device__ __forceinline__ bool grid_barrier(unsigned* counter, unsigned& epoch,
         asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
         bool ok = true;
         uint32_t spins = 0;
+        const unsigned long long t0 = globaltimer();
         while (ld_acquire_gpu(counter) < target) {
-            if (++spins > kGridSpinLimit) {
+            // short sleeps between polls leave the issue slots to the warps that still stream
+            __nanosleep(32);
+            if (++spins > kGridSpinLimit || globaltimer() - t0 > kWaitLimitNs) {
                 set_device_error(DEV_GRID_TIMEOUT);
                 ok = false;
                 break;

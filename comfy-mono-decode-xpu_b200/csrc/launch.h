@@ -1,0 +1,51 @@
+// Argument blocks and launchers shared by the C-ABI entry points and the kernel translation units.
+#pragma once
+#include "abi_internal.h"
+#include "engine.cuh"
+
+namespace mono {
+
+// Shared bytes after the staged rows for the fused quantization: 16 row scales + 8 reduction floats per
+// warp-group.
+constexpr int kQuantExtra = 256;
+
+struct LinearEpi {
+    const uint16_t* xb;      // bf16 activations [M][K]: quantized per token inside the kernel (xs unused), or null
+    const float* xs;         // [M]
+    const float* s_channel;  // REF: [N]
+    const void* residual;    // [M][N] output dtype, or null
+    void* out;               // [M][N]
+    int out_bf16;
+    int max_items;
+};
+int launch_linear(int fmt, int layout, Program& P, LinearEpi& E, cudaStream_t stream);
+
+struct MlpArgs {
+    const uint16_t* x;       // [M][H] bf16
+    const uint16_t* norm_w;  // [H] bf16 or null
+    const uint16_t* lut;     // [65536] bf16: silu of every bf16 pattern
+    uint16_t* out;           // [M][H] bf16
+    float eps;
+    int H, I, residual, max_items;
+    // workspace
+    uint16_t* xn;     // [M][H]
+    int8_t* q1;       // [M][H]
+    float* s1;        // [16]
+    uint16_t* h;      // [M][I]
+    unsigned* amax2;  // [16] (float bits of non-negative values)
+    int8_t* q2;       // [M][I]
+    float* s2;        // [16]
+    unsigned* bar;    // [2] grid barrier words (zero between launches)
+};
+int launch_mlp(Program& P, MlpArgs& A, cudaStream_t stream);
+size_t mlp_workspace_bytes(int H, int I);
+
+int launch_repack(int fmt, const void* q, const void* s, int N, int K, void* out, cudaStream_t stream);
+size_t tiled_bytes(int fmt, int64_t N, int64_t K);
+int launch_pair_table(const float* codebook, uint16_t* tab, cudaStream_t stream);
+int launch_act_quant(const void* x, int M, int K, int8_t* q, float* xs, cudaStream_t stream);
+size_t rot_quant_workspace(int M, int K);
+int launch_rot_quant(const void* x, const void* h, int M, int K, int8_t* q, float* s, void* ws, cudaStream_t stream);
+int launch_rot_quant_noalloc(const void* x, const void* h, int M, int K, int8_t* q, float* s, cudaStream_t stream);
+
+}  // namespace mono

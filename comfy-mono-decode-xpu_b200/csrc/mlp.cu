@@ -10,30 +10,15 @@
 // gate/up and down weights stream while rows are normalized and quantized.
 #include <mutex>
 
-#include "abi_internal.h"
-#include "engine.cuh"
+#include "launch.h"
 #include "grid.cuh"
 #include "rowops.cuh"
 
 namespace mono {
 
-struct MlpArgs {
-    const uint16_t* x;       // [M][H] bf16
-    const uint16_t* norm_w;  // [H] bf16 or null
-    const uint16_t* lut;     // [65536] bf16: silu of every bf16 pattern
-    uint16_t* out;           // [M][H] bf16
-    float eps;
-    int H, I, residual, max_items;
-    // workspace
-    uint16_t* xn;     // [M][H]
-    int8_t* q1;       // [M][H]
-    float* s1;        // [16]
-    uint16_t* h;      // [M][I]
-    unsigned* amax2;  // [16] (float bits of non-negative values)
-    int8_t* q2;       // [M][I]
-    float* s2;        // [16]
-    unsigned* bar;    // [2] grid barrier words (zero between launches)
-};
+// Items each warp keeps requested into L2 beyond its ring: the weight stream runs on through the row
+// phases and grid barriers (the role of the reference's prefetch_stream, csrc/mono_common.hpp:318-340).
+constexpr int kMlpPrefetch = 6;
 
 template <int MT, int GROUPS, int ST>
 __global__ void __launch_bounds__(GROUPS * 128) mlp_kernel(const Program P, const MlpArgs A) {
@@ -64,14 +49,12 @@ __global__ void __launch_bounds__(GROUPS * 128) mlp_kernel(const Program P, cons
     }
     __syncthreads();
     trace_stamp(0);
-    TileCursor pf = tile_start(P, sq, 0);
-    const bool pf_lane = tig == 0;
-    if (pf_lane) {
-        tile_advance(P, sq, pf);  // the first tile is in the rings
-        prefetch_ahead<FMT_GPTQ>(P, sq, pf, true);
-    }
-    ring.init(P, sq, lane);
     pdl_launch_dependents();  // the next kernel may launch and stream its weights as our CTAs exit
+    // Warp-groups without a P1 row start their weight streams before the dependency wait; those with a
+    // row load it first (vector loads), so its requests are not queued behind weight copies in this SM's
+    // TMA unit, and start their streams right after.
+    const bool has_row = sq.vc < M;
+    if (!has_row) ring.init(P, sq, lane, kMlpPrefetch);
     pdl_wait();
     trace_stamp(1);
     unsigned epoch = 0;
@@ -82,6 +65,7 @@ __global__ void __launch_bounds__(GROUPS * 128) mlp_kernel(const Program P, cons
     for (int m = sq.vc; m < M; m += sq.nvc)
         norm_quant_row(A.x + size_t(m) * A.H, A.norm_w, A.eps, A.H, nullptr, A.q1 + size_t(m) * A.H, A.s1 + m, red[wg],
                        tig, wg);
+    if (has_row) ring.init(P, sq, lane, kMlpPrefetch);
     trace_stamp(2);
     ok = grid_barrier(A.bar, epoch, &flag);
     trace_stamp(3);
@@ -91,7 +75,6 @@ __global__ void __launch_bounds__(GROUPS * 128) mlp_kernel(const Program P, cons
         const PhaseDesc& p = P.ph[ph];
         if (!p.xsmem) return XSrc{p.x, p.K, false, true};
         ok = stage_x(p, M, xsm, xbar, xpar) && ok;
-        xpar ^= 1;
         return XSrc{xsm, p.K + 16, true, true};
     };
 
@@ -106,7 +89,6 @@ __global__ void __launch_bounds__(GROUPS * 128) mlp_kernel(const Program P, cons
         for (int ti = 0; ti < ntiles && ok; ++ti) {
             const int T = sq.vc + ti * sq.nvc;
             uint32_t* pt = part + (ti & 1) * A.max_items * MT * 128;
-            if (pf_lane) prefetch_ahead<FMT_GPTQ>(P, sq, pf, false);
             for (int item = warp; item < items; item += kGroupWarps) {
                 uint32_t R[MT][4];
                 consume_item<FMT_GPTQ, LAYOUT_TILED, MT, ST>(ring, P, sq, xs, M, item % C, lane, R);
@@ -173,7 +155,6 @@ __global__ void __launch_bounds__(GROUPS * 128) mlp_kernel(const Program P, cons
         for (int ti = 0; ti < ntiles && ok; ++ti) {
             const int T = sq.vc + ti * sq.nvc;
             uint32_t* pt = part + (ti & 1) * A.max_items * MT * 128;
-            if (pf_lane) prefetch_ahead<FMT_GPTQ>(P, sq, pf, false);
             for (int item = warp; item < items; item += kGroupWarps) {
                 uint32_t R[MT][4];
                 consume_item<FMT_GPTQ, LAYOUT_TILED, MT, ST>(ring, P, sq, xs, M, item % C, lane, R);

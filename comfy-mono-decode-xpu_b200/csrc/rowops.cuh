@@ -114,4 +114,91 @@ __device__ __forceinline__ void norm_quant_row(const uint16_t* __restrict__ x, c
     wg_sync(wg);
 }
 
+// Per-token quantization of a whole activation block x [M][K] bf16 by the first T threads of the CTA
+// (named barrier BAR), into the permuted int8 rows of a shared buffer (row pitch `pitch`) and the row
+// scales xs[M]. Rows are taken in batches whose 16-byte pieces fit 8 per thread, so a batch costs one round
+// trip to L2: every load of a batch is issued before any is used. Row maxima meet in shared memory
+// (rowmax[16], float bits: the values are non-negative, so integer order is float order; zeroed here).
+// Same results as the per-token quantization above (amax is order-free).
+template <int T, int BAR>
+__device__ __forceinline__ void quant_block(const uint16_t* __restrict__ x, int M, int K, int8_t* __restrict__ xsm,
+                                            int pitch, float* __restrict__ xs, unsigned* rowmax) {
+    auto sync = [] { asm volatile("bar.sync %0, %1;" ::"n"(BAR), "n"(T) : "memory"); };
+    const int tid = threadIdx.x, lane = tid & 31, P = K >> 3;  // P % 128 == 0
+    if (tid < 16) rowmax[tid] = 0u;
+    sync();
+    const int RB = (8 * T) / P > 0 ? ((8 * T) / P < M ? (8 * T) / P : M) : 1;
+    for (int r0 = 0; r0 < M; r0 += RB) {
+        const int rb = M - r0 < RB ? M - r0 : RB;
+        const int n = rb * P;
+        const uint4* src = reinterpret_cast<const uint4*>(x + size_t(r0) * K);
+        uint4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int i = tid + T * j;
+            if (i < n) v[j] = __ldcg(src + i);
+        }
+        if (RB == 1 && P > 8 * T) {
+            // one row longer than the threads hold in registers: fold the rest of it in a second loop (the
+            // quantization pass below re-reads those pieces)
+            float am = 0.f;
+            for (int i = tid + 8 * T; i < P; i += T) {
+                const uint4 w = __ldcg(src + i);
+                const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                    am = fmaxf(am, fabsf(__uint_as_float((e & 1) ? (u[e >> 1] & 0xFFFF0000u) : (u[e >> 1] << 16))));
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+            if (lane == 0) atomicMax(rowmax + r0, __float_as_uint(am));
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int i = tid + T * j;
+            if (T * j < n) {  // warp-uniform: n and T are multiples of 32
+                float am = 0.f;
+                if (i < n) {
+                    const uint32_t u[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        am = fmaxf(am, fabsf(__uint_as_float((e & 1) ? (u[e >> 1] & 0xFFFF0000u) : (u[e >> 1] << 16))));
+                }
+#pragma unroll
+                for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+                // the 32 pieces of a warp lie in one row (P % 32 == 0)
+                if (lane == 0 && i < n) atomicMax(rowmax + r0 + i / P, __float_as_uint(am));
+            }
+        }
+        sync();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int i = tid + T * j;
+            if (i < n) {
+                const int r = i / P, c = i - r * P;
+                const float s = __fdiv_rn(__uint_as_float(rowmax[r0 + r]), 127.f);
+                const uint32_t u[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+                float vals[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) vals[e] = __uint_as_float((e & 1) ? (u[e >> 1] & 0xFFFF0000u) : (u[e >> 1] << 16));
+                reinterpret_cast<uint2*>(xsm + size_t(r0 + r) * pitch)[c] = quant8_perm(vals, s);
+            }
+        }
+        if (RB == 1 && P > 8 * T) {
+            const float s = __fdiv_rn(__uint_as_float(rowmax[r0]), 127.f);
+            for (int i = tid + 8 * T; i < P; i += T) {
+                const uint4 w = __ldcg(src + i);
+                const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+                float vals[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) vals[e] = __uint_as_float((e & 1) ? (u[e >> 1] & 0xFFFF0000u) : (u[e >> 1] << 16));
+                reinterpret_cast<uint2*>(xsm + size_t(r0) * pitch)[i] = quant8_perm(vals, s);
+            }
+        }
+    }
+    sync();
+    if (tid < M) xs[tid] = __fdiv_rn(__uint_as_float(rowmax[tid]), 127.f);
+    sync();
+}
+
 }  // namespace mono

@@ -2,8 +2,7 @@
 #include <cstdio>
 #include <mutex>
 
-#include "abi_internal.h"
-#include "engine.cuh"
+#include "launch.h"
 
 namespace mono {
 

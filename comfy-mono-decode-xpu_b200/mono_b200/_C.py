@@ -91,7 +91,7 @@ def w4a8_decode_linear(x, x_scale, packed, s_rel, s_channel, codebook=None, resi
     return out
 
 
-def w4a8_gptq_linear(x, x_scale, packed, scales, residual=None, out_dtype_code=2, tiled=False, N=None):
+def w4a8_gptq_linear(x, x_scale, packed, scales, residual=None, out_dtype_code=2, tiled=False, N=None, out=None):
     """GPTQ W4A8 linear (BASELINE configs[0] format): int4 nibbles v + 8 [N, K/2], fp16 scales [N, K/128];
     tiled=True: `packed` is the w4_repack copy (pass N; `scales` is ignored)."""
     _cuda(x, x_scale, packed)
@@ -107,13 +107,40 @@ def w4a8_gptq_linear(x, x_scale, packed, scales, residual=None, out_dtype_code=2
                "scales must be contiguous fp16 [N, K/128]")
     _check(x_scale.dtype == torch.float32 and x_scale.numel() == M, "x_scale f32 [M]")
     dtype = torch.float32 if out_dtype_code == 0 else torch.bfloat16
-    out = torch.empty((M, N), dtype=dtype, device=x.device)
+    if out is None:
+        out = torch.empty((M, N), dtype=dtype, device=x.device)
+    _check(out.dtype == dtype and out.is_contiguous() and out.numel() == M * N, "out must be contiguous [M, N]")
     if residual is not None:
         _check(residual.dtype == dtype and residual.is_contiguous() and residual.numel() == M * N,
                "residual must match output")
     with torch.cuda.device(x.device):
         _lib.call("mono_w4a8_gptq_linear", _p(x), _p(x_scale), _p(packed), _p(scales), _p(residual), M, N, K,
                   out_dtype_code, _lib.LAYOUT_TILED if tiled else _lib.LAYOUT_ROW, _p(out), _stream(x.device))
+    return out
+
+
+def w4a8_gptq_linear_bf16(x, packed, scales, residual=None, out_dtype_code=2, tiled=False, N=None, out=None):
+    """Config 0's whole op in one launch: bf16 x [M, K] -> per-token int8 quant (in the kernel) -> GPTQ W4A8
+    GEMV -> out. Same results as act_quant followed by w4a8_gptq_linear."""
+    _cuda(x, packed)
+    _check(x.dtype == torch.bfloat16 and x.dim() == 2 and x.is_contiguous(), "x must be contiguous bf16 [M, K]")
+    M, K = x.shape
+    if tiled:
+        _check(N is not None and packed.numel() == _lib.load().mono_w4_tiled_bytes(0, N, K), "tiled weight size")
+    else:
+        N = packed.shape[0]
+        _check(packed.numel() * packed.element_size() == N * K // 2 and packed.is_contiguous(), "packed [N, K/2] bytes")
+        _check(scales.dtype == torch.float16 and scales.numel() == N * (K // 128), "scales fp16 [N, K/128]")
+    dtype = torch.float32 if out_dtype_code == 0 else torch.bfloat16
+    if out is None:
+        out = torch.empty((M, N), dtype=dtype, device=x.device)
+    _check(out.dtype == dtype and out.is_contiguous() and out.numel() == M * N, "out must be contiguous [M, N]")
+    if residual is not None:
+        _check(residual.dtype == dtype and residual.is_contiguous() and residual.numel() == M * N,
+               "residual must match output")
+    with torch.cuda.device(x.device):
+        _lib.call("mono_w4a8_gptq_linear_bf16", _p(x), _p(packed), _p(scales), _p(residual), M, N, K, out_dtype_code,
+                  _lib.LAYOUT_TILED if tiled else _lib.LAYOUT_ROW, _p(out), _stream(x.device))
     return out
 
 

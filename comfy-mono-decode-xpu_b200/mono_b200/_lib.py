@@ -27,6 +27,7 @@ SIGNATURES = {
     "mono_w4a8_decode_linear": (I, [P, P, P, P, I, P, P, P, I64, I64, I64, I64, I, I, P, P]),
     "mono_w4_pair_table": (I, [P, P, P]),
     "mono_w4a8_gptq_linear": (I, [P, P, P, P, P, I64, I64, I64, I, I, P, P]),
+    "mono_w4a8_gptq_linear_bf16": (I, [P, P, P, P, I64, I64, I64, I, I, P, P]),
     "mono_w4_tiled_bytes": (SZ, [I, I64, I64]),
     "mono_w4_repack": (I, [I, P, P, I64, I64, P, P]),
     "mono_act_quant": (I, [P, I64, I64, P, P, P]),

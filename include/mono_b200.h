@@ -86,6 +86,16 @@ MONO_API int mono_w4a8_gptq_linear(const int8_t* x, const float* x_scale, const 
                           const void* residual, int64_t M, int64_t N, int64_t K, int out_dtype_code, int layout,
                           void* out, mono_stream_t stream);
 
+/* The same linear from bf16 activations x [M, K]: the per-token int8 quantization (mono_act_quant's
+ * arithmetic, bit for bit) runs inside the kernel, so config 0's whole op (bf16 in -> quant -> W4A8 GEMV
+ * -> bf16 out) is one launch. The quantized rows are held in shared memory: shapes whose M * (K + 16)
+ * bytes do not fit next to the weight rings return MONO_EINVAL (use mono_act_quant + the entry above).
+ * No reference counterpart (the reference quantizes inside its fused layer kernels,
+ * csrc/mono_layer.sycl:69-155). */
+MONO_API int mono_w4a8_gptq_linear_bf16(const void* x, const void* packed, const void* scales, const void* residual,
+                                        int64_t M, int64_t N, int64_t K, int out_dtype_code, int layout, void* out,
+                                        mono_stream_t stream);
+
 /* Tile-major copy of a W4 weight for the TILED layout (the role of tiles.py tile_major,
  * comfy_mono_decode_xpu/tiles.py:45-48, in this build's own layout): one buffer of
  * mono_w4_tiled_bytes(fmt, N, K) bytes holding, per (16-row tile, 1024-wide chunk), the chunk's weights in

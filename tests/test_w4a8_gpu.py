@@ -35,6 +35,47 @@ def test_gptq_linear_bit_exact(cuda, N, K, tiled):
         assert bits_equal(bf16_bits(out), ref), (M, N, K, tiled)
 
 
+@pytest.mark.parametrize("N,K", [(12288, 4096), (4096, 12288), (1024, 4096), (48, 3072)])
+@pytest.mark.parametrize("tiled", [False, True])
+def test_gptq_linear_bf16_fused_quant(cuda, N, K, tiled):
+    """bf16 x with the per-token quantization inside the kernel == act_quant then the int8 linear (oracle),
+    including all-zero rows (scale 0) and a row of one large value."""
+    from mono_b200 import _C
+    packed, scales = ow.gen_gptq(N, K, seed=0x5EED + 7 * N + K)
+    pk = torch.from_numpy(packed).to(cuda)
+    sc = torch.from_numpy(scales).to(cuda)
+    if tiled:
+        pk, sc = _C.w4_repack(0, pk, sc, N, K), None
+    g = torch.Generator().manual_seed(N + 5 * K)
+    for M in (1, 4, 8, 13, 16):
+        if K > 4096 and M > 8:  # the staged rows of larger blocks do not fit next to the rings
+            continue
+        x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+        if M >= 4:
+            x[1] = 0
+            x[2] = 0
+            x[2, K // 3] = 300.0
+        xb = x.view(torch.int16).numpy().view(np.uint16)
+        xq, xs = ow.act_quant(xb)
+        ref = ow.gptq_linear(xq, xs, packed, scales)
+        out = _C.w4a8_gptq_linear_bf16(x.to(cuda), pk, sc, tiled=tiled, N=N)
+        assert bits_equal(bf16_bits(out), ref), (M, N, K, tiled)
+        res = torch.randn(M, N, generator=g).to(torch.bfloat16)
+        ref_r = ow.gptq_linear(xq, xs, packed, scales, residual=bf16_bits(res))
+        out_r = _C.w4a8_gptq_linear_bf16(x.to(cuda), pk, sc, residual=res.to(cuda), tiled=tiled, N=N)
+        assert bits_equal(bf16_bits(out_r), ref_r), (M, N, K, tiled, "residual")
+
+
+def test_gptq_linear_bf16_rejects_oversized_rows(cuda):
+    from mono_b200 import _C
+    from mono_b200._lib import MonoError
+    N, K, M = 64, 16384, 16
+    packed, scales = ow.gen_gptq(N, K, seed=1)
+    x = torch.zeros(M, K, dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(MonoError, match="bf16 input"):
+        _C.w4a8_gptq_linear_bf16(x, torch.from_numpy(packed).to(cuda), torch.from_numpy(scales).to(cuda))
+
+
 def test_gptq_linear_residual_and_fp32(cuda):
     from mono_b200 import _C
     N, K, M = 2048, 4096, 5
