@@ -54,4 +54,41 @@ __device__ __forceinline__ void grid_exit(unsigned* counter) {
     }
 }
 
+// The same two operations for kernels whose CTA-wide syncs are a named barrier of the first NT threads
+// (the consumer warps of a stream kernel; its producer warps never wait at a grid barrier).
+template <int BAR, int NT>
+__device__ __forceinline__ bool grid_barrier_named(unsigned* counter, unsigned& epoch, int* flag) {
+    asm volatile("bar.sync %0, %1;" ::"n"(BAR), "n"(NT) : "memory");
+    ++epoch;
+    if (threadIdx.x == 0) {
+        const unsigned target = epoch * gridDim.x;
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
+        bool ok = true;
+        uint32_t spins = 0;
+        const unsigned long long t0 = globaltimer();
+        while (ld_acquire_gpu(counter) < target) {
+            if ((++spins & 255) == 0 && globaltimer() - t0 > kWaitLimitNs) {
+                set_device_error(DEV_GRID_TIMEOUT);
+                ok = false;
+                break;
+            }
+        }
+        *flag = ok;
+    }
+    asm volatile("bar.sync %0, %1;" ::"n"(BAR), "n"(NT) : "memory");
+    return *flag != 0;
+}
+
+template <int BAR, int NT>
+__device__ __forceinline__ void grid_exit_named(unsigned* counter) {
+    asm volatile("bar.sync %0, %1;" ::"n"(BAR), "n"(NT) : "memory");
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(counter + 1, 1u) == gridDim.x - 1) {
+            atomicExch(counter, 0u);
+            atomicExch(counter + 1, 0u);
+        }
+    }
+}
+
 }  // namespace mono
