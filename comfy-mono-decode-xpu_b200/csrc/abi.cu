@@ -228,4 +228,82 @@ int mono_mlp_gptq(const void* x, const void* norm_w, float eps, const void* gate
     return launch_mlp(P, A, reinterpret_cast<cudaStream_t>(stream));
 }
 
+
+int mono_qk_norm_rope_kv(const void* rawq, int64_t q_row_stride, int64_t q_head_stride, const void* rawk,
+                         int64_t k_row_stride, const void* v, int64_t v_row_stride, const void* wq, const void* wk,
+                         const float* freqs, void* key_cache, void* value_cache, int64_t cap, const int64_t* position,
+                         int64_t S, int64_t Hq, int64_t Hk, float epsq, float epsk, int64_t rd, void* out_q,
+                         void* out_k, mono_stream_t stream) {
+    MONO_CHECK(rawq && rawk && v && wq && wk && freqs && key_cache && value_cache && position && out_q && out_k,
+               "null operand");
+    MONO_CHECK(S >= 1 && S <= 8, "1 <= S <= 8 decode rows (got %lld)", (long long)S);
+    MONO_CHECK(Hq >= 1 && Hk >= 1 && Hq <= 1024 && Hk <= 1024, "head counts");
+    MONO_CHECK(rd >= 2 && rd <= 256 && rd % 2 == 0, "even rotary dimension in [2, 256] (got %lld)", (long long)rd);
+    MONO_CHECK(cap >= 1 && epsq > 0.f && epsk > 0.f, "positive capacity and eps");
+    MONO_CHECK(q_head_stride >= 256 && q_row_stride >= Hq * q_head_stride && k_row_stride >= Hk * 256 &&
+                   v_row_stride >= Hk * 256 && q_head_stride % 8 == 0 && q_row_stride % 8 == 0 &&
+                   k_row_stride % 8 == 0 && v_row_stride % 8 == 0,
+               "strides (elements): q head >= 256, rows cover their heads, multiples of 8");
+    const void* ptrs[] = {rawq, rawk, v, wq, wk, key_cache, value_cache, out_q, out_k};
+    for (const void* ptr : ptrs) MONO_CHECK(aligned(ptr, 16), "16-byte aligned operands");
+    MONO_CHECK(aligned(freqs, 4) && aligned(position, 8), "aligned freqs / positions");
+    NormRopeArgs A{};
+    A.q = static_cast<const uint16_t*>(rawq);
+    A.k = static_cast<const uint16_t*>(rawk);
+    A.v = static_cast<const uint16_t*>(v);
+    A.wq = static_cast<const uint16_t*>(wq);
+    A.wk = static_cast<const uint16_t*>(wk);
+    A.freqs = freqs;
+    A.kc = static_cast<uint16_t*>(key_cache);
+    A.vc = static_cast<uint16_t*>(value_cache);
+    A.pos = position;
+    A.oq = static_cast<uint16_t*>(out_q);
+    A.ok = static_cast<uint16_t*>(out_k);
+    A.qs = q_row_stride;
+    A.qh = q_head_stride;
+    A.ks = k_row_stride;
+    A.vs = v_row_stride;
+    A.cap = cap;
+    A.S = int(S);
+    A.Hq = int(Hq);
+    A.Hk = int(Hk);
+    A.rd = int(rd);
+    A.epsq = epsq;
+    A.epsk = epsk;
+    return launch_qk_norm_rope_kv(A, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t mono_tree_attention_workspace(int64_t Hk, int64_t cap) {
+    if (Hk < 1 || cap < 1) return 0;
+    return attn_workspace_bytes(int(Hk), int(cap), sm_count());
+}
+
+int mono_tree_attention(const void* q, const void* key_cache, const void* value_cache, const int32_t* seqlen,
+                        const void* xk, const void* xv, const int32_t* mask, int64_t H, int64_t Hk, int64_t S,
+                        int64_t cap, void* out, void* workspace, size_t workspace_bytes, mono_stream_t stream) {
+    MONO_CHECK(q && key_cache && value_cache && seqlen && out && workspace, "null operand");
+    MONO_CHECK(S >= 1 && S <= 8 && Hk >= 1 && H % Hk == 0 && (H / Hk) * S <= 32,
+               "1..8 rows, H a multiple of Hk, (H / Hk) * S <= 32 query rows per kv head");
+    MONO_CHECK(mask != nullptr || S == 1, "a tree mask for S > 1 rows (S = 1 without a mask: the draft row)");
+    MONO_CHECK(mask == nullptr || (xk && xv), "tree rows need xk / xv");
+    MONO_CHECK(cap >= 1 && cap <= (int64_t(1) << 30), "cache capacity");
+    MONO_CHECK(workspace_bytes >= mono_tree_attention_workspace(Hk, cap), "workspace too small (mono_tree_attention_workspace)");
+    const void* ptrs[] = {q, key_cache, value_cache, out, workspace};
+    for (const void* ptr : ptrs) MONO_CHECK(aligned(ptr, 16), "16-byte aligned operands");
+    AttnArgs A{};
+    A.q = static_cast<const uint16_t*>(q);
+    A.kc = static_cast<const uint16_t*>(key_cache);
+    A.vc = static_cast<const uint16_t*>(value_cache);
+    A.seqlen = seqlen;
+    A.xk = static_cast<const uint16_t*>(xk);
+    A.xv = static_cast<const uint16_t*>(xv);
+    A.mask = mask;
+    A.out = static_cast<uint16_t*>(out);
+    A.H = int(H);
+    A.Hk = int(Hk);
+    A.S = int(S);
+    A.cap = int(cap);
+    return launch_tree_attention(A, workspace, reinterpret_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

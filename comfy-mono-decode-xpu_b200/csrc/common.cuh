@@ -16,6 +16,7 @@ enum DeviceError : int {
     DEV_MBAR_TIMEOUT = 1,   // an mbarrier wait ran past its iteration limit
     DEV_GRID_TIMEOUT = 2,   // a grid-wide barrier ran past its iteration limit
     DEV_FLAG_TIMEOUT = 3,   // a flag wait (peer / producer) ran past its iteration limit
+    DEV_BAD_POSITION = 4,   // a KV-cache position outside [0, capacity): the write was skipped
 };
 extern __device__ int g_device_error;
 

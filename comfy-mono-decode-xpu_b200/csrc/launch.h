@@ -48,4 +48,38 @@ size_t rot_quant_workspace(int M, int K);
 int launch_rot_quant(const void* x, const void* h, int M, int K, int8_t* q, float* s, void* ws, cudaStream_t stream);
 int launch_rot_quant_noalloc(const void* x, const void* h, int M, int K, int8_t* q, float* s, cudaStream_t stream);
 
+struct NormRopeArgs {
+    const uint16_t* q;  // [S][Hq] heads, row stride qs, head stride qh (elements)
+    const uint16_t* k;  // [S][Hk][256], row stride ks
+    const uint16_t* v;  // [S][Hk][256], row stride vs
+    const uint16_t* wq;
+    const uint16_t* wk;
+    const float* freqs;  // [S][rd/2][2][2]
+    uint16_t* kc;        // [Hk][cap][256]
+    uint16_t* vc;
+    const int64_t* pos;
+    uint16_t* oq;  // [Hq][S][256]
+    uint16_t* ok;  // [Hk][S][256]
+    int64_t qs, qh, ks, vs, cap;
+    int S, Hq, Hk, rd;
+    float epsq, epsk;
+};
+int launch_qk_norm_rope_kv(const NormRopeArgs& A, cudaStream_t stream);
+
+struct AttnArgs {
+    const uint16_t* q;    // [H][S][256]
+    const uint16_t* kc;   // [Hk][cap][256]
+    const uint16_t* vc;
+    const int32_t* seqlen;
+    const uint16_t* xk;   // [Hk][S][256]
+    const uint16_t* xv;
+    const int32_t* mask;  // [S] or null
+    uint16_t* out;        // [S][H * 256]
+    float* part;          // [Hk][chunks][32][256]
+    float* ml;            // [Hk][chunks][32][2]
+    int H, Hk, S, cap, chunks;
+};
+size_t attn_workspace_bytes(int Hk, int cap, int sms);
+int launch_tree_attention(AttnArgs A, void* ws, cudaStream_t stream);
+
 }  // namespace mono

@@ -250,3 +250,57 @@ def mlp_gptq(x, norm_w, eps, gate, up, down, silu_lut=None, residual=True, out=N
         _lib.call("mono_mlp_gptq", _p(x), _p(norm_w), float(eps), _p(gate), _p(up), _p(down), _p(silu_lut), M, H, I,
                   1 if residual else 0, _p(out), _p(ws), need, _stream(x.device))
     return out
+
+
+def qk_norm_rope_kv(rawq, rawk, vn, weightq, weightk, freqs, key, value, position, epsq, epsk, rd):
+    """Q/K head RMSNorm + partial RoPE + K/V cache write (the reference's _C.qk_norm_rope_kv,
+    csrc/rope_kv.sycl:120-245). rawq bf16 [1, S, Hq, 256] (the query half of gated heads: head stride 512, or
+    dense), rawk / vn bf16 [1, S, Hk, 256] (dense heads), weights bf16 [256], freqs fp32 [S, rd/2, 2, 2], key /
+    value caches bf16 [1, Hk, cap, 256] (written in place at position[s]), position int64 [>= S].
+    Returns (q [1, Hq, S, 256], k [1, Hk, S, 256])."""
+    _cuda(rawq, rawk, vn, weightq, weightk, freqs, key, value, position)
+    _check(rawq.dtype == torch.bfloat16 and rawq.dim() == 4 and rawq.size(0) == 1 and rawq.size(3) == 256
+           and rawq.stride(3) == 1, "Q: bf16 [1, S, Hq, 256]")
+    S, Hq, Hk = rawq.size(1), rawq.size(2), rawk.size(2)
+    _check(rawk.dim() == 4 and rawk.shape == vn.shape and rawk.size(1) == S and rawk.stride(3) == 1 and
+           rawk.stride(2) == 256 and vn.stride(3) == 1 and vn.stride(2) == 256, "K/V: bf16 [1, S, Hk, 256], dense heads")
+    _check(key.is_contiguous() and value.is_contiguous() and key.shape == value.shape and key.dim() == 4 and
+           key.size(1) == Hk and key.size(3) == 256, "K/V cache: bf16 [1, Hk, cap, 256]")
+    _check(freqs.dtype == torch.float32 and freqs.is_contiguous() and freqs.numel() == S * (rd // 2) * 4,
+           "frequencies: fp32 [S, rd/2, 2, 2]")
+    _check(position.dtype == torch.int64 and position.is_contiguous() and position.numel() >= S, "int64 positions")
+    _check(weightq.is_contiguous() and weightk.is_contiguous(), "contiguous norm weights")
+    q = torch.empty((1, Hq, S, 256), dtype=torch.bfloat16, device=rawq.device)
+    k = torch.empty((1, Hk, S, 256), dtype=torch.bfloat16, device=rawq.device)
+    with torch.cuda.device(rawq.device):
+        _lib.call("mono_qk_norm_rope_kv", _p(rawq), rawq.stride(1), rawq.stride(2), _p(rawk), rawk.stride(1), _p(vn),
+                  vn.stride(1), _p(weightq), _p(weightk), _p(freqs), _p(key), _p(value), key.size(2), _p(position), S, Hq,
+                  Hk, float(epsq), float(epsk), int(rd), _p(q), _p(k), _stream(rawq.device))
+    return q, k
+
+
+_attn_ws = {}
+
+
+def attn_dpas(q, key, value, seqlen, xk, xv, mask, chunks_hint=0):
+    """Tree decode attention (the reference's _C.attn_dpas, csrc/attn_dpas.sycl:269-342). q bf16 [1, H, S, 256];
+    key / value bf16 [1, Hk, cap, 256]; seqlen int32 [1] on the device (L, no host sync); xk / xv bf16
+    [1, Hk, S, 256]; mask int32 [S] (an empty tensor: the single draft row over the prefix only).
+    Returns bf16 [1, S, H * 256]. chunks_hint is accepted for the reference's signature and unused."""
+    _cuda(q, key, value, seqlen, xk, xv)
+    _check(q.dtype == torch.bfloat16 and q.dim() == 4 and q.size(0) == 1 and q.size(3) == 256, "q bf16 [1, H, S, 256]")
+    H, S, Hk, cap = q.size(1), q.size(2), key.size(1), key.size(2)
+    _check(key.is_contiguous() and value.is_contiguous() and key.shape == value.shape and key.size(3) == 256,
+           "cache bf16 [1, Hk, cap, 256]")
+    _check(seqlen.dtype == torch.int32 and mask.dtype == torch.int32, "int32 seqlen / mask")
+    tree = mask.numel() > 0
+    _check(mask.numel() == S if tree else S == 1, "mask [S] (or empty with one row)")
+    q = q.contiguous()
+    xk, xv = xk.contiguous(), xv.contiguous()
+    nbytes = _lib.load().mono_tree_attention_workspace(Hk, cap)
+    ws = _workspace(_attn_ws, (q.device, Hk, cap), nbytes, q.device)
+    out = torch.empty((1, S, H * 256), dtype=torch.bfloat16, device=q.device)
+    with torch.cuda.device(q.device):
+        _lib.call("mono_tree_attention", _p(q), _p(key), _p(value), _p(seqlen), _p(xk), _p(xv),
+                  _p(mask) if tree else None, H, Hk, S, cap, _p(out), _p(ws), nbytes, _stream(q.device))
+    return out

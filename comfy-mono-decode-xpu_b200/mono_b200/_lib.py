@@ -36,6 +36,10 @@ SIGNATURES = {
     "mono_rot_quant_noalloc": (I, [P, P, I64, I64, P, P, P]),
     "mono_mlp_gptq_workspace": (SZ, [I64, I64]),
     "mono_mlp_gptq": (I, [P, P, ctypes.c_float, P, P, P, P, I64, I64, I64, I, P, P, SZ, P]),
+    "mono_qk_norm_rope_kv": (I, [P, I64, I64, P, I64, P, I64, P, P, P, P, P, I64, P, I64, I64, I64, ctypes.c_float,
+                                 ctypes.c_float, I64, P, P, P]),
+    "mono_tree_attention_workspace": (SZ, [I64, I64]),
+    "mono_tree_attention": (I, [P, P, P, P, P, P, P, I64, I64, I64, I64, P, P, SZ, P]),
 }
 
 MONO_OK, MONO_EINVAL, MONO_ECUDA, MONO_ETIMEOUT, MONO_EDEVICE = 0, 1, 2, 3, 4

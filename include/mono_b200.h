@@ -151,6 +151,39 @@ MONO_API int mono_mlp_gptq(const void* x, const void* norm_w, float eps, const v
                            const void* down, const void* silu_lut, int64_t M, int64_t H, int64_t I, int residual,
                            void* out, void* workspace, size_t workspace_bytes, mono_stream_t stream);
 
+/* ---- full-attention decode layer ------------------------------------------------------------------ */
+
+/* Per-head Q/K RMSNorm + partial split-half RoPE + K/V cache write (the role of the reference's
+ * qk_norm_rope_kv, csrc/rope_kv.sycl:120-245; bindings.cpp exposes it as _C.qk_norm_rope_kv).
+ * rawq: bf16 query heads [S][Hq] of 256 (row / head strides in elements: the query half of gated heads has
+ * head stride 512); rawk, v: bf16 [S][Hk][256] (row strides in elements); wq, wk: bf16 [256] norm weights;
+ * freqs: fp32 [S][rd/2][2][2] ([[f00, f01], [f10, f11]] per pair); key/value caches bf16 [Hk][cap][256];
+ * position: int64 [S] device positions (outside [0, cap): the write is skipped, mono_device_status reports
+ * code 4). Head norm: lane sums of squares over 8-element pieces, xor butterfly, r = 1 / sqrt(sum / 256 + eps),
+ * bf16((x * r) * w) (this build's pinned order); RoPE per pair j < rd/2 of the normalized row:
+ *   o0 = t[j] * f00 + t[j + rd/2] * f01,  o1 = t[j + rd/2] * f11 + t[j] * f10
+ * each product rounded to fp32, the sum once to bf16 (csrc/rope_kv.sycl:7-9). out_q bf16 [Hq][S][256],
+ * out_k bf16 [Hk][S][256]. 1 <= S <= 8. */
+MONO_API int mono_qk_norm_rope_kv(const void* rawq, int64_t q_row_stride, int64_t q_head_stride, const void* rawk,
+                                  int64_t k_row_stride, const void* v, int64_t v_row_stride, const void* wq,
+                                  const void* wk, const float* freqs, void* key_cache, void* value_cache, int64_t cap,
+                                  const int64_t* position, int64_t S, int64_t Hq, int64_t Hk, float epsq, float epsk,
+                                  int64_t rd, void* out_q, void* out_k, mono_stream_t stream);
+
+/* Tree decode attention (the role of the reference's attn_dpas, csrc/attn_dpas.sycl:269-342): every query row
+ * (q head h, row s) attends the committed prefix [0, L) of the cache of kv head h / (H / Hk) and the tree
+ * rows t with (mask[s] >> t) & 1 (their keys / values in xk / xv), softmax of (k . q) / 16, P rounded to bf16
+ * for P V, fp32 accumulation, bf16 output. L = clamp(seqlen[0], 0, cap) is read on the device (no host sync).
+ * q bf16 [H][S][256]; caches bf16 [Hk][cap][256]; xk, xv bf16 [Hk][S][256]; mask int32 [S] (NULL with S = 1:
+ * the MTP draft row, prefix only); out bf16 [S][H * 256]. (H / Hk) * S <= 32, 1 <= S <= 8. workspace:
+ * mono_tree_attention_workspace(Hk, cap) bytes (no initial contents needed); one call at a time per
+ * workspace. Not bit-exact with any other implementation: results are within the tolerance of an fp64
+ * reference stated by the tests. */
+MONO_API size_t mono_tree_attention_workspace(int64_t Hk, int64_t cap);
+MONO_API int mono_tree_attention(const void* q, const void* key_cache, const void* value_cache, const int32_t* seqlen,
+                                 const void* xk, const void* xv, const int32_t* mask, int64_t H, int64_t Hk, int64_t S,
+                                 int64_t cap, void* out, void* workspace, size_t workspace_bytes, mono_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
