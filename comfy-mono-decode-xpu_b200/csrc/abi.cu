@@ -306,4 +306,42 @@ int mono_tree_attention(const void* q, const void* key_cache, const void* value_
     return launch_tree_attention(A, workspace, reinterpret_cast<cudaStream_t>(stream));
 }
 
+size_t mono_gdn_step_workspace(int64_t M, int64_t C, int64_t HV) {
+    if (M < 1 || C < 1 || HV < 1) return 0;
+    return gdn_workspace_bytes(int(M), int(C), int(HV));
+}
+
+int mono_gdn_step(const void* qkv, const void* z, const void* a, const void* b, const void* conv_w, void* conv_state,
+                  const float* dt_bias, const float* g_decay, float* state, const void* gnorm_w, float gnorm_eps,
+                  float qscale, int64_t M, int64_t HK, int64_t HV, void* core, void* workspace, size_t workspace_bytes,
+                  mono_stream_t stream) {
+    MONO_CHECK(qkv && z && a && b && conv_w && conv_state && dt_bias && g_decay && state && gnorm_w && core && workspace,
+               "null operand");
+    MONO_CHECK(M >= 1 && M <= 8, "1 <= M <= 8 rows (got %lld)", (long long)M);
+    MONO_CHECK(HK >= 1 && HV >= HK && HV % HK == 0 && HV <= 1024, "value heads a multiple of key heads");
+    MONO_CHECK(gnorm_eps > 0.f, "positive eps");
+    const int64_t C = (2 * HK + HV) * 128;
+    MONO_CHECK(workspace_bytes >= mono_gdn_step_workspace(M, C, HV), "workspace too small (mono_gdn_step_workspace)");
+    MONO_CHECK(aligned(workspace, 256) && aligned(state, 16), "aligned workspace / state");
+    GdnArgs A{};
+    A.qkv = static_cast<const uint16_t*>(qkv);
+    A.z = static_cast<const uint16_t*>(z);
+    A.a = static_cast<const uint16_t*>(a);
+    A.b = static_cast<const uint16_t*>(b);
+    A.conv_w = static_cast<const uint16_t*>(conv_w);
+    A.conv_state = static_cast<uint16_t*>(conv_state);
+    A.dt_bias = dt_bias;
+    A.g_decay = g_decay;
+    A.state = state;
+    A.gnorm_w = static_cast<const uint16_t*>(gnorm_w);
+    A.gnorm_eps = gnorm_eps;
+    A.qscale = qscale;
+    A.core = static_cast<uint16_t*>(core);
+    A.M = int(M);
+    A.C = int(C);
+    A.HK = int(HK);
+    A.HV = int(HV);
+    return launch_gdn_step(A, workspace, reinterpret_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -82,4 +82,24 @@ struct AttnArgs {
 size_t attn_workspace_bytes(int Hk, int cap, int sms);
 int launch_tree_attention(AttnArgs A, void* ws, cudaStream_t stream);
 
+struct GdnArgs {
+    const uint16_t* qkv;     // [M][C] projections: q heads | k heads | v heads (bf16)
+    const uint16_t* z;       // [M][HV * 128]
+    const uint16_t* a;       // [M][HV]
+    const uint16_t* b;       // [M][HV]
+    const uint16_t* conv_w;  // [C][4]
+    uint16_t* conv_state;    // [C][3], updated
+    const float* dt_bias;    // [HV]
+    const float* g_decay;    // [HV]
+    float* state;            // [HV][128][128] ([k][v]), updated
+    const uint16_t* gnorm_w; // [128]
+    float gnorm_eps, qscale;
+    uint16_t* core;          // [M][HV * 128]
+    uint16_t* conv_out;      // workspace [M][C]
+    float* gates;            // workspace [M][HV][2]
+    int M, C, HK, HV;
+};
+size_t gdn_workspace_bytes(int M, int C, int HV);
+int launch_gdn_step(GdnArgs A, void* ws, cudaStream_t stream);
+
 }  // namespace mono

@@ -304,3 +304,27 @@ def attn_dpas(q, key, value, seqlen, xk, xv, mask, chunks_hint=0):
         _lib.call("mono_tree_attention", _p(q), _p(key), _p(value), _p(seqlen), _p(xk), _p(xv),
                   _p(mask) if tree else None, H, Hk, S, cap, _p(out), _p(ws), nbytes, _stream(q.device))
     return out
+
+
+_gdn_ws = {}
+
+
+def gdn_step(qkv, z, a, b, conv_w, conv_state, dt_bias, g_decay, state, gnorm_w, gnorm_eps, qscale, hk):
+    """Gated-DeltaNet decode step for M sequential rows (include/mono_b200.h mono_gdn_step). Updates conv_state
+    and state in place; returns core bf16 [M, HV * 128]."""
+    _cuda(qkv, z, a, b, conv_w, conv_state, dt_bias, g_decay, state, gnorm_w)
+    M, C = qkv.shape
+    HV = a.shape[1]
+    _check(C == (2 * hk + HV) * 128 and z.shape == (M, HV * 128) and b.shape == a.shape, "GDN shapes")
+    for t in (qkv, z, a, b, conv_w, conv_state, gnorm_w):
+        _check(t.dtype == torch.bfloat16 and t.is_contiguous(), "bf16 contiguous operands")
+    _check(state.dtype == torch.float32 and state.is_contiguous() and state.shape == (HV, 128, 128), "fp32 state")
+    _check(dt_bias.dtype == torch.float32 and g_decay.dtype == torch.float32, "fp32 dt_bias / g_decay")
+    nbytes = _lib.load().mono_gdn_step_workspace(M, C, HV)
+    ws = _workspace(_gdn_ws, (qkv.device, M, C, HV), nbytes, qkv.device)
+    core = torch.empty((M, HV * 128), dtype=torch.bfloat16, device=qkv.device)
+    with torch.cuda.device(qkv.device):
+        _lib.call("mono_gdn_step", _p(qkv), _p(z), _p(a), _p(b), _p(conv_w), _p(conv_state), _p(dt_bias), _p(g_decay),
+                  _p(state), _p(gnorm_w), float(gnorm_eps), float(qscale), M, hk, HV, _p(core), _p(ws), nbytes,
+                  _stream(qkv.device))
+    return core

@@ -40,6 +40,8 @@ SIGNATURES = {
                                  ctypes.c_float, I64, P, P, P]),
     "mono_tree_attention_workspace": (SZ, [I64, I64]),
     "mono_tree_attention": (I, [P, P, P, P, P, P, P, I64, I64, I64, I64, P, P, SZ, P]),
+    "mono_gdn_step_workspace": (SZ, [I64, I64, I64]),
+    "mono_gdn_step": (I, [P, P, P, P, P, P, P, P, P, P, ctypes.c_float, ctypes.c_float, I64, I64, I64, P, P, SZ, P]),
 }
 
 MONO_OK, MONO_EINVAL, MONO_ECUDA, MONO_ETIMEOUT, MONO_EDEVICE = 0, 1, 2, 3, 4

@@ -184,6 +184,27 @@ MONO_API int mono_tree_attention(const void* q, const void* key_cache, const voi
                                  const void* xk, const void* xv, const int32_t* mask, int64_t H, int64_t Hk, int64_t S,
                                  int64_t cap, void* out, void* workspace, size_t workspace_bytes, mono_stream_t stream);
 
+/* ---- Gated-DeltaNet ----------------------------------------------------------------------------------- */
+
+/* Gated-DeltaNet decode step for M sequential rows that all commit (the conv / gates / L2 norm / delta rule /
+ * gated RMSNorm of the reference's layer_gdn, csrc/mono_gdn.sycl:313-611):
+ *   conv   y = bf16(sum_d x[t-d] w[3-d]) over the conv state and the new rows, out = bf16(y / (1 + exp(-y)))
+ *   gates  decay = exp(g_decay * softplus(a + dt_bias)), beta = bf16(sigmoid(b))
+ *   l2     q <- (q * qscale) / max(|q|, 1e-12), k <- k / max(|k|, 1e-12)   (per key head)
+ *   delta  S <- S decay; delta = (v - S^T k) beta; S <- S + k delta^T; o = S^T q   (value head h: key head
+ *          h / (HV / HK))
+ *   gnorm  core = bf16(bf16(bf16(o) * w * rsqrt(mean(bf16(o)^2) + eps)) * bf16(silu(z)))
+ * qkv bf16 [M][C] with C = (2 HK + HV) * 128 (q heads, k heads, v heads); z bf16 [M][HV * 128]; a, b bf16
+ * [M][HV]; conv_w bf16 [C][4]; conv_state bf16 [C][3] (oldest first, updated); dt_bias, g_decay fp32 [HV];
+ * state fp32 [HV][128][128] ([k][v], updated); gnorm_w bf16 [128]; core bf16 [M][HV * 128]. 1 <= M <= 8.
+ * fp32 arithmetic; results within the tolerance of an fp64 reference stated by the tests. workspace:
+ * mono_gdn_step_workspace(M, C, HV) bytes (256-byte aligned). */
+MONO_API size_t mono_gdn_step_workspace(int64_t M, int64_t C, int64_t HV);
+MONO_API int mono_gdn_step(const void* qkv, const void* z, const void* a, const void* b, const void* conv_w,
+                           void* conv_state, const float* dt_bias, const float* g_decay, float* state,
+                           const void* gnorm_w, float gnorm_eps, float qscale, int64_t M, int64_t HK, int64_t HV,
+                           void* core, void* workspace, size_t workspace_bytes, mono_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

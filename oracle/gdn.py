@@ -1,0 +1,78 @@
+"""Gated-DeltaNet decode step on the CPU in fp64 (test infrastructure only; see oracle/__init__.py).
+
+Follows the reference's arithmetic (csrc/mono_gdn.sycl) for M sequential rows (a chain: every row commits):
+  conv   (:313-375)  y = bf16(sum_{d=0..3} x[t-d] * w[3-d]) with x[-1..-3] the conv state (newest last),
+                     out = bf16(y / (1 + exp(-y)));  the conv state becomes the last 3 inputs
+  gates  (:427-456)  decay = exp(g_decay[h] * softplus(a + dt_bias[h])) (softplus(v) = v for v > 20),
+                     beta = bf16(sigmoid(b))
+  l2     (:458-498)  qi = 1 / max(sqrt(sum q^2), 1e-12); q <- (q * scale) * qi; k <- k * ki  (per key head)
+  delta  (:531-567)  S <- S * decay; mem = S^T k; delta = (v - mem) * beta; S <- S + k delta^T; o = S^T q
+                     (S[h] is [k][v]; value head h reads key head h / (HV / HK))
+  gnorm  (:574-607)  raw = bf16(o); core = bf16(bf16(raw * w * rsqrt(mean(raw^2) + eps)) * bf16(silu(z)))
+Everything in fp64 except the bf16 roundings the reference makes explicit.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from .numerics import bf16_bits_to_f32, f64_to_bf16_bits
+
+DH = 128
+
+
+def _bf(x):
+    """Round fp64 values to bf16 (RNE) and back to fp64."""
+    return bf16_bits_to_f32(f64_to_bf16_bits(np.asarray(x, dtype=np.float64))).astype(np.float64)
+
+
+def gdn_step(qkv, z, a, b, conv_w, conv_state, dt_bias, g_decay, state, gnorm_w, gnorm_eps, qscale, HK):
+    """qkv [M, C] bf16 bits (C = 2 HK 128 + HV 128: q heads | k heads | v heads), z [M, HV 128], a / b [M, HV]
+    bf16 bits; conv_w [C, 4] bf16 bits; conv_state [C, 3] bf16 bits; dt_bias / g_decay [HV] fp32; state
+    [HV, 128, 128] fp32 ([k][v]); gnorm_w [128] bf16 bits.
+    Returns (core [M, HV 128] fp64, conv_state' [C, 3] bf16 bits, state' [HV, 128, 128] fp64)."""
+    x = bf16_bits_to_f32(qkv).astype(np.float64)
+    M, C = x.shape
+    HV = a.shape[1]
+    KD = HK * DH
+    w = bf16_bits_to_f32(conv_w).astype(np.float64)
+    hist = bf16_bits_to_f32(conv_state).astype(np.float64)  # [C, 3], oldest first
+    seq = np.concatenate([hist, x.T], axis=1)  # [C, 3 + M]
+    conv = np.zeros((M, C))
+    for t in range(M):
+        win = seq[:, t:t + 4]  # x[t-3] .. x[t]
+        s = np.zeros(C)
+        for d in range(4):  # d steps back, weight w[3 - d]
+            s = s + win[:, 3 - d] * w[:, 3 - d]
+        y = _bf(s)
+        conv[t] = _bf(y / (1.0 + np.exp(-y)))
+    new_hist = seq[:, -3:]
+    av = _bf(bf16_bits_to_f32(a).astype(np.float64)) + dt_bias.astype(np.float64)[None, :]
+    sp = np.where(av > 20.0, av, np.log1p(np.exp(np.minimum(av, 20.0))))
+    decay = np.exp(g_decay.astype(np.float64)[None, :] * sp)
+    beta = _bf(1.0 / (1.0 + np.exp(-bf16_bits_to_f32(b).astype(np.float64))))
+    q = conv[:, :KD].reshape(M, HK, DH)
+    k = conv[:, KD:2 * KD].reshape(M, HK, DH)
+    v = conv[:, 2 * KD:].reshape(M, HV, DH)
+    qi = 1.0 / np.maximum(np.sqrt((q * q).sum(-1)), 1e-12)
+    ki = 1.0 / np.maximum(np.sqrt((k * k).sum(-1)), 1e-12)
+    qn = (q * qscale) * qi[..., None]
+    kn = k * ki[..., None]
+    S = state.astype(np.float64).copy()
+    raw = np.zeros((M, HV, DH))
+    for t in range(M):
+        for h in range(HV):
+            kh = h // (HV // HK)
+            St = S[h] * decay[t, h]
+            mem = St.T @ kn[t, kh]
+            delta = (v[t, h] - mem) * beta[t, h]
+            St = St + np.outer(kn[t, kh], delta)
+            S[h] = St
+            raw[t, h] = St.T @ qn[t, kh]
+    rawb = _bf(raw)
+    gw = bf16_bits_to_f32(gnorm_w).astype(np.float64)
+    rs = 1.0 / np.sqrt((rawb * rawb).mean(-1, keepdims=True) + gnorm_eps)
+    normed = _bf(rawb * gw * rs)
+    zf = bf16_bits_to_f32(z).astype(np.float64).reshape(M, HV, DH)
+    gz = _bf(zf / (1.0 + np.exp(-zf)))
+    core = (normed * gz).reshape(M, HV * DH)
+    return core, f64_to_bf16_bits(new_hist), S

@@ -1,0 +1,49 @@
+"""Gated-DeltaNet decode step on the GPU (through the C ABI) against the fp64 oracle (oracle/gdn.py), BASELINE
+configs[3] shapes: 16 key heads, 32 value heads, d = 128, state ~ N(0, 0.1), M in {1, 3, 8} sequential rows.
+Tolerances (fp32 kernel vs fp64 with the reference's explicit bf16 roundings applied in both):
+    core:        max |out - ref| <= 2^-6 |ref| + 2e-3,  mean |out - ref| <= 2e-3 mean |ref|
+    state:       |S - S_ref| <= 1e-4 (1 + |S_ref|)
+    conv state:  bit-exact (a copy of the newest inputs)"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import bf16_bits
+from oracle import gdn as og
+from oracle.numerics import bf16_bits_to_f32
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("M", [1, 3, 8])
+@pytest.mark.parametrize("seed", [0, 1])
+def test_gdn_step_within_tolerance_of_fp64(cuda, M, seed):
+    from mono_b200 import _C
+    HK, HV, D = 16, 32, 128
+    C = (2 * HK + HV) * D
+    g = torch.Generator().manual_seed(0x5EED + 3 + 10 * M + seed)
+    qkv = torch.randn(M, C, generator=g).bfloat16()
+    z = torch.randn(M, HV * D, generator=g).bfloat16()
+    a = torch.randn(M, HV, generator=g).bfloat16()
+    b = torch.randn(M, HV, generator=g).bfloat16()
+    conv_w = (torch.randn(C, 4, generator=g) * 0.5).bfloat16()
+    conv_state = torch.randn(C, 3, generator=g).bfloat16()
+    dt_bias = torch.randn(HV, generator=g) * 0.1 if seed else torch.zeros(HV)
+    g_decay = -torch.exp(torch.randn(HV, generator=g) * 0.5) if seed else -torch.ones(HV)
+    state = torch.randn(HV, D, D, generator=g) * 0.1
+    gw = (1 + torch.randn(D, generator=g) * 0.1).bfloat16()
+    qscale = D ** -0.5
+    core_ref, hist_ref, state_ref = og.gdn_step(bf16_bits(qkv), bf16_bits(z), bf16_bits(a), bf16_bits(b),
+                                                bf16_bits(conv_w), bf16_bits(conv_state), dt_bias.numpy(),
+                                                g_decay.numpy(), state.numpy(), bf16_bits(gw), 1e-6, qscale, HK)
+    cs, st = conv_state.to(cuda), state.to(cuda)
+    core = _C.gdn_step(qkv.to(cuda), z.to(cuda), a.to(cuda), b.to(cuda), conv_w.to(cuda), cs, dt_bias.to(cuda),
+                       g_decay.to(cuda), st, gw.to(cuda), 1e-6, qscale, HK)
+    o = bf16_bits_to_f32(bf16_bits(core)).astype(np.float64)
+    err = np.abs(o - core_ref)
+    assert np.isfinite(o).all()
+    assert (err <= 2 ** -6 * np.abs(core_ref) + 2e-3).all(), err.max()
+    assert err.mean() <= 2e-3 * np.abs(core_ref).mean(), err.mean()
+    assert np.array_equal(bf16_bits(cs), hist_ref)
+    serr = np.abs(st.cpu().numpy().astype(np.float64) - state_ref)
+    assert (serr <= 1e-4 * (1 + np.abs(state_ref))).all(), serr.max()
