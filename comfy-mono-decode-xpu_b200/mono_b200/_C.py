@@ -328,3 +328,44 @@ def gdn_step(qkv, z, a, b, conv_w, conv_state, dt_bias, g_decay, state, gnorm_w,
                   _p(state), _p(gnorm_w), float(gnorm_eps), float(qscale), M, hk, HV, _p(core), _p(ws), nbytes,
                   _stream(qkv.device))
     return core
+
+
+def mtp_prep_draft(st, k, ftab, freqs, mpos, mseq):
+    """The reference's _C.mtp_prep_draft (csrc/mtp_loop.sycl:29-55): rope row, MTP KV positions / seqlen of
+    draft k from the device counters st."""
+    _cuda(st, ftab, freqs, mpos, mseq)
+    _check(st.dtype == torch.int64 and mpos.dtype == torch.int64 and mseq.dtype == torch.int32, "int64 st / mpos, int32 mseq")
+    _check(ftab.dtype == torch.float32 and ftab.is_contiguous() and freqs.is_contiguous() and freqs.dim() == ftab.dim()
+           and freqs.size(2) == 1, "rope table [.., .., cap, ...] / row [.., .., 1, ...] float")
+    n, cap = freqs.numel(), ftab.size(2)
+    _check(ftab.numel() == cap * n, "rope table row size")
+    with torch.cuda.device(st.device):
+        _lib.call("mono_mtp_prep_draft", _p(st), int(k), _p(ftab), n, cap, _p(freqs), _p(mpos), mpos.numel(), _p(mseq),
+                  _stream(st.device))
+
+
+def mtp_prep_verify(st, apos, aseq, vpos, tree_pos, ctl, tree_ctl, parity, rope_offset):
+    """The reference's _C.mtp_prep_verify (csrc/mtp_loop.sycl:57-90)."""
+    _cuda(st, apos, aseq, vpos, tree_pos, ctl, tree_ctl)
+    _check(ctl.dtype == torch.int32 and ctl.numel() == 26 and tree_ctl.dtype == torch.int32 and tree_ctl.numel() == 16,
+           "ctl / tree program")
+    _check(tree_pos.numel() == vpos.numel(), "rows")
+    with torch.cuda.device(st.device):
+        _lib.call("mono_mtp_prep_verify", _p(st), _p(apos), apos.numel(), _p(aseq), _p(vpos), _p(tree_pos), vpos.numel(),
+                  _p(ctl), _p(tree_ctl), int(parity), int(rope_offset), _stream(st.device))
+
+
+def mtp_accept(st, toks, vtok, cand, children, rows, depth, x, nt_buf, h_buf, ctl, kv_ptrs, kv_heads, kv_cap, head_dim,
+               result):
+    """The reference's _C.mtp_accept (csrc/mtp_loop.sycl:92-196): accept walk, result row, counters, ctl, next
+    token / hidden row and the off-chain KV slot moves, all on the device."""
+    _cuda(st, toks, vtok, children, x, nt_buf, h_buf, ctl, kv_ptrs, result)
+    _check(st.dtype == torch.int64 and toks.dtype == torch.int64 and vtok.dtype == torch.int64, "int64 tokens / st")
+    _check(children.dtype == torch.int32 and children.numel() == 64, "children [8][8]")
+    _check(x.dtype == torch.bfloat16 and h_buf.dtype == torch.bfloat16 and x.numel() >= rows * h_buf.numel(), "hidden rows")
+    _check(result.numel() >= 32 and result.dtype == torch.int64, "result slot")
+    has_cand = cand is not None and cand.numel() > 0
+    with torch.cuda.device(st.device):
+        _lib.call("mono_mtp_accept", _p(st), _p(toks), _p(vtok), _p(cand) if has_cand else None, _p(children), int(rows),
+                  int(depth), _p(x), h_buf.numel(), _p(nt_buf), _p(h_buf), _p(ctl), _p(kv_ptrs), kv_ptrs.numel(),
+                  int(kv_heads), int(kv_cap), int(head_dim), _p(result), _stream(st.device))

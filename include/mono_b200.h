@@ -205,6 +205,34 @@ MONO_API int mono_gdn_step(const void* qkv, const void* z, const void* a, const 
                            const void* gnorm_w, float gnorm_eps, float qscale, int64_t M, int64_t HK, int64_t HV,
                            void* core, void* workspace, size_t workspace_bytes, mono_stream_t stream);
 
+/* ---- MTP loop bookkeeping on the device (the role of csrc/mtp_loop.sycl:29-196) ------------------------ */
+/* st: int64 [4] loop state (st[0] committed length = attention index, st[1] MTP KV length); ctl: int32 [26] =
+ * [pending, parity, accepted slots[8], tree parents[8], tree program[8]]. Nothing reads back to the host. */
+
+/* freqs[0 .. row_elems) = ftab[min(st[0] + k, cap - 1)] (fp32 rows of row_elems), mpos[i] = st[1] + k + i
+ * (i < np), mseq = st[1] + k + 1 (reference: mtp_prep_draft). */
+MONO_API int mono_mtp_prep_draft(const int64_t* st, int64_t k, const float* ftab, int64_t row_elems, int64_t cap,
+                                 float* freqs, int64_t* mpos, int64_t np, int32_t* mseq, mono_stream_t stream);
+
+/* apos[i] = st[0] + i (i < np <= 64), aseq = st[0], vpos[r] = tree_pos[r] + st[0] + rope_offset (r < rows <= 8),
+ * ctl[1] = parity, ctl[10 .. 26) = tree_ctl[0 .. 16) (reference: mtp_prep_verify). */
+MONO_API int mono_mtp_prep_verify(const int64_t* st, int64_t* apos, int64_t np, int32_t* aseq, int64_t* vpos,
+                                  const int64_t* tree_pos, int64_t rows, int32_t* ctl, const int32_t* tree_ctl,
+                                  int64_t parity, int64_t rope_offset, mono_stream_t stream);
+
+/* The accept step (reference: mtp_accept; host twin comfy_mono_decode_xpu/mtp_loop.py:117-136): from row 0,
+ * continue along the first child c (children int32 [8][8], -1 ends a list) with drafts[c] == toks[current];
+ * result int64 [32] = [n, commit[8] (drafts along the path, then toks[last], -1 padded), row, on_chain,
+ * nranks, ranks[7] (rank of toks[node] among cand[node][0..7), 7 if absent, for path nodes < depth), pos,
+ * kept]; st[0] += n, st[1] += kept (kept = min(on_chain ? n : n - 1, depth)); ctl[0] = n,
+ * ctl[2 + i] = path[i] (i < n, else i); next_tok = toks[row]; h_out = x[row] (bf16 [rows][H]); for an
+ * off-chain path, in every bf16 KV cache [heads][cap][head_dim] listed in kv_ptrs (device int64 [nkv]),
+ * slot (pos + path[k]) % cap moves to (pos + k) % cap for k = 1 .. n - 1. cand NULL: no ranks. */
+MONO_API int mono_mtp_accept(int64_t* st, const int64_t* toks, const int64_t* drafts, const int64_t* cand,
+                             const int32_t* children, int64_t rows, int64_t depth, const void* x, int64_t H,
+                             int64_t* next_tok, void* h_out, int32_t* ctl, const int64_t* kv_ptrs, int64_t nkv,
+                             int64_t heads, int64_t cap, int64_t head_dim, int64_t* result, mono_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

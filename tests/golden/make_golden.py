@@ -81,10 +81,44 @@ def make_attn(ref_root: str):
     np.savez_compressed(os.path.join(HERE, "attn_fp64.npz"), n=np.int64(len(cases)), **out)
 
 
+def make_accept(ref_root: str):
+    import random
+    walk = _functions(os.path.join(ref_root, "comfy_mono_decode_xpu", "mtp_loop.py"), ["_upstream_walk"], {})
+    tfn = _functions(os.path.join(ref_root, "tests", "test_mtp_accept.py"), ["_tree", "_spec", "SLOTS"], {})
+    spec, tree, SLOTS = tfn["_spec"], tfn["_tree"], tfn["SLOTS"]
+    specs = [spec(w) for w in ((4, 3), (7,), (1, 1, 1, 1, 1, 1, 1), (2, 2, 3), (3, 1, 1, 2))]
+    specs += [[[[[[]], []], []], []], [[[[[]]]]]]  # tree4s1m8, chain 4 (the reference test's list)
+    out, k = {}, 0
+    for si, sp in enumerate(specs):
+        rng = random.Random(0x5EED + 4 + si)
+        parent, children, depth_of, chain = tree(sp, SLOTS)
+        for trial in range(12):
+            toks = [rng.randrange(50) for _ in range(SLOTS)]
+            dr = [rng.randrange(50) for _ in range(SLOTS)]
+            for r in range(SLOTS):
+                if children[r] and rng.random() < 0.8:
+                    dr[rng.choice(children[r])] = toks[r]
+            cand = [rng.randrange(50) for _ in range(49)]
+            for node in range(chain):
+                if rng.random() < 0.7:
+                    cand[7 * node + rng.randrange(7)] = toks[node]
+            path, commit, ranks, row, on_chain, kept = walk["_upstream_walk"](children, toks, dr, chain, cand)
+            ch = np.full((SLOTS, SLOTS), -1, dtype=np.int32)
+            for r, cs in enumerate(children):
+                ch[r, :len(cs)] = cs
+            out.update({f"children{k}": ch, f"toks{k}": np.array(toks), f"dr{k}": np.array(dr),
+                        f"cand{k}": np.array(cand), f"depth{k}": np.int64(chain), f"path{k}": np.array(path),
+                        f"commit{k}": np.array(commit), f"ranks{k}": np.array(ranks, dtype=np.int64),
+                        f"row{k}": np.int64(row), f"on_chain{k}": np.int64(on_chain), f"kept{k}": np.int64(kept)})
+            k += 1
+    np.savez_compressed(os.path.join(HERE, "accept_walk.npz"), n=np.int64(k), **out)
+
+
 if __name__ == "__main__":
     root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("REFERENCE_ROOT")
     if not root or not os.path.isdir(root):
         raise SystemExit("usage: make_golden.py <reference checkout>")
     make_rope(root)
     make_attn(root)
+    make_accept(root)
     print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
