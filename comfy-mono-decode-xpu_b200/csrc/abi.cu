@@ -344,4 +344,27 @@ int mono_gdn_step(const void* qkv, const void* z, const void* a, const void* b, 
     return launch_gdn_step(A, workspace, reinterpret_cast<cudaStream_t>(stream));
 }
 
+size_t mono_topk_workspace(int64_t rows) { return rows < 1 ? 0 : topk_workspace_bytes(rows); }
+
+int mono_fast_topk(const void* x, int64_t rows, int64_t V, int64_t k, int argmax_order, int with_argmax, void* values,
+                   int64_t* indices, int64_t* argmax, void* workspace, size_t workspace_bytes, mono_stream_t stream) {
+    MONO_CHECK(x && values && indices && workspace && (argmax || !with_argmax), "null operand");
+    MONO_CHECK(rows >= 1 && rows <= 65535, "1 <= rows <= 65535");
+    MONO_CHECK(k >= 1 && k <= 8 && V >= k && V < (int64_t(1) << 31), "1 <= k <= 8, k <= V < 2^31");
+    MONO_CHECK(!argmax_order || k == 1, "argmax order ranks k = 1 only");
+    MONO_CHECK(workspace_bytes >= mono_topk_workspace(rows) && aligned(workspace, 8), "workspace (mono_topk_workspace)");
+    TopkArgs A{};
+    A.x = static_cast<const uint16_t*>(x);
+    A.values = static_cast<uint16_t*>(values);
+    A.indices = indices;
+    A.argmax = argmax;
+    A.ws = static_cast<uint64_t*>(workspace);
+    A.V = V;
+    A.rows = int(rows);
+    A.k = int(k);
+    A.argmax_order = argmax_order != 0;
+    A.with_argmax = with_argmax != 0;
+    return launch_topk(A, reinterpret_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -102,4 +102,16 @@ struct GdnArgs {
 size_t gdn_workspace_bytes(int M, int C, int HV);
 int launch_gdn_step(GdnArgs A, void* ws, cudaStream_t stream);
 
+struct TopkArgs {
+    const uint16_t* x;  // [rows][V] bf16
+    uint16_t* values;   // [rows][k]
+    int64_t* indices;   // [rows][k]
+    int64_t* argmax;    // [rows] (with_argmax)
+    uint64_t* ws;       // [rows][slices][k + 1]
+    int64_t V;
+    int rows, k, argmax_order, with_argmax;
+};
+size_t topk_workspace_bytes(int64_t rows);
+int launch_topk(const TopkArgs& A, cudaStream_t stream);
+
 }  // namespace mono

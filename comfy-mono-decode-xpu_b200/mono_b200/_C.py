@@ -369,3 +369,33 @@ def mtp_accept(st, toks, vtok, cand, children, rows, depth, x, nt_buf, h_buf, ct
         _lib.call("mono_mtp_accept", _p(st), _p(toks), _p(vtok), _p(cand) if has_cand else None, _p(children), int(rows),
                   int(depth), _p(x), h_buf.numel(), _p(nt_buf), _p(h_buf), _p(ctl), _p(kv_ptrs), kv_ptrs.numel(),
                   int(kv_heads), int(kv_cap), int(head_dim), _p(result), _stream(st.device))
+
+
+_topk_ws = {}
+
+
+def _topk(x, k, argmax_order, with_argmax):
+    _cuda(x)
+    _check(x.dtype == torch.bfloat16 and x.is_contiguous(), "bf16 contiguous")
+    V = x.size(-1)
+    rows = x.numel() // V
+    values = torch.empty((*x.shape[:-1], k) if x.dim() > 1 else (k,), dtype=torch.bfloat16, device=x.device)
+    indices = torch.empty(values.shape, dtype=torch.int64, device=x.device)
+    am = torch.empty((rows,) if with_argmax else (0,), dtype=torch.int64, device=x.device)
+    nbytes = _lib.load().mono_topk_workspace(rows)
+    ws = _workspace(_topk_ws, (x.device, rows), nbytes, x.device)
+    with torch.cuda.device(x.device):
+        _lib.call("mono_fast_topk", _p(x), rows, V, int(k), int(argmax_order), int(with_argmax), _p(values), _p(indices),
+                  _p(am) if with_argmax else None, _p(ws), nbytes, _stream(x.device))
+    return values, indices, am
+
+
+def fast_topk(x, k, argmax_order):
+    """The reference's _C.fast_topk (csrc/fast_topk.sycl:164-167) for every row of x: (values, indices)."""
+    v, i, _ = _topk(x, k, argmax_order, False)
+    return v, i
+
+
+def fast_pick(x, k):
+    """The reference's _C.fast_pick (:169-171): top-k (top-k order) and the argmax of the same rows in one pass."""
+    return _topk(x, k, False, True)

@@ -205,6 +205,19 @@ MONO_API int mono_gdn_step(const void* qkv, const void* z, const void* a, const 
                            const void* gnorm_w, float gnorm_eps, float qscale, int64_t M, int64_t HK, int64_t HV,
                            void* core, void* workspace, size_t workspace_bytes, mono_stream_t stream);
 
+/* ---- logit picks ----------------------------------------------------------------------------------------- */
+
+/* Exact top-k (k <= 8) of every bf16 row x [rows][V] (the role of the reference's fast_topk / fast_pick,
+ * csrc/fast_topk.sycl:22-176, which take one row): ranks = the bf16 radix key (NaN on top, -0 below +0), ties
+ * in the XPU topk gather order (i >> 15, then (i & 8191) >> 3, then (i & 32767) >> 13, then i & 7);
+ * argmax_order != 0 (k = 1): the float argmax order (NaN first, -0 == +0, smallest index on ties).
+ * with_argmax != 0 also writes argmax [rows] (int64) from the same pass. values bf16 [rows][k], indices int64
+ * [rows][k], best first. workspace: mono_topk_workspace(rows) bytes. */
+MONO_API size_t mono_topk_workspace(int64_t rows);
+MONO_API int mono_fast_topk(const void* x, int64_t rows, int64_t V, int64_t k, int argmax_order, int with_argmax,
+                            void* values, int64_t* indices, int64_t* argmax, void* workspace, size_t workspace_bytes,
+                            mono_stream_t stream);
+
 /* ---- MTP loop bookkeeping on the device (the role of csrc/mtp_loop.sycl:29-196) ------------------------ */
 /* st: int64 [4] loop state (st[0] committed length = attention index, st[1] MTP KV length); ctl: int32 [26] =
  * [pending, parity, accepted slots[8], tree parents[8], tree program[8]]. Nothing reads back to the host. */
