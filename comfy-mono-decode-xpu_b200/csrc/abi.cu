@@ -367,4 +367,56 @@ int mono_fast_topk(const void* x, int64_t rows, int64_t V, int64_t k, int argmax
     return launch_topk(A, reinterpret_cast<cudaStream_t>(stream));
 }
 
+size_t mono_rowlin_gptq_workspace(int64_t K) { return K < 1 ? 0 : rowlin_workspace_bytes(int(K)); }
+
+int mono_rowlin_gptq(const void* x, int mode, const void* norm_w, float eps, const void* gate, int64_t gate_row_stride,
+                     int64_t gate_head_stride, const void* lut, const void* const* weights, const int64_t* rows, int nm,
+                     int64_t M, int64_t K, const void* residual, void* out, void* xn_out, void* workspace,
+                     size_t workspace_bytes, mono_stream_t stream) {
+    MONO_CHECK(x && weights && rows && out && workspace, "null operand");
+    MONO_CHECK(mode == ROWLIN_NORM || mode == ROWLIN_GATE || mode == ROWLIN_QUANT, "mode 0 (norm), 1 (gate), 2 (quant)");
+    MONO_CHECK(mode != ROWLIN_NORM || norm_w, "norm mode needs norm_w");
+    MONO_CHECK(mode != ROWLIN_GATE || (gate && lut && gate_head_stride >= 256 && gate_head_stride % 8 == 0 &&
+                                       gate_row_stride % 8 == 0 && aligned(gate, 16)),
+               "gate mode: gate (16-byte aligned, strides multiples of 8 elements) and lut");
+    MONO_CHECK(nm >= 1 && nm <= 3, "1 to 3 matrices");
+    MONO_CHECK(M >= 1 && M <= 16, "1 <= M <= 16 (got %lld)", (long long)M);
+    MONO_CHECK(K >= kChunkK && K % kChunkK == 0 && K <= 4096, "K a multiple of 1024 up to 4096 (got %lld)", (long long)K);
+    MONO_CHECK(workspace_bytes >= rowlin_workspace_bytes(int(K)) && aligned(workspace, 256), "workspace (mono_rowlin_gptq_workspace)");
+    MONO_CHECK(aligned(x, 16) && aligned(out, 16) && (!xn_out || aligned(xn_out, 16)), "16-byte aligned rows");
+    Program P{};
+    P.nph = 1;
+    P.M = int(M);
+    int64_t N = 0;
+    for (int i = 0; i < nm; ++i) {
+        MONO_CHECK(weights[i] && aligned(weights[i], 16) && rows[i] >= 16 && rows[i] % 16 == 0, "weight %d: tiled, rows a multiple of 16", i);
+        P.ph[0].m[i] = MatDesc{static_cast<const uint8_t*>(weights[i]), nullptr, int(rows[i])};
+        N += rows[i];
+    }
+    MONO_CHECK(N < (int64_t(1) << 24), "output rows");
+    uint8_t* w = static_cast<uint8_t*>(workspace);
+    P.ph[0].nm = nm;
+    P.ph[0].K = int(K);
+    P.ph[0].x = reinterpret_cast<const int8_t*>(w);
+    P.ph[0].xperm = 1;
+    RowLinArgs A{};
+    A.x = static_cast<const uint16_t*>(x);
+    A.norm_w = static_cast<const uint16_t*>(norm_w);
+    A.eps = eps;
+    A.gate = static_cast<const uint16_t*>(gate);
+    A.gate_row_stride = gate_row_stride;
+    A.gate_head_stride = gate_head_stride;
+    A.lut = static_cast<const uint16_t*>(lut);
+    A.residual = static_cast<const uint16_t*>(residual);
+    A.out = static_cast<uint16_t*>(out);
+    A.xn_out = static_cast<uint16_t*>(xn_out);
+    A.q = reinterpret_cast<int8_t*>(w);
+    const size_t qb = (16 * size_t(K) + 255) / 256 * 256;
+    A.s = reinterpret_cast<float*>(w + qb);
+    A.bar = reinterpret_cast<unsigned*>(w + qb + 256);
+    A.mode = mode;
+    A.N = int(N);
+    return launch_rowlin(P, A, reinterpret_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -37,7 +37,32 @@ struct MlpArgs {
     float* s2;        // [16]
     unsigned* bar;    // [2] grid barrier words (zero between launches)
 };
+// Shared-memory shape of a cooperative stream kernel: ring stages, partial bytes, staged-activation bytes.
+struct MlpShape {
+    int S;
+    int part_bytes;  // partials of the larger phase
+    int x_bytes;     // staged activations of the larger staged phase
+};
 int launch_mlp(Program& P, MlpArgs& A, cudaStream_t stream);
+
+enum RowLinMode : int { ROWLIN_NORM = 0, ROWLIN_GATE = 1, ROWLIN_QUANT = 2 };
+struct RowLinArgs {
+    const uint16_t* x;  // [M][K] bf16
+    const uint16_t* norm_w;
+    float eps;
+    const uint16_t* gate;  // GATE: element (m, c) at gate[m * gate_row_stride + (c / 256) * gate_head_stride + c % 256]
+    int64_t gate_row_stride, gate_head_stride;
+    const uint16_t* lut;  // GATE: sigmoid of every bf16 pattern
+    const uint16_t* residual;  // [M][N] or null
+    uint16_t* out;             // [M][N]
+    uint16_t* xn_out;          // NORM: normalized rows [M][K], or null
+    int8_t* q;                 // workspace [16][K]
+    float* s;                  // workspace [16]
+    unsigned* bar;             // workspace [2], zero between launches
+    int mode, N;
+};
+size_t rowlin_workspace_bytes(int K);
+int launch_rowlin(Program& P, RowLinArgs& A, cudaStream_t stream);
 size_t mlp_workspace_bytes(int H, int I);
 
 int launch_repack(int fmt, const void* q, const void* s, int N, int K, void* out, cudaStream_t stream);

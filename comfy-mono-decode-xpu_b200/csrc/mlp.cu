@@ -21,12 +21,6 @@ namespace mono {
 // producers stream gate/up and then down weights straight through the row phases and the grid barriers.
 constexpr int kMlpCW = 12, kMlpPW = 4, kMlpThreads = (kMlpCW + kMlpPW) * 32;
 
-struct MlpShape {
-    int S;
-    int part_bytes;  // partials of the larger phase
-    int x_bytes;     // staged activations of the larger staged phase
-};
-
 template <int MT>
 __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const Program P, const MlpArgs A, const MlpShape Z) {
     extern __shared__ __align__(128) uint8_t smem[];

@@ -1,0 +1,185 @@
+// Row preparation + W4A8 GPTQ linear in one cooperative launch: the reference's layer_pre (input RMSNorm ->
+// quantization -> q / k / v projections, csrc/mono_layer.sycl:69-155) and the front of layer_post (sigmoid gate
+// -> quantization -> out projection + residual, csrc/mono_layer.sycl:243-270), on the stream engine.
+//
+//   P1 rows  mode NORM:  xn = RMSNorm(x; w) (pinned order, rowops.cuh), q, s = quant(xn)   (xn_out optional)
+//            mode GATE:  y = bf16(x * sigmoid_lut[gate]), q, s = quant(y)   (gate element (m, c) at
+//                        gate[m * gate_row_stride + (c / 256) * gate_head_stride + c % 256])
+//            mode QUANT: q, s = quant(x)
+//   P2 all   out[m][n] = bf16(total[m][n] * s[m]) (+ residual: bf16(residual + that)) for the up to three
+//            matrices of the phase, outputs concatenated along n (row stride = the sum of their rows)
+// The producer warps stream the weights from the start, across the row phase and the grid barrier.
+#include <mutex>
+
+#include "launch.h"
+#include "grid.cuh"
+#include "rowops.cuh"
+#include "stream.cuh"
+
+namespace mono {
+
+constexpr int kRlCW = 12, kRlPW = 4, kRlThreads = (kRlCW + kRlPW) * 32;
+
+// Sigmoid gate and per-token quantization of one row by a warp-group (H = 128 t + 1024 j pieces as in
+// norm_quant_row; H <= 4096).
+__device__ __forceinline__ void gate_quant_row(const uint16_t* __restrict__ x, const uint16_t* __restrict__ gate,
+                                               int64_t gate_head_stride, const uint16_t* __restrict__ lut, int H,
+                                               int8_t* __restrict__ q, float* __restrict__ s_out, float* red, int tig,
+                                               int wg) {
+    const int lane = tig & 31, warp = tig >> 5, J = H >> 10;
+    float vals[kRowMaxPieces][8];
+#pragma unroll
+    for (int j = 0; j < kRowMaxPieces; ++j)
+        if (j < J) {
+            const int c0 = (tig + 128 * j) * 8;  // 8 columns inside one 256-wide head
+            const uint4 xv = __ldcg(reinterpret_cast<const uint4*>(x + c0));
+            const uint4 gv = __ldcg(reinterpret_cast<const uint4*>(gate + (c0 >> 8) * gate_head_stride + (c0 & 255)));
+            const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w}, gu[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const uint32_t xb = (e & 1) ? (xu[e >> 1] >> 16) : (xu[e >> 1] & 0xFFFFu);
+                const uint32_t gb = (e & 1) ? (gu[e >> 1] >> 16) : (gu[e >> 1] & 0xFFFFu);
+                vals[j][e] = bf16_round(__fmul_rn(bf16_bits_to_f32(uint16_t(xb)), bf16_bits_to_f32(__ldg(lut + gb))));
+            }
+        }
+    float amax = 0.f;
+#pragma unroll
+    for (int j = 0; j < kRowMaxPieces; ++j)
+        if (j < J)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(vals[j][e]));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (lane == 0) red[8 + warp] = amax;
+    wg_sync(wg);
+    const float m = fmaxf(fmaxf(red[8], red[9]), fmaxf(red[10], red[11]));
+    const float s = __fdiv_rn(m, 127.f);
+    if (tig == 0) *s_out = s;
+#pragma unroll
+    for (int j = 0; j < kRowMaxPieces; ++j)
+        if (j < J) reinterpret_cast<uint2*>(q)[tig + 128 * j] = quant8_perm(vals[j], s);
+    wg_sync(wg);
+}
+
+template <int MT>
+__global__ void __launch_bounds__(kRlThreads, 1) rowlin_kernel(const Program P, const RowLinArgs A, const MlpShape Z) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ float red[3][16];
+    __shared__ int flag;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int M = P.M, S = Z.S, K = P.ph[0].K;
+    const StreamPlan plan(stage_bytes<FMT_GPTQ>(), S, Z.part_bytes, Z.x_bytes, 0);
+    uint8_t* ring = smem;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + plan.ring);
+    uint64_t* empty = full + S;
+    uint32_t* part = reinterpret_cast<uint32_t*>(smem + plan.ring + plan.bars);
+    int8_t* xsm = reinterpret_cast<int8_t*>(smem + plan.ring + plan.bars + plan.part);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    trace_stamp(0);
+    pdl_launch_dependents();
+    if (warp >= kRlCW) {
+        produce_all<FMT_GPTQ, LAYOUT_TILED, kRlPW>(P, ring, full, empty, S, warp - kRlCW, lane);
+        return;
+    }
+    constexpr int NT = kRlCW * 32;
+    pdl_wait();
+    unsigned epoch = 0;
+    bool ok = true;
+    {
+        const int wg = threadIdx.x >> 7, tig = threadIdx.x & 127;
+        for (int m = wg * int(gridDim.x) + int(blockIdx.x); m < M; m += 3 * int(gridDim.x)) {
+            const uint16_t* xr = A.x + size_t(m) * K;
+            if (A.mode == ROWLIN_GATE)
+                gate_quant_row(xr, A.gate + size_t(m) * A.gate_row_stride, A.gate_head_stride, A.lut, K, A.q + size_t(m) * K,
+                               A.s + m, red[wg], tig, wg);
+            else
+                norm_quant_row(xr, A.mode == ROWLIN_NORM ? A.norm_w : nullptr, A.eps, K,
+                               A.xn_out ? A.xn_out + size_t(m) * K : nullptr, A.q + size_t(m) * K, A.s + m, red[wg],
+                               tig, wg);
+        }
+    }
+    trace_stamp(1);
+    ok = grid_barrier_named<kConsumerBar, NT>(A.bar, epoch, &flag);
+    trace_stamp(2);
+    const PhaseDesc& ph = P.ph[0];
+    XSrc xs{ph.x, K, false, true};
+    if (ph.xsmem) {
+        stage_x_consumers<kRlCW>(ph.x, M, K, true, xsm);
+        xs = XSrc{xsm, K + 16, true, true};
+    }
+    trace_stamp(3);
+    const int C = phase_chunks(ph), ntl = cta_tiles(ph);
+    ok = consume_phase<FMT_GPTQ, LAYOUT_TILED, MT, kRlCW>(P, 0, xs, ring, full, empty, S, part, warp, lane) && ok;
+    ok = consumer_sync_and<kRlCW>(ok);
+    for (int e = threadIdx.x; e < ntl * M * 16 && ok; e += NT) {
+        const int k = e / (M * 16), r = e - k * (M * 16), m = r >> 4, nl = r & 15;
+        const int n = (int(blockIdx.x) + k * int(gridDim.x)) * 16 + nl;  // concatenated output column
+        const float tot = __uint_as_float(tile_total<FMT_GPTQ, MT>(part + size_t(k) * C * MT * 128, C, 0, m, nl));
+        uint16_t rr = f32_to_bf16_bits(__fmul_rn(tot, __ldcg(A.s + m)));
+        const size_t o = size_t(m) * A.N + n;
+        if (A.residual) rr = f32_to_bf16_bits(__fadd_rn(bf16_bits_to_f32(A.residual[o]), bf16_bits_to_f32(rr)));
+        A.out[o] = rr;
+    }
+    trace_stamp(4);
+    grid_exit_named<kConsumerBar, NT>(A.bar);
+}
+
+size_t rowlin_workspace_bytes(int K) { return (16 * size_t(K) + 255) / 256 * 256 + 3 * 256; }
+
+template <int MT>
+static int launch_rowlin_t(const Program& P, const RowLinArgs& A, const MlpShape& Z, size_t smem, cudaStream_t stream) {
+    auto kern = rowlin_kernel<MT>;
+    static std::mutex mu;
+    static size_t opt_in = 0;
+    static int per_sm = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (smem > opt_in) {
+            CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+            opt_in = smem;
+            CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kRlThreads, smem));
+        }
+    }
+    if (per_sm < 1) return fail(MONO_EINVAL, "rowlin: one CTA does not fit an SM (%zu B shared)", smem);
+    const int tiles = phase_tiles(P.ph[0]);
+    const int grid = tiles < sm_count() ? tiles : sm_count();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kRlThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, P, A, Z));
+    return MONO_OK;
+}
+
+int launch_rowlin(Program& P, RowLinArgs& A, cudaStream_t stream) {
+    const int M = P.M, G = sm_count();
+    const int MT = M > 8 ? 2 : 1;
+    const int nt = phase_tiles(P.ph[0]), grid = nt < G ? nt : G, per_cta = (nt + grid - 1) / grid;
+    const size_t part = size_t(per_cta) * phase_chunks(P.ph[0]) * MT * 128 * 4;
+    for (int staged = 1; staged >= 0; --staged) {
+        P.ph[0].xsmem = staged;
+        const size_t xb = staged ? size_t(M) * (P.ph[0].K + 16) : 0;
+        const StreamPlan plan(stage_bytes<FMT_GPTQ>(), kRlCW, part, xb, 0);
+        if (plan.total > 227 * 1024 - 512) continue;
+        const MlpShape Z{kRlCW, int(part), int(xb)};
+        return MT == 2 ? launch_rowlin_t<2>(P, A, Z, plan.total, stream) : launch_rowlin_t<1>(P, A, Z, plan.total, stream);
+    }
+    return fail(MONO_EINVAL, "rowlin: no shared-memory plan fits (M=%d K=%d)", M, P.ph[0].K);
+}
+
+}  // namespace mono

@@ -399,3 +399,38 @@ def fast_topk(x, k, argmax_order):
 def fast_pick(x, k):
     """The reference's _C.fast_pick (:169-171): top-k (top-k order) and the argmax of the same rows in one pass."""
     return _topk(x, k, False, True)
+
+
+ROWLIN_NORM, ROWLIN_GATE, ROWLIN_QUANT = 0, 1, 2
+_rowlin_ws = {}
+
+
+def rowlin_gptq(x, mode, weights, norm_w=None, eps=1e-6, gate=None, gate_head_stride=512, lut=None, residual=None,
+                out=None, xn_out=None):
+    """Row preparation (RMSNorm / sigmoid gate / plain) + per-token quant + GPTQ W4A8 linear of up to three TILED
+    matrices in one launch (include/mono_b200.h mono_rowlin_gptq). weights: list of (tiled uint8 tensor, rows).
+    gate: bf16 [M, ...] whose row m holds the gate of column c at (c / 256) * gate_head_stride + c % 256.
+    Returns out bf16 [M, sum rows]."""
+    import ctypes
+    _cuda(x)
+    _check(x.dtype == torch.bfloat16 and x.dim() == 2 and x.is_contiguous(), "x bf16 [M, K] contiguous")
+    M, K = x.shape
+    N = sum(int(r) for _, r in weights)
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    _check(out.is_contiguous() and out.numel() == M * N, "out [M, N]")
+    if residual is not None:
+        _check(residual.dtype == torch.bfloat16 and residual.is_contiguous() and residual.numel() == M * N, "residual")
+    for w, r in weights:
+        _check(w.is_cuda and w.dtype == torch.uint8 and w.numel() == _lib.load().mono_w4_tiled_bytes(0, int(r), K),
+               "tiled GPTQ weights")
+    ptrs = (ctypes.c_void_p * len(weights))(*[w.data_ptr() for w, _ in weights])
+    rows = (ctypes.c_int64 * len(weights))(*[int(r) for _, r in weights])
+    nbytes = _lib.load().mono_rowlin_gptq_workspace(K)
+    ws = _workspace(_rowlin_ws, (x.device, K), nbytes, x.device)
+    gate_row_stride = gate.stride(0) if gate is not None else 0
+    with torch.cuda.device(x.device):
+        _lib.call("mono_rowlin_gptq", _p(x), int(mode), _p(norm_w), float(eps), _p(gate), gate_row_stride,
+                  int(gate_head_stride), _p(lut), ctypes.cast(ptrs, ctypes.c_void_p), ctypes.cast(rows, ctypes.c_void_p),
+                  len(weights), M, K, _p(residual), _p(out), _p(xn_out), _p(ws), nbytes, _stream(x.device))
+    return out

@@ -41,6 +41,8 @@ SIGNATURES = {
     "mono_tree_attention_workspace": (SZ, [I64, I64]),
     "mono_tree_attention": (I, [P, P, P, P, P, P, P, I64, I64, I64, I64, P, P, SZ, P]),
     "mono_gdn_step_workspace": (SZ, [I64, I64, I64]),
+    "mono_rowlin_gptq_workspace": (SZ, [I64]),
+    "mono_rowlin_gptq": (I, [P, I, P, ctypes.c_float, P, I64, I64, P, P, P, I, I64, I64, P, P, P, P, SZ, P]),
     "mono_topk_workspace": (SZ, [I64]),
     "mono_fast_topk": (I, [P, I64, I64, I64, I, I, P, P, P, P, SZ, P]),
     "mono_mtp_prep_draft": (I, [P, I64, P, I64, I64, P, P, I64, P, P]),

@@ -151,6 +151,25 @@ MONO_API int mono_mlp_gptq(const void* x, const void* norm_w, float eps, const v
                            const void* down, const void* silu_lut, int64_t M, int64_t H, int64_t I, int residual,
                            void* out, void* workspace, size_t workspace_bytes, mono_stream_t stream);
 
+/* Row preparation + GPTQ W4A8 linear in one cooperative launch (the reference's layer_pre, csrc/mono_layer.sycl:
+ * 69-155, and the gate / out-projection front of layer_post, :243-270):
+ *   mode 0 (norm):  xn = RMSNorm(x; norm_w, eps) (the order of mono_mlp_gptq), q, s = act_quant(xn)
+ *                   (xn_out, if not NULL, receives xn)
+ *   mode 1 (gate):  y = bf16(x * lut[gate]) with gate element (m, c) at
+ *                   gate[m * gate_row_stride + (c / 256) * gate_head_stride + c % 256] (the gate half of the
+ *                   gated query heads: head stride 512) and lut the sigmoid of every bf16 pattern; q, s = act_quant(y)
+ *   mode 2 (quant): q, s = act_quant(x)
+ *   out[m][n] = bf16(GPTQ linear(q, s)) (+ residual: bf16(residual + that)) for nm (1..3) TILED weights of
+ *   rows[i] outputs each, concatenated along n (out row stride = sum of rows).
+ * x bf16 [M][K], 1 <= M <= 16, K a multiple of 1024 up to 4096. workspace: mono_rowlin_gptq_workspace(K) bytes,
+ * zero-filled before its first use (the kernel leaves it reusable); one call at a time per workspace. */
+MONO_API size_t mono_rowlin_gptq_workspace(int64_t K);
+MONO_API int mono_rowlin_gptq(const void* x, int mode, const void* norm_w, float eps, const void* gate,
+                              int64_t gate_row_stride, int64_t gate_head_stride, const void* lut,
+                              const void* const* weights, const int64_t* rows, int nm, int64_t M, int64_t K,
+                              const void* residual, void* out, void* xn_out, void* workspace, size_t workspace_bytes,
+                              mono_stream_t stream);
+
 /* ---- full-attention decode layer ------------------------------------------------------------------ */
 
 /* Per-head Q/K RMSNorm + partial split-half RoPE + K/V cache write (the role of the reference's
