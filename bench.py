@@ -413,6 +413,138 @@ def run_mlp(args):
         dist.destroy_process_group()
 
 
+def run_decode(args):
+    """Config 4: the synthetic Qwen3.5-9B-shaped W4A8 decoder with the device MTP loop (depth-4 chain draft,
+    5 verify rows, greedy accept), one stream per GPU. Steps are captured in two CUDA graphs (the GDN replay
+    buffers alternate) and replayed back to back; the committed tokens are summed on the device."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from mono_b200.decoder import Qwen35Config, Qwen35W4A8
+
+    rank, world, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    cfg = Qwen35Config()
+    prompt = args.prompt
+    model = Qwen35W4A8(cfg, dev, prompt_len=prompt, gen_tokens=max(512, args.steps * 8 + 64), seed=0x5EED + 4 + rank)
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for _ in range(2):  # eager warm-up: workspaces, cuBLAS handles
+            model.step()
+    stream.synchronize()
+    graphs = []
+    for _ in range(2):
+        gph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gph, stream=stream):
+            model.step()
+        graphs.append(gph)
+    for i in range(max(args.warmup, 3)):
+        graphs[i % 2].replay()
+    torch.cuda.synchronize()
+    n0 = int(model.total.item())
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for i in range(args.steps):
+                graphs[i % 2].replay()
+            e1.record(stream)
+        stream.synchronize()
+    ms = e0.elapsed_time(e1)
+    toks = int(model.total.item()) - n0
+    if world > 1:
+        t = torch.tensor([ms, float(toks)], device=dev)
+        dist.all_reduce(t[:1], op=dist.ReduceOp.MAX)
+        tt = t[1:].clone()
+        dist.all_reduce(tt, op=dist.ReduceOp.SUM)
+        ms, toks = float(t[0].item()), int(tt.item())
+    step_ms = ms / args.steps
+    step_bytes = model.step_bytes()
+    hbm, src = peaks()
+    achieved = step_bytes / (step_ms * 1e-3) / 1e9
+    # e2e: the same loop with the step's result row read back to pinned host memory every step
+    host_res = torch.empty(32, dtype=torch.int64).pin_memory()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    m0 = int(model.total.item())
+    e2e_steps = max(8, args.steps // 4)
+    with torch.cuda.stream(stream):
+        f0.record(stream)
+        for i in range(e2e_steps):
+            graphs[(args.steps + i) % 2].replay()
+            host_res.copy_(model.result, non_blocking=True)
+        f1.record(stream)
+    stream.synchronize()
+    e2e_ms = f0.elapsed_time(f1)
+    e2e_toks = int(model.total.item()) - m0
+    if world > 1:
+        t = torch.tensor([e2e_ms, float(e2e_toks)], device=dev)
+        dist.all_reduce(t[:1], op=dist.ReduceOp.MAX)
+        tt = t[1:].clone()
+        dist.all_reduce(tt, op=dist.ReduceOp.SUM)
+        e2e_ms, e2e_toks = float(t[0].item()), int(tt.item())
+    cpu = cpu_decode_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
+    del graphs
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(toks / (ms * 1e-3), 2), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (random-init Qwen3.5-9B-shaped W4A8 weights, random tokens, seeded)",
+            "config": {"workload": f"Qwen3.5-9B-shaped W4A8 MTP decode (configs[4]), prompt {prompt}, depth-4 chain "
+                                   "draft, 5 verify rows, greedy accept, 1 stream per GPU",
+                       "layers": cfg.layers, "steps_per_s": round(args.steps / (ms * 1e-3), 2),
+                       "tokens_per_step": round(toks / (args.steps * world), 3),
+                       "l2": "inputs larger than L2 (6.6 GB of weights read per step)",
+                       "parallelism": f"independent streams x{world}"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(achieved / hbm, 4), "peak_source": src, "traffic": None,
+                         "kernel": "whole decode step (weights + GDN states + KV read once per step)",
+                         "us_per_launch": round(step_ms * 1e3, 2), "algorithmic_bytes_per_launch": step_bytes},
+            "e2e": {"value": round(e2e_toks / (e2e_ms * 1e-3), 2), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 32 * 8},
+            "gpu_launches": None, "clocks": clk.summary()}
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_decode_baseline():
+    """The oracle's eager chain on the host cores for a bounded sample of one decode step: one GDN layer's
+    projections (qkv | z, out) and MLP (gate, up, down) as act-quant + GPTQ linears over 5 verify rows, timed and
+    scaled to the 32 layers' W4A8 bytes (attention layers have 0.97x a GDN layer's bytes: counted as GDN)."""
+    import numpy as np
+    import torch
+
+    from oracle import w4a8 as ow
+    torch.set_num_threads(os.cpu_count() or 1)
+    rng = np.random.default_rng(0)
+    M, H, I = 5, 4096, 12288
+    mats = [(8192 + 4096, H), (H, 4096), (I, H), (I, H), (H, I)]
+    t0 = time.perf_counter()
+    for N, K in mats:
+        packed = rng.integers(0, 2 ** 31, size=(N, K // 8), dtype=np.int64).astype(np.int32).view(np.uint8).reshape(N, K // 2)
+        scales = (np.abs(rng.standard_normal((N, K // 128))) * 0.02 / 7 + 1e-4).astype(np.float16)
+        x = torch.randn(M, K).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+        q, s = ow.act_quant(x)
+        ow.gptq_linear(q, s, packed, scales)
+    layer_s = time.perf_counter() - t0
+    step_s = layer_s * 32
+    return {"value": round(1.0 / step_s, 4), "unit": "tok/s", "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": f"one GDN layer's W4A8 projections + MLP over 5 verify rows ({layer_s:.1f} s), x 32 layers; "
+                      "lm_head, attention, GDN recurrence and the MTP head not counted (a lower bound on the CPU time)"}
+
+
 def cpu_baseline(ow, packed, scales, rows=None):
     """The oracle's eager chain (act quant + GPTQ linear) on the host cores, on a bounded sample."""
     import numpy as np
@@ -474,7 +606,8 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="gemv", choices=["gemv", "mlp"])
+    ap.add_argument("--workload", default="gemv", choices=["gemv", "mlp", "decode"])
+    ap.add_argument("--prompt", type=int, default=1024, help="decode: committed prompt length (KV prefix)")
     ap.add_argument("--rows", type=int, default=8, help="activation rows (tree-verify rows)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     args = ap.parse_args()
@@ -484,6 +617,8 @@ def main():
         run_reference(args)
     elif args.workload == "mlp":
         run_mlp(args)
+    elif args.workload == "decode":
+        run_decode(args)
     else:
         run_ours(args)
 

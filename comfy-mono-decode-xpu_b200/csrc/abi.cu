@@ -311,10 +311,11 @@ size_t mono_gdn_step_workspace(int64_t M, int64_t C, int64_t HV) {
     return gdn_workspace_bytes(int(M), int(C), int(HV));
 }
 
-int mono_gdn_step(const void* qkv, const void* z, const void* a, const void* b, const void* conv_w, void* conv_state,
-                  const float* dt_bias, const float* g_decay, float* state, const void* gnorm_w, float gnorm_eps,
-                  float qscale, int64_t M, int64_t HK, int64_t HV, void* core, void* workspace, size_t workspace_bytes,
-                  mono_stream_t stream) {
+static int gdn_step_impl(const void* qkv, const void* z, const void* a, const void* b, const void* conv_w,
+                         void* conv_state, const float* dt_bias, const float* g_decay, float* state, const void* gnorm_w,
+                         float gnorm_eps, float qscale, int64_t M, int64_t HK, int64_t HV, void* core, void* workspace,
+                         size_t workspace_bytes, const int32_t* ctl, const void* prev_qkv, const void* prev_a,
+                         const void* prev_b, void* save_qkv, void* save_a, void* save_b, mono_stream_t stream) {
     MONO_CHECK(qkv && z && a && b && conv_w && conv_state && dt_bias && g_decay && state && gnorm_w && core && workspace,
                "null operand");
     MONO_CHECK(M >= 1 && M <= 8, "1 <= M <= 8 rows (got %lld)", (long long)M);
@@ -337,11 +338,40 @@ int mono_gdn_step(const void* qkv, const void* z, const void* a, const void* b, 
     A.gnorm_eps = gnorm_eps;
     A.qscale = qscale;
     A.core = static_cast<uint16_t*>(core);
+    A.ctl = ctl;
+    A.prev_qkv = static_cast<const uint16_t*>(prev_qkv);
+    A.prev_a = static_cast<const uint16_t*>(prev_a);
+    A.prev_b = static_cast<const uint16_t*>(prev_b);
+    A.save_qkv = static_cast<uint16_t*>(save_qkv);
+    A.save_a = static_cast<uint16_t*>(save_a);
+    A.save_b = static_cast<uint16_t*>(save_b);
     A.M = int(M);
     A.C = int(C);
     A.HK = int(HK);
     A.HV = int(HV);
     return launch_gdn_step(A, workspace, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int mono_gdn_step(const void* qkv, const void* z, const void* a, const void* b, const void* conv_w, void* conv_state,
+                  const float* dt_bias, const float* g_decay, float* state, const void* gnorm_w, float gnorm_eps,
+                  float qscale, int64_t M, int64_t HK, int64_t HV, void* core, void* workspace, size_t workspace_bytes,
+                  mono_stream_t stream) {
+    return gdn_step_impl(qkv, z, a, b, conv_w, conv_state, dt_bias, g_decay, state, gnorm_w, gnorm_eps, qscale, M, HK,
+                         HV, core, workspace, workspace_bytes, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                         nullptr, stream);
+}
+
+int mono_gdn_step_deferred(const void* qkv, const void* z, const void* a, const void* b, const void* conv_w,
+                           void* conv_state, const float* dt_bias, const float* g_decay, float* state,
+                           const void* gnorm_w, float gnorm_eps, float qscale, int64_t M, int64_t HK, int64_t HV,
+                           void* core, const int32_t* ctl, const void* prev_qkv, const void* prev_a, const void* prev_b,
+                           void* save_qkv, void* save_a, void* save_b, void* workspace, size_t workspace_bytes,
+                           mono_stream_t stream) {
+    MONO_CHECK(ctl && prev_qkv && prev_a && prev_b && save_qkv && save_a && save_b, "deferred form: ctl, prev and save buffers");
+    MONO_CHECK(prev_qkv != save_qkv && prev_a != save_a && prev_b != save_b, "save buffers must not alias the replayed ones");
+    return gdn_step_impl(qkv, z, a, b, conv_w, conv_state, dt_bias, g_decay, state, gnorm_w, gnorm_eps, qscale, M, HK,
+                         HV, core, workspace, workspace_bytes, ctl, prev_qkv, prev_a, prev_b, save_qkv, save_a, save_b,
+                         stream);
 }
 
 size_t mono_topk_workspace(int64_t rows) { return rows < 1 ? 0 : topk_workspace_bytes(rows); }

@@ -120,8 +120,17 @@ struct GdnArgs {
     const uint16_t* gnorm_w; // [128]
     float gnorm_eps, qscale;
     uint16_t* core;          // [M][HV * 128]
-    uint16_t* conv_out;      // workspace [M][C]
-    float* gates;            // workspace [M][HV][2]
+    uint16_t* conv_out;      // workspace [8 + M][C]
+    float* gates;            // workspace [8 + M][HV][2]
+    // deferred form (ctl != null): replay ctl[0] rows of the previous step (slots ctl[2 + i]) from prev_*,
+    // save this step's inputs to save_* (which must not alias prev_*)
+    const int32_t* ctl;
+    const uint16_t* prev_qkv;  // [8][C]
+    const uint16_t* prev_a;    // [8][HV]
+    const uint16_t* prev_b;
+    uint16_t* save_qkv;
+    uint16_t* save_a;
+    uint16_t* save_b;
     int M, C, HK, HV;
 };
 size_t gdn_workspace_bytes(int M, int C, int HV);

@@ -434,3 +434,28 @@ def rowlin_gptq(x, mode, weights, norm_w=None, eps=1e-6, gate=None, gate_head_st
                   int(gate_head_stride), _p(lut), ctypes.cast(ptrs, ctypes.c_void_p), ctypes.cast(rows, ctypes.c_void_p),
                   len(weights), M, K, _p(residual), _p(out), _p(xn_out), _p(ws), nbytes, _stream(x.device))
     return out
+
+
+def gdn_step_deferred(qkv, z, a, b, conv_w, conv_state, dt_bias, g_decay, state, gnorm_w, gnorm_eps, qscale, hk, ctl,
+                      prev, save):
+    """The deferred GDN step of the device MTP loop (include/mono_b200.h mono_gdn_step_deferred): replays the
+    ctl[0] accepted rows of the previous step from prev = (qkv [8, C], a [8, HV], b [8, HV]), persists, then runs
+    this step's rows as a chain without persisting and saves their inputs to save (same shapes, not aliasing
+    prev). Returns core bf16 [M, HV * 128]."""
+    _cuda(qkv, z, a, b, conv_w, conv_state, dt_bias, g_decay, state, gnorm_w, ctl, *prev, *save)
+    M, C = qkv.shape
+    HV = a.shape[1]
+    _check(C == (2 * hk + HV) * 128 and z.shape == (M, HV * 128) and b.shape == a.shape, "GDN shapes")
+    _check(ctl.dtype == torch.int32 and ctl.numel() >= 10, "ctl int32 [26]")
+    for t in (qkv, z, a, b, conv_w, conv_state, gnorm_w, *prev, *save):
+        _check(t.dtype == torch.bfloat16 and t.is_contiguous(), "bf16 contiguous operands")
+    _check(prev[0].shape == (8, C) and prev[1].shape == (8, HV) and save[0].shape == (8, C), "saved rows [8, ...]")
+    nbytes = _lib.load().mono_gdn_step_workspace(M, C, HV)
+    ws = _workspace(_gdn_ws, (qkv.device, M, C, HV), nbytes, qkv.device)
+    core = torch.empty((M, HV * 128), dtype=torch.bfloat16, device=qkv.device)
+    with torch.cuda.device(qkv.device):
+        _lib.call("mono_gdn_step_deferred", _p(qkv), _p(z), _p(a), _p(b), _p(conv_w), _p(conv_state), _p(dt_bias),
+                  _p(g_decay), _p(state), _p(gnorm_w), float(gnorm_eps), float(qscale), M, hk, HV, _p(core), _p(ctl),
+                  _p(prev[0]), _p(prev[1]), _p(prev[2]), _p(save[0]), _p(save[1]), _p(save[2]), _p(ws), nbytes,
+                  _stream(qkv.device))
+    return core

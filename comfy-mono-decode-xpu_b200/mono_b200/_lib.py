@@ -49,6 +49,8 @@ SIGNATURES = {
     "mono_mtp_prep_verify": (I, [P, P, I64, P, P, P, I64, P, P, I64, I64, P]),
     "mono_mtp_accept": (I, [P, P, P, P, P, I64, I64, P, I64, P, P, P, P, I64, I64, I64, I64, P, P]),
     "mono_gdn_step": (I, [P, P, P, P, P, P, P, P, P, P, ctypes.c_float, ctypes.c_float, I64, I64, I64, P, P, SZ, P]),
+    "mono_gdn_step_deferred": (I, [P, P, P, P, P, P, P, P, P, P, ctypes.c_float, ctypes.c_float, I64, I64, I64, P, P, P,
+                                   P, P, P, P, P, P, SZ, P]),
 }
 
 MONO_OK, MONO_EINVAL, MONO_ECUDA, MONO_ETIMEOUT, MONO_EDEVICE = 0, 1, 2, 3, 4

@@ -1,0 +1,255 @@
+"""Synthetic Qwen3.5-9B-shaped W4A8 decoder on the B200 kernels, with the device-side MTP loop.
+
+Random-init weights of the model's architecture (no checkpoint is available): 32 layers in a 3:1 Gated-DeltaNet :
+full-attention pattern, hidden 4096, MLP 12288, vocab 151936, bf16 embedding and lm_head ~ N(0, 0.02), every body
+projection GPTQ W4A8 (int4 uniform in [-8, 7], fp16 group-128 scales |N(0,1)| * 0.02 / 7 + 1e-4), a 1-layer bf16 MTP
+head. One decode step of one stream, queued without any host read-back (the reference's device MTP loop,
+comfy_mono_decode_xpu/mtp_loop.py):
+
+  draft    depth-D chain: d_0 = the step's next token, h_0 = its hidden row; d_j = argmax lm_head(MTP(h_{j-1},
+           embed(d_{j-1}))) (the reference's draft head, comfy_mono_decode_xpu/draft_head.py:190-232)
+  verify   the D + 1 rows [d_0 .. d_D] through the 32 layers (layer_pre / attention or GDN / layer_post / MLP),
+           final norm, lm_head, greedy argmax per row
+  accept   mono_mtp_accept: the accept walk over the chain, the counters, the GDN replay ctl, next token and
+           hidden row (all on the device)
+
+Per layer: full attention = rowlin(norm -> q|k|v) -> qk_norm_rope_kv -> tree attention -> rowlin(gate -> o_proj +
+residual) -> fused MLP; GDN = rowlin(norm -> qkv|z, xn) -> a|b (bf16 GEMM of xn) -> deferred GDN step ->
+rowlin(quant -> out_proj + residual) -> fused MLP. The verify rows form a chain (the GDN step's verify rows run as a
+chain); the bf16 MTP head and the two lm_heads run as cuBLAS GEMMs through torch.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from . import _C
+
+
+@dataclass
+class Qwen35Config:
+    hidden: int = 4096
+    inter: int = 12288
+    vocab: int = 151936
+    layers: int = 32
+    attn_every: int = 4          # layers 3, 7, ..., 31 are full attention (3:1 GDN : attention)
+    heads: int = 16
+    kv_heads: int = 4
+    head_dim: int = 256
+    rotary_dim: int = 64
+    rope_theta: float = 1e7
+    gdn_k_heads: int = 16
+    gdn_v_heads: int = 32
+    gdn_dim: int = 128
+    eps: float = 1e-6
+    depth: int = 4               # MTP draft depth: D + 1 verify rows
+
+    def is_attn(self, i: int) -> bool:
+        return (i + 1) % self.attn_every == 0
+
+
+def _w4(N, K, g, dev):
+    """A random GPTQ W4 matrix (BASELINE configs[0] distributions) in the TILED layout."""
+    packed = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev, generator=g)
+    scales = (torch.randn(N, K // 128, device=dev, generator=g).abs() * (0.02 / 7) + 1e-4).half()
+    t = _C.w4_repack(0, packed, scales, N, K)
+    del packed, scales
+    return t
+
+
+def _bf(shape, g, dev, std=0.02, mean=0.0):
+    return (torch.randn(*shape, device=dev, generator=g) * std + mean).to(torch.bfloat16)
+
+
+def _rms(x, w, eps):
+    xf = x.float()
+    return ((xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)) * w.float()).to(torch.bfloat16)
+
+
+def rope_table(cfg: Qwen35Config, cap: int, dev):
+    """[cap, rd/2, 2, 2] fp32 split-half rotation per position: [[cos, -sin], [sin, cos]] (theta 1e7)."""
+    half = cfg.rotary_dim // 2
+    inv = 1.0 / (cfg.rope_theta ** (torch.arange(half, dtype=torch.float64) * 2 / cfg.rotary_dim))
+    ang = torch.arange(cap, dtype=torch.float64)[:, None] * inv[None, :]
+    c, s = torch.cos(ang), torch.sin(ang)
+    return torch.stack([torch.stack([c, -s], -1), torch.stack([s, c], -1)], -2).float().to(dev).contiguous()
+
+
+class Qwen35W4A8:
+    """Weights and decode state of one stream on one device."""
+
+    def __init__(self, cfg: Qwen35Config, device, prompt_len: int, gen_tokens: int = 512, seed: int = 0x5EED + 4):
+        self.cfg, self.dev = cfg, torch.device(device)
+        c, dev = cfg, self.dev
+        g = torch.Generator(device=dev).manual_seed(seed)
+        H, I, hd = c.hidden, c.inter, c.head_dim
+        self.cap = ((prompt_len + gen_tokens + 64) + 63) // 64 * 64
+        self.embed = _bf((c.vocab, H), g, dev)
+        self.lm_head = _bf((c.vocab, H), g, dev)
+        self.final_norm = _bf((H,), g, dev, 0.02, 1.0)
+        self.layers = []
+        Ck = 2 * c.gdn_k_heads * c.gdn_dim + c.gdn_v_heads * c.gdn_dim
+        for i in range(c.layers):
+            L = {"ln1": _bf((H,), g, dev, 0.02, 1.0), "ln2": _bf((H,), g, dev, 0.02, 1.0),
+                 "gate": _w4(I, H, g, dev), "up": _w4(I, H, g, dev), "down": _w4(H, I, g, dev)}
+            if c.is_attn(i):
+                L.update(q=_w4(2 * c.heads * hd, H, g, dev), k=_w4(c.kv_heads * hd, H, g, dev),
+                         v=_w4(c.kv_heads * hd, H, g, dev), o=_w4(H, c.heads * hd, g, dev),
+                         q_norm=_bf((hd,), g, dev, 0.3, 1.0), k_norm=_bf((hd,), g, dev, 0.3, 1.0),
+                         kc=torch.randn(1, c.kv_heads, self.cap, hd, device=dev, generator=g).to(torch.bfloat16),
+                         vc=torch.randn(1, c.kv_heads, self.cap, hd, device=dev, generator=g).to(torch.bfloat16))
+            else:
+                HV = c.gdn_v_heads
+                L.update(qkv=_w4(Ck, H, g, dev), z=_w4(HV * c.gdn_dim, H, g, dev), out=_w4(H, HV * c.gdn_dim, g, dev),
+                         wab=_bf((2 * HV, H), g, dev), conv_w=_bf((Ck, 4), g, dev, 0.5),
+                         conv_state=_bf((Ck, 3), g, dev, 1.0), dt_bias=torch.zeros(HV, device=dev),
+                         g_decay=-torch.ones(HV, device=dev), gnorm=_bf((c.gdn_dim,), g, dev, 0.1, 1.0),
+                         state=(torch.randn(HV, c.gdn_dim, c.gdn_dim, device=dev, generator=g) * 0.1).contiguous(),
+                         saved=[(torch.zeros(8, Ck, dtype=torch.bfloat16, device=dev),
+                                 torch.zeros(8, HV, dtype=torch.bfloat16, device=dev),
+                                 torch.zeros(8, HV, dtype=torch.bfloat16, device=dev)) for _ in range(2)])
+            self.layers.append(L)
+        # MTP head (bf16): fc 2H -> H, one full-attention layer with its own KV cache, MLP
+        self.mtp = {"enorm": _bf((H,), g, dev, 0.02, 1.0), "hnorm": _bf((H,), g, dev, 0.02, 1.0),
+                    "fc": _bf((H, 2 * H), g, dev), "ln1": _bf((H,), g, dev, 0.02, 1.0),
+                    "qkv": _bf((2 * c.heads * hd + 2 * c.kv_heads * hd, H), g, dev),
+                    "o": _bf((H, c.heads * hd), g, dev), "q_norm": _bf((hd,), g, dev, 0.3, 1.0),
+                    "k_norm": _bf((hd,), g, dev, 0.3, 1.0), "ln2": _bf((H,), g, dev, 0.02, 1.0),
+                    "gate_up": _bf((2 * I, H), g, dev), "down": _bf((H, I), g, dev), "norm": _bf((H,), g, dev, 0.02, 1.0),
+                    "kc": torch.randn(1, c.kv_heads, self.cap, hd, device=dev, generator=g).to(torch.bfloat16),
+                    "vc": torch.randn(1, c.kv_heads, self.cap, hd, device=dev, generator=g).to(torch.bfloat16)}
+        self.rope = rope_table(c, self.cap, dev)
+        self.silu_lut, self.sig_lut = _C.act_luts(dev)
+        # device loop state: st = [committed length, MTP KV length, 0, 0]; ctl of the GDN replay
+        self.st = torch.tensor([prompt_len, prompt_len, 0, 0], dtype=torch.int64, device=dev)
+        self.ctl = torch.zeros(26, dtype=torch.int32, device=dev)
+        self.next_tok = torch.randint(0, c.vocab, (1, 1), device=dev, generator=g)
+        self.hidden = _bf((1, 1, H), g, dev, 1.0)
+        self.parity = 0
+        R = c.depth + 1
+        ch = torch.full((8, 8), -1, dtype=torch.int32)
+        for r in range(R - 1):
+            ch[r, 0] = r + 1
+        self.children = ch.reshape(-1).to(dev)
+        self.mask = torch.tensor([(1 << (r + 1)) - 1 for r in range(R)], dtype=torch.int32, device=dev)
+        self.tree_pos = torch.arange(R, dtype=torch.int64, device=dev)
+        self.tree_ctl = torch.zeros(16, dtype=torch.int32, device=dev)
+        self.result = torch.zeros(32, dtype=torch.int64, device=dev)
+        self.apos = torch.empty(8, dtype=torch.int64, device=dev)
+        self.aseq = torch.empty(1, dtype=torch.int32, device=dev)
+        self.vpos = torch.empty(1, R, dtype=torch.int64, device=dev)
+        self.mpos = torch.empty(8, dtype=torch.int64, device=dev)
+        self.mseq = torch.empty(1, dtype=torch.int32, device=dev)
+        self.mfreq = torch.empty(1, self.cfg.rotary_dim // 2, 2, 2, device=dev)
+        self.kv_ptrs = torch.tensor([t.data_ptr() for L in self.layers if "kc" in L for t in (L["kc"], L["vc"])],
+                                    dtype=torch.int64, device=dev)
+        self.drafts = torch.zeros(R, dtype=torch.int64, device=dev)
+        self.total = torch.zeros(1, dtype=torch.int64, device=dev)  # tokens committed, summed on the device
+
+    # ---- layers ------------------------------------------------------------------------------------------
+    def _attention(self, L, x, freqs):
+        c = self.cfg
+        M = x.shape[0]
+        hd = c.head_dim
+        pre = _C.rowlin_gptq(x, _C.ROWLIN_NORM, [(L["q"], 2 * c.heads * hd), (L["k"], c.kv_heads * hd),
+                                                 (L["v"], c.kv_heads * hd)], norm_w=L["ln1"], eps=c.eps)
+        nq = 2 * c.heads * hd
+        qg = pre[:, :nq].view(1, M, c.heads, 2 * hd)
+        rawk = pre[:, nq:nq + c.kv_heads * hd].view(1, M, c.kv_heads, hd)
+        v = pre[:, nq + c.kv_heads * hd:].view(1, M, c.kv_heads, hd)
+        q, k = _C.qk_norm_rope_kv(qg[..., :hd], rawk, v, L["q_norm"], L["k_norm"], freqs, L["kc"], L["vc"],
+                                  self.apos, c.eps, c.eps, c.rotary_dim)
+        y = _C.attn_dpas(q, L["kc"], L["vc"], self.aseq, k, v.transpose(1, 2), self.mask[:M])
+        x1 = _C.rowlin_gptq(y[0], _C.ROWLIN_GATE, [(L["o"], c.hidden)], gate=pre[:, hd:nq], gate_head_stride=2 * hd,
+                            lut=self.sig_lut, residual=x)
+        return _C.mlp_gptq(x1, L["ln2"], c.eps, L["gate"], L["up"], L["down"], silu_lut=self.silu_lut, I=c.inter)
+
+    def _gdn(self, L, x):
+        c = self.cfg
+        M = x.shape[0]
+        HV, D = c.gdn_v_heads, c.gdn_dim
+        Ck = 2 * c.gdn_k_heads * D + HV * D
+        xn = torch.empty_like(x)
+        pre = _C.rowlin_gptq(x, _C.ROWLIN_NORM, [(L["qkv"], Ck), (L["z"], HV * D)], norm_w=L["ln1"], eps=c.eps,
+                             xn_out=xn)
+        ab = F.linear(xn, L["wab"])
+        prev, save = L["saved"][self.parity], L["saved"][1 - self.parity]
+        core = _C.gdn_step_deferred(pre[:, :Ck].contiguous(), pre[:, Ck:].contiguous(), ab[:, :HV].contiguous(),
+                                    ab[:, HV:].contiguous(), L["conv_w"], L["conv_state"], L["dt_bias"], L["g_decay"],
+                                    L["state"], L["gnorm"], c.eps, D ** -0.5, c.gdn_k_heads, self.ctl, prev, save)
+        x1 = _C.rowlin_gptq(core, _C.ROWLIN_QUANT, [(L["out"], c.hidden)], residual=x)
+        return _C.mlp_gptq(x1, L["ln2"], c.eps, L["gate"], L["up"], L["down"], silu_lut=self.silu_lut, I=c.inter)
+
+    def verify(self, tokens):
+        """The D + 1 chain rows through the body; returns (greedy tokens [1, R], final hidden rows [R, H])."""
+        c = self.cfg
+        R = tokens.numel()
+        _C.mtp_prep_verify(self.st, self.apos, self.aseq, self.vpos, self.tree_pos, self.ctl, self.tree_ctl,
+                           self.parity, 0)
+        x = self.embed[tokens.view(-1)]
+        freqs = self.rope[self.vpos.view(-1).clamp(max=self.cap - 1)]
+        for i, L in enumerate(self.layers):
+            x = self._attention(L, x, freqs) if c.is_attn(i) else self._gdn(L, x)
+        logits = F.linear(_rms(x, self.final_norm, c.eps), self.lm_head)
+        _, toks = _C.fast_topk(logits, 1, True)
+        return toks.view(1, R), x
+
+    def draft_token(self, token, hidden, k):
+        """One MTP draft: (token [1, 1], hidden [1, 1, H]) -> (draft token [1, 1], MTP hidden [1, 1, H])."""
+        c, m = self.cfg, self.mtp
+        hd = c.head_dim
+        _C.mtp_prep_draft(self.st, k, self.rope.view(1, 1, self.cap, -1, 2, 2), self.mfreq.view(1, 1, 1, -1, 2, 2),
+                          self.mpos, self.mseq)
+        e = self.embed[token.view(-1)]
+        x = F.linear(torch.cat([_rms(e, m["enorm"], c.eps), _rms(hidden.view(1, -1), m["hnorm"], c.eps)], -1), m["fc"])
+        qkv = F.linear(_rms(x, m["ln1"], c.eps), m["qkv"])
+        nq = 2 * c.heads * hd
+        qg = qkv[:, :nq].view(1, 1, c.heads, 2 * hd)
+        rawk = qkv[:, nq:nq + c.kv_heads * hd].view(1, 1, c.kv_heads, hd)
+        v = qkv[:, nq + c.kv_heads * hd:].view(1, 1, c.kv_heads, hd)
+        q, kk = _C.qk_norm_rope_kv(qg[..., :hd], rawk, v, m["q_norm"], m["k_norm"], self.mfreq, m["kc"], m["vc"],
+                                   self.mpos, c.eps, c.eps, c.rotary_dim)
+        y = _C.attn_dpas(q, m["kc"], m["vc"], self.mseq, kk, v.transpose(1, 2),
+                         torch.empty(0, dtype=torch.int32, device=self.dev))
+        gate = qg[..., hd:].reshape(1, -1)
+        x = x + F.linear(y[0] * torch.sigmoid(gate), m["o"])
+        gu = F.linear(_rms(x, m["ln2"], c.eps), m["gate_up"])
+        x = x + F.linear(F.silu(gu[:, :c.inter]) * gu[:, c.inter:], m["down"])
+        logits = F.linear(_rms(x, m["norm"], c.eps), self.lm_head)
+        _, t = _C.fast_topk(logits, 1, True)
+        return t.view(1, 1), x.view(1, 1, -1)
+
+    def step(self):
+        """One decode step, queued on the current stream: draft chain, verify, accept. Returns the device result
+        row of mono_mtp_accept ([n, commit[8], ...])."""
+        c = self.cfg
+        tok, h = self.next_tok.view(1, 1), self.hidden
+        self.drafts[0:1] = tok.view(-1)
+        for j in range(1, c.depth + 1):
+            tok, h = self.draft_token(tok, h, j - 1)
+            self.drafts[j:j + 1] = tok.view(-1)
+        toks, x = self.verify(self.drafts)
+        _C.mtp_accept(self.st, toks, self.drafts.view(1, -1), None, self.children, c.depth + 1, c.depth, x,
+                      self.next_tok, self.hidden, self.ctl, self.kv_ptrs, c.kv_heads, self.cap, c.head_dim,
+                      self.result)
+        self.total += self.result[0]
+        self.parity = 1 - self.parity
+        return self.result
+
+    def step_bytes(self) -> int:
+        """Algorithmic HBM bytes of one step: every weight byte read (W4 body once for the verify rows, the
+        bf16 lm_head by the verify and by each draft, the MTP block per draft), GDN states read and written,
+        the attended KV prefix."""
+        c = self.cfg
+        body = sum(t.numel() for L in self.layers for k, t in L.items()
+                   if k in ("gate", "up", "down", "q", "k", "v", "o", "qkv", "z", "out"))
+        small = sum(L[k].numel() * L[k].element_size() for L in self.layers for k in ("wab", "conv_w")
+                    if k in L)
+        state = sum(L["state"].numel() * 4 * 2 for L in self.layers if "state" in L)
+        lm = self.lm_head.numel() * 2
+        mtp = sum(t.numel() * t.element_size() for k, t in self.mtp.items() if k not in ("kc", "vc"))
+        kv = int(self.st[0].item()) * c.kv_heads * c.head_dim * 2 * 2 * sum(1 for L in self.layers if "kc" in L)
+        return body + small + state + lm * (1 + c.depth) + mtp * c.depth + kv

@@ -218,11 +218,24 @@ MONO_API int mono_tree_attention(const void* q, const void* key_cache, const voi
  * state fp32 [HV][128][128] ([k][v], updated); gnorm_w bf16 [128]; core bf16 [M][HV * 128]. 1 <= M <= 8.
  * fp32 arithmetic; results within the tolerance of an fp64 reference stated by the tests. workspace:
  * mono_gdn_step_workspace(M, C, HV) bytes (256-byte aligned). */
-MONO_API size_t mono_gdn_step_workspace(int64_t M, int64_t C, int64_t HV);
+MONO_API size_t mono_gdn_step_workspace(int64_t M, int64_t C, int64_t HV);  /* covers both forms */
 MONO_API int mono_gdn_step(const void* qkv, const void* z, const void* a, const void* b, const void* conv_w,
                            void* conv_state, const float* dt_bias, const float* g_decay, float* state,
                            const void* gnorm_w, float gnorm_eps, float qscale, int64_t M, int64_t HK, int64_t HV,
                            void* core, void* workspace, size_t workspace_bytes, mono_stream_t stream);
+
+/* The deferred form used by the device MTP loop (the reference's replay + verify, csrc/mono_gdn.sycl:385-567):
+ * first the n = ctl[0] rows accepted at the previous step (slots ctl[2 + i], their inputs in prev_qkv [8][C],
+ * prev_a / prev_b [8][HV] as saved by that step) are replayed and the recurrent and conv states persisted;
+ * then the M verify rows run as a chain on a register copy of the state (core outputs only, nothing persisted)
+ * and their inputs are saved to save_qkv / save_a / save_b (which must not alias the prev buffers: alternate
+ * two sets between steps). ctl: int32 [26] as written by mono_mtp_accept. */
+MONO_API int mono_gdn_step_deferred(const void* qkv, const void* z, const void* a, const void* b, const void* conv_w,
+                                    void* conv_state, const float* dt_bias, const float* g_decay, float* state,
+                                    const void* gnorm_w, float gnorm_eps, float qscale, int64_t M, int64_t HK,
+                                    int64_t HV, void* core, const int32_t* ctl, const void* prev_qkv,
+                                    const void* prev_a, const void* prev_b, void* save_qkv, void* save_a, void* save_b,
+                                    void* workspace, size_t workspace_bytes, mono_stream_t stream);
 
 /* ---- logit picks ----------------------------------------------------------------------------------------- */
 

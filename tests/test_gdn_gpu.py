@@ -47,3 +47,45 @@ def test_gdn_step_within_tolerance_of_fp64(cuda, M, seed):
     assert np.array_equal(bf16_bits(cs), hist_ref)
     serr = np.abs(st.cpu().numpy().astype(np.float64) - state_ref)
     assert (serr <= 1e-4 * (1 + np.abs(state_ref))).all(), serr.max()
+
+
+def test_gdn_deferred_replay_then_verify(cuda):
+    """Step 1 verifies 5 rows without persisting; step 2 replays 3 of them (slots 0, 1, 2, as an accept of a
+    chain writes them) and verifies 4 new rows. Reference: the committing oracle on the replayed rows, then on the
+    verify rows from a copy of that state."""
+    from mono_b200 import _C
+    HK, HV, D = 16, 32, 128
+    C = (2 * HK + HV) * D
+    g = torch.Generator().manual_seed(77)
+    rnd = lambda *s: torch.randn(*s, generator=g).bfloat16()
+    conv_w = (torch.randn(C, 4, generator=g) * 0.5).bfloat16()
+    conv_state = rnd(C, 3)
+    dt_bias, g_decay = torch.randn(HV, generator=g) * 0.1, -torch.exp(torch.randn(HV, generator=g) * 0.5)
+    state = torch.randn(HV, D, D, generator=g) * 0.1
+    gw = (1 + torch.randn(D, generator=g) * 0.1).bfloat16()
+    qs = D ** -0.5
+    rows1 = (rnd(5, C), rnd(5, HV * D), rnd(5, HV), rnd(5, HV))
+    rows2 = (rnd(4, C), rnd(4, HV * D), rnd(4, HV), rnd(4, HV))
+    bufs = [(torch.zeros(8, C, dtype=torch.bfloat16, device=cuda), torch.zeros(8, HV, dtype=torch.bfloat16, device=cuda),
+             torch.zeros(8, HV, dtype=torch.bfloat16, device=cuda)) for _ in range(2)]
+    ctl = torch.zeros(26, dtype=torch.int32, device=cuda)
+    cs, st = conv_state.to(cuda), state.to(cuda)
+    args = (conv_w.to(cuda), cs, dt_bias.to(cuda), g_decay.to(cuda), st, gw.to(cuda), 1e-6, qs, HK)
+    core1 = _C.gdn_step_deferred(*[t.to(cuda) for t in rows1], *args, ctl, bufs[1], bufs[0])
+    assert torch.equal(cs.cpu(), conv_state) and torch.equal(st.cpu(), state)  # nothing persisted
+    ref1, _, _ = og.gdn_step(*[bf16_bits(t) for t in rows1], bf16_bits(conv_w), bf16_bits(conv_state), dt_bias.numpy(),
+                             g_decay.numpy(), state.numpy(), bf16_bits(gw), 1e-6, qs, HK)
+    o1 = bf16_bits_to_f32(bf16_bits(core1)).astype(np.float64)
+    assert (np.abs(o1 - ref1) <= 2 ** -6 * np.abs(ref1) + 2e-3).all()
+    ctl[0] = 3
+    ctl[2:10] = torch.arange(8, dtype=torch.int32)
+    core2 = _C.gdn_step_deferred(*[t.to(cuda) for t in rows2], *args, ctl, bufs[0], bufs[1])
+    rep = tuple(t[:3] for t in rows1)
+    _, hist_r, state_r = og.gdn_step(*[bf16_bits(t) for t in rep], bf16_bits(conv_w), bf16_bits(conv_state),
+                                     dt_bias.numpy(), g_decay.numpy(), state.numpy(), bf16_bits(gw), 1e-6, qs, HK)
+    ref2, _, _ = og.gdn_step(*[bf16_bits(t) for t in rows2], bf16_bits(conv_w), hist_r, dt_bias.numpy(), g_decay.numpy(),
+                             state_r.astype(np.float32), bf16_bits(gw), 1e-6, qs, HK)
+    o2 = bf16_bits_to_f32(bf16_bits(core2)).astype(np.float64)
+    assert (np.abs(o2 - ref2) <= 2 ** -6 * np.abs(ref2) + 2e-3).all(), np.abs(o2 - ref2).max()
+    assert np.array_equal(bf16_bits(cs), hist_r)
+    assert (np.abs(st.cpu().numpy() - state_r) <= 1e-4 * (1 + np.abs(state_r))).all()
