@@ -315,7 +315,8 @@ static int gdn_step_impl(const void* qkv, const void* z, const void* a, const vo
                          void* conv_state, const float* dt_bias, const float* g_decay, float* state, const void* gnorm_w,
                          float gnorm_eps, float qscale, int64_t M, int64_t HK, int64_t HV, void* core, void* workspace,
                          size_t workspace_bytes, const int32_t* ctl, const void* prev_qkv, const void* prev_a,
-                         const void* prev_b, void* save_qkv, void* save_a, void* save_b, mono_stream_t stream) {
+                         const void* prev_b, void* save_qkv, void* save_a, void* save_b, int64_t qkv_stride,
+                         int64_t z_stride, int64_t ab_stride, mono_stream_t stream) {
     MONO_CHECK(qkv && z && a && b && conv_w && conv_state && dt_bias && g_decay && state && gnorm_w && core && workspace,
                "null operand");
     MONO_CHECK(M >= 1 && M <= 8, "1 <= M <= 8 rows (got %lld)", (long long)M);
@@ -338,6 +339,10 @@ static int gdn_step_impl(const void* qkv, const void* z, const void* a, const vo
     A.gnorm_eps = gnorm_eps;
     A.qscale = qscale;
     A.core = static_cast<uint16_t*>(core);
+    MONO_CHECK(qkv_stride >= C && z_stride >= HV * 128 && ab_stride >= HV, "row strides cover the rows");
+    A.qkv_stride = qkv_stride;
+    A.z_stride = z_stride;
+    A.ab_stride = ab_stride;
     A.ctl = ctl;
     A.prev_qkv = static_cast<const uint16_t*>(prev_qkv);
     A.prev_a = static_cast<const uint16_t*>(prev_a);
@@ -358,20 +363,20 @@ int mono_gdn_step(const void* qkv, const void* z, const void* a, const void* b, 
                   mono_stream_t stream) {
     return gdn_step_impl(qkv, z, a, b, conv_w, conv_state, dt_bias, g_decay, state, gnorm_w, gnorm_eps, qscale, M, HK,
                          HV, core, workspace, workspace_bytes, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
-                         nullptr, stream);
+                         nullptr, (2 * HK + HV) * 128, HV * 128, HV, stream);
 }
 
 int mono_gdn_step_deferred(const void* qkv, const void* z, const void* a, const void* b, const void* conv_w,
                            void* conv_state, const float* dt_bias, const float* g_decay, float* state,
                            const void* gnorm_w, float gnorm_eps, float qscale, int64_t M, int64_t HK, int64_t HV,
                            void* core, const int32_t* ctl, const void* prev_qkv, const void* prev_a, const void* prev_b,
-                           void* save_qkv, void* save_a, void* save_b, void* workspace, size_t workspace_bytes,
-                           mono_stream_t stream) {
+                           void* save_qkv, void* save_a, void* save_b, int64_t qkv_stride, int64_t z_stride,
+                           int64_t ab_stride, void* workspace, size_t workspace_bytes, mono_stream_t stream) {
     MONO_CHECK(ctl && prev_qkv && prev_a && prev_b && save_qkv && save_a && save_b, "deferred form: ctl, prev and save buffers");
     MONO_CHECK(prev_qkv != save_qkv && prev_a != save_a && prev_b != save_b, "save buffers must not alias the replayed ones");
     return gdn_step_impl(qkv, z, a, b, conv_w, conv_state, dt_bias, g_decay, state, gnorm_w, gnorm_eps, qscale, M, HK,
                          HV, core, workspace, workspace_bytes, ctl, prev_qkv, prev_a, prev_b, save_qkv, save_a, save_b,
-                         stream);
+                         qkv_stride, z_stride, ab_stride, stream);
 }
 
 size_t mono_topk_workspace(int64_t rows) { return rows < 1 ? 0 : topk_workspace_bytes(rows); }

@@ -41,16 +41,17 @@ __global__ void __launch_bounds__(256) gdn_conv_kernel(const GdnArgs A) {
     const int n = gdn_pending(A), R = n + A.M;
     if (i < R * A.HV) {  // gates of every row (replayed rows: from the saved a / b)
         const int t = i / A.HV, h = i % A.HV;
-        const uint16_t ab = t < n ? A.prev_a[size_t(gdn_slot(A, t)) * A.HV + h] : A.a[size_t(t - n) * A.HV + h];
-        const uint16_t bb = t < n ? A.prev_b[size_t(gdn_slot(A, t)) * A.HV + h] : A.b[size_t(t - n) * A.HV + h];
+        const uint16_t ab = t < n ? A.prev_a[size_t(gdn_slot(A, t)) * A.HV + h] : A.a[size_t(t - n) * A.ab_stride + h];
+        const uint16_t bb = t < n ? A.prev_b[size_t(gdn_slot(A, t)) * A.HV + h] : A.b[size_t(t - n) * A.ab_stride + h];
         const float av = bf16_bits_to_f32(ab) + A.dt_bias[h];
         const float sp = av > 20.f ? av : logf(1.f + expf(av));
         A.gates[i * 2] = expf(A.g_decay[h] * sp);
         A.gates[i * 2 + 1] = bf16_round(1.f / (1.f + expf(-bf16_bits_to_f32(bb))));
     }
     if (A.save_a != nullptr && i < A.M * A.HV) {
-        A.save_a[i] = A.a[i];
-        A.save_b[i] = A.b[i];
+        const int t = i / A.HV, h = i % A.HV;
+        A.save_a[i] = A.a[size_t(t) * A.ab_stride + h];
+        A.save_b[i] = A.b[size_t(t) * A.ab_stride + h];
     }
     if (i >= A.C) return;
     float w[4], hist[3 + kGdnMaxAll];
@@ -62,7 +63,7 @@ __global__ void __launch_bounds__(256) gdn_conv_kernel(const GdnArgs A) {
     for (int t = 0; t < kGdnMaxAll; ++t) {
         if (t < n) hist[3 + t] = bf16_bits_to_f32(A.prev_qkv[size_t(gdn_slot(A, t)) * A.C + i]);
         else if (t < R) {
-            const uint16_t v = A.qkv[size_t(t - n) * A.C + i];
+            const uint16_t v = A.qkv[size_t(t - n) * A.qkv_stride + i];
             hist[3 + t] = bf16_bits_to_f32(v);
             if (A.save_qkv != nullptr) A.save_qkv[size_t(t - n) * A.C + i] = v;
         }
@@ -168,7 +169,7 @@ __global__ void __launch_bounds__(kRG * kDH) gdn_delta_kernel(const GdnArgs A) {
         const int t = e / kDH, d = e % kDH;
         const float rs = 1.f / sqrtf(sums[t] / float(kDH) + A.gnorm_eps);
         const float normed = bf16_round((raw[t][d] * bf16_bits_to_f32(A.gnorm_w[d])) * rs);
-        const float z = bf16_bits_to_f32(A.z[size_t(t) * A.HV * kDH + h * kDH + d]);
+        const float z = bf16_bits_to_f32(A.z[size_t(t) * A.z_stride + h * kDH + d]);
         const float gz = bf16_round(z / (1.f + expf(-z)));
         A.core[size_t(t) * A.HV * kDH + h * kDH + d] = f32_to_bf16_bits(normed * gz);
     }

@@ -131,6 +131,7 @@ struct GdnArgs {
     uint16_t* save_qkv;
     uint16_t* save_a;
     uint16_t* save_b;
+    int64_t qkv_stride, z_stride, ab_stride;  // row strides (elements) of qkv, z, a / b
     int M, C, HK, HV;
 };
 size_t gdn_workspace_bytes(int M, int C, int HV);

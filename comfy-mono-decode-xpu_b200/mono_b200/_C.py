@@ -447,7 +447,10 @@ def gdn_step_deferred(qkv, z, a, b, conv_w, conv_state, dt_bias, g_decay, state,
     HV = a.shape[1]
     _check(C == (2 * hk + HV) * 128 and z.shape == (M, HV * 128) and b.shape == a.shape, "GDN shapes")
     _check(ctl.dtype == torch.int32 and ctl.numel() >= 10, "ctl int32 [26]")
-    for t in (qkv, z, a, b, conv_w, conv_state, gnorm_w, *prev, *save):
+    for t in (qkv, z, a, b):  # column slices of wider rows are fine
+        _check(t.dtype == torch.bfloat16 and t.stride(1) == 1, "bf16 rows with unit column stride")
+    _check(a.stride(0) == b.stride(0), "a and b share a row stride")
+    for t in (conv_w, conv_state, gnorm_w, *prev, *save):
         _check(t.dtype == torch.bfloat16 and t.is_contiguous(), "bf16 contiguous operands")
     _check(prev[0].shape == (8, C) and prev[1].shape == (8, HV) and save[0].shape == (8, C), "saved rows [8, ...]")
     nbytes = _lib.load().mono_gdn_step_workspace(M, C, HV)
@@ -456,6 +459,34 @@ def gdn_step_deferred(qkv, z, a, b, conv_w, conv_state, dt_bias, g_decay, state,
     with torch.cuda.device(qkv.device):
         _lib.call("mono_gdn_step_deferred", _p(qkv), _p(z), _p(a), _p(b), _p(conv_w), _p(conv_state), _p(dt_bias),
                   _p(g_decay), _p(state), _p(gnorm_w), float(gnorm_eps), float(qscale), M, hk, HV, _p(core), _p(ctl),
-                  _p(prev[0]), _p(prev[1]), _p(prev[2]), _p(save[0]), _p(save[1]), _p(save[2]), _p(ws), nbytes,
-                  _stream(qkv.device))
+                  _p(prev[0]), _p(prev[1]), _p(prev[2]), _p(save[0]), _p(save[1]), _p(save[2]), qkv.stride(0),
+                  z.stride(0), a.stride(0), _p(ws), nbytes, _stream(qkv.device))
     return core
+
+
+def rmsnorm_add(x, w, eps, add=None, out=None, sum_out=None):
+    """out = RMSNorm(x (+ add, rounded to bf16 and written to sum_out)) for bf16 rows [M, H] (column slices of
+    wider rows are fine). Returns out (and sum_out when add is given)."""
+    _cuda(x, w)
+    M, H = x.shape
+    if out is None:
+        out = torch.empty((M, H), dtype=torch.bfloat16, device=x.device)
+    if add is not None and sum_out is None:
+        sum_out = torch.empty_like(out)
+    _check(out.stride(0) == (sum_out.stride(0) if sum_out is not None else out.stride(0)), "out / sum_out strides")
+    with torch.cuda.device(x.device):
+        _lib.call("mono_rmsnorm_add", _p(x), x.stride(0), _p(add), add.stride(0) if add is not None else 0, _p(w),
+                  float(eps), M, H, _p(out), _p(sum_out), out.stride(0), _stream(x.device))
+    return (out, sum_out) if add is not None else out
+
+
+def lut_mul(a, b, lut, b_head_stride=256, out=None):
+    """bf16(a * lut[b]) elementwise over rows [M, K]; b's column c at (c / 256) * b_head_stride + c % 256."""
+    _cuda(a, b, lut)
+    M, K = a.shape
+    if out is None:
+        out = torch.empty((M, K), dtype=torch.bfloat16, device=a.device)
+    with torch.cuda.device(a.device):
+        _lib.call("mono_lut_mul", _p(a), a.stride(0), _p(b), b.stride(0), int(b_head_stride), _p(lut), M, K, _p(out),
+                  out.stride(0), _stream(a.device))
+    return out

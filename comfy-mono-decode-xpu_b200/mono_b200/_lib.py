@@ -43,6 +43,8 @@ SIGNATURES = {
     "mono_gdn_step_workspace": (SZ, [I64, I64, I64]),
     "mono_rowlin_gptq_workspace": (SZ, [I64]),
     "mono_rowlin_gptq": (I, [P, I, P, ctypes.c_float, P, I64, I64, P, P, P, I, I64, I64, P, P, P, P, SZ, P]),
+    "mono_rmsnorm_add": (I, [P, I64, P, I64, P, ctypes.c_float, I64, I64, P, P, I64, P]),
+    "mono_lut_mul": (I, [P, I64, P, I64, I64, P, I64, I64, P, I64, P]),
     "mono_topk_workspace": (SZ, [I64]),
     "mono_fast_topk": (I, [P, I64, I64, I64, I, I, P, P, P, P, SZ, P]),
     "mono_mtp_prep_draft": (I, [P, I64, P, I64, I64, P, P, I64, P, P]),
@@ -50,7 +52,7 @@ SIGNATURES = {
     "mono_mtp_accept": (I, [P, P, P, P, P, I64, I64, P, I64, P, P, P, P, I64, I64, I64, I64, P, P]),
     "mono_gdn_step": (I, [P, P, P, P, P, P, P, P, P, P, ctypes.c_float, ctypes.c_float, I64, I64, I64, P, P, SZ, P]),
     "mono_gdn_step_deferred": (I, [P, P, P, P, P, P, P, P, P, P, ctypes.c_float, ctypes.c_float, I64, I64, I64, P, P, P,
-                                   P, P, P, P, P, P, SZ, P]),
+                                   P, P, P, P, P, I64, I64, I64, P, SZ, P]),
 }
 
 MONO_OK, MONO_EINVAL, MONO_ECUDA, MONO_ETIMEOUT, MONO_EDEVICE = 0, 1, 2, 3, 4

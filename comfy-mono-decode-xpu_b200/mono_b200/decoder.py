@@ -16,7 +16,8 @@ comfy_mono_decode_xpu/mtp_loop.py):
 Per layer: full attention = rowlin(norm -> q|k|v) -> qk_norm_rope_kv -> tree attention -> rowlin(gate -> o_proj +
 residual) -> fused MLP; GDN = rowlin(norm -> qkv|z, xn) -> a|b (bf16 GEMM of xn) -> deferred GDN step ->
 rowlin(quant -> out_proj + residual) -> fused MLP. The verify rows form a chain (the GDN step's verify rows run as a
-chain); the bf16 MTP head and the two lm_heads run as cuBLAS GEMMs through torch.
+chain); the bf16 MTP head and the two lm_heads run as cuBLAS GEMMs through torch; their norms and gates are the row kernels
+(mono_rmsnorm_add, mono_lut_mul).
 """
 from __future__ import annotations
 
@@ -147,6 +148,7 @@ class Qwen35W4A8:
         self.kv_ptrs = torch.tensor([t.data_ptr() for L in self.layers if "kc" in L for t in (L["kc"], L["vc"])],
                                     dtype=torch.int64, device=dev)
         self.drafts = torch.zeros(R, dtype=torch.int64, device=dev)
+        self.no_mask = torch.empty(0, dtype=torch.int32, device=dev)
         self.total = torch.zeros(1, dtype=torch.int64, device=dev)  # tokens committed, summed on the device
 
     # ---- layers ------------------------------------------------------------------------------------------
@@ -177,8 +179,8 @@ class Qwen35W4A8:
                              xn_out=xn)
         ab = F.linear(xn, L["wab"])
         prev, save = L["saved"][self.parity], L["saved"][1 - self.parity]
-        core = _C.gdn_step_deferred(pre[:, :Ck].contiguous(), pre[:, Ck:].contiguous(), ab[:, :HV].contiguous(),
-                                    ab[:, HV:].contiguous(), L["conv_w"], L["conv_state"], L["dt_bias"], L["g_decay"],
+        core = _C.gdn_step_deferred(pre[:, :Ck], pre[:, Ck:], ab[:, :HV], ab[:, HV:], L["conv_w"], L["conv_state"],
+                                    L["dt_bias"], L["g_decay"],
                                     L["state"], L["gnorm"], c.eps, D ** -0.5, c.gdn_k_heads, self.ctl, prev, save)
         x1 = _C.rowlin_gptq(core, _C.ROWLIN_QUANT, [(L["out"], c.hidden)], residual=x)
         return _C.mlp_gptq(x1, L["ln2"], c.eps, L["gate"], L["up"], L["down"], silu_lut=self.silu_lut, I=c.inter)
@@ -193,32 +195,35 @@ class Qwen35W4A8:
         freqs = self.rope[self.vpos.view(-1).clamp(max=self.cap - 1)]
         for i, L in enumerate(self.layers):
             x = self._attention(L, x, freqs) if c.is_attn(i) else self._gdn(L, x)
-        logits = F.linear(_rms(x, self.final_norm, c.eps), self.lm_head)
+        logits = F.linear(_C.rmsnorm_add(x, self.final_norm, c.eps), self.lm_head)
         _, toks = _C.fast_topk(logits, 1, True)
         return toks.view(1, R), x
 
     def draft_token(self, token, hidden, k):
         """One MTP draft: (token [1, 1], hidden [1, 1, H]) -> (draft token [1, 1], MTP hidden [1, 1, H])."""
         c, m = self.cfg, self.mtp
-        hd = c.head_dim
+        hd, H = c.head_dim, c.hidden
         _C.mtp_prep_draft(self.st, k, self.rope.view(1, 1, self.cap, -1, 2, 2), self.mfreq.view(1, 1, 1, -1, 2, 2),
                           self.mpos, self.mseq)
         e = self.embed[token.view(-1)]
-        x = F.linear(torch.cat([_rms(e, m["enorm"], c.eps), _rms(hidden.view(1, -1), m["hnorm"], c.eps)], -1), m["fc"])
-        qkv = F.linear(_rms(x, m["ln1"], c.eps), m["qkv"])
+        cat = torch.empty(1, 2 * H, dtype=torch.bfloat16, device=self.dev)
+        _C.rmsnorm_add(e, m["enorm"], c.eps, out=cat[:, :H])
+        _C.rmsnorm_add(hidden.view(1, -1), m["hnorm"], c.eps, out=cat[:, H:])
+        x = F.linear(cat, m["fc"])
+        qkv = F.linear(_C.rmsnorm_add(x, m["ln1"], c.eps), m["qkv"])
         nq = 2 * c.heads * hd
         qg = qkv[:, :nq].view(1, 1, c.heads, 2 * hd)
         rawk = qkv[:, nq:nq + c.kv_heads * hd].view(1, 1, c.kv_heads, hd)
         v = qkv[:, nq + c.kv_heads * hd:].view(1, 1, c.kv_heads, hd)
         q, kk = _C.qk_norm_rope_kv(qg[..., :hd], rawk, v, m["q_norm"], m["k_norm"], self.mfreq, m["kc"], m["vc"],
                                    self.mpos, c.eps, c.eps, c.rotary_dim)
-        y = _C.attn_dpas(q, m["kc"], m["vc"], self.mseq, kk, v.transpose(1, 2),
-                         torch.empty(0, dtype=torch.int32, device=self.dev))
-        gate = qg[..., hd:].reshape(1, -1)
-        x = x + F.linear(y[0] * torch.sigmoid(gate), m["o"])
-        gu = F.linear(_rms(x, m["ln2"], c.eps), m["gate_up"])
-        x = x + F.linear(F.silu(gu[:, :c.inter]) * gu[:, c.inter:], m["down"])
-        logits = F.linear(_rms(x, m["norm"], c.eps), self.lm_head)
+        y = _C.attn_dpas(q, m["kc"], m["vc"], self.mseq, kk, v.transpose(1, 2), self.no_mask)
+        yg = _C.lut_mul(y[0], qkv[:, hd:nq], self.sig_lut, b_head_stride=2 * hd)
+        xn, x = _C.rmsnorm_add(x, m["ln2"], c.eps, add=F.linear(yg, m["o"]))
+        gu = F.linear(xn, m["gate_up"])
+        h = _C.lut_mul(gu[:, c.inter:], gu[:, :c.inter], self.silu_lut)
+        xf, x = _C.rmsnorm_add(x, m["norm"], c.eps, add=F.linear(h, m["down"]))
+        logits = F.linear(xf, self.lm_head)
         _, t = _C.fast_topk(logits, 1, True)
         return t.view(1, 1), x.view(1, 1, -1)
 

@@ -229,13 +229,30 @@ MONO_API int mono_gdn_step(const void* qkv, const void* z, const void* a, const 
  * prev_a / prev_b [8][HV] as saved by that step) are replayed and the recurrent and conv states persisted;
  * then the M verify rows run as a chain on a register copy of the state (core outputs only, nothing persisted)
  * and their inputs are saved to save_qkv / save_a / save_b (which must not alias the prev buffers: alternate
- * two sets between steps). ctl: int32 [26] as written by mono_mtp_accept. */
+ * two sets between steps). ctl: int32 [26] as written by mono_mtp_accept. qkv, z and a / b may be column
+ * slices of wider rows: their row strides (elements) are given (qkv_stride >= C, z_stride >= HV * 128,
+ * ab_stride >= HV). */
 MONO_API int mono_gdn_step_deferred(const void* qkv, const void* z, const void* a, const void* b, const void* conv_w,
                                     void* conv_state, const float* dt_bias, const float* g_decay, float* state,
                                     const void* gnorm_w, float gnorm_eps, float qscale, int64_t M, int64_t HK,
                                     int64_t HV, void* core, const int32_t* ctl, const void* prev_qkv,
                                     const void* prev_a, const void* prev_b, void* save_qkv, void* save_a, void* save_b,
-                                    void* workspace, size_t workspace_bytes, mono_stream_t stream);
+                                    int64_t qkv_stride, int64_t z_stride, int64_t ab_stride, void* workspace,
+                                    size_t workspace_bytes, mono_stream_t stream);
+
+/* ---- small row kernels of the bf16 parts of the step (MTP draft head, final norm) ------------------------- */
+
+/* s = add ? bf16(x + add) : x (sum_out receives s when add is given); out = bf16((s * r) * w),
+ * r = 1 / sqrt(mean(s^2) + eps) (fp32, per-thread then butterfly then warp-order sums; IEEE div / sqrt).
+ * bf16 rows with strides in elements (multiples of 8), H a multiple of 8. */
+MONO_API int mono_rmsnorm_add(const void* x, int64_t x_stride, const void* add, int64_t add_stride, const void* w,
+                              float eps, int64_t M, int64_t H, void* out, void* sum_out, int64_t out_stride,
+                              mono_stream_t stream);
+
+/* out[m][c] = bf16(a[m][c] * lut[b[m][(c / 256) * b_head_stride + c % 256]]) (lut: bf16 [65536], e.g. SiLU or
+ * sigmoid of every bf16 pattern): SiLU(gate) * up, or attention * sigmoid(gate of gated heads). */
+MONO_API int mono_lut_mul(const void* a, int64_t a_stride, const void* b, int64_t b_stride, int64_t b_head_stride,
+                          const void* lut, int64_t M, int64_t K, void* out, int64_t out_stride, mono_stream_t stream);
 
 /* ---- logit picks ----------------------------------------------------------------------------------------- */
 
