@@ -244,6 +244,15 @@ class Qwen35W4A8:
         self.parity = 1 - self.parity
         return self.result
 
+    def own_launches_per_step(self) -> int:
+        """This build's kernel launches per step (the rest are cuBLAS GEMMs and a few torch gathers / copies)."""
+        c = self.cfg
+        n_attn = sum(1 for i in range(c.layers) if c.is_attn(i))
+        n_gdn = c.layers - n_attn
+        body = c.layers * 3 + n_gdn * 2 + n_attn * 3          # rowlin x2 + MLP; GDN conv + delta; rope + attention x2
+        draft = c.depth * (1 + 3 + 1 + 2 + 2 + 2 + 2)       # prep, norms, rope, attention, lut x2, norm-adds, argmax
+        return body + draft + 1 + 2 + 1 + 1                   # prep_verify, final norm + argmax, accept, verify norm
+
     def step_bytes(self) -> int:
         """Algorithmic HBM bytes of one step: every weight byte read (W4 body once for the verify rows, the
         bf16 lm_head by the verify and by each draft, the MTP block per draft), GDN states read and written,
