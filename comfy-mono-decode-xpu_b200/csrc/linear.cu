@@ -57,34 +57,41 @@ __global__ void __launch_bounds__(kLinThreads, 1) linear_kernel(const Program P,
         xs = XSrc{xsm, K + 16, true, true};
     }
     trace_stamp(1);
-    const bool ok = consume_phase<FMT, LAYOUT, MT, kLinCW>(P, 0, xs, ring, full, empty, S, part, warp, lane);
-    const bool all_ok = consumer_sync_and<kLinCW>(ok);
-    trace_stamp(2);
-    if (!all_ok) return;
-    const int N = ph.m[0].n, ntl = cta_tiles(ph);
-    for (int e = threadIdx.x; e < ntl * M * 16; e += kLinCW * 32) {
-        const int k = e / (M * 16), r = e - k * (M * 16), m = r >> 4, nl = r & 15;
-        const int n = (int(blockIdx.x) + k * int(gridDim.x)) * 16 + nl;
-        const uint32_t tot = tile_total<FMT, MT>(part + size_t(k) * C * MT * 128, C, 0, m, nl);
-        float f;
-        const float xsv = E.xb ? xs_sm[m] : E.xs[m];
-        if constexpr (FMT == FMT_GPTQ) {
-            f = __fmul_rn(__uint_as_float(tot), xsv);
-        } else {
-            f = __fmul_rn(__int2float_rn(int(tot)), xsv);
-            f = __fmul_rn(f, E.s_channel[n]);
+    // tiles in batches of E.max_items / C (the partials of one batch fit the shared buffer), epilogue per batch
+    const int N = ph.m[0].n, ntl = cta_tiles(ph), TB = E.max_items / C;
+    bool all_ok = true;
+    for (int k0 = 0; k0 < ntl && all_ok; k0 += TB) {
+        const int kb = ntl - k0 < TB ? ntl - k0 : TB;
+        const bool ok = consume_phase<FMT, LAYOUT, MT, kLinCW>(P, 0, xs, ring, full, empty, S, part, warp, lane, k0 * C,
+                                                               kb * C);
+        all_ok = consumer_sync_and<kLinCW>(ok);
+        if (k0 == 0) trace_stamp(2);
+        if (!all_ok) break;
+        for (int e = threadIdx.x; e < kb * M * 16; e += kLinCW * 32) {
+            const int kk = e / (M * 16), r = e - kk * (M * 16), m = r >> 4, nl = r & 15;
+            const int n = (int(blockIdx.x) + (k0 + kk) * int(gridDim.x)) * 16 + nl;
+            const uint32_t tot = tile_total<FMT, MT>(part + size_t(kk) * C * MT * 128, C, 0, m, nl);
+            float f;
+            const float xsv = E.xb ? xs_sm[m] : E.xs[m];
+            if constexpr (FMT == FMT_GPTQ) {
+                f = __fmul_rn(__uint_as_float(tot), xsv);
+            } else {
+                f = __fmul_rn(__int2float_rn(int(tot)), xsv);
+                f = __fmul_rn(f, E.s_channel[n]);
+            }
+            const size_t o = size_t(m) * N + n;
+            if (E.out_bf16) {
+                uint16_t rb = f32_to_bf16_bits(f);
+                if (E.residual)
+                    rb = f32_to_bf16_bits(__fadd_rn(bf16_bits_to_f32(static_cast<const uint16_t*>(E.residual)[o]),
+                                                    bf16_bits_to_f32(rb)));
+                static_cast<uint16_t*>(E.out)[o] = rb;
+            } else {
+                if (E.residual) f = __fadd_rn(static_cast<const float*>(E.residual)[o], f);
+                static_cast<float*>(E.out)[o] = f;
+            }
         }
-        const size_t o = size_t(m) * N + n;
-        if (E.out_bf16) {
-            uint16_t rb = f32_to_bf16_bits(f);
-            if (E.residual)
-                rb = f32_to_bf16_bits(__fadd_rn(bf16_bits_to_f32(static_cast<const uint16_t*>(E.residual)[o]),
-                                                bf16_bits_to_f32(rb)));
-            static_cast<uint16_t*>(E.out)[o] = rb;
-        } else {
-            if (E.residual) f = __fadd_rn(static_cast<const float*>(E.residual)[o], f);
-            static_cast<float*>(E.out)[o] = f;
-        }
+        consumer_sync<kLinCW>();  // the batch's partials are read before the next batch writes them
     }
     trace_stamp(3);
 }
@@ -96,7 +103,8 @@ static int launch_linear_mt(Program& P, LinearEpi& E, cudaStream_t stream) {
     PhaseDesc& ph = P.ph[0];
     const int tiles = phase_tiles(ph), grid = tiles < sm_count() ? tiles : sm_count();
     const int tiles_cta = (tiles + grid - 1) / grid, C = phase_chunks(ph);
-    E.max_items = tiles_cta * C;  // partial slots of one CTA: all its items
+    // partial slots: the CTA's tiles in batches of at most 8 (for very wide matrices such as an lm_head)
+    E.max_items = (tiles_cta < 8 ? tiles_cta : 8) * C;
     const size_t part_bytes = size_t(E.max_items) * MT * 128 * 4;
     // stage the activations when they fit next to the partials and the ring
     for (int staged = 1; staged >= (E.xb ? 1 : 0); --staged) {

@@ -19,12 +19,13 @@ namespace mono {
 
 // One CTA per SM (cooperative): 12 consumer warps + 4 producer warps (stream.cuh), S = 12 ring stages. The
 // producers stream gate/up and then down weights straight through the row phases and the grid barriers.
-constexpr int kMlpCW = 12, kMlpPW = 4, kMlpThreads = (kMlpCW + kMlpPW) * 32;
+// Warp configurations (consumer warps CW, producer warps PW, ring stages S = a common multiple): the deepest
+// ring that fits next to the partials and the staged activations is taken (stream_config in stream.cuh).
 
-template <int MT>
-__global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const Program P, const MlpArgs A, const MlpShape Z) {
+template <int MT, int CW, int PW>
+__global__ void __launch_bounds__((CW + PW) * 32, 1) mlp_kernel(const Program P, const MlpArgs A, const MlpShape Z) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ float red[3][16];
+    __shared__ float red[CW / 4][16];
     __shared__ unsigned rowmax[16];
     __shared__ int flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -45,12 +46,12 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const Program P, co
     __syncthreads();
     trace_stamp(0);
     pdl_launch_dependents();  // the next kernel may launch and stream its weights as our CTAs exit
-    if (warp >= kMlpCW) {
+    if (warp >= CW) {
         // weights do not depend on the preceding kernel: stream them before (without) the dependency wait
-        produce_all<FMT_GPTQ, LAYOUT_TILED, kMlpPW>(P, ring, full, empty, S, warp - kMlpCW, lane);
+        produce_all<FMT_GPTQ, LAYOUT_TILED, PW>(P, ring, full, empty, S, warp - CW, lane);
         return;
     }
-    constexpr int NT = kMlpCW * 32;
+    constexpr int NT = CW * 32, NWG = CW / 4;  // whole warp-groups do the row phases
     pdl_wait();
     trace_stamp(1);
     unsigned epoch = 0;
@@ -60,7 +61,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const Program P, co
     if (blockIdx.x == 0 && threadIdx.x < 16) A.amax2[threadIdx.x] = 0u;
     {
         const int wg = threadIdx.x >> 7, tig = threadIdx.x & 127;  // consumer warp-groups 0..2
-        for (int m = wg * int(gridDim.x) + int(blockIdx.x); m < M; m += 3 * int(gridDim.x))
+        for (int m = wg * int(gridDim.x) + int(blockIdx.x); wg < NWG && m < M; m += NWG * int(gridDim.x))
             norm_quant_row(A.x + size_t(m) * A.H, A.norm_w, A.eps, A.H, nullptr, A.q1 + size_t(m) * A.H, A.s1 + m, red[wg],
                            tig, wg);
     }
@@ -71,7 +72,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const Program P, co
     auto phase_x = [&](int ph) {
         const PhaseDesc& p = P.ph[ph];
         if (!p.xsmem) return XSrc{p.x, p.K, false, true};
-        stage_x_consumers<kMlpCW>(p.x, M, p.K, true, xsm);
+        stage_x_consumers<CW>(p.x, M, p.K, true, xsm);
         return XSrc{xsm, p.K + 16, true, true};
     };
 
@@ -82,8 +83,8 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const Program P, co
         const PhaseDesc& ph = P.ph[0];
         const int C = phase_chunks(ph), ntl = cta_tiles(ph);
         if (threadIdx.x < 16) rowmax[threadIdx.x] = 0u;
-        ok = consume_phase<FMT_GPTQ, LAYOUT_TILED, MT, kMlpCW>(P, 0, xs, ring, full, empty, S, part, warp, lane) && ok;
-        ok = consumer_sync_and<kMlpCW>(ok);
+        ok = consume_phase<FMT_GPTQ, LAYOUT_TILED, MT, CW>(P, 0, xs, ring, full, empty, S, part, warp, lane) && ok;
+        ok = consumer_sync_and<CW>(ok);
         for (int e = threadIdx.x; e < ntl * M * 16 && ok; e += NT) {
             const int k = e / (M * 16), r = e - k * (M * 16), m = r >> 4, nl = r & 15;
             const int n = (int(blockIdx.x) + k * int(gridDim.x)) * 16 + nl;
@@ -97,7 +98,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const Program P, co
             A.h[size_t(m) * A.I + n] = hb;
             atomicMax(&rowmax[m], __float_as_uint(fabsf(bf16_bits_to_f32(hb))));
         }
-        consumer_sync<kMlpCW>();
+        consumer_sync<CW>();
         if (threadIdx.x < M) atomicMax(A.amax2 + threadIdx.x, rowmax[threadIdx.x]);
     }
     trace_stamp(5);
@@ -131,8 +132,8 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const Program P, co
         trace_stamp(9);
         const PhaseDesc& ph = P.ph[1];
         const int C = phase_chunks(ph), ntl = cta_tiles(ph);
-        ok = consume_phase<FMT_GPTQ, LAYOUT_TILED, MT, kMlpCW>(P, 1, xs, ring, full, empty, S, part, warp, lane) && ok;
-        ok = consumer_sync_and<kMlpCW>(ok);
+        ok = consume_phase<FMT_GPTQ, LAYOUT_TILED, MT, CW>(P, 1, xs, ring, full, empty, S, part, warp, lane) && ok;
+        ok = consumer_sync_and<CW>(ok);
         for (int e = threadIdx.x; e < ntl * M * 16 && ok; e += NT) {
             const int k = e / (M * 16), r = e - k * (M * 16), m = r >> 4, nl = r & 15;
             const int n = (int(blockIdx.x) + k * int(gridDim.x)) * 16 + nl;
@@ -154,9 +155,9 @@ size_t mlp_workspace_bytes(int H, int I) {
     return al(16 * size_t(H) * 2) + al(16 * size_t(H)) + al(16 * size_t(I) * 2) + al(16 * size_t(I)) + 4 * 256;
 }
 
-template <int MT>
+template <int MT, int CW, int PW>
 static int launch_mlp_t(const Program& P, const MlpArgs& A, const MlpShape& Z, size_t smem, cudaStream_t stream) {
-    auto kern = mlp_kernel<MT>;
+    auto kern = mlp_kernel<MT, CW, PW>;
     static std::mutex mu;
     static size_t opt_in = 0;
     static int per_sm = 0;
@@ -165,13 +166,13 @@ static int launch_mlp_t(const Program& P, const MlpArgs& A, const MlpShape& Z, s
         if (smem > opt_in) {
             CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
             opt_in = smem;
-            CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kMlpThreads, smem));
+            CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, (CW + PW) * 32, smem));
         }
     }
     if (per_sm < 1) return fail(MONO_EINVAL, "mlp: one CTA does not fit an SM (%zu B shared)", smem);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(sm_count());
-    cfg.blockDim = dim3(kMlpThreads);
+    cfg.blockDim = dim3((CW + PW) * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
@@ -185,7 +186,6 @@ static int launch_mlp_t(const Program& P, const MlpArgs& A, const MlpShape& Z, s
     return MONO_OK;
 }
 
-constexpr size_t kMlpSmemLimit = 227 * 1024 - 512;  // leave room for the static shared memory
 
 int launch_mlp(Program& P, MlpArgs& A, cudaStream_t stream) {
     const int M = P.M, G = sm_count();
@@ -205,10 +205,22 @@ int launch_mlp(Program& P, MlpArgs& A, cudaStream_t stream) {
         size_t xb = 0;
         for (int i = 0; i < P.nph; ++i)
             if (P.ph[i].xsmem) xb = size_t(M) * (P.ph[i].K + 16) > xb ? size_t(M) * (P.ph[i].K + 16) : xb;
-        const StreamPlan plan(stage_bytes<FMT_GPTQ>(), kMlpCW, part, xb, 0);
-        if (plan.total <= kMlpSmemLimit) {
-            const MlpShape Z{kMlpCW, int(part), int(xb)};
-            return two ? launch_mlp_t<2>(P, A, Z, plan.total, stream) : launch_mlp_t<1>(P, A, Z, plan.total, stream);
+        for (int c = 0; c < kStreamConfigs; ++c) {
+            const StreamConfig sc = kStreamConfig[c];
+            const StreamPlan plan(stage_bytes<FMT_GPTQ>(), sc.S, part, xb, 0);
+            if (plan.total > kStreamSmemLimit) continue;
+            const MlpShape Z{sc.S, int(part), int(xb)};
+#define MONO_MLP(MTV, CWV, PWV) return launch_mlp_t<MTV, CWV, PWV>(P, A, Z, plan.total, stream)
+            if (!two) {
+                if (c == 0) MONO_MLP(1, 10, 2);
+                if (c == 1) MONO_MLP(1, 8, 4);
+                MONO_MLP(1, 12, 4);
+            } else {
+                if (c == 0) MONO_MLP(2, 10, 2);
+                if (c == 1) MONO_MLP(2, 8, 4);
+                MONO_MLP(2, 12, 4);
+            }
+#undef MONO_MLP
         }
         int big = -1;
         for (int i = 0; i < P.nph; ++i)

@@ -18,7 +18,8 @@
 
 namespace mono {
 
-constexpr int kRlCW = 12, kRlPW = 4, kRlThreads = (kRlCW + kRlPW) * 32;
+// Warp configurations (consumer warps CW, producer warps PW, ring stages S = a common multiple): the deepest
+// ring that fits next to the partials and the staged activations is taken (stream_config in stream.cuh).
 
 // Sigmoid gate and per-token quantization of one row by a warp-group (H = 128 t + 1024 j pieces as in
 // norm_quant_row; H <= 4096).
@@ -61,10 +62,10 @@ __device__ __forceinline__ void gate_quant_row(const uint16_t* __restrict__ x, c
     wg_sync(wg);
 }
 
-template <int MT>
-__global__ void __launch_bounds__(kRlThreads, 1) rowlin_kernel(const Program P, const RowLinArgs A, const MlpShape Z) {
+template <int MT, int CW, int PW>
+__global__ void __launch_bounds__((CW + PW) * 32, 1) rowlin_kernel(const Program P, const RowLinArgs A, const MlpShape Z) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ float red[3][16];
+    __shared__ float red[CW / 4][16];
     __shared__ int flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int M = P.M, S = Z.S, K = P.ph[0].K;
@@ -84,17 +85,17 @@ __global__ void __launch_bounds__(kRlThreads, 1) rowlin_kernel(const Program P, 
     __syncthreads();
     trace_stamp(0);
     pdl_launch_dependents();
-    if (warp >= kRlCW) {
-        produce_all<FMT_GPTQ, LAYOUT_TILED, kRlPW>(P, ring, full, empty, S, warp - kRlCW, lane);
+    if (warp >= CW) {
+        produce_all<FMT_GPTQ, LAYOUT_TILED, PW>(P, ring, full, empty, S, warp - CW, lane);
         return;
     }
-    constexpr int NT = kRlCW * 32;
+    constexpr int NT = CW * 32, NWG = CW / 4;  // whole warp-groups do the row phases
     pdl_wait();
     unsigned epoch = 0;
     bool ok = true;
     {
         const int wg = threadIdx.x >> 7, tig = threadIdx.x & 127;
-        for (int m = wg * int(gridDim.x) + int(blockIdx.x); m < M; m += 3 * int(gridDim.x)) {
+        for (int m = wg * int(gridDim.x) + int(blockIdx.x); wg < NWG && m < M; m += NWG * int(gridDim.x)) {
             const uint16_t* xr = A.x + size_t(m) * K;
             if (A.mode == ROWLIN_GATE)
                 gate_quant_row(xr, A.gate + size_t(m) * A.gate_row_stride, A.gate_head_stride, A.lut, K, A.q + size_t(m) * K,
@@ -111,13 +112,13 @@ __global__ void __launch_bounds__(kRlThreads, 1) rowlin_kernel(const Program P, 
     const PhaseDesc& ph = P.ph[0];
     XSrc xs{ph.x, K, false, true};
     if (ph.xsmem) {
-        stage_x_consumers<kRlCW>(ph.x, M, K, true, xsm);
+        stage_x_consumers<CW>(ph.x, M, K, true, xsm);
         xs = XSrc{xsm, K + 16, true, true};
     }
     trace_stamp(3);
     const int C = phase_chunks(ph), ntl = cta_tiles(ph);
-    ok = consume_phase<FMT_GPTQ, LAYOUT_TILED, MT, kRlCW>(P, 0, xs, ring, full, empty, S, part, warp, lane) && ok;
-    ok = consumer_sync_and<kRlCW>(ok);
+    ok = consume_phase<FMT_GPTQ, LAYOUT_TILED, MT, CW>(P, 0, xs, ring, full, empty, S, part, warp, lane) && ok;
+    ok = consumer_sync_and<CW>(ok);
     for (int e = threadIdx.x; e < ntl * M * 16 && ok; e += NT) {
         const int k = e / (M * 16), r = e - k * (M * 16), m = r >> 4, nl = r & 15;
         const int n = (int(blockIdx.x) + k * int(gridDim.x)) * 16 + nl;  // concatenated output column
@@ -133,9 +134,9 @@ __global__ void __launch_bounds__(kRlThreads, 1) rowlin_kernel(const Program P, 
 
 size_t rowlin_workspace_bytes(int K) { return (16 * size_t(K) + 255) / 256 * 256 + 3 * 256; }
 
-template <int MT>
+template <int MT, int CW, int PW>
 static int launch_rowlin_t(const Program& P, const RowLinArgs& A, const MlpShape& Z, size_t smem, cudaStream_t stream) {
-    auto kern = rowlin_kernel<MT>;
+    auto kern = rowlin_kernel<MT, CW, PW>;
     static std::mutex mu;
     static size_t opt_in = 0;
     static int per_sm = 0;
@@ -144,7 +145,7 @@ static int launch_rowlin_t(const Program& P, const RowLinArgs& A, const MlpShape
         if (smem > opt_in) {
             CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
             opt_in = smem;
-            CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kRlThreads, smem));
+            CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, (CW + PW) * 32, smem));
         }
     }
     if (per_sm < 1) return fail(MONO_EINVAL, "rowlin: one CTA does not fit an SM (%zu B shared)", smem);
@@ -152,7 +153,7 @@ static int launch_rowlin_t(const Program& P, const RowLinArgs& A, const MlpShape
     const int grid = tiles < sm_count() ? tiles : sm_count();
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kRlThreads);
+    cfg.blockDim = dim3((CW + PW) * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
@@ -174,10 +175,23 @@ int launch_rowlin(Program& P, RowLinArgs& A, cudaStream_t stream) {
     for (int staged = 1; staged >= 0; --staged) {
         P.ph[0].xsmem = staged;
         const size_t xb = staged ? size_t(M) * (P.ph[0].K + 16) : 0;
-        const StreamPlan plan(stage_bytes<FMT_GPTQ>(), kRlCW, part, xb, 0);
-        if (plan.total > 227 * 1024 - 512) continue;
-        const MlpShape Z{kRlCW, int(part), int(xb)};
-        return MT == 2 ? launch_rowlin_t<2>(P, A, Z, plan.total, stream) : launch_rowlin_t<1>(P, A, Z, plan.total, stream);
+        for (int c = 0; c < kStreamConfigs; ++c) {
+            const StreamConfig sc = kStreamConfig[c];
+            const StreamPlan plan(stage_bytes<FMT_GPTQ>(), sc.S, part, xb, 0);
+            if (plan.total > kStreamSmemLimit) continue;
+            const MlpShape Z{sc.S, int(part), int(xb)};
+#define MONO_RL(MTV, CWV, PWV) return launch_rowlin_t<MTV, CWV, PWV>(P, A, Z, plan.total, stream)
+            if (MT == 1) {
+                if (c == 0) MONO_RL(1, 10, 2);
+                if (c == 1) MONO_RL(1, 8, 4);
+                MONO_RL(1, 12, 4);
+            } else {
+                if (c == 0) MONO_RL(2, 10, 2);
+                if (c == 1) MONO_RL(2, 8, 4);
+                MONO_RL(2, 12, 4);
+            }
+#undef MONO_RL
+        }
     }
     return fail(MONO_EINVAL, "rowlin: no shared-memory plan fits (M=%d K=%d)", M, P.ph[0].K);
 }

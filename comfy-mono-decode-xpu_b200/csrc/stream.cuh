@@ -28,6 +28,15 @@ namespace mono {
 
 constexpr int kConsumerBar = 15;  // named barrier of the consumer warps
 
+// Warp configurations of the cooperative stream kernels, deepest ring first: the launchers take the first whose
+// ring fits next to the partials and the staged activations. S is a multiple of CW and PW.
+struct StreamConfig {
+    int CW, PW, S;
+};
+constexpr int kStreamConfigs = 3;
+constexpr StreamConfig kStreamConfig[kStreamConfigs] = {{10, 2, 20}, {8, 4, 16}, {12, 4, 12}};
+constexpr size_t kStreamSmemLimit = 227 * 1024 - 512;  // dynamic bytes, leaving room for the static ones
+
 // Barrier of the CW consumer warps (the producer warp is warp CW, the last one).
 template <int CW>
 __device__ __forceinline__ void consumer_sync() {
@@ -185,16 +194,19 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Consumer side: the items of phase ph that consumer warp `cw` (of CW) computes, each partial stored at
-// part[(k * subs + sub) * C + chunk]. S must be a multiple of CW. Returns false if a wait gave up.
+// Consumer side: the items [first, first + count) of phase ph (count < 0: to the end of the phase) that consumer
+// warp `cw` (of CW) computes, each partial stored at part[item - first] (item = (k * subs + sub) * C + chunk).
+// S must be a multiple of CW. Returns false if a wait gave up.
 template <int FMT, int LAYOUT, int MT, int CW>
 __device__ __forceinline__ bool consume_phase(const Program& P, int ph, const XSrc& xs, uint8_t* ring, uint64_t* full,
-                                              uint64_t* empty, int S, uint32_t* part, int cw, int lane) {
-    const int base = cta_base(P, ph), n = cta_items(P.ph[ph]), C = P.ph[ph].K >> 10;
+                                              uint64_t* empty, int S, uint32_t* part, int cw, int lane, int first = 0,
+                                              int count = -1) {
+    const int base0 = cta_base(P, ph), nph = cta_items(P.ph[ph]), C = P.ph[ph].K >> 10;
+    const int base = base0 + first, n = count < 0 || first + count > nph ? nph - first : count;
     bool ok = true;
     int i = base + ((cw - base % CW) + CW) % CW;
     for (; i < base + n && ok; i += CW) {
-        const int s = i % S, li = i - base;
+        const int s = i % S, li = i - base0;
         ok = mbar_wait(&full[s], (i / S) & 1);
         if (!ok) break;
         uint32_t R[MT][4];
@@ -207,7 +219,7 @@ __device__ __forceinline__ bool consume_phase(const Program& P, int ph, const XS
             compute_item<FMT, LAYOUT, MT, 0>(stage, P.pair_tab, xs, P.M, li % C, lane, R);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
-        store_partial<MT>(part, li, lane, R);
+        store_partial<MT>(part, li - first, lane, R);
     }
     return ok;
 }

@@ -16,7 +16,8 @@ comfy_mono_decode_xpu/mtp_loop.py):
 Per layer: full attention = rowlin(norm -> q|k|v) -> qk_norm_rope_kv -> tree attention -> rowlin(gate -> o_proj +
 residual) -> fused MLP; GDN = rowlin(norm -> qkv|z, xn) -> a|b (bf16 GEMM of xn) -> deferred GDN step ->
 rowlin(quant -> out_proj + residual) -> fused MLP. The verify rows form a chain (the GDN step's verify rows run as a
-chain); the bf16 MTP head and the two lm_heads run as cuBLAS GEMMs through torch; their norms and gates are the row kernels
+chain); the bf16 MTP head and the verify's lm_head run as cuBLAS GEMMs through torch; the drafts' lm_head is a W4A8 GPTQ copy on this build's
+linear kernel; the head's norms and gates are the row kernels
 (mono_rmsnorm_add, mono_lut_mul).
 """
 from __future__ import annotations
@@ -61,6 +62,17 @@ def _w4(N, K, g, dev):
     return t
 
 
+def quantize_gptq(w, group=128):
+    """Round-to-nearest GPTQ-format copy of a bf16 [N, K] weight: fp16 scale per (row, 128-group) = amax / 7,
+    int4 v = clamp(rint(w / s), -8, 7) stored as nibble v + 8 (low nibble = even k). Returns the TILED copy."""
+    N, K = w.shape
+    wf = w.float().view(N, K // group, group)
+    s = (wf.abs().amax(-1) / 7).clamp(min=1e-8).half()
+    v = torch.clamp(torch.round(wf / s.float()[..., None]), -8, 7).to(torch.int32).view(N, K) + 8
+    packed = (v[:, 0::2] | (v[:, 1::2] << 4)).to(torch.uint8).contiguous()
+    return _C.w4_repack(0, packed, s.contiguous(), N, K)
+
+
 def _bf(shape, g, dev, std=0.02, mean=0.0):
     return (torch.randn(*shape, device=dev, generator=g) * std + mean).to(torch.bfloat16)
 
@@ -90,6 +102,10 @@ class Qwen35W4A8:
         self.cap = ((prompt_len + gen_tokens + 64) + 63) // 64 * 64
         self.embed = _bf((c.vocab, H), g, dev)
         self.lm_head = _bf((c.vocab, H), g, dev)
+        # the drafts' lm_head: a W4A8 GPTQ copy of the bf16 one (4x fewer bytes per draft). Only drafts use it;
+        # the verify's bf16 lm_head decides every output token (the reference drafts with an INT8 ConvRot copy,
+        # comfy_mono_decode_xpu/draft_lmhead.py).
+        self.lm_head_w4 = quantize_gptq(self.lm_head)
         self.final_norm = _bf((H,), g, dev, 0.02, 1.0)
         self.layers = []
         Ck = 2 * c.gdn_k_heads * c.gdn_dim + c.gdn_v_heads * c.gdn_dim
@@ -223,7 +239,7 @@ class Qwen35W4A8:
         gu = F.linear(xn, m["gate_up"])
         h = _C.lut_mul(gu[:, c.inter:], gu[:, :c.inter], self.silu_lut)
         xf, x = _C.rmsnorm_add(x, m["norm"], c.eps, add=F.linear(h, m["down"]))
-        logits = F.linear(xf, self.lm_head)
+        logits = _C.w4a8_gptq_linear_bf16(xf, self.lm_head_w4, None, tiled=True, N=c.vocab)
         _, t = _C.fast_topk(logits, 1, True)
         return t.view(1, 1), x.view(1, 1, -1)
 
@@ -250,7 +266,7 @@ class Qwen35W4A8:
         n_attn = sum(1 for i in range(c.layers) if c.is_attn(i))
         n_gdn = c.layers - n_attn
         body = c.layers * 3 + n_gdn * 2 + n_attn * 3          # rowlin x2 + MLP; GDN conv + delta; rope + attention x2
-        draft = c.depth * (1 + 3 + 1 + 2 + 2 + 2 + 2)       # prep, norms, rope, attention, lut x2, norm-adds, argmax
+        draft = c.depth * (1 + 3 + 1 + 2 + 2 + 2 + 1 + 2)   # prep, norms, rope, attention, lut x2, norm-adds, lm_head, argmax
         return body + draft + 1 + 2 + 1 + 1                   # prep_verify, final norm + argmax, accept, verify norm
 
     def step_bytes(self) -> int:
@@ -264,6 +280,7 @@ class Qwen35W4A8:
                     if k in L)
         state = sum(L["state"].numel() * 4 * 2 for L in self.layers if "state" in L)
         lm = self.lm_head.numel() * 2
+        lm4 = self.lm_head_w4.numel()
         mtp = sum(t.numel() * t.element_size() for k, t in self.mtp.items() if k not in ("kc", "vc"))
         kv = int(self.st[0].item()) * c.kv_heads * c.head_dim * 2 * 2 * sum(1 for L in self.layers if "kc" in L)
-        return body + small + state + lm * (1 + c.depth) + mtp * c.depth + kv
+        return body + small + state + lm + lm4 * c.depth + mtp * c.depth + kv

@@ -35,7 +35,7 @@ def test_gptq_linear_bit_exact(cuda, N, K, tiled):
         assert bits_equal(bf16_bits(out), ref), (M, N, K, tiled)
 
 
-@pytest.mark.parametrize("N,K", [(12288, 4096), (4096, 12288), (1024, 4096), (48, 3072)])
+@pytest.mark.parametrize("N,K", [(12288, 4096), (4096, 12288), (1024, 4096), (48, 3072), (16 * 148 * 10 + 48, 4096)])
 @pytest.mark.parametrize("tiled", [False, True])
 def test_gptq_linear_bf16_fused_quant(cuda, N, K, tiled):
     """bf16 x with the per-token quantization inside the kernel == act_quant then the int8 linear (oracle),
