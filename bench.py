@@ -1,13 +1,16 @@
 """Benchmark of the W4A8 decode step on B200 (driver contract: one JSON line from rank 0).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload gemv]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload decode|gemv|mlp]
 
-Workload `gemv` (the W4A8 GEMV HBM GB/s part of the metric): one step is a batch
-of 64 verify-row linears (M = 8 tree rows, bf16 x [8, 4096] -> per-token int8 quant -> GPTQ W4A8 GEMV
-4096 -> 12288 -> bf16 [8, 12288]) that cycle through 8 distinct weight copies (208 MB, more than the 126 MB
-L2, so every linear streams its weights from HBM). value = algorithmic bytes / device time (CUDA graph
-replay of the K steps, CUDA events, max over ranks). e2e = the same through the public op calls
-(mono_b200._C) with pinned host inputs copied in and outputs read back every linear.
+Workload `decode` (default; BASELINE.json configs[4], the headline "decode tok/s"): the synthetic
+Qwen3.5-9B-shaped W4A8 model (random-init weights, mono_b200.decoder) decoding with the device-side MTP loop
+(depth-4 chain draft, 5 verify rows, greedy accept), one stream per GPU; value = committed tokens / device
+time of K steps (two CUDA graphs replayed back to back, CUDA events, max over ranks); roofline of the step's
+dominant kernel (the fused MLP) timed alone; e2e reads every step's result row back to the host.
+
+Workload `gemv` (configs[0], the "W4A8 GEMV HBM GB/s" part): 64 verify-row linears per step (M = 8, bf16 x
+[8, 4096] -> act quant -> GPTQ W4A8 GEMV 4096 -> 12288) over 8 weight copies (208 MB > L2). Workload `mlp`
+(configs[1]): the fused MLP block over 4 weight copies (312 MB > L2).
 
 Multi-GPU: every rank runs its own replica (independent decode streams, no collective): scaling "weak".
 --impl reference: the reference's arithmetic on the host cores (the CPU oracle restatement; the reference
@@ -413,6 +416,20 @@ def run_mlp(args):
         dist.destroy_process_group()
 
 
+def reduce_time_and_count(ms, count, device, world):
+    """Max of the device time and sum of the counted units over the ranks (every rank calls it, in the same
+    order); identity on one rank."""
+    if world <= 1:
+        return ms, count
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    c = torch.tensor([count], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.all_reduce(c, op=dist.ReduceOp.SUM)
+    return float(t.item()), int(c.item())
+
+
 def run_decode(args):
     """Config 4: the synthetic Qwen3.5-9B-shaped W4A8 decoder with the device MTP loop (depth-4 chain draft,
     5 verify rows, greedy accept), one stream per GPU. Steps are captured in two CUDA graphs (the GDN replay
@@ -458,14 +475,7 @@ def run_decode(args):
                 graphs[i % 2].replay()
             e1.record(stream)
         stream.synchronize()
-    ms = e0.elapsed_time(e1)
-    toks = int(model.total.item()) - n0
-    if world > 1:
-        t = torch.tensor([ms, float(toks)], device=dev)
-        dist.all_reduce(t[:1], op=dist.ReduceOp.MAX)
-        tt = t[1:].clone()
-        dist.all_reduce(tt, op=dist.ReduceOp.SUM)
-        ms, toks = float(t[0].item()), int(tt.item())
+    ms, toks = reduce_time_and_count(e0.elapsed_time(e1), int(model.total.item()) - n0, dev, world)
     step_ms = ms / args.steps
     step_bytes = model.step_bytes()
     hbm, src = peaks()
@@ -482,14 +492,7 @@ def run_decode(args):
             host_res.copy_(model.result, non_blocking=True)
         f1.record(stream)
     stream.synchronize()
-    e2e_ms = f0.elapsed_time(f1)
-    e2e_toks = int(model.total.item()) - m0
-    if world > 1:
-        t = torch.tensor([e2e_ms, float(e2e_toks)], device=dev)
-        dist.all_reduce(t[:1], op=dist.ReduceOp.MAX)
-        tt = t[1:].clone()
-        dist.all_reduce(tt, op=dist.ReduceOp.SUM)
-        e2e_ms, e2e_toks = float(t[0].item()), int(tt.item())
+    e2e_ms, e2e_toks = reduce_time_and_count(f0.elapsed_time(f1), int(model.total.item()) - m0, dev, world)
     # the dominant kernel alone (the fused MLP block, 19 % of the step): a graph of its launches over the layers'
     # weights at the step's 5 verify rows, averaged per launch with CUDA events
     import mono_b200._C as C_
@@ -537,7 +540,7 @@ def run_decode(args):
                          "us_per_launch": round(mlp_us, 3), "algorithmic_bytes_per_launch": mlp_b},
             "step_roofline": {"achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                               "algorithmic_bytes_per_step": step_bytes,
-                              "what": "whole step: W4 body + bf16 lm_head x 5 + MTP block x 4 + GDN states + KV"},
+                              "what": "whole step: W4 body + bf16 lm_head (verify) + W4 lm_head x 4 and MTP block x 4 (drafts) + GDN states + KV"},
             "e2e": {"value": round(e2e_toks / (e2e_ms * 1e-3), 2), "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 32 * 8},
             "gpu_launches": args.steps * model.own_launches_per_step(), "clocks": clk.summary()}
@@ -595,10 +598,60 @@ def cpu_baseline(ow, packed, scales, rows=None):
                                       f"median of 3 ({t:.2f} s)"}
 
 
+def run_reference_decode(args):
+    """The reference arm of the decode workload: the reference's eager chain for the W4A8 layers (act quant +
+    GPTQ linear, the oracle port) on the host cores. Each step is a bounded sample: 1/256 of the output rows of
+    every W4A8 projection of one GDN layer (qkv|z, out, gate, up, down) over the 5 verify rows; the step time of
+    the whole model is the sample time x 256 x 32 layers (lm_head, attention, GDN recurrence and the MTP head not
+    counted: a lower bound on the CPU's step time, so an upper bound on its tok/s at one token per step)."""
+    import numpy as np
+    import torch
+
+    from oracle import w4a8 as ow
+    torch.set_num_threads(os.cpu_count() or 1)
+    M, H, I = 5, 4096, 12288
+    mats = [(8192 + 4096, H), (H, 4096), (I, H), (I, H), (H, I)]
+    rng = np.random.default_rng(0)
+    samples = []
+    for N, K in mats:
+        n = N // 256
+        packed, scales = ow.gen_gptq(n, K, seed=0x5EED + N + K)
+        x = torch.randn(M, K).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+        samples.append((packed, scales, x))
+
+    def step():
+        for packed, scales, x in samples:
+            q, s_ = ow.act_quant(x)
+            ow.gptq_linear(q, s_, packed, scales)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    t = (time.perf_counter() - t0) / args.steps
+    step_s = t * 256 * 32
+    value = 1.0 / step_s
+    cores = torch.get_num_threads()
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "tok/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (seeded, BASELINE configs[4] shapes)",
+            "config": {"workload": "Qwen3.5-9B-shaped W4A8 MTP decode (configs[4]): the W4A8 layers of the eager "
+                                   "chain on the host cores, one token per step"},
+            "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": cores, "kind": "port",
+                             "sample": f"per step 1/256 of the output rows of one GDN layer's 5 W4A8 projections over "
+                                       f"5 verify rows ({t * 1e3:.1f} ms), scaled x 256 x 32 layers"},
+            "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args):
     rank, world, _ = dist_setup(args.gpus)
     if rank != 0:
         return
+    if args.workload == "decode":
+        return run_reference_decode(args)
     from oracle import w4a8 as ow
     packed, scales = ow.gen_gptq(N_OUT, K_IN, seed=0x5EED)
     rows = 1024
@@ -633,14 +686,16 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=None, help="default: 200 (decode), 2000 (gemv, mlp)")
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="gemv", choices=["gemv", "mlp", "decode"])
+    ap.add_argument("--workload", default="decode", choices=["gemv", "mlp", "decode"])
     ap.add_argument("--prompt", type=int, default=1024, help="decode: committed prompt length (KV prefix)")
     ap.add_argument("--rows", type=int, default=8, help="activation rows (tree-verify rows)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 200 if args.workload == "decode" else 2000
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
