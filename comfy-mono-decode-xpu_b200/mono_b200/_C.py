@@ -8,6 +8,7 @@ before anything is launched, as the reference's TORCH_CHECKs do.
 from __future__ import annotations
 
 import threading
+import weakref
 
 import torch
 
@@ -39,11 +40,18 @@ def _p(t):
 
 
 def pair_table(codebook, device):
-    """REF decode table for `codebook` (None = float(i - 8)), cached per (device, storage, version)."""
+    """REF decode table for `codebook` (None = float(i - 8)), cached per (device, codebook tensor, version).
+    The entry holds a weak reference to the codebook: a new tensor that reuses a freed codebook's address
+    (same data_ptr, version 0) gets its own table."""
     dev = torch.device(device)
-    key = (dev, None) if codebook is None else (dev, codebook.data_ptr(), codebook._version)
+    key = (dev, None) if codebook is None else (dev, codebook.data_ptr())
     with _tables_lock:
-        tab = _tables.get(key)
+        hit = _tables.get(key)
+    tab = None
+    if hit is not None:
+        ref, version, cached = hit
+        if codebook is None or (ref() is codebook and version == codebook._version):
+            tab = cached
     if tab is None:
         if codebook is not None:
             _check(codebook.dtype == torch.float32 and codebook.numel() == 16 and codebook.is_contiguous(),
@@ -53,7 +61,8 @@ def pair_table(codebook, device):
         with torch.cuda.device(dev):
             _lib.call("mono_w4_pair_table", _p(codebook), tab.data_ptr(), _stream(dev))
         with _tables_lock:
-            _tables[key] = tab
+            _tables[key] = (None if codebook is None else weakref.ref(codebook),
+                            None if codebook is None else codebook._version, tab)
     return tab
 
 
