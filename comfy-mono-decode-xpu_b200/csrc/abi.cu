@@ -48,6 +48,55 @@ static int check_linear_common(const int8_t* x, const float* xs, const void* pac
     return MONO_OK;
 }
 
+int fill_gdn_args(GdnArgs& A, const void* qkv, const void* z, const void* a, const void* b, const void* conv_w,
+                         void* conv_state, const float* dt_bias, const float* g_decay, float* state, const void* gnorm_w,
+                         float gnorm_eps, float qscale, int64_t M, int64_t HK, int64_t HV, void* core, void* workspace,
+                         size_t workspace_bytes, const int32_t* ctl, const void* prev_qkv, const void* prev_a,
+                         const void* prev_b, void* save_qkv, void* save_a, void* save_b, int64_t qkv_stride,
+                         int64_t z_stride, int64_t ab_stride) {
+    MONO_CHECK(qkv && z && a && b && conv_w && conv_state && dt_bias && g_decay && state && gnorm_w && core && workspace,
+               "null operand");
+    MONO_CHECK(M >= 1 && M <= 8, "1 <= M <= 8 rows (got %lld)", (long long)M);
+    MONO_CHECK(HK >= 1 && HV >= HK && HV % HK == 0 && HV <= 1024, "value heads a multiple of key heads");
+    MONO_CHECK(gnorm_eps > 0.f, "positive eps");
+    const int64_t C = (2 * HK + HV) * 128;
+    MONO_CHECK(workspace_bytes >= mono_gdn_step_workspace(M, C, HV), "workspace too small (mono_gdn_step_workspace)");
+    MONO_CHECK(aligned(workspace, 256) && aligned(state, 16), "aligned workspace / state");
+    A = GdnArgs{};
+    A.qkv = static_cast<const uint16_t*>(qkv);
+    A.z = static_cast<const uint16_t*>(z);
+    A.a = static_cast<const uint16_t*>(a);
+    A.b = static_cast<const uint16_t*>(b);
+    A.conv_w = static_cast<const uint16_t*>(conv_w);
+    A.conv_state = static_cast<uint16_t*>(conv_state);
+    A.dt_bias = dt_bias;
+    A.g_decay = g_decay;
+    A.state = state;
+    A.gnorm_w = static_cast<const uint16_t*>(gnorm_w);
+    A.gnorm_eps = gnorm_eps;
+    A.qscale = qscale;
+    A.core = static_cast<uint16_t*>(core);
+    MONO_CHECK(qkv_stride >= C && z_stride >= HV * 128 && ab_stride >= HV, "row strides cover the rows");
+    A.qkv_stride = qkv_stride;
+    A.z_stride = z_stride;
+    A.ab_stride = ab_stride;
+    A.ctl = ctl;
+    A.prev_qkv = static_cast<const uint16_t*>(prev_qkv);
+    A.prev_a = static_cast<const uint16_t*>(prev_a);
+    A.prev_b = static_cast<const uint16_t*>(prev_b);
+    A.save_qkv = static_cast<uint16_t*>(save_qkv);
+    A.save_a = static_cast<uint16_t*>(save_a);
+    A.save_b = static_cast<uint16_t*>(save_b);
+    A.M = int(M);
+    A.C = int(C);
+    A.HK = int(HK);
+    A.HV = int(HV);
+    const size_t rows = size_t(M) + 8;
+    A.conv_out = static_cast<uint16_t*>(workspace);
+    A.gates = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + (rows * C * 2 + 255) / 256 * 256);
+    return MONO_OK;
+}
+
 }  // namespace mono
 
 using namespace mono;
@@ -317,43 +366,11 @@ static int gdn_step_impl(const void* qkv, const void* z, const void* a, const vo
                          size_t workspace_bytes, const int32_t* ctl, const void* prev_qkv, const void* prev_a,
                          const void* prev_b, void* save_qkv, void* save_a, void* save_b, int64_t qkv_stride,
                          int64_t z_stride, int64_t ab_stride, mono_stream_t stream) {
-    MONO_CHECK(qkv && z && a && b && conv_w && conv_state && dt_bias && g_decay && state && gnorm_w && core && workspace,
-               "null operand");
-    MONO_CHECK(M >= 1 && M <= 8, "1 <= M <= 8 rows (got %lld)", (long long)M);
-    MONO_CHECK(HK >= 1 && HV >= HK && HV % HK == 0 && HV <= 1024, "value heads a multiple of key heads");
-    MONO_CHECK(gnorm_eps > 0.f, "positive eps");
-    const int64_t C = (2 * HK + HV) * 128;
-    MONO_CHECK(workspace_bytes >= mono_gdn_step_workspace(M, C, HV), "workspace too small (mono_gdn_step_workspace)");
-    MONO_CHECK(aligned(workspace, 256) && aligned(state, 16), "aligned workspace / state");
-    GdnArgs A{};
-    A.qkv = static_cast<const uint16_t*>(qkv);
-    A.z = static_cast<const uint16_t*>(z);
-    A.a = static_cast<const uint16_t*>(a);
-    A.b = static_cast<const uint16_t*>(b);
-    A.conv_w = static_cast<const uint16_t*>(conv_w);
-    A.conv_state = static_cast<uint16_t*>(conv_state);
-    A.dt_bias = dt_bias;
-    A.g_decay = g_decay;
-    A.state = state;
-    A.gnorm_w = static_cast<const uint16_t*>(gnorm_w);
-    A.gnorm_eps = gnorm_eps;
-    A.qscale = qscale;
-    A.core = static_cast<uint16_t*>(core);
-    MONO_CHECK(qkv_stride >= C && z_stride >= HV * 128 && ab_stride >= HV, "row strides cover the rows");
-    A.qkv_stride = qkv_stride;
-    A.z_stride = z_stride;
-    A.ab_stride = ab_stride;
-    A.ctl = ctl;
-    A.prev_qkv = static_cast<const uint16_t*>(prev_qkv);
-    A.prev_a = static_cast<const uint16_t*>(prev_a);
-    A.prev_b = static_cast<const uint16_t*>(prev_b);
-    A.save_qkv = static_cast<uint16_t*>(save_qkv);
-    A.save_a = static_cast<uint16_t*>(save_a);
-    A.save_b = static_cast<uint16_t*>(save_b);
-    A.M = int(M);
-    A.C = int(C);
-    A.HK = int(HK);
-    A.HV = int(HV);
+    GdnArgs A;
+    const int rc = fill_gdn_args(A, qkv, z, a, b, conv_w, conv_state, dt_bias, g_decay, state, gnorm_w, gnorm_eps, qscale,
+                                 M, HK, HV, core, workspace, workspace_bytes, ctl, prev_qkv, prev_a, prev_b, save_qkv,
+                                 save_a, save_b, qkv_stride, z_stride, ab_stride);
+    if (rc != MONO_OK) return rc;
     return launch_gdn_step(A, workspace, reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -309,12 +309,14 @@ struct XSrc {
     const int8_t* p;
     int pitch;
     bool smem, perm;
+    bool cg = false;  // global rows written earlier in the same launch: read through L2 only (ld.global.cg)
 };
 
 // Consume one item (8 groups). R = the chunk partial per fragment element: fp32 bits (GPTQ, carrying a
 // factor 16, see below) or the int32 dot (REF). Fragment element i of m-tile mt: (row g + 8 (i >> 1),
 // activation 2t + (i & 1)).
-// XMODE: 0 = global, natural byte order; 1 = global, permuted; 2 = shared (pitch K + 16), permuted.
+// XMODE: 0 = global, natural byte order; 1 = global, permuted; 2 = shared (pitch K + 16), permuted;
+// 3 = global, permuted, read through L2 only (rows written by other CTAs of the same launch).
 template <int FMT, int LAYOUT, int MT, int XMODE>
 __device__ __forceinline__ void compute_item(const uint8_t* __restrict__ stage, const uint16_t* __restrict__ pair_tab,
                                              const XSrc& xs, int M, int chunk, int lane, uint32_t (&R)[MT][4]) {
@@ -347,6 +349,9 @@ __device__ __forceinline__ void compute_item(const uint8_t* __restrict__ stage, 
                 if (XMODE == 2) {
                     xv[mt][0] = lds_v4(xr);
                     xv[mt][1] = lds_v4(xr + 16);
+                } else if (XMODE == 3) {
+                    xv[mt][0] = __ldcg(reinterpret_cast<const uint4*>(xr));
+                    xv[mt][1] = __ldcg(reinterpret_cast<const uint4*>(xr + 16));
                 } else {
                     xv[mt][0] = __ldg(reinterpret_cast<const uint4*>(xr));
                     xv[mt][1] = __ldg(reinterpret_cast<const uint4*>(xr + 16));

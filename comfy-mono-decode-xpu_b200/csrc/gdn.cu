@@ -20,74 +20,12 @@
 // results are checked against an fp64 reference with a stated tolerance.
 #include <cmath>
 
-#include "launch.h"
+#include "gdn.cuh"
 
 namespace mono {
 
-constexpr int kDH = 128, kRG = 4, kRPG = kDH / kRG, kGdnMaxRows = 8, kGdnMaxAll = 2 * kGdnMaxRows;
-
-__device__ __forceinline__ int gdn_pending(const GdnArgs& A) {
-    if (A.ctl == nullptr) return 0;
-    const int n = A.ctl[0];
-    return n < 0 ? 0 : (n > kGdnMaxRows ? kGdnMaxRows : n);
-}
-__device__ __forceinline__ int gdn_slot(const GdnArgs& A, int i) {
-    const int s = A.ctl[2 + i];
-    return s < 0 ? 0 : (s >= kGdnMaxRows ? kGdnMaxRows - 1 : s);
-}
-
 __global__ void __launch_bounds__(256) gdn_conv_kernel(const GdnArgs A) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    const int n = gdn_pending(A), R = n + A.M;
-    if (i < R * A.HV) {  // gates of every row (replayed rows: from the saved a / b)
-        const int t = i / A.HV, h = i % A.HV;
-        const uint16_t ab = t < n ? A.prev_a[size_t(gdn_slot(A, t)) * A.HV + h] : A.a[size_t(t - n) * A.ab_stride + h];
-        const uint16_t bb = t < n ? A.prev_b[size_t(gdn_slot(A, t)) * A.HV + h] : A.b[size_t(t - n) * A.ab_stride + h];
-        const float av = bf16_bits_to_f32(ab) + A.dt_bias[h];
-        const float sp = av > 20.f ? av : logf(1.f + expf(av));
-        A.gates[i * 2] = expf(A.g_decay[h] * sp);
-        A.gates[i * 2 + 1] = bf16_round(1.f / (1.f + expf(-bf16_bits_to_f32(bb))));
-    }
-    if (A.save_a != nullptr && i < A.M * A.HV) {
-        const int t = i / A.HV, h = i % A.HV;
-        A.save_a[i] = A.a[size_t(t) * A.ab_stride + h];
-        A.save_b[i] = A.b[size_t(t) * A.ab_stride + h];
-    }
-    if (i >= A.C) return;
-    float w[4], hist[3 + kGdnMaxAll];
-#pragma unroll
-    for (int d = 0; d < 4; ++d) w[d] = bf16_bits_to_f32(A.conv_w[size_t(i) * 4 + d]);
-#pragma unroll
-    for (int r = 0; r < 3; ++r) hist[r] = bf16_bits_to_f32(A.conv_state[size_t(i) * 3 + r]);
-#pragma unroll
-    for (int t = 0; t < kGdnMaxAll; ++t) {
-        if (t < n) hist[3 + t] = bf16_bits_to_f32(A.prev_qkv[size_t(gdn_slot(A, t)) * A.C + i]);
-        else if (t < R) {
-            const uint16_t v = A.qkv[size_t(t - n) * A.qkv_stride + i];
-            hist[3 + t] = bf16_bits_to_f32(v);
-            if (A.save_qkv != nullptr) A.save_qkv[size_t(t - n) * A.C + i] = v;
-        }
-    }
-#pragma unroll
-    for (int t = 0; t < kGdnMaxAll; ++t) {
-        if (t >= R) break;
-        float sum = 0.f;
-#pragma unroll
-        for (int d = 0; d < 4; ++d) sum = fmaf(hist[3 + t - d], w[3 - d], sum);
-        const float y = bf16_round(sum);
-        A.conv_out[size_t(t) * A.C + i] = f32_to_bf16_bits(y / (1.f + expf(-y)));
-    }
-    // the state becomes the three newest committed inputs (oldest first): the replayed rows in the deferred
-    // form, all rows in the committing form
-    const int keep = A.ctl != nullptr ? n : R;
-#pragma unroll
-    for (int r = 0; r < 3; ++r) {
-        float v = hist[r];
-#pragma unroll
-        for (int t = 0; t < kGdnMaxAll + 3; ++t)
-            if (t == keep + r) v = hist[t];
-        A.conv_state[size_t(i) * 3 + r] = f32_to_bf16_bits(v);
-    }
+    gdn_conv_item(A, blockIdx.x * blockDim.x + threadIdx.x);
 }
 
 __global__ void __launch_bounds__(kRG * kDH) gdn_delta_kernel(const GdnArgs A) {
@@ -102,21 +40,13 @@ __global__ void __launch_bounds__(kRG * kDH) gdn_delta_kernel(const GdnArgs A) {
     // sums of squares of q and k of the key head per row: (row, q or k) pairs over the 16 warps
     for (int pr = warp; pr < 2 * R; pr += 16) {
         const int t = pr >> 1, which = pr & 1;
-        const uint16_t* src = A.conv_out + size_t(t) * A.C + which * KD + kh * kDH;
-        float s = 0.f;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float v = bf16_bits_to_f32(src[lane + 32 * j]);
-            s = fmaf(v, v, s);
-        }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        const float s = gdn_sumsq128(A.conv_out + size_t(t) * A.C + which * KD + kh * kDH, lane);
         if (lane == 0) sums[pr] = s;
     }
     __syncthreads();
     for (int e = tid; e < R * kDH; e += blockDim.x) {
         const int t = e / kDH, d = e % kDH;
-        const float qi = 1.f / fmaxf(sqrtf(sums[2 * t]), 1e-12f), ki = 1.f / fmaxf(sqrtf(sums[2 * t + 1]), 1e-12f);
+        const float qi = gdn_l2_inv(sums[2 * t]), ki = gdn_l2_inv(sums[2 * t + 1]);
         qn[t][d] = (bf16_bits_to_f32(A.conv_out[size_t(t) * A.C + kh * kDH + d]) * A.qscale) * qi;
         kn[t][d] = bf16_bits_to_f32(A.conv_out[size_t(t) * A.C + KD + kh * kDH + d]) * ki;
     }
@@ -155,11 +85,11 @@ __global__ void __launch_bounds__(kRG * kDH) gdn_delta_kernel(const GdnArgs A) {
 #pragma unroll
         for (int r = 0; r < kRPG; ++r) S[size_t(r) * kDH] = st[r];
     __syncthreads();
-    // gated RMSNorm of every output row: warp w < M sums row w's squares
+    // gated RMSNorm of every output row: warp w < M sums row w's squares (order of gdn_sumsq128)
     if (warp < M) {
         float s = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) s += raw[warp][lane + 32 * j] * raw[warp][lane + 32 * j];
+        for (int j = 0; j < 4; ++j) s = fmaf(raw[warp][lane + 32 * j], raw[warp][lane + 32 * j], s);
 #pragma unroll
         for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
         if (lane == 0) sums[warp] = s;
@@ -167,12 +97,24 @@ __global__ void __launch_bounds__(kRG * kDH) gdn_delta_kernel(const GdnArgs A) {
     __syncthreads();
     for (int e = tid; e < M * kDH; e += blockDim.x) {
         const int t = e / kDH, d = e % kDH;
-        const float rs = 1.f / sqrtf(sums[t] / float(kDH) + A.gnorm_eps);
-        const float normed = bf16_round((raw[t][d] * bf16_bits_to_f32(A.gnorm_w[d])) * rs);
         const float z = bf16_bits_to_f32(A.z[size_t(t) * A.z_stride + h * kDH + d]);
-        const float gz = bf16_round(z / (1.f + expf(-z)));
-        A.core[size_t(t) * A.HV * kDH + h * kDH + d] = f32_to_bf16_bits(normed * gz);
+        A.core[size_t(t) * A.HV * kDH + h * kDH + d] =
+            gdn_core(raw[t][d], bf16_bits_to_f32(A.gnorm_w[d]), gdn_norm_inv(sums[t], A.gnorm_eps), z);
     }
+}
+
+// a | b projection: one warp per output column.
+__global__ void __launch_bounds__(128) gdn_ab_kernel(const uint16_t* x, int64_t x_stride, const uint16_t* w, int K,
+                                                      int M, int N, uint16_t* out, int64_t out_stride) {
+    const int n = blockIdx.x * 4 + (threadIdx.x >> 5);
+    if (n < N) gdn_ab_column(x, x_stride, w, K, M, out, out_stride, n, threadIdx.x & 31);
+}
+
+int launch_gdn_ab(const uint16_t* x, int64_t x_stride, const uint16_t* w, int K, int M, int N, uint16_t* out,
+                  int64_t out_stride, cudaStream_t stream) {
+    gdn_ab_kernel<<<(N + 3) / 4, 128, 0, stream>>>(x, x_stride, w, K, M, N, out, out_stride);
+    CUDA_TRY(cudaGetLastError());
+    return MONO_OK;
 }
 
 size_t gdn_workspace_bytes(int M, int C, int HV) {

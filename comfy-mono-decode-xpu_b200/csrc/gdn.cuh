@@ -1,0 +1,198 @@
+// Gated-DeltaNet pieces shared by the standalone GDN kernels (gdn.cu) and the layer programs (program.cu), so
+// both run the same floating-point operations in the same order (results agree bit for bit).
+// Reference: csrc/mono_gdn.sycl:313-611 (deferred conv, gates, sums, replay + verify delta, gated RMSNorm).
+#pragma once
+#include "launch.h"
+#include "rowops.cuh"
+
+namespace mono {
+
+constexpr int kDH = 128, kRG = 4, kRPG = kDH / kRG, kGdnMaxRows = 8, kGdnMaxAll = 2 * kGdnMaxRows;
+
+__device__ __forceinline__ int gdn_pending(const GdnArgs& A) {
+    if (A.ctl == nullptr) return 0;
+    const int n = __ldcg(A.ctl);
+    return n < 0 ? 0 : (n > kGdnMaxRows ? kGdnMaxRows : n);
+}
+__device__ __forceinline__ int gdn_slot(const GdnArgs& A, int i) {
+    const int s = __ldcg(A.ctl + 2 + i);
+    return s < 0 ? 0 : (s >= kGdnMaxRows ? kGdnMaxRows - 1 : s);
+}
+
+// Work item i of the conv step (one thread each, i < max(C, (n + M) * HV)): the gates of (row, head) i, the
+// saved a / b of this step's rows, and the depthwise causal conv of channel i over the conv state and the
+// replayed then the verify rows:
+//   gates: decay = exp(g_decay * softplus(a + dt_bias)) (softplus(v) = v above 20), beta = bf16(sigmoid(b))
+//   conv:  y = bf16(fma chain x[t] w[3], x[t-1] w[2], .. from 0), out = bf16(y / (1 + exp(-y)))
+// The conv state becomes the three newest committed inputs (the replayed rows in the deferred form, all rows
+// in the committing form). All activations are read through L2 (they may have been written by this launch).
+__device__ __forceinline__ void gdn_conv_item(const GdnArgs& A, int i) {
+    const int n = gdn_pending(A), R = n + A.M;
+    if (i < R * A.HV) {
+        const int t = i / A.HV, h = i % A.HV;
+        const uint16_t ab = t < n ? __ldcg(A.prev_a + size_t(gdn_slot(A, t)) * A.HV + h) : __ldcg(A.a + size_t(t - n) * A.ab_stride + h);
+        const uint16_t bb = t < n ? __ldcg(A.prev_b + size_t(gdn_slot(A, t)) * A.HV + h) : __ldcg(A.b + size_t(t - n) * A.ab_stride + h);
+        const float av = bf16_bits_to_f32(ab) + A.dt_bias[h];
+        const float sp = av > 20.f ? av : logf(1.f + expf(av));
+        A.gates[i * 2] = expf(A.g_decay[h] * sp);
+        A.gates[i * 2 + 1] = bf16_round(1.f / (1.f + expf(-bf16_bits_to_f32(bb))));
+    }
+    if (A.save_a != nullptr && i < A.M * A.HV) {
+        const int t = i / A.HV, h = i % A.HV;
+        A.save_a[i] = __ldcg(A.a + size_t(t) * A.ab_stride + h);
+        A.save_b[i] = __ldcg(A.b + size_t(t) * A.ab_stride + h);
+    }
+    if (i >= A.C) return;
+    float w[4], hist[3 + kGdnMaxAll];
+#pragma unroll
+    for (int d = 0; d < 4; ++d) w[d] = bf16_bits_to_f32(A.conv_w[size_t(i) * 4 + d]);
+#pragma unroll
+    for (int r = 0; r < 3; ++r) hist[r] = bf16_bits_to_f32(A.conv_state[size_t(i) * 3 + r]);
+#pragma unroll
+    for (int t = 0; t < kGdnMaxAll; ++t) {
+        if (t < n) hist[3 + t] = bf16_bits_to_f32(__ldcg(A.prev_qkv + size_t(gdn_slot(A, t)) * A.C + i));
+        else if (t < R) {
+            const uint16_t v = __ldcg(A.qkv + size_t(t - n) * A.qkv_stride + i);
+            hist[3 + t] = bf16_bits_to_f32(v);
+            if (A.save_qkv != nullptr) A.save_qkv[size_t(t - n) * A.C + i] = v;
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < kGdnMaxAll; ++t) {
+        if (t >= R) break;
+        float sum = 0.f;
+#pragma unroll
+        for (int d = 0; d < 4; ++d) sum = fmaf(hist[3 + t - d], w[3 - d], sum);
+        const float y = bf16_round(sum);
+        A.conv_out[size_t(t) * A.C + i] = f32_to_bf16_bits(y / (1.f + expf(-y)));
+    }
+    const int keep = A.ctl != nullptr ? n : R;
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+        float v = hist[r];
+#pragma unroll
+        for (int t = 0; t < kGdnMaxAll + 3; ++t)
+            if (t == keep + r) v = hist[t];
+        A.conv_state[size_t(i) * 3 + r] = f32_to_bf16_bits(v);
+    }
+}
+
+// Sum of squares of 128 bf16 values by one warp: lane l takes elements l + 32 j (j = 0..3) in order (fma chain
+// from 0), then the xor butterfly (16, 8, 4, 2, 1).
+__device__ __forceinline__ float gdn_sumsq128(const uint16_t* src, int lane) {
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float v = bf16_bits_to_f32(__ldcg(src + lane + 32 * j));
+        s = fmaf(v, v, s);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    return s;
+}
+__device__ __forceinline__ float gdn_l2_inv(float sumsq) { return 1.f / fmaxf(sqrtf(sumsq), 1e-12f); }
+
+// Gated RMSNorm of one head of a raw output row: r = 1 / sqrt(sum(raw^2) / 128 + eps) (sum as gdn_sumsq128 over
+// the bf16 raw values), core = bf16(bf16((raw * w) * r) * bf16(silu(z))).
+__device__ __forceinline__ float gdn_norm_inv(float sumsq, float eps) { return 1.f / sqrtf(sumsq / float(kDH) + eps); }
+__device__ __forceinline__ uint16_t gdn_core(float raw, float w, float r, float z) {
+    const float normed = bf16_round((raw * w) * r);
+    const float gz = bf16_round(z / (1.f + expf(-z)));
+    return f32_to_bf16_bits(normed * gz);
+}
+
+// a | b projection of one output column n (a warp): out[m][n] = bf16(sum over k of x[m][k] * w[n][k]) for the M
+// rows, fp32 with every product and sum rounded on its own (no fma): lane l takes the 8-element pieces
+// l + 32 j (j outer, element inner) from +0, then the xor butterfly (16, 8, 4, 2, 1). K % 256 == 0, M <= 16.
+// The role of the reference's in_proj_a / in_proj_b BF16 linear (csrc/mono_gdn.sycl:10-11).
+__device__ __forceinline__ void gdn_ab_column(const uint16_t* __restrict__ x, int64_t x_stride,
+                                              const uint16_t* __restrict__ w, int K, int M, uint16_t* out,
+                                              int64_t out_stride, int n, int lane) {
+    float acc[16];
+#pragma unroll
+    for (int m = 0; m < 16; ++m) acc[m] = 0.f;
+    const uint4* wr = reinterpret_cast<const uint4*>(w + size_t(n) * K);
+    for (int j = 0; j < (K >> 8); ++j) {
+        const int p = lane + 32 * j;
+        const uint4 wv = __ldg(wr + p);
+        const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+            if (m < M) {
+                const uint4 xv = __ldcg(reinterpret_cast<const uint4*>(x + size_t(m) * x_stride) + p);
+                const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float a = __uint_as_float((e & 1) ? (xu[e >> 1] & 0xFFFF0000u) : (xu[e >> 1] << 16));
+                    const float b = __uint_as_float((e & 1) ? (wu[e >> 1] & 0xFFFF0000u) : (wu[e >> 1] << 16));
+                    acc[m] = __fadd_rn(acc[m], __fmul_rn(a, b));
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
+        if (m < M) {
+            float v = acc[m];
+#pragma unroll
+            for (int o = 16; o; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+            if (lane == 0) out[size_t(m) * out_stride + n] = f32_to_bf16_bits(v);
+        }
+    }
+}
+
+// Gated RMSNorm of every head of one raw row (K = heads * 128 <= 4096) and the row's per-token quantization, by
+// one warp-group: warp w takes heads w, w + 4, .. for the norm factors (gdn_sumsq128, gdn_norm_inv); thread t
+// then forms core = gdn_core(..) for its 8-element pieces t + 128 j and quantizes them (rowops.cuh order).
+// core_out (optional): the core row. hs: >= 32 floats of the warp-group's shared memory.
+__device__ __forceinline__ void gdn_norm_quant_row(const uint16_t* __restrict__ raw, const uint16_t* __restrict__ z,
+                                                   const uint16_t* __restrict__ w, float eps, int K,
+                                                   uint16_t* __restrict__ core_out, int8_t* __restrict__ q,
+                                                   float* __restrict__ s_out, float* red, float* hs, int tig, int wg) {
+    const int lane = tig & 31, warp = tig >> 5, J = K >> 10, nh = K >> 7;
+    for (int h = warp; h < nh; h += 4) {
+        const float ss = gdn_sumsq128(raw + h * kDH, lane);
+        if (lane == 0) hs[h] = gdn_norm_inv(ss, eps);
+    }
+    wg_sync(wg);
+    uint32_t cw[kRowMaxPieces][4];  // the core values, bf16 pairs
+    float amax = 0.f;
+#pragma unroll
+    for (int j = 0; j < kRowMaxPieces; ++j)
+        if (j < J) {
+            const int c0 = (tig + 128 * j) * 8, h = c0 / kDH, d0 = c0 % kDH;
+            const uint4 rv = __ldcg(reinterpret_cast<const uint4*>(raw + c0));
+            const uint4 zv = __ldcg(reinterpret_cast<const uint4*>(z + c0));
+            const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w + d0));
+            const uint32_t ru[4] = {rv.x, rv.y, rv.z, rv.w}, zu[4] = {zv.x, zv.y, zv.z, zv.w}, wu[4] = {wv.x, wv.y, wv.z, wv.w};
+            const float r = hs[h];
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+                const uint16_t lo = gdn_core(__uint_as_float(ru[p] << 16), __uint_as_float(wu[p] << 16), r,
+                                             __uint_as_float(zu[p] << 16));
+                const uint16_t hi = gdn_core(__uint_as_float(ru[p] & 0xFFFF0000u), __uint_as_float(wu[p] & 0xFFFF0000u), r,
+                                             __uint_as_float(zu[p] & 0xFFFF0000u));
+                cw[j][p] = uint32_t(lo) | (uint32_t(hi) << 16);
+                amax = fmaxf(amax, fmaxf(fabsf(bf16_bits_to_f32(lo)), fabsf(bf16_bits_to_f32(hi))));
+            }
+            if (core_out) reinterpret_cast<uint4*>(core_out)[tig + 128 * j] = make_uint4(cw[j][0], cw[j][1], cw[j][2], cw[j][3]);
+        }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (lane == 0) red[8 + warp] = amax;
+    wg_sync(wg);
+    const float m = fmaxf(fmaxf(red[8], red[9]), fmaxf(red[10], red[11]));
+    const float s = __fdiv_rn(m, 127.f);
+    if (tig == 0) *s_out = s;
+#pragma unroll
+    for (int j = 0; j < kRowMaxPieces; ++j)
+        if (j < J) {
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = __uint_as_float((e & 1) ? (cw[j][e >> 1] & 0xFFFF0000u) : (cw[j][e >> 1] << 16));
+            reinterpret_cast<uint2*>(q)[tig + 128 * j] = quant8_perm(v, s);
+        }
+    wg_sync(wg);
+}
+
+}  // namespace mono

@@ -135,7 +135,17 @@ struct GdnArgs {
     int M, C, HK, HV;
 };
 size_t gdn_workspace_bytes(int M, int C, int HV);
+// Validates the GDN step's operands and fills A (workspace: gdn_workspace_bytes; conv_out and gates in it).
+int fill_gdn_args(GdnArgs& A, const void* qkv, const void* z, const void* a, const void* b, const void* conv_w,
+                  void* conv_state, const float* dt_bias, const float* g_decay, float* state, const void* gnorm_w,
+                  float gnorm_eps, float qscale, int64_t M, int64_t HK, int64_t HV, void* core, void* workspace,
+                  size_t workspace_bytes, const int32_t* ctl, const void* prev_qkv, const void* prev_a,
+                  const void* prev_b, void* save_qkv, void* save_a, void* save_b, int64_t qkv_stride,
+                  int64_t z_stride, int64_t ab_stride);
 int launch_gdn_step(GdnArgs A, void* ws, cudaStream_t stream);
+// a | b projection (gdn.cuh gdn_ab_column): out[m][n] for n < N, one warp per column
+int launch_gdn_ab(const uint16_t* x, int64_t x_stride, const uint16_t* w, int K, int M, int N, uint16_t* out,
+                  int64_t out_stride, cudaStream_t stream);
 
 struct TopkArgs {
     const uint16_t* x;  // [rows][V] bf16

@@ -71,7 +71,7 @@ __global__ void __launch_bounds__((CW + PW) * 32, 1) mlp_kernel(const Program P,
 
     auto phase_x = [&](int ph) {
         const PhaseDesc& p = P.ph[ph];
-        if (!p.xsmem) return XSrc{p.x, p.K, false, true};
+        if (!p.xsmem) return XSrc{p.x, p.K, false, true, true};  // written by this launch: L2 reads
         stage_x_consumers<CW>(p.x, M, p.K, true, xsm);
         return XSrc{xsm, p.K + 16, true, true};
     };

@@ -114,6 +114,47 @@ __device__ __forceinline__ void norm_quant_row(const uint16_t* __restrict__ x, c
     wg_sync(wg);
 }
 
+// Sigmoid gate and per-token quantization of one row by a warp-group (H = 128 t + 1024 j pieces as in
+// norm_quant_row; H <= 4096).
+__device__ __forceinline__ void gate_quant_row(const uint16_t* __restrict__ x, const uint16_t* __restrict__ gate,
+                                               int64_t gate_head_stride, const uint16_t* __restrict__ lut, int H,
+                                               int8_t* __restrict__ q, float* __restrict__ s_out, float* red, int tig,
+                                               int wg) {
+    const int lane = tig & 31, warp = tig >> 5, J = H >> 10;
+    float vals[kRowMaxPieces][8];
+#pragma unroll
+    for (int j = 0; j < kRowMaxPieces; ++j)
+        if (j < J) {
+            const int c0 = (tig + 128 * j) * 8;  // 8 columns inside one 256-wide head
+            const uint4 xv = __ldcg(reinterpret_cast<const uint4*>(x + c0));
+            const uint4 gv = __ldcg(reinterpret_cast<const uint4*>(gate + (c0 >> 8) * gate_head_stride + (c0 & 255)));
+            const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w}, gu[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const uint32_t xb = (e & 1) ? (xu[e >> 1] >> 16) : (xu[e >> 1] & 0xFFFFu);
+                const uint32_t gb = (e & 1) ? (gu[e >> 1] >> 16) : (gu[e >> 1] & 0xFFFFu);
+                vals[j][e] = bf16_round(__fmul_rn(bf16_bits_to_f32(uint16_t(xb)), bf16_bits_to_f32(__ldg(lut + gb))));
+            }
+        }
+    float amax = 0.f;
+#pragma unroll
+    for (int j = 0; j < kRowMaxPieces; ++j)
+        if (j < J)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(vals[j][e]));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (lane == 0) red[8 + warp] = amax;
+    wg_sync(wg);
+    const float m = fmaxf(fmaxf(red[8], red[9]), fmaxf(red[10], red[11]));
+    const float s = __fdiv_rn(m, 127.f);
+    if (tig == 0) *s_out = s;
+#pragma unroll
+    for (int j = 0; j < kRowMaxPieces; ++j)
+        if (j < J) reinterpret_cast<uint2*>(q)[tig + 128 * j] = quant8_perm(vals[j], s);
+    wg_sync(wg);
+}
+
 // Per-token quantization of a whole activation block x [M][K] bf16 by the first T threads of the CTA
 // (named barrier BAR), into the permuted int8 rows of a shared buffer (row pitch `pitch`) and the row
 // scales xs[M]. Rows are taken in batches whose 16-byte pieces fit 8 per thread, so a batch costs one round

@@ -58,6 +58,10 @@ __device__ __forceinline__ bool consumer_sync_and(bool v) {
     return r != 0;
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ int phase_subs(const PhaseDesc& p) { return p.paired ? 2 : 1; }
 __device__ __forceinline__ int cta_tiles(const PhaseDesc& p) {
     const int nt = phase_tiles(p), b = int(blockIdx.x), G = int(gridDim.x);
@@ -90,27 +94,26 @@ __device__ __forceinline__ ItemRef item_at(const Program& P, int i) {
     return r;
 }
 
-// Issue the copy of item r into `stage`, completing on `full`. TILED: lane 0, one bulk copy (the full
-// barrier counts 1 arrival + the bytes). ROW: every lane gathers its 16-byte pieces with cp.async and
-// arrives once when they land (the full barrier counts 32 arrivals).
+// Issue the copy of item (k, sub, c) of phase p into `stage`, completing on `full`. TILED: lane 0, one bulk
+// copy (the full barrier counts 1 arrival + the bytes). ROW: every lane gathers its 16-byte pieces with
+// cp.async and arrives once when they land (the full barrier counts 32 arrivals).
 template <int FMT, int LAYOUT>
-__device__ __forceinline__ void produce_item(const Program& P, const ItemRef& r, uint8_t* stage, uint64_t* full,
-                                             int lane) {
+__device__ __forceinline__ void issue_item(const PhaseDesc& p, int k, int sub, int c, uint8_t* stage, uint64_t* full,
+                                           int lane) {
     constexpr int SB = Fmt<FMT>::SB;
-    const PhaseDesc& p = P.ph[r.ph];
-    const int T = int(blockIdx.x) + r.k * int(gridDim.x);
+    const int T = int(blockIdx.x) + k * int(gridDim.x);
     int mat, lt;
-    resolve(p, T, r.sub, mat, lt);
+    resolve(p, T, sub, mat, lt);
     const MatDesc& w = p.m[mat];
     if constexpr (LAYOUT == LAYOUT_TILED) {
         if (lane == 0) {
             mbar_arrive_expect_tx(full, kStageW + SB);
-            bulk_g2s(stage, w.q + (size_t(lt) * (p.K >> 10) + r.c) * (kStageW + SB), kStageW + SB, full);
+            bulk_g2s(stage, w.q + (size_t(lt) * (p.K >> 10) + c) * (kStageW + SB), kStageW + SB, full);
         }
     } else {
         const int g = lane >> 2, t = lane & 3;
         const size_t rowb = size_t(p.K) >> 1;
-        const uint8_t* r0 = w.q + size_t(lt * 16 + g) * rowb + size_t(r.c) * 512 + t * 16;
+        const uint8_t* r0 = w.q + size_t(lt * 16 + g) * rowb + size_t(c) * 512 + t * 16;
         const uint8_t* r1 = r0 + 8 * rowb;
 #pragma unroll
         for (int gi = 0; gi < 8; ++gi) {
@@ -118,16 +121,33 @@ __device__ __forceinline__ void produce_item(const Program& P, const ItemRef& r,
             cp_async16(stage + gi * 1024 + 512 + lane * 16, r1 + gi * 64);
         }
         if constexpr (FMT == FMT_GPTQ) {
-            if (lane < 16) cp_async16(stage + kStageW + lane * 16, w.s + (size_t(lt * 16 + lane) * (p.K >> 7) + r.c * 8) * 2);
+            if (lane < 16) cp_async16(stage + kStageW + lane * 16, w.s + (size_t(lt * 16 + lane) * (p.K >> 7) + c * 8) * 2);
         } else {
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const int piece = lane + 32 * h, row = piece >> 2, part = piece & 3;
-                cp_async16(stage + kStageW + row * 64 + part * 16, w.s + size_t(lt * 16 + row) * (p.K >> 4) + r.c * 64 + part * 16);
+                cp_async16(stage + kStageW + row * 64 + part * 16, w.s + size_t(lt * 16 + row) * (p.K >> 4) + c * 64 + part * 16);
             }
         }
         asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(full)) : "memory");
     }
+}
+
+// Ask the L2 to fetch item (k, sub, c) of phase p (TILED layout: one contiguous block) ahead of its copy.
+template <int FMT>
+__device__ __forceinline__ void prefetch_item_l2(const PhaseDesc& p, int k, int sub, int c) {
+    constexpr int SB = Fmt<FMT>::SB;
+    const int T = int(blockIdx.x) + k * int(gridDim.x);
+    int mat, lt;
+    resolve(p, T, sub, mat, lt);
+    const uint8_t* src = p.m[mat].q + (size_t(lt) * (p.K >> 10) + c) * (kStageW + SB);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(kStageW + SB) : "memory");
+}
+
+template <int FMT, int LAYOUT>
+__device__ __forceinline__ void produce_item(const Program& P, const ItemRef& r, uint8_t* stage, uint64_t* full,
+                                             int lane) {
+    issue_item<FMT, LAYOUT>(P.ph[r.ph], r.k, r.sub, r.c, stage, full, lane);
 }
 
 // Incremental walk over a CTA's items (no divisions per step).
@@ -190,18 +210,15 @@ __device__ __forceinline__ bool produce_all(const Program& P, uint8_t* ring, uin
     return ok;
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-// Consumer side: the items [first, first + count) of phase ph (count < 0: to the end of the phase) that consumer
+// Consumer side: the items [first, first + count) of phase p (count < 0: to the end of the phase) that consumer
 // warp `cw` (of CW) computes, each partial stored at part[item - first] (item = (k * subs + sub) * C + chunk).
-// S must be a multiple of CW. Returns false if a wait gave up.
+// base0 = the CTA's request index of the phase's first item. S must be a multiple of CW. Returns false if a
+// wait gave up.
 template <int FMT, int LAYOUT, int MT, int CW>
-__device__ __forceinline__ bool consume_phase(const Program& P, int ph, const XSrc& xs, uint8_t* ring, uint64_t* full,
-                                              uint64_t* empty, int S, uint32_t* part, int cw, int lane, int first = 0,
-                                              int count = -1) {
-    const int base0 = cta_base(P, ph), nph = cta_items(P.ph[ph]), C = P.ph[ph].K >> 10;
+__device__ __forceinline__ bool consume_items(const PhaseDesc& p, int base0, const uint16_t* pair_tab, int M,
+                                              const XSrc& xs, uint8_t* ring, uint64_t* full, uint64_t* empty, int S,
+                                              uint32_t* part, int cw, int lane, int first = 0, int count = -1) {
+    const int nph = cta_items(p), C = p.K >> 10;
     const int base = base0 + first, n = count < 0 || first + count > nph ? nph - first : count;
     bool ok = true;
     int i = base + ((cw - base % CW) + CW) % CW;
@@ -212,16 +229,26 @@ __device__ __forceinline__ bool consume_phase(const Program& P, int ph, const XS
         uint32_t R[MT][4];
         const uint8_t* stage = ring + size_t(s) * stage_bytes<FMT>();
         if (xs.smem)
-            compute_item<FMT, LAYOUT, MT, 2>(stage, P.pair_tab, xs, P.M, li % C, lane, R);
+            compute_item<FMT, LAYOUT, MT, 2>(stage, pair_tab, xs, M, li % C, lane, R);
+        else if (xs.cg)
+            compute_item<FMT, LAYOUT, MT, 3>(stage, pair_tab, xs, M, li % C, lane, R);
         else if (xs.perm)
-            compute_item<FMT, LAYOUT, MT, 1>(stage, P.pair_tab, xs, P.M, li % C, lane, R);
+            compute_item<FMT, LAYOUT, MT, 1>(stage, pair_tab, xs, M, li % C, lane, R);
         else
-            compute_item<FMT, LAYOUT, MT, 0>(stage, P.pair_tab, xs, P.M, li % C, lane, R);
+            compute_item<FMT, LAYOUT, MT, 0>(stage, pair_tab, xs, M, li % C, lane, R);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
         store_partial<MT>(part, li - first, lane, R);
     }
     return ok;
+}
+
+template <int FMT, int LAYOUT, int MT, int CW>
+__device__ __forceinline__ bool consume_phase(const Program& P, int ph, const XSrc& xs, uint8_t* ring, uint64_t* full,
+                                              uint64_t* empty, int S, uint32_t* part, int cw, int lane, int first = 0,
+                                              int count = -1) {
+    return consume_items<FMT, LAYOUT, MT, CW>(P.ph[ph], cta_base(P, ph), P.pair_tab, P.M, xs, ring, full, empty, S, part,
+                                              cw, lane, first, count);
 }
 
 // Vector staging of an activation block x [M][K] (rows contiguous) by the consumer threads into shared

@@ -291,11 +291,12 @@ def qk_norm_rope_kv(rawq, rawk, vn, weightq, weightk, freqs, key, value, positio
 _attn_ws = {}
 
 
-def attn_dpas(q, key, value, seqlen, xk, xv, mask, chunks_hint=0):
+def attn_dpas(q, key, value, seqlen, xk, xv, mask, chunks_hint=0, out=None):
     """Tree decode attention (the reference's _C.attn_dpas, csrc/attn_dpas.sycl:269-342). q bf16 [1, H, S, 256];
     key / value bf16 [1, Hk, cap, 256]; seqlen int32 [1] on the device (L, no host sync); xk / xv bf16
     [1, Hk, S, 256]; mask int32 [S] (an empty tensor: the single draft row over the prefix only).
-    Returns bf16 [1, S, H * 256]. chunks_hint is accepted for the reference's signature and unused."""
+    Returns bf16 [1, S, H * 256] (into `out` when given). chunks_hint is accepted for the reference's signature and
+    unused."""
     _cuda(q, key, value, seqlen, xk, xv)
     _check(q.dtype == torch.bfloat16 and q.dim() == 4 and q.size(0) == 1 and q.size(3) == 256, "q bf16 [1, H, S, 256]")
     H, S, Hk, cap = q.size(1), q.size(2), key.size(1), key.size(2)
@@ -308,7 +309,9 @@ def attn_dpas(q, key, value, seqlen, xk, xv, mask, chunks_hint=0):
     xk, xv = xk.contiguous(), xv.contiguous()
     nbytes = _lib.load().mono_tree_attention_workspace(Hk, cap)
     ws = _workspace(_attn_ws, (q.device, Hk, cap), nbytes, q.device)
-    out = torch.empty((1, S, H * 256), dtype=torch.bfloat16, device=q.device)
+    if out is None:
+        out = torch.empty((1, S, H * 256), dtype=torch.bfloat16, device=q.device)
+    _check(out.dtype == torch.bfloat16 and out.is_contiguous() and out.numel() == S * H * 256, "out bf16 [1, S, H * 256]")
     with torch.cuda.device(q.device):
         _lib.call("mono_tree_attention", _p(q), _p(key), _p(value), _p(seqlen), _p(xk), _p(xv),
                   _p(mask) if tree else None, H, Hk, S, cap, _p(out), _p(ws), nbytes, _stream(q.device))
@@ -498,4 +501,156 @@ def lut_mul(a, b, lut, b_head_stride=256, out=None):
     with torch.cuda.device(a.device):
         _lib.call("mono_lut_mul", _p(a), a.stride(0), _p(b), b.stride(0), int(b_head_stride), _p(lut), M, K, _p(out),
                   out.stride(0), _stream(a.device))
+    return out
+
+
+# ---- layer programs (include/mono_b200.h mono_program_*) ----------------------------------------------------------
+
+ROWS_NORM, ROWS_GATE, ROWS_QUANT, ROWS_GDN = 0, 1, 2, 3
+
+
+class Program:
+    """A layer program: ops appended in order, planned for M rows, copied to the device once, then launched as
+    one persistent cooperative kernel per call (graph-capturable). Every tensor an op names is kept alive by
+    the program; the ops hold raw pointers, so those tensors must not be reallocated afterwards."""
+
+    def __init__(self, device, capacity=512):
+        import numpy as np
+        lib = _lib.load()
+        self.device = torch.device(device)
+        self.opb = int(lib.mono_program_op_bytes())
+        self.host = np.zeros(capacity * self.opb, dtype=np.uint8)
+        self.n = 0
+        self.keep = []
+        self.dev_ops = None
+        self.M = None
+        self.ws = torch.zeros(int(lib.mono_program_workspace()), dtype=torch.uint8, device=self.device)
+
+    def _ptr(self):
+        return self.host.ctypes.data
+
+    def _next(self):
+        _check(self.dev_ops is None, "program already planned")
+        _check(self.n * self.opb < self.host.size, "program capacity")
+        i = self.n
+        self.n += 1
+        return i
+
+    def _hold(self, *ts):
+        self.keep.extend(t for t in ts if t is not None)
+
+    def rows(self, mode, x, K, q, s, norm_w=None, eps=1e-6, gate=None, gate_row_stride=0, gate_head_stride=0, lut=None,
+             xn_out=None, zero=None, barrier=True, x_stride=None):
+        self._hold(x, q, s, norm_w, gate, lut, xn_out, zero)
+        _lib.call("mono_program_rows", self._ptr(), self._next(), int(mode), _p(x), int(x_stride or K), int(K), _p(norm_w),
+                  float(eps), _p(gate), int(gate_row_stride), int(gate_head_stride), _p(lut), _p(xn_out), _p(q), _p(s),
+                  _p(zero), int(bool(barrier)))
+
+    def gemv(self, weights, K, q, s, out, out_stride, residual=None, residual_stride=0, paired=False, silu_lut=None,
+             amax=None, barrier=True):
+        import ctypes
+        self._hold(q, s, out, residual, silu_lut, amax, *[w for w, _ in weights])
+        ptrs = (ctypes.c_void_p * len(weights))(*[w.data_ptr() for w, _ in weights])
+        rows = (ctypes.c_int64 * len(weights))(*[int(r) for _, r in weights])
+        _lib.call("mono_program_gemv", self._ptr(), self._next(), ctypes.cast(ptrs, ctypes.c_void_p),
+                  ctypes.cast(rows, ctypes.c_void_p), len(weights), int(bool(paired)), int(K), _p(q), _p(s), _p(out),
+                  int(out_stride), _p(residual), int(residual_stride), _p(silu_lut), _p(amax), int(bool(barrier)))
+
+    def quant(self, h, K, amax, q, s, barrier=True):
+        self._hold(h, amax, q, s)
+        _lib.call("mono_program_quant", self._ptr(), self._next(), _p(h), int(K), _p(amax), _p(q), _p(s),
+                  int(bool(barrier)))
+
+    def ab(self, x, x_stride, K, w, out, barrier=False):
+        self._hold(x, w, out)
+        _lib.call("mono_program_ab", self._ptr(), self._next(), _p(x), int(x_stride), int(K), _p(w), int(w.shape[0]),
+                  _p(out), int(bool(barrier)))
+
+    def gdn(self, delta, qkv, z, a, b, conv_w, conv_state, dt_bias, g_decay, state, gnorm_w, gnorm_eps, qscale, M, hk,
+            hv, raw, ctl, prev, save, qkv_stride, z_stride, ab_stride, workspace, barrier=True):
+        prev = prev if prev is not None else (None, None, None)
+        save = save if save is not None else (None, None, None)
+        self._hold(qkv, z, a, b, conv_w, conv_state, dt_bias, g_decay, state, gnorm_w, raw, ctl, workspace, *prev, *save)
+        _lib.call("mono_program_gdn", self._ptr(), self._next(), int(bool(delta)), _p(qkv), _p(z), _p(a), _p(b),
+                  _p(conv_w), _p(conv_state), _p(dt_bias), _p(g_decay), _p(state), _p(gnorm_w), float(gnorm_eps),
+                  float(qscale), int(M), int(hk), int(hv), _p(raw), _p(ctl), _p(prev[0]), _p(prev[1]), _p(prev[2]),
+                  _p(save[0]), _p(save[1]), _p(save[2]), int(qkv_stride), int(z_stride), int(ab_stride),
+                  _p(workspace), workspace.numel() * workspace.element_size(), int(bool(barrier)))
+
+    def plan(self, M):
+        """Checks and plans the ops for M rows and copies them to the device."""
+        _lib.call("mono_program_plan", self._ptr(), self.n, int(M))
+        self.M = int(M)
+        self.dev_ops = torch.from_numpy(self.host[: self.n * self.opb].copy()).to(self.device)
+        return self
+
+    def launch(self, prefetch=0):
+        _check(self.dev_ops is not None, "program not planned")
+        with torch.cuda.device(self.device):
+            _lib.call("mono_program_launch", self._ptr(), _p(self.dev_ops), self.n, self.M, _p(self.ws), int(prefetch),
+                      _stream(self.device))
+
+
+def gdn_ab(x, w, out=None):
+    """The GDN gates' a | b projection (include/mono_b200.h mono_gdn_ab): x bf16 [M, K] (unit column stride),
+    w bf16 [N, K] -> bf16 [M, N]."""
+    _cuda(x, w)
+    _check(x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1, "x bf16 [M, K] rows")
+    _check(w.dtype == torch.bfloat16 and w.is_contiguous() and w.shape[1] == x.shape[1], "w bf16 [N, K]")
+    M, K = x.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    _check(out.is_contiguous() and out.numel() == M * N, "out [M, N]")
+    with torch.cuda.device(x.device):
+        _lib.call("mono_gdn_ab", _p(x), x.stride(0), _p(w), K, M, N, _p(out), _stream(x.device))
+    return out
+
+
+_post_ws = {}
+_gdn_layer_ws = {}
+
+
+def layer_post(x, y, o_w, norm_w, eps, gate_w, up_w, down_w, silu_lut, I, gate=None, sig_lut=None,
+               gate_head_stride=512, out=None):
+    """The reference's layer_post in one launch (include/mono_b200.h mono_layer_post_gptq): sigmoid gate (if
+    gate is given) -> quant -> o projection + residual x -> RMSNorm -> MLP + residual. x, y bf16 [M, H] / [M, K]
+    contiguous; weights TILED GPTQ. Returns out bf16 [M, H] (may be x)."""
+    _cuda(x, y)
+    _check(x.dtype == torch.bfloat16 and x.dim() == 2 and x.is_contiguous(), "x bf16 [M, H] contiguous")
+    _check(y.dtype == torch.bfloat16 and y.dim() == 2 and y.is_contiguous() and y.shape[0] == x.shape[0], "y bf16 [M, K]")
+    M, H = x.shape
+    K = y.shape[1]
+    if out is None:
+        out = torch.empty_like(x)
+    nbytes = _lib.load().mono_layer_post_gptq_workspace(K, H, I)
+    ws = _workspace(_post_ws, (x.device, K, H, I), nbytes, x.device)
+    with torch.cuda.device(x.device):
+        _lib.call("mono_layer_post_gptq", _p(x), _p(y), K, _p(gate), gate.stride(0) if gate is not None else 0,
+                  int(gate_head_stride), _p(sig_lut), _p(o_w), _p(norm_w), float(eps), _p(gate_w), _p(up_w), _p(down_w),
+                  _p(silu_lut), M, H, int(I), _p(out), _p(ws), nbytes, _stream(x.device))
+    return out
+
+
+def layer_gdn(x, norm_in, eps_in, qkv_w, z_w, wab, conv_w, conv_state, dt_bias, g_decay, state, gnorm_w, gnorm_eps,
+              qscale, hk, ctl, prev, save, out_w, norm_post, eps_post, gate_w, up_w, down_w, silu_lut, I, out=None):
+    """The reference's layer_gdn in one launch (include/mono_b200.h mono_layer_gdn_gptq): the whole Gated-DeltaNet
+    decoder layer for x bf16 [M, H] (M <= 8); deferred GDN state handling as gdn_step_deferred (ctl None:
+    committing). Returns out bf16 [M, H] (may be x)."""
+    _cuda(x)
+    _check(x.dtype == torch.bfloat16 and x.dim() == 2 and x.is_contiguous(), "x bf16 [M, H] contiguous")
+    M, H = x.shape
+    HV = dt_bias.numel()
+    if out is None:
+        out = torch.empty_like(x)
+    prev = prev if prev is not None else (None, None, None)
+    save = save if save is not None else (None, None, None)
+    nbytes = _lib.load().mono_layer_gdn_gptq_workspace(M, H, I, hk, HV)
+    ws = _workspace(_gdn_layer_ws, (x.device, M, H, I, hk, HV), nbytes, x.device)
+    with torch.cuda.device(x.device):
+        _lib.call("mono_layer_gdn_gptq", _p(x), _p(norm_in), float(eps_in), _p(qkv_w), _p(z_w), _p(wab), _p(conv_w),
+                  _p(conv_state), _p(dt_bias), _p(g_decay), _p(state), _p(gnorm_w), float(gnorm_eps), float(qscale),
+                  _p(ctl), _p(prev[0]), _p(prev[1]), _p(prev[2]), _p(save[0]), _p(save[1]), _p(save[2]), _p(out_w),
+                  _p(norm_post), float(eps_post), _p(gate_w), _p(up_w), _p(down_w), _p(silu_lut), M, H, int(I), int(hk),
+                  HV, _p(out), _p(ws), nbytes, _stream(x.device))
     return out

@@ -53,6 +53,23 @@ SIGNATURES = {
     "mono_gdn_step": (I, [P, P, P, P, P, P, P, P, P, P, ctypes.c_float, ctypes.c_float, I64, I64, I64, P, P, SZ, P]),
     "mono_gdn_step_deferred": (I, [P, P, P, P, P, P, P, P, P, P, ctypes.c_float, ctypes.c_float, I64, I64, I64, P, P, P,
                                    P, P, P, P, P, I64, I64, I64, P, SZ, P]),
+    "mono_program_op_bytes": (SZ, []),
+    "mono_program_workspace": (SZ, []),
+    "mono_program_rows": (I, [P, I, I, P, I64, I64, P, ctypes.c_float, P, I64, I64, P, P, P, P, P, I]),
+    "mono_program_gemv": (I, [P, I, P, P, I, I, I64, P, P, P, I64, P, I64, P, P, I]),
+    "mono_program_quant": (I, [P, I, P, I64, P, P, P, I]),
+    "mono_program_ab": (I, [P, I, P, I64, I64, P, I64, P, I]),
+    "mono_program_gdn": (I, [P, I, I, P, P, P, P, P, P, P, P, P, P, ctypes.c_float, ctypes.c_float, I64, I64, I64, P, P,
+                             P, P, P, P, P, P, I64, I64, I64, P, SZ, I]),
+    "mono_program_plan": (I, [P, I, I64]),
+    "mono_program_launch": (I, [P, P, I, I64, P, I, P]),
+    "mono_gdn_ab": (I, [P, I64, P, I64, I64, I64, P, P]),
+    "mono_layer_post_gptq_workspace": (SZ, [I64, I64, I64]),
+    "mono_layer_post_gptq": (I, [P, P, I64, P, I64, I64, P, P, P, ctypes.c_float, P, P, P, P, I64, I64, I64, P, P, SZ,
+                                 P]),
+    "mono_layer_gdn_gptq_workspace": (SZ, [I64, I64, I64, I64, I64]),
+    "mono_layer_gdn_gptq": (I, [P, P, ctypes.c_float, P, P, P, P, P, P, P, P, P, ctypes.c_float, ctypes.c_float, P, P, P,
+                                P, P, P, P, P, P, ctypes.c_float, P, P, P, P, I64, I64, I64, I64, I64, P, P, SZ, P]),
 }
 
 MONO_OK, MONO_EINVAL, MONO_ECUDA, MONO_ETIMEOUT, MONO_EDEVICE = 0, 1, 2, 3, 4

@@ -14,7 +14,7 @@ comfy_mono_decode_xpu/mtp_loop.py):
            hidden row (all on the device)
 
 Per layer: full attention = rowlin(norm -> q|k|v) -> qk_norm_rope_kv -> tree attention -> rowlin(gate -> o_proj +
-residual) -> fused MLP; GDN = rowlin(norm -> qkv|z, xn) -> a|b (bf16 GEMM of xn) -> deferred GDN step ->
+residual) -> fused MLP; GDN = rowlin(norm -> qkv|z, xn) -> a|b (mono_gdn_ab) -> deferred GDN step ->
 rowlin(quant -> out_proj + residual) -> fused MLP. The verify rows form a chain (the GDN step's verify rows run as a
 chain); the bf16 MTP head and the verify's lm_head run as cuBLAS GEMMs through torch; the drafts' lm_head is a W4A8 GPTQ copy on this build's
 linear kernel; the head's norms and gates are the row kernels
@@ -29,6 +29,7 @@ import torch
 import torch.nn.functional as F
 
 from . import _C
+from ._C import ROWS_GATE, ROWS_GDN, ROWS_NORM
 
 
 @dataclass
@@ -94,7 +95,8 @@ def rope_table(cfg: Qwen35Config, cap: int, dev):
 class Qwen35W4A8:
     """Weights and decode state of one stream on one device."""
 
-    def __init__(self, cfg: Qwen35Config, device, prompt_len: int, gen_tokens: int = 512, seed: int = 0x5EED + 4):
+    def __init__(self, cfg: Qwen35Config, device, prompt_len: int, gen_tokens: int = 512, seed: int = 0x5EED + 4,
+                 fused: bool = True, prefetch: int = 0):
         self.cfg, self.dev = cfg, torch.device(device)
         c, dev = cfg, self.dev
         g = torch.Generator(device=dev).manual_seed(seed)
@@ -166,6 +168,8 @@ class Qwen35W4A8:
         self.drafts = torch.zeros(R, dtype=torch.int64, device=dev)
         self.no_mask = torch.empty(0, dtype=torch.int32, device=dev)
         self.total = torch.zeros(1, dtype=torch.int64, device=dev)  # tokens committed, summed on the device
+        self.fused, self.prefetch = fused, prefetch
+        self.programs = self._build_programs() if fused else None
 
     # ---- layers ------------------------------------------------------------------------------------------
     def _attention(self, L, x, freqs):
@@ -193,7 +197,7 @@ class Qwen35W4A8:
         xn = torch.empty_like(x)
         pre = _C.rowlin_gptq(x, _C.ROWLIN_NORM, [(L["qkv"], Ck), (L["z"], HV * D)], norm_w=L["ln1"], eps=c.eps,
                              xn_out=xn)
-        ab = F.linear(xn, L["wab"])
+        ab = _C.gdn_ab(xn, L["wab"])
         prev, save = L["saved"][self.parity], L["saved"][1 - self.parity]
         core = _C.gdn_step_deferred(pre[:, :Ck], pre[:, Ck:], ab[:, :HV], ab[:, HV:], L["conv_w"], L["conv_state"],
                                     L["dt_bias"], L["g_decay"],
@@ -201,16 +205,100 @@ class Qwen35W4A8:
         x1 = _C.rowlin_gptq(core, _C.ROWLIN_QUANT, [(L["out"], c.hidden)], residual=x)
         return _C.mlp_gptq(x1, L["ln2"], c.eps, L["gate"], L["up"], L["down"], silu_lut=self.silu_lut, I=c.inter)
 
+    # ---- layer programs: the verify body as 9 persistent launches (one per run of layers between two attention
+    # cores), separated by the attention kernels ----------------------------------------------------------------
+    def _build_programs(self):
+        """Two program sets (the GDN replay buffers alternate with the step parity); each set is a list of
+        programs, program j running [post of attention layer 4j - 1 (j > 0)], the GDN layers, [pre of the next
+        attention layer]. All activations live in fixed scratch buffers."""
+        c, dev = self.cfg, self.dev
+        R, H, I, hd = c.depth + 1, c.hidden, c.inter, c.head_dim
+        HV, D, hk = c.gdn_v_heads, c.gdn_dim, c.gdn_k_heads
+        Ck, Z = 2 * hk * D + HV * D, HV * D
+        nq, nkv = 2 * c.heads * hd, c.kv_heads * hd
+        bf, i8, f32 = torch.bfloat16, torch.int8, torch.float32
+        e = lambda *shape, dtype=bf: torch.zeros(*shape, dtype=dtype, device=dev)  # noqa: E731
+        B = dict(X=e(R, H), X1=e(R, H), XN=e(R, H), Q1=e(16, max(H, 4096), dtype=i8), S1=e(64, dtype=f32),
+                 PROJ=e(R, Ck + Z), AB=e(R, 2 * HV), RAW=e(R, Z), QC=e(16, max(Z, c.heads * hd), dtype=i8),
+                 SC=e(64, dtype=f32), HB=e(R, I), Q2=e(16, I, dtype=i8), S2=e(64, dtype=f32),
+                 AMAX=e(64, dtype=torch.int32), PRE=e(R, nq + 2 * nkv), Y=e(1, R, c.heads * hd),
+                 GWS=e(_C._lib.load().mono_gdn_step_workspace(R, Ck, HV), dtype=torch.uint8))
+        self.buf = B
+
+        def post(P, L, w_o, K):  # out / o projection + residual, then the MLP block (the reference's layer_post)
+            P.gemv([(w_o, H)], K, B["QC"], B["SC"], B["X1"], H, residual=B["X"], residual_stride=H)
+            P.rows(ROWS_NORM, B["X1"], H, B["Q1"], B["S1"], norm_w=L["ln2"], eps=c.eps, zero=B["AMAX"])
+            P.gemv([(L["gate"], I), (L["up"], I)], H, B["Q1"], B["S1"], B["HB"], I, paired=True, silu_lut=self.silu_lut,
+                   amax=B["AMAX"])
+            P.quant(B["HB"], I, B["AMAX"], B["Q2"], B["S2"])
+            P.gemv([(L["down"], H)], I, B["Q2"], B["S2"], B["X"], H, residual=B["X1"], residual_stride=H)
+
+        def gdn(P, L, parity):
+            prev, save = L["saved"][parity], L["saved"][1 - parity]
+            P.rows(ROWS_NORM, B["X"], H, B["Q1"], B["S1"], norm_w=L["ln1"], eps=c.eps, xn_out=B["XN"])
+            P.ab(B["XN"], H, H, L["wab"], B["AB"])
+            P.gemv([(L["qkv"], Ck), (L["z"], Z)], H, B["Q1"], B["S1"], B["PROJ"], Ck + Z)
+            proj, ab = B["PROJ"], B["AB"]
+            for delta in (0, 1):
+                P.gdn(delta, proj, proj[:, Ck:], ab, ab[:, HV:], L["conv_w"], L["conv_state"], L["dt_bias"],
+                      L["g_decay"], L["state"], L["gnorm"], c.eps, D ** -0.5, R, hk, HV, B["RAW"], self.ctl, prev, save,
+                      Ck + Z, Ck + Z, 2 * HV, B["GWS"])
+            P.rows(ROWS_GDN, B["RAW"], Z, B["QC"], B["SC"], norm_w=L["gnorm"], eps=c.eps, gate=proj[:, Ck:],
+                   gate_row_stride=Ck + Z)
+            post(P, L, L["out"], Z)
+
+        sets = []
+        for parity in (0, 1):
+            progs, P = [], _C.Program(dev)
+            for i, L in enumerate(self.layers):
+                if c.is_attn(i):
+                    P.rows(ROWS_NORM, B["X"], H, B["Q1"], B["S1"], norm_w=L["ln1"], eps=c.eps)
+                    P.gemv([(L["q"], nq), (L["k"], nkv), (L["v"], nkv)], H, B["Q1"], B["S1"], B["PRE"], nq + 2 * nkv,
+                           barrier=False)
+                    progs.append(P.plan(R))
+                    P = _C.Program(dev)
+                    P.rows(ROWS_GATE, B["Y"].view(R, -1), c.heads * hd, B["QC"], B["SC"], gate=B["PRE"][:, hd:],
+                           gate_row_stride=nq + 2 * nkv, gate_head_stride=2 * hd, lut=self.sig_lut)
+                    post(P, L, L["o"], c.heads * hd)
+                else:
+                    gdn(P, L, parity)
+            progs.append(P.plan(R))
+            sets.append(progs)
+        return sets
+
+    def _verify_programs(self, tokens, freqs):
+        c, B = self.cfg, self.buf
+        R, hd = tokens.numel(), c.head_dim
+        nq, nkv = 2 * c.heads * hd, c.kv_heads * hd
+        torch.index_select(self.embed, 0, tokens.view(-1), out=B["X"])
+        progs = self.programs[self.parity]
+        attn = [L for i, L in enumerate(self.layers) if c.is_attn(i)]
+        for j, P in enumerate(progs):
+            P.launch(self.prefetch)
+            if j < len(attn):
+                L = attn[j]
+                pre = B["PRE"]
+                qg = pre[:, :nq].view(1, R, c.heads, 2 * hd)
+                rawk = pre[:, nq:nq + nkv].view(1, R, c.kv_heads, hd)
+                v = pre[:, nq + nkv:].view(1, R, c.kv_heads, hd)
+                q, k = _C.qk_norm_rope_kv(qg[..., :hd], rawk, v, L["q_norm"], L["k_norm"], freqs, L["kc"], L["vc"],
+                                          self.apos, c.eps, c.eps, c.rotary_dim)
+                _C.attn_dpas(q, L["kc"], L["vc"], self.aseq, k, v.transpose(1, 2), self.mask[:R], out=B["Y"])
+        return B["X"]
+
     def verify(self, tokens):
         """The D + 1 chain rows through the body; returns (greedy tokens [1, R], final hidden rows [R, H])."""
         c = self.cfg
         R = tokens.numel()
         _C.mtp_prep_verify(self.st, self.apos, self.aseq, self.vpos, self.tree_pos, self.ctl, self.tree_ctl,
                            self.parity, 0)
-        x = self.embed[tokens.view(-1)]
         freqs = self.rope[self.vpos.view(-1).clamp(max=self.cap - 1)]
-        for i, L in enumerate(self.layers):
-            x = self._attention(L, x, freqs) if c.is_attn(i) else self._gdn(L, x)
+        if self.fused:
+            x = self._verify_programs(tokens, freqs)
+        else:
+            x = self.embed[tokens.view(-1)]
+            for i, L in enumerate(self.layers):
+                x = self._attention(L, x, freqs) if c.is_attn(i) else self._gdn(L, x)
         logits = F.linear(_C.rmsnorm_add(x, self.final_norm, c.eps), self.lm_head)
         _, toks = _C.fast_topk(logits, 1, True)
         return toks.view(1, R), x
@@ -265,7 +353,10 @@ class Qwen35W4A8:
         c = self.cfg
         n_attn = sum(1 for i in range(c.layers) if c.is_attn(i))
         n_gdn = c.layers - n_attn
-        body = c.layers * 3 + n_gdn * 2 + n_attn * 3          # rowlin x2 + MLP; GDN conv + delta; rope + attention x2
+        if self.fused:  # one layer program per run of layers between attention cores; rope + attention x2
+            body = (n_attn + 1) + n_attn * 3
+        else:  # rowlin x2 + MLP; GDN a|b + conv + delta; rope + attention x2
+            body = c.layers * 3 + n_gdn * 3 + n_attn * 3
         draft = c.depth * (1 + 3 + 1 + 2 + 2 + 2 + 1 + 2)   # prep, norms, rope, attention, lut x2, norm-adds, lm_head, argmax
         return body + draft + 1 + 2 + 1 + 1                   # prep_verify, final norm + argmax, accept, verify norm
 

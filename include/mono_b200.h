@@ -295,6 +295,97 @@ MONO_API int mono_mtp_accept(int64_t* st, const int64_t* toks, const int64_t* dr
                              int64_t* next_tok, void* h_out, int32_t* ctl, const int64_t* kv_ptrs, int64_t nkv,
                              int64_t heads, int64_t cap, int64_t head_dim, int64_t* result, mono_stream_t stream);
 
+/* ---- Layer programs: the reference's single-launch layers (layer_pre / layer_post, csrc/mono_layer.sycl:1-9;
+ * layer_gdn, csrc/mono_gdn.sycl:5-20), generalised to any sequence of their phases ----
+ * A program is an array of ops of mono_program_op_bytes() bytes each, filled on the host by the builders below
+ * (op `index` of the array `ops`), planned once by mono_program_plan (which stores the shared-memory staging
+ * choice in the ops) and run by mono_program_launch as ONE persistent cooperative kernel: its producer warps
+ * stream the tiled GPTQ weights of every GEMV op in order (and `prefetch` items ahead into L2) while its
+ * consumer warps run the ops; `barrier` != 0 puts a grid barrier after an op. M (rows) is the program's.
+ * Arithmetic: each op is the same as the standalone entry it mirrors (mono_rowlin_gptq's row modes,
+ * mono_w4a8_gptq_linear's GEMV, mono_mlp_gptq's SiLU pair and re-quantization, mono_gdn_step_deferred) and
+ * gives the same bits. */
+MONO_API size_t mono_program_op_bytes(void);
+/* Barrier words of a launch: zero-filled once, left zero by every launch; one launch in flight per workspace. */
+MONO_API size_t mono_program_workspace(void);
+/* Rows op: for m < M, mode 0: xn = RMSNorm(x[m]; norm_w, eps); 1: y = bf16(x * lut[gate]) (gate element (m, c)
+ * at gate[m * gate_row_stride + (c / 256) * gate_head_stride + c % 256]); 2: x; 3 (GDN gated norm): per
+ * 128-wide head of the raw row x[m], core = bf16(bf16((raw * norm_w[d]) / sqrt(mean(raw^2) + eps)) *
+ * bf16(silu(z))) with z element (m, c) at gate[m * gate_row_stride + c] (norm_w [128]); then q[m], s[m] =
+ * act_quant of that row (xn_out, if not NULL: the normalized / core rows [M][K]). zero: 16 words set to 0, or
+ * NULL. K a multiple of 1024 up to 4096; x row stride x_stride elements. */
+MONO_API int mono_program_rows(void* ops, int index, int mode, const void* x, int64_t x_stride, int64_t K,
+                               const void* norm_w, float eps, const void* gate, int64_t gate_row_stride,
+                               int64_t gate_head_stride, const void* lut, void* xn_out, void* q, void* s, void* zero,
+                               int barrier);
+/* GEMV op: out[m][n] = bf16(GPTQ linear(q, s)) (+ residual: bf16(residual + that)) for nm (1..3) tiled
+ * weights of rows[i] outputs, concatenated along n (row strides out_stride / residual_stride elements); or,
+ * paired (nm = 2: gate, up of one shape), h = bf16(silu_lut[bf16(g s)] * bf16(u s)) to out and the row maxima
+ * of |h| (float bits) into amax[m] (zeroed by an earlier rows op). q int8 [M][K] permuted (written by a rows or
+ * quant op of the program), s [M]. */
+MONO_API int mono_program_gemv(void* ops, int index, const void* const* weights, const int64_t* rows, int nm,
+                               int paired, int64_t K, const void* q, const void* s, void* out, int64_t out_stride,
+                               const void* residual, int64_t residual_stride, const void* silu_lut, void* amax,
+                               int barrier);
+/* Quant op: q[m], s[m] = quantization of h [M][K] bf16 with s = amax[m] / 127 (the paired GEMV's maxima). */
+MONO_API int mono_program_quant(void* ops, int index, const void* h, int64_t K, const void* amax, void* q, void* s,
+                                int barrier);
+/* a | b op (the GDN gates' bf16 projection, mono_gdn_ab's arithmetic): out [M][N] = x [M][K] w^T. */
+MONO_API int mono_program_ab(void* ops, int index, const void* x, int64_t x_stride, int64_t K, const void* w,
+                             int64_t N, void* out, int barrier);
+/* GDN op: delta = 0: the conv + gates step; delta = 1: the replay + verify delta rule, raw outputs bf16(o) to
+ * raw [M][HV * 128] (the gated norm is a rows op, mode 3). Operands as mono_gdn_step_deferred (ctl NULL: the
+ * committing form); the two ops of one step share `workspace` (mono_gdn_step_workspace bytes). HV <= 32. */
+MONO_API int mono_program_gdn(void* ops, int index, int delta, const void* qkv, const void* z, const void* a,
+                              const void* b, const void* conv_w, void* conv_state, const float* dt_bias,
+                              const float* g_decay, float* state, const void* gnorm_w, float gnorm_eps, float qscale,
+                              int64_t M, int64_t HK, int64_t HV, void* raw, const int32_t* ctl, const void* prev_qkv,
+                              const void* prev_a, const void* prev_b, void* save_qkv, void* save_a, void* save_b,
+                              int64_t qkv_stride, int64_t z_stride, int64_t ab_stride, void* workspace,
+                              size_t workspace_bytes, int barrier);
+/* Checks the ops and plans the launch for M rows (1..16); call before copying the ops to the device. */
+MONO_API int mono_program_plan(void* ops, int nops, int64_t M);
+/* Runs a planned program. ops: the host array; ops_device: the same bytes in device memory (16-byte aligned),
+ * or NULL to pass up to 16 ops by value. prefetch: L2 look-ahead in weight items per producer warp (0 = none).
+ * Every buffer an op names must stay valid until the launch completes. */
+MONO_API int mono_program_launch(const void* ops, const void* ops_device, int nops, int64_t M, void* workspace,
+                                 int prefetch, mono_stream_t stream);
+
+/* The GDN gates' a | b projection (the reference's in_proj_a / in_proj_b BF16 linear, csrc/mono_gdn.sycl:10-11):
+ * out[m][n] = bf16(sum_k x[m][k] w[n][k]), fp32 with every product and sum rounded on its own: lane l of the
+ * column's warp takes the 8-element pieces l + 32 j (j outer, element inner) from +0, then the xor butterfly
+ * (16, 8, 4, 2, 1). x bf16 [M][K] (row stride x_stride), w bf16 [N][K], out bf16 [M][N]; K % 256 == 0, M <= 16. */
+MONO_API int mono_gdn_ab(const void* x, int64_t x_stride, const void* w, int64_t K, int64_t M, int64_t N, void* out,
+                         mono_stream_t stream);
+
+/* layer_post (csrc/mono_layer.sycl:243-313) in one launch: y' = gate ? bf16(y * sigmoid_lut[gate]) : y (gate
+ * element (m, c) as the rows op, mode 1), x1 = bf16(x + GPTQ linear(act_quant(y'); o_w)), out = bf16(x1 +
+ * down(quant(h))), h = silu(gate_w(q1)) * up_w(q1), q1 = act_quant(RMSNorm(x1; norm_w, eps)) — the bits of
+ * mono_rowlin_gptq (mode gate / quant, residual x) followed by mono_mlp_gptq (residual). y bf16 [M][K] (K a
+ * multiple of 1024 up to 4096), x / out bf16 [M][H] (out may alias x). workspace:
+ * mono_layer_post_gptq_workspace(K, H, I) bytes, zero-filled before its first use. */
+MONO_API size_t mono_layer_post_gptq_workspace(int64_t K, int64_t H, int64_t I);
+MONO_API int mono_layer_post_gptq(const void* x, const void* y, int64_t K, const void* gate, int64_t gate_row_stride,
+                                  int64_t gate_head_stride, const void* sig_lut, const void* o_w, const void* norm_w,
+                                  float eps, const void* gate_w, const void* up_w, const void* down_w,
+                                  const void* silu_lut, int64_t M, int64_t H, int64_t I, void* out, void* workspace,
+                                  size_t workspace_bytes, mono_stream_t stream);
+
+/* layer_gdn (csrc/mono_gdn.sycl:5-20) in one launch: xn = RMSNorm(x; norm_in), proj | z = W4(act_quant(xn);
+ * qkv_w, z_w), a | b = mono_gdn_ab(xn; wab [2 HV][H]), the deferred GDN step (mono_gdn_step_deferred operands;
+ * ctl NULL: committing), core = the gated norm (rows op mode 3), then x1 = x + W4(act_quant(core); out_w) and the
+ * MLP block with norm_post (as mono_layer_post_gptq). 1 <= M <= 8; HV * 128 a multiple of 1024 up to 4096.
+ * workspace: mono_layer_gdn_gptq_workspace(M, H, I, HK, HV) bytes, zero-filled before its first use. */
+MONO_API size_t mono_layer_gdn_gptq_workspace(int64_t M, int64_t H, int64_t I, int64_t HK, int64_t HV);
+MONO_API int mono_layer_gdn_gptq(const void* x, const void* norm_in, float eps_in, const void* qkv_w, const void* z_w,
+                                 const void* wab, const void* conv_w, void* conv_state, const float* dt_bias,
+                                 const float* g_decay, float* state, const void* gnorm_w, float gnorm_eps, float qscale,
+                                 const int32_t* ctl, const void* prev_qkv, const void* prev_a, const void* prev_b,
+                                 void* save_qkv, void* save_a, void* save_b, const void* out_w, const void* norm_post,
+                                 float eps_post, const void* gate_w, const void* up_w, const void* down_w,
+                                 const void* silu_lut, int64_t M, int64_t H, int64_t I, int64_t HK, int64_t HV,
+                                 void* out, void* workspace, size_t workspace_bytes, mono_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
