@@ -19,10 +19,37 @@
 // gated RMSNorm core = bf16(bf16(raw * w * rsqrt(mean(raw^2) + eps)) * bf16(silu(z))). fp32 throughout;
 // results are checked against an fp64 reference with a stated tolerance.
 #include <cmath>
+#include <mutex>
 
 #include "gdn.cuh"
 
 namespace mono {
+
+__device__ uint16_t g_gdn_silu[65536];
+
+__global__ void gdn_silu_lut_kernel() {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < 65536) g_gdn_silu[i] = f32_to_bf16_bits(gdn_silu_formula(bf16_bits_to_f32(uint16_t(i))));
+}
+
+int ensure_gdn_silu_lut(cudaStream_t stream) {
+    static std::mutex mu;
+    static bool done[64] = {};
+    int dev = 0;
+    CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(MONO_EINVAL, "device index");
+    std::lock_guard<std::mutex> lock(mu);
+    if (done[dev]) return MONO_OK;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    CUDA_TRY(cudaStreamIsCapturing(stream, &cs));
+    if (cs != cudaStreamCaptureStatusNone)
+        return fail(MONO_EINVAL, "the first GDN launch on a device must not be inside a graph capture");
+    gdn_silu_lut_kernel<<<256, 256, 0, stream>>>();
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(cudaStreamSynchronize(stream));
+    done[dev] = true;
+    return MONO_OK;
+}
 
 __global__ void __launch_bounds__(256) gdn_conv_kernel(const GdnArgs A) {
     gdn_conv_item(A, blockIdx.x * blockDim.x + threadIdx.x);
@@ -33,6 +60,8 @@ __global__ void __launch_bounds__(kRG * kDH) gdn_delta_kernel(const GdnArgs A) {
     __shared__ float part[2][kRG][kDH];
     __shared__ float raw[kGdnMaxRows][kDH];
     __shared__ float sums[2 * kGdnMaxAll];
+    __shared__ float vsm[kGdnMaxAll][kDH];  // v of every row (the recurrence reads no global memory)
+    __shared__ float gsm[kGdnMaxAll][2];    // decay, beta of every row
     const int h = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int rg = tid / kDH, col = tid % kDH;
     const int kh = h / (A.HV / A.HK), KD = A.HK * kDH, M = A.M;
@@ -49,15 +78,17 @@ __global__ void __launch_bounds__(kRG * kDH) gdn_delta_kernel(const GdnArgs A) {
         const float qi = gdn_l2_inv(sums[2 * t]), ki = gdn_l2_inv(sums[2 * t + 1]);
         qn[t][d] = (bf16_bits_to_f32(A.conv_out[size_t(t) * A.C + kh * kDH + d]) * A.qscale) * qi;
         kn[t][d] = bf16_bits_to_f32(A.conv_out[size_t(t) * A.C + KD + kh * kDH + d]) * ki;
+        vsm[t][d] = bf16_bits_to_f32(A.conv_out[size_t(t) * A.C + 2 * KD + h * kDH + d]);
     }
+    if (tid < 2 * R) gsm[tid >> 1][tid & 1] = A.gates[((tid >> 1) * A.HV + h) * 2 + (tid & 1)];
     float st[kRPG];
     float* S = A.state + (size_t(h) * kDH + rg * kRPG) * kDH + col;
 #pragma unroll
     for (int r = 0; r < kRPG; ++r) st[r] = S[size_t(r) * kDH];
     __syncthreads();
     for (int t = 0; t < R; ++t) {
-        const float decay = A.gates[(t * A.HV + h) * 2], beta = A.gates[(t * A.HV + h) * 2 + 1];
-        const float v = bf16_bits_to_f32(A.conv_out[size_t(t) * A.C + 2 * KD + h * kDH + col]);
+        const float decay = gsm[t][0], beta = gsm[t][1];
+        const float v = vsm[t][col];
         float mem = 0.f;
 #pragma unroll
         for (int r = 0; r < kRPG; ++r) {
@@ -103,16 +134,33 @@ __global__ void __launch_bounds__(kRG * kDH) gdn_delta_kernel(const GdnArgs A) {
     }
 }
 
-// a | b projection: one warp per output column.
-__global__ void __launch_bounds__(128) gdn_ab_kernel(const uint16_t* x, int64_t x_stride, const uint16_t* w, int K,
+// a | b projection: the CTA copies the M rows into shared memory, then each of its 8 warps takes one column.
+__global__ void __launch_bounds__(256) gdn_ab_kernel(const uint16_t* x, int64_t x_stride, const uint16_t* w, int K,
                                                       int M, int N, uint16_t* out, int64_t out_stride) {
-    const int n = blockIdx.x * 4 + (threadIdx.x >> 5);
-    if (n < N) gdn_ab_column(x, x_stride, w, K, M, out, out_stride, n, threadIdx.x & 31);
+    extern __shared__ __align__(16) uint16_t xs[];
+    const int per = K >> 3;
+    for (int i = threadIdx.x; i < M * per; i += blockDim.x) {
+        const int m = i / per, c = i - m * per;
+        reinterpret_cast<uint4*>(xs + size_t(m) * K)[c] = __ldcg(reinterpret_cast<const uint4*>(x + size_t(m) * x_stride) + c);
+    }
+    __syncthreads();
+    const int n = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (n < N) gdn_ab_column<true>(xs, K, w, K, M, out, out_stride, n, threadIdx.x & 31);
 }
 
 int launch_gdn_ab(const uint16_t* x, int64_t x_stride, const uint16_t* w, int K, int M, int N, uint16_t* out,
                   int64_t out_stride, cudaStream_t stream) {
-    gdn_ab_kernel<<<(N + 3) / 4, 128, 0, stream>>>(x, x_stride, w, K, M, N, out, out_stride);
+    const size_t smem = size_t(M) * K * 2;
+    static std::mutex mu;
+    static size_t opt_in = 48 * 1024;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (smem > opt_in) {
+            CUDA_TRY(cudaFuncSetAttribute(gdn_ab_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+            opt_in = smem;
+        }
+    }
+    gdn_ab_kernel<<<(N + 7) / 8, 256, smem, stream>>>(x, x_stride, w, K, M, N, out, out_stride);
     CUDA_TRY(cudaGetLastError());
     return MONO_OK;
 }
@@ -124,6 +172,8 @@ size_t gdn_workspace_bytes(int M, int C, int HV) {
 }
 
 int launch_gdn_step(GdnArgs A, void* ws, cudaStream_t stream) {
+    const int rc = ensure_gdn_silu_lut(stream);
+    if (rc != MONO_OK) return rc;
     const size_t rows = size_t(A.M) + kGdnMaxRows;
     A.conv_out = static_cast<uint16_t*>(ws);
     A.gates = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + (rows * A.C * 2 + 255) / 256 * 256);

@@ -9,6 +9,12 @@ namespace mono {
 
 constexpr int kDH = 128, kRG = 4, kRPG = kDH / kRG, kGdnMaxRows = 8, kGdnMaxAll = 2 * kGdnMaxRows;
 
+// bf16(y / (1 + exp(-y))) of every bf16 pattern y (fp32 arithmetic): the conv and gated-norm SiLU as one load
+// each, the same bits as evaluating the formula per value. Built once per device (ensure_gdn_silu_lut).
+extern __device__ uint16_t g_gdn_silu[65536];
+__device__ __forceinline__ float gdn_silu_formula(float y) { return y / (1.f + expf(-y)); }
+__device__ __forceinline__ float gdn_silu(float y_bf16) { return bf16_bits_to_f32(g_gdn_silu[f32_to_bf16_bits(y_bf16)]); }
+
 __device__ __forceinline__ int gdn_pending(const GdnArgs& A) {
     if (A.ctl == nullptr) return 0;
     const int n = __ldcg(A.ctl);
@@ -28,6 +34,13 @@ __device__ __forceinline__ int gdn_slot(const GdnArgs& A, int i) {
 // in the committing form). All activations are read through L2 (they may have been written by this launch).
 __device__ __forceinline__ void gdn_conv_item(const GdnArgs& A, int i) {
     const int n = gdn_pending(A), R = n + A.M;
+    uint16_t sa = 0, sb = 0;
+    const bool saving = A.save_a != nullptr && i < A.M * A.HV;
+    if (saving) {
+        const int t = i / A.HV, h = i % A.HV;
+        sa = __ldcg(A.a + size_t(t) * A.ab_stride + h);
+        sb = __ldcg(A.b + size_t(t) * A.ab_stride + h);
+    }
     if (i < R * A.HV) {
         const int t = i / A.HV, h = i % A.HV;
         const uint16_t ab = t < n ? __ldcg(A.prev_a + size_t(gdn_slot(A, t)) * A.HV + h) : __ldcg(A.a + size_t(t - n) * A.ab_stride + h);
@@ -37,26 +50,31 @@ __device__ __forceinline__ void gdn_conv_item(const GdnArgs& A, int i) {
         A.gates[i * 2] = expf(A.g_decay[h] * sp);
         A.gates[i * 2 + 1] = bf16_round(1.f / (1.f + expf(-bf16_bits_to_f32(bb))));
     }
-    if (A.save_a != nullptr && i < A.M * A.HV) {
-        const int t = i / A.HV, h = i % A.HV;
-        A.save_a[i] = __ldcg(A.a + size_t(t) * A.ab_stride + h);
-        A.save_b[i] = __ldcg(A.b + size_t(t) * A.ab_stride + h);
+    if (saving) {
+        A.save_a[i] = sa;
+        A.save_b[i] = sb;
     }
     if (i >= A.C) return;
+    // every load first (the stores below may alias nothing the compiler can prove, so loads after a store
+    // would wait for it)
+    uint16_t raw[kGdnMaxAll];
     float w[4], hist[3 + kGdnMaxAll];
+#pragma unroll
+    for (int t = 0; t < kGdnMaxAll; ++t) {
+        raw[t] = 0;
+        if (t < n) raw[t] = __ldcg(A.prev_qkv + size_t(gdn_slot(A, t)) * A.C + i);
+        else if (t < R) raw[t] = __ldcg(A.qkv + size_t(t - n) * A.qkv_stride + i);
+    }
 #pragma unroll
     for (int d = 0; d < 4; ++d) w[d] = bf16_bits_to_f32(A.conv_w[size_t(i) * 4 + d]);
 #pragma unroll
     for (int r = 0; r < 3; ++r) hist[r] = bf16_bits_to_f32(A.conv_state[size_t(i) * 3 + r]);
 #pragma unroll
-    for (int t = 0; t < kGdnMaxAll; ++t) {
-        if (t < n) hist[3 + t] = bf16_bits_to_f32(__ldcg(A.prev_qkv + size_t(gdn_slot(A, t)) * A.C + i));
-        else if (t < R) {
-            const uint16_t v = __ldcg(A.qkv + size_t(t - n) * A.qkv_stride + i);
-            hist[3 + t] = bf16_bits_to_f32(v);
-            if (A.save_qkv != nullptr) A.save_qkv[size_t(t - n) * A.C + i] = v;
-        }
-    }
+    for (int t = 0; t < kGdnMaxAll; ++t) hist[3 + t] = bf16_bits_to_f32(raw[t]);
+    if (A.save_qkv != nullptr)
+#pragma unroll
+        for (int t = 0; t < kGdnMaxAll; ++t)
+            if (t >= n && t < R) A.save_qkv[size_t(t - n) * A.C + i] = raw[t];
 #pragma unroll
     for (int t = 0; t < kGdnMaxAll; ++t) {
         if (t >= R) break;
@@ -64,7 +82,7 @@ __device__ __forceinline__ void gdn_conv_item(const GdnArgs& A, int i) {
 #pragma unroll
         for (int d = 0; d < 4; ++d) sum = fmaf(hist[3 + t - d], w[3 - d], sum);
         const float y = bf16_round(sum);
-        A.conv_out[size_t(t) * A.C + i] = f32_to_bf16_bits(y / (1.f + expf(-y)));
+        A.conv_out[size_t(t) * A.C + i] = g_gdn_silu[f32_to_bf16_bits(y)];
     }
     const int keep = A.ctl != nullptr ? n : R;
 #pragma unroll
@@ -97,29 +115,35 @@ __device__ __forceinline__ float gdn_l2_inv(float sumsq) { return 1.f / fmaxf(sq
 __device__ __forceinline__ float gdn_norm_inv(float sumsq, float eps) { return 1.f / sqrtf(sumsq / float(kDH) + eps); }
 __device__ __forceinline__ uint16_t gdn_core(float raw, float w, float r, float z) {
     const float normed = bf16_round((raw * w) * r);
-    const float gz = bf16_round(z / (1.f + expf(-z)));
-    return f32_to_bf16_bits(normed * gz);
+    return f32_to_bf16_bits(normed * gdn_silu(z));  // z is a bf16 value
 }
 
 // a | b projection of one output column n (a warp): out[m][n] = bf16(sum over k of x[m][k] * w[n][k]) for the M
 // rows, fp32 with every product and sum rounded on its own (no fma): lane l takes the 8-element pieces
-// l + 32 j (j outer, element inner) from +0, then the xor butterfly (16, 8, 4, 2, 1). K % 256 == 0, M <= 16.
+// l + 32 j (j outer, element inner) from +0, then the xor butterfly (16, 8, 4, 2, 1). K % 256 == 0, K <= 4096,
+// M <= 16. XS: x in shared memory (else global, read through L2).
 // The role of the reference's in_proj_a / in_proj_b BF16 linear (csrc/mono_gdn.sycl:10-11).
+template <bool XS>
 __device__ __forceinline__ void gdn_ab_column(const uint16_t* __restrict__ x, int64_t x_stride,
                                               const uint16_t* __restrict__ w, int K, int M, uint16_t* out,
                                               int64_t out_stride, int n, int lane) {
+    const int J = K >> 8;
+    const uint4* wr = reinterpret_cast<const uint4*>(w + size_t(n) * K);
     float acc[16];
 #pragma unroll
     for (int m = 0; m < 16; ++m) acc[m] = 0.f;
-    const uint4* wr = reinterpret_cast<const uint4*>(w + size_t(n) * K);
-    for (int j = 0; j < (K >> 8); ++j) {
-        const int p = lane + 32 * j;
-        const uint4 wv = __ldg(wr + p);
+    uint4 wn = __ldg(wr + lane);
+    // a rolled loop (short code for a once-per-layer op), the next weight piece loaded one iteration ahead
+#pragma unroll 1
+    for (int j = 0; j < J; ++j) {
+        const uint4 wv = wn;
+        if (j + 1 < J) wn = __ldg(wr + lane + 32 * (j + 1));
         const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
         for (int m = 0; m < 16; ++m) {
             if (m < M) {
-                const uint4 xv = __ldcg(reinterpret_cast<const uint4*>(x + size_t(m) * x_stride) + p);
+                const uint4* xp = reinterpret_cast<const uint4*>(x + size_t(m) * x_stride) + lane + 32 * j;
+                const uint4 xv = XS ? *xp : __ldcg(xp);
                 const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
@@ -150,9 +174,23 @@ __device__ __forceinline__ void gdn_norm_quant_row(const uint16_t* __restrict__ 
                                                    uint16_t* __restrict__ core_out, int8_t* __restrict__ q,
                                                    float* __restrict__ s_out, float* red, float* hs, int tig, int wg) {
     const int lane = tig & 31, warp = tig >> 5, J = K >> 10, nh = K >> 7;
-    for (int h = warp; h < nh; h += 4) {
-        const float ss = gdn_sumsq128(raw + h * kDH, lane);
-        if (lane == 0) hs[h] = gdn_norm_inv(ss, eps);
+    {
+        // every head's values loaded before any sum (8 heads per warp at most)
+        float v[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                v[i][j] = warp + 4 * i < nh ? bf16_bits_to_f32(__ldcg(raw + (warp + 4 * i) * kDH + lane + 32 * j)) : 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            float ss = 0.f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) ss = fmaf(v[i][j], v[i][j], ss);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            if (lane == 0 && warp + 4 * i < nh) hs[warp + 4 * i] = gdn_norm_inv(ss, eps);
+        }
     }
     wg_sync(wg);
     uint32_t cw[kRowMaxPieces][4];  // the core values, bf16 pairs
@@ -193,6 +231,64 @@ __device__ __forceinline__ void gdn_norm_quant_row(const uint16_t* __restrict__ 
             reinterpret_cast<uint2*>(q)[tig + 128 * j] = quant8_perm(v, s);
         }
     wg_sync(wg);
+}
+
+// The gated norm + quantization of one raw row over NT threads of one CTA (gdn_norm_quant_row's arithmetic):
+// head h's norm factor by warp h % (NT / 32) (gdn_sumsq128 order), then the elements spread as the _cta row ops.
+// hs: >= 32 floats of shared memory.
+template <int NT, int BAR>
+__device__ __forceinline__ void gdn_norm_quant_row_cta(const uint16_t* __restrict__ raw, const uint16_t* __restrict__ z,
+                                                       const uint16_t* __restrict__ w, float eps, int K,
+                                                       uint16_t* __restrict__ core_out, int8_t* __restrict__ q,
+                                                       float* __restrict__ s_out, float* red, float* hs) {
+    constexpr int KP = RowPieces<NT>::kMax, NW = NT / 32, HPW = (32 + NW - 1) / NW;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, np = K >> 3, nh = K >> 7;
+    {
+        float v[HPW][4];
+#pragma unroll
+        for (int i = 0; i < HPW; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                v[i][j] = warp + NW * i < nh ? bf16_bits_to_f32(__ldcg(raw + (warp + NW * i) * kDH + lane + 32 * j)) : 0.f;
+#pragma unroll
+        for (int i = 0; i < HPW; ++i) {
+            float ss = 0.f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) ss = fmaf(v[i][j], v[i][j], ss);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            if (lane == 0 && warp + NW * i < nh) hs[warp + NW * i] = gdn_norm_inv(ss, eps);
+        }
+    }
+    float vals[KP][8];
+    uint4 rv[KP], zv[KP], wv[KP];
+#pragma unroll
+    for (int i = 0; i < KP; ++i)
+        if (tid + NT * i < np) {
+            const int c0 = (tid + NT * i) * 8;
+            rv[i] = __ldcg(reinterpret_cast<const uint4*>(raw + c0));
+            zv[i] = __ldcg(reinterpret_cast<const uint4*>(z + c0));
+            wv[i] = __ldg(reinterpret_cast<const uint4*>(w + c0 % kDH));
+        }
+    row_sync<NT, BAR>();
+#pragma unroll
+    for (int i = 0; i < KP; ++i)
+        if (tid + NT * i < np) {
+            const int c0 = (tid + NT * i) * 8;
+            const float r = hs[c0 / kDH];
+            const uint32_t ru[4] = {rv[i].x, rv[i].y, rv[i].z, rv[i].w}, zu[4] = {zv[i].x, zv[i].y, zv[i].z, zv[i].w},
+                           wu[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+            uint32_t o[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const auto f = [](uint32_t u, int e) { return __uint_as_float((e & 1) ? (u & 0xFFFF0000u) : (u << 16)); };
+                const uint16_t c = gdn_core(f(ru[e >> 1], e), f(wu[e >> 1], e), r, f(zu[e >> 1], e));
+                vals[i][e] = bf16_bits_to_f32(c);
+                o[e >> 1] |= uint32_t(c) << (16 * (e & 1));
+            }
+            if (core_out) reinterpret_cast<uint4*>(core_out)[tid + NT * i] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+    row_quant_pieces<NT, BAR>(vals, np, q, s_out, red);
 }
 
 }  // namespace mono

@@ -25,7 +25,7 @@ namespace mono {
 template <int MT, int CW, int PW>
 __global__ void __launch_bounds__((CW + PW) * 32, 1) mlp_kernel(const Program P, const MlpArgs A, const MlpShape Z) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ float red[CW / 4][16];
+    __shared__ float red[64];
     __shared__ unsigned rowmax[16];
     __shared__ int flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -51,7 +51,7 @@ __global__ void __launch_bounds__((CW + PW) * 32, 1) mlp_kernel(const Program P,
         produce_all<FMT_GPTQ, LAYOUT_TILED, PW>(P, ring, full, empty, S, warp - CW, lane);
         return;
     }
-    constexpr int NT = CW * 32, NWG = CW / 4;  // whole warp-groups do the row phases
+    constexpr int NT = CW * 32;
     pdl_wait();
     trace_stamp(1);
     unsigned epoch = 0;
@@ -59,12 +59,10 @@ __global__ void __launch_bounds__((CW + PW) * 32, 1) mlp_kernel(const Program P,
 
     // ---- P1: norm + quant of the rows (one warp-group of consumers per row) ----
     if (blockIdx.x == 0 && threadIdx.x < 16) A.amax2[threadIdx.x] = 0u;
-    {
-        const int wg = threadIdx.x >> 7, tig = threadIdx.x & 127;  // consumer warp-groups 0..2
-        for (int m = wg * int(gridDim.x) + int(blockIdx.x); wg < NWG && m < M; m += NWG * int(gridDim.x))
-            norm_quant_row(A.x + size_t(m) * A.H, A.norm_w, A.eps, A.H, nullptr, A.q1 + size_t(m) * A.H, A.s1 + m, red[wg],
-                           tig, wg);
-    }
+    // row m on CTA m, all consumer threads (rowops.cuh: the pinned order of the warp-group form)
+    for (int m = int(blockIdx.x); m < M; m += int(gridDim.x))
+        norm_quant_row_cta<NT, kConsumerBar>(A.x + size_t(m) * A.H, A.norm_w, A.eps, A.H, nullptr, A.q1 + size_t(m) * A.H,
+                                             A.s1 + m, red);
     trace_stamp(2);
     ok = grid_barrier_named<kConsumerBar, NT>(A.bar, epoch, &flag);
     trace_stamp(3);

@@ -103,34 +103,34 @@ __device__ __forceinline__ void program_produce(const Op* ops, int nops, int pre
 
 // Cold ops (rows, quantization, a | b, GDN) are separate functions, so their registers are not added to those
 // the GEMV path keeps live; each row mode is its own function for the same reason.
-template <int MODE>
-static __device__ __noinline__ void prog_rows_mode(const OpRows& r, int M, int NWG, float* red, float* hs) {
-    const int wg = threadIdx.x >> 7, tig = threadIdx.x & 127;
-    for (int m = wg * int(gridDim.x) + int(blockIdx.x); m < M; m += NWG * int(gridDim.x)) {
+template <int MODE, int CW>
+static __device__ __noinline__ void prog_rows_mode(const OpRows& r, int M, float* red, float* hs) {
+    constexpr int NT = CW * 32;
+    for (int m = int(blockIdx.x); m < M; m += int(gridDim.x)) {
         const uint16_t* xr = r.x + size_t(m) * r.x_stride;
         int8_t* q = r.q + size_t(m) * r.K;
         uint16_t* xn = r.xn_out ? r.xn_out + size_t(m) * r.K : nullptr;
         if constexpr (MODE == ROWS_GATE)
-            gate_quant_row(xr, r.gate + size_t(m) * r.gate_row_stride, r.gate_head_stride, r.lut, r.K, q, r.s + m, red, tig,
-                           wg);
+            gate_quant_row_cta<NT, kConsumerBar>(xr, r.gate + size_t(m) * r.gate_row_stride, r.gate_head_stride, r.lut,
+                                                 r.K, q, r.s + m, red);
         else if constexpr (MODE == ROWS_GDN)
-            gdn_norm_quant_row(xr, r.gate + size_t(m) * r.gate_row_stride, r.norm_w, r.eps, r.K, xn, q, r.s + m, red, hs,
-                               tig, wg);
+            gdn_norm_quant_row_cta<NT, kConsumerBar>(xr, r.gate + size_t(m) * r.gate_row_stride, r.norm_w, r.eps, r.K,
+                                                     xn, q, r.s + m, red, hs);
         else
-            norm_quant_row(xr, MODE == ROWS_NORM ? r.norm_w : nullptr, r.eps, r.K, xn, q, r.s + m, red, tig, wg);
+            norm_quant_row_cta<NT, kConsumerBar>(xr, MODE == ROWS_NORM ? r.norm_w : nullptr, r.eps, r.K, xn, q,
+                                                 r.s + m, red);
     }
 }
 
+// One row per CTA (all consumer threads of CTA m take row m).
 template <int CW>
-__device__ __forceinline__ void prog_rows(const OpRows& r, int M, float (*red)[16], float (*hs)[32]) {
-    constexpr int NWG = CW / 4;
-    const int wg = threadIdx.x >> 7;
+__device__ __forceinline__ void prog_rows(const OpRows& r, int M, float* red, float* hs) {
     if (r.zero != nullptr && blockIdx.x == 0 && threadIdx.x < 16) r.zero[threadIdx.x] = 0u;
-    if (wg >= NWG || wg * int(gridDim.x) + int(blockIdx.x) >= M) return;
-    if (r.mode == ROWS_GATE) prog_rows_mode<ROWS_GATE>(r, M, NWG, red[wg], hs[wg]);
-    else if (r.mode == ROWS_GDN) prog_rows_mode<ROWS_GDN>(r, M, NWG, red[wg], hs[wg]);
-    else if (r.mode == ROWS_NORM) prog_rows_mode<ROWS_NORM>(r, M, NWG, red[wg], hs[wg]);
-    else prog_rows_mode<ROWS_QUANT>(r, M, NWG, red[wg], hs[wg]);
+    if (int(blockIdx.x) >= M) return;
+    if (r.mode == ROWS_GATE) prog_rows_mode<ROWS_GATE, CW>(r, M, red, hs);
+    else if (r.mode == ROWS_GDN) prog_rows_mode<ROWS_GDN, CW>(r, M, red, hs);
+    else if (r.mode == ROWS_NORM) prog_rows_mode<ROWS_NORM, CW>(r, M, red, hs);
+    else prog_rows_mode<ROWS_QUANT, CW>(r, M, red, hs);
 }
 
 template <int MT, int CW>
@@ -198,11 +198,22 @@ static __device__ __noinline__ void prog_quant(const OpQuant& o, int M) {
 }
 
 template <int CW>
-static __device__ __noinline__ void prog_ab(const OpAb& a, int M) {
-    // output column n on warp n % CW of CTA G - 1 - n / CW: the last CTAs, which hold the fewest GEMV tiles
+static __device__ __noinline__ void prog_ab(const OpAb& a, int M, uint16_t* xsm) {
+    // output column n on warp n % CW of CTA G - 1 - n / CW: the last CTAs, which hold the fewest GEMV tiles. Such
+    // a CTA first copies the M normalized rows into shared memory (one round trip), then its warps take columns.
+    constexpr int NT = CW * 32;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, G = int(gridDim.x);
-    for (int n = (G - 1 - int(blockIdx.x)) * CW + warp; n < a.N; n += G * CW)
-        gdn_ab_column(a.x, a.x_stride, a.w, a.K, M, a.out, a.N, n, lane);
+    const int first = (G - 1 - int(blockIdx.x)) * CW;
+    if (first >= a.N) return;
+    const int per = a.K >> 3;  // 16-byte pieces per row
+    for (int i = threadIdx.x; i < M * per; i += NT) {
+        const int m = i / per, c = i - m * per;
+        reinterpret_cast<uint4*>(xsm + size_t(m) * a.K)[c] = __ldcg(reinterpret_cast<const uint4*>(a.x + size_t(m) * a.x_stride) + c);
+    }
+    consumer_sync<CW>();
+    for (int n = first + warp; n < a.N; n += G * CW)
+        gdn_ab_column<true>(xsm, a.K, a.w, a.K, M, a.out, a.N, n, lane);
+    consumer_sync<CW>();
 }
 
 template <int CW>
@@ -215,7 +226,8 @@ static __device__ __noinline__ void prog_gdn_conv(const GdnArgs& A) {
 // Shared scratch of the delta op: q / k rows of up to two heads, the row-group partials, the sums of squares.
 template <int CW>
 __host__ __device__ constexpr size_t delta_scratch_bytes() {
-    return (2 * 2 * kGdnMaxAll * kDH + 2 * kRG * (CW * 32 / kRG) + 2 * 2 * kGdnMaxAll) * sizeof(float);
+    return (2 * 2 * kGdnMaxAll * kDH + 2 * kRG * (CW * 32 / kRG) + 2 * 2 * kGdnMaxAll + kGdnMaxAll * (CW * 32 / kRG) +
+            kGdnMaxAll * 2 * 2) * sizeof(float);
 }
 
 // The delta rule of CTA b's value columns (gdn_delta_kernel's arithmetic, value columns spread over CTAs): raw
@@ -234,6 +246,8 @@ static __device__ __noinline__ void prog_gdn_delta(const GdnArgs& A, float* scra
     float* kn = qn + 2 * kGdnMaxAll * kDH;       // [2][kGdnMaxAll][kDH]
     float* part = kn + 2 * kGdnMaxAll * kDH;     // [2][kRG][CPC]
     float* sums = part + 2 * kRG * CPC;          // [2 heads][q, k][kGdnMaxAll]
+    float* vsm = sums + 2 * 2 * kGdnMaxAll;      // [kGdnMaxAll][CPC]: v of the CTA's columns
+    float* gsm = vsm + kGdnMaxAll * CPC;         // [kGdnMaxAll][2 heads][decay, beta]
     for (int pr = warp; pr < nhl * 2 * R; pr += CW) {
         const int hl = pr / (2 * R), rem = pr - hl * 2 * R, t = rem >> 1, which = rem & 1;
         const int kh = (h0 + hl) / grp;
@@ -248,6 +262,14 @@ static __device__ __noinline__ void prog_gdn_delta(const GdnArgs& A, float* scra
         qn[(hl * kGdnMaxAll + t) * kDH + d] =
             (bf16_bits_to_f32(__ldcg(A.conv_out + size_t(t) * A.C + kh * kDH + d)) * A.qscale) * qi;
         kn[(hl * kGdnMaxAll + t) * kDH + d] = bf16_bits_to_f32(__ldcg(A.conv_out + size_t(t) * A.C + KD + kh * kDH + d)) * ki;
+    }
+    for (int e = tid; e < R * CPC; e += NT) {
+        const int t = e / CPC, c = e % CPC;
+        vsm[e] = c0 + c < total ? bf16_bits_to_f32(__ldcg(A.conv_out + size_t(t) * A.C + 2 * KD + c0 + c)) : 0.f;
+    }
+    if (tid < R * nhl * 2) {
+        const int t = tid / (nhl * 2), hl = (tid >> 1) % nhl, which = tid & 1;
+        gsm[(t * 2 + hl) * 2 + which] = __ldcg(A.gates + (t * A.HV + h0 + hl) * 2 + which);
     }
     const int h = active ? gc / kDH : h0, col = gc % kDH, hl = h - h0;
     float st[kRPG];
@@ -267,9 +289,9 @@ static __device__ __noinline__ void prog_gdn_delta(const GdnArgs& A, float* scra
     for (int t = 0; t < R; ++t) {
         float mem = 0.f, decay = 1.f, beta = 0.f, v = 0.f;
         if (active) {
-            decay = __ldcg(A.gates + (t * A.HV + h) * 2);
-            beta = __ldcg(A.gates + (t * A.HV + h) * 2 + 1);
-            v = bf16_bits_to_f32(__ldcg(A.conv_out + size_t(t) * A.C + 2 * KD + h * kDH + col));
+            decay = gsm[(t * 2 + hl) * 2];
+            beta = gsm[(t * 2 + hl) * 2 + 1];
+            v = vsm[t * CPC + cl];
 #pragma unroll
             for (int r = 0; r < kRPG; ++r) {
                 st[r] *= decay;
@@ -304,8 +326,8 @@ static __device__ __noinline__ void prog_gdn_delta(const GdnArgs& A, float* scra
 template <int MT, int CW, int PW>
 __global__ void __launch_bounds__((CW + PW) * 32, 1) program_kernel(const __grid_constant__ ProgParam G, const MlpShape Z) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ float red[CW / 4][16];
-    __shared__ float hs[CW / 4][32];
+    __shared__ float red[64];
+    __shared__ float hs[32];
     __shared__ unsigned rowmax[16];
     __shared__ int flag;
     const Op* ops = G.by_value ? G.op : G.ext;
@@ -348,7 +370,7 @@ __global__ void __launch_bounds__((CW + PW) * 32, 1) program_kernel(const __grid
         } else if (kind == OP_QUANT) {
             prog_quant<CW>(op.q, M);
         } else if (kind == OP_AB) {
-            prog_ab<CW>(op.ab, M);
+            prog_ab<CW>(op.ab, M, reinterpret_cast<uint16_t*>(xsm));
         } else if (kind == OP_GDN_CONV) {
             prog_gdn_conv<CW>(op.gdn);
         } else if (kind == OP_GDN_DELTA) {
@@ -381,7 +403,11 @@ static int program_shape(const Op* ops, int nops, int M, MlpShape& Z) {
             const size_t b = size_t(M) * (ops[i].g.ph.K + 16);
             xb = b > xb ? b : xb;
         }
-        if (ops[i].kind == OP_GDN_DELTA) scratch = delta_scratch_bytes<12>();
+        if (ops[i].kind == OP_GDN_DELTA) scratch = scratch > delta_scratch_bytes<12>() ? scratch : delta_scratch_bytes<12>();
+        if (ops[i].kind == OP_AB) {
+            const size_t b = size_t(M) * ops[i].ab.K * 2;  // the staged rows of the a | b op
+            scratch = b > scratch ? b : scratch;
+        }
     }
     xb = scratch > xb ? scratch : xb;
     for (int c = 0; c < kStreamConfigs; ++c) {
@@ -421,7 +447,7 @@ static int check_op(const Op& op, int M) {
         MONO_CHECK(op.q.h && op.q.amax && op.q.q && op.q.s && op.q.K % 8 == 0 && aligned(op.q.h, 16), "quant op");
         return MONO_OK;
     case OP_AB:
-        MONO_CHECK(op.ab.x && op.ab.w && op.ab.out && op.ab.K % 256 == 0 && op.ab.x_stride % 8 == 0 && aligned(op.ab.x, 16) &&
+        MONO_CHECK(op.ab.x && op.ab.w && op.ab.out && op.ab.K % 256 == 0 && op.ab.K <= 4096 && op.ab.x_stride % 8 == 0 && aligned(op.ab.x, 16) &&
                        aligned(op.ab.w, 16),
                    "a|b op");
         return MONO_OK;
@@ -495,6 +521,12 @@ int launch_program(const Op* ops_host, const Op* ops_dev, int nops, int M, unsig
     MlpShape Z;
     const int c = program_shape(ops_host, nops, M, Z);
     MONO_CHECK(c >= 0, "program: not planned (mono_program_plan)");
+    for (int i = 0; i < nops; ++i)
+        if (ops_host[i].kind == OP_GDN_CONV || ops_host[i].kind == OP_GDN_DELTA || ops_host[i].kind == OP_ROWS) {
+            const int rc = ensure_gdn_silu_lut(stream);
+            if (rc != MONO_OK) return rc;
+            break;
+        }
     static_assert(sizeof(ProgParam) < 32000, "kernel parameter space");
     ProgParam G;
     std::memset(&G, 0, sizeof(G));

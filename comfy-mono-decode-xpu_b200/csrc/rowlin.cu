@@ -24,7 +24,7 @@ namespace mono {
 template <int MT, int CW, int PW>
 __global__ void __launch_bounds__((CW + PW) * 32, 1) rowlin_kernel(const Program P, const RowLinArgs A, const MlpShape Z) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ float red[CW / 4][16];
+    __shared__ float red[64];
     __shared__ int flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int M = P.M, S = Z.S, K = P.ph[0].K;
@@ -48,22 +48,20 @@ __global__ void __launch_bounds__((CW + PW) * 32, 1) rowlin_kernel(const Program
         produce_all<FMT_GPTQ, LAYOUT_TILED, PW>(P, ring, full, empty, S, warp - CW, lane);
         return;
     }
-    constexpr int NT = CW * 32, NWG = CW / 4;  // whole warp-groups do the row phases
+    constexpr int NT = CW * 32;
     pdl_wait();
     unsigned epoch = 0;
     bool ok = true;
-    {
-        const int wg = threadIdx.x >> 7, tig = threadIdx.x & 127;
-        for (int m = wg * int(gridDim.x) + int(blockIdx.x); wg < NWG && m < M; m += NWG * int(gridDim.x)) {
-            const uint16_t* xr = A.x + size_t(m) * K;
-            if (A.mode == ROWLIN_GATE)
-                gate_quant_row(xr, A.gate + size_t(m) * A.gate_row_stride, A.gate_head_stride, A.lut, K, A.q + size_t(m) * K,
-                               A.s + m, red[wg], tig, wg);
-            else
-                norm_quant_row(xr, A.mode == ROWLIN_NORM ? A.norm_w : nullptr, A.eps, K,
-                               A.xn_out ? A.xn_out + size_t(m) * K : nullptr, A.q + size_t(m) * K, A.s + m, red[wg],
-                               tig, wg);
-        }
+    // row m on CTA m, all consumer threads (rowops.cuh: the pinned order of the warp-group forms)
+    for (int m = int(blockIdx.x); m < M; m += int(gridDim.x)) {
+        const uint16_t* xr = A.x + size_t(m) * K;
+        if (A.mode == ROWLIN_GATE)
+            gate_quant_row_cta<NT, kConsumerBar>(xr, A.gate + size_t(m) * A.gate_row_stride, A.gate_head_stride, A.lut, K,
+                                                 A.q + size_t(m) * K, A.s + m, red);
+        else
+            norm_quant_row_cta<NT, kConsumerBar>(xr, A.mode == ROWLIN_NORM ? A.norm_w : nullptr, A.eps, K,
+                                                 A.xn_out ? A.xn_out + size_t(m) * K : nullptr, A.q + size_t(m) * K,
+                                                 A.s + m, red);
     }
     trace_stamp(1);
     ok = grid_barrier_named<kConsumerBar, NT>(A.bar, epoch, &flag);

@@ -11,8 +11,9 @@
 //   total  = W[0] + W[1] + W[2] + W[3]                                        sequential from +0
 //   r      = 1 / sqrt(total / H + eps)                                        (IEEE division, square root)
 //   out[i] = bf16((x[i] * r) * w[i])
-// Per-token GPTQ quantization: s = amax / 127, q = clamp(rint(x / s), -127, 127), s = 0 -> q = 0; q is
-// written in the engine's permuted activation layout (bytes 0 2 4 6 1 3 5 7 of every 8).
+// Per-token GPTQ quantization: s = amax / 127, q = clamp(rint(x / s), -127, 127) (x / s the IEEE quotient; see
+// quant_one), s = 0 -> q = 0; q is written in the engine's permuted activation layout (bytes 0 2 4 6 1 3 5 7 of
+// every 8).
 #pragma once
 #include "common.cuh"
 
@@ -24,9 +25,20 @@ __device__ __forceinline__ void wg_sync(int wg) {
     asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");
 }
 
-__device__ __forceinline__ int8_t quant_one(float v, float s) {
+// q = clamp(rint(fl(v / s)), -127, 127), fl = the IEEE fp32 quotient; s = 0 -> 0. inv = fl(1 / s).
+// a = fl(v * inv) lies within |v / s| 2^-23 (<= 3.1e-5 for |v / s| <= 256) of v / s, and fl(v / s) within
+// |v / s| 2^-24, so when a is farther than 2^-12 from every half-integer, rint(a) == rint(fl(v / s)) (rint only
+// changes at half-integers); otherwise (about 1 value in 2000), or when the product is out of that range, the
+// quotient itself is formed. Same results as dividing every value, at the cost of a multiply.
+// The quotient, out of line: the rare path stays a real branch instead of being evaluated for every value.
+static __device__ __noinline__ float quant_quotient(float v, float s) { return __fdiv_rn(v, s); }
+
+__device__ __forceinline__ int8_t quant_one(float v, float s, float inv) {
     if (!(s > 0.f)) return 0;
-    int q = __float2int_rn(__fdiv_rn(v, s));
+    const float a = __fmul_rn(v, inv), fa = fabsf(a);
+    float t = a;
+    if (!(fa <= 256.f && fabsf((fa - floorf(fa)) - 0.5f) > 0x1p-12f)) t = quant_quotient(v, s);
+    int q = __float2int_rn(t);
     q = q > 127 ? 127 : (q < -127 ? -127 : q);
     return int8_t(q);
 }
@@ -37,9 +49,10 @@ __device__ __forceinline__ int perm8(int i) { return (i & ~7) | ((i & 1) ? 4 + (
 // 8 quantized values -> the permuted 8-byte word
 __device__ __forceinline__ uint2 quant8_perm(const float (&v)[8], float s) {
     uint32_t lo = 0, hi = 0;
+    const float inv = s > 0.f ? __frcp_rn(s) : 0.f;
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-        const uint32_t q = uint32_t(uint8_t(quant_one(v[e], s)));
+        const uint32_t q = uint32_t(uint8_t(quant_one(v[e], s, inv)));
         if (e & 1) hi |= q << (8 * (e >> 1));
         else lo |= q << (8 * (e >> 1));
     }
@@ -153,6 +166,132 @@ __device__ __forceinline__ void gate_quant_row(const uint16_t* __restrict__ x, c
     for (int j = 0; j < kRowMaxPieces; ++j)
         if (j < J) reinterpret_cast<uint2*>(q)[tig + 128 * j] = quant8_perm(vals[j], s);
     wg_sync(wg);
+}
+
+// ---- the same row operations spread over NT threads of one CTA (named barrier BAR of those NT threads) ----
+// Same bits as the warp-group forms above: the RMSNorm sum of squares is still formed by threads t < 128 over
+// pieces t + 128 j (the pinned order); everything per element (normalize, gate, quantize) and the row maximum
+// (order-free) is spread over all NT threads, piece c on thread c % NT. red: >= 64 floats of shared memory.
+template <int NT>
+struct RowPieces {
+    static constexpr int kMax = (512 + NT - 1) / NT;  // 8-element pieces per thread (rows up to 4096)
+};
+
+template <int NT, int BAR>
+__device__ __forceinline__ void row_sync() {
+    asm volatile("bar.sync %0, %1;" ::"n"(BAR), "n"(NT) : "memory");
+}
+
+// Row maximum of |vals| over the NT threads and the quantization of the thread's pieces.
+template <int NT, int BAR>
+__device__ __forceinline__ void row_quant_pieces(const float (&vals)[RowPieces<NT>::kMax][8], int np, int8_t* q,
+                                                 float* s_out, float* red) {
+    constexpr int KP = RowPieces<NT>::kMax;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < KP; ++i)
+        if (tid + NT * i < np)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(vals[i][e]));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (lane == 0) red[16 + warp] = amax;
+    row_sync<NT, BAR>();
+    float m = 0.f;
+#pragma unroll
+    for (int w = 0; w < NT / 32; ++w) m = fmaxf(m, red[16 + w]);
+    const float s = __fdiv_rn(m, 127.f);
+    if (tid == 0) *s_out = s;
+#pragma unroll
+    for (int i = 0; i < KP; ++i)
+        if (tid + NT * i < np) reinterpret_cast<uint2*>(q)[tid + NT * i] = quant8_perm(vals[i], s);
+    row_sync<NT, BAR>();
+}
+
+// Optional RMSNorm (w != null) and per-token quantization of one row (norm_quant_row's arithmetic).
+template <int NT, int BAR>
+__device__ __forceinline__ void norm_quant_row_cta(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
+                                                   float eps, int H, uint16_t* __restrict__ xn_out, int8_t* __restrict__ q,
+                                                   float* __restrict__ s_out, float* red) {
+    constexpr int KP = RowPieces<NT>::kMax;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, np = H >> 3, J = H >> 10;
+    float vals[KP][8];
+    uint4 wv[KP];
+#pragma unroll
+    for (int i = 0; i < KP; ++i)
+        if (tid + NT * i < np) {
+            const uint4 v = __ldcg(reinterpret_cast<const uint4*>(x) + tid + NT * i);
+            if (w) wv[i] = __ldg(reinterpret_cast<const uint4*>(w) + tid + NT * i);
+            const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) vals[i][e] = __uint_as_float((e & 1) ? (u[e >> 1] & 0xFFFF0000u) : (u[e >> 1] << 16));
+        }
+    if (w) {
+        if (tid < 128) {  // the pinned sum of squares: thread t over pieces t + 128 j
+            uint4 sv[kRowMaxPieces];
+#pragma unroll
+            for (int j = 0; j < kRowMaxPieces; ++j)
+                if (j < J) sv[j] = __ldcg(reinterpret_cast<const uint4*>(x) + tid + 128 * j);
+            float p = 0.f;
+#pragma unroll
+            for (int j = 0; j < kRowMaxPieces; ++j)
+                if (j < J) {
+                    const uint32_t u[4] = {sv[j].x, sv[j].y, sv[j].z, sv[j].w};
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const float f = __uint_as_float((e & 1) ? (u[e >> 1] & 0xFFFF0000u) : (u[e >> 1] << 16));
+                        p = __fadd_rn(p, __fmul_rn(f, f));
+                    }
+                }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) p = __fadd_rn(p, __shfl_xor_sync(0xffffffffu, p, o));
+            if (lane == 0) red[warp] = p;
+        }
+        row_sync<NT, BAR>();
+        const float tot = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.f, red[0]), red[1]), red[2]), red[3]);
+        const float r = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, float(H)), eps)));
+#pragma unroll
+        for (int i = 0; i < KP; ++i)
+            if (tid + NT * i < np) {
+                const uint32_t u[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+                uint32_t o[4] = {0, 0, 0, 0};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float wf = __uint_as_float((e & 1) ? (u[e >> 1] & 0xFFFF0000u) : (u[e >> 1] << 16));
+                    const uint16_t b = f32_to_bf16_bits(__fmul_rn(__fmul_rn(vals[i][e], r), wf));
+                    vals[i][e] = bf16_bits_to_f32(b);
+                    o[e >> 1] |= uint32_t(b) << (16 * (e & 1));
+                }
+                if (xn_out) reinterpret_cast<uint4*>(xn_out)[tid + NT * i] = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+    }
+    row_quant_pieces<NT, BAR>(vals, np, q, s_out, red);
+}
+
+// Sigmoid gate and quantization of one row (gate_quant_row's arithmetic).
+template <int NT, int BAR>
+__device__ __forceinline__ void gate_quant_row_cta(const uint16_t* __restrict__ x, const uint16_t* __restrict__ gate,
+                                                   int64_t gate_head_stride, const uint16_t* __restrict__ lut, int H,
+                                                   int8_t* __restrict__ q, float* __restrict__ s_out, float* red) {
+    constexpr int KP = RowPieces<NT>::kMax;
+    const int tid = threadIdx.x, np = H >> 3;
+    float vals[KP][8];
+#pragma unroll
+    for (int i = 0; i < KP; ++i)
+        if (tid + NT * i < np) {
+            const int c0 = (tid + NT * i) * 8;
+            const uint4 xv = __ldcg(reinterpret_cast<const uint4*>(x + c0));
+            const uint4 gv = __ldcg(reinterpret_cast<const uint4*>(gate + (c0 >> 8) * gate_head_stride + (c0 & 255)));
+            const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w}, gu[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const uint32_t xb = (e & 1) ? (xu[e >> 1] >> 16) : (xu[e >> 1] & 0xFFFFu);
+                const uint32_t gb = (e & 1) ? (gu[e >> 1] >> 16) : (gu[e >> 1] & 0xFFFFu);
+                vals[i][e] = bf16_round(__fmul_rn(bf16_bits_to_f32(uint16_t(xb)), bf16_bits_to_f32(__ldg(lut + gb))));
+            }
+        }
+    row_quant_pieces<NT, BAR>(vals, np, q, s_out, red);
 }
 
 // Per-token quantization of a whole activation block x [M][K] bf16 by the first T threads of the CTA

@@ -108,7 +108,8 @@ __device__ __forceinline__ void issue_item(const PhaseDesc& p, int k, int sub, i
     if constexpr (LAYOUT == LAYOUT_TILED) {
         if (lane == 0) {
             mbar_arrive_expect_tx(full, kStageW + SB);
-            bulk_g2s(stage, w.q + (size_t(lt) * (p.K >> 10) + c) * (kStageW + SB), kStageW + SB, full);
+            bulk_g2s_hint(stage, w.q + (size_t(lt) * (p.K >> 10) + c) * (kStageW + SB), kStageW + SB, full,
+                          l2_evict_first_policy());
         }
     } else {
         const int g = lane >> 2, t = lane & 3;
