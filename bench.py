@@ -449,7 +449,7 @@ def run_decode(args):
     cfg = Qwen35Config()
     prompt = args.prompt
     model = Qwen35W4A8(cfg, dev, prompt_len=prompt, gen_tokens=max(512, args.steps * 8 + 64), seed=0x5EED + 4 + rank,
-                       fused=not args.op_by_op, prefetch=args.prefetch)
+                       fused=args.programs, prefetch=args.prefetch)
     stream = torch.cuda.Stream(dev)
     with torch.cuda.stream(stream):
         for _ in range(2):  # eager warm-up: workspaces, cuBLAS handles
@@ -533,8 +533,8 @@ def run_decode(args):
                        "layers": cfg.layers, "steps_per_s": round(args.steps / (ms * 1e-3), 2),
                        "tokens_per_step": round(toks / (args.steps * world), 3),
                        "l2": "inputs larger than L2 (6.6 GB of weights read per step)",
-                       "body": ("op-by-op launches" if args.op_by_op else
-                                f"{len(model.programs[0])} layer programs per step (prefetch {args.prefetch})"),
+                       "body": (f"{len(model.programs[0])} layer programs per step (prefetch {args.prefetch})"
+                                if args.programs else "one launch per fused op (rowlin / a|b / GDN / MLP / attention)"),
                        "parallelism": f"independent streams x{world}"},
             "roofline": {"bound": "hbm", "achieved": round(mlp_b / (mlp_us * 1e-6) / 1e9, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(mlp_b / (mlp_us * 1e-6) / 1e9 / hbm, 4), "peak_source": src,
@@ -696,7 +696,9 @@ def main():
     ap.add_argument("--prompt", type=int, default=1024, help="decode: committed prompt length (KV prefix)")
     ap.add_argument("--rows", type=int, default=8, help="activation rows (tree-verify rows)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
-    ap.add_argument("--op-by-op", action="store_true", help="decode: one launch per op instead of the layer programs")
+    ap.add_argument("--programs", action="store_true",
+                    help="decode: run the verify body as layer programs (one persistent launch per run of layers) "
+                         "instead of one launch per fused op")
     ap.add_argument("--prefetch", type=int, default=0, help="decode: L2 look-ahead of the layer programs (items)")
     args = ap.parse_args()
     if args.steps is None:

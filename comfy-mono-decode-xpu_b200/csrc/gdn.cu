@@ -134,18 +134,24 @@ __global__ void __launch_bounds__(kRG * kDH) gdn_delta_kernel(const GdnArgs A) {
     }
 }
 
-// a | b projection: the CTA copies the M rows into shared memory, then each of its 8 warps takes one column.
+// a | b projection: the CTA copies the M rows into shared memory; its 8 warps take the 4 quarters of 2 columns.
 __global__ void __launch_bounds__(256) gdn_ab_kernel(const uint16_t* x, int64_t x_stride, const uint16_t* w, int K,
                                                       int M, int N, uint16_t* out, int64_t out_stride) {
     extern __shared__ __align__(16) uint16_t xs[];
-    const int per = K >> 3;
+    __shared__ float qs[2][4][16];
+    const int per = K >> 3, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int i = threadIdx.x; i < M * per; i += blockDim.x) {
         const int m = i / per, c = i - m * per;
         reinterpret_cast<uint4*>(xs + size_t(m) * K)[c] = __ldcg(reinterpret_cast<const uint4*>(x + size_t(m) * x_stride) + c);
     }
     __syncthreads();
-    const int n = blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (n < N) gdn_ab_column<true>(xs, K, w, K, M, out, out_stride, n, threadIdx.x & 31);
+    const int cl = warp >> 2, q = warp & 3, n = blockIdx.x * 2 + cl;
+    if (n < N) gdn_ab_quarter(xs, w, K, M, n, q, lane, &qs[cl][q][0]);
+    __syncthreads();
+    if (threadIdx.x < 2 * M) {
+        const int c = threadIdx.x / M, m = threadIdx.x % M, nn = blockIdx.x * 2 + c;
+        if (nn < N) out[size_t(m) * out_stride + nn] = gdn_ab_combine(&qs[c][0][0], 16, m);
+    }
 }
 
 int launch_gdn_ab(const uint16_t* x, int64_t x_stride, const uint16_t* w, int K, int M, int N, uint16_t* out,
@@ -160,7 +166,7 @@ int launch_gdn_ab(const uint16_t* x, int64_t x_stride, const uint16_t* w, int K,
             opt_in = smem;
         }
     }
-    gdn_ab_kernel<<<(N + 7) / 8, 256, smem, stream>>>(x, x_stride, w, K, M, N, out, out_stride);
+    gdn_ab_kernel<<<(N + 1) / 2, 256, smem, stream>>>(x, x_stride, w, K, M, N, out, out_stride);
     CUDA_TRY(cudaGetLastError());
     return MONO_OK;
 }

@@ -118,51 +118,46 @@ __device__ __forceinline__ uint16_t gdn_core(float raw, float w, float r, float 
     return f32_to_bf16_bits(normed * gdn_silu(z));  // z is a bf16 value
 }
 
-// a | b projection of one output column n (a warp): out[m][n] = bf16(sum over k of x[m][k] * w[n][k]) for the M
-// rows, fp32 with every product and sum rounded on its own (no fma): lane l takes the 8-element pieces
-// l + 32 j (j outer, element inner) from +0, then the xor butterfly (16, 8, 4, 2, 1). K % 256 == 0, K <= 4096,
-// M <= 16. XS: x in shared memory (else global, read through L2).
-// The role of the reference's in_proj_a / in_proj_b BF16 linear (csrc/mono_gdn.sycl:10-11).
-template <bool XS>
-__device__ __forceinline__ void gdn_ab_column(const uint16_t* __restrict__ x, int64_t x_stride,
-                                              const uint16_t* __restrict__ w, int K, int M, uint16_t* out,
-                                              int64_t out_stride, int n, int lane) {
-    const int J = K >> 8;
-    const uint4* wr = reinterpret_cast<const uint4*>(w + size_t(n) * K);
-    float acc[16];
+// a | b projection (the role of the reference's in_proj_a / in_proj_b BF16 linear, csrc/mono_gdn.sycl:10-11), in
+// this build's pinned fp32 order, every product and sum rounded on its own (no fma):
+//   column n's K range is cut into 4 quarters of K / 1024 slices of 256; for quarter q, lane l of 32 sums
+//   x[m][k] * w[n][k] over its 8-element pieces l + 32 j (j ascending over the quarter's slices, elements in
+//   order) from +0, then the xor butterfly (16, 8, 4, 2, 1) gives Q_q;  out[m][n] = bf16(((Q_0 + Q_1) + Q_2) + Q_3).
+// One warp per (column, quarter): its weight pieces (<= 4 per lane) are all in flight at once; x [M][K] is read
+// from shared memory. K % 1024 == 0, K <= 4096, M <= 16.
+__device__ __forceinline__ void gdn_ab_quarter(const uint16_t* __restrict__ xs, const uint16_t* __restrict__ w, int K,
+                                               int M, int n, int q, int lane, float* qsum) {
+    const int J4 = K >> 10;
+    const uint4* wr = reinterpret_cast<const uint4*>(w + size_t(n) * K) + 32 * (q * J4) + lane;
+    uint4 wv[4];
 #pragma unroll
-    for (int m = 0; m < 16; ++m) acc[m] = 0.f;
-    uint4 wn = __ldg(wr + lane);
-    // a rolled loop (short code for a once-per-layer op), the next weight piece loaded one iteration ahead
+    for (int j = 0; j < 4; ++j)
+        if (j < J4) wv[j] = __ldg(wr + 32 * j);
 #pragma unroll 1
-    for (int j = 0; j < J; ++j) {
-        const uint4 wv = wn;
-        if (j + 1 < J) wn = __ldg(wr + lane + 32 * (j + 1));
-        const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
+    for (int m = 0; m < M; ++m) {
+        const uint4* xr = reinterpret_cast<const uint4*>(xs + size_t(m) * K) + 32 * (q * J4) + lane;
+        float acc = 0.f;
 #pragma unroll
-        for (int m = 0; m < 16; ++m) {
-            if (m < M) {
-                const uint4* xp = reinterpret_cast<const uint4*>(x + size_t(m) * x_stride) + lane + 32 * j;
-                const uint4 xv = XS ? *xp : __ldcg(xp);
-                const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w};
+        for (int j = 0; j < 4; ++j)
+            if (j < J4) {
+                const uint4 xv = xr[32 * j];
+                const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w}, wu[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
                     const float a = __uint_as_float((e & 1) ? (xu[e >> 1] & 0xFFFF0000u) : (xu[e >> 1] << 16));
                     const float b = __uint_as_float((e & 1) ? (wu[e >> 1] & 0xFFFF0000u) : (wu[e >> 1] << 16));
-                    acc[m] = __fadd_rn(acc[m], __fmul_rn(a, b));
+                    acc = __fadd_rn(acc, __fmul_rn(a, b));
                 }
             }
-        }
-    }
 #pragma unroll
-    for (int m = 0; m < 16; ++m) {
-        if (m < M) {
-            float v = acc[m];
-#pragma unroll
-            for (int o = 16; o; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-            if (lane == 0) out[size_t(m) * out_stride + n] = f32_to_bf16_bits(v);
-        }
+        for (int o = 16; o; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+        if (lane == 0) qsum[m] = acc;
     }
+}
+// out[m][n] from the four quarter sums of one column (qs[q * stride + m]).
+__device__ __forceinline__ uint16_t gdn_ab_combine(const float* qs, int stride, int m) {
+    return f32_to_bf16_bits(
+        __fadd_rn(__fadd_rn(__fadd_rn(qs[m], qs[stride + m]), qs[2 * stride + m]), qs[3 * stride + m]));
 }
 
 // Gated RMSNorm of every head of one raw row (K = heads * 128 <= 4096) and the row's per-token quantization, by

@@ -199,20 +199,26 @@ static __device__ __noinline__ void prog_quant(const OpQuant& o, int M) {
 
 template <int CW>
 static __device__ __noinline__ void prog_ab(const OpAb& a, int M, uint16_t* xsm) {
-    // output column n on warp n % CW of CTA G - 1 - n / CW: the last CTAs, which hold the fewest GEMV tiles. Such
-    // a CTA first copies the M normalized rows into shared memory (one round trip), then its warps take columns.
-    constexpr int NT = CW * 32;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, G = int(gridDim.x);
-    const int first = (G - 1 - int(blockIdx.x)) * CW;
+    // the last CTAs take CW / 4 columns each (the 4 quarters of a column on 4 warps, gdn.cuh gdn_ab_quarter): they
+    // hold the fewest GEMV tiles. Such a CTA first copies the M normalized rows into shared memory.
+    constexpr int NT = CW * 32, CPA = CW / 4;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int first = (int(gridDim.x) - 1 - int(blockIdx.x)) * CPA;
     if (first >= a.N) return;
+    float* qs = reinterpret_cast<float*>(xsm + size_t(M) * a.K);  // [CPA][4][16]
     const int per = a.K >> 3;  // 16-byte pieces per row
     for (int i = threadIdx.x; i < M * per; i += NT) {
         const int m = i / per, c = i - m * per;
         reinterpret_cast<uint4*>(xsm + size_t(m) * a.K)[c] = __ldcg(reinterpret_cast<const uint4*>(a.x + size_t(m) * a.x_stride) + c);
     }
     consumer_sync<CW>();
-    for (int n = first + warp; n < a.N; n += G * CW)
-        gdn_ab_column<true>(xsm, a.K, a.w, a.K, M, a.out, a.N, n, lane);
+    const int cl = warp >> 2, q = warp & 3;
+    if (cl < CPA && first + cl < a.N) gdn_ab_quarter(xsm, a.w, a.K, M, first + cl, q, lane, qs + (cl * 4 + q) * 16);
+    consumer_sync<CW>();
+    if (int(threadIdx.x) < CPA * M) {
+        const int c = threadIdx.x / M, m = threadIdx.x % M;
+        if (first + c < a.N) a.out[size_t(m) * a.N + first + c] = gdn_ab_combine(qs + c * 64, 16, m);
+    }
     consumer_sync<CW>();
 }
 
@@ -405,7 +411,7 @@ static int program_shape(const Op* ops, int nops, int M, MlpShape& Z) {
         }
         if (ops[i].kind == OP_GDN_DELTA) scratch = scratch > delta_scratch_bytes<12>() ? scratch : delta_scratch_bytes<12>();
         if (ops[i].kind == OP_AB) {
-            const size_t b = size_t(M) * ops[i].ab.K * 2;  // the staged rows of the a | b op
+            const size_t b = size_t(M) * ops[i].ab.K * 2 + 12 / 4 * 4 * 16 * 4;  // staged rows + quarter sums
             scratch = b > scratch ? b : scratch;
         }
     }
@@ -447,7 +453,7 @@ static int check_op(const Op& op, int M) {
         MONO_CHECK(op.q.h && op.q.amax && op.q.q && op.q.s && op.q.K % 8 == 0 && aligned(op.q.h, 16), "quant op");
         return MONO_OK;
     case OP_AB:
-        MONO_CHECK(op.ab.x && op.ab.w && op.ab.out && op.ab.K % 256 == 0 && op.ab.K <= 4096 && op.ab.x_stride % 8 == 0 && aligned(op.ab.x, 16) &&
+        MONO_CHECK(op.ab.x && op.ab.w && op.ab.out && op.ab.K % 1024 == 0 && op.ab.K <= 4096 && op.ab.x_stride % 8 == 0 && aligned(op.ab.x, 16) &&
                        aligned(op.ab.w, 16),
                    "a|b op");
         return MONO_OK;

@@ -96,9 +96,9 @@ int set_quant(Op& op, const void* h, int64_t K, const void* amax, void* q, void*
 }
 
 int set_ab(Op& op, const void* x, int64_t x_stride, int64_t K, const void* w, int64_t N, void* out, int barrier) {
-    MONO_CHECK(x && w && out && K % 256 == 0 && K > 0 && K <= 4096 && N >= 1 && x_stride >= K && x_stride % 8 == 0 &&
+    MONO_CHECK(x && w && out && K % 1024 == 0 && K > 0 && K <= 4096 && N >= 1 && x_stride >= K && x_stride % 8 == 0 &&
                    aligned(x, 16) && aligned(w, 16),
-               "a|b op: K a multiple of 256 up to 4096, 16-byte aligned rows");
+               "a|b op: K a multiple of 1024 up to 4096, 16-byte aligned rows");
     std::memset(&op, 0, sizeof(op));
     op.kind = OP_AB;
     op.barrier = barrier != 0;
@@ -238,8 +238,8 @@ int mono_program_launch(const void* ops, const void* ops_device, int nops, int64
 int mono_gdn_ab(const void* x, int64_t x_stride, const void* w, int64_t K, int64_t M, int64_t N, void* out,
                 mono_stream_t stream) {
     MONO_CHECK(x && w && out, "null operand");
-    MONO_CHECK(M >= 1 && M <= 16 && N >= 1 && K % 256 == 0 && K > 0 && K <= 4096 && x_stride >= K && x_stride % 8 == 0,
-               "1 <= M <= 16, K a multiple of 256 up to 4096");
+    MONO_CHECK(M >= 1 && M <= 16 && N >= 1 && K % 1024 == 0 && K > 0 && K <= 4096 && x_stride >= K && x_stride % 8 == 0,
+               "1 <= M <= 16, K a multiple of 1024 up to 4096");
     MONO_CHECK(aligned(x, 16) && aligned(w, 16), "16-byte aligned rows");
     return launch_gdn_ab(static_cast<const uint16_t*>(x), x_stride, static_cast<const uint16_t*>(w), int(K), int(M), int(N),
                          static_cast<uint16_t*>(out), N, reinterpret_cast<cudaStream_t>(stream));

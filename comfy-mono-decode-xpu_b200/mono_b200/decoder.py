@@ -96,7 +96,7 @@ class Qwen35W4A8:
     """Weights and decode state of one stream on one device."""
 
     def __init__(self, cfg: Qwen35Config, device, prompt_len: int, gen_tokens: int = 512, seed: int = 0x5EED + 4,
-                 fused: bool = True, prefetch: int = 0):
+                 fused: bool = False, prefetch: int = 0):
         self.cfg, self.dev = cfg, torch.device(device)
         c, dev = cfg, self.dev
         g = torch.Generator(device=dev).manual_seed(seed)

@@ -80,21 +80,28 @@ def gdn_step(qkv, z, a, b, conv_w, conv_state, dt_bias, g_decay, state, gnorm_w,
 
 def ab_projection(x_bits, w_bits):
     """The GDN gates' a | b projection in the kernel's pinned fp32 order (mono_gdn_ab; the role of the reference's
-    in_proj_a / in_proj_b BF16 linear, csrc/mono_gdn.sycl:10-11): out[m][n] = bf16(sum_k x[m][k] w[n][k]) with
-    every product and sum rounded to fp32 on its own; lane l of 32 takes the 8-element pieces l + 32 j (j outer,
-    element inner) from +0, then the xor butterfly (16, 8, 4, 2, 1). x bf16 bits [M, K], w bf16 bits [N, K]
-    (K % 256 == 0). Returns bf16 bits [M, N]. Bit-exact by construction (numpy float32 rounds each op RNE)."""
+    in_proj_a / in_proj_b BF16 linear, csrc/mono_gdn.sycl:10-11): out[m][n] = bf16(sum_k x[m][k] w[n][k]) with every
+    product and sum rounded to fp32 on its own. K is cut into 4 quarters of K / 1024 slices of 256; in quarter q,
+    lane l of 32 sums its 8-element pieces l + 32 j (j ascending over the quarter's slices, elements in order)
+    from +0, then the xor butterfly (16, 8, 4, 2, 1) gives Q_q; out = bf16(((Q_0 + Q_1) + Q_2) + Q_3). x bf16
+    bits [M, K], w bf16 bits [N, K] (K % 1024 == 0). Returns bf16 bits [M, N]. Bit-exact by construction (numpy
+    float32 rounds each operation to nearest even)."""
     from .numerics import f32_to_bf16_bits
     x = bf16_bits_to_f32(np.asarray(x_bits)).astype(np.float32)
     w = bf16_bits_to_f32(np.asarray(w_bits)).astype(np.float32)
     M, K = x.shape
     N, J = w.shape[0], K // 256
+    J4 = J // 4
     xr, wr = x.reshape(M, J, 32, 8), w.reshape(N, J, 32, 8)
-    acc = np.zeros((M, N, 32), dtype=np.float32)
-    for j in range(J):
-        for e in range(8):
-            acc = (acc + (xr[:, None, j, :, e] * wr[None, :, j, :, e]).astype(np.float32)).astype(np.float32)
     lanes = np.arange(32)
-    for o in (16, 8, 4, 2, 1):
-        acc = (acc + acc[:, :, lanes ^ o]).astype(np.float32)
-    return f32_to_bf16_bits(acc[:, :, 0])
+    Q = []
+    for q in range(4):
+        acc = np.zeros((M, N, 32), dtype=np.float32)
+        for j in range(q * J4, (q + 1) * J4):
+            for e in range(8):
+                acc = (acc + (xr[:, None, j, :, e] * wr[None, :, j, :, e]).astype(np.float32)).astype(np.float32)
+        for o in (16, 8, 4, 2, 1):
+            acc = (acc + acc[:, :, lanes ^ o]).astype(np.float32)
+        Q.append(acc[:, :, 0])
+    out = (((Q[0] + Q[1]).astype(np.float32) + Q[2]).astype(np.float32) + Q[3]).astype(np.float32)
+    return f32_to_bf16_bits(out)
