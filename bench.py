@@ -538,7 +538,7 @@ def run_decode(args):
                        "parallelism": f"independent streams x{world}"},
             "roofline": {"bound": "hbm", "achieved": round(mlp_b / (mlp_us * 1e-6) / 1e9, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(mlp_b / (mlp_us * 1e-6) / 1e9 / hbm, 4), "peak_source": src,
-                         "traffic": profile_traffic("mlp_kernel_m8"),
+                         "traffic": profile_traffic("mlp_kernel_m5"),
                          "kernel": "mlp_kernel<MT=1> (fused MLP block, the step's dominant kernel), M = 5 verify rows",
                          "us_per_launch": round(mlp_us, 3), "algorithmic_bytes_per_launch": mlp_b},
             "step_roofline": {"achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
