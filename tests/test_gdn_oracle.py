@@ -22,3 +22,39 @@ def test_conv_state_is_the_newest_inputs_and_delta_rule_reduces_to_outer_product
     assert np.array_equal(new_hist, qkv[-3:].T)
     # zero conv weights: every conv output is silu(0) = 0, so k = 0 and the state stays 0
     assert np.abs(S).max() == 0 and np.abs(core).max() == 0
+
+
+def test_ab_projection_follows_its_pinned_order():
+    """The a|b oracle against a direct restatement of its order (one column, scalar loops) and against fp64 within
+    one bf16 rounding plus the fp32 accumulation error."""
+    import numpy as np
+
+    from oracle.gdn import ab_projection
+    from oracle.numerics import bf16_bits_to_f32, f32_to_bf16_bits
+    r = np.random.default_rng(7)
+    M, N, K = 2, 3, 2048
+    x = f32_to_bf16_bits(r.standard_normal((M, K)).astype(np.float32))
+    w = f32_to_bf16_bits((r.standard_normal((N, K)) * 0.05).astype(np.float32))
+    got = ab_projection(x, w)
+    xf, wf = bf16_bits_to_f32(x).astype(np.float32), bf16_bits_to_f32(w).astype(np.float32)
+    J4 = K // 1024
+    for m in range(M):
+        for n in range(N):
+            Q = []
+            for q in range(4):
+                lanes = []
+                for lane in range(32):
+                    acc = np.float32(0)
+                    for j in range(q * J4, (q + 1) * J4):
+                        for e in range(8):
+                            k = 256 * j + 8 * lane + e
+                            acc = np.float32(acc + np.float32(xf[m, k] * wf[n, k]))
+                    lanes.append(acc)
+                v = np.array(lanes, dtype=np.float32)
+                for o in (16, 8, 4, 2, 1):
+                    v = (v + v[np.arange(32) ^ o]).astype(np.float32)
+                Q.append(v[0])
+            ref = np.float32(np.float32(np.float32(Q[0] + Q[1]) + Q[2]) + Q[3])
+            assert got[m, n] == f32_to_bf16_bits(np.array([ref], dtype=np.float32))[0]
+    exact = xf.astype(np.float64) @ wf.astype(np.float64).T
+    assert np.allclose(bf16_bits_to_f32(got), exact, rtol=2 ** -7, atol=1e-4)
