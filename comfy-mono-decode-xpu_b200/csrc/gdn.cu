@@ -140,13 +140,15 @@ __global__ void __launch_bounds__(256) gdn_ab_kernel(const uint16_t* x, int64_t 
     extern __shared__ __align__(16) uint16_t xs[];
     __shared__ float qs[2][4][16];
     const int per = K >> 3, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int cl = warp >> 2, q = warp & 3, n = blockIdx.x * 2 + cl;
+    uint4 wv[4];
+    if (n < N) gdn_ab_load_w(w, K, n, q, lane, wv);  // in flight while the rows are copied
     for (int i = threadIdx.x; i < M * per; i += blockDim.x) {
         const int m = i / per, c = i - m * per;
         reinterpret_cast<uint4*>(xs + size_t(m) * K)[c] = __ldcg(reinterpret_cast<const uint4*>(x + size_t(m) * x_stride) + c);
     }
     __syncthreads();
-    const int cl = warp >> 2, q = warp & 3, n = blockIdx.x * 2 + cl;
-    if (n < N) gdn_ab_quarter(xs, w, K, M, n, q, lane, &qs[cl][q][0]);
+    if (n < N) gdn_ab_quarter(xs, wv, K, M, q, lane, &qs[cl][q][0]);
     __syncthreads();
     if (threadIdx.x < 2 * M) {
         const int c = threadIdx.x / M, m = threadIdx.x % M, nn = blockIdx.x * 2 + c;

@@ -125,14 +125,17 @@ __device__ __forceinline__ uint16_t gdn_core(float raw, float w, float r, float 
 //   order) from +0, then the xor butterfly (16, 8, 4, 2, 1) gives Q_q;  out[m][n] = bf16(((Q_0 + Q_1) + Q_2) + Q_3).
 // One warp per (column, quarter): its weight pieces (<= 4 per lane) are all in flight at once; x [M][K] is read
 // from shared memory. K % 1024 == 0, K <= 4096, M <= 16.
-__device__ __forceinline__ void gdn_ab_quarter(const uint16_t* __restrict__ xs, const uint16_t* __restrict__ w, int K,
-                                               int M, int n, int q, int lane, float* qsum) {
+// The quarter's weight pieces of column n (issued before anything waits on them).
+__device__ __forceinline__ void gdn_ab_load_w(const uint16_t* __restrict__ w, int K, int n, int q, int lane, uint4 (&wv)[4]) {
     const int J4 = K >> 10;
     const uint4* wr = reinterpret_cast<const uint4*>(w + size_t(n) * K) + 32 * (q * J4) + lane;
-    uint4 wv[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j)
         if (j < J4) wv[j] = __ldg(wr + 32 * j);
+}
+__device__ __forceinline__ void gdn_ab_quarter(const uint16_t* __restrict__ xs, const uint4 (&wv)[4], int K, int M, int q,
+                                               int lane, float* qsum) {
+    const int J4 = K >> 10;
 #pragma unroll 1
     for (int m = 0; m < M; ++m) {
         const uint4* xr = reinterpret_cast<const uint4*>(xs + size_t(m) * K) + 32 * (q * J4) + lane;

@@ -206,14 +206,16 @@ static __device__ __noinline__ void prog_ab(const OpAb& a, int M, uint16_t* xsm)
     const int first = (int(gridDim.x) - 1 - int(blockIdx.x)) * CPA;
     if (first >= a.N) return;
     float* qs = reinterpret_cast<float*>(xsm + size_t(M) * a.K);  // [CPA][4][16]
+    const int cl = warp >> 2, q = warp & 3;
+    uint4 wv[4];
+    if (cl < CPA && first + cl < a.N) gdn_ab_load_w(a.w, a.K, first + cl, q, lane, wv);  // in flight during the copy
     const int per = a.K >> 3;  // 16-byte pieces per row
     for (int i = threadIdx.x; i < M * per; i += NT) {
         const int m = i / per, c = i - m * per;
         reinterpret_cast<uint4*>(xsm + size_t(m) * a.K)[c] = __ldcg(reinterpret_cast<const uint4*>(a.x + size_t(m) * a.x_stride) + c);
     }
     consumer_sync<CW>();
-    const int cl = warp >> 2, q = warp & 3;
-    if (cl < CPA && first + cl < a.N) gdn_ab_quarter(xsm, a.w, a.K, M, first + cl, q, lane, qs + (cl * 4 + q) * 16);
+    if (cl < CPA && first + cl < a.N) gdn_ab_quarter(xsm, wv, a.K, M, q, lane, qs + (cl * 4 + q) * 16);
     consumer_sync<CW>();
     if (int(threadIdx.x) < CPA * M) {
         const int c = threadIdx.x / M, m = threadIdx.x % M;
