@@ -416,6 +416,87 @@ def run_mlp(args):
         dist.destroy_process_group()
 
 
+def run_topk_rows(args):
+    """The verify sampling's top-k filter (the reference's topk_rows): exact top-64 of 8 fp32
+    rows of 248,320 logits per call (the reference's "8 x 248k"); 32 input copies (254 MB) cycled so every call
+    reads its rows from HBM. GB/s of row bytes read; parity checked against the oracle on the first call."""
+    import numpy as np
+    import torch
+
+    from mono_b200 import _C
+    from oracle.topk import topk_rows as ref_topk_rows
+
+    R, N, k, copies, per_step = 8, 248320, 64, 32, 32
+    rank, world, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    g = torch.Generator().manual_seed(0x5EED + 8 + rank)
+    host = torch.randn(R, N, generator=g) * 3
+    xs = [(host + c * 1e-3).to(dev) if c else host.to(dev) for c in range(copies)]
+    rv, ri = ref_topk_rows(host.numpy(), k)
+    v, i = _C.topk_rows(xs[0], k)
+    ok = bool(np.array_equal(i.cpu().numpy(), ri) and np.array_equal(v.cpu().numpy(), rv))
+    stream = torch.cuda.Stream(dev)
+
+    def step():
+        for j in range(per_step):
+            _C.topk_rows(xs[j % copies], k)
+
+    with torch.cuda.stream(stream):
+        step()
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(stream)
+        stream.synchronize()
+    ms = e0.elapsed_time(e1)
+    b = R * N * 4 + R * k * 12
+    us = ms * 1e3 / (args.steps * per_step)
+    hbm, src = peaks()
+    # e2e: host rows in, values / indices back, per call through the public op
+    hx = host.pin_memory()
+    hv = torch.empty(R, k).pin_memory()
+    hi = torch.empty(R, k, dtype=torch.int64).pin_memory()
+    n_e2e = 16
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        f0.record(stream)
+        for _ in range(n_e2e):
+            vv, ii = _C.topk_rows(hx.to(dev, non_blocking=True), k)
+            hv.copy_(vv, non_blocking=True)
+            hi.copy_(ii, non_blocking=True)
+        f1.record(stream)
+    stream.synchronize()
+    e2e_us = f0.elapsed_time(f1) * 1e3 / n_e2e
+    if rank == 0:
+        print(json.dumps({
+            "metric": "topk_rows GB/s (verify sampling top-k, 8 x 248320 fp32, k = 64)",
+            "value": round(b / (us * 1e-6) / 1e9, 1), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int64 ranks (fp32 keys)",
+            "data": "synthetic (seeded N(0, 3) logits)",
+            "config": {"workload": "exact top-64 of 8 rows x 248320 fp32 (the reference's topk_rows)",
+                       "calls_per_step": per_step, "copies": copies,
+                       "l2": "inputs larger than L2 (32 copies = 254 MB cycled)", "parity_gate": ok},
+            "roofline": {"bound": "hbm", "achieved": round(b / (us * 1e-6) / 1e9, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(b / (us * 1e-6) / 1e9 / hbm, 4), "peak_source": src, "traffic": None,
+                         "kernel": "topk_rows_partial + topk_rows_final", "us_per_call": round(us, 3),
+                         "algorithmic_bytes_per_call": b},
+            "e2e": {"value": round(b / (e2e_us * 1e-6) / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": R * N * 4,
+                    "d2h_bytes_per_step": R * k * 12},
+            "gpu_launches": args.steps * per_step * 2, "clocks": clk.summary()}), flush=True)
+
+
 def reduce_time_and_count(ms, count, device, world):
     """Max of the device time and sum of the counted units over the ranks (every rank calls it, in the same
     order); identity on one rank."""
@@ -692,7 +773,7 @@ def main():
     ap.add_argument("--steps", type=int, default=None, help="default: 200 (decode), 2000 (gemv, mlp)")
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["gemv", "mlp", "decode"])
+    ap.add_argument("--workload", default="decode", choices=["gemv", "mlp", "decode", "topk_rows"])
     ap.add_argument("--prompt", type=int, default=1024, help="decode: committed prompt length (KV prefix)")
     ap.add_argument("--rows", type=int, default=8, help="activation rows (tree-verify rows)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
@@ -711,6 +792,8 @@ def main():
         run_mlp(args)
     elif args.workload == "decode":
         run_decode(args)
+    elif args.workload == "topk_rows":
+        run_topk_rows(args)
     else:
         run_ours(args)
 

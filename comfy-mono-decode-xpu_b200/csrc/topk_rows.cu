@@ -1,0 +1,211 @@
+// Exact top-k (k <= 64) of a few long rows: the verify step's sampling filter (the role of the reference's
+// topk_rows, csrc/topk_rows.sycl:2-17). The result is torch.topk of the rows' fp32 values: per row the k
+// largest by the radix key (the fp32 bits with the sign flipped: -0 below +0, no NaN case), sorted descending,
+// ties in the torch-XPU gather order. Each element gets a unique 64-bit rank (csrc/topk_rows.sycl:34-42):
+//   key = bits ^ (sign ? 0xFFFFFFFF : 0x80000000);   off = i % 32768;
+//   g = (i / 32768) << 15 | ((off % 4096) / 4) << 5 | (off / 4096) << 2 | off % 4
+//   rank = key << 32 | (0xFFFFFFFF - g)        (larger = earlier in the output)
+// Kernel 1, CTA = (row, slice): each warp keeps the 64 best ranks of its elements sorted in registers (lane l
+// holds entries l and 32 + l); an element enters only if it beats the list's last entry, by a warp-wide
+// insertion (a ballot counts the entries above it, the rest shift by one lane). The CTA merges its warps'
+// lists in a tree and writes one list per slice. Kernel 2, one CTA per row: each warp merges a share of the
+// slices' lists, the warps' lists meet in a tree, and the first k entries become indices and fp32 values.
+// Integer work: bit-exact.
+#include <mutex>
+
+#include "launch.h"
+
+namespace mono {
+
+constexpr int kTrK = 64, kTrWarps = 8, kTrThreads = kTrWarps * 32, kTrMaxSlices = 64, kTrMaxRows = 16;
+
+__device__ __forceinline__ uint64_t tr_rank(uint32_t bits, uint32_t i) {
+    const uint32_t key = bits ^ ((bits & 0x80000000u) ? 0xFFFFFFFFu : 0x80000000u);
+    const uint32_t off = i & 32767u;
+    const uint32_t g = ((i >> 15) << 15) | (((off & 4095u) >> 2) << 5) | ((off >> 12) << 2) | (off & 3u);
+    return (uint64_t(key) << 32) | uint64_t(0xFFFFFFFFu - g);
+}
+__device__ __forceinline__ uint32_t tr_index(uint64_t r) {
+    const uint32_t g = 0xFFFFFFFFu - uint32_t(r);
+    return ((g >> 15) << 15) | (((g >> 2) & 7u) << 12) | (((g >> 5) & 1023u) << 2) | (g & 3u);
+}
+
+// The warp's sorted list: L[l] = a (lane l), L[32 + l] = b (lane l), descending.
+struct WarpList {
+    uint64_t a, b;
+    __device__ uint64_t last() const { return __shfl_sync(0xffffffffu, b, 31); }
+    // insert rank c (the same on every lane, known to beat last())
+    __device__ void insert(uint64_t c, int lane) {
+        const int p = __popc(__ballot_sync(0xffffffffu, a > c)) + __popc(__ballot_sync(0xffffffffu, b > c));
+        const uint64_t a_up = __shfl_up_sync(0xffffffffu, a, 1), b_up = __shfl_up_sync(0xffffffffu, b, 1);
+        const uint64_t a31 = __shfl_sync(0xffffffffu, a, 31);
+        const uint64_t na = lane < p ? a : (lane == p ? c : a_up);
+        const uint64_t nb = 32 + lane < p ? b : (32 + lane == p ? c : (lane == 0 ? a31 : b_up));
+        a = na;
+        b = nb;
+    }
+    // offer one rank per lane
+    __device__ void offer(uint64_t r, bool valid, int lane) {
+        uint64_t t = last();
+        unsigned mask = __ballot_sync(0xffffffffu, valid && r > t);
+        while (mask) {
+            const int j = __ffs(mask) - 1;
+            mask &= mask - 1;
+            const uint64_t c = __shfl_sync(0xffffffffu, r, j);
+            if (c > t) {
+                insert(c, lane);
+                t = last();
+            }
+        }
+    }
+};
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t tr_bits_at(const void* x, size_t i) {
+    if constexpr (BF16) return uint32_t(__ldg(static_cast<const uint16_t*>(x) + i)) << 16;
+    else return __ldg(static_cast<const uint32_t*>(x) + i);
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(kTrThreads) topk_rows_partial(const void* x, int64_t N, int slices, uint64_t* ws) {
+    __shared__ uint64_t lists[kTrWarps][kTrK];
+    const int row = blockIdx.y, slice = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t per = (N + slices - 1) / slices, c0 = slice * per, c1 = c0 + per < N ? c0 + per : N;
+    const size_t base = size_t(row) * N;
+    WarpList L{0, 0};
+    // 4 batches of 32 elements per warp per iteration; the next iteration's loads are issued before this one's
+    // elements are offered
+    const int64_t step = int64_t(kTrWarps) * 128;
+    uint32_t bits[4], next[4];
+    int64_t b0 = c0 + int64_t(warp) * 128;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const int64_t i = b0 + u * 32 + lane;
+        next[u] = i < c1 ? tr_bits_at<BF16>(x, base + i) : 0u;
+    }
+    for (; b0 < c1; b0 += step) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) bits[u] = next[u];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t i = b0 + step + u * 32 + lane;
+            next[u] = i < c1 ? tr_bits_at<BF16>(x, base + i) : 0u;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t i = b0 + u * 32 + lane;
+            L.offer(tr_rank(bits[u], uint32_t(i)), i < c1, lane);
+        }
+    }
+    lists[warp][lane] = L.a;
+    lists[warp][32 + lane] = L.b;
+    // tree merge: at level d, warp w (a multiple of 2d) takes in warp w + d's list
+    for (int d = 1; d < kTrWarps; d *= 2) {
+        __syncthreads();
+        if (warp % (2 * d) == 0) {
+            uint64_t t = L.last();
+            for (int j = 0; j < kTrK; ++j) {
+                const uint64_t c = lists[warp + d][j];
+                if (c <= t) break;  // each list is sorted: the rest cannot enter
+                L.insert(c, lane);
+                t = L.last();
+            }
+            lists[warp][lane] = L.a;
+            lists[warp][32 + lane] = L.b;
+        }
+    }
+    if (warp == 0) {
+        uint64_t* out = ws + (size_t(row) * slices + slice) * kTrK;
+        out[lane] = L.a;
+        out[32 + lane] = L.b;
+    }
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(kTrThreads) topk_rows_final(const void* x, int64_t N, int slices, int k,
+                                                              const uint64_t* ws, float* values, int64_t* indices) {
+    __shared__ uint64_t lists[kTrWarps][kTrK];
+    const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint64_t* lst = ws + size_t(row) * slices * kTrK;
+    // warp w merges slices w, w + 8, ..., then the warps' lists meet in a tree
+    WarpList L{0, 0};
+    for (int s = warp; s < slices; s += kTrWarps) {
+        uint64_t t = L.last();
+        for (int j = 0; j < kTrK; ++j) {
+            const uint64_t c = lst[size_t(s) * kTrK + j];
+            if (c <= t) break;
+            L.insert(c, lane);
+            t = L.last();
+        }
+    }
+    lists[warp][lane] = L.a;
+    lists[warp][32 + lane] = L.b;
+    for (int d = 1; d < kTrWarps; d *= 2) {
+        __syncthreads();
+        if (warp % (2 * d) == 0) {
+            uint64_t t = L.last();
+            for (int j = 0; j < kTrK; ++j) {
+                const uint64_t c = lists[warp + d][j];
+                if (c <= t) break;
+                L.insert(c, lane);
+                t = L.last();
+            }
+            lists[warp][lane] = L.a;
+            lists[warp][32 + lane] = L.b;
+        }
+    }
+    if (warp == 0) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int o = lane + 32 * h;
+            if (o < k) {
+                const uint32_t i = tr_index(h ? L.b : L.a);
+                indices[size_t(row) * k + o] = int64_t(i);
+                values[size_t(row) * k + o] = __uint_as_float(tr_bits_at<BF16>(x, size_t(row) * N + i));
+            }
+        }
+    }
+}
+
+static int topk_rows_slices(int64_t rows, int64_t N) {
+    int s = int((2 * int64_t(sm_count()) + rows - 1) / rows);  // about two CTAs per SM over all rows
+    s = s < 1 ? 1 : (s > kTrMaxSlices ? kTrMaxSlices : s);
+    while (s > 1 && (N + s - 1) / s < kTrK) --s;  // every slice holds at least k elements
+    return s;
+}
+
+}  // namespace mono
+
+using namespace mono;
+
+extern "C" {
+
+size_t mono_topk_rows_workspace(int64_t rows, int64_t N) {
+    if (rows < 1 || N < 1) return 0;
+    return size_t(rows) * topk_rows_slices(rows, N) * kTrK * sizeof(uint64_t);
+}
+
+int mono_topk_rows(const void* x, int bf16, int64_t rows, int64_t N, int64_t k, float* values, int64_t* indices,
+                   void* workspace, size_t workspace_bytes, mono_stream_t stream) {
+    MONO_CHECK(x && values && indices && workspace, "null operand");
+    MONO_CHECK(rows >= 1 && rows <= kTrMaxRows, "1 <= rows <= %d", kTrMaxRows);
+    MONO_CHECK(k >= 1 && k <= kTrK && N >= kTrK && N < (int64_t(1) << 31), "1 <= k <= 64, 64 <= N < 2^31");
+    MONO_CHECK(workspace_bytes >= mono_topk_rows_workspace(rows, N) && aligned(workspace, 8),
+               "workspace (mono_topk_rows_workspace)");
+    const int slices = topk_rows_slices(rows, N);
+    const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    uint64_t* ws = static_cast<uint64_t*>(workspace);
+    if (bf16) {
+        topk_rows_partial<true><<<dim3(slices, unsigned(rows)), kTrThreads, 0, s>>>(x, N, slices, ws);
+        CUDA_TRY(cudaGetLastError());
+        topk_rows_final<true><<<unsigned(rows), kTrThreads, 0, s>>>(x, N, slices, int(k), ws, values, indices);
+    } else {
+        topk_rows_partial<false><<<dim3(slices, unsigned(rows)), kTrThreads, 0, s>>>(x, N, slices, ws);
+        CUDA_TRY(cudaGetLastError());
+        topk_rows_final<false><<<unsigned(rows), kTrThreads, 0, s>>>(x, N, slices, int(k), ws, values, indices);
+    }
+    CUDA_TRY(cudaGetLastError());
+    return MONO_OK;
+}
+
+}  // extern "C"

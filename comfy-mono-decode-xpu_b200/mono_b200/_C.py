@@ -654,3 +654,23 @@ def layer_gdn(x, norm_in, eps_in, qkv_w, z_w, wab, conv_w, conv_state, dt_bias, 
                   _p(norm_post), float(eps_post), _p(gate_w), _p(up_w), _p(down_w), _p(silu_lut), M, H, int(I), int(hk),
                   HV, _p(out), _p(ws), nbytes, _stream(x.device))
     return out
+
+
+_topk_rows_ws = {}
+
+
+def topk_rows(x, k):
+    """Exact top-k (k <= 64) of a few long rows (the reference's _C.topk_rows, csrc/topk_rows.sycl): x fp32 or
+    bf16 [R, N] (R <= 16) -> (values fp32 [R, k], indices int64 [R, k]) = torch.topk(x.float(), k) in the
+    torch-XPU tie order (include/mono_b200.h mono_topk_rows)."""
+    _cuda(x)
+    _check(x.dim() == 2 and x.is_contiguous() and x.dtype in (torch.float32, torch.bfloat16), "x fp32 / bf16 [R, N]")
+    R, N = x.shape
+    values = torch.empty((R, int(k)), dtype=torch.float32, device=x.device)
+    indices = torch.empty((R, int(k)), dtype=torch.int64, device=x.device)
+    nbytes = _lib.load().mono_topk_rows_workspace(R, N)
+    ws = _workspace(_topk_rows_ws, (x.device, R, N), nbytes, x.device)
+    with torch.cuda.device(x.device):
+        _lib.call("mono_topk_rows", _p(x), int(x.dtype == torch.bfloat16), R, N, int(k), _p(values), _p(indices), _p(ws),
+                  nbytes, _stream(x.device))
+    return values, indices

@@ -53,6 +53,8 @@ SIGNATURES = {
     "mono_gdn_step": (I, [P, P, P, P, P, P, P, P, P, P, ctypes.c_float, ctypes.c_float, I64, I64, I64, P, P, SZ, P]),
     "mono_gdn_step_deferred": (I, [P, P, P, P, P, P, P, P, P, P, ctypes.c_float, ctypes.c_float, I64, I64, I64, P, P, P,
                                    P, P, P, P, P, I64, I64, I64, P, SZ, P]),
+    "mono_topk_rows_workspace": (SZ, [I64, I64]),
+    "mono_topk_rows": (I, [P, I, I64, I64, I64, P, P, P, SZ, P]),
     "mono_program_op_bytes": (SZ, []),
     "mono_program_workspace": (SZ, []),
     "mono_program_rows": (I, [P, I, I, P, I64, I64, P, ctypes.c_float, P, I64, I64, P, P, P, P, P, I]),

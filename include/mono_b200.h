@@ -295,6 +295,17 @@ MONO_API int mono_mtp_accept(int64_t* st, const int64_t* toks, const int64_t* dr
                              int64_t* next_tok, void* h_out, int32_t* ctl, const int64_t* kv_ptrs, int64_t nkv,
                              int64_t heads, int64_t cap, int64_t head_dim, int64_t* result, mono_stream_t stream);
 
+/* Exact top-k of a few long rows, k <= 64 (the reference's topk_rows, csrc/topk_rows.sycl:2-17: the verify
+ * sampling's torch.topk(logits.float(), k)): per row the k largest by the radix key of the fp32 value (sign-flipped
+ * bits: -0 below +0; rows holding NaN are not torch's order), sorted descending, ties in the torch-XPU gather
+ * order, i.e. by the 64-bit rank key << 32 | (0xFFFFFFFF - g), g = (i >> 15) << 15 | ((i % 4096) >> 2) << 5 |
+ * ((i % 32768) >> 12) << 2 | (i % 4) (csrc/topk_rows.sycl:34-42). x: fp32 (bf16 = 0) or bf16 (bf16 = 1)
+ * [rows][N]; values fp32 [rows][k], indices int64 [rows][k]. 1 <= rows <= 16, 64 <= N < 2^31.
+ * workspace: mono_topk_rows_workspace(rows, N) bytes. */
+MONO_API size_t mono_topk_rows_workspace(int64_t rows, int64_t N);
+MONO_API int mono_topk_rows(const void* x, int bf16, int64_t rows, int64_t N, int64_t k, float* values, int64_t* indices,
+                            void* workspace, size_t workspace_bytes, mono_stream_t stream);
+
 /* ---- Layer programs: the reference's single-launch layers (layer_pre / layer_post, csrc/mono_layer.sycl:1-9;
  * layer_gdn, csrc/mono_gdn.sycl:5-20), generalised to any sequence of their phases ----
  * A program is an array of ops of mono_program_op_bytes() bytes each, filled on the host by the builders below
