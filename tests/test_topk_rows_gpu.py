@@ -43,3 +43,18 @@ def test_topk_rows_rejects_bad_shapes(cuda):
         _C.topk_rows(torch.zeros(17, 1000, device=cuda), 8)  # 17 rows
     with pytest.raises(_lib.MonoError):
         _C.topk_rows(torch.zeros(2, 1000, device=cuda), 65)  # k > 64
+
+
+def test_sampling_mode_serves_torch_topk_on_cuda(cuda):
+    """Inside the verify sampling's context, torch.topk on the CUDA verify rows returns topk_rows' result: the
+    oracle's indices (bf16 rows hold ties: the torch-XPU tie order) and torch's own values."""
+    from mono_b200 import _C, sampling
+    g = torch.Generator().manual_seed(12)
+    lg0 = (torch.randn(8, 248320, generator=g) * 3).bfloat16().to(cuda)
+    before = sampling.stats()["calls"]
+    ctx, rows = sampling.verify_rows(_C, lg0)
+    with ctx:
+        v, i = torch.topk(rows, 64)
+    assert sampling.stats()["calls"] == before + 1
+    rv, ri = ref_topk_rows(lg0.float().cpu().numpy(), 64)
+    assert np.array_equal(i.cpu().numpy(), ri) and torch.equal(v, torch.topk(lg0.float(), 64).values)
