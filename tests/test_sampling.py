@@ -71,9 +71,13 @@ def test_off_and_check_modes(monkeypatch):
     ctx, rows = sampling.verify_rows(_C, lg0)
     assert rows.dtype == torch.float32 and rows is not lg0
     monkeypatch.setattr(sampling, "MODE", "check")
+    before = sampling.stats()
+    x = torch.randn(2, 40000, generator=torch.Generator().manual_seed(5))  # fp32: no ties
     with sampling.topk_mode(_C):
-        v, i = torch.topk(lg0.float(), 10)
-    assert _C.calls == 1 and sampling.stats()["check_mismatch"] == 0
+        v, i = torch.topk(x, 10)
+    after = sampling.stats()
+    assert _C.calls == 1 and after["checked"] == before["checked"] + 1
+    assert after["check_mismatch"] == before["check_mismatch"] and torch.equal(v, torch.topk(x, 10).values)
 
 
 def test_a_failing_topk_rows_disables_the_piece():
