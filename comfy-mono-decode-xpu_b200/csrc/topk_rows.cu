@@ -7,8 +7,9 @@
 //   rank = key << 32 | (0xFFFFFFFF - g)        (larger = earlier in the output)
 // Kernel 1, CTA = (row, slice): each warp keeps the 64 best ranks of its elements sorted in registers (lane l
 // holds entries l and 32 + l); an element enters only if it beats the list's last entry, by a warp-wide
-// insertion (a ballot counts the entries above it, the rest shift by one lane). The CTA merges its warps'
-// lists in a tree and writes one list per slice. Kernel 2, one CTA per row: each warp merges a share of the
+// insertion (a ballot counts the entries above it, the rest shift by one lane), or, when 4 or more lanes hold a
+// candidate, by a bitonic merge of the whole batch (measured faster than buffering candidates across batches).
+// The CTA merges its warps' lists in a tree and writes one list per slice. Kernel 2, one CTA per row: each warp merges a share of the
 // slices' lists, the warps' lists meet in a tree, and the first k entries become indices and fp32 values.
 // Integer work: bit-exact.
 #include <mutex>
@@ -44,10 +45,46 @@ struct WarpList {
         a = na;
         b = nb;
     }
+    // 32 values across the lanes, one per lane, sorted descending (bitonic network)
+    __device__ static uint64_t sort32(uint64_t v, int lane) {
+#pragma unroll
+        for (int k = 2; k <= 32; k <<= 1)
+#pragma unroll
+            for (int j = k >> 1; j > 0; j >>= 1) {
+                const uint64_t p = __shfl_xor_sync(0xffffffffu, v, j);
+                const bool keep_max = ((lane & k) == 0) == ((lane & j) == 0);
+                v = keep_max ? (v > p ? v : p) : (v < p ? v : p);
+            }
+        return v;
+    }
+    // a bitonic sequence of 32 across the lanes, sorted descending
+    __device__ static uint64_t merge32(uint64_t v, int lane) {
+#pragma unroll
+        for (int j = 16; j > 0; j >>= 1) {
+            const uint64_t p = __shfl_xor_sync(0xffffffffu, v, j);
+            v = (lane & j) == 0 ? (v > p ? v : p) : (v < p ? v : p);
+        }
+        return v;
+    }
+    // merge one candidate per lane (0 = none): the new 64 best of A u B u C are A u top32(B u C) (every entry
+    // of A beats all of B and at least as many entries of C as it loses to), re-sorted into A, B
+    __device__ void merge_batch(uint64_t c, int lane) {
+        c = sort32(c, lane);
+        const uint64_t cr = __shfl_sync(0xffffffffu, c, 31 - lane);
+        const uint64_t d = merge32(b > cr ? b : cr, lane);  // top 32 of B u C
+        const uint64_t dr = __shfl_sync(0xffffffffu, d, 31 - lane);
+        const uint64_t hi = a > dr ? a : dr, lo = a > dr ? dr : a;
+        a = merge32(hi, lane);
+        b = merge32(lo, lane);
+    }
     // offer one rank per lane
     __device__ void offer(uint64_t r, bool valid, int lane) {
         uint64_t t = last();
         unsigned mask = __ballot_sync(0xffffffffu, valid && r > t);
+        if (__popc(mask) >= 4) {  // many candidates: one merge instead of one insertion each
+            merge_batch(valid && r > t ? r : 0ull, lane);
+            return;
+        }
         while (mask) {
             const int j = __ffs(mask) - 1;
             mask &= mask - 1;
