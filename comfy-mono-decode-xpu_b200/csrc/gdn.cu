@@ -56,7 +56,8 @@ __global__ void __launch_bounds__(256) gdn_conv_kernel(const GdnArgs A) {
 }
 
 __global__ void __launch_bounds__(kRG * kDH) gdn_delta_kernel(const GdnArgs A) {
-    __shared__ float qn[kGdnMaxAll][kDH], kn[kGdnMaxAll][kDH];
+    __shared__ __align__(16) float qn[kGdnMaxAll][kDH];
+    __shared__ __align__(16) float kn[kGdnMaxAll][kDH];
     __shared__ float part[2][kRG][kDH];
     __shared__ float raw[kGdnMaxRows][kDH];
     __shared__ float sums[2 * kGdnMaxAll];
@@ -89,11 +90,20 @@ __global__ void __launch_bounds__(kRG * kDH) gdn_delta_kernel(const GdnArgs A) {
     for (int t = 0; t < R; ++t) {
         const float decay = gsm[t][0], beta = gsm[t][1];
         const float v = vsm[t][col];
+        // the row group's 32 k and q values as 16-byte shared loads (a warp's lanes share the row group: broadcast)
+        float kr[kRPG], qr[kRPG];
+#pragma unroll
+        for (int r4 = 0; r4 < kRPG / 4; ++r4) {
+            const float4 k4 = reinterpret_cast<const float4*>(&kn[t][rg * kRPG])[r4];
+            const float4 q4 = reinterpret_cast<const float4*>(&qn[t][rg * kRPG])[r4];
+            kr[4 * r4] = k4.x, kr[4 * r4 + 1] = k4.y, kr[4 * r4 + 2] = k4.z, kr[4 * r4 + 3] = k4.w;
+            qr[4 * r4] = q4.x, qr[4 * r4 + 1] = q4.y, qr[4 * r4 + 2] = q4.z, qr[4 * r4 + 3] = q4.w;
+        }
         float mem = 0.f;
 #pragma unroll
         for (int r = 0; r < kRPG; ++r) {
             st[r] *= decay;
-            mem = fmaf(st[r], kn[t][rg * kRPG + r], mem);
+            mem = fmaf(st[r], kr[r], mem);
         }
         part[0][rg][col] = mem;
         __syncthreads();
@@ -102,8 +112,8 @@ __global__ void __launch_bounds__(kRG * kDH) gdn_delta_kernel(const GdnArgs A) {
         float o = 0.f;
 #pragma unroll
         for (int r = 0; r < kRPG; ++r) {
-            st[r] = fmaf(kn[t][rg * kRPG + r], delta, st[r]);
-            o = fmaf(st[r], qn[t][rg * kRPG + r], o);
+            st[r] = fmaf(kr[r], delta, st[r]);
+            o = fmaf(st[r], qr[r], o);
         }
         part[1][rg][col] = o;
         __syncthreads();

@@ -103,8 +103,8 @@ static int launch_linear_mt(Program& P, LinearEpi& E, cudaStream_t stream) {
     PhaseDesc& ph = P.ph[0];
     const int tiles = phase_tiles(ph), grid = tiles < sm_count() ? tiles : sm_count();
     const int tiles_cta = (tiles + grid - 1) / grid, C = phase_chunks(ph);
-    // partial slots: the CTA's tiles in batches of at most 8 (for very wide matrices such as an lm_head)
-    E.max_items = (tiles_cta < 8 ? tiles_cta : 8) * C;
+    // partial slots: the CTA's tiles in batches of at most 16 (for very wide matrices such as an lm_head)
+    E.max_items = (tiles_cta < 16 ? tiles_cta : 16) * C;
     const size_t part_bytes = size_t(E.max_items) * MT * 128 * 4;
     // stage the activations when they fit next to the partials and the ring
     for (int staged = 1; staged >= (E.xb ? 1 : 0); --staged) {
