@@ -656,6 +656,25 @@ def layer_gdn(x, norm_in, eps_in, qkv_w, z_w, wab, conv_w, conv_state, dt_bias, 
     return out
 
 
+def gemv_bf16(x, w, out=None):
+    """bf16 GEMV of the draft head's projections (include/mono_b200.h mono_gemv_bf16): x bf16 [M, K] (M <= 8,
+    unit column stride), w bf16 [N, K] contiguous -> bf16 [M, N] (out: any [M, N] view with unit column stride),
+    fp32 accumulation; what F.linear(x, w) computes for a few rows."""
+    _cuda(x, w)
+    _check(x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1, "x bf16 [M, K] rows")
+    _check(w.dtype == torch.bfloat16 and w.dim() == 2 and w.is_contiguous() and w.shape[1] == x.shape[1],
+           "w bf16 [N, K]")
+    M, K = x.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    _check(out.dtype == torch.bfloat16 and out.dim() == 2 and tuple(out.shape) == (M, N) and out.stride(1) == 1,
+           "out bf16 [M, N] rows")
+    with torch.cuda.device(x.device):
+        _lib.call("mono_gemv_bf16", _p(x), x.stride(0), _p(w), M, N, K, _p(out), out.stride(0), _stream(x.device))
+    return out
+
+
 _topk_rows_ws = {}
 
 

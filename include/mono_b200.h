@@ -295,6 +295,13 @@ MONO_API int mono_mtp_accept(int64_t* st, const int64_t* toks, const int64_t* dr
                              int64_t* next_tok, void* h_out, int32_t* ctl, const int64_t* kv_ptrs, int64_t nkv,
                              int64_t heads, int64_t cap, int64_t head_dim, int64_t* result, mono_stream_t stream);
 
+/* bf16 GEMV of the MTP draft head (the reference's F.linear on one draft row, comfy_mono_decode_xpu/draft_head.py:
+ * 198-210: fc, qkv, o, gate | up, down): out[m][n] = bf16(sum_k x[m][k] * w[n][k]), fp32 accumulation (torch's
+ * bf16 linear contract; the summation order is this kernel's). x bf16 [M][x_stride], w bf16 [N][K] row-major,
+ * out bf16 [M][out_stride]. 1 <= M <= 8, K a multiple of 256, x and w 16-byte aligned, x_stride % 8 == 0. */
+MONO_API int mono_gemv_bf16(const void* x, int64_t x_stride, const void* w, int64_t M, int64_t N, int64_t K, void* out,
+                            int64_t out_stride, mono_stream_t stream);
+
 /* Exact top-k of a few long rows, k <= 64 (the reference's topk_rows, csrc/topk_rows.sycl:2-17: the verify
  * sampling's torch.topk(logits.float(), k)): per row the k largest by the radix key of the fp32 value (sign-flipped
  * bits: -0 below +0; rows holding NaN are not torch's order), sorted descending, ties in the torch-XPU gather
