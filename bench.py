@@ -530,7 +530,7 @@ def run_decode(args):
     cfg = Qwen35Config()
     prompt = args.prompt
     model = Qwen35W4A8(cfg, dev, prompt_len=prompt, gen_tokens=max(512, args.steps * 8 + 64), seed=0x5EED + 4 + rank,
-                       fused=args.programs, prefetch=args.prefetch)
+                       fused=args.programs, prefetch=args.prefetch, draft_gemv=not args.cublas_draft)
     stream = torch.cuda.Stream(dev)
     with torch.cuda.stream(stream):
         for _ in range(2):  # eager warm-up: workspaces, cuBLAS handles
@@ -616,6 +616,7 @@ def run_decode(args):
                        "l2": "inputs larger than L2 (6.6 GB of weights read per step)",
                        "body": (f"{len(model.programs[0])} layer programs per step (prefetch {args.prefetch})"
                                 if args.programs else "one launch per fused op (rowlin / a|b / GDN / MLP / attention)"),
+                       "draft_projections": "cuBLAS (F.linear)" if args.cublas_draft else "mono_gemv_bf16",
                        "parallelism": f"independent streams x{world}"},
             "roofline": {"bound": "hbm", "achieved": round(mlp_b / (mlp_us * 1e-6) / 1e9, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(mlp_b / (mlp_us * 1e-6) / 1e9 / hbm, 4), "peak_source": src,
@@ -781,6 +782,8 @@ def main():
                     help="decode: run the verify body as layer programs (one persistent launch per run of layers) "
                          "instead of one launch per fused op")
     ap.add_argument("--prefetch", type=int, default=0, help="decode: L2 look-ahead of the layer programs (items)")
+    ap.add_argument("--cublas-draft", action="store_true",
+                    help="decode: the MTP head's bf16 projections on cuBLAS (F.linear) instead of mono_gemv_bf16")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = 200 if args.workload == "decode" else 2000

@@ -16,9 +16,9 @@ comfy_mono_decode_xpu/mtp_loop.py):
 Per layer: full attention = rowlin(norm -> q|k|v) -> qk_norm_rope_kv -> tree attention -> rowlin(gate -> o_proj +
 residual) -> fused MLP; GDN = rowlin(norm -> qkv|z, xn) -> a|b (mono_gdn_ab) -> deferred GDN step ->
 rowlin(quant -> out_proj + residual) -> fused MLP. The verify rows form a chain (the GDN step's verify rows run as a
-chain); the bf16 MTP head and the verify's lm_head run as cuBLAS GEMMs through torch; the drafts' lm_head is a W4A8 GPTQ copy on this build's
-linear kernel; the head's norms and gates are the row kernels
-(mono_rmsnorm_add, mono_lut_mul).
+chain); the bf16 MTP head's five projections run on this build's bf16 GEMV (mono_gemv_bf16; cuBLAS through torch's
+F.linear with draft_gemv=False) and the verify's 5-row lm_head on cuBLAS; the drafts' lm_head is a W4A8 GPTQ copy on
+this build's linear kernel; the head's norms and gates are the row kernels (mono_rmsnorm_add, mono_lut_mul).
 """
 from __future__ import annotations
 
@@ -96,7 +96,7 @@ class Qwen35W4A8:
     """Weights and decode state of one stream on one device."""
 
     def __init__(self, cfg: Qwen35Config, device, prompt_len: int, gen_tokens: int = 512, seed: int = 0x5EED + 4,
-                 fused: bool = False, prefetch: int = 0):
+                 fused: bool = False, prefetch: int = 0, draft_gemv: bool = True):
         self.cfg, self.dev = cfg, torch.device(device)
         c, dev = cfg, self.dev
         g = torch.Generator(device=dev).manual_seed(seed)
@@ -168,7 +168,7 @@ class Qwen35W4A8:
         self.drafts = torch.zeros(R, dtype=torch.int64, device=dev)
         self.no_mask = torch.empty(0, dtype=torch.int32, device=dev)
         self.total = torch.zeros(1, dtype=torch.int64, device=dev)  # tokens committed, summed on the device
-        self.fused, self.prefetch = fused, prefetch
+        self.fused, self.prefetch, self.draft_gemv = fused, prefetch, draft_gemv
         self.programs = self._build_programs() if fused else None
 
     # ---- layers ------------------------------------------------------------------------------------------
@@ -303,6 +303,11 @@ class Qwen35W4A8:
         _, toks = _C.fast_topk(logits, 1, True)
         return toks.view(1, R), x
 
+    def _linear(self, x, w):
+        """A draft projection x [1, K] @ w [N, K]^T (the reference's F.linear, draft_head.py:198-210): this build's
+        GEMV, or torch's cuBLAS linear when the model was built with draft_gemv=False."""
+        return _C.gemv_bf16(x, w) if self.draft_gemv else F.linear(x, w)
+
     def draft_token(self, token, hidden, k):
         """One MTP draft: (token [1, 1], hidden [1, 1, H]) -> (draft token [1, 1], MTP hidden [1, 1, H])."""
         c, m = self.cfg, self.mtp
@@ -313,8 +318,8 @@ class Qwen35W4A8:
         cat = torch.empty(1, 2 * H, dtype=torch.bfloat16, device=self.dev)
         _C.rmsnorm_add(e, m["enorm"], c.eps, out=cat[:, :H])
         _C.rmsnorm_add(hidden.view(1, -1), m["hnorm"], c.eps, out=cat[:, H:])
-        x = F.linear(cat, m["fc"])
-        qkv = F.linear(_C.rmsnorm_add(x, m["ln1"], c.eps), m["qkv"])
+        x = self._linear(cat, m["fc"])
+        qkv = self._linear(_C.rmsnorm_add(x, m["ln1"], c.eps), m["qkv"])
         nq = 2 * c.heads * hd
         qg = qkv[:, :nq].view(1, 1, c.heads, 2 * hd)
         rawk = qkv[:, nq:nq + c.kv_heads * hd].view(1, 1, c.kv_heads, hd)
@@ -323,10 +328,10 @@ class Qwen35W4A8:
                                    self.mpos, c.eps, c.eps, c.rotary_dim)
         y = _C.attn_dpas(q, m["kc"], m["vc"], self.mseq, kk, v.transpose(1, 2), self.no_mask)
         yg = _C.lut_mul(y[0], qkv[:, hd:nq], self.sig_lut, b_head_stride=2 * hd)
-        xn, x = _C.rmsnorm_add(x, m["ln2"], c.eps, add=F.linear(yg, m["o"]))
-        gu = F.linear(xn, m["gate_up"])
+        xn, x = _C.rmsnorm_add(x, m["ln2"], c.eps, add=self._linear(yg, m["o"]))
+        gu = self._linear(xn, m["gate_up"])
         h = _C.lut_mul(gu[:, c.inter:], gu[:, :c.inter], self.silu_lut)
-        xf, x = _C.rmsnorm_add(x, m["norm"], c.eps, add=F.linear(h, m["down"]))
+        xf, x = _C.rmsnorm_add(x, m["norm"], c.eps, add=self._linear(h, m["down"]))
         logits = _C.w4a8_gptq_linear_bf16(xf, self.lm_head_w4, None, tiled=True, N=c.vocab)
         _, t = _C.fast_topk(logits, 1, True)
         return t.view(1, 1), x.view(1, 1, -1)
@@ -357,7 +362,8 @@ class Qwen35W4A8:
             body = (n_attn + 1) + n_attn * 3
         else:  # rowlin x2 + MLP; GDN a|b + conv + delta; rope + attention x2
             body = c.layers * 3 + n_gdn * 3 + n_attn * 3
-        draft = c.depth * (1 + 3 + 1 + 2 + 2 + 2 + 1 + 2)   # prep, norms, rope, attention, lut x2, norm-adds, lm_head, argmax
+        # prep, norms, rope, attention, lut x2, norm-adds, lm_head, argmax (+ fc, qkv, o, gate | up, down)
+        draft = c.depth * (1 + 3 + 1 + 2 + 2 + 2 + 1 + 2 + (5 if self.draft_gemv else 0))
         return body + draft + 1 + 2 + 1 + 1                   # prep_verify, final norm + argmax, accept, verify norm
 
     def step_bytes(self) -> int:
