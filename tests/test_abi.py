@@ -51,6 +51,17 @@ def test_host_validation_without_gpu():
     assert rc == _lib.MONO_EINVAL and b"group_size" in lib.mono_last_error()
     rc = lib.mono_w4a8_gptq_linear(ctypes.c_void_p(8), p, p, p, None, 1, 4096, 4096, 2, 0, p, None)
     assert rc == _lib.MONO_EINVAL and b"aligned" in lib.mono_last_error()
+    # bf16 GEMV: rows, K granularity, strides and alignment are checked before the launch
+    rc = lib.mono_gemv_bf16(p, 4096, p, 9, 4096, 4096, p, 4096, None)
+    assert rc == _lib.MONO_EINVAL and b"M" in lib.mono_last_error()
+    rc = lib.mono_gemv_bf16(p, 4096, p, 1, 4096, 4000, p, 4096, None)
+    assert rc == _lib.MONO_EINVAL and b"K" in lib.mono_last_error()
+    rc = lib.mono_gemv_bf16(p, 4100, p, 2, 4096, 4096, p, 4096, None)
+    assert rc == _lib.MONO_EINVAL and b"x_stride" in lib.mono_last_error()
+    rc = lib.mono_gemv_bf16(p, 4096, ctypes.c_void_p(24), 1, 4096, 4096, p, 4096, None)
+    assert rc == _lib.MONO_EINVAL and b"aligned" in lib.mono_last_error()
+    rc = lib.mono_gemv_bf16(p, 4096, p, 1, 4096, 4096, p, 4000, None)
+    assert rc == _lib.MONO_EINVAL and b"out_stride" in lib.mono_last_error()
 
 
 def _fake(addr):
