@@ -53,6 +53,13 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def traffic_fields(name):
+    """roofline.traffic and its provenance: the per-launch DRAM bytes (dram__bytes_read.sum +
+    dram__bytes_write.sum) of the kernel's committed ncu capture profiles/<name>.md, not of this run."""
+    return {"traffic": profile_traffic(name),
+            "traffic_source": f"ncu capture in profiles/{name}.md (an earlier run of the same kernel and shape)"}
+
+
 def profile_traffic(name):
     """Per-launch DRAM bytes of a kernel from its committed ncu summary (profiles/<name>.md line
     `traffic_bytes_per_launch: N`), or None."""
@@ -289,7 +296,7 @@ def run_ours(args):
                        "layout": "tile-major (mono_w4_repack)", "parity_gate": bool(ok)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(achieved / hbm, 4), "peak_source": src,
-                         "traffic": profile_traffic("w4a8_gemv_gptq_m8_4096x12288"),
+                         **traffic_fields("w4a8_gemv_gptq_m8_4096x12288"),
                          "kernel": "linear_kernel<GPTQ,TILED,MT=1>", "us_per_launch": round(kern_us, 3),
                          "algorithmic_bytes_per_launch": kbytes},
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": PER_STEP * M_ROWS * K_IN * 2,
@@ -406,7 +413,7 @@ def run_mlp(args):
                        "l2": "inputs larger than L2 (4 weight copies = 312 MB cycled)", "parity_gate": bool(ok)},
             "roofline": {"bound": "hbm", "achieved": round(b / (us * 1e-6) / 1e9, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(b / (us * 1e-6) / 1e9 / hbm, 4), "peak_source": src,
-                         "traffic": profile_traffic("mlp_kernel_m8"), "kernel": "mlp_kernel<1,2>",
+                         **traffic_fields("mlp_kernel_m8"), "kernel": "mlp_kernel<1,2>",
                          "us_per_launch": round(us, 3), "algorithmic_bytes_per_launch": b},
             "e2e": {"value": round(e2e, 1), "unit": "GB/s", "h2d_bytes_per_step": per_step * M * H * 2,
                     "d2h_bytes_per_step": per_step * M * H * 2},
@@ -417,7 +424,7 @@ def run_mlp(args):
 
 
 def run_topk_rows(args):
-    """The verify sampling's top-k filter (the reference's topk_rows): exact top-64 of 8 fp32
+    """The verify sampling's top-k filter (the reference's topk_rows, csrc/topk_rows.sycl): exact top-64 of 8 fp32
     rows of 248,320 logits per call (the reference's "8 x 248k"); 32 input copies (254 MB) cycled so every call
     reads its rows from HBM. GB/s of row bytes read; parity checked against the oracle on the first call."""
     import numpy as np
@@ -620,7 +627,7 @@ def run_decode(args):
                        "parallelism": f"independent streams x{world}"},
             "roofline": {"bound": "hbm", "achieved": round(mlp_b / (mlp_us * 1e-6) / 1e9, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(mlp_b / (mlp_us * 1e-6) / 1e9 / hbm, 4), "peak_source": src,
-                         "traffic": profile_traffic("mlp_kernel_m5"),
+                         **traffic_fields("mlp_kernel_m5"),
                          "kernel": "mlp_kernel<MT=1> (fused MLP block, the step's dominant kernel), M = 5 verify rows",
                          "us_per_launch": round(mlp_us, 3), "algorithmic_bytes_per_launch": mlp_b},
             "step_roofline": {"achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),

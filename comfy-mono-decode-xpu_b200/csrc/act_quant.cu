@@ -184,19 +184,43 @@ constexpr int kNoAllocK = 12288;
 constexpr size_t kNoAllocBytes = size_t(kRotMaxRows) * 8 + size_t(kNoAllocRows) * kNoAllocK * 2;
 static __device__ __align__(256) uint8_t g_rot_scratch[kNoAllocBytes];
 
-// Device address of g_rot_scratch on the current device, looked up once per device. In host code the
-// symbol names a host-side stand-in, never the device memory: only this address may reach a kernel.
+// Device address of g_rot_scratch in the current context, looked up once per (device, context). In host code
+// the symbol names a host-side stand-in, never the device memory: only this address may reach a kernel. The
+// cache remembers which context the address belongs to (the driver's cuCtxGetCurrent, reached through the
+// runtime's entry-point query so no driver library is linked): after cudaDeviceReset, or with another context
+// made current on the same device, the address is looked up again instead of reusing a stale one.
+typedef int (*CtxGetCurrentFn)(void**);
+static CtxGetCurrentFn ctx_get_current() {
+    static CtxGetCurrentFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<CtxGetCurrentFn>(p);
+    }();
+    return fn;
+}
+
 static int rot_scratch_address(void** out) {
     static std::mutex mu;
     static void* addr[64] = {};
+    static void* owner[64] = {};
     int dev = 0;
     CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return fail(MONO_EINVAL, "rot_quant_noalloc: device ordinal %d out of range", dev);
+    const CtxGetCurrentFn get = ctx_get_current();
+    if (get == nullptr) return fail(MONO_ECUDA, "rot_quant_noalloc: cuCtxGetCurrent is not available");
+    void* ctx = nullptr;
+    if (get(&ctx) != 0) return fail(MONO_ECUDA, "rot_quant_noalloc: cuCtxGetCurrent failed");
     std::lock_guard<std::mutex> lock(mu);
-    if (addr[dev] == nullptr) {
+    if (ctx == nullptr || addr[dev] == nullptr || owner[dev] != ctx) {
         void* p = nullptr;
-        CUDA_TRY(cudaGetSymbolAddress(&p, g_rot_scratch));
+        CUDA_TRY(cudaGetSymbolAddress(&p, g_rot_scratch));  // (initializes the device's context if none was current)
+        if (ctx == nullptr && (get(&ctx) != 0 || ctx == nullptr))
+            return fail(MONO_ECUDA, "rot_quant_noalloc: no current CUDA context");
         addr[dev] = p;
+        owner[dev] = ctx;
     }
     *out = addr[dev];
     return MONO_OK;

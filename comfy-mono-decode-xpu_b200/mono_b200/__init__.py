@@ -1,5 +1,6 @@
 """mono_b200: B200 (sm_100a) kernels for the Qwen3.5-9B W4A8 decode step behind the reference's hook surface.
 
-Submodules mirror comfy_mono_decode_xpu: _C (native ops), guard, patch (W4 linear / rot-quant routes),
-mono (MLP route), layer (decode block route), tiles (tile-major weight copies).
+Submodules mirror comfy_mono_decode_xpu: _C (native ops over the C ABI), guard (error contract), patch (W4
+linear / rot-quant routes), mono (MLP route), layer (decode block route), logits (lm_head route), mtp_loop
+(device MTP loop), sampling (verify top-k), decoder (the synthetic Qwen3.5-9B-shaped model on these kernels).
 """

@@ -120,15 +120,17 @@ MONO_API size_t mono_rot_quant_workspace(int64_t M, int64_t K);
 MONO_API int mono_rot_quant(const void* x_bf16, const void* h_bf16, int64_t M, int64_t K, int8_t* q, float* scale,
                    void* workspace, mono_stream_t stream);
 
-/* rot_quant for callers that cannot allocate device memory (no counterpart in the reference): code that
- * runs where cudaMalloc is off limits — inside a CUDA-graph capture that must not allocate, under a
- * framework that owns every device allocation (a fixed memory pool), or in a plugin that may not touch
- * the allocator — gets the same result as mono_rot_quant without passing a workspace. The scratch is a
- * fixed array inside the library (about 386 KB per GPU that loads it, held until the process exits), so
- * shapes are limited to 1 <= M <= 16 rows and K <= 12288 (K % 256 == 0); larger shapes return
- * MONO_EINVAL. The first call on each device looks up the array's device address (call it once before
- * any stream capture). All calls share the array: calls that overlap on the GPU (other streams, other
- * threads) race and must be serialized by the caller. Allocates nothing (no cudaMalloc / cudaFree). */
+/* rot_quant for callers that cannot allocate device memory (no counterpart in the reference): a host
+ * framework that owns every device allocation through its own fixed pool and forbids others, or a plugin
+ * loaded into a process whose allocator it may not touch, gets the same result as mono_rot_quant without
+ * passing a workspace. The scratch is a fixed array inside the library (about 386 KB per GPU that loads
+ * it, held until the process exits), so shapes are limited to 1 <= M <= 16 rows and K <= 12288
+ * (K % 256 == 0); larger shapes return MONO_EINVAL. The first call in each device context looks up the
+ * array's device address (a runtime query, done again if the context changes); make that first call
+ * before any stream capture. All calls share the array and it keeps the last call's contents (the
+ * counters that must start at zero are cleared by every call): calls that overlap on the GPU (other
+ * streams, other threads) race and must be serialized by the caller. Allocates nothing (no cudaMalloc /
+ * cudaFree). */
 MONO_API int mono_rot_quant_noalloc(const void* x_bf16, const void* h_bf16, int64_t M, int64_t K, int8_t* q,
                                     float* scale, mono_stream_t stream);
 

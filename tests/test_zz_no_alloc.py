@@ -1,7 +1,7 @@
-"""mono_rot_quant_noalloc: rot_quant for callers that cannot allocate device memory (a graph capture that
-must not allocate, a framework that owns every allocation, a plugin kept away from the allocator). It
-uses a fixed scratch array inside the library instead of a caller workspace; its results must equal
-those of mono_rot_quant with a workspace. This file is collected last on purpose: if it fails, a run
+"""mono_rot_quant_noalloc: rot_quant for callers that cannot allocate device memory (a host framework that
+owns every device allocation through its own pool, a plugin loaded into a process whose allocator it may
+not touch). It uses a fixed scratch array inside the library instead of a caller workspace; its results
+must equal those of mono_rot_quant with a workspace. This file is collected last on purpose: if it fails, a run
 that stops at the first failure has already run every other test."""
 import ctypes
 
