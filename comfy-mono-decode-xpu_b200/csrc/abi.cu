@@ -247,16 +247,13 @@ int mono_mlp_gptq(const void* x, const void* norm_w, float eps, const void* gate
     A.H = int(H);
     A.I = int(I);
     A.residual = residual != 0;
-    A.xn = reinterpret_cast<uint16_t*>(w);
-    w += al(16 * size_t(H) * 2);
     A.q1 = reinterpret_cast<int8_t*>(w);
     w += al(16 * size_t(H));
     A.h = reinterpret_cast<uint16_t*>(w);
     w += al(16 * size_t(I) * 2);
     A.q2 = reinterpret_cast<int8_t*>(w);
     w += al(16 * size_t(I));
-    A.s1 = reinterpret_cast<float*>(w);
-    A.s2 = reinterpret_cast<float*>(w + 256);
+    A.s1 = reinterpret_cast<float*>(w + 256);
     A.amax2 = reinterpret_cast<unsigned*>(w + 512);
     A.bar = reinterpret_cast<unsigned*>(w + 768);
     Program P{};
@@ -267,7 +264,7 @@ int mono_mlp_gptq(const void* x, const void* norm_w, float eps, const void* gate
     P.ph[0].nm = 2;
     P.ph[0].paired = 1;
     P.ph[0].K = int(H);
-    P.ph[0].x = A.q1;
+    P.ph[0].x = nullptr;  // (staged by the kernel itself)
     P.ph[0].xperm = 1;
     P.ph[1].m[0] = MatDesc{static_cast<const uint8_t*>(down_q), nullptr, int(H)};
     P.ph[1].nm = 1;

@@ -15,6 +15,7 @@
 #include <mutex>
 
 #include "launch.h"
+#include "rowops.cuh"
 
 namespace mono {
 
@@ -69,19 +70,10 @@ __global__ void __launch_bounds__(kAqThreads) act_quant_kernel(const uint16_t* _
     for (int i = threadIdx.x * 8; i < K; i += kAqThreads * 8) {
         const uint4 v = *reinterpret_cast<const uint4*>(xr + i);
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-        uint32_t out[2] = {0, 0};
+        float f[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const uint32_t bits = (j & 1) ? (w[j >> 1] & 0xFFFF0000u) : (w[j >> 1] << 16);
-            int qi = 0;
-            if (s > 0.f) {
-                const float d = __fdiv_rn(__uint_as_float(bits), s);
-                qi = __float2int_rn(d);
-                qi = qi > 127 ? 127 : (qi < -127 ? -127 : qi);
-            }
-            out[j >> 2] |= (uint32_t(qi) & 0xFF) << (8 * (j & 3));
-        }
-        *reinterpret_cast<uint2*>(qr + i) = make_uint2(out[0], out[1]);
+        for (int j = 0; j < 8; ++j) f[j] = __uint_as_float((j & 1) ? (w[j >> 1] & 0xFFFF0000u) : (w[j >> 1] << 16));
+        *reinterpret_cast<uint2*>(qr + i) = quant8(f, s);  // rowops.cuh: the quotient's rounding without dividing
     }
 }
 

@@ -71,6 +71,7 @@ struct PhaseDesc {
     const int8_t* x;  // activation rows [M][K] (row stride K)
     int xsmem;        // 1: staged in shared memory
     int xperm;        // 1: x is already in the permuted byte order
+    int rev;          // 1: tiles dealt to the CTAs in reverse order (stream.cuh cta_slot)
 };
 
 struct Program {

@@ -28,13 +28,11 @@ struct MlpArgs {
     float eps;
     int H, I, residual, max_items;
     // workspace
-    uint16_t* xn;     // [M][H]
     int8_t* q1;       // [M][H]
     float* s1;        // [16]
     uint16_t* h;      // [M][I]
-    unsigned* amax2;  // [16] (float bits of non-negative values)
-    int8_t* q2;       // [M][I]
-    float* s2;        // [16]
+    unsigned* amax2;  // [16] (float bits of non-negative values; zero between launches)
+    int8_t* q2;       // [M][I] (only when the down phase's activations are not staged in shared memory)
     unsigned* bar;    // [2] grid barrier words (zero between launches)
 };
 // Shared-memory shape of a cooperative stream kernel: ring stages, partial bytes, staged-activation bytes.

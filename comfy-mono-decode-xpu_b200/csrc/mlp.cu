@@ -1,13 +1,13 @@
 // Fused decode MLP block in one cooperative launch (the role of csrc/mono_mlp.sycl:34-180 and of the MLP
 // phases 3-6 of layer_post, csrc/mono_layer.sycl:272-313), GPTQ W4A8:
 //
-//   P1 rows  xn = RMSNorm(x) (or x when no norm weight); q1, s1 = quant(xn)
-//   P2 all   g, u = W4A8 gate / up (q1);  h = bf16(silu_lut[bf16 g] * bf16 u);  row amax of h
-//   P3 all   q2, s2 = quant(h)
-//   P4 all   out = bf16(x + bf16(W4A8 down (q2)))  (or bf16(W4A8 down (q2)) without the residual)
+//   xn = RMSNorm(x) (or x when no norm weight); q1, s1 = quant(xn)
+//   g, u = W4A8 gate / up (q1);  h = bf16(silu_lut[bf16 g] * bf16 u);  q2, s2 = quant(h)
+//   out = bf16(x + bf16(W4A8 down (q2)))  (or bf16(W4A8 down (q2)) without the residual)
 //
-// Phases are separated by bounded grid barriers; the weight rings run across them (engine.cuh), so
-// gate/up and down weights stream while rows are normalized and quantized.
+// Phases are separated by bounded grid barriers; the weight rings run across them, so gate / up and down
+// weights stream while rows are normalized and quantized.
+#include <algorithm>
 #include <mutex>
 
 #include "launch.h"
@@ -17,15 +17,27 @@
 
 namespace mono {
 
-// One CTA per SM (cooperative): 12 consumer warps + 4 producer warps (stream.cuh), S = 12 ring stages. The
-// producers stream gate/up and then down weights straight through the row phases and the grid barriers.
-// Warp configurations (consumer warps CW, producer warps PW, ring stages S = a common multiple): the deepest
-// ring that fits next to the partials and the staged activations is taken (stream_config in stream.cuh).
-
+// One CTA per SM (cooperative): CW consumer + PW producer warps (stream.cuh) and a ring of S stages; the
+// producers stream the gate / up and then the down weights from the first instruction, straight through the
+// row phases and the grid barriers. The down tiles are dealt in reverse CTA order (PhaseDesc::rev): the CTAs with
+// an extra gate / up tile get fewer down tiles, and their rings carry the difference across the barriers.
+//
+//   P1  rows: row m on CTA m (norm_quant_row_cta, the pinned order) -> q1, s1;  barrier;  every CTA stages q1
+//   P2  gate / up tiles: h = bf16(silu_lut[bf16 g] * bf16 u) to the workspace, row maxima of |h| (atomic max,
+//       order-free);  barrier
+//   P3  q2 = quant(h), spread over all CTAs;  barrier;  every CTA stages q2 (when it fits next to the ring; else
+//       the down items read it through L2)
+//   P4  down tiles: out = bf16(x + bf16(total * s2)) (or without the residual)
+// The last CTA to leave clears the row maxima for the next launch (every CTA has read them by then).
+// Measured alternatives (not kept): every CTA preparing all rows itself, or quantizing all of h itself, to drop
+// a barrier: the per-element work of M full rows on one SM outweighs a barrier (12 us against 6 us for P1 at
+// M = 5); and tiles split across CTAs for an even item count: the exchange of the cut tiles' partials costs
+// three L2 round trips per phase.
 template <int MT, int CW, int PW>
 __global__ void __launch_bounds__((CW + PW) * 32, 1) mlp_kernel(const Program P, const MlpArgs A, const MlpShape Z) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float red[64];
+    __shared__ float s1s[16], s2s[16];
     __shared__ unsigned rowmax[16];
     __shared__ int flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -51,43 +63,36 @@ __global__ void __launch_bounds__((CW + PW) * 32, 1) mlp_kernel(const Program P,
         produce_all<FMT_GPTQ, LAYOUT_TILED, PW>(P, ring, full, empty, S, warp - CW, lane);
         return;
     }
-    constexpr int NT = CW * 32;
+    constexpr int NT = CW * 32, NWG = CW / 4;
     pdl_wait();
     trace_stamp(1);
     unsigned epoch = 0;
     bool ok = true;
 
-    // ---- P1: norm + quant of the rows (one warp-group of consumers per row) ----
-    if (blockIdx.x == 0 && threadIdx.x < 16) A.amax2[threadIdx.x] = 0u;
-    // row m on CTA m, all consumer threads (rowops.cuh: the pinned order of the warp-group form)
+    // ---- P1: RMSNorm + quant of the rows: row m on CTA m (all consumer threads) to the workspace, a grid
+    // barrier, then every CTA stages them ----
     for (int m = int(blockIdx.x); m < M; m += int(gridDim.x))
         norm_quant_row_cta<NT, kConsumerBar>(A.x + size_t(m) * A.H, A.norm_w, A.eps, A.H, nullptr, A.q1 + size_t(m) * A.H,
                                              A.s1 + m, red);
+    if (threadIdx.x < 16) rowmax[threadIdx.x] = 0u;
+    ok = grid_barrier_named<kConsumerBar, NT>(A.bar, epoch, &flag) && ok;
+    if (threadIdx.x < M) s1s[threadIdx.x] = __ldcg(A.s1 + threadIdx.x);
+    stage_x_consumers<CW>(A.q1, M, A.H, true, xsm);
     trace_stamp(2);
-    ok = grid_barrier_named<kConsumerBar, NT>(A.bar, epoch, &flag);
-    trace_stamp(3);
-
-    auto phase_x = [&](int ph) {
-        const PhaseDesc& p = P.ph[ph];
-        if (!p.xsmem) return XSrc{p.x, p.K, false, true, true};  // written by this launch: L2 reads
-        stage_x_consumers<CW>(p.x, M, p.K, true, xsm);
-        return XSrc{xsm, p.K + 16, true, true};
-    };
 
     // ---- P2: gate / up, h = silu(g) * u, row maxima of |h| ----
     {
-        const XSrc xs = phase_x(0);
-        trace_stamp(4);
         const PhaseDesc& ph = P.ph[0];
+        const XSrc xs{xsm, A.H + 16, true, true};
         const int C = phase_chunks(ph), ntl = cta_tiles(ph);
-        if (threadIdx.x < 16) rowmax[threadIdx.x] = 0u;
         ok = consume_phase<FMT_GPTQ, LAYOUT_TILED, MT, CW>(P, 0, xs, ring, full, empty, S, part, warp, lane) && ok;
         ok = consumer_sync_and<CW>(ok);
+        trace_stamp(3);
         for (int e = threadIdx.x; e < ntl * M * 16 && ok; e += NT) {
             const int k = e / (M * 16), r = e - k * (M * 16), m = r >> 4, nl = r & 15;
-            const int n = (int(blockIdx.x) + k * int(gridDim.x)) * 16 + nl;
+            const int n = cta_tile(ph, k) * 16 + nl;
             const uint32_t* pk = part + size_t(k) * 2 * C * MT * 128;
-            const float s = __ldcg(A.s1 + m);
+            const float s = s1s[m];
             const float tg = __uint_as_float(tile_total<FMT_GPTQ, MT>(pk, C, 0, m, nl));
             const float tu = __uint_as_float(tile_total<FMT_GPTQ, MT>(pk, C, 1, m, nl));
             const uint16_t gb = f32_to_bf16_bits(__fmul_rn(tg, s));
@@ -99,58 +104,69 @@ __global__ void __launch_bounds__((CW + PW) * 32, 1) mlp_kernel(const Program P,
         consumer_sync<CW>();
         if (threadIdx.x < M) atomicMax(A.amax2 + threadIdx.x, rowmax[threadIdx.x]);
     }
-    trace_stamp(5);
+    trace_stamp(4);
     ok = grid_barrier_named<kConsumerBar, NT>(A.bar, epoch, &flag) && ok;
-    trace_stamp(6);
+    trace_stamp(5);
 
     // ---- P3: q2 = quant(h) ----
+    XSrc xs1{A.q2, A.I, false, true, true};
+    if (threadIdx.x < M) s2s[threadIdx.x] = __fdiv_rn(__uint_as_float(__ldcg(A.amax2 + threadIdx.x)), 127.f);
+    consumer_sync<CW>();
     {
-        // 8-element pieces: one 16-byte load of h, one 8-byte store of permuted q2
+        // 8-element pieces: one 16-byte load of h, one 8-byte store of permuted q2, spread over all CTAs
         const int ppr = A.I >> 3, pieces = M * ppr;
         const int stride = int(gridDim.x) * NT;
         for (int i = int(blockIdx.x) * NT + int(threadIdx.x); i < pieces; i += stride) {
             const int m = i / ppr;
-            const float s = __fdiv_rn(__uint_as_float(__ldcg(A.amax2 + m)), 127.f);
             const uint4 hv = __ldcg(reinterpret_cast<const uint4*>(A.h) + i);
             const uint32_t u[4] = {hv.x, hv.y, hv.z, hv.w};
             float v[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) v[e] = __uint_as_float((e & 1) ? (u[e >> 1] & 0xFFFF0000u) : (u[e >> 1] << 16));
-            reinterpret_cast<uint2*>(A.q2)[i] = quant8_perm(v, s);
+            reinterpret_cast<uint2*>(A.q2)[i] = quant8_perm(v, s2s[m]);
         }
-        if (blockIdx.x == 0 && threadIdx.x < M) A.s2[threadIdx.x] = __fdiv_rn(__uint_as_float(__ldcg(A.amax2 + threadIdx.x)), 127.f);
+        ok = grid_barrier_named<kConsumerBar, NT>(A.bar, epoch, &flag) && ok;
+        if (P.ph[1].xsmem) {
+            stage_x_consumers<CW>(A.q2, M, A.I, true, xsm);
+            xs1 = XSrc{xsm, A.I + 16, true, true};
+        }
     }
-    trace_stamp(7);
-    ok = grid_barrier_named<kConsumerBar, NT>(A.bar, epoch, &flag) && ok;
-    trace_stamp(8);
+    trace_stamp(6);
 
     // ---- P4: down (+ residual) ----
     {
-        const XSrc xs = phase_x(1);
-        trace_stamp(9);
         const PhaseDesc& ph = P.ph[1];
         const int C = phase_chunks(ph), ntl = cta_tiles(ph);
-        ok = consume_phase<FMT_GPTQ, LAYOUT_TILED, MT, CW>(P, 1, xs, ring, full, empty, S, part, warp, lane) && ok;
+        ok = consume_phase<FMT_GPTQ, LAYOUT_TILED, MT, CW>(P, 1, xs1, ring, full, empty, S, part, warp, lane) && ok;
         ok = consumer_sync_and<CW>(ok);
+        trace_stamp(7);
         for (int e = threadIdx.x; e < ntl * M * 16 && ok; e += NT) {
             const int k = e / (M * 16), r = e - k * (M * 16), m = r >> 4, nl = r & 15;
-            const int n = (int(blockIdx.x) + k * int(gridDim.x)) * 16 + nl;
-            const float s = __fdiv_rn(__uint_as_float(__ldcg(A.amax2 + m)), 127.f);
+            const int n = cta_tile(ph, k) * 16 + nl;
             const float tot = __uint_as_float(tile_total<FMT_GPTQ, MT>(part + size_t(k) * C * MT * 128, C, 0, m, nl));
-            uint16_t rr = f32_to_bf16_bits(__fmul_rn(tot, s));
+            uint16_t rr = f32_to_bf16_bits(__fmul_rn(tot, s2s[m]));
             const size_t o = size_t(m) * A.H + n;
             if (A.residual) rr = f32_to_bf16_bits(__fadd_rn(bf16_bits_to_f32(A.x[o]), bf16_bits_to_f32(rr)));
             A.out[o] = rr;
         }
     }
-    trace_stamp(10);
-    grid_exit_named<kConsumerBar, NT>(A.bar);
+    trace_stamp(8);
+    // exit: the last CTA resets the barrier words and clears the row maxima
+    asm volatile("bar.sync %0, %1;" ::"n"(kConsumerBar), "n"(NT) : "memory");
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(A.bar + 1, 1u) == gridDim.x - 1) {
+            for (int m = 0; m < 16; ++m) atomicExch(A.amax2 + m, 0u);
+            atomicExch(A.bar, 0u);
+            atomicExch(A.bar + 1, 0u);
+        }
+    }
 }
 
 size_t mlp_workspace_bytes(int H, int I) {
-    // xn, q1, h, q2 (16 rows each), s1, s2, amax2, barrier words; every piece 256-byte aligned
+    // q1, h, q2 (16 rows each), s1, amax2, barrier words; every piece 256-byte aligned
     auto al = [](size_t b) { return (b + 255) / 256 * 256; };
-    return al(16 * size_t(H) * 2) + al(16 * size_t(H)) + al(16 * size_t(I) * 2) + al(16 * size_t(I)) + 4 * 256;
+    return al(16 * size_t(H)) + al(16 * size_t(I) * 2) + al(16 * size_t(I)) + 4 * 256;
 }
 
 template <int MT, int CW, int PW>
@@ -193,16 +209,17 @@ int launch_mlp(Program& P, MlpArgs& A, cudaStream_t stream) {
     size_t part = 0;
     for (int i = 0; i < P.nph; ++i) {
         const int nt = phase_tiles(P.ph[i]), per_cta = (nt + G - 1) / G;
-        const size_t b = size_t(per_cta) * (P.ph[i].paired ? 2 : 1) * phase_chunks(P.ph[i]) * MT * 128 * 4;
-        part = b > part ? b : part;
+        part = std::max(part, size_t(per_cta) * (P.ph[i].paired ? 2 : 1) * phase_chunks(P.ph[i]) * MT * 128 * 4);
     }
+    P.ph[0].rev = 0;
+    P.ph[1].rev = 1;
     A.max_items = 0;
-    // stage every phase's activations when they fit next to the ring; else drop the largest block
-    for (int i = 0; i < P.nph; ++i) P.ph[i].xsmem = 1;
-    for (int attempt = 0; attempt <= P.nph; ++attempt) {
-        size_t xb = 0;
-        for (int i = 0; i < P.nph; ++i)
-            if (P.ph[i].xsmem) xb = size_t(M) * (P.ph[i].K + 16) > xb ? size_t(M) * (P.ph[i].K + 16) : xb;
+    // the first phase's block is always staged (P1 writes it); the down phase's when it fits next to the ring
+    P.ph[0].xsmem = 1;
+    for (int staged = 1; staged >= 0; --staged) {
+        P.ph[1].xsmem = staged;
+        size_t xb = size_t(M) * (P.ph[0].K + 16);
+        if (staged) xb = std::max(xb, size_t(M) * (P.ph[1].K + 16));
         for (int c = 0; c < kStreamConfigs; ++c) {
             const StreamConfig sc = kStreamConfig[c];
             const StreamPlan plan(stage_bytes<FMT_GPTQ>(), sc.S, part, xb, 0);
@@ -220,11 +237,6 @@ int launch_mlp(Program& P, MlpArgs& A, cudaStream_t stream) {
             }
 #undef MONO_MLP
         }
-        int big = -1;
-        for (int i = 0; i < P.nph; ++i)
-            if (P.ph[i].xsmem && (big < 0 || P.ph[i].K > P.ph[big].K)) big = i;
-        if (big < 0) break;
-        P.ph[big].xsmem = 0;
     }
     return fail(MONO_EINVAL, "mlp: no shared-memory plan fits (M=%d)", M);
 }

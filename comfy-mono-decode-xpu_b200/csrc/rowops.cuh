@@ -12,7 +12,7 @@
 //   r      = 1 / sqrt(total / H + eps)                                        (IEEE division, square root)
 //   out[i] = bf16((x[i] * r) * w[i])
 // Per-token GPTQ quantization: s = amax / 127, q = clamp(rint(x / s), -127, 127) (x / s the IEEE quotient; see
-// quant_one), s = 0 -> q = 0; q is written in the engine's permuted activation layout (bytes 0 2 4 6 1 3 5 7 of
+// quant_i), s = 0 -> q = 0; q is written in the engine's permuted activation layout (bytes 0 2 4 6 1 3 5 7 of
 // every 8).
 #pragma once
 #include "common.cuh"
@@ -25,38 +25,83 @@ __device__ __forceinline__ void wg_sync(int wg) {
     asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");
 }
 
-// q = clamp(rint(fl(v / s)), -127, 127), fl = the IEEE fp32 quotient; s = 0 -> 0. inv = fl(1 / s).
-// a = fl(v * inv) lies within |v / s| 2^-23 (<= 3.1e-5 for |v / s| <= 256) of v / s, and fl(v / s) within
-// |v / s| 2^-24, so when a is farther than 2^-12 from every half-integer, rint(a) == rint(fl(v / s)) (rint only
-// changes at half-integers); otherwise (about 1 value in 2000), or when the product is out of that range, the
-// quotient itself is formed. Same results as dividing every value, at the cost of a multiply.
-// The quotient, out of line: the rare path stays a real branch instead of being evaluated for every value.
-static __device__ __noinline__ float quant_quotient(float v, float s) { return __fdiv_rn(v, s); }
+// Per-token quantization of one value: q = clamp(rint(RN32(v / s)), -127, 127), RN32(v / s) the IEEE fp32 quotient
+// (round to nearest even), rint ties to even; s <= 0 (or NaN) gives 0. Division-free, with the same results:
+//   a = RN(v * inv), inv = RN(1 / s), with s in [2^-120, 2^120] (inv normal): |a - v / s| <= |v / s| 2^-23 and
+//   |RN32(v / s) - v / s| <= |v / s| 2^-24, so for |a| < 200 both lie within 2^-14 of each other. rint(a) is formed
+//   by the magic-number addition t = a + 1.5 * 2^23 (exact integer rounding, ties to even, for |a| < 2^22).
+//   When a is farther than 2^-14 from the half-integer between the two candidate integers, rint(a) is the
+//   answer (about 2^13 values in 2^14). Otherwise quant_near_half decides exactly.
+// quant_near_half: with h the half-integer, X = v - h s is exact in fp64 (h has <= 9 significant bits, s 24, and
+//   v - h s is a small multiple of their common quantum); RN32(v / s) = h exactly when X lies in
+//   [-gap_below s, gap_above s], the gaps being half the fp32 spacing on each side of h (a quarter below |h| =
+//   0.5, the one power of two among half-integers; the ties at the ends go to h, whose significand is even),
+//   and rint(h) is the even neighbour; otherwise RN32(v / s) lies on the side given by the sign of X.
+static __device__ __noinline__ int quant_near_half(float v, float s, float a) {
+    if (!(a == a)) return 0;                                  // NaN (the quotient converts to 0)
+    if (!(fabsf(a) < 200.f)) return a > 0.f ? 127 : -127;     // clamps either way
+    const float h = floorf(a) + 0.5f;
+    const double X = double(v) - double(h) * double(s);
+    const int eb = (__float_as_int(h) >> 23) & 0xFF;
+    const double half_u = ldexp(1.0, eb - 151);               // half the fp32 spacing at |h|: 2^(e - 24)
+    const bool pow2 = (__float_as_int(h) & 0x7FFFFF) == 0;    // |h| = 0.5
+    const double away = half_u * double(s), toward = (pow2 ? 0.5 * half_u : half_u) * double(s);
+    const double above = h > 0.f ? away : toward, below = h > 0.f ? toward : away;
+    const int k = int(h - 0.5f);                              // the integer below h
+    if (X > above) return k + 1;
+    if (X < -below) return k;
+    return (k & 1) ? k + 1 : k;
+}
+// the IEEE quotient itself, for scales outside [2^-120, 2^120]
+static __device__ __noinline__ int quant_by_division(float v, float s) { return __float2int_rn(__fdiv_rn(v, s)); }
 
-__device__ __forceinline__ int8_t quant_one(float v, float s, float inv) {
-    if (!(s > 0.f)) return 0;
-    const float a = __fmul_rn(v, inv), fa = fabsf(a);
-    float t = a;
-    if (!(fa <= 256.f && fabsf((fa - floorf(fa)) - 0.5f) > 0x1p-12f)) t = quant_quotient(v, s);
-    int q = __float2int_rn(t);
-    q = q > 127 ? 127 : (q < -127 ? -127 : q);
-    return int8_t(q);
+__device__ __forceinline__ bool quant_scale_fast(float s) { return s >= 0x1p-120f && s <= 0x1p120f; }
+
+__device__ __forceinline__ int quant_i(float v, float s, float inv) {
+    const float a = __fmul_rn(v, inv);
+    const float t = __fadd_rn(a, 12582912.f);
+    const float d = __fsub_rn(a, __fsub_rn(t, 12582912.f));
+    int q = __float_as_int(t) - 0x4B400000;
+    if (!(fabsf(a) < 200.f && fabsf(d) < 0.5f - 0x1p-14f)) q = quant_near_half(v, s, a);
+    return max(-127, min(127, q));
+}
+
+// 8 values -> 8 int8 (as int) with the scale's checks done once
+__device__ __forceinline__ void quant8_ints(const float (&v)[8], float s, int (&q)[8]) {
+    if (!(s > 0.f)) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) q[e] = 0;
+    } else if (quant_scale_fast(s)) {
+        const float inv = __frcp_rn(s);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) q[e] = quant_i(v[e], s, inv);
+    } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) q[e] = max(-127, min(127, quant_by_division(v[e], s)));
+    }
+}
+
+// 8 quantized values in natural byte order (bytes 0..7)
+__device__ __forceinline__ uint2 quant8(const float (&v)[8], float s) {
+    int q[8];
+    quant8_ints(v, s, q);
+    uint32_t b[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) b[e] = uint32_t(q[e]) & 0xFFu;
+    return make_uint2(b[0] | b[1] << 8 | b[2] << 16 | b[3] << 24, b[4] | b[5] << 8 | b[6] << 16 | b[7] << 24);
 }
 
 // Position of byte i in the engine's permuted activation layout (bytes 0 2 4 6 1 3 5 7 of every 8).
 __device__ __forceinline__ int perm8(int i) { return (i & ~7) | ((i & 1) ? 4 + ((i & 7) >> 1) : ((i & 7) >> 1)); }
 
-// 8 quantized values -> the permuted 8-byte word
+// 8 quantized values -> the permuted 8-byte word (bytes 0 2 4 6 | 1 3 5 7)
 __device__ __forceinline__ uint2 quant8_perm(const float (&v)[8], float s) {
-    uint32_t lo = 0, hi = 0;
-    const float inv = s > 0.f ? __frcp_rn(s) : 0.f;
+    int q[8];
+    quant8_ints(v, s, q);
+    uint32_t b[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-        const uint32_t q = uint32_t(uint8_t(quant_one(v[e], s, inv)));
-        if (e & 1) hi |= q << (8 * (e >> 1));
-        else lo |= q << (8 * (e >> 1));
-    }
-    return make_uint2(lo, hi);
+    for (int e = 0; e < 8; ++e) b[e] = uint32_t(q[e]) & 0xFFu;
+    return make_uint2(b[0] | b[2] << 8 | b[4] << 16 | b[6] << 24, b[1] | b[3] << 8 | b[5] << 16 | b[7] << 24);
 }
 
 // Optional RMSNorm (w != null) and per-token quantization of one row. xn_out (optional): the normalized

@@ -14,8 +14,10 @@
 // of its current phase, and a warp that waited for a slot's use u + 1 while use u had not landed yet
 // would see the older phase of the same parity as complete.
 //
-// Items of a CTA: for every phase of the program, the CTA's 16-row tiles T = blockIdx.x + k * gridDim.x,
-// and per tile its subtiles (gate | up of a paired phase) and 1024-wide chunks:
+// Items of a CTA: for every phase of the program, the CTA's 16-row tiles T = b + k * gridDim.x (b = blockIdx.x, or
+// gridDim.x - 1 - blockIdx.x for a phase marked `rev`: CTAs with more tiles in one phase get fewer in the next,
+// and the ring carries the difference across the grid barrier), and per tile its subtiles (gate | up of a
+// paired phase) and 1024-wide chunks:
 //     i = base(phase) + (k * subs + sub) * C + chunk.
 // Ring slot s = i % S; the producer waits for empty[s] (phase (i / S - 1) & 1) before reusing it, the
 // consumer waits for full[s] (phase (i / S) & 1). Item partials (engine.cuh compute_item) go to shared
@@ -63,10 +65,16 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 }
 
 __device__ __forceinline__ int phase_subs(const PhaseDesc& p) { return p.paired ? 2 : 1; }
+// this CTA's position in the phase's round robin
+__device__ __forceinline__ int cta_slot(const PhaseDesc& p) {
+    return p.rev ? int(gridDim.x) - 1 - int(blockIdx.x) : int(blockIdx.x);
+}
 __device__ __forceinline__ int cta_tiles(const PhaseDesc& p) {
-    const int nt = phase_tiles(p), b = int(blockIdx.x), G = int(gridDim.x);
+    const int nt = phase_tiles(p), b = cta_slot(p), G = int(gridDim.x);
     return b < nt ? (nt - 1 - b) / G + 1 : 0;
 }
+// global tile of this CTA's k-th tile of the phase
+__device__ __forceinline__ int cta_tile(const PhaseDesc& p, int k) { return cta_slot(p) + k * int(gridDim.x); }
 __device__ __forceinline__ int cta_items(const PhaseDesc& p) { return cta_tiles(p) * phase_subs(p) * (p.K >> 10); }
 __device__ __forceinline__ int cta_base(const Program& P, int ph) {
     int b = 0;
@@ -75,33 +83,13 @@ __device__ __forceinline__ int cta_base(const Program& P, int ph) {
 }
 __device__ __forceinline__ int cta_total(const Program& P) { return cta_base(P, P.nph); }
 
-struct ItemRef {
-    int ph, k, sub, c;
-};
-__device__ __forceinline__ ItemRef item_at(const Program& P, int i) {
-    ItemRef r{0, 0, 0, 0};
-    while (r.ph < P.nph - 1) {
-        const int n = cta_items(P.ph[r.ph]);
-        if (i < n) break;
-        i -= n;
-        ++r.ph;
-    }
-    const int C = P.ph[r.ph].K >> 10, per = phase_subs(P.ph[r.ph]) * C;
-    r.k = i / per;
-    const int rem = i - r.k * per;
-    r.sub = rem / C;
-    r.c = rem - r.sub * C;
-    return r;
-}
-
-// Issue the copy of item (k, sub, c) of phase p into `stage`, completing on `full`. TILED: lane 0, one bulk
+// Issue the copy of item (tile T, sub, c) of phase p into `stage`, completing on `full`. TILED: lane 0, one bulk
 // copy (the full barrier counts 1 arrival + the bytes). ROW: every lane gathers its 16-byte pieces with
 // cp.async and arrives once when they land (the full barrier counts 32 arrivals).
 template <int FMT, int LAYOUT>
-__device__ __forceinline__ void issue_item(const PhaseDesc& p, int k, int sub, int c, uint8_t* stage, uint64_t* full,
-                                           int lane) {
+__device__ __forceinline__ void issue_tile_item(const PhaseDesc& p, int T, int sub, int c, uint8_t* stage, uint64_t* full,
+                                                int lane) {
     constexpr int SB = Fmt<FMT>::SB;
-    const int T = int(blockIdx.x) + k * int(gridDim.x);
     int mat, lt;
     resolve(p, T, sub, mat, lt);
     const MatDesc& w = p.m[mat];
@@ -134,6 +122,13 @@ __device__ __forceinline__ void issue_item(const PhaseDesc& p, int k, int sub, i
     }
 }
 
+// The same for the k-th round-robin tile of this CTA (T = blockIdx.x + k * gridDim.x).
+template <int FMT, int LAYOUT>
+__device__ __forceinline__ void issue_item(const PhaseDesc& p, int k, int sub, int c, uint8_t* stage, uint64_t* full,
+                                           int lane) {
+    issue_tile_item<FMT, LAYOUT>(p, cta_tile(p, k), sub, c, stage, full, lane);
+}
+
 // Ask the L2 to fetch item (k, sub, c) of phase p (TILED layout: one contiguous block) ahead of its copy.
 template <int FMT>
 __device__ __forceinline__ void prefetch_item_l2(const PhaseDesc& p, int k, int sub, int c) {
@@ -145,43 +140,47 @@ __device__ __forceinline__ void prefetch_item_l2(const PhaseDesc& p, int k, int 
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(kStageW + SB) : "memory");
 }
 
-template <int FMT, int LAYOUT>
-__device__ __forceinline__ void produce_item(const Program& P, const ItemRef& r, uint8_t* stage, uint64_t* full,
-                                             int lane) {
-    issue_item<FMT, LAYOUT>(P.ph[r.ph], r.k, r.sub, r.c, stage, full, lane);
-}
-
-// Incremental walk over a CTA's items (no divisions per step).
+// Incremental walk over a CTA's items across the phases of a program, in request order (no divisions per
+// step): the current item is (phase ph, tile T, subtile sub, chunk c); `left` items of the phase remain after it.
 struct ItemWalk {
-    ItemRef r;
-    int ntk, subs, C;
+    int ph, T, sub, c, left, subs, C, tstep;
     bool done;
-    __device__ void load_phase(const Program& P) {
-        const PhaseDesc& p = P.ph[r.ph];
-        ntk = cta_tiles(p);
+    // position at the n-th item of phase ph for this CTA; false if the phase has fewer
+    __device__ bool enter(const Program& P, int n) {
+        const PhaseDesc& p = P.ph[ph];
+        const int cnt = cta_items(p);
+        if (n >= cnt) return false;
         subs = phase_subs(p);
         C = p.K >> 10;
+        const int per = subs * C, k = n / per, r = n - k * per;
+        T = cta_tile(p, k);
+        tstep = int(gridDim.x);
+        sub = r / C;
+        c = r - sub * C;
+        left = cnt - 1 - n;
+        return true;
     }
     __device__ void start(const Program& P, int i) {
-        done = i >= cta_total(P);
-        if (done) return;
-        r = item_at(P, i);
-        load_phase(P);
+        done = false;
+        for (ph = 0; ph < P.nph; ++ph) {
+            if (enter(P, i)) return;
+            i -= cta_items(P.ph[ph]);
+        }
+        done = true;
     }
     __device__ void step(const Program& P) {
-        if (++r.c < C) return;
-        r.c = 0;
-        if (++r.sub < subs) return;
-        r.sub = 0;
-        if (++r.k < ntk) return;
-        r.k = 0;
-        do {
-            if (++r.ph >= P.nph) {
-                done = true;
-                return;
-            }
-            load_phase(P);
-        } while (ntk == 0);
+        if (left == 0) {
+            while (++ph < P.nph)
+                if (enter(P, 0)) return;
+            done = true;
+            return;
+        }
+        --left;
+        if (++c < C) return;
+        c = 0;
+        if (++sub < subs) return;
+        sub = 0;
+        T += tstep;
     }
 };
 
@@ -199,7 +198,7 @@ __device__ __forceinline__ bool produce_all(const Program& P, uint8_t* ring, uin
         const int s = i % S;
         if (i >= S) ok = __all_sync(0xffffffffu, mbar_wait(&empty[s], ((i / S) - 1) & 1));
         if (!ok) break;
-        produce_item<FMT, LAYOUT>(P, w.r, ring + size_t(s) * stage_bytes<FMT>(), &full[s], lane);
+        issue_tile_item<FMT, LAYOUT>(P.ph[w.ph], w.T, w.sub, w.c, ring + size_t(s) * stage_bytes<FMT>(), &full[s], lane);
         for (int q = 0; q < PW && !w.done; ++q) w.step(P);
     }
     // items p, p + PW, ..., i - PW were issued: wait for the last use of each of this producer's S / PW slots
