@@ -3,9 +3,11 @@
 // Two forms. Committing (ctl == null): M sequential rows, each advancing the recurrent and conv state, which
 // are written back. Deferred (ctl != null; the reference's replay + verify, :385-567): the n = ctl[0] rows
 // accepted at the previous step (slots ctl[2 + i], inputs saved by that step) are replayed first and their
-// states persisted; then the M verify rows of this step run as a chain on a register copy (outputs only,
-// nothing persisted); their inputs are saved for the next step's replay. The conv state advances by the
-// replayed rows only.
+// states persisted; then this step's verify tree runs on a register copy (outputs only, nothing persisted): each
+// verify row's conv reads its ancestors (parents ctl[10 + t]), and the program ctl[18 + e] (slot | 32 * commit)
+// orders the rows so that every row sees the state after its parent (committing entries advance the copy,
+// the others use temporaries). The verify inputs are saved for the next step's replay. The conv state advances
+// by the replayed rows only.
 //
 // Kernel 1 (one thread per qkv channel): the depthwise causal conv of width 4, y = bf16(fma chain x[t] w[3],
 // x[t-1] w[2], .. from 0), out = bf16(y / (1 + exp(-y))), over the conv state (3 newest inputs, oldest
@@ -82,12 +84,17 @@ __global__ void __launch_bounds__(kRG * kDH) gdn_delta_kernel(const GdnArgs A) {
         vsm[t][d] = bf16_bits_to_f32(A.conv_out[size_t(t) * A.C + 2 * KD + h * kDH + d]);
     }
     if (tid < 2 * R) gsm[tid >> 1][tid & 1] = A.gates[((tid >> 1) * A.HV + h) * 2 + (tid & 1)];
+    for (int e = tid; e < M * kDH; e += blockDim.x) raw[e / kDH][e % kDH] = 0.f;  // rows no entry names
     float st[kRPG];
     float* S = A.state + (size_t(h) * kDH + rg * kRPG) * kDH + col;
 #pragma unroll
     for (int r = 0; r < kRPG; ++r) st[r] = S[size_t(r) * kDH];
     __syncthreads();
-    for (int t = 0; t < R; ++t) {
+    // the entries: the replayed rows (committing), then the verify program (gdn_entry)
+    const int E = n + gdn_verify_entries(A);
+    for (int e = 0; e < E; ++e) {
+        const GdnEntry en = gdn_entry(A, n, e);
+        const int t = en.row;
         const float decay = gsm[t][0], beta = gsm[t][1];
         const float v = vsm[t][col];
         // the row group's 32 k and q values as 16-byte shared loads (a warp's lanes share the row group: broadcast)
@@ -99,26 +106,37 @@ __global__ void __launch_bounds__(kRG * kDH) gdn_delta_kernel(const GdnArgs A) {
             kr[4 * r4] = k4.x, kr[4 * r4 + 1] = k4.y, kr[4 * r4 + 2] = k4.z, kr[4 * r4 + 3] = k4.w;
             qr[4 * r4] = q4.x, qr[4 * r4 + 1] = q4.y, qr[4 * r4 + 2] = q4.z, qr[4 * r4 + 3] = q4.w;
         }
+        // a committing entry advances the state; another computes its row from temporaries (the same operations)
         float mem = 0.f;
+        if (en.commit) {
 #pragma unroll
-        for (int r = 0; r < kRPG; ++r) {
-            st[r] *= decay;
-            mem = fmaf(st[r], kr[r], mem);
+            for (int r = 0; r < kRPG; ++r) {
+                st[r] *= decay;
+                mem = fmaf(st[r], kr[r], mem);
+            }
+        } else {
+#pragma unroll
+            for (int r = 0; r < kRPG; ++r) mem = fmaf(st[r] * decay, kr[r], mem);
         }
         part[0][rg][col] = mem;
         __syncthreads();
         const float kv = part[0][0][col] + part[0][1][col] + part[0][2][col] + part[0][3][col];
         const float delta = (v - kv) * beta;
         float o = 0.f;
+        if (en.commit) {
 #pragma unroll
-        for (int r = 0; r < kRPG; ++r) {
-            st[r] = fmaf(kr[r], delta, st[r]);
-            o = fmaf(st[r], qr[r], o);
+            for (int r = 0; r < kRPG; ++r) {
+                st[r] = fmaf(kr[r], delta, st[r]);
+                o = fmaf(st[r], qr[r], o);
+            }
+        } else {
+#pragma unroll
+            for (int r = 0; r < kRPG; ++r) o = fmaf(fmaf(kr[r], delta, st[r] * decay), qr[r], o);
         }
         part[1][rg][col] = o;
         __syncthreads();
-        if (rg == 0 && t >= n) raw[t - n][col] = bf16_round(part[1][0][col] + part[1][1][col] + part[1][2][col] + part[1][3][col]);
-        if (A.ctl != nullptr && t == n - 1)  // the committed state after the replay
+        if (rg == 0 && en.out >= 0) raw[en.out][col] = bf16_round(part[1][0][col] + part[1][1][col] + part[1][2][col] + part[1][3][col]);
+        if (A.ctl != nullptr && e == n - 1)  // the committed state after the replay
 #pragma unroll
             for (int r = 0; r < kRPG; ++r) S[size_t(r) * kDH] = st[r];
     }

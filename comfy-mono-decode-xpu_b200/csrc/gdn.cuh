@@ -15,6 +15,39 @@ extern __device__ uint16_t g_gdn_silu[65536];
 __device__ __forceinline__ float gdn_silu_formula(float y) { return y / (1.f + expf(-y)); }
 __device__ __forceinline__ float gdn_silu(float y_bf16) { return bf16_bits_to_f32(g_gdn_silu[f32_to_bf16_bits(y_bf16)]); }
 
+// ctl (deferred form) = [pending, parity, accepted slots[8], parents[8], program[8]] (csrc/mono_gdn.sycl:38-40).
+// parent(t) of verify row t: a row before it, or -1 (the root's parent; anything else reads as -1). Without ctl (the
+// committing form) the rows are a chain.
+__device__ __forceinline__ int gdn_parent(const GdnArgs& A, int t) {
+    if (A.ctl == nullptr) return t - 1;
+    const int p = __ldcg(A.ctl + 2 + kGdnMaxRows + t);
+    return p >= 0 && p < t ? p : -1;
+}
+// Verify entries of the step: the program's words p = slot | 32 * commit, up to the first one whose slot is outside
+// [0, M) (the committing form: every row in order, each committing).
+__device__ __forceinline__ int gdn_verify_entries(const GdnArgs& A) {
+    if (A.ctl == nullptr) return A.M;
+    int e = 0;
+    while (e < kGdnMaxRows) {
+        const int p = __ldcg(A.ctl + 2 + 2 * kGdnMaxRows + e);
+        if (p < 0 || (p & 15) >= A.M) break;
+        ++e;
+    }
+    return e;
+}
+// Entry e of the step's list (replayed rows first: e < n): its conv-output row, its output slot (-1: none) and
+// whether it advances the running state.
+struct GdnEntry {
+    int row, out;
+    bool commit;
+};
+__device__ __forceinline__ GdnEntry gdn_entry(const GdnArgs& A, int n, int e) {
+    if (e < n) return GdnEntry{e, -1, true};
+    if (A.ctl == nullptr) return GdnEntry{e, e, true};
+    const int p = __ldcg(A.ctl + 2 + 2 * kGdnMaxRows + (e - n));
+    return GdnEntry{n + (p & 15), p & 15, (p & 32) != 0};
+}
+
 __device__ __forceinline__ int gdn_pending(const GdnArgs& A) {
     if (A.ctl == nullptr) return 0;
     const int n = __ldcg(A.ctl);
@@ -25,13 +58,24 @@ __device__ __forceinline__ int gdn_slot(const GdnArgs& A, int i) {
     return s < 0 ? 0 : (s >= kGdnMaxRows ? kGdnMaxRows - 1 : s);
 }
 
+// a[i] of a small register array at a run-time index, as a select chain (no local-memory indexing)
+template <int N>
+__device__ __forceinline__ float pick(const float (&a)[N], int i) {
+    float v = a[0];
+#pragma unroll
+    for (int k = 1; k < N; ++k) v = i == k ? a[k] : v;
+    return v;
+}
+
 // Work item i of the conv step (one thread each, i < max(C, (n + M) * HV)): the gates of (row, head) i, the
-// saved a / b of this step's rows, and the depthwise causal conv of channel i over the conv state and the
-// replayed then the verify rows:
+// saved a / b of this step's rows, and the depthwise causal conv of channel i:
 //   gates: decay = exp(g_decay * softplus(a + dt_bias)) (softplus(v) = v above 20), beta = bf16(sigmoid(b))
 //   conv:  y = bf16(fma chain x[t] w[3], x[t-1] w[2], .. from 0), out = bf16(y / (1 + exp(-y)))
-// The conv state becomes the three newest committed inputs (the replayed rows in the deferred form, all rows
-// in the committing form). All activations are read through L2 (they may have been written by this launch).
+// The replayed rows run as a chain over the conv state (an accepted path: each row's predecessors are the rows
+// before it); verify row t reads its own input, then its ancestors' (gdn_parent), then the committed history (the
+// conv state after the replay), newest first (csrc/mono_gdn.sycl:313-375). The conv state becomes the three
+// newest committed inputs (the replayed rows in the deferred form, all rows in the committing form). All
+// activations are read through L2 (they may have been written by this launch).
 __device__ __forceinline__ void gdn_conv_item(const GdnArgs& A, int i) {
     const int n = gdn_pending(A), R = n + A.M;
     uint16_t sa = 0, sb = 0;
@@ -57,40 +101,81 @@ __device__ __forceinline__ void gdn_conv_item(const GdnArgs& A, int i) {
     if (i >= A.C) return;
     // every load first (the stores below may alias nothing the compiler can prove, so loads after a store
     // would wait for it)
-    uint16_t raw[kGdnMaxAll];
-    float w[4], hist[3 + kGdnMaxAll];
+    uint16_t rp[kGdnMaxRows], rv[kGdnMaxRows];  // raw inputs of the replayed rows / of the verify rows
+    float w[4], hist[3 + kGdnMaxRows], vr[kGdnMaxRows];
+    int par[kGdnMaxRows];
 #pragma unroll
-    for (int t = 0; t < kGdnMaxAll; ++t) {
-        raw[t] = 0;
-        if (t < n) raw[t] = __ldcg(A.prev_qkv + size_t(gdn_slot(A, t)) * A.C + i);
-        else if (t < R) raw[t] = __ldcg(A.qkv + size_t(t - n) * A.qkv_stride + i);
+    for (int t = 0; t < kGdnMaxRows; ++t) {
+        rp[t] = t < n ? __ldcg(A.prev_qkv + size_t(gdn_slot(A, t)) * A.C + i) : uint16_t(0);
+        rv[t] = t < A.M ? __ldcg(A.qkv + size_t(t) * A.qkv_stride + i) : uint16_t(0);
+        par[t] = t < A.M ? gdn_parent(A, t) : -1;
     }
 #pragma unroll
     for (int d = 0; d < 4; ++d) w[d] = bf16_bits_to_f32(A.conv_w[size_t(i) * 4 + d]);
 #pragma unroll
     for (int r = 0; r < 3; ++r) hist[r] = bf16_bits_to_f32(A.conv_state[size_t(i) * 3 + r]);
-#pragma unroll
-    for (int t = 0; t < kGdnMaxAll; ++t) hist[3 + t] = bf16_bits_to_f32(raw[t]);
     if (A.save_qkv != nullptr)
 #pragma unroll
-        for (int t = 0; t < kGdnMaxAll; ++t)
-            if (t >= n && t < R) A.save_qkv[size_t(t - n) * A.C + i] = raw[t];
+        for (int t = 0; t < kGdnMaxRows; ++t)
+            if (t < A.M) A.save_qkv[size_t(t) * A.C + i] = rv[t];
+    // replayed rows: a chain over the conv state; hist[3 + t] = input of replayed row t
 #pragma unroll
-    for (int t = 0; t < kGdnMaxAll; ++t) {
-        if (t >= R) break;
-        float sum = 0.f;
+    for (int t = 0; t < kGdnMaxRows; ++t) {
+        hist[3 + t] = bf16_bits_to_f32(rp[t]);
+        if (t < n) {
+            float sum = 0.f;
 #pragma unroll
-        for (int d = 0; d < 4; ++d) sum = fmaf(hist[3 + t - d], w[3 - d], sum);
-        const float y = bf16_round(sum);
-        A.conv_out[size_t(t) * A.C + i] = g_gdn_silu[f32_to_bf16_bits(y)];
+            for (int d = 0; d < 4; ++d) sum = fmaf(hist[3 + t - d], w[3 - d], sum);
+            const float y = bf16_round(sum);
+            A.conv_out[size_t(t) * A.C + i] = g_gdn_silu[f32_to_bf16_bits(y)];
+        }
     }
-    const int keep = A.ctl != nullptr ? n : R;
+    // the committed window after the replay: the three newest of (conv state, replayed inputs), oldest first
+    float win[3];
 #pragma unroll
     for (int r = 0; r < 3; ++r) {
         float v = hist[r];
 #pragma unroll
-        for (int t = 0; t < kGdnMaxAll + 3; ++t)
-            if (t == keep + r) v = hist[t];
+        for (int t = 1; t < 3 + kGdnMaxRows; ++t)
+            if (t == n + r) v = hist[t];
+        win[r] = v;
+    }
+    // verify rows: own input, then the ancestors' inputs, then the committed window (newest first)
+#pragma unroll
+    for (int t = 0; t < kGdnMaxRows; ++t) vr[t] = bf16_bits_to_f32(rv[t]);
+#pragma unroll
+    for (int t = 0; t < kGdnMaxRows; ++t) {
+        if (t >= A.M) break;
+        float sum = fmaf(vr[t], w[3], 0.f);
+        int anc = t, miss = 0;
+#pragma unroll
+        for (int d = 1; d < 4; ++d) {
+            int pa = -1;
+#pragma unroll
+            for (int u = 0; u < kGdnMaxRows; ++u)
+                if (u == anc) pa = par[u];
+            anc = anc >= 0 ? pa : -1;
+            miss += anc < 0;
+            const float v = anc >= 0 ? pick(vr, anc) : (miss == 1 ? win[2] : (miss == 2 ? win[1] : win[0]));
+            sum = fmaf(v, w[3 - d], sum);
+        }
+        const float y = bf16_round(sum);
+        A.conv_out[size_t(n + t) * A.C + i] = g_gdn_silu[f32_to_bf16_bits(y)];
+    }
+    // the new conv state: the committed window (deferred form), or the three newest of (conv state, all M rows)
+    // (committing form, n = 0: sequence position M + r, oldest first)
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+        float v = win[r];
+        if (A.ctl == nullptr) {
+            v = hist[r];
+#pragma unroll
+            for (int k = 1; k < 3; ++k)
+                if (A.M + r == k) v = hist[k];
+#pragma unroll
+            for (int t = 0; t < kGdnMaxRows; ++t)
+                if (A.M + r == t + 3) v = vr[t];
+        }
         A.conv_state[size_t(i) * 3 + r] = f32_to_bf16_bits(v);
     }
 }

@@ -294,16 +294,26 @@ static __device__ __noinline__ void prog_gdn_delta(const GdnArgs& A, float* scra
     const float* kh_ = kn + hl * kGdnMaxAll * kDH + rg * kRPG;
     float* p0 = part;
     float* p1 = part + kRG * CPC;
-    for (int t = 0; t < R; ++t) {
+    if (active && rg == 0)  // rows no entry names read as zero (the entries below overwrite the others)
+        for (int m = 0; m < A.M; ++m) A.core[size_t(m) * total + gc] = 0;
+    const int E = n + gdn_verify_entries(A);
+    for (int e = 0; e < E; ++e) {
+        const GdnEntry en = gdn_entry(A, n, e);
+        const int t = en.row;
         float mem = 0.f, decay = 1.f, beta = 0.f, v = 0.f;
         if (active) {
             decay = gsm[(t * 2 + hl) * 2];
             beta = gsm[(t * 2 + hl) * 2 + 1];
             v = vsm[t * CPC + cl];
+            if (en.commit) {
 #pragma unroll
-            for (int r = 0; r < kRPG; ++r) {
-                st[r] *= decay;
-                mem = fmaf(st[r], kh_[t * kDH + r], mem);
+                for (int r = 0; r < kRPG; ++r) {
+                    st[r] *= decay;
+                    mem = fmaf(st[r], kh_[t * kDH + r], mem);
+                }
+            } else {
+#pragma unroll
+                for (int r = 0; r < kRPG; ++r) mem = fmaf(st[r] * decay, kh_[t * kDH + r], mem);
             }
         }
         p0[rg * CPC + cl] = mem;
@@ -312,17 +322,22 @@ static __device__ __noinline__ void prog_gdn_delta(const GdnArgs& A, float* scra
         if (active) {
             const float kv = p0[cl] + p0[CPC + cl] + p0[2 * CPC + cl] + p0[3 * CPC + cl];
             const float delta = (v - kv) * beta;
+            if (en.commit) {
 #pragma unroll
-            for (int r = 0; r < kRPG; ++r) {
-                st[r] = fmaf(kh_[t * kDH + r], delta, st[r]);
-                o = fmaf(st[r], qh[t * kDH + r], o);
+                for (int r = 0; r < kRPG; ++r) {
+                    st[r] = fmaf(kh_[t * kDH + r], delta, st[r]);
+                    o = fmaf(st[r], qh[t * kDH + r], o);
+                }
+            } else {
+#pragma unroll
+                for (int r = 0; r < kRPG; ++r) o = fmaf(fmaf(kh_[t * kDH + r], delta, st[r] * decay), qh[t * kDH + r], o);
             }
         }
         p1[rg * CPC + cl] = o;
         consumer_sync<CW>();
-        if (active && rg == 0 && t >= n)
-            A.core[size_t(t - n) * total + gc] = f32_to_bf16_bits(bf16_round(p1[cl] + p1[CPC + cl] + p1[2 * CPC + cl] + p1[3 * CPC + cl]));
-        if (active && A.ctl != nullptr && t == n - 1)
+        if (active && rg == 0 && en.out >= 0)
+            A.core[size_t(en.out) * total + gc] = f32_to_bf16_bits(bf16_round(p1[cl] + p1[CPC + cl] + p1[2 * CPC + cl] + p1[3 * CPC + cl]));
+        if (active && A.ctl != nullptr && e == n - 1)
 #pragma unroll
             for (int r = 0; r < kRPG; ++r) Sp[size_t(r) * kDH] = st[r];
     }

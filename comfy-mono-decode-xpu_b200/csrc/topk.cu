@@ -9,69 +9,11 @@
 // pairwise in shared memory and writes its list (and argmax best) to the workspace. Kernel 2, CTA = row: merges
 // the slices' lists and inverts the ranks to indices. Integer work: bit-exact.
 #include "launch.h"
+#include "ranks.cuh"
 
 namespace mono {
 
-constexpr int kTkK = 8, kTkThreads = 256, kTkSlices = 128;
-
-__device__ __forceinline__ uint64_t rank_topk(uint16_t bits, uint32_t i) {
-    const uint32_t mask = (bits & 0x8000u) ? 0xFFFFu : 0x8000u;
-    const bool nan = (bits & 0x7FFFu) > 0x7F80u;
-    const uint32_t conv = nan ? 0xFFFFu : ((bits ^ mask) & 0xFFFFu);
-    const uint32_t it = i >> 15, off = i & 32767u;
-    const uint32_t g = (it << 15) | (((off & 8191u) >> 3) << 5) | ((off >> 13) << 3) | (off & 7u);
-    return (uint64_t(conv) << 32) | uint64_t(0xFFFFFFFFu - g);
-}
-__device__ __forceinline__ uint64_t rank_argmax(uint16_t bits, uint32_t i) {
-    const bool nan = (bits & 0x7FFFu) > 0x7F80u;
-    uint32_t key;
-    if (nan) {
-        key = 0xFFFFFFFFu;
-    } else {
-        const uint16_t b = (bits & 0x7FFFu) == 0 ? 0 : bits;
-        key = (b & 0x8000u) ? uint32_t(0x7FFFu - (b & 0x7FFFu)) : uint32_t(0x8000u + b);
-    }
-    return (uint64_t(key) << 32) | uint64_t(0xFFFFFFFFu - i);
-}
-__device__ __forceinline__ uint32_t topk_index(uint64_t r) {
-    const uint32_t g = 0xFFFFFFFFu - uint32_t(r);
-    return ((g >> 15) << 15) | (((g >> 3) & 3u) << 13) | (((g >> 5) & 1023u) << 3) | (g & 7u);
-}
-__device__ __forceinline__ void insert_rank(uint64_t (&top)[kTkK], uint64_t r, int k) {
-    if (r <= top[k - 1]) return;
-    int p = k - 1;
-#pragma unroll
-    for (int q = kTkK - 1; q > 0; --q)
-        if (q <= p && top[q - 1] < r) {
-            top[q] = top[q - 1];
-            p = q - 1;
-        }
-    // p is the first slot whose predecessor is >= r (or 0)
-#pragma unroll
-    for (int q = 0; q < kTkK; ++q)
-        if (q == p) top[q] = r;
-}
-// merge the sorted (descending) lists at a and b, keep the k best at a
-__device__ __forceinline__ void merge_lists(uint64_t* lst, int a, int b, int k) {
-    uint64_t out[kTkK];
-    int i = 0, j = 0;
-#pragma unroll
-    for (int o = 0; o < kTkK; ++o) {
-        if (o < k) {
-            const uint64_t x = lst[a + i], y = lst[b + j];
-            if (x >= y) {
-                out[o] = x;
-                ++i;
-            } else {
-                out[o] = y;
-                ++j;
-            }
-        }
-    }
-#pragma unroll
-    for (int o = 0; o < kTkK; ++o)
-        if (o < k) lst[a + o] = out[o];
-}
+constexpr int kTkThreads = 256, kTkSlices = 128;
 
 __global__ void __launch_bounds__(kTkThreads) topk_partial_kernel(const TopkArgs A) {
     __shared__ uint64_t lst[kTkThreads * kTkK];

@@ -656,6 +656,32 @@ def layer_gdn(x, norm_in, eps_in, qkv_w, z_w, wab, conv_w, conv_state, dt_bias, 
     return out
 
 
+_lmhead_ws = {}
+
+
+def lmhead_pick(x, w, k=0, logits=False, argmax_out=None, topk_out=None, children=None, dst=None):
+    """bf16 lm_head of M <= 8 rows with the greedy / draft pick fused (include/mono_b200.h mono_lmhead_pick):
+    x bf16 [M, K] (rows 16-byte aligned), w bf16 [V, K]. Returns (argmax int64 [M], top-k int64 [M, k] or None,
+    logits bf16 [M, V] or None). With children (int32 device tensor of up to 8 slots, -1 ends) and dst (int64 device
+    row), also writes the draft pick into dst (M must be 1)."""
+    _cuda(x, w)
+    _check(x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1 and
+           w.is_contiguous() and w.dim() == 2 and w.size(1) == x.size(1), "x bf16 [M, K], w bf16 [V, K]")
+    M, K = x.shape
+    V = w.size(0)
+    am = argmax_out if argmax_out is not None else torch.empty(M, dtype=torch.int64, device=x.device)
+    tk = None
+    if k > 0 and children is None:
+        tk = topk_out if topk_out is not None else torch.empty(M, k, dtype=torch.int64, device=x.device)
+    lg = torch.empty(M, V, dtype=torch.bfloat16, device=x.device) if logits else None
+    need = _lib.load().mono_lmhead_workspace()
+    ws = _workspace(_lmhead_ws, (x.device,), need, x.device)
+    with torch.cuda.device(x.device):
+        _lib.call("mono_lmhead_pick", _p(x), x.stride(0), _p(w), M, V, K, k, _p(lg), _p(am), _p(tk), _p(children),
+                  _p(dst), _p(ws), need, _stream(x.device))
+    return am, tk, lg
+
+
 def gemv_bf16(x, w, out=None):
     """bf16 GEMV of the draft head's projections (include/mono_b200.h mono_gemv_bf16): x bf16 [M, K] (M <= 8,
     unit column stride), w bf16 [N, K] contiguous -> bf16 [M, N] (out: any [M, N] view with unit column stride),

@@ -4,21 +4,23 @@ Random-init weights of the model's architecture (no checkpoint is available): 32
 full-attention pattern, hidden 4096, MLP 12288, vocab 151936, bf16 embedding and lm_head ~ N(0, 0.02), every body
 projection GPTQ W4A8 (int4 uniform in [-8, 7], fp16 group-128 scales |N(0,1)| * 0.02 / 7 + 1e-4), a 1-layer bf16 MTP
 head. One decode step of one stream, queued without any host read-back (the reference's device MTP loop,
-comfy_mono_decode_xpu/mtp_loop.py):
+comfy_mono_decode_xpu/mtp_loop.py:270-341):
 
-  draft    depth-D chain: d_0 = the step's next token, h_0 = its hidden row; d_j = argmax lm_head(MTP(h_{j-1},
-           embed(d_{j-1}))) (the reference's draft head, comfy_mono_decode_xpu/draft_head.py:190-232)
-  verify   the D + 1 rows [d_0 .. d_D] through the 32 layers (layer_pre / attention or GDN / layer_post / MLP),
-           final norm, lm_head, greedy argmax per row
-  accept   mono_mtp_accept: the accept walk over the chain, the counters, the GDN replay ctl, next token and
-           hidden row (all on the device)
+  draft    a depth-4 top-k tree of 8 nodes (the reference test's tree4s1m8 spec, tests/test_mtp_accept.py:46-47: the
+           chain 0-1-2-3-4 and one sibling beside each of nodes 1, 2, 3): draft k (k = 0..3) runs the MTP head on
+           chain node k's token and the previous draft's hidden row; its lm_head pick (the bf16 lm_head, fused with
+           the argmax and top-2: mono_lmhead_pick) writes the argmax into the first child's verify token and the
+           second-best into the second child's (the reference's draft pick, csrc/draft_lmhead.sycl:4-17)
+  verify   the 8 tree rows through the 32 layers (layer_pre / attention or GDN / layer_post / MLP), with the tree
+           attention mask, the GDN verify tree (parents and program in the ctl row), final norm, lm_head + argmax
+  accept   mono_mtp_accept: the greedy accept walk over the tree, the counters, the GDN replay ctl, the KV slot moves
+           of an off-chain path, next token and hidden row (all on the device)
 
 Per layer: full attention = rowlin(norm -> q|k|v) -> qk_norm_rope_kv -> tree attention -> rowlin(gate -> o_proj +
 residual) -> fused MLP; GDN = rowlin(norm -> qkv|z, xn) -> a|b (mono_gdn_ab) -> deferred GDN step ->
-rowlin(quant -> out_proj + residual) -> fused MLP. The verify rows form a chain (the GDN step's verify rows run as a
-chain); the bf16 MTP head's five projections run on this build's bf16 GEMV (mono_gemv_bf16; cuBLAS through torch's
-F.linear with draft_gemv=False) and the verify's 5-row lm_head on cuBLAS; the drafts' lm_head is a W4A8 GPTQ copy on
-this build's linear kernel; the head's norms and gates are the row kernels (mono_rmsnorm_add, mono_lut_mul).
+rowlin(quant -> out_proj + residual) -> fused MLP. The MTP head's five bf16 projections run on this build's bf16
+GEMV (mono_gemv_bf16; cuBLAS through torch's F.linear with draft_gemv=False); its norms and gates are the row kernels
+(mono_rmsnorm_add, mono_lut_mul).
 """
 from __future__ import annotations
 
@@ -48,30 +50,25 @@ class Qwen35Config:
     gdn_v_heads: int = 32
     gdn_dim: int = 128
     eps: float = 1e-6
-    depth: int = 4               # MTP draft depth: D + 1 verify rows
+    tree: tuple = (2, 2, 2, 1)   # children per chain node (tree4s1m8: depth 4, 8 verify rows); (1, 1, 1, 1): chain
+
+    @property
+    def depth(self) -> int:      # MTP drafts per step = the tree's chain depth
+        return len(self.tree)
 
     def is_attn(self, i: int) -> bool:
         return (i + 1) % self.attn_every == 0
 
 
-def _w4(N, K, g, dev):
-    """A random GPTQ W4 matrix (BASELINE configs[0] distributions) in the TILED layout."""
+def _w4(N, K, g, dev, keep=None, name=None):
+    """A random GPTQ W4 matrix (BASELINE configs[0] distributions) in the TILED layout. keep (a dict): also keep
+    the checkpoint-layout packed / scales under `name` (for tests)."""
     packed = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev, generator=g)
     scales = (torch.randn(N, K // 128, device=dev, generator=g).abs() * (0.02 / 7) + 1e-4).half()
     t = _C.w4_repack(0, packed, scales, N, K)
-    del packed, scales
+    if keep is not None:
+        keep[name] = (packed, scales)
     return t
-
-
-def quantize_gptq(w, group=128):
-    """Round-to-nearest GPTQ-format copy of a bf16 [N, K] weight: fp16 scale per (row, 128-group) = amax / 7,
-    int4 v = clamp(rint(w / s), -8, 7) stored as nibble v + 8 (low nibble = even k). Returns the TILED copy."""
-    N, K = w.shape
-    wf = w.float().view(N, K // group, group)
-    s = (wf.abs().amax(-1) / 7).clamp(min=1e-8).half()
-    v = torch.clamp(torch.round(wf / s.float()[..., None]), -8, 7).to(torch.int32).view(N, K) + 8
-    packed = (v[:, 0::2] | (v[:, 1::2] << 4)).to(torch.uint8).contiguous()
-    return _C.w4_repack(0, packed, s.contiguous(), N, K)
 
 
 def _bf(shape, g, dev, std=0.02, mean=0.0):
@@ -92,37 +89,81 @@ def rope_table(cfg: Qwen35Config, cap: int, dev):
     return torch.stack([torch.stack([c, -s], -1), torch.stack([s, c], -1)], -2).float().to(dev).contiguous()
 
 
+def verify_tree(widths):
+    """The verify tree of a draft: chain node k (k = 0 .. len(widths) - 1) has widths[k] children, the first one
+    continuing the chain, the others leaves (the shape qwen35's tree_spec builds; (2, 2, 2, 1) is the reference
+    test's tree4s1m8). Rows are numbered depth-first, first child first (tests/test_mtp_accept.py:15-35 _tree).
+    Returns rows, parents, children [8][8] (-1 padded), depth, attention mask (mask[r] = mask[parent] | 1 << r),
+    and the GDN verify program (chain nodes commit, leaves follow their parent)."""
+    spec = []
+    for w in reversed(widths):
+        spec = [spec] + [[] for _ in range(w - 1)]
+    parents, depth = [], []
+
+    def add(node, p):
+        r = len(parents)
+        parents.append(p)
+        depth.append(0 if p < 0 else depth[p] + 1)
+        for child in node:
+            add(child, r)
+    add(spec, -1)
+    rows = len(parents)
+    if rows > 8:
+        raise ValueError(f"tree of {rows} rows: at most 8 verify rows")
+    children = [[-1] * 8 for _ in range(8)]
+    for r in range(1, rows):
+        ch = children[parents[r]]
+        ch[ch.index(-1)] = r
+    mask = []
+    for r in range(rows):
+        mask.append((mask[parents[r]] if parents[r] >= 0 else 0) | (1 << r))
+    # the GDN program: walk the chain, each chain node committing and followed by its leaves
+    program, node = [], 0
+    while True:
+        program.append(node | 32)
+        kids = [c for c in children[node] if c >= 0]
+        program.extend(kids[1:])
+        if not kids:
+            break
+        node = kids[0]
+    return {"rows": rows, "parents": parents + [-1] * (8 - rows), "children": children, "depth": depth,
+            "mask": mask, "program": program + [-1] * (8 - len(program)), "chain": len(widths)}
+
+
 class Qwen35W4A8:
     """Weights and decode state of one stream on one device."""
 
     def __init__(self, cfg: Qwen35Config, device, prompt_len: int, gen_tokens: int = 512, seed: int = 0x5EED + 4,
-                 fused: bool = False, prefetch: int = 0, draft_gemv: bool = True):
+                 fused: bool = False, prefetch: int = 0, draft_gemv: bool = True, keep_sources: bool = False):
         self.cfg, self.dev = cfg, torch.device(device)
         c, dev = cfg, self.dev
         g = torch.Generator(device=dev).manual_seed(seed)
+        # keep_sources: the checkpoint-layout W4 weights too (w4_src[(layer, name)] = (packed, scales)), for checks
+        # against the CPU oracle; trace: a callable(name, layer, tensors) the layer code reports to (None: off)
+        self.w4_src = {} if keep_sources else None
+        self.trace = None
         H, I, hd = c.hidden, c.inter, c.head_dim
         self.cap = ((prompt_len + gen_tokens + 64) + 63) // 64 * 64
         self.embed = _bf((c.vocab, H), g, dev)
-        self.lm_head = _bf((c.vocab, H), g, dev)
-        # the drafts' lm_head: a W4A8 GPTQ copy of the bf16 one (4x fewer bytes per draft). Only drafts use it;
-        # the verify's bf16 lm_head decides every output token (the reference drafts with an INT8 ConvRot copy,
-        # comfy_mono_decode_xpu/draft_lmhead.py).
-        self.lm_head_w4 = quantize_gptq(self.lm_head)
+        self.lm_head = _bf((c.vocab, H), g, dev)  # shared by the verify and the drafts (configs[4]: bf16)
         self.final_norm = _bf((H,), g, dev, 0.02, 1.0)
         self.layers = []
         Ck = 2 * c.gdn_k_heads * c.gdn_dim + c.gdn_v_heads * c.gdn_dim
         for i in range(c.layers):
+            kp = self.w4_src
             L = {"ln1": _bf((H,), g, dev, 0.02, 1.0), "ln2": _bf((H,), g, dev, 0.02, 1.0),
-                 "gate": _w4(I, H, g, dev), "up": _w4(I, H, g, dev), "down": _w4(H, I, g, dev)}
+                 "gate": _w4(I, H, g, dev, kp, (i, "gate")), "up": _w4(I, H, g, dev, kp, (i, "up")),
+                 "down": _w4(H, I, g, dev, kp, (i, "down"))}
             if c.is_attn(i):
-                L.update(q=_w4(2 * c.heads * hd, H, g, dev), k=_w4(c.kv_heads * hd, H, g, dev),
-                         v=_w4(c.kv_heads * hd, H, g, dev), o=_w4(H, c.heads * hd, g, dev),
+                L.update(q=_w4(2 * c.heads * hd, H, g, dev, kp, (i, "q")), k=_w4(c.kv_heads * hd, H, g, dev, kp, (i, "k")),
+                         v=_w4(c.kv_heads * hd, H, g, dev, kp, (i, "v")), o=_w4(H, c.heads * hd, g, dev, kp, (i, "o")),
                          q_norm=_bf((hd,), g, dev, 0.3, 1.0), k_norm=_bf((hd,), g, dev, 0.3, 1.0),
                          kc=torch.randn(1, c.kv_heads, self.cap, hd, device=dev, generator=g).to(torch.bfloat16),
                          vc=torch.randn(1, c.kv_heads, self.cap, hd, device=dev, generator=g).to(torch.bfloat16))
             else:
                 HV = c.gdn_v_heads
-                L.update(qkv=_w4(Ck, H, g, dev), z=_w4(HV * c.gdn_dim, H, g, dev), out=_w4(H, HV * c.gdn_dim, g, dev),
+                L.update(qkv=_w4(Ck, H, g, dev, kp, (i, "qkv")), z=_w4(HV * c.gdn_dim, H, g, dev, kp, (i, "z")),
+                         out=_w4(H, HV * c.gdn_dim, g, dev, kp, (i, "out")),
                          wab=_bf((2 * HV, H), g, dev), conv_w=_bf((Ck, 4), g, dev, 0.5),
                          conv_state=_bf((Ck, 3), g, dev, 1.0), dt_bias=torch.zeros(HV, device=dev),
                          g_decay=-torch.ones(HV, device=dev), gnorm=_bf((c.gdn_dim,), g, dev, 0.1, 1.0),
@@ -148,14 +189,13 @@ class Qwen35W4A8:
         self.next_tok = torch.randint(0, c.vocab, (1, 1), device=dev, generator=g)
         self.hidden = _bf((1, 1, H), g, dev, 1.0)
         self.parity = 0
-        R = c.depth + 1
-        ch = torch.full((8, 8), -1, dtype=torch.int32)
-        for r in range(R - 1):
-            ch[r, 0] = r + 1
-        self.children = ch.reshape(-1).to(dev)
-        self.mask = torch.tensor([(1 << (r + 1)) - 1 for r in range(R)], dtype=torch.int32, device=dev)
-        self.tree_pos = torch.arange(R, dtype=torch.int64, device=dev)
-        self.tree_ctl = torch.zeros(16, dtype=torch.int32, device=dev)
+        tree = verify_tree(c.tree)
+        R = tree["rows"]
+        self.tree = tree
+        self.children = torch.tensor(tree["children"], dtype=torch.int32).reshape(-1).to(dev)
+        self.mask = torch.tensor(tree["mask"], dtype=torch.int32, device=dev)
+        self.tree_pos = torch.tensor(tree["depth"], dtype=torch.int64, device=dev)
+        self.tree_ctl = torch.tensor(tree["parents"] + tree["program"], dtype=torch.int32, device=dev)
         self.result = torch.zeros(32, dtype=torch.int64, device=dev)
         self.apos = torch.empty(8, dtype=torch.int64, device=dev)
         self.aseq = torch.empty(1, dtype=torch.int32, device=dev)
@@ -165,14 +205,19 @@ class Qwen35W4A8:
         self.mfreq = torch.empty(1, self.cfg.rotary_dim // 2, 2, 2, device=dev)
         self.kv_ptrs = torch.tensor([t.data_ptr() for L in self.layers if "kc" in L for t in (L["kc"], L["vc"])],
                                     dtype=torch.int64, device=dev)
-        self.drafts = torch.zeros(R, dtype=torch.int64, device=dev)
+        self.drafts = torch.zeros(R, dtype=torch.int64, device=dev)  # the verify tokens of the tree's rows
+        self.toks = torch.zeros(1, R, dtype=torch.int64, device=dev)
         self.no_mask = torch.empty(0, dtype=torch.int32, device=dev)
         self.total = torch.zeros(1, dtype=torch.int64, device=dev)  # tokens committed, summed on the device
         self.fused, self.prefetch, self.draft_gemv = fused, prefetch, draft_gemv
         self.programs = self._build_programs() if fused else None
 
+    def _t(self, name, layer, **tensors):
+        if self.trace is not None:
+            self.trace(name, layer, {k: v.clone() for k, v in tensors.items()})
+
     # ---- layers ------------------------------------------------------------------------------------------
-    def _attention(self, L, x, freqs):
+    def _attention(self, L, x, freqs, i=-1):
         c = self.cfg
         M = x.shape[0]
         hd = c.head_dim
@@ -187,9 +232,12 @@ class Qwen35W4A8:
         y = _C.attn_dpas(q, L["kc"], L["vc"], self.aseq, k, v.transpose(1, 2), self.mask[:M])
         x1 = _C.rowlin_gptq(y[0], _C.ROWLIN_GATE, [(L["o"], c.hidden)], gate=pre[:, hd:nq], gate_head_stride=2 * hd,
                             lut=self.sig_lut, residual=x)
-        return _C.mlp_gptq(x1, L["ln2"], c.eps, L["gate"], L["up"], L["down"], silu_lut=self.silu_lut, I=c.inter)
+        out = _C.mlp_gptq(x1, L["ln2"], c.eps, L["gate"], L["up"], L["down"], silu_lut=self.silu_lut, I=c.inter)
+        self._t("attn", i, x=x, pre=pre, q=q, k=k, kc=L["kc"], vc=L["vc"], y=y, x1=x1, out=out, freqs=freqs,
+                apos=self.apos, aseq=self.aseq)
+        return out
 
-    def _gdn(self, L, x):
+    def _gdn(self, L, x, i=-1):
         c = self.cfg
         M = x.shape[0]
         HV, D = c.gdn_v_heads, c.gdn_dim
@@ -203,7 +251,10 @@ class Qwen35W4A8:
                                     L["dt_bias"], L["g_decay"],
                                     L["state"], L["gnorm"], c.eps, D ** -0.5, c.gdn_k_heads, self.ctl, prev, save)
         x1 = _C.rowlin_gptq(core, _C.ROWLIN_QUANT, [(L["out"], c.hidden)], residual=x)
-        return _C.mlp_gptq(x1, L["ln2"], c.eps, L["gate"], L["up"], L["down"], silu_lut=self.silu_lut, I=c.inter)
+        out = _C.mlp_gptq(x1, L["ln2"], c.eps, L["gate"], L["up"], L["down"], silu_lut=self.silu_lut, I=c.inter)
+        self._t("gdn", i, x=x, pre=pre, xn=xn, ab=ab, core=core, x1=x1, out=out, state=L["state"],
+                conv_state=L["conv_state"])
+        return out
 
     # ---- layer programs: the verify body as 9 persistent launches (one per run of layers between two attention
     # cores), separated by the attention kernels ----------------------------------------------------------------
@@ -212,7 +263,7 @@ class Qwen35W4A8:
         programs, program j running [post of attention layer 4j - 1 (j > 0)], the GDN layers, [pre of the next
         attention layer]. All activations live in fixed scratch buffers."""
         c, dev = self.cfg, self.dev
-        R, H, I, hd = c.depth + 1, c.hidden, c.inter, c.head_dim
+        R, H, I, hd = self.tree["rows"], c.hidden, c.inter, c.head_dim
         HV, D, hk = c.gdn_v_heads, c.gdn_dim, c.gdn_k_heads
         Ck, Z = 2 * hk * D + HV * D, HV * D
         nq, nkv = 2 * c.heads * hd, c.kv_heads * hd
@@ -287,7 +338,7 @@ class Qwen35W4A8:
         return B["X"]
 
     def verify(self, tokens):
-        """The D + 1 chain rows through the body; returns (greedy tokens [1, R], final hidden rows [R, H])."""
+        """The tree's rows through the body; returns (greedy tokens [1, R], final hidden rows [R, H])."""
         c = self.cfg
         R = tokens.numel()
         _C.mtp_prep_verify(self.st, self.apos, self.aseq, self.vpos, self.tree_pos, self.ctl, self.tree_ctl,
@@ -298,23 +349,27 @@ class Qwen35W4A8:
         else:
             x = self.embed[tokens.view(-1)]
             for i, L in enumerate(self.layers):
-                x = self._attention(L, x, freqs) if c.is_attn(i) else self._gdn(L, x)
-        logits = F.linear(_C.rmsnorm_add(x, self.final_norm, c.eps), self.lm_head)
-        _, toks = _C.fast_topk(logits, 1, True)
-        return toks.view(1, R), x
+                x = self._attention(L, x, freqs, i) if c.is_attn(i) else self._gdn(L, x, i)
+        # final norm, then the bf16 lm_head with the greedy argmax fused (no logits written)
+        xf = _C.rmsnorm_add(x, self.final_norm, c.eps)
+        _C.lmhead_pick(xf, self.lm_head, k=0, argmax_out=self.toks.view(-1))
+        self._t("verify", -1, tokens=tokens, x=x, xf=xf, toks=self.toks)
+        return self.toks, x
 
     def _linear(self, x, w):
         """A draft projection x [1, K] @ w [N, K]^T (the reference's F.linear, draft_head.py:198-210): this build's
         GEMV, or torch's cuBLAS linear when the model was built with draft_gemv=False."""
         return _C.gemv_bf16(x, w) if self.draft_gemv else F.linear(x, w)
 
-    def draft_token(self, token, hidden, k):
-        """One MTP draft: (token [1, 1], hidden [1, 1, H]) -> (draft token [1, 1], MTP hidden [1, 1, H])."""
+    def draft_token(self, hidden, k):
+        """Draft k: the MTP head on chain node k's verify token (self.drafts[k]) and the previous hidden row [1, 1, H];
+        its lm_head pick writes node k's children's verify tokens (argmax to the first child, the second best to the
+        second). Returns the MTP hidden row [1, 1, H] for the next draft."""
         c, m = self.cfg, self.mtp
         hd, H = c.head_dim, c.hidden
         _C.mtp_prep_draft(self.st, k, self.rope.view(1, 1, self.cap, -1, 2, 2), self.mfreq.view(1, 1, 1, -1, 2, 2),
                           self.mpos, self.mseq)
-        e = self.embed[token.view(-1)]
+        e = self.embed[self.drafts[k:k + 1]]
         cat = torch.empty(1, 2 * H, dtype=torch.bfloat16, device=self.dev)
         _C.rmsnorm_add(e, m["enorm"], c.eps, out=cat[:, :H])
         _C.rmsnorm_add(hidden.view(1, -1), m["hnorm"], c.eps, out=cat[:, H:])
@@ -332,21 +387,25 @@ class Qwen35W4A8:
         gu = self._linear(xn, m["gate_up"])
         h = _C.lut_mul(gu[:, c.inter:], gu[:, :c.inter], self.silu_lut)
         xf, x = _C.rmsnorm_add(x, m["norm"], c.eps, add=self._linear(h, m["down"]))
-        logits = _C.w4a8_gptq_linear_bf16(xf, self.lm_head_w4, None, tiled=True, N=c.vocab)
-        _, t = _C.fast_topk(logits, 1, True)
-        return t.view(1, 1), x.view(1, 1, -1)
+        _C.lmhead_pick(xf, self.lm_head, k=c.tree[k], children=self.children[8 * k:8 * k + 8], dst=self.drafts)
+        self._t("draft", k, xf=xf, drafts=self.drafts)
+        return x.view(1, 1, -1)
 
-    def step(self):
-        """One decode step, queued on the current stream: draft chain, verify, accept. Returns the device result
-        row of mono_mtp_accept ([n, commit[8], ...])."""
+    def step(self, steer=None):
+        """One decode step, queued on the current stream: the draft tree, the verify, the accept. Returns the device
+        result row of mono_mtp_accept ([n, commit[8], row, on_chain, ...]). steer (tests): a callable given the
+        verify tokens [1, R] (device) before the accept, which may change them to force an accepted path."""
         c = self.cfg
-        tok, h = self.next_tok.view(1, 1), self.hidden
-        self.drafts[0:1] = tok.view(-1)
-        for j in range(1, c.depth + 1):
-            tok, h = self.draft_token(tok, h, j - 1)
-            self.drafts[j:j + 1] = tok.view(-1)
+        self.drafts[0:1] = self.next_tok.view(-1)
+        h = self.hidden
+        for k in range(c.depth):
+            h = self.draft_token(h, k)
         toks, x = self.verify(self.drafts)
-        _C.mtp_accept(self.st, toks, self.drafts.view(1, -1), None, self.children, c.depth + 1, c.depth, x,
+        if steer is not None:
+            steer(toks)
+        self._t("accept_in", -1, toks=toks, drafts=self.drafts, st=self.st, ctl=self.ctl,
+                kv=torch.stack([t for L in self.layers if "kc" in L for t in (L["kc"], L["vc"])]))
+        _C.mtp_accept(self.st, toks, self.drafts.view(1, -1), None, self.children, self.tree["rows"], c.depth, x,
                       self.next_tok, self.hidden, self.ctl, self.kv_ptrs, c.kv_heads, self.cap, c.head_dim,
                       self.result)
         self.total += self.result[0]
@@ -354,7 +413,7 @@ class Qwen35W4A8:
         return self.result
 
     def own_launches_per_step(self) -> int:
-        """This build's kernel launches per step (the rest are cuBLAS GEMMs and a few torch gathers / copies)."""
+        """This build's kernel launches per step (the rest are a few torch gathers / copies)."""
         c = self.cfg
         n_attn = sum(1 for i in range(c.layers) if c.is_attn(i))
         n_gdn = c.layers - n_attn
@@ -362,9 +421,9 @@ class Qwen35W4A8:
             body = (n_attn + 1) + n_attn * 3
         else:  # rowlin x2 + MLP; GDN a|b + conv + delta; rope + attention x2
             body = c.layers * 3 + n_gdn * 3 + n_attn * 3
-        # prep, norms, rope, attention, lut x2, norm-adds, lm_head, argmax (+ fc, qkv, o, gate | up, down)
-        draft = c.depth * (1 + 3 + 1 + 2 + 2 + 2 + 1 + 2 + (5 if self.draft_gemv else 0))
-        return body + draft + 1 + 2 + 1 + 1                   # prep_verify, final norm + argmax, accept, verify norm
+        # per draft: prep, 2 norms, rope, attention x2, 2 luts, 3 norm(-add)s, lm_head pick (+ 5 projections)
+        draft = c.depth * (1 + 2 + 1 + 2 + 2 + 3 + 1 + (5 if self.draft_gemv else 0))
+        return body + draft + 1 + 1 + 1 + 1  # prep_verify, final norm, lm_head pick, accept
 
     def step_bytes(self) -> int:
         """Algorithmic HBM bytes of one step: every weight byte read (W4 body once for the verify rows, the
@@ -377,7 +436,6 @@ class Qwen35W4A8:
                     if k in L)
         state = sum(L["state"].numel() * 4 * 2 for L in self.layers if "state" in L)
         lm = self.lm_head.numel() * 2
-        lm4 = self.lm_head_w4.numel()
         mtp = sum(t.numel() * t.element_size() for k, t in self.mtp.items() if k not in ("kc", "vc"))
         kv = int(self.st[0].item()) * c.kv_heads * c.head_dim * 2 * 2 * sum(1 for L in self.layers if "kc" in L)
-        return body + small + state + lm + lm4 * c.depth + mtp * c.depth + kv
+        return body + small + state + lm * (1 + c.depth) + mtp * c.depth + kv

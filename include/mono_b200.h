@@ -304,6 +304,23 @@ MONO_API int mono_mtp_accept(int64_t* st, const int64_t* toks, const int64_t* dr
 MONO_API int mono_gemv_bf16(const void* x, int64_t x_stride, const void* w, int64_t M, int64_t N, int64_t K, void* out,
                             int64_t out_stride, mono_stream_t stream);
 
+/* bf16 lm_head with the pick fused: the verify's greedy logits + argmax (the reference's verify_logits then
+ * lg.argmax, comfy_mono_decode_xpu/mtp_loop.py:325-327) and the draft pick (csrc/draft_lmhead.sycl:87-292: the
+ * draft token, the top-n row and the children's verify tokens in one launch). For M <= 8 rows of x [M][x_stride]
+ * against w [V][K]: logits = bf16(sum_k x[m][k] * w[n][k]) in a pinned order (lane l of 32 accumulates the 8-element
+ * pieces l, l + 32, ... with fmaf in element order, then the xor butterfly 16, 8, 4, 2, 1), then per row
+ *   argmax[m]   the argmax by the rank (float order, NaN largest, -0 == +0, smallest index on ties)
+ *   topk[m][j]  j < k <= 8, descending by the top-k rank (the reference's fast_topk tie order)
+ *   logits      (optional, NULL: not written) bf16 [M][V]
+ * and, with children (device int32, up to 8 slots of dst, -1 ends) and dst (device int64), M == 1: dst[children[0]]
+ * = argmax, dst[children[j]] = topk[j] for 1 <= j < k (the draft token and its siblings' tokens). K % 256 == 0;
+ * workspace: mono_lmhead_workspace() bytes, zero-filled before first use (the kernel leaves it reusable); one call
+ * at a time per workspace. */
+MONO_API size_t mono_lmhead_workspace(void);
+MONO_API int mono_lmhead_pick(const void* x, int64_t x_stride, const void* w, int64_t M, int64_t V, int64_t K, int64_t k,
+                              void* logits, int64_t* argmax, int64_t* topk, const int32_t* children, int64_t* dst,
+                              void* workspace, size_t workspace_bytes, mono_stream_t stream);
+
 /* Exact top-k of a few long rows, k <= 64 (the reference's topk_rows, csrc/topk_rows.sycl:2-17: the verify
  * sampling's torch.topk(logits.float(), k)): per row the k largest by the radix key of the fp32 value (sign-flipped
  * bits: -0 below +0; rows holding NaN are not torch's order), sorted descending, ties in the torch-XPU gather

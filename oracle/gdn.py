@@ -105,3 +105,115 @@ def ab_projection(x_bits, w_bits):
         Q.append(acc[:, :, 0])
     out = (((Q[0] + Q[1]).astype(np.float32) + Q[2]).astype(np.float32) + Q[3]).astype(np.float32)
     return f32_to_bf16_bits(out)
+
+
+def gdn_step_tree(qkv, z, a, b, conv_w, conv_state, dt_bias, g_decay, state, gnorm_w, gnorm_eps, qscale, HK,
+                  parents, prog, replay=None):
+    """The deferred (replay + tree verify) form of the step (csrc/mono_gdn.sycl:38-40 ctl, :313-375 conv,
+    :398-571 entries), in fp64 with the reference's bf16 roundings:
+      replay   `replay` = (qkv, a, b) of the previous step's accepted rows, in path order: they run the committing
+               chain (gdn_step) from (conv_state, state); the resulting conv state and recurrent state persist
+      conv     verify row t reads its own input, then its ancestors' (parents[t], parents[parents[t]], ..., -1
+               ends), then the committed history (the conv state after the replay), newest first
+      delta    the program entries in order: entry p = slot | 32 * commit; the running state starts from the
+               persisted one; a committing entry advances it, a non-committing one computes its row from
+               temporaries (S * decay, then the rank-one update) and leaves it; the list ends at the first entry
+               whose slot is negative or >= M
+      output   core of the rows the program names; other rows have raw = 0
+    Returns (core [M, HV 128], conv_state' [C, 3] bf16 bits, state' [HV, 128, 128] fp64): the persisted states."""
+    M, C = np.asarray(qkv).shape
+    HV = np.asarray(a).shape[1]
+    KD = HK * DH
+    if replay is not None and len(replay[0]):
+        rq, ra, rb = replay
+        rz = np.zeros((len(rq), HV * DH), dtype=np.uint16)
+        _, hist_bits, S0 = gdn_step(rq, rz, ra, rb, conv_w, conv_state, dt_bias, g_decay, state, gnorm_w, gnorm_eps,
+                                    qscale, HK)
+    else:
+        hist_bits, S0 = np.asarray(conv_state), state.astype(np.float64)
+    x = bf16_bits_to_f32(qkv).astype(np.float64)
+    w = bf16_bits_to_f32(conv_w).astype(np.float64)
+    hist = bf16_bits_to_f32(hist_bits).astype(np.float64)  # [C, 3], oldest first
+    conv = np.zeros((M, C))
+    for t in range(M):
+        taps, anc, miss = [x[t]], t, 0
+        for d in range(1, 4):
+            anc = parents[anc] if anc >= 0 else -1
+            if anc is not None and 0 <= anc < t:
+                taps.append(x[anc])
+            else:
+                anc = -1
+                miss += 1
+                taps.append(hist[:, 3 - miss])
+        s = np.zeros(C)
+        for d in range(4):  # newest first, weight w[3 - d]
+            s = s + taps[d] * w[:, 3 - d]
+        y = _bf(s)
+        conv[t] = _bf(y / (1.0 + np.exp(-y)))
+    av = _bf(bf16_bits_to_f32(a).astype(np.float64)) + dt_bias.astype(np.float64)[None, :]
+    sp = np.where(av > 20.0, av, np.log1p(np.exp(np.minimum(av, 20.0))))
+    decay = np.exp(g_decay.astype(np.float64)[None, :] * sp)
+    beta = _bf(1.0 / (1.0 + np.exp(-bf16_bits_to_f32(b).astype(np.float64))))
+    q = conv[:, :KD].reshape(M, HK, DH)
+    k = conv[:, KD:2 * KD].reshape(M, HK, DH)
+    v = conv[:, 2 * KD:].reshape(M, HV, DH)
+    qi = 1.0 / np.maximum(np.sqrt((q * q).sum(-1)), 1e-12)
+    ki = 1.0 / np.maximum(np.sqrt((k * k).sum(-1)), 1e-12)
+    qn = (q * qscale) * qi[..., None]
+    kn = k * ki[..., None]
+    S = S0.copy()
+    raw = np.zeros((M, HV, DH))
+    for p in prog:
+        if p < 0 or (p & 15) >= M:
+            break
+        t, commit = p & 15, bool(p & 32)
+        for h in range(HV):
+            kh = h // (HV // HK)
+            St = S[h] * decay[t, h]
+            mem = St.T @ kn[t, kh]
+            delta = (v[t, h] - mem) * beta[t, h]
+            St = St + np.outer(kn[t, kh], delta)
+            raw[t, h] = St.T @ qn[t, kh]
+            if commit:
+                S[h] = St
+    rawb = _bf(raw)
+    gw = bf16_bits_to_f32(gnorm_w).astype(np.float64)
+    rs = 1.0 / np.sqrt((rawb * rawb).mean(-1, keepdims=True) + gnorm_eps)
+    normed = _bf(rawb * gw * rs)
+    zf = bf16_bits_to_f32(z).astype(np.float64).reshape(M, HV, DH)
+    gz = _bf(zf / (1.0 + np.exp(-zf)))
+    core = (normed * gz).reshape(M, HV * DH)
+    return core, np.asarray(hist_bits), S0
+
+
+def chain_program(rows):
+    """parents / program of a chain of `rows` verify rows (every entry commits), padded to 8 with -1."""
+    parents = [r - 1 for r in range(rows)] + [-1] * (8 - rows)
+    prog = [r | 32 for r in range(rows)] + [-1] * (8 - rows)
+    return parents, prog
+
+
+def tree_program(parents, rows):
+    """The verify program of a tree whose branches off the first-child chain are leaves (the shape qwen35's
+    tree_spec builds): walk the chain from the root; each chain node commits and is followed by its other
+    children (leaves, not committed). Returns prog padded to 8 with -1. Raises ValueError for other shapes."""
+    children = [[] for _ in range(rows)]
+    for r in range(1, rows):
+        p = parents[r]
+        if not 0 <= p < r:
+            raise ValueError(f"row {r}: parent {p} must precede it")
+        children[p].append(r)
+    prog, node = [], 0
+    while True:
+        prog.append(node | 32)
+        kids = children[node]
+        for leaf in kids[1:]:
+            if children[leaf]:
+                raise ValueError(f"row {leaf}: an off-chain node with children")
+            prog.append(leaf)
+        if not kids:
+            break
+        node = kids[0]
+    if sorted(p & 15 for p in prog) != list(range(rows)):
+        raise ValueError("the program does not cover every row")
+    return prog + [-1] * (8 - len(prog))

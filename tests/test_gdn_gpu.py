@@ -69,6 +69,8 @@ def test_gdn_deferred_replay_then_verify(cuda):
     bufs = [(torch.zeros(8, C, dtype=torch.bfloat16, device=cuda), torch.zeros(8, HV, dtype=torch.bfloat16, device=cuda),
              torch.zeros(8, HV, dtype=torch.bfloat16, device=cuda)) for _ in range(2)]
     ctl = torch.zeros(26, dtype=torch.int32, device=cuda)
+    par, prog = og.chain_program(5)
+    ctl[10:26] = torch.tensor(par + prog, dtype=torch.int32)
     cs, st = conv_state.to(cuda), state.to(cuda)
     args = (conv_w.to(cuda), cs, dt_bias.to(cuda), g_decay.to(cuda), st, gw.to(cuda), 1e-6, qs, HK)
     core1 = _C.gdn_step_deferred(*[t.to(cuda) for t in rows1], *args, ctl, bufs[1], bufs[0])
@@ -79,6 +81,8 @@ def test_gdn_deferred_replay_then_verify(cuda):
     assert (np.abs(o1 - ref1) <= 2 ** -6 * np.abs(ref1) + 2e-3).all()
     ctl[0] = 3
     ctl[2:10] = torch.arange(8, dtype=torch.int32)
+    par, prog = og.chain_program(4)
+    ctl[10:26] = torch.tensor(par + prog, dtype=torch.int32)
     core2 = _C.gdn_step_deferred(*[t.to(cuda) for t in rows2], *args, ctl, bufs[0], bufs[1])
     rep = tuple(t[:3] for t in rows1)
     _, hist_r, state_r = og.gdn_step(*[bf16_bits(t) for t in rep], bf16_bits(conv_w), bf16_bits(conv_state),
@@ -89,3 +93,53 @@ def test_gdn_deferred_replay_then_verify(cuda):
     assert (np.abs(o2 - ref2) <= 2 ** -6 * np.abs(ref2) + 2e-3).all(), np.abs(o2 - ref2).max()
     assert np.array_equal(bf16_bits(cs), hist_r)
     assert (np.abs(st.cpu().numpy() - state_r) <= 1e-4 * (1 + np.abs(state_r))).all()
+
+
+# tree4s1m8 (the reference test's spec, tests/test_mtp_accept.py:46-47): the chain 0-1-2-3-4 with one leaf beside
+# each of rows 1, 2, 3 (rows 7, 6, 5, whose parents are 0, 1, 2)
+TREE8_PARENTS = [-1, 0, 1, 2, 3, 2, 1, 0]
+
+
+@pytest.mark.parametrize("path", [[0, 1, 6], [0, 7], [0, 1, 2, 3, 4], [0]])
+def test_gdn_deferred_tree_verify_then_replay_off_chain(cuda, path):
+    """Step 1 verifies the 8-node tree (each row's conv over its ancestors, leaves from temporaries); step 2 replays
+    an accepted path of step 1 (possibly ending on a leaf) and verifies the tree again. Reference: oracle
+    gdn_step_tree (fp64), same tolerances as above; the conv state is bit-exact."""
+    from mono_b200 import _C
+    HK, HV, D = 16, 32, 128
+    C = (2 * HK + HV) * D
+    g = torch.Generator().manual_seed(1000 + len(path) + path[-1])
+    rnd = lambda *s: torch.randn(*s, generator=g).bfloat16()
+    conv_w = (torch.randn(C, 4, generator=g) * 0.5).bfloat16()
+    conv_state = rnd(C, 3)
+    dt_bias, g_decay = torch.randn(HV, generator=g) * 0.1, -torch.exp(torch.randn(HV, generator=g) * 0.5)
+    state = torch.randn(HV, D, D, generator=g) * 0.1
+    gw = (1 + torch.randn(D, generator=g) * 0.1).bfloat16()
+    qs = D ** -0.5
+    prog = og.tree_program(TREE8_PARENTS, 8)
+    rows1 = (rnd(8, C), rnd(8, HV * D), rnd(8, HV), rnd(8, HV))
+    rows2 = (rnd(8, C), rnd(8, HV * D), rnd(8, HV), rnd(8, HV))
+    bufs = [(torch.zeros(8, C, dtype=torch.bfloat16, device=cuda), torch.zeros(8, HV, dtype=torch.bfloat16, device=cuda),
+             torch.zeros(8, HV, dtype=torch.bfloat16, device=cuda)) for _ in range(2)]
+    ctl = torch.zeros(26, dtype=torch.int32, device=cuda)
+    ctl[10:26] = torch.tensor(TREE8_PARENTS + prog, dtype=torch.int32)
+    cs, st = conv_state.to(cuda), state.to(cuda)
+    args = (conv_w.to(cuda), cs, dt_bias.to(cuda), g_decay.to(cuda), st, gw.to(cuda), 1e-6, qs, HK)
+    common = (bf16_bits(conv_w), bf16_bits(conv_state), dt_bias.numpy(), g_decay.numpy(), state.numpy(), bf16_bits(gw),
+              1e-6, qs, HK)
+    core1 = _C.gdn_step_deferred(*[t.to(cuda) for t in rows1], *args, ctl, bufs[1], bufs[0])
+    ref1, _, _ = og.gdn_step_tree(*[bf16_bits(t) for t in rows1], *common, TREE8_PARENTS, prog)
+    o1 = bf16_bits_to_f32(bf16_bits(core1)).astype(np.float64)
+    assert (np.abs(o1 - ref1) <= 2 ** -6 * np.abs(ref1) + 2e-3).all(), np.abs(o1 - ref1).max()
+    assert torch.equal(cs.cpu(), conv_state) and torch.equal(st.cpu(), state)  # nothing persisted
+    # step 2: replay the accepted path (slots of step 1), verify the tree again
+    ctl[0] = len(path)
+    ctl[2:10] = torch.tensor(path + list(range(len(path), 8)), dtype=torch.int32)
+    core2 = _C.gdn_step_deferred(*[t.to(cuda) for t in rows2], *args, ctl, bufs[0], bufs[1])
+    rep = tuple(bf16_bits(t)[path] for t in (rows1[0], rows1[2], rows1[3]))
+    ref2, hist2, state2 = og.gdn_step_tree(*[bf16_bits(t) for t in rows2], *common, TREE8_PARENTS, prog, replay=rep)
+    o2 = bf16_bits_to_f32(bf16_bits(core2)).astype(np.float64)
+    assert (np.abs(o2 - ref2) <= 2 ** -6 * np.abs(ref2) + 2e-3).all(), np.abs(o2 - ref2).max()
+    assert np.abs(o2 - ref2).mean() <= 2e-3 * np.abs(ref2).mean()
+    assert np.array_equal(bf16_bits(cs), hist2)
+    assert (np.abs(st.cpu().numpy() - state2) <= 1e-4 * (1 + np.abs(state2))).all()

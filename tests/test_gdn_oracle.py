@@ -58,3 +58,27 @@ def test_ab_projection_follows_its_pinned_order():
             assert got[m, n] == f32_to_bf16_bits(np.array([ref], dtype=np.float32))[0]
     exact = xf.astype(np.float64) @ wf.astype(np.float64).T
     assert np.allclose(bf16_bits_to_f32(got), exact, rtol=2 ** -7, atol=1e-4)
+
+
+def test_gdn_tree_oracle_reduces_to_the_chain():
+    """The tree oracle on a chain program equals the committing oracle (consistency of the restatement)."""
+    HK, HV, D = 2, 4, 128
+    C = (2 * HK + HV) * D
+    rng = np.random.default_rng(3)
+    from oracle.numerics import f64_to_bf16_bits
+    bits = lambda *s: f64_to_bf16_bits(rng.standard_normal(s))
+    qkv, z, a, b = bits(5, C), bits(5, HV * D), bits(5, HV), bits(5, HV)
+    conv_w, conv_state = f64_to_bf16_bits(rng.standard_normal((C, 4)) * 0.5), bits(C, 3)
+    dt, gd = np.zeros(HV, np.float32), -np.ones(HV, np.float32)
+    state = (rng.standard_normal((HV, D, D)) * 0.1).astype(np.float32)
+    gw = f64_to_bf16_bits(1 + rng.standard_normal(D) * 0.1)
+    ref, _, _ = og.gdn_step(qkv, z, a, b, conv_w, conv_state, dt, gd, state, gw, 1e-6, D ** -0.5, HK)
+    par, prog = og.chain_program(5)
+    got, _, _ = og.gdn_step_tree(qkv, z, a, b, conv_w, conv_state, dt, gd, state, gw, 1e-6, D ** -0.5, HK, par, prog)
+    assert np.allclose(got, ref, rtol=0, atol=0)
+
+
+def test_tree_program_of_tree4s1m8():
+    """tree4s1m8 (parents -1 0 1 2 3 2 1 0): each chain node commits and is followed by its leaf."""
+    assert og.tree_program([-1, 0, 1, 2, 3, 2, 1, 0], 8) == [32, 7, 33, 6, 34, 5, 35, 36]
+    assert og.chain_program(5) == ([-1, 0, 1, 2, 3, -1, -1, -1], [32, 33, 34, 35, 36, -1, -1, -1])

@@ -74,22 +74,3 @@ def test_rowlin_quant_residual_bit_exact(cuda):
     assert np.array_equal(bf16_bits(out), ref)
     out2 = _C.rowlin_gptq(x.to(cuda), _C.ROWLIN_QUANT, dev, residual=res.to(cuda))  # workspace reuse
     assert np.array_equal(bf16_bits(out2), ref)
-
-
-def test_quantize_gptq_roundtrip_matches_oracle_linear(cuda):
-    """The decoder's RTN GPTQ copy of a bf16 matrix, as a tiled weight, gives the oracle's linear of the same
-    packed / scales."""
-    from mono_b200 import _C
-    from mono_b200.decoder import quantize_gptq
-    g = torch.Generator().manual_seed(9)
-    w = (torch.randn(256, 2048, generator=g) * 0.02).bfloat16().to(cuda)
-    tiled = quantize_gptq(w)
-    wf = w.float().view(256, 16, 128)
-    s = (wf.abs().amax(-1) / 7).clamp(min=1e-8).half()
-    v = torch.clamp(torch.round(wf / s.float()[..., None]), -8, 7).to(torch.int32).view(256, 2048) + 8
-    packed = (v[:, 0::2] | (v[:, 1::2] << 4)).to(torch.uint8)
-    x = torch.randn(1, 2048, generator=g).bfloat16()
-    q, xs = ow.act_quant(bf16_bits(x))
-    ref = ow.gptq_linear(q, xs, packed.cpu().numpy(), s.cpu().numpy())
-    out = _C.w4a8_gptq_linear_bf16(x.to(cuda), tiled, None, tiled=True, N=256)
-    assert np.array_equal(bf16_bits(out), ref)
