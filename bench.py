@@ -4,7 +4,8 @@
 
 Workload `decode` (default; BASELINE.json configs[4], the headline "decode tok/s"): the synthetic
 Qwen3.5-9B-shaped W4A8 model (random-init weights, mono_b200.decoder) decoding with the device-side MTP loop
-(depth-4 chain draft, 5 verify rows, greedy accept), one stream per GPU; value = committed tokens / device
+(8-node tree4s1m8 draft tree of depth 4, bf16 MTP head and lm_head, 8 verify rows, greedy accept), one stream
+per GPU, prompt 1024 (a shorter second run at prompt 4096 goes into config); value = committed tokens / device
 time of K steps (two CUDA graphs replayed back to back, CUDA events, max over ranks); roofline of the step's
 dominant kernel (the fused MLP) timed alone; e2e reads every step's result row back to the host.
 
@@ -518,10 +519,44 @@ def reduce_time_and_count(ms, count, device, world):
     return float(t.item()), int(c.item())
 
 
+def _decode_measure(model, stream, steps, warmup, world, dev):
+    """Steps of the decode loop, captured in two CUDA graphs (the GDN replay buffers alternate) and replayed back to
+    back; returns (ms, committed tokens, graphs)."""
+    import torch
+    with torch.cuda.stream(stream):
+        for _ in range(2):  # eager warm-up: workspaces
+            model.step()
+    stream.synchronize()
+    graphs = []
+    for _ in range(2):
+        gph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gph, stream=stream):
+            model.step()
+        graphs.append(gph)
+    for i in range(max(warmup, 3)):
+        graphs[i % 2].replay()
+    torch.cuda.synchronize()
+    n0 = int(model.total.item())
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(steps):
+            graphs[i % 2].replay()
+        e1.record(stream)
+    stream.synchronize()
+    ms, toks = reduce_time_and_count(e0.elapsed_time(e1), int(model.total.item()) - n0, dev, world)
+    return ms, toks, graphs
+
+
 def run_decode(args):
-    """Config 4: the synthetic Qwen3.5-9B-shaped W4A8 decoder with the device MTP loop (depth-4 chain draft,
-    5 verify rows, greedy accept), one stream per GPU. Steps are captured in two CUDA graphs (the GDN replay
-    buffers alternate) and replayed back to back; the committed tokens are summed on the device."""
+    """Config 4: the synthetic Qwen3.5-9B-shaped W4A8 decoder with the device MTP loop (the 8-node tree4s1m8 draft
+    tree of depth 4 from the bf16 MTP head and bf16 lm_head, 8 verify rows, greedy accept), one stream per GPU.
+    Steps are captured in two CUDA graphs and replayed back to back; the committed tokens are summed on the device.
+    A second, shorter measurement at prompt 4096 goes into config (configs[4] names prompts 1024 and 4096)."""
     import datetime
 
     import torch
@@ -539,32 +574,8 @@ def run_decode(args):
     model = Qwen35W4A8(cfg, dev, prompt_len=prompt, gen_tokens=max(512, args.steps * 8 + 64), seed=0x5EED + 4 + rank,
                        fused=args.programs, prefetch=args.prefetch, draft_gemv=not args.cublas_draft)
     stream = torch.cuda.Stream(dev)
-    with torch.cuda.stream(stream):
-        for _ in range(2):  # eager warm-up: workspaces, cuBLAS handles
-            model.step()
-    stream.synchronize()
-    graphs = []
-    for _ in range(2):
-        gph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gph, stream=stream):
-            model.step()
-        graphs.append(gph)
-    for i in range(max(args.warmup, 3)):
-        graphs[i % 2].replay()
-    torch.cuda.synchronize()
-    n0 = int(model.total.item())
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
-        with torch.cuda.stream(stream):
-            e0.record(stream)
-            for i in range(args.steps):
-                graphs[i % 2].replay()
-            e1.record(stream)
-        stream.synchronize()
-    ms, toks = reduce_time_and_count(e0.elapsed_time(e1), int(model.total.item()) - n0, dev, world)
+        ms, toks, graphs = _decode_measure(model, stream, args.steps, args.warmup, world, dev)
     step_ms = ms / args.steps
     step_bytes = model.step_bytes()
     hbm, src = peaks()
@@ -582,10 +593,12 @@ def run_decode(args):
         f1.record(stream)
     stream.synchronize()
     e2e_ms, e2e_toks = reduce_time_and_count(f0.elapsed_time(f1), int(model.total.item()) - m0, dev, world)
-    # the dominant kernel alone (the fused MLP block, 19 % of the step): a graph of its launches over the layers'
-    # weights at the step's 5 verify rows, averaged per launch with CUDA events
+    del graphs
+    # the dominant kernel alone (the fused MLP block): a graph of its launches over the layers' weights at the
+    # step's 8 verify rows, averaged per launch with CUDA events
     import mono_b200._C as C_
-    xs = torch.randn(cfg.depth + 1, cfg.hidden, device=dev).to(torch.bfloat16)
+    R = model.tree["rows"]
+    xs = torch.randn(R, cfg.hidden, device=dev).to(torch.bfloat16)
     outs = torch.empty_like(xs)
     with torch.cuda.stream(stream):
         for L in model.layers[:4]:
@@ -606,33 +619,51 @@ def run_decode(args):
         k1.record(stream)
     stream.synchronize()
     mlp_us = k0.elapsed_time(k1) * 1e3 / (reps * cfg.layers)
-    mlp_b = mlp_bytes(cfg.depth + 1, cfg.hidden, cfg.inter)
+    mlp_b = mlp_bytes(R, cfg.hidden, cfg.inter)
     del gm
-    cpu = cpu_decode_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
-    del graphs
+    # prompt 4096: a second model, a shorter run
+    p4096 = None
+    if prompt != 4096 and not args.no_second_prompt:
+        del model
+        torch.cuda.empty_cache()
+        m2 = Qwen35W4A8(cfg, dev, prompt_len=4096, gen_tokens=max(512, args.steps * 8 + 64), seed=0x5EED + 4 + rank,
+                        fused=args.programs, prefetch=args.prefetch, draft_gemv=not args.cublas_draft)
+        steps2 = max(10, args.steps // 2)
+        ms2, toks2, g2 = _decode_measure(m2, stream, steps2, args.warmup, world, dev)
+        del g2
+        p4096 = {"tok_s": round(toks2 / (ms2 * 1e-3), 2), "ms_per_step": round(ms2 / steps2, 4), "steps": steps2,
+                 "algorithmic_bytes_per_step": m2.step_bytes()}
+        model = m2
+    cpu = cpu_decode_baseline(args) if (rank == 0 and world == 1 and not args.no_cpu) else None
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(toks / (ms * 1e-3), 2), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic (random-init Qwen3.5-9B-shaped W4A8 weights, random tokens, seeded)",
-            "config": {"workload": f"Qwen3.5-9B-shaped W4A8 MTP decode (configs[4]), prompt {prompt}, depth-4 chain "
-                                   "draft, 5 verify rows, greedy accept, 1 stream per GPU",
+            "config": {"workload": f"Qwen3.5-9B-shaped W4A8 MTP decode (configs[4]): 8-node tree4s1m8 draft tree of "
+                                   f"depth 4 (bf16 MTP head, bf16 lm_head), 8 verify rows, greedy accept, prompt {prompt}, "
+                                   "1 stream per GPU",
                        "layers": cfg.layers, "steps_per_s": round(args.steps / (ms * 1e-3), 2),
                        "tokens_per_step": round(toks / (args.steps * world), 3),
-                       "l2": "inputs larger than L2 (6.6 GB of weights read per step)",
+                       "tokens_per_step_note": "random-init weights: the drafts rarely match the verify (about one "
+                                               "token per step, as expected; not tuned away)",
+                       "l2": "inputs larger than L2 (11.9 GB of weights read per step)",
                        "body": (f"{len(model.programs[0])} layer programs per step (prefetch {args.prefetch})"
                                 if args.programs else "one launch per fused op (rowlin / a|b / GDN / MLP / attention)"),
                        "draft_projections": "cuBLAS (F.linear)" if args.cublas_draft else "mono_gemv_bf16",
+                       "lm_head": "mono_lmhead_pick (bf16 GEMV with the argmax / top-2 pick fused), verify and drafts",
+                       "prompt_4096": p4096,
                        "parallelism": f"independent streams x{world}"},
             "roofline": {"bound": "hbm", "achieved": round(mlp_b / (mlp_us * 1e-6) / 1e9, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(mlp_b / (mlp_us * 1e-6) / 1e9 / hbm, 4), "peak_source": src,
-                         **traffic_fields("mlp_kernel_m5"),
-                         "kernel": "mlp_kernel<MT=1> (fused MLP block, the step's dominant kernel), M = 5 verify rows",
+                         **traffic_fields("mlp_kernel_m8"),
+                         "kernel": f"mlp_kernel (fused MLP block, the step's dominant W4A8 kernel), M = {R} verify rows",
                          "us_per_launch": round(mlp_us, 3), "algorithmic_bytes_per_launch": mlp_b},
             "step_roofline": {"achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                               "algorithmic_bytes_per_step": step_bytes,
-                              "what": "whole step: W4 body + bf16 lm_head (verify) + W4 lm_head x 4 and MTP block x 4 (drafts) + GDN states + KV"},
+                              "what": "whole step: W4 body + bf16 lm_head (verify and 4 drafts) + bf16 MTP block x 4 + "
+                                      "GDN states + KV"},
             "e2e": {"value": round(e2e_toks / (e2e_ms * 1e-3), 2), "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 32 * 8},
             "gpu_launches": args.steps * model.own_launches_per_step(), "clocks": clk.summary()}
@@ -644,7 +675,7 @@ def run_decode(args):
         dist.destroy_process_group()
 
 
-def cpu_decode_baseline():
+def cpu_decode_baseline(args=None):
     """The oracle's eager chain on the host cores for a bounded sample of one decode step: one GDN layer's
     projections (qkv | z, out) and MLP (gate, up, down) as act-quant + GPTQ linears over 5 verify rows, timed and
     scaled to the 32 layers' W4A8 bytes (attention layers have 0.97x a GDN layer's bytes: counted as GDN)."""
@@ -785,6 +816,7 @@ def main():
     ap.add_argument("--prompt", type=int, default=1024, help="decode: committed prompt length (KV prefix)")
     ap.add_argument("--rows", type=int, default=8, help="activation rows (tree-verify rows)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--no-second-prompt", action="store_true", help="decode: skip the prompt-4096 measurement")
     ap.add_argument("--programs", action="store_true",
                     help="decode: run the verify body as layer programs (one persistent launch per run of layers) "
                          "instead of one launch per fused op")
