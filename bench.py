@@ -14,8 +14,8 @@ Workload `gemv` (configs[0], the "W4A8 GEMV HBM GB/s" part): 64 verify-row linea
 (configs[1]): the fused MLP block over 4 weight copies (312 MB > L2).
 
 Multi-GPU: every rank runs its own replica (independent decode streams, no collective): scaling "weak".
---impl reference: the reference's arithmetic on the host cores (the CPU oracle restatement; the reference
-itself is SYCL for Intel GPUs and cannot run here), on a bounded sample of the same workload.
+--impl reference: the reference's arithmetic on the host cores (the CPU restatement; the reference itself is SYCL
+for Intel GPUs and cannot run here): for decode, the whole decode step of the same model as torch-CPU eager ops.
 """
 from __future__ import annotations
 
@@ -580,20 +580,30 @@ def run_decode(args):
     step_bytes = model.step_bytes()
     hbm, src = peaks()
     achieved = step_bytes / (step_ms * 1e-3) / 1e9
-    # e2e: the same loop with the step's result row read back to pinned host memory every step
-    host_res = torch.empty(32, dtype=torch.int64).pin_memory()
+    del graphs
+    # e2e through the plugin entry: mono_b200.mtp_loop.generate_device, what the _generate_mtp install point runs for
+    # a greedy generate (steps replayed from CUDA graphs, every step's result row copied to a device ring, the ring
+    # read back to the host every 8 steps to collect the committed tokens and check for stop tokens). Inside the
+    # timed region: the prompt's token ids copied host -> device (pinned) and seeding the loop (the prefill itself is
+    # left to stock, as in the reference), and the committed tokens read back.
+    from mono_b200 import mtp_loop
+    prompt_ids = torch.randint(0, cfg.vocab, (prompt,), generator=torch.Generator().manual_seed(rank)).pin_memory()
+    dev_ids = torch.empty(prompt, dtype=torch.int64, device=dev)
+    with torch.cuda.stream(stream):
+        mtp_loop.generate_device(model, 16)  # captures the loop's graphs (outside the timing)
+    stream.synchronize()
+    n_new = max(64, args.steps)
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    m0 = int(model.total.item())
-    e2e_steps = max(8, args.steps // 4)
     with torch.cuda.stream(stream):
         f0.record(stream)
-        for i in range(e2e_steps):
-            graphs[(args.steps + i) % 2].replay()
-            host_res.copy_(model.result, non_blocking=True)
+        dev_ids.copy_(prompt_ids, non_blocking=True)
+        model.next_tok.view(-1).copy_(dev_ids[-1:])
+        committed = mtp_loop.generate_device(model, n_new)
         f1.record(stream)
     stream.synchronize()
-    e2e_ms, e2e_toks = reduce_time_and_count(f0.elapsed_time(f1), int(model.total.item()) - m0, dev, world)
-    del graphs
+    e2e_steps = -(-n_new // 8) * 8  # whole rings of 8 steps (about one token per step)
+    e2e_ms, e2e_toks = reduce_time_and_count(f0.elapsed_time(f1), len(committed), dev, world)
+    model.release_graphs()
     # the dominant kernel alone (the fused MLP block): a graph of its launches over the layers' weights at the
     # step's 8 verify rows, averaged per launch with CUDA events
     import mono_b200._C as C_
@@ -664,8 +674,11 @@ def run_decode(args):
                               "algorithmic_bytes_per_step": step_bytes,
                               "what": "whole step: W4 body + bf16 lm_head (verify and 4 drafts) + bf16 MTP block x 4 + "
                                       "GDN states + KV"},
-            "e2e": {"value": round(e2e_toks / (e2e_ms * 1e-3), 2), "unit": "tok/s", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 32 * 8},
+            "e2e": {"value": round(e2e_toks / (e2e_ms * 1e-3), 2), "unit": "tok/s",
+                    "h2d_bytes_per_step": round(prompt * 8 / e2e_steps, 1), "d2h_bytes_per_step": 32 * 8,
+                    "path": "mono_b200.mtp_loop.generate_device (the _generate_mtp install point's greedy loop)",
+                    "copies": f"h2d: the prompt's {prompt} token ids (pinned) once per generate; d2h: a 256-byte "
+                              "result row per step, read in rings of 8"},
             "gpu_launches": args.steps * model.own_launches_per_step(), "clocks": clk.summary()}
         if cpu is not None:
             line["cpu_baseline"] = cpu
@@ -675,30 +688,44 @@ def run_decode(args):
         dist.destroy_process_group()
 
 
-def cpu_decode_baseline(args=None):
-    """The oracle's eager chain on the host cores for a bounded sample of one decode step: one GDN layer's
-    projections (qkv | z, out) and MLP (gate, up, down) as act-quant + GPTQ linears over 5 verify rows, timed and
-    scaled to the 32 layers' W4A8 bytes (attention layers have 0.97x a GDN layer's bytes: counted as GDN)."""
-    import numpy as np
+def _cpu_decode_run(prompt, warmup, steps, budget_s=None):
+    """The decode step of the same model (configs[4] shapes, tree4s1m8, greedy) as torch-CPU eager ops
+    (oracle/cpu_decode.py: int8 _int_mm per 128-group with fp32 epilogues, bf16 linears) on all the host's cores.
+    Runs `warmup` untimed steps, then up to `steps` timed ones (fewer when budget_s of timed work is spent).
+    Returns (seconds per step: list, committed tokens, threads, build seconds)."""
     import torch
 
-    from oracle import w4a8 as ow
+    from oracle.cpu_decode import CpuDecoder
     torch.set_num_threads(os.cpu_count() or 1)
-    rng = np.random.default_rng(0)
-    M, H, I = 5, 4096, 12288
-    mats = [(8192 + 4096, H), (H, 4096), (I, H), (I, H), (H, I)]
     t0 = time.perf_counter()
-    for N, K in mats:
-        packed = rng.integers(0, 2 ** 31, size=(N, K // 8), dtype=np.int64).astype(np.int32).view(np.uint8).reshape(N, K // 2)
-        scales = (np.abs(rng.standard_normal((N, K // 128))) * 0.02 / 7 + 1e-4).astype(np.float16)
-        x = torch.randn(M, K).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
-        q, s = ow.act_quant(x)
-        ow.gptq_linear(q, s, packed, scales)
-    layer_s = time.perf_counter() - t0
-    step_s = layer_s * 32
-    return {"value": round(1.0 / step_s, 4), "unit": "tok/s", "cores": os.cpu_count() or 1, "kind": "port",
-            "sample": f"one GDN layer's W4A8 projections + MLP over 5 verify rows ({layer_s:.1f} s), x 32 layers; "
-                      "lm_head, attention, GDN recurrence and the MTP head not counted (a lower bound on the CPU time)"}
+    model = CpuDecoder(prompt_len=prompt, gen_tokens=64 + 8 * (warmup + steps))
+    build = time.perf_counter() - t0
+    for _ in range(warmup):
+        model.step()
+    times, toks = [], 0
+    spent = 0.0
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        toks += len(model.step())
+        times.append(time.perf_counter() - t0)
+        spent += times[-1]
+        if budget_s is not None and spent > budget_s and len(times) >= 5:
+            break
+    return times, toks, torch.get_num_threads(), build
+
+
+def cpu_decode_baseline(args=None):
+    """cpu_baseline of the decode line: the median of 5 actually-run steps of the same decode step on the host
+    cores (_cpu_decode_run), in tok/s (committed tokens per step / the median step time)."""
+    prompt = args.prompt if args is not None else 1024
+    times, toks, threads, build = _cpu_decode_run(prompt, warmup=1, steps=5)
+    med = statistics.median(times)
+    per_step = toks / len(times)
+    return {"value": round(per_step / med, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"the whole decode step of the same model and tree (prompt {prompt}) as torch-CPU eager ops "
+                      f"(oracle/cpu_decode.py: int8 x int8 -> int32 per 128-group, fp32 epilogues, bf16 linears); "
+                      f"median of {len(times)} steps = {med:.3f} s, {per_step:.2f} tokens per step "
+                      f"(model built in {build:.0f} s)"}
 
 
 def cpu_baseline(ow, packed, scales, rows=None):
@@ -722,49 +749,28 @@ def cpu_baseline(ow, packed, scales, rows=None):
 
 
 def run_reference_decode(args):
-    """The reference arm of the decode workload: the reference's eager chain for the W4A8 layers (act quant +
-    GPTQ linear, the oracle port) on the host cores. Each step is a bounded sample: 1/256 of the output rows of
-    every W4A8 projection of one GDN layer (qkv|z, out, gate, up, down) over the 5 verify rows; the step time of
-    the whole model is the sample time x 256 x 32 layers (lm_head, attention, GDN recurrence and the MTP head not
-    counted: a lower bound on the CPU's step time, so an upper bound on its tok/s at one token per step)."""
-    import numpy as np
-    import torch
-
-    from oracle import w4a8 as ow
-    torch.set_num_threads(os.cpu_count() or 1)
-    M, H, I = 5, 4096, 12288
-    mats = [(8192 + 4096, H), (H, 4096), (I, H), (I, H), (H, I)]
-    rng = np.random.default_rng(0)
-    samples = []
-    for N, K in mats:
-        n = N // 256
-        packed, scales = ow.gen_gptq(n, K, seed=0x5EED + N + K)
-        x = torch.randn(M, K).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
-        samples.append((packed, scales, x))
-
-    def step():
-        for packed, scales, x in samples:
-            q, s_ = ow.act_quant(x)
-            ow.gptq_linear(q, s_, packed, scales)
-
-    for _ in range(args.warmup):
-        step()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        step()
-    t = (time.perf_counter() - t0) / args.steps
-    step_s = t * 256 * 32
-    value = 1.0 / step_s
-    cores = torch.get_num_threads()
+    """The reference arm of the decode workload, on the repo arm's config: the reference's eager chain for the
+    whole decode step (drafts of the tree, the verify of its 8 rows through all 32 layers, lm_head, greedy accept,
+    replay) restated as torch-CPU eager ops (oracle/cpu_decode.py; the reference's own chain is XPU torch / oneDNN
+    and cannot run here), on all the host's cores. W untimed steps, then the timed steps actually run (at most
+    --steps; fewer if 150 s of timed work is spent: `steps` reports the count timed). value = committed tokens /
+    the time of the timed steps."""
+    warm = min(args.warmup, 2)
+    times, toks, threads, build = _cpu_decode_run(args.prompt, warmup=warm, steps=args.steps, budget_s=150.0)
+    total = sum(times)
+    value = toks / total
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "tok/s", "n_gpus": 1,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 2),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
-            "data": "synthetic (seeded, BASELINE configs[4] shapes)",
-            "config": {"workload": "Qwen3.5-9B-shaped W4A8 MTP decode (configs[4]): the W4A8 layers of the eager "
-                                   "chain on the host cores, one token per step"},
-            "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": cores, "kind": "port",
-                             "sample": f"per step 1/256 of the output rows of one GDN layer's 5 W4A8 projections over "
-                                       f"5 verify rows ({t * 1e3:.1f} ms), scaled x 256 x 32 layers"},
+            "steps": len(times), "steps_requested": args.steps, "warmup": warm,
+            "ms_per_step": round(total / len(times) * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic (random-init Qwen3.5-9B-shaped W4A8 weights, seeded)",
+            "config": {"workload": f"Qwen3.5-9B-shaped W4A8 MTP decode (configs[4]): 8-node tree4s1m8 draft tree of "
+                                   f"depth 4 (bf16 MTP head, bf16 lm_head), 8 verify rows, greedy accept, prompt "
+                                   f"{args.prompt}, 1 stream",
+                       "layers": 32, "tokens_per_step": round(toks / len(times), 3),
+                       "engine": "torch-CPU eager ops (oracle/cpu_decode.py)", "model_build_s": round(build, 1)},
+            "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+                             "sample": f"{len(times)} whole decode steps of the same model and tree, all timed "
+                                       f"({total:.1f} s)"},
             "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 

@@ -412,6 +412,29 @@ class Qwen35W4A8:
         self.parity = 1 - self.parity
         return self.result
 
+    def step_graphed(self):
+        """step(), replayed from CUDA graphs: the first call runs two eager steps (workspaces, tables) and captures
+        one graph per GDN-buffer parity; every call then replays the graph of the current parity (the result row is
+        the same device tensor as step()'s)."""
+        if getattr(self, "_graphs", None) is None:
+            self.step()
+            self.step()
+            torch.cuda.current_stream(self.dev).synchronize()
+            graphs = {}
+            for _ in range(2):
+                p = self.parity
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    self.step()  # (flips self.parity; nothing runs until a replay)
+                graphs[p] = g
+            self._graphs = graphs
+        self._graphs[self.parity].replay()
+        self.parity = 1 - self.parity
+        return self.result
+
+    def release_graphs(self):
+        self._graphs = None
+
     def own_launches_per_step(self) -> int:
         """This build's kernel launches per step (the rest are a few torch gathers / copies)."""
         c = self.cfg

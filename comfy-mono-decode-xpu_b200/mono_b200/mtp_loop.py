@@ -44,23 +44,27 @@ def _install_device_kv(classes):
     return done
 
 
-def generate_device(decoder, max_new_tokens, stop_tokens=()):
-    """Greedy MTP generation on a mono_b200 decoder: steps are queued without host reads; the committed tokens
-    are read back once every `sync_every` steps to check the stop condition."""
+def generate_device(decoder, max_new_tokens, stop_tokens=(), sync_every=8):
+    """Greedy MTP generation on a mono_b200 decoder: steps are queued without host reads (replayed from CUDA graphs
+    when the decoder offers step_graphed); each step's result row is copied to a device ring, and the committed
+    tokens are read back once every `sync_every` steps (one device -> host copy of the ring) to check the stop
+    condition (the reference reads each step one step late from a pinned ring, mtp_loop.py:413-441)."""
     out = []
     stop = set(int(t) for t in stop_tokens)
-    sync_every = 8
-    results = []
+    step = getattr(decoder, "step_graphed", None) or decoder.step
+    ring = None
     while len(out) < max_new_tokens:
-        for _ in range(sync_every):
-            results.append(decoder.step().clone())
-        for r in torch.stack(results).cpu().tolist():
+        for i in range(sync_every):
+            r = step()
+            if ring is None:
+                ring = torch.empty(sync_every, r.numel(), dtype=r.dtype, device=r.device)
+            ring[i].copy_(r)
+        for r in ring.cpu().tolist():
             n = r[0]
             for t in r[1:1 + n]:
                 out.append(t)
                 if t in stop or len(out) >= max_new_tokens:
                     return out
-        results.clear()
     return out
 
 

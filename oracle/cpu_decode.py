@@ -20,13 +20,33 @@ import torch.nn.functional as F
 from .mtp import accept_walk
 
 
+class _Pool:
+    """Random bytes for the int4 weights, made fast: one 64 MB block of uniform random bytes, from which each matrix
+    takes a window at a random offset, XORed with a random byte (every matrix gets its own bytes, uniform)."""
+
+    def __init__(self, g):
+        self.g = g
+        self.block = torch.randint(0, 256, (1 << 26,), dtype=torch.uint8, generator=g)
+
+    def int4(self, n):
+        out = torch.empty(n, dtype=torch.uint8)
+        o, key = int(torch.randint(0, 1 << 26, (1,), generator=self.g)), int(torch.randint(0, 256, (1,), generator=self.g))
+        done = 0
+        while done < n:
+            take = min(n - done, (1 << 26) - o)
+            torch.bitwise_xor(self.block[o:o + take], key, out=out[done:done + take])
+            done += take
+            o = 0
+        return (out & 15).view(torch.int8) - 8
+
+
 class _W4:
     """GPTQ W4 weight for the CPU: int8 values in [-8, 7] laid out [G][128][N] (per group, K-major), fp32 scales
     [G][N]."""
 
-    def __init__(self, N, K, g):
+    def __init__(self, N, K, g, pool):
         G = K // 128
-        self.q = torch.randint(-8, 8, (G, 128, N), dtype=torch.int8, generator=g)
+        self.q = pool.int4(G * 128 * N).view(G, 128, N)
         self.s = (torch.randn(G, N, generator=g).abs() * (0.02 / 7) + 1e-4).half().float()
         self.N, self.K = N, K
 
@@ -43,6 +63,7 @@ class CpuDecoder:
                  head_dim=256, rotary_dim=64, rope_theta=1e7, gdn_k_heads=16, gdn_v_heads=32, gdn_dim=128, eps=1e-6,
                  tree=(2, 2, 2, 1), prompt_len=1024, gen_tokens=256, seed=0x5EED + 4):
         g = torch.Generator().manual_seed(seed)
+        pool = _Pool(g)
         self.H, self.I, self.V, self.eps = hidden, inter, vocab, eps
         self.heads, self.kvh, self.hd, self.rd = heads, kv_heads, head_dim, rotary_dim
         self.HK, self.HV, self.D = gdn_k_heads, gdn_v_heads, gdn_dim
@@ -55,15 +76,15 @@ class CpuDecoder:
         self.layers = []
         for i in range(layers):
             L = {"attn": (i + 1) % attn_every == 0, "ln1": _bf((H,), g, 0.02, 1.0), "ln2": _bf((H,), g, 0.02, 1.0),
-                 "gate": _W4(I, H, g), "up": _W4(I, H, g), "down": _W4(H, I, g)}
+                 "gate": _W4(I, H, g, pool), "up": _W4(I, H, g, pool), "down": _W4(H, I, g, pool)}
             if L["attn"]:
-                L.update(q=_W4(2 * heads * hd, H, g), k=_W4(kv_heads * hd, H, g), v=_W4(kv_heads * hd, H, g),
-                         o=_W4(H, heads * hd, g), q_norm=_bf((hd,), g, 0.3, 1.0), k_norm=_bf((hd,), g, 0.3, 1.0),
+                L.update(q=_W4(2 * heads * hd, H, g, pool), k=_W4(kv_heads * hd, H, g, pool), v=_W4(kv_heads * hd, H, g, pool),
+                         o=_W4(H, heads * hd, g, pool), q_norm=_bf((hd,), g, 0.3, 1.0), k_norm=_bf((hd,), g, 0.3, 1.0),
                          kc=torch.randn(kv_heads, self.cap, hd, generator=g).bfloat16(),
                          vc=torch.randn(kv_heads, self.cap, hd, generator=g).bfloat16())
             else:
                 HV, Dg = gdn_v_heads, gdn_dim
-                L.update(qkv=_W4(self.C, H, g), z=_W4(HV * Dg, H, g), out=_W4(H, HV * Dg, g), wab=_bf((2 * HV, H), g),
+                L.update(qkv=_W4(self.C, H, g, pool), z=_W4(HV * Dg, H, g, pool), out=_W4(H, HV * Dg, g, pool), wab=_bf((2 * HV, H), g),
                          conv_w=_bf((self.C, 4), g, 0.5), conv_state=_bf((self.C, 3), g, 1.0),
                          dt_bias=torch.zeros(HV), g_decay=-torch.ones(HV), gnorm=_bf((Dg,), g, 0.1, 1.0),
                          state=torch.randn(HV, Dg, Dg, generator=g) * 0.1, saved=None)
