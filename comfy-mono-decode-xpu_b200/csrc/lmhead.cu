@@ -6,7 +6,8 @@
 // and the top-k (k <= 8, top-k rank), without writing the logits (optional).
 //
 // Work: a persistent grid; warp w of CTA b takes column groups of NC columns g = b * 8 + w, + G * 8, ... (NC > 1
-// at several rows: one load of each x piece serves NC columns; the per-column arithmetic is unchanged). Lane m < M
+// at several rows: one load of each x piece serves NC columns; the per-column arithmetic is unchanged; two rows
+// share each paired fma, __ffma2_rn, whose halves round exactly as fmaf). Lane m < M
 // keeps row m's running top-k list and argmax in registers. At the end the CTA merges its warps' lists in shared
 // memory and writes them to the workspace; the last CTA to finish (an arrival counter) merges the CTAs' lists -
 // ranks are distinct, so the merge order does not matter - and writes the indices. The pick form then scatters the
@@ -37,15 +38,15 @@ struct LmHeadArgs {
     int64_t* topk;            // [M][k] or null (k = 0: none)
     const int32_t* children;  // pick form: up to 8 slots of dst, -1 ends (row 0's tokens), or null
     int64_t* dst;             // pick form: the verify-token row
-    uint64_t* ws;             // [G][kLhMaxM][kTkK + 1] CTA lists, then the arrival counter
+    uint64_t* ws;             // the arrival counter (first 256 bytes), then [G][kLhMaxM][kTkK + 1] CTA lists
     int64_t x_stride;
     int K, V, M, k;
 };
 
 size_t lmhead_workspace_bytes(int grid) { return size_t(grid) * kLhMaxM * (kTkK + 1) * 8 + 256; }
 
-template <int M, int NC>
-__global__ void __launch_bounds__(kLhWarps * 32, kLhCtasPerSm) lmhead_pick_kernel(const LmHeadArgs A) {
+template <int M, int NC, int CPS>
+__global__ void __launch_bounds__(kLhWarps * 32, CPS) lmhead_pick_kernel(const LmHeadArgs A) {
     constexpr int NT = kLhWarps * 32;
     __shared__ uint64_t lst[kLhWarps][M][kTkK + 1];
     __shared__ uint64_t fin[NT * kTkK];
@@ -60,28 +61,26 @@ __global__ void __launch_bounds__(kLhWarps * 32, kLhCtasPerSm) lmhead_pick_kerne
     uint64_t top[kTkK], best = 0;
 #pragma unroll
     for (int j = 0; j < kTkK; ++j) top[j] = 0;
+    constexpr int MP = (M + 1) / 2;  // row pairs (an odd M pads its last pair with a zero row)
     for (int grp = int(blockIdx.x) * kLhWarps + warp; grp < groups; grp += G * kLhWarps) {
         const int n0 = grp * NC;
         float acc[NC][M];
+        if constexpr (M == 1) {
 #pragma unroll
-        for (int c = 0; c < NC; ++c)
+            for (int c = 0; c < NC; ++c) acc[c][0] = 0.f;
+            for (int j = 0; j < per_lane; ++j) {
+                const int64_t piece = int64_t(j) * 32 + lane;
+                uint4 wv[NC];
 #pragma unroll
-            for (int m = 0; m < M; ++m) acc[c][m] = 0.f;
-        for (int j = 0; j < per_lane; ++j) {
-            const int64_t piece = int64_t(j) * 32 + lane;
-            uint4 wv[NC];
-#pragma unroll
-            for (int c = 0; c < NC; ++c)
-                wv[c] = n0 + c < A.V ? lh_ld_stream(reinterpret_cast<const uint4*>(A.w + int64_t(n0 + c) * A.K) + piece, pol)
-                                     : make_uint4(0, 0, 0, 0);
-#pragma unroll
-            for (int m = 0; m < M; ++m) {
-                const uint4 xv = __ldg(reinterpret_cast<const uint4*>(A.x + m * A.x_stride) + piece);
+                for (int c = 0; c < NC; ++c)
+                    wv[c] = n0 + c < A.V ? lh_ld_stream(reinterpret_cast<const uint4*>(A.w + int64_t(n0 + c) * A.K) + piece, pol)
+                                         : make_uint4(0, 0, 0, 0);
+                const uint4 xv = __ldg(reinterpret_cast<const uint4*>(A.x) + piece);
                 const float xf[8] = {lh_lo(xv.x), lh_hi(xv.x), lh_lo(xv.y), lh_hi(xv.y),
                                      lh_lo(xv.z), lh_hi(xv.z), lh_lo(xv.w), lh_hi(xv.w)};
 #pragma unroll
                 for (int c = 0; c < NC; ++c) {
-                    float a = acc[c][m];
+                    float a = acc[c][0];
                     a = fmaf(lh_lo(wv[c].x), xf[0], a);
                     a = fmaf(lh_hi(wv[c].x), xf[1], a);
                     a = fmaf(lh_lo(wv[c].y), xf[2], a);
@@ -90,9 +89,57 @@ __global__ void __launch_bounds__(kLhWarps * 32, kLhCtasPerSm) lmhead_pick_kerne
                     a = fmaf(lh_hi(wv[c].z), xf[5], a);
                     a = fmaf(lh_lo(wv[c].w), xf[6], a);
                     a = fmaf(lh_hi(wv[c].w), xf[7], a);
-                    acc[c][m] = a;
+                    acc[c][0] = a;
                 }
             }
+        } else {
+            // two rows per paired fma (__ffma2_rn: each half rounds as fmaf, so the bits are the scalar order's)
+            float2 acc2[NC][MP];
+#pragma unroll
+            for (int c = 0; c < NC; ++c)
+#pragma unroll
+                for (int p = 0; p < MP; ++p) acc2[c][p] = make_float2(0.f, 0.f);
+            // the weight pieces of step j + 1 are requested before step j's arithmetic (one step of look-ahead)
+            uint4 wn[NC];
+#pragma unroll
+            for (int c = 0; c < NC; ++c)
+                wn[c] = n0 + c < A.V ? lh_ld_stream(reinterpret_cast<const uint4*>(A.w + int64_t(n0 + c) * A.K) + lane, pol)
+                                     : make_uint4(0, 0, 0, 0);
+            for (int j = 0; j < per_lane; ++j) {
+                const int64_t piece = int64_t(j) * 32 + lane;
+                uint4 wv[NC];
+#pragma unroll
+                for (int c = 0; c < NC; ++c) {
+                    wv[c] = wn[c];
+                    if (j + 1 < per_lane && n0 + c < A.V)
+                        wn[c] = lh_ld_stream(reinterpret_cast<const uint4*>(A.w + int64_t(n0 + c) * A.K) + piece + 32, pol);
+                }
+                uint4 xv[2 * MP];
+#pragma unroll
+                for (int m = 0; m < 2 * MP; ++m)
+                    xv[m] = m < M ? __ldg(reinterpret_cast<const uint4*>(A.x + m * A.x_stride) + piece) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    float2 xp[MP];
+#pragma unroll
+                    for (int p = 0; p < MP; ++p) {
+                        const uint32_t ua = (&xv[2 * p].x)[e >> 1], ub = (&xv[2 * p + 1].x)[e >> 1];
+                        xp[p] = make_float2((e & 1) ? lh_hi(ua) : lh_lo(ua), (e & 1) ? lh_hi(ub) : lh_lo(ub));
+                    }
+#pragma unroll
+                    for (int c = 0; c < NC; ++c) {
+                        const uint32_t uw = (&wv[c].x)[e >> 1];
+                        const float wf = (e & 1) ? lh_hi(uw) : lh_lo(uw);
+                        const float2 w2 = make_float2(wf, wf);
+#pragma unroll
+                        for (int p = 0; p < MP; ++p) acc2[c][p] = __ffma2_rn(w2, xp[p], acc2[c][p]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < NC; ++c)
+#pragma unroll
+                for (int m = 0; m < M; ++m) acc[c][m] = (m & 1) ? acc2[c][m >> 1].y : acc2[c][m >> 1].x;
         }
 #pragma unroll
         for (int c = 0; c < NC; ++c) {
@@ -124,8 +171,9 @@ __global__ void __launch_bounds__(kLhWarps * 32, kLhCtasPerSm) lmhead_pick_kerne
         lst[warp][lane][kTkK] = best;
     }
     __syncthreads();
-    uint64_t* ws = A.ws;
-    unsigned* counter = reinterpret_cast<unsigned*>(A.ws + size_t(G) * kLhMaxM * (kTkK + 1));
+    // the counter sits at a fixed offset, so calls of any grid size share a workspace safely
+    unsigned* counter = reinterpret_cast<unsigned*>(A.ws);
+    uint64_t* ws = A.ws + 32;
     if (warp == 0 && lane < M) {
         for (int w = 1; w < kLhWarps; ++w) {
             for (int j = 0; j < A.k; ++j) insert_rank(top, lst[w][lane][j], A.k);
@@ -197,10 +245,12 @@ static int launch_lh(const LmHeadArgs& A, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    CUDA_TRY(cudaLaunchKernelEx(&cfg, lmhead_pick_kernel<M, NC>, A));
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, lmhead_pick_kernel<M, NC, kLhCtasPerSm>, A));
     return MONO_OK;
 }
 
+// (measured at 8 rows: 4 columns per warp at 2 CTAs per SM, 460 us; 2 columns at 3 CTAs per SM, 599 us; 8 columns
+// at 1 CTA per SM, 575 us)
 int launch_lmhead(const LmHeadArgs& A, cudaStream_t stream) {
     switch (A.M) {
         case 1: return launch_lh<1, 1>(A, stream);

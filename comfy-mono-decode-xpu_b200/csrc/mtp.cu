@@ -3,9 +3,10 @@
 //   prep_draft   MTP KV positions / seqlen of draft k and the draft's rope row
 //   prep_verify  attention positions / seqlen, verify rope positions, ctl parity and tree program
 //   accept       the greedy accept walk (continue along the child whose draft token is the token the verify
-//                chose), the result row [n, commit[8], row, on_chain, nranks, ranks[7], pos, kept], the
-//                counters st (st[0] committed length, st[1] MTP KV length), ctl (pending, slots), the next
-//                token and hidden row, and the attention KV slot moves of an off-chain path
+//                chose; warp-parallel over a node's children), the result row [n, commit[8], row, on_chain,
+//                nranks, ranks[7], pos, kept], the counters st (st[0] committed length, st[1] MTP KV length), ctl
+//                (pending, slots), the next token and hidden row, and the attention KV slot moves of an off-chain
+//                path (vector copies)
 // st int64 [4]; ctl int32 [2 + 3 * 8] = [pending, parity, accepted[8], parent[8], prog[8]].
 #include "launch.h"
 
@@ -53,85 +54,115 @@ struct AcceptArgs {
     int rows, depth;
 };
 
-__global__ void __launch_bounds__(1024) mtp_accept_kernel(const AcceptArgs A) {
-    __shared__ int sh[kSlots + 4];
+// The accept step, in three parts:
+//   walk     warp 0: at node `cur`, lane j < 8 reads child j of cur and tests its draft token against the verify's
+//            token at cur; the first passing child (a ballot, lowest lane) is the next node. A child index that is
+//            not after its parent or not below `rows` ends the walk and records DEV_BAD_TREE (a malformed table
+//            would otherwise repeat rows or move a KV slot before it is read). Then lanes write the result row,
+//            counters, ctl and next token in parallel: result = [n, commit[8], row, on_chain, nranks, ranks[7], pos,
+//            kept] (csrc/mtp_loop.sycl:143 layout).
+//   hidden   every thread copies 16-byte pieces of the chosen row's hidden state.
+//   KV       an off-chain path: accepted row path[k] moves to slot pos + k (FixedKVState.commit_path), one 16-byte
+//            piece of one (cache, head) row per thread, k ascending with a barrier between (path[k] >= k, so a slot is
+//            read before a later move could write it).
+__global__ void __launch_bounds__(256) mtp_accept_kernel(const AcceptArgs A) {
+    __shared__ int path[kSlots];
+    __shared__ int meta[4];  // len, row, on_chain
     __shared__ int64_t base;
-    const int t = threadIdx.x;
-    if (t == 0) {
-        int path[kSlots], len = 1;
-        path[0] = 0;
+    const int t = threadIdx.x, lane = t & 31;
+    if (t < 32) {
+        int len = 1, cur = 0;
+        if (lane == 0) path[0] = 0;
+        bool bad = false;
         while (len < A.rows) {
-            const int cur = path[len - 1];
-            int next = -1;
-            for (int j = 0; j < kSlots; ++j) {
-                const int c = A.children[cur * kSlots + j];
-                if (c < 0 || c >= A.rows) break;
-                if (A.drafts[c] == A.toks[cur]) {
-                    next = c;
-                    break;
-                }
+            const int c = lane < kSlots ? A.children[cur * kSlots + lane] : -1;
+            // children end at the first -1: lanes past it do not count
+            const unsigned ends = ~__ballot_sync(0xffffffffu, c >= 0) & ((1u << kSlots) - 1u);
+            const int first_end = ends ? __ffs(ends) - 1 : kSlots;  // lanes below it are listed children
+            const bool listed = lane < first_end && c >= 0;
+            const bool valid = !listed || (c > cur && c < A.rows);
+            if (__any_sync(0xffffffffu, !valid)) {
+                bad = true;
+                break;
             }
-            if (next < 0) break;
-            path[len++] = next;
+            const unsigned hit = __ballot_sync(0xffffffffu, listed && A.drafts[listed ? c : 0] == A.toks[cur]);
+            if (hit == 0u) break;
+            const int next = __shfl_sync(0xffffffffu, c, __ffs(hit) - 1);
+            if (lane == 0) path[len] = next;
+            ++len;
+            cur = next;
         }
-        const int row = path[len - 1];
+        if (bad && lane == 0) set_device_error(DEV_BAD_TREE);
+        __syncwarp();
+        const int row = cur;
         const bool on_chain = row == len - 1;
         const int keep = on_chain ? len : len - 1;
         const int kept = keep < A.depth ? keep : A.depth;
         const int64_t pos = A.st[0];
         int64_t* rp = A.result;
-        rp[0] = len;
-        for (int i = 1; i < len; ++i) rp[i] = A.drafts[path[i]];
-        rp[len] = A.toks[row];
-        for (int i = len + 1; i <= kSlots; ++i) rp[i] = -1;
-        rp[9] = row;
-        rp[10] = on_chain;
-        int nr = 0;
-        if (A.cand != nullptr)
-            for (int i = 0; i < len && path[i] < A.depth; ++i) {
-                const int node = path[i];
-                int r = kRanks;
-                for (int q = 0; q < kRanks; ++q)
-                    if (A.cand[node * kRanks + q] == A.toks[node]) {
-                        r = q;
-                        break;
-                    }
-                rp[12 + nr++] = r;
-            }
-        rp[11] = nr;
-        for (int i = 12 + nr; i < 19; ++i) rp[i] = 0;
-        rp[19] = pos;
-        rp[20] = kept;
-        A.st[0] = pos + len;
-        A.st[1] = A.st[1] + kept;
-        A.ctl[0] = len;
-        for (int i = 0; i < kSlots; ++i) A.ctl[2 + i] = i < len ? path[i] : i;
-        A.next_tok[0] = A.toks[row];
-        for (int i = 0; i < kSlots; ++i) sh[i] = i < len ? path[i] : i;
-        sh[kSlots] = len;
-        sh[kSlots + 1] = row;
-        sh[kSlots + 2] = on_chain;
-        base = pos;
+        // rank of the verify token among a chain node's candidates (auto-tree statistics), lanes = path entries
+        int r = kRanks;
+        const int node = lane < len ? path[lane] : 0;
+        const bool ranked = A.cand != nullptr && lane < len && node < A.depth;
+        if (ranked)
+            for (int q = 0; q < kRanks; ++q)
+                if (A.cand[node * kRanks + q] == A.toks[node]) {
+                    r = q;
+                    break;
+                }
+        // ranks are recorded for the path's leading run of chain nodes (the walk's order)
+        const unsigned rk = __ballot_sync(0xffffffffu, ranked);
+        const int nr = __ffs(~rk) - 1;
+        if (lane <= kSlots)
+            rp[lane] = lane == 0 ? len : (lane < len ? A.drafts[path[lane]] : (lane == len ? A.toks[row] : -1));
+        if (lane < kRanks) rp[12 + lane] = lane < nr ? r : 0;
+        if (lane < kSlots) A.ctl[2 + lane] = lane < len ? path[lane] : lane;
+        if (lane == 0) {
+            rp[9] = row;
+            rp[10] = on_chain;
+            rp[11] = nr;
+            rp[19] = pos;
+            rp[20] = kept;
+            A.st[0] = pos + len;
+            A.st[1] = A.st[1] + kept;
+            A.ctl[0] = len;
+            A.next_tok[0] = A.toks[row];
+            meta[0] = len;
+            meta[1] = row;
+            meta[2] = on_chain;
+            base = pos;
+        }
     }
     __syncthreads();
-    const int len = sh[kSlots], row = sh[kSlots + 1];
-    for (int64_t i = t; i < A.H; i += blockDim.x) A.h_out[i] = A.x[int64_t(row) * A.H + i];
-    if (!sh[kSlots + 2]) {
-        // accepted row path[k] becomes slot base + k, in ascending k (a row never sits above its depth, so no
-        // later source is overwritten first)
-        const int64_t slot = A.heads * A.head_dim;
-        for (int k = 1; k < len; ++k) {
-            const int r = sh[k];
-            if (r != k) {
-                const int64_t dst = (base + k) % A.cap, src = (base + r) % A.cap;
-                for (int64_t e = t; e < A.nkv * slot; e += blockDim.x) {
-                    const int64_t which = e / slot, w = e % slot, h = w / A.head_dim, d = w % A.head_dim;
-                    uint16_t* p = reinterpret_cast<uint16_t*>(A.kv_ptrs[which]);
-                    p[(h * A.cap + dst) * A.head_dim + d] = p[(h * A.cap + src) * A.head_dim + d];
-                }
+    const int len = meta[0], row = meta[1];
+    // the chosen row's hidden state (16-byte pieces when the sizes allow, else elements)
+    if ((A.H & 7) == 0 && (reinterpret_cast<uintptr_t>(A.x) & 15) == 0 && (reinterpret_cast<uintptr_t>(A.h_out) & 15) == 0) {
+        const uint4* src = reinterpret_cast<const uint4*>(A.x + int64_t(row) * A.H);
+        uint4* dst = reinterpret_cast<uint4*>(A.h_out);
+        for (int64_t i = t; i < A.H / 8; i += blockDim.x) dst[i] = src[i];
+    } else {
+        for (int64_t i = t; i < A.H; i += blockDim.x) A.h_out[i] = A.x[int64_t(row) * A.H + i];
+    }
+    if (meta[2]) return;  // on the chain: every accepted row already sits at its slot
+    // pieces of 8 elements (a 16-byte copy when the cache row is 16-byte aligned, else 8 element copies)
+    const int64_t per_row = (A.head_dim + 7) / 8, pieces = A.nkv * A.heads * per_row;
+    for (int k = 1; k < len; ++k) {
+        const int src_row = path[k];
+        if (src_row != k) {
+            const int64_t dst = (base + k) % A.cap, src = (base + src_row) % A.cap;
+            for (int64_t i = t; i < pieces; i += blockDim.x) {
+                const int64_t which = i / (A.heads * per_row), rem = i - which * A.heads * per_row;
+                const int64_t h = rem / per_row, e0 = (rem - h * per_row) * 8;
+                uint16_t* cache = reinterpret_cast<uint16_t*>(A.kv_ptrs[which]);
+                uint16_t* d = cache + (h * A.cap + dst) * A.head_dim + e0;
+                const uint16_t* s0 = cache + (h * A.cap + src) * A.head_dim + e0;
+                if (e0 + 8 <= A.head_dim && ((reinterpret_cast<uintptr_t>(d) | reinterpret_cast<uintptr_t>(s0)) & 15) == 0)
+                    *reinterpret_cast<uint4*>(d) = *reinterpret_cast<const uint4*>(s0);
+                else
+                    for (int64_t e = 0; e < 8 && e0 + e < A.head_dim; ++e) d[e] = s0[e];
             }
-            __syncthreads();
         }
+        __syncthreads();
     }
 }
 
@@ -188,7 +219,7 @@ int mono_mtp_accept(int64_t* st, const int64_t* toks, const int64_t* drafts, con
     A.head_dim = head_dim;
     A.rows = int(rows);
     A.depth = int(depth);
-    mtp_accept_kernel<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(A);
+    mtp_accept_kernel<<<1, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(A);
     CUDA_TRY(cudaGetLastError());
     return MONO_OK;
 }

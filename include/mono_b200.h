@@ -229,7 +229,10 @@ MONO_API int mono_gdn_step(const void* qkv, const void* z, const void* a, const 
 /* The deferred form used by the device MTP loop (the reference's replay + verify, csrc/mono_gdn.sycl:385-567):
  * first the n = ctl[0] rows accepted at the previous step (slots ctl[2 + i], their inputs in prev_qkv [8][C],
  * prev_a / prev_b [8][HV] as saved by that step) are replayed and the recurrent and conv states persisted;
- * then the M verify rows run as a chain on a register copy of the state (core outputs only, nothing persisted)
+ * then the M verify rows run as a tree on a register copy of the state (core outputs only, nothing persisted):
+ * verify row t's conv reads its own input, then its ancestors' (parents ctl[10 + t], -1 at the root), then the
+ * committed history; the program ctl[18 + e] (slot | 32 to advance the copy, up to the first slot outside
+ * [0, M)) orders the rows so each sees the state after its parent (rows no entry names give a zero raw output);
  * and their inputs are saved to save_qkv / save_a / save_b (which must not alias the prev buffers: alternate
  * two sets between steps). ctl: int32 [26] as written by mono_mtp_accept. qkv, z and a / b may be column
  * slices of wider rows: their row strides (elements) are given (qkv_stride >= C, z_stride >= HV * 128,
@@ -291,7 +294,9 @@ MONO_API int mono_mtp_prep_verify(const int64_t* st, int64_t* apos, int64_t np, 
  * kept]; st[0] += n, st[1] += kept (kept = min(on_chain ? n : n - 1, depth)); ctl[0] = n,
  * ctl[2 + i] = path[i] (i < n, else i); next_tok = toks[row]; h_out = x[row] (bf16 [rows][H]); for an
  * off-chain path, in every bf16 KV cache [heads][cap][head_dim] listed in kv_ptrs (device int64 [nkv]),
- * slot (pos + path[k]) % cap moves to (pos + k) % cap for k = 1 .. n - 1. cand NULL: no ranks. */
+ * slot (pos + path[k]) % cap moves to (pos + k) % cap for k = 1 .. n - 1. cand NULL: no ranks. A listed child
+ * index that is not after its parent or not below rows ends the walk there and sets the device status to 5
+ * (mono_device_status). */
 MONO_API int mono_mtp_accept(int64_t* st, const int64_t* toks, const int64_t* drafts, const int64_t* cand,
                              const int32_t* children, int64_t rows, int64_t depth, const void* x, int64_t H,
                              int64_t* next_tok, void* h_out, int32_t* ctl, const int64_t* kv_ptrs, int64_t nkv,

@@ -114,3 +114,26 @@ def test_mtp_prep_match_oracle(cuda):
     apos_h, aseq_h, vpos_h = om.prep_verify(st.cpu().numpy(), SLOTS, tpos.cpu().numpy(), ctl_h, tctl.cpu().numpy(), 1, 5)
     assert list(apos.cpu().numpy()) == list(apos_h) and aseq.item() == aseq_h
     assert list(vpos.view(-1).cpu().numpy()) == list(vpos_h) and np.array_equal(ctl.cpu().numpy(), ctl_h)
+
+
+def test_mtp_accept_malformed_children_table_stops_with_status(cuda):
+    """A children table whose entry points back to an earlier row (a cycle) ends the walk at that node and sets the
+    device status (5), instead of repeating rows or moving a KV slot before it is read."""
+    from mono_b200 import _C
+    _C.device_status()  # clear
+    ch = torch.full((SLOTS, SLOTS), -1, dtype=torch.int32)
+    ch[0, 0], ch[1, 0] = 1, 0  # 0 -> 1 -> 0
+    toks = torch.tensor([[5, 5, 0, 0, 0, 0, 0, 0]], dtype=torch.int64, device=cuda)
+    dr = torch.tensor([[5, 5, 0, 0, 0, 0, 0, 0]], dtype=torch.int64, device=cuda)
+    st = torch.tensor([10, 10, 0, 0], dtype=torch.int64, device=cuda)
+    x = torch.zeros(SLOTS, 64, dtype=torch.bfloat16, device=cuda)
+    nt = torch.zeros(1, 1, dtype=torch.int64, device=cuda)
+    hb = torch.zeros(1, 1, 64, dtype=torch.bfloat16, device=cuda)
+    ctl = torch.zeros(26, dtype=torch.int32, device=cuda)
+    result = torch.zeros(32, dtype=torch.int64, device=cuda)
+    ptrs = torch.empty(0, dtype=torch.int64, device=cuda)
+    _C.mtp_accept(st, toks, dr, None, ch.reshape(-1).to(cuda), SLOTS, 4, x, nt, hb, ctl, ptrs, 1, 32, 64, result)
+    torch.cuda.synchronize()
+    assert result[0].item() == 2  # rows 0 and 1, then the bad entry (back to 0) ends the walk
+    assert _C.device_status() == 5
+    assert _C.device_status() == 0  # (reset by the read)
