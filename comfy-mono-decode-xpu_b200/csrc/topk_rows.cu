@@ -1,10 +1,13 @@
 // Exact top-k (k <= 64) of a few long rows: the verify step's sampling filter (the role of the reference's
 // topk_rows, csrc/topk_rows.sycl:2-17). The result is torch.topk of the rows' fp32 values: per row the k
 // largest by the radix key (the fp32 bits with the sign flipped: -0 below +0, no NaN case), sorted descending,
-// ties in the torch-XPU gather order. Each element gets a unique 64-bit rank (csrc/topk_rows.sycl:34-42):
-//   key = bits ^ (sign ? 0xFFFFFFFF : 0x80000000);   off = i % 32768;
-//   g = (i / 32768) << 15 | ((off % 4096) / 4) << 5 | (off / 4096) << 2 | off % 4
-//   rank = key << 32 | (0xFFFFFFFF - g)        (larger = earlier in the output)
+// ties in one of two orders. Each element gets a unique 64-bit rank (larger = earlier in the output):
+//   key = bits ^ (sign ? 0xFFFFFFFF : 0x80000000);   rank = key << 32 | (0xFFFFFFFF - g)
+//   gather order (ORD 0, the reference platform's torch topk, csrc/topk_rows.sycl:34-42):
+//     off = i % 32768;  g = (i / 32768) << 15 | ((off % 4096) / 4) << 5 | (off / 4096) << 2 | off % 4
+//   index order (ORD 1): g = i, equal values by ascending index -- torch's CUDA topk order for k >= 33 (and k = 1)
+//     as measured on B200 over tie-heavy rows (for 2 <= k <= 32 its order among equal values is its small
+//     sorting network's, which no fixed rule reproduces)
 // Kernel 1, CTA = (row, slice): each warp keeps the 64 best ranks of its elements sorted in registers (lane l
 // holds entries l and 32 + l); an element enters only if it beats the list's last entry, by a warp-wide
 // insertion (a ballot counts the entries above it, the rest shift by one lane), or, when 4 or more lanes hold a
@@ -20,15 +23,17 @@ namespace mono {
 
 constexpr int kTrK = 64, kTrWarps = 8, kTrThreads = kTrWarps * 32, kTrMaxSlices = 64, kTrMaxRows = 16;
 
+template <int ORD>
 __device__ __forceinline__ uint64_t tr_rank(uint32_t bits, uint32_t i) {
     const uint32_t key = bits ^ ((bits & 0x80000000u) ? 0xFFFFFFFFu : 0x80000000u);
     const uint32_t off = i & 32767u;
-    const uint32_t g = ((i >> 15) << 15) | (((off & 4095u) >> 2) << 5) | ((off >> 12) << 2) | (off & 3u);
+    const uint32_t g = ORD ? i : ((i >> 15) << 15) | (((off & 4095u) >> 2) << 5) | ((off >> 12) << 2) | (off & 3u);
     return (uint64_t(key) << 32) | uint64_t(0xFFFFFFFFu - g);
 }
+template <int ORD>
 __device__ __forceinline__ uint32_t tr_index(uint64_t r) {
     const uint32_t g = 0xFFFFFFFFu - uint32_t(r);
-    return ((g >> 15) << 15) | (((g >> 2) & 7u) << 12) | (((g >> 5) & 1023u) << 2) | (g & 3u);
+    return ORD ? g : ((g >> 15) << 15) | (((g >> 2) & 7u) << 12) | (((g >> 5) & 1023u) << 2) | (g & 3u);
 }
 
 // The warp's sorted list: L[l] = a (lane l), L[32 + l] = b (lane l), descending.
@@ -103,7 +108,7 @@ __device__ __forceinline__ uint32_t tr_bits_at(const void* x, size_t i) {
     else return __ldg(static_cast<const uint32_t*>(x) + i);
 }
 
-template <bool BF16>
+template <bool BF16, int ORD>
 __global__ void __launch_bounds__(kTrThreads) topk_rows_partial(const void* x, int64_t N, int slices, uint64_t* ws) {
     __shared__ uint64_t lists[kTrWarps][kTrK];
     const int row = blockIdx.y, slice = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -131,7 +136,7 @@ __global__ void __launch_bounds__(kTrThreads) topk_rows_partial(const void* x, i
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const int64_t i = b0 + u * 32 + lane;
-            L.offer(tr_rank(bits[u], uint32_t(i)), i < c1, lane);
+            L.offer(tr_rank<ORD>(bits[u], uint32_t(i)), i < c1, lane);
         }
     }
     lists[warp][lane] = L.a;
@@ -158,7 +163,7 @@ __global__ void __launch_bounds__(kTrThreads) topk_rows_partial(const void* x, i
     }
 }
 
-template <bool BF16>
+template <bool BF16, int ORD>
 __global__ void __launch_bounds__(kTrThreads) topk_rows_final(const void* x, int64_t N, int slices, int k,
                                                               const uint64_t* ws, float* values, int64_t* indices) {
     __shared__ uint64_t lists[kTrWarps][kTrK];
@@ -196,7 +201,7 @@ __global__ void __launch_bounds__(kTrThreads) topk_rows_final(const void* x, int
         for (int h = 0; h < 2; ++h) {
             const int o = lane + 32 * h;
             if (o < k) {
-                const uint32_t i = tr_index(h ? L.b : L.a);
+                const uint32_t i = tr_index<ORD>(h ? L.b : L.a);
                 indices[size_t(row) * k + o] = int64_t(i);
                 values[size_t(row) * k + o] = __uint_as_float(tr_bits_at<BF16>(x, size_t(row) * N + i));
             }
@@ -211,6 +216,17 @@ static int topk_rows_slices(int64_t rows, int64_t N) {
     return s;
 }
 
+template <bool BF16, int ORD>
+int launch_topk_rows(const void* x, int64_t rows, int64_t N, int64_t k, float* values, int64_t* indices,
+                            uint64_t* ws, cudaStream_t s) {
+    const int slices = topk_rows_slices(rows, N);
+    topk_rows_partial<BF16, ORD><<<dim3(slices, unsigned(rows)), kTrThreads, 0, s>>>(x, N, slices, ws);
+    CUDA_TRY(cudaGetLastError());
+    topk_rows_final<BF16, ORD><<<unsigned(rows), kTrThreads, 0, s>>>(x, N, slices, int(k), ws, values, indices);
+    CUDA_TRY(cudaGetLastError());
+    return MONO_OK;
+}
+
 }  // namespace mono
 
 using namespace mono;
@@ -222,27 +238,22 @@ size_t mono_topk_rows_workspace(int64_t rows, int64_t N) {
     return size_t(rows) * topk_rows_slices(rows, N) * kTrK * sizeof(uint64_t);
 }
 
-int mono_topk_rows(const void* x, int bf16, int64_t rows, int64_t N, int64_t k, float* values, int64_t* indices,
+int mono_topk_rows(const void* x, int flags, int64_t rows, int64_t N, int64_t k, float* values, int64_t* indices,
                    void* workspace, size_t workspace_bytes, mono_stream_t stream) {
     MONO_CHECK(x && values && indices && workspace, "null operand");
     MONO_CHECK(rows >= 1 && rows <= kTrMaxRows, "1 <= rows <= %d", kTrMaxRows);
     MONO_CHECK(k >= 1 && k <= kTrK && N >= kTrK && N < (int64_t(1) << 31), "1 <= k <= 64, 64 <= N < 2^31");
     MONO_CHECK(workspace_bytes >= mono_topk_rows_workspace(rows, N) && aligned(workspace, 8),
                "workspace (mono_topk_rows_workspace)");
-    const int slices = topk_rows_slices(rows, N);
+    MONO_CHECK((flags & ~(MONO_TOPK_BF16 | MONO_TOPK_INDEX_ORDER)) == 0, "flags: MONO_TOPK_BF16 | MONO_TOPK_INDEX_ORDER");
     const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     uint64_t* ws = static_cast<uint64_t*>(workspace);
-    if (bf16) {
-        topk_rows_partial<true><<<dim3(slices, unsigned(rows)), kTrThreads, 0, s>>>(x, N, slices, ws);
-        CUDA_TRY(cudaGetLastError());
-        topk_rows_final<true><<<unsigned(rows), kTrThreads, 0, s>>>(x, N, slices, int(k), ws, values, indices);
-    } else {
-        topk_rows_partial<false><<<dim3(slices, unsigned(rows)), kTrThreads, 0, s>>>(x, N, slices, ws);
-        CUDA_TRY(cudaGetLastError());
-        topk_rows_final<false><<<unsigned(rows), kTrThreads, 0, s>>>(x, N, slices, int(k), ws, values, indices);
+    switch (flags) {
+        case 0: return launch_topk_rows<false, 0>(x, rows, N, k, values, indices, ws, s);
+        case MONO_TOPK_BF16: return launch_topk_rows<true, 0>(x, rows, N, k, values, indices, ws, s);
+        case MONO_TOPK_INDEX_ORDER: return launch_topk_rows<false, 1>(x, rows, N, k, values, indices, ws, s);
+        default: return launch_topk_rows<true, 1>(x, rows, N, k, values, indices, ws, s);
     }
-    CUDA_TRY(cudaGetLastError());
-    return MONO_OK;
 }
 
 }  // extern "C"

@@ -19,8 +19,9 @@ _tables_lock = threading.Lock()
 
 
 def _check(cond, msg):
+    """An argument check of the binding: raises the C ABI's argument rejection (MonoError, MONO_EINVAL)."""
     if not cond:
-        raise RuntimeError(msg)
+        raise _lib.MonoError("argument", _lib.MONO_EINVAL, msg)
 
 
 def _cuda(*ts):
@@ -273,6 +274,7 @@ def qk_norm_rope_kv(rawq, rawk, vn, weightq, weightk, freqs, key, value, positio
     S, Hq, Hk = rawq.size(1), rawq.size(2), rawk.size(2)
     _check(rawk.dim() == 4 and rawk.shape == vn.shape and rawk.size(1) == S and rawk.stride(3) == 1 and
            rawk.stride(2) == 256 and vn.stride(3) == 1 and vn.stride(2) == 256, "K/V: bf16 [1, S, Hk, 256], dense heads")
+    _check(all(t.dtype == torch.bfloat16 for t in (rawk, vn, key, value, weightq, weightk)), "bf16 K/V, caches, weights")
     _check(key.is_contiguous() and value.is_contiguous() and key.shape == value.shape and key.dim() == 4 and
            key.size(1) == Hk and key.size(3) == 256, "K/V cache: bf16 [1, Hk, cap, 256]")
     _check(freqs.dtype == torch.float32 and freqs.is_contiguous() and freqs.numel() == S * (rd // 2) * 4,
@@ -704,10 +706,11 @@ def gemv_bf16(x, w, out=None):
 _topk_rows_ws = {}
 
 
-def topk_rows(x, k):
+def topk_rows(x, k, index_order=False):
     """Exact top-k (k <= 64) of a few long rows (the reference's _C.topk_rows, csrc/topk_rows.sycl): x fp32 or
-    bf16 [R, N] (R <= 16) -> (values fp32 [R, k], indices int64 [R, k]) = torch.topk(x.float(), k) in the
-    torch-XPU tie order (include/mono_b200.h mono_topk_rows)."""
+    bf16 [R, N] (R <= 16) -> (values fp32 [R, k], indices int64 [R, k]) = torch.topk(x.float(), k); equal values in
+    the torch-XPU order, or with index_order by ascending index, torch's CUDA order for k >= 33 and k = 1
+    (include/mono_b200.h mono_topk_rows)."""
     _cuda(x)
     _check(x.dim() == 2 and x.is_contiguous() and x.dtype in (torch.float32, torch.bfloat16), "x fp32 / bf16 [R, N]")
     R, N = x.shape
@@ -715,7 +718,8 @@ def topk_rows(x, k):
     indices = torch.empty((R, int(k)), dtype=torch.int64, device=x.device)
     nbytes = _lib.load().mono_topk_rows_workspace(R, N)
     ws = _workspace(_topk_rows_ws, (x.device, R, N), nbytes, x.device)
+    flags = (_lib.TOPK_BF16 if x.dtype == torch.bfloat16 else 0) | (_lib.TOPK_INDEX_ORDER if index_order else 0)
     with torch.cuda.device(x.device):
-        _lib.call("mono_topk_rows", _p(x), int(x.dtype == torch.bfloat16), R, N, int(k), _p(values), _p(indices), _p(ws),
-                  nbytes, _stream(x.device))
+        _lib.call("mono_topk_rows", _p(x), flags, R, N, int(k), _p(values), _p(indices), _p(ws), nbytes,
+                  _stream(x.device))
     return values, indices

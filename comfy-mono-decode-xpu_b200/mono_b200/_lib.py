@@ -7,6 +7,7 @@ from __future__ import annotations
 
 import ctypes
 import os
+import re
 import threading
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -82,17 +83,31 @@ OUT_F32, OUT_BF16 = 0, 2
 FMT_GPTQ, FMT_REF = 0, 1
 LAYOUT_ROW, LAYOUT_TILED = 0, 1
 SCALE_FP8, SCALE_F32 = 0, 1
+TOPK_BF16, TOPK_INDEX_ORDER = 1, 2
 
 _lock = threading.Lock()
 _lib = None
 
 
 class MonoError(RuntimeError):
-    """A C-ABI call returned a non-zero status (message from mono_last_error())."""
+    """A C-ABI call returned a non-zero status (message from mono_last_error()), or the Python binding refused an
+    argument before the call (status MONO_EINVAL, like the C-side checks)."""
 
     def __init__(self, name, status, message):
         super().__init__(f"{name}: status {status}: {message}")
         self.status = status
+        self.message = message
+
+    @property
+    def reason(self):
+        """The message without its "(got ...)" detail: one key per kind of rejection."""
+        return re.sub(r"\s*\(got [^)]*\)", "", self.message).strip()
+
+
+def rejected(exc) -> bool:
+    """True when `exc` is an argument rejection (status MONO_EINVAL): the call lies outside what the kernels
+    accept and nothing was launched; any other exception is a failure."""
+    return isinstance(exc, MonoError) and exc.status == MONO_EINVAL
 
 
 def load():

@@ -1,9 +1,11 @@
 """Failure handling shared by every fast path (the role of comfy_mono_decode_xpu/guard.py).
 
-A fast path that raises (an argument check of the C ABI, a CUDA error at launch, an out-of-memory) is logged
-once with its traceback and switched off for the rest of the process; the call that hit the error runs the
-original code instead. Callers fall back only while no state has been modified; otherwise they re-raise after
-switching the path off. A user interrupt (ComfyUI's InterruptProcessingException) is not a failure.
+Two kinds of refusal reach a fast path. An argument rejection (mono_b200._lib.rejected: the binding or the C ABI
+found the call outside what the kernels take, before anything was launched) sends that one call to the original
+code. A failure (a CUDA error at launch, an out-of-memory, any other exception) is logged once with its traceback
+and switches the path off for the rest of the process; the call that hit it runs the original code instead.
+Callers fall back only while no state has been modified; otherwise they re-raise after switching the path off.
+A user interrupt (ComfyUI's InterruptProcessingException) is neither: it propagates.
 """
 from __future__ import annotations
 
@@ -48,3 +50,25 @@ def reset():
     """Re-enable every path (tests)."""
     with _lock:
         _off.clear()
+
+
+def route(piece: str, kernel, original, refused=None):
+    """kernel() when `piece` is on and the kernel takes the call, else original(); both are zero-argument calls
+    that compute the same pure function of the call's inputs. refused(reason), when given, hears why a call ran
+    the original: "off", the rejection's reason (the ABI's message), or "failed"."""
+    if piece in _off:
+        if refused:
+            refused("off")
+        return original()
+    try:
+        return kernel()
+    except Exception as e:
+        from . import _lib
+        if _lib.rejected(e):
+            reason = e.reason
+        else:
+            failed(piece, e)
+            reason = "failed"
+    if refused:
+        refused(reason)
+    return original()

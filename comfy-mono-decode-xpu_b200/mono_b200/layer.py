@@ -35,6 +35,10 @@ class SubpathError(RuntimeError):
     """A fused sub-route failed after writing state; it is switched off and the block is not replayed."""
 
 
+class Ineligible(RuntimeError):
+    """A fused route cannot serve this call; raised before anything was written (the caller runs the original)."""
+
+
 def stats():
     with _lock:
         return dict(_stats)
@@ -88,18 +92,38 @@ def _install_attend(llama=None):
     return True
 
 
-def _norm_rope_eligible(mix, rawq, rawk, xv4, freqs, kv):
-    return (_rope and not guard.off("norm_rope") and not torch.is_grad_enabled() and rawq.device.type == "cuda"
-            and rawq.dtype == torch.bfloat16 and rawq.shape[0] == 1 and rawq.shape[-1] == 256
-            and 1 <= rawq.shape[1] <= 8 and rawk.is_contiguous() and freqs is not None
-            and getattr(kv, "position", None) is not None and kv.position.dtype == torch.int64
-            and kv.key.is_contiguous() and kv.value.is_contiguous() and mix.rotary_dim % 2 == 0)
+def attention_core(mix, qg, xk, xv, freqs_cis, kv):
+    """The attention core of a GatedAttention decode call after its projections: Q/K RMSNorm + partial RoPE + K/V
+    cache write in one launch (mono_qk_norm_rope_kv), then kv.attend (the attend route). qg [1, S, heads * 2 *
+    head_dim] (query | gate per head), xk / xv [1, S, kv_heads * head_dim]. Returns the attention rows
+    [1, S, heads * head_dim] (before the gate). Raises Ineligible before any write when the call is not one the
+    kernels serve; a failure after the write switches the piece off and raises SubpathError."""
+    from . import _C
+    B, S = qg.shape[0], qg.shape[1]
+    qgv = qg.view(B, S, mix.num_heads, mix.head_dim * 2)
+    rawq = qgv[..., :mix.head_dim]
+    rawk = xk.view(B, S, mix.num_kv_heads, mix.head_dim)
+    xv4 = xv.view(B, S, mix.num_kv_heads, mix.head_dim)
+    if (not _rope or guard.off("norm_rope") or torch.is_grad_enabled() or freqs_cis is None
+            or getattr(kv, "position", None) is None or mix.rotary_dim % 2):
+        raise Ineligible("norm_rope")
+    try:
+        f = freqs_cis.reshape(S, mix.rotary_dim // 2, 2, 2).float().contiguous()
+        q, k = _C.qk_norm_rope_kv(rawq, rawk, xv4, mix.q_norm.weight, mix.k_norm.weight, f, kv.key, kv.value,
+                                  kv.position[:S], mix.q_norm.eps, mix.k_norm.eps, mix.rotary_dim)
+    except Exception as e:
+        from . import _lib
+        if _lib.rejected(e):  # the binding refused the operands before the launch: nothing was written
+            raise Ineligible("norm_rope: " + e.reason) from e
+        guard.failed("norm_rope", e, can_fallback=False)  # the KV cache may be written: no replay
+        raise SubpathError("norm_rope") from e
+    _count("norm_rope")
+    return kv.attend(q, k, xv4.transpose(1, 2))
 
 
 def _install_gated_attention(q35=None):
     if q35 is None:
         from comfy.text_encoders import qwen35 as q35
-    from . import _C
     cls = q35.GatedAttention
     original = cls.forward
     if _claimed(original):
@@ -111,23 +135,11 @@ def _install_gated_attention(q35=None):
             return original(self, x, attention_mask, freqs_cis, optimized_attention, past_key_value)
         B, S = x.shape[0], x.shape[1]
         qg, xk, xv = self.q_proj(x), self.k_proj(x), self.v_proj(x)
-        qgv = qg.view(B, S, self.num_heads, self.head_dim * 2)
-        rawq = qgv[..., :self.head_dim]
-        rawk = xk.view(B, S, self.num_kv_heads, self.head_dim)
-        xv4 = xv.view(B, S, self.num_kv_heads, self.head_dim)
-        gate = qgv[..., self.head_dim:].reshape(B, S, -1)
-        kv = past_key_value
-        if not _norm_rope_eligible(self, rawq, rawk, xv4, freqs_cis, kv):
-            return original(self, x, attention_mask, freqs_cis, optimized_attention, past_key_value)
         try:
-            f = freqs_cis.reshape(S, self.rotary_dim // 2, 2, 2).float().contiguous()
-            q, k = _C.qk_norm_rope_kv(rawq, rawk, xv4, self.q_norm.weight, self.k_norm.weight, f, kv.key, kv.value,
-                                      kv.position[:S], self.q_norm.eps, self.k_norm.eps, self.rotary_dim)
-        except Exception as e:  # the KV cache may be written: no replay
-            guard.failed("norm_rope", e, can_fallback=False)
-            raise SubpathError("norm_rope") from e
-        _count("norm_rope")
-        out = kv.attend(q, k, xv4.transpose(1, 2))
+            out = attention_core(self, qg, xk, xv, freqs_cis, past_key_value)
+        except Ineligible:
+            return original(self, x, attention_mask, freqs_cis, optimized_attention, past_key_value)
+        gate = qg.view(B, S, self.num_heads, self.head_dim * 2)[..., self.head_dim:].reshape(B, S, -1)
         out = out * gate.sigmoid()
         return self.o_proj(out), past_key_value
 
@@ -162,10 +174,14 @@ def _install_norm_scale(llama=None):
     return True
 
 
-def _block_plan(block):
-    """The tile-major GPTQ weights of a block, or None (any other format runs the original forward)."""
+def _block_plan(block, x):
+    """The block's decode plan: one attached as ``mono_b200_w4`` (a dict with "run"), else the generate session's
+    (bridge.block_plan), else None (the original forward)."""
     w = getattr(block, "mono_b200_w4", None)
-    return w if isinstance(w, dict) else None
+    if isinstance(w, dict):
+        return w
+    from . import bridge
+    return bridge.block_plan(block, x.device) if x.device.type == "cuda" else None
 
 
 def install(q35=None, llama=None):
@@ -186,15 +202,19 @@ def install(q35=None, llama=None):
 
     def forward(self, x, attention_mask=None, freqs_cis=None, optimized_attention=None, past_key_value=None):
         S = x.shape[1] if x.dim() == 3 else 0
-        plan = _block_plan(self)
-        if (guard.off("layer") or plan is None or past_key_value is None or x.device.type != "cuda"
-                or x.dtype != torch.bfloat16 or x.shape[0] != 1 or not 1 <= S <= 8 or not x.is_contiguous()):
-            if plan is None:
-                _count("fallback_weights")
+        if (guard.off("layer") or past_key_value is None or x.device.type != "cuda" or x.dtype != torch.bfloat16
+                or x.shape[0] != 1 or not 1 <= S <= 8 or not x.is_contiguous() or attention_mask is not None):
+            return original(self, x, attention_mask, freqs_cis, optimized_attention, past_key_value)
+        plan = _block_plan(self, x)
+        if plan is None:
+            _count("fallback_weights")
             return original(self, x, attention_mask, freqs_cis, optimized_attention, past_key_value)
         state = {"mutated": False}
         try:
             out = plan["run"](self, x, attention_mask, freqs_cis, past_key_value, state)
+        except Ineligible:  # nothing was written
+            _count("fallback_call")
+            return original(self, x, attention_mask, freqs_cis, optimized_attention, past_key_value)
         except SubpathError:
             raise
         except Exception as e:

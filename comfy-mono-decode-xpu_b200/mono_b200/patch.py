@@ -1,17 +1,24 @@
-"""Route small-M packed W4A8 linears and the decode-row rotate + quantize step to the B200 kernels (the install
-points of comfy_mono_decode_xpu/patch.py:68-96 and :122-137).
+"""Route the Kitchen INT8 backend's packed W4A8 linears and its rotate + quantize row step to this build's kernels
+(the install points of comfy_mono_decode_xpu/patch.py:68-96 and :122-137).
 
-install() wraps ``omni_xpu_kernel.int8.w4a8_linear_prequantized`` (the entry the Kitchen backend looks up on
-every call): a call that matches the kernel contract (CUDA tensors, 1-16 rows, K a multiple of 1024 up to 16384,
-G16 FP8 relative scales, no bias, bf16 / fp32 output, aligned contiguous operands) runs mono_w4a8_decode_linear,
-bit-identical to the original chain; every other call runs the original. install_prep() wraps
-``quantize_and_rotate_rowwise`` of the loaded ``*.w4a8_int8`` backend modules the same way (rot_quant).
-Both are idempotent (the CLAIM attribute, the original kept as __wrapped__) and switched by the reference's
-environment variables (MONO_DECODE_XPU_STATS: a JSON file of the counters written at exit).
+install() replaces ``omni_xpu_kernel.int8.w4a8_linear_prequantized`` (the backend looks it up on every call) and
+install_prep() replaces ``quantize_and_rotate_rowwise`` in each loaded ``*.w4a8_int8`` backend module. A replaced
+entry hands its call to the mono_b200 binding, and the binding and the C ABI decide whether the kernel takes it
+(mono_w4a8_decode_linear: 1-16 rows, K a multiple of 1024 up to 16384, N a multiple of 16, G16 FP8 relative scales,
+16-byte aligned operands, one CUDA device; mono_rot_quant: bf16 rows, K a multiple of 256, a 256 x 256 bf16
+rotation). A refused call runs the original and is counted under the ABI's reason; a failure switches the piece off
+(guard.route). Decided here are only what the C ABI has no parameter for: a bias, an output dtype other than bf16 /
+fp32, stochastic rounding, a rotation group other than 256, and torch.compile tracing.
+
+Both entries are pure functions of their inputs, so the original recomputes exactly what a refused call would
+have returned; the kernels' results are bit-identical to the original chain's. Replacements are idempotent (the
+CLAIM attribute; the original is kept as __wrapped__). MONO_DECODE_XPU_STATS names a JSON file the counters are
+written to at exit.
 """
 from __future__ import annotations
 
 import atexit
+import collections
 import json
 import os
 import sys
@@ -19,63 +26,60 @@ import threading
 
 import torch
 
-from . import guard
+from . import _lib, guard
 
 CLAIM = "__comfy_mono_decode_b200__"
-_stats = {"fused": 0, "fallback": 0, "reasons": {}}
+_OUT_CODES = {torch.bfloat16: _lib.OUT_BF16, torch.float32: _lib.OUT_F32}
+_ROTATION = 256  # the rotation block the kernel applies (K is rotated in 256-wide groups)
+
 _lock = threading.Lock()
+_served = collections.Counter()  # piece -> calls run by the kernels
+_refused = collections.Counter()  # reason -> calls run by the original
+_stats_file = []
 
 
 def stats():
+    """{"fused": linear calls served, "prep": rotate + quantize calls served, "fallback": calls sent to the
+    original, "reasons": {reason: count}}."""
     with _lock:
-        return dict(_stats, reasons=dict(_stats["reasons"]))
+        return {"fused": _served["w4"], "prep": _served["prep"], "fallback": sum(_refused.values()),
+                "reasons": dict(_refused)}
 
 
-def _reason(r):
+def _refuse(reason):
     with _lock:
-        _stats["fallback"] += 1
-        _stats["reasons"][r] = _stats["reasons"].get(r, 0) + 1
+        _refused[reason] += 1
+
+
+def _serve(piece, kernel, original):
+    def counted():
+        out = kernel()
+        with _lock:
+            _served[piece] += 1
+        return out
+    return guard.route(piece, counted, original, _refuse)
 
 
 def claimed(fn) -> bool:
     return getattr(fn, CLAIM, False) or getattr(fn, "__comfy_mono_decode_xpu__", False)
 
 
-def contract(x, x_scale, packed, s_rel, s_channel, codebook, bias, group_size, out_dtype):
-    """None when the call fits mono_w4a8_decode_linear, else the reason (the reference's _contract, with this
-    build's limits)."""
-    if bias is not None:
-        return "bias"
-    if out_dtype not in (torch.bfloat16, torch.float32):
-        return "out_dtype"
-    if x.device.type != "cuda" or x.dtype != torch.int8 or not x.is_contiguous():
-        return "x"
-    k = x.shape[-1]
-    rows = x.numel() // k if k else 0
-    if not 1 <= rows <= 16:
-        return "rows"
-    if k % 1024 or k > 16384 or group_size != 16:
-        return "shape"
-    if packed.dtype not in (torch.int8, torch.uint8) or packed.dim() != 2 or not packed.is_contiguous() \
-            or packed.shape[1] * 2 != k or packed.shape[0] % 16:
-        return "packed"
-    if packed.data_ptr() % 16 or x.data_ptr() % 16:
-        return "align"
-    if s_rel.dtype != torch.float8_e4m3fn or not s_rel.is_contiguous():
-        return "s_rel"
-    if s_channel.numel() != packed.shape[0]:
-        return "s_channel"
-    if codebook is not None and (codebook.dtype != torch.float32 or codebook.numel() != 16):
-        return "codebook"
-    devs = {t.device for t in (x, x_scale, packed, s_rel, s_channel) + ((codebook,) if codebook is not None else ())}
-    if len(devs) != 1 or x_scale.numel() != rows:
-        return "operands"
-    return None
+def _claim(wrapper, original):
+    setattr(wrapper, CLAIM, True)
+    wrapper.__wrapped__ = original
+    return wrapper
+
+
+def _write_stats_at_exit():
+    path = os.environ.get("MONO_DECODE_XPU_STATS")
+    if path and not _stats_file:
+        _stats_file.append(path)
+        atexit.register(lambda: json.dump(stats(), open(path, "w")))
 
 
 def install(module=None):
-    """Wrap omni_xpu_kernel.int8.w4a8_linear_prequantized (or `module`'s, for tests). False if already wrapped
-    or the module is missing."""
+    """Replace omni_xpu_kernel.int8.w4a8_linear_prequantized (or `module`'s, for tests). False when it is already
+    replaced or the module is missing."""
     if module is None:
         try:
             from omni_xpu_kernel import int8 as module
@@ -88,64 +92,56 @@ def install(module=None):
 
     def w4a8_linear_prequantized(x_int8, x_scale, packed, relative_scale, channel_scale, codebook=None, bias=None,
                                  group_size=16, out_dtype=torch.bfloat16):
-        if guard.off("w4") or torch.compiler.is_compiling():
-            return original(x_int8, x_scale, packed, relative_scale, channel_scale, codebook, bias, group_size, out_dtype)
-        why = contract(x_int8, x_scale, packed, relative_scale, channel_scale, codebook, bias, group_size, out_dtype)
-        if why is not None:
-            _reason(why)
-            return original(x_int8, x_scale, packed, relative_scale, channel_scale, codebook, bias, group_size, out_dtype)
-        k = x_int8.shape[-1]
-        try:
-            out = _C.w4a8_decode_linear(x_int8.reshape(-1, k), x_scale.reshape(-1).to(torch.float32).contiguous(), packed,
-                                        relative_scale, channel_scale.reshape(-1).to(torch.float32).contiguous(), codebook,
-                                        None, group_size, 0 if out_dtype == torch.float32 else 2, 0, False)
-        except Exception as e:  # a pure function of its inputs: the original recomputes it
-            guard.failed("w4", e)
-            return original(x_int8, x_scale, packed, relative_scale, channel_scale, codebook, bias, group_size, out_dtype)
-        with _lock:
-            _stats["fused"] += 1
-        return out.reshape(*x_int8.shape[:-1], packed.shape[0])
+        def stock():
+            return original(x_int8, x_scale, packed, relative_scale, channel_scale, codebook, bias, group_size,
+                            out_dtype)
 
-    setattr(w4a8_linear_prequantized, CLAIM, True)
-    w4a8_linear_prequantized.__wrapped__ = original
-    module.w4a8_linear_prequantized = w4a8_linear_prequantized
-    output = os.environ.get("MONO_DECODE_XPU_STATS")
-    if output:
-        atexit.register(lambda: json.dump(stats(), open(output, "w")))
+        if torch.compiler.is_compiling():
+            return stock()
+        if bias is not None or out_dtype not in _OUT_CODES:
+            _refuse("bias" if bias is not None else "out_dtype")
+            return stock()
+
+        def kernel():
+            k = x_int8.shape[-1]
+            y = _C.w4a8_decode_linear(x_int8.reshape(-1, k), x_scale.reshape(-1).float(), packed, relative_scale,
+                                      channel_scale.reshape(-1).float(), codebook, None, group_size,
+                                      _OUT_CODES[out_dtype])
+            return y.reshape(*x_int8.shape[:-1], y.shape[-1])
+
+        return _serve("w4", kernel, stock)
+
+    module.w4a8_linear_prequantized = _claim(w4a8_linear_prequantized, original)
+    _write_stats_at_exit()
     return True
 
 
 def install_prep(modules=None):
-    """Wrap quantize_and_rotate_rowwise of every loaded ``*.w4a8_int8`` backend module (or `modules`). Returns the
-    number wrapped."""
+    """Replace quantize_and_rotate_rowwise in every loaded ``*.w4a8_int8`` backend module (or in `modules`).
+    Returns how many were replaced."""
+    if modules is None:
+        modules = [m for n, m in list(sys.modules.items())
+                   if n.endswith(".w4a8_int8") and hasattr(m, "quantize_and_rotate_rowwise")]
     from . import _C
-    targets = modules if modules is not None else [
-        m for n, m in list(sys.modules.items()) if n.endswith(".w4a8_int8") and hasattr(m, "quantize_and_rotate_rowwise")]
     done = 0
-    for mod in targets:
+    for mod in modules:
         original = mod.quantize_and_rotate_rowwise
         if claimed(original):
             continue
 
         def quantize_and_rotate_rowwise(x, h, group_size, stochastic_rounding=0, _original=original):
-            k = x.shape[-1] if x.dim() else 0
-            ok = (not guard.off("prep") and group_size == 256 and not stochastic_rounding and x.device.type == "cuda"
-                  and x.dtype == torch.bfloat16 and h.dtype == torch.bfloat16 and h.numel() == 65536 and k
-                  and k % 256 == 0 and 1 <= x.numel() // k <= 256)
-            if not ok:
-                _reason("prep")
+            def stock():
                 return _original(x, h, group_size, stochastic_rounding)
-            try:
-                out = _C.rot_quant(x.reshape(-1, k).contiguous(), h.contiguous(), 3)
-            except Exception as e:
-                guard.failed("prep", e)
-                return _original(x, h, group_size, stochastic_rounding)
-            with _lock:
-                _stats["prep"] = _stats.get("prep", 0) + 1
-            return out
 
-        setattr(quantize_and_rotate_rowwise, CLAIM, True)
-        quantize_and_rotate_rowwise.__wrapped__ = original
-        mod.quantize_and_rotate_rowwise = quantize_and_rotate_rowwise
+            if torch.compiler.is_compiling():
+                return stock()
+            if group_size != _ROTATION or stochastic_rounding:
+                _refuse("group_size" if group_size != _ROTATION else "stochastic_rounding")
+                return stock()
+            return _serve("prep", lambda: _C.rot_quant(x.contiguous(), h.contiguous()), stock)
+
+        mod.quantize_and_rotate_rowwise = _claim(quantize_and_rotate_rowwise, original)
         done += 1
+    if done:
+        _write_stats_at_exit()
     return done

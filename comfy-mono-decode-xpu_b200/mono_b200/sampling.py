@@ -1,164 +1,141 @@
-"""Exact fast top-k for the verify step's sampling filter (the reference's comfy_mono_decode_xpu/sampling.py,
-switch MONO_DECODE_XPU_SAMPLE_TOPK), on CUDA tensors through mono_topk_rows.
+"""One-launch exact top-k for the verify step's sampling filter on CUDA (the role of
+comfy_mono_decode_xpu/sampling.py; switch MONO_DECODE_XPU_SAMPLE_TOPK: "1" on (default), "0" off, "check": both
+run, torch's answer is returned and disagreements are counted).
 
-ComfyUI's sampling filters start with torch.topk(logits, top_k) over the verify rows (a few rows of ~248k fp32
-logits). Inside the verify sampling's context this module answers that call with _C.topk_rows, which returns
-the same values and indices in the same order as torch's top-k, ties included (include/mono_b200.h
-mono_topk_rows). Every other sampling op (temperature, min-p, top-p, softmax, multinomial) stays upstream's.
+Upstream's sampling (ComfyUI's sample_token / processed_probs) starts its top-k filter with torch.topk(rows,
+top_k) over the verify rows: up to 16 rows of the ~248k-entry vocabulary. Inside the context that topk_mode /
+verify_rows return, every torch.topk / Tensor.topk call is bound to torch.topk's own signature; a call that asks
+for the k largest, sorted, along the last dimension, without out=, of a CUDA tensor is handed to C.topk_rows over
+its rows (leading dimensions flattened). Whether the kernel answers is decided by the binding and the C ABI (row
+count, row length, k, dtype: include/mono_b200.h mono_topk_rows): an argument rejection (_lib.rejected) runs
+torch's topk for that call only; any other exception switches the piece off (guard) and runs torch's topk. No
+other operation is intercepted: torch.sort, softmax, multinomial and the masked writes stay upstream's.
 
-verify_rows(C, lg0) hands the sampling the bf16 logits themselves as the stand-in for their fp32 copy: shape
-queries pass through, .dtype reads fp32, torch.topk reads the bf16 rows directly (bf16 -> fp32 is exact) and any
-other op gets the fp32 copy, made on first use. A later torch.sort(values, descending=True) of values this
-context returned gets a copy and the index arange: they are already sorted, ties in order, and a stable sort
-would return exactly that.
-
-MODE: "1" (default) on, "0" off, "check": both run, torch's result is returned and mismatches are counted.
+Values are torch's bit for bit (the same multiset, sorted descending; bf16 rows give bf16 values, which their fp32
+results convert to exactly). Equal values come out by ascending index (mono_topk_rows with MONO_TOPK_INDEX_ORDER):
+torch's own CUDA topk order for k >= 33 and for k = 1, as measured on B200 over tie-heavy rows, so those calls
+return torch's indices exactly. For 2 <= k <= 32 torch orders equal values by its small sorting network, which no
+fixed rule reproduces: there "check" mode can count a tie as a disagreement while the value sets agree. (The
+reference keeps its platform's torch-XPU order; that order is the kernel's other mode.)
 """
 from __future__ import annotations
 
+import collections
 import contextlib
+import inspect
+import operator
 import os
 import threading
 
 import torch
 
-from . import guard
+from . import _lib, guard
 
 MODE = os.environ.get("MONO_DECODE_XPU_SAMPLE_TOPK", "1")
-DEVICES = ("cuda",)  # device types served (the reference serves "xpu")
+DEVICES = ("cuda",)  # device types whose topk calls are offered to the kernel
+PIECE = "sample_topk"
+
+_counts = collections.Counter()
 _lock = threading.Lock()
-_stats = {"calls": 0, "checked": 0, "check_mismatch": 0, "skipped": 0, "sorted": 0, "lazy_rows": 0}
-_aranges = {}
+
+
+def _topk_parameters(input, k, dim=-1, largest=True, sorted=True, *, out=None):
+    """torch.topk's parameters; Tensor.topk binds self as `input`."""
+
+
+_SIGNATURE = inspect.signature(_topk_parameters)
+_TOPK = (torch.topk, torch.Tensor.topk)
 
 
 def stats():
+    """Counters: "calls" (answered by the kernel), "passed" (topk calls of another form), "rejected" and
+    "rejected: <reason>" (the ABI refused the arguments), "checked" / "check_mismatch" (check mode)."""
     with _lock:
-        return dict(_stats)
+        return dict(_counts)
 
 
-def _bump(key, n=1):
+def _count(*keys):
     with _lock:
-        _stats[key] = _stats.get(key, 0) + n
+        for key in keys:
+            _counts[key] += 1
 
 
-def _topk_request(args, kwargs, want_dtype):
-    """(x, k) when torch.topk(*args, **kwargs) is a call topk_rows answers exactly, else None: the last dim,
-    largest first, sorted, no out=, a plain contiguous 2-D tensor of want_dtype with 1..16 rows of at least
-    32768 elements, 1 <= k <= 64."""
-    if len(args) < 2 or kwargs.get("out") is not None:
+def _bind(args, kwargs):
+    try:
+        bound = _SIGNATURE.bind(*args, **kwargs)
+    except TypeError:
         return None
-    x, k = args[0], args[1]
-    dim = args[2] if len(args) > 2 else kwargs.get("dim", -1)
-    largest = args[3] if len(args) > 3 else kwargs.get("largest", True)
-    srt = args[4] if len(args) > 4 else kwargs.get("sorted", True)
-    if type(x) is not torch.Tensor or type(k) is not int or dim not in (-1, 1) or largest is not True or srt is not True:
+    bound.apply_defaults()
+    return bound.arguments
+
+
+def _request(a):
+    """(rows [R, N], k) when the bound call asks for the k largest along the last dim, sorted, into fresh tensors,
+    of a plain CUDA tensor; None otherwise (the kernel's own limits are not tested here)."""
+    x = a["input"]
+    if type(x) is not torch.Tensor or x.device.type not in DEVICES or x.dim() == 0:
         return None
-    if (x.device.type not in DEVICES or x.dtype != want_dtype or x.dim() != 2 or not x.is_contiguous()
-            or not 1 <= x.shape[0] <= 16 or x.shape[1] < 32768 or not 1 <= k <= 64):
+    if a["out"] is not None or a["largest"] is not True or a["sorted"] is not True:
         return None
-    return x, k
+    if isinstance(a["k"], bool) or isinstance(a["dim"], bool):
+        return None
+    try:
+        k, dim = operator.index(a["k"]), operator.index(a["dim"])
+    except TypeError:
+        return None
+    if dim not in (-1, x.dim() - 1):
+        return None
+    return x.reshape(-1, x.shape[-1]), k
 
 
-def _index_rows(R, k, device):
-    key = (R, k, str(device))
-    if key not in _aranges:
-        _aranges[key] = torch.arange(k, device=device).expand(R, k).contiguous()
-    return _aranges[key]
+class TopkServer(torch.overrides.TorchFunctionMode):
+    """Answers the eligible torch.topk calls made inside it with C.topk_rows (module docstring)."""
 
-
-_SHAPE_QUERIES = (torch.Tensor.size, torch.Tensor.dim, torch.Tensor.numel, torch.Tensor.is_contiguous,
-                  torch.Tensor.shape.__get__, torch.Tensor.ndim.__get__, torch.Tensor.device.__get__)
-_TOPK = (torch.topk, torch.Tensor.topk)
-_SORT = (torch.sort, torch.Tensor.sort)
-
-
-class TopkRowsMode(torch.overrides.TorchFunctionMode):
-    """Serves eligible torch.topk calls with C.topk_rows; `stand_in` (optional) is a bf16 [R, N] tensor that
-    stands for stand_in.float() inside the context."""
-
-    def __init__(self, C, stand_in=None):
+    def __init__(self, C):
         super().__init__()
         self.C = C
-        self.stand_in = stand_in
-        self.fp32 = None
-        self.returned = []  # value tensors returned by topk_rows (sorted descending)
-
-    def _dense(self, a):
-        if a is self.stand_in:
-            if self.fp32 is None:
-                self.fp32 = self.stand_in.float()  # torch functions run without this mode inside the handler
-            return self.fp32
-        if isinstance(a, (list, tuple)):
-            return type(a)(self._dense(v) for v in a)
-        return a
-
-    def _serve(self, x, k):
-        try:
-            v, i = self.C.topk_rows(x, k)
-        except Exception as e:  # an argument check: torch computes it
-            guard.failed("sample_topk", e)
-            return None
-        return v, i
 
     def __torch_function__(self, func, types, args=(), kwargs=None):
         kwargs = kwargs or {}
-        on_stand_in = self.stand_in is not None and len(args) > 0 and args[0] is self.stand_in
-        if on_stand_in:
-            if func in _SHAPE_QUERIES:
-                return func(*args, **kwargs)
-            if func is torch.Tensor.dtype.__get__:
-                return torch.float32
-            if func in _TOPK and MODE != "check" and not guard.off("sample_topk"):
-                req = _topk_request(args, kwargs, torch.bfloat16)
-                if req is not None:
-                    got = self._serve(*req)
-                    if got is not None:
-                        _bump("calls")
-                        _bump("lazy_rows")
-                        self.returned.append(got[0])
-                        return torch.return_types.topk(got)
-        if func in _SORT and len(args) > 0 and any(args[0] is v for v in self.returned):
-            dim = args[1] if len(args) > 1 else kwargs.get("dim", -1)
-            desc = args[2] if len(args) > 2 else kwargs.get("descending", False)
-            if len(args) <= 3 and set(kwargs) <= {"dim", "descending", "stable"} and dim in (-1, 1) and desc is True:
-                x = args[0]
-                _bump("sorted")
-                return torch.return_types.sort((x.clone(), _index_rows(x.shape[0], x.shape[1], x.device)))
-        if self.stand_in is not None:
-            args = self._dense(tuple(args))
-            kwargs = {key: self._dense(val) for key, val in kwargs.items()}
-        if func in _TOPK and not guard.off("sample_topk"):
-            req = _topk_request(args, kwargs, torch.float32)
-            if req is not None:
-                got = self._serve(*req)
-                if got is not None:
-                    if MODE != "check":
-                        _bump("calls")
-                        self.returned.append(got[0])
-                        return torch.return_types.topk(got)
-                    ref = func(*args, **kwargs)
-                    same = torch.equal(ref.indices, got[1]) and torch.equal(ref.values.view(torch.int32),
-                                                                            got[0].view(torch.int32))
-                    _bump("checked")
-                    _bump("check_mismatch", int(not same))
-                    return ref
-            _bump("skipped")
-        return func(*args, **kwargs)
+        if func not in _TOPK or guard.off(PIECE):
+            return func(*args, **kwargs)
+        a = _bind(args, kwargs)
+        req = None if a is None else _request(a)
+        if req is None:
+            _count("passed")
+            return func(*args, **kwargs)
+        rows, k = req
+        try:
+            values, indices = self.C.topk_rows(rows, k, index_order=True)
+        except Exception as e:
+            if _lib.rejected(e):
+                _count("rejected", "rejected: " + e.reason)
+            else:
+                guard.failed(PIECE, e)
+            return func(*args, **kwargs)
+        x = a["input"]
+        shape = (*x.shape[:-1], k)
+        got = torch.return_types.topk((values.to(x.dtype).reshape(shape), indices.reshape(shape)))
+        if MODE != "check":
+            _count("calls")
+            return got
+        ref = func(*args, **kwargs)
+        same = (torch.equal(ref.indices, got.indices) and ref.values.dtype == got.values.dtype
+                and torch.equal(ref.values.contiguous().view(torch.uint8), got.values.view(torch.uint8)))
+        _count("checked", *(() if same else ("check_mismatch",)))
+        return ref
 
 
 def topk_mode(C):
-    """The verify sampling's context: C.topk_rows serves its eligible torch.topk calls (a null context when the
-    mode is off or C has no topk_rows)."""
-    if MODE == "0" or guard.off("sample_topk") or not hasattr(C, "topk_rows"):
+    """The context in which C.topk_rows answers the sampling's top-k (a null context when the switch is "0", the
+    piece is off, or C has no topk_rows)."""
+    if MODE == "0" or guard.off(PIECE) or not hasattr(C, "topk_rows"):
         return contextlib.nullcontext()
-    return TopkRowsMode(C)
+    return TopkServer(C)
 
 
 def verify_rows(C, lg0):
-    """(context, rows) for sampling from the bf16 logits lg0 [R, N]: rows stands for lg0.float() — the bf16
-    tensor itself, served lazily inside the context, or (mode off / check, or lg0 not eligible) the fp32 copy."""
-    if (MODE in ("0", "check") or guard.off("sample_topk") or not hasattr(C, "topk_rows")
-            or lg0.dtype != torch.bfloat16 or lg0.dim() != 2 or not lg0.is_contiguous()
-            or lg0.device.type not in DEVICES):
-        return topk_mode(C), lg0.float()
-    return TopkRowsMode(C, stand_in=lg0), lg0
+    """(context, rows) for sampling from the verify logits lg0 [R, N]: rows is the fp32 tensor upstream's sampling
+    takes (lg0 itself when already fp32, else its fp32 copy: 6 bytes of traffic per logit, ~2 us for 8 x 248k on
+    this device, so no lazy stand-in is kept for it), context is topk_mode(C)."""
+    return topk_mode(C), (lg0 if lg0.dtype == torch.float32 else lg0.float())

@@ -328,13 +328,18 @@ MONO_API int mono_lmhead_pick(const void* x, int64_t x_stride, const void* w, in
 
 /* Exact top-k of a few long rows, k <= 64 (the reference's topk_rows, csrc/topk_rows.sycl:2-17: the verify
  * sampling's torch.topk(logits.float(), k)): per row the k largest by the radix key of the fp32 value (sign-flipped
- * bits: -0 below +0; rows holding NaN are not torch's order), sorted descending, ties in the torch-XPU gather
- * order, i.e. by the 64-bit rank key << 32 | (0xFFFFFFFF - g), g = (i >> 15) << 15 | ((i % 4096) >> 2) << 5 |
- * ((i % 32768) >> 12) << 2 | (i % 4) (csrc/topk_rows.sycl:34-42). x: fp32 (bf16 = 0) or bf16 (bf16 = 1)
- * [rows][N]; values fp32 [rows][k], indices int64 [rows][k]. 1 <= rows <= 16, 64 <= N < 2^31.
- * workspace: mono_topk_rows_workspace(rows, N) bytes. */
+ * bits: -0 below +0; rows holding NaN are not torch's order), sorted descending. Equal values come out in one of two
+ * orders, by the 64-bit rank key << 32 | (0xFFFFFFFF - g):
+ *   flags without MONO_TOPK_INDEX_ORDER: the reference platform's (torch-XPU) gather order, g = (i >> 15) << 15 |
+ *     ((i % 4096) >> 2) << 5 | ((i % 32768) >> 12) << 2 | (i % 4) (csrc/topk_rows.sycl:34-42);
+ *   MONO_TOPK_INDEX_ORDER: g = i, ascending index -- torch's CUDA topk order for k >= 33 and k = 1 (measured on
+ *     B200; for 2 <= k <= 32 torch's order among equal values is its sorting network's and not reproduced).
+ * x: fp32, or bf16 with MONO_TOPK_BF16 in flags, [rows][N]; values fp32 [rows][k], indices int64 [rows][k].
+ * 1 <= rows <= 16, 64 <= N < 2^31. workspace: mono_topk_rows_workspace(rows, N) bytes. */
+#define MONO_TOPK_BF16 1
+#define MONO_TOPK_INDEX_ORDER 2
 MONO_API size_t mono_topk_rows_workspace(int64_t rows, int64_t N);
-MONO_API int mono_topk_rows(const void* x, int bf16, int64_t rows, int64_t N, int64_t k, float* values, int64_t* indices,
+MONO_API int mono_topk_rows(const void* x, int flags, int64_t rows, int64_t N, int64_t k, float* values, int64_t* indices,
                             void* workspace, size_t workspace_bytes, mono_stream_t stream);
 
 /* ---- Layer programs: the reference's single-launch layers (layer_pre / layer_post, csrc/mono_layer.sycl:1-9;

@@ -47,29 +47,33 @@ def argmax(bits: np.ndarray) -> np.ndarray:
     return np.argmax(rank_argmax(bits), axis=-1).astype(np.int64)
 
 
-def topk_rows_rank(bits32, i):
-    """The reference's topk_rows rank (csrc/topk_rows.sycl:34-42) of fp32 bit patterns at indices i: the radix
-    key (sign-flipped bits) << 32 | ~g, g the torch-XPU gather key of index i."""
+def topk_rows_rank(bits32, i, index_order=False):
+    """The topk_rows rank of fp32 bit patterns at indices i: the radix key (sign-flipped bits) << 32 | ~g, g the
+    torch-XPU gather key of index i (the reference's, csrc/topk_rows.sycl:34-42), or with index_order g = i (equal
+    values by ascending index: torch's CUDA topk order for k >= 33 and k = 1, measured on B200)."""
     b = np.asarray(bits32, dtype=np.uint64)
     key = b ^ np.where(b & 0x80000000, np.uint64(0xFFFFFFFF), np.uint64(0x80000000))
     i = np.asarray(i, dtype=np.uint64)
-    off = i & np.uint64(32767)
-    g = ((i >> np.uint64(15)) << np.uint64(15)) | (((off & np.uint64(4095)) >> np.uint64(2)) << np.uint64(5)) | \
-        ((off >> np.uint64(12)) << np.uint64(2)) | (off & np.uint64(3))
+    if index_order:
+        g = i
+    else:
+        off = i & np.uint64(32767)
+        g = ((i >> np.uint64(15)) << np.uint64(15)) | (((off & np.uint64(4095)) >> np.uint64(2)) << np.uint64(5)) | \
+            ((off >> np.uint64(12)) << np.uint64(2)) | (off & np.uint64(3))
     return (key << np.uint64(32)) | (np.uint64(0xFFFFFFFF) - g)
 
 
-def topk_rows(x_f32, k):
-    """torch.topk(x, k) of fp32 rows [R, N] in the torch-XPU tie order, as the reference's topk_rows defines it
-    (csrc/topk_rows.sycl:7-10): the k largest 64-bit ranks per row, descending. Returns (values fp32 [R, k],
-    indices int64 [R, k])."""
+def topk_rows(x_f32, k, index_order=False):
+    """torch.topk(x, k) of fp32 rows [R, N] as the topk_rows kernel defines it: the k largest 64-bit ranks per row,
+    descending (equal values in the torch-XPU gather order of the reference's csrc/topk_rows.sycl:7-10, or by
+    ascending index with index_order). Returns (values fp32 [R, k], indices int64 [R, k])."""
     x = np.ascontiguousarray(x_f32, dtype=np.float32)
     R, N = x.shape
     bits = x.view(np.uint32)
     idx = np.arange(N, dtype=np.uint64)
     vals, inds = [], []
     for r in range(R):
-        rank = topk_rows_rank(bits[r], idx)
+        rank = topk_rows_rank(bits[r], idx, index_order)
         top = np.argsort(rank)[::-1][:k]
         inds.append(top.astype(np.int64))
         vals.append(x[r, top])
