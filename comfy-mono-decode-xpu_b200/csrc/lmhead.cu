@@ -1,34 +1,47 @@
 // bf16 lm_head with the greedy / draft pick fused (the role of the reference's verify logits + argmax, and of its
 // draft pick, csrc/draft_lmhead.sycl:87-292): for M <= 8 rows of x [M][K] against W [V][K] (bf16, far larger than
-// L2), logits = bf16(x W^T) in the bf16 GEMV's pinned order (gemv_bf16.cu: lane l accumulates its 16-byte pieces
-// l, l + 32, ... with fmaf, element by element, then the xor butterfly 16, 8, 4, 2, 1; bf16 x bf16 products are
-// exact in fp32, so the oracle reproduces every bit), and per row the argmax (argmax rank: smallest index on ties)
-// and the top-k (k <= 8, top-k rank), without writing the logits (optional).
+// L2), logits = bf16(x W^T) on the tensor cores, and per row the argmax (argmax rank: smallest index on ties) and
+// the top-k (k <= 8, top-k rank), without writing the logits (optional).
 //
-// Work: a persistent grid; warp w of CTA b takes column groups of NC columns g = b * 8 + w, + G * 8, ... (NC > 1
-// at several rows: one load of each x piece serves NC columns; the per-column arithmetic is unchanged; two rows
-// share each paired fma, __ffma2_rn, whose halves round exactly as fmaf). Lane m < M
-// keeps row m's running top-k list and argmax in registers. At the end the CTA merges its warps' lists in shared
-// memory and writes them to the workspace; the last CTA to finish (an arrival counter) merges the CTAs' lists -
-// ranks are distinct, so the merge order does not matter - and writes the indices. The pick form then scatters the
-// draft's tokens into the verify-token row: dst[children[0]] = argmax, dst[children[j]] = top-k[j] (j >= 1), the
-// reference's draft pick (csrc/draft_lmhead.sycl:4-17).
+// Work: a persistent grid of one CTA per SM, 8 warps each; warp j of CTA b takes the tiles of 8 vocabulary rows
+// b * 8 + j, + G * 8, ... For each tile it streams the rows in chunks of 512 k: lanes 0..7 each copy one row's 1 KB
+// (a bulk copy, evict-first, completion on the stage's mbarrier) into the warp's own ring of S stages (rows 16-byte
+// skewed: conflict-free ldmatrix), so every request is a contiguous kilobyte and the ring keeps S chunks per warp
+// in flight. The MMA is m16n8k16 with A = the x rows (rows 8..15 zero) and B = the 8 weight rows, both read with
+// ldmatrix; two accumulators take alternate k-steps of the tile and are added at its end (one fixed partition and
+// order: the same bits on every launch), then rounded once to bf16.
+//
+// Pick: thread (g, t) of a warp holds row g's logits at columns 2t, 2t + 1 of each tile and keeps that row's running
+// top-k list and argmax in registers; at the end the CTA merges its 32 lists per row and writes them to the
+// workspace; the last CTA to finish (an arrival counter) merges the CTAs' lists - ranks are distinct, so the merge
+// order does not matter - and writes the indices. The pick form then scatters the draft's tokens into the verify-token row: dst[children[0]] =
+// argmax, dst[children[j]] = top-k[j] (j >= 1), the reference's draft pick (csrc/draft_lmhead.sycl:4-17).
+#include <algorithm>
+#include <mutex>
+
 #include "launch.h"
 #include "ranks.cuh"
 
 namespace mono {
 
-constexpr int kLhWarps = 8, kLhMaxM = 8, kLhCtasPerSm = 2;
+constexpr int kLhWarps = 8, kLhMaxM = 8, kLhRows = 8, kLhChunk = 512;
+constexpr int kLhRowPitch = kLhChunk * 2 + 16;   // bytes per staged weight row (16-byte skew: conflict-free ldmatrix)
+constexpr int kLhStage = kLhRows * kLhRowPitch;  // one ring stage: 8 rows x 512 k
+constexpr size_t kLhSmemLimit = 227 * 1024 - 256;  // dynamic bytes: the opt-in maximum less the static ones
 
-__device__ __forceinline__ uint4 lh_ld_stream(const uint4* p, uint64_t pol) {
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p), "l"(pol));
-    return v;
+__device__ __forceinline__ void lh_mma(float (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+    // rows 8..15 of A are zero (a1 = a3 = 0): only rows 0..7, the x rows, carry data
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
 }
-__device__ __forceinline__ float lh_lo(uint32_t u) { return __uint_as_float(u << 16); }
-__device__ __forceinline__ float lh_hi(uint32_t u) { return __uint_as_float(u & 0xFFFF0000u); }
+__device__ __forceinline__ void lh_ldsm_x4(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
 
 struct LmHeadArgs {
     const uint16_t* x;        // [M][x_stride] bf16
@@ -45,146 +58,144 @@ struct LmHeadArgs {
 
 size_t lmhead_workspace_bytes(int grid) { return size_t(grid) * kLhMaxM * (kTkK + 1) * 8 + 256; }
 
-template <int M, int NC, int CPS>
-__global__ void __launch_bounds__(kLhWarps * 32, CPS) lmhead_pick_kernel(const LmHeadArgs A) {
+// Shared memory of one CTA: the warps' rings [warp][S][stage], their barriers, then x [M][K + 8] and a 16-byte zero
+// row (the ldmatrix rows of x past M). The pick's lists reuse the ring area after the last chunk.
+struct LhPlan {
+    size_t rings, bars, x, total;
+    __host__ __device__ LhPlan(int M, int K, int S) {
+        rings = size_t(kLhWarps) * S * kLhStage;
+        bars = (size_t(kLhWarps) * S * 8 + 127) / 128 * 128;
+        x = size_t(M) * (K + 8) * 2 + 16;
+        total = rings + bars + x;
+    }
+};
+
+template <int S>
+__global__ void __launch_bounds__(kLhWarps * 32, 1) lmhead_pick_kernel(const LmHeadArgs A) {
     constexpr int NT = kLhWarps * 32;
-    __shared__ uint64_t lst[kLhWarps][M][kTkK + 1];
-    __shared__ uint64_t fin[NT * kTkK];
+    extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t finb[kLhWarps];
     __shared__ int last;
-    pdl_launch_dependents();
-    pdl_wait();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const LhPlan plan(A.M, A.K, S);
+    uint8_t* ring = smem + size_t(warp) * S * kLhStage;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + plan.rings) + warp * S;
+    uint16_t* xs = reinterpret_cast<uint16_t*>(smem + plan.rings + plan.bars);
+    const int pitch = A.K + 8;
+    const uint16_t* zero16 = xs + size_t(A.M) * pitch;
+    if (lane < S) mbar_init(&bars[lane], 1);
+    fence_mbar_init();
+    __syncwarp();
+    pdl_launch_dependents();
+    // this warp's tiles of 8 vocabulary rows: wg, wg + NW, ...; chunk q = (tile q / CPT, k chunk q % CPT)
+    const int CPT = A.K / kLhChunk;
+    const int tiles = (A.V + kLhRows - 1) / kLhRows;
+    const int wg = int(blockIdx.x) * kLhWarps + warp, NW = int(gridDim.x) * kLhWarps;
+    const int mine = wg < tiles ? (tiles - 1 - wg) / NW + 1 : 0;
+    const int Q = mine * CPT;
     const uint64_t pol = l2_evict_first_policy();
-    const int per_lane = A.K / 256;  // 8-element pieces per lane
-    const int groups = (A.V + NC - 1) / NC, G = int(gridDim.x);
+    auto issue = [&](int q) {  // lane r < 8 copies row r of chunk q (1 KB) into stage q % S
+        const int tile = wg + (q / CPT) * NW, c = q - (q / CPT) * CPT;
+        const int n0 = tile * kLhRows, rows = min(kLhRows, A.V - n0);
+        uint64_t* bar = &bars[q % S];
+        if (lane == 0) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the stage's earlier reads first
+            mbar_arrive_expect_tx(bar, uint32_t(rows) * (kLhChunk * 2));
+        }
+        __syncwarp();
+        if (lane < rows)
+            bulk_g2s_hint(ring + (q % S) * kLhStage + lane * kLhRowPitch,
+                          A.w + int64_t(n0 + lane) * A.K + int64_t(c) * kLhChunk, kLhChunk * 2, bar, pol);
+    };
+    // the weights do not depend on the preceding kernel: start the rings before waiting for it
+    for (int q = 0; q < S && q < Q; ++q) issue(q);
+    pdl_wait();
+    {
+        const int per_row = A.K >> 3;
+        for (int i = threadIdx.x; i < A.M * per_row; i += NT) {
+            const int m = i / per_row, c = i - m * per_row;
+            *reinterpret_cast<uint4*>(xs + size_t(m) * pitch + 8 * c) =
+                __ldg(reinterpret_cast<const uint4*>(A.x + m * A.x_stride) + c);
+        }
+        if (threadIdx.x == 0) *reinterpret_cast<uint4*>(const_cast<uint16_t*>(zero16)) = make_uint4(0, 0, 0, 0);
+    }
+    __syncthreads();
     uint64_t top[kTkK], best = 0;
 #pragma unroll
     for (int j = 0; j < kTkK; ++j) top[j] = 0;
-    constexpr int MP = (M + 1) / 2;  // row pairs (an odd M pads its last pair with a zero row)
-    for (int grp = int(blockIdx.x) * kLhWarps + warp; grp < groups; grp += G * kLhWarps) {
-        const int n0 = grp * NC;
-        float acc[NC][M];
-        if constexpr (M == 1) {
-#pragma unroll
-            for (int c = 0; c < NC; ++c) acc[c][0] = 0.f;
-            for (int j = 0; j < per_lane; ++j) {
-                const int64_t piece = int64_t(j) * 32 + lane;
-                uint4 wv[NC];
-#pragma unroll
-                for (int c = 0; c < NC; ++c)
-                    wv[c] = n0 + c < A.V ? lh_ld_stream(reinterpret_cast<const uint4*>(A.w + int64_t(n0 + c) * A.K) + piece, pol)
-                                         : make_uint4(0, 0, 0, 0);
-                const uint4 xv = __ldg(reinterpret_cast<const uint4*>(A.x) + piece);
-                const float xf[8] = {lh_lo(xv.x), lh_hi(xv.x), lh_lo(xv.y), lh_hi(xv.y),
-                                     lh_lo(xv.z), lh_hi(xv.z), lh_lo(xv.w), lh_hi(xv.w)};
-#pragma unroll
-                for (int c = 0; c < NC; ++c) {
-                    float a = acc[c][0];
-                    a = fmaf(lh_lo(wv[c].x), xf[0], a);
-                    a = fmaf(lh_hi(wv[c].x), xf[1], a);
-                    a = fmaf(lh_lo(wv[c].y), xf[2], a);
-                    a = fmaf(lh_hi(wv[c].y), xf[3], a);
-                    a = fmaf(lh_lo(wv[c].z), xf[4], a);
-                    a = fmaf(lh_hi(wv[c].z), xf[5], a);
-                    a = fmaf(lh_lo(wv[c].w), xf[6], a);
-                    a = fmaf(lh_hi(wv[c].w), xf[7], a);
-                    acc[c][0] = a;
-                }
-            }
-        } else {
-            // two rows per paired fma (__ffma2_rn: each half rounds as fmaf, so the bits are the scalar order's)
-            float2 acc2[NC][MP];
-#pragma unroll
-            for (int c = 0; c < NC; ++c)
-#pragma unroll
-                for (int p = 0; p < MP; ++p) acc2[c][p] = make_float2(0.f, 0.f);
-            // the weight pieces of step j + 1 are requested before step j's arithmetic (one step of look-ahead)
-            uint4 wn[NC];
-#pragma unroll
-            for (int c = 0; c < NC; ++c)
-                wn[c] = n0 + c < A.V ? lh_ld_stream(reinterpret_cast<const uint4*>(A.w + int64_t(n0 + c) * A.K) + lane, pol)
-                                     : make_uint4(0, 0, 0, 0);
-            for (int j = 0; j < per_lane; ++j) {
-                const int64_t piece = int64_t(j) * 32 + lane;
-                uint4 wv[NC];
-#pragma unroll
-                for (int c = 0; c < NC; ++c) {
-                    wv[c] = wn[c];
-                    if (j + 1 < per_lane && n0 + c < A.V)
-                        wn[c] = lh_ld_stream(reinterpret_cast<const uint4*>(A.w + int64_t(n0 + c) * A.K) + piece + 32, pol);
-                }
-                uint4 xv[2 * MP];
-#pragma unroll
-                for (int m = 0; m < 2 * MP; ++m)
-                    xv[m] = m < M ? __ldg(reinterpret_cast<const uint4*>(A.x + m * A.x_stride) + piece) : make_uint4(0, 0, 0, 0);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    float2 xp[MP];
-#pragma unroll
-                    for (int p = 0; p < MP; ++p) {
-                        const uint32_t ua = (&xv[2 * p].x)[e >> 1], ub = (&xv[2 * p + 1].x)[e >> 1];
-                        xp[p] = make_float2((e & 1) ? lh_hi(ua) : lh_lo(ua), (e & 1) ? lh_hi(ub) : lh_lo(ub));
-                    }
-#pragma unroll
-                    for (int c = 0; c < NC; ++c) {
-                        const uint32_t uw = (&wv[c].x)[e >> 1];
-                        const float wf = (e & 1) ? lh_hi(uw) : lh_lo(uw);
-                        const float2 w2 = make_float2(wf, wf);
-#pragma unroll
-                        for (int p = 0; p < MP; ++p) acc2[c][p] = __ffma2_rn(w2, xp[p], acc2[c][p]);
-                    }
-                }
-            }
-#pragma unroll
-            for (int c = 0; c < NC; ++c)
-#pragma unroll
-                for (int m = 0; m < M; ++m) acc[c][m] = (m & 1) ? acc2[c][m >> 1].y : acc2[c][m >> 1].x;
+    // ldmatrix row addresses: W rows lane & 7 at k + 8 (lane >> 3); x rows likewise (past M: the zero row)
+    const int lr = lane & 7, lk = 8 * (lane >> 3);
+    const uint16_t* xrow = lr < A.M ? xs + size_t(lr) * pitch + lk : nullptr;
+    float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+    int q = 0;
+    for (; q < Q; ++q) {
+        if (!mbar_wait(&bars[q % S], uint32_t(q / S) & 1u)) break;
+        const int c = q % CPT;
+        const uint8_t* st = ring + (q % S) * kLhStage + lr * kLhRowPitch + lk * 2;
+        const int kx = c * kLhChunk;
+#pragma unroll 4
+        for (int kk = 0; kk < kLhChunk; kk += 32) {
+            uint32_t b[4], a[4];
+            lh_ldsm_x4(b, st + kk * 2);
+            lh_ldsm_x4(a, xrow ? xrow + kx + kk : zero16);
+            lh_mma(c0, a[0], a[1], b[0], b[1]);
+            lh_mma(c1, a[2], a[3], b[2], b[3]);
         }
+        __syncwarp();
+        if (q + S < Q) issue(q + S);
+        if (c == CPT - 1) {
+            // the tile's logits: token g (< M) at columns n0 + 2t, n0 + 2t + 1 (the two k-step chains summed in order)
+            const int n0 = (wg + (q / CPT) * NW) * kLhRows;
+            if (g < A.M) {
 #pragma unroll
-        for (int c = 0; c < NC; ++c) {
-            const int n = n0 + c;
-#pragma unroll
-            for (int m = 0; m < M; ++m) {
-                float a = acc[c][m];
-#pragma unroll
-                for (int d = 16; d > 0; d >>= 1) a += __shfl_xor_sync(0xffffffffu, a, d);
-                acc[c][m] = a;  // every lane holds the same sum
-            }
-            if (n < A.V) {
-                // lane m takes row m: rank the logit into its running lists
-#pragma unroll
-                for (int m = 0; m < M; ++m)
-                    if (lane == m) {
-                        const uint16_t b = __bfloat16_as_ushort(__float2bfloat16_rn(acc[c][m]));
-                        if (A.logits) A.logits[int64_t(m) * A.V + n] = b;
-                        if (A.k > 0) insert_rank(top, rank_topk(b, uint32_t(n)), A.k);
-                        best = max(best, rank_argmax(b, uint32_t(n)));
+                for (int e = 0; e < 2; ++e) {
+                    const int n = n0 + 2 * t + e;
+                    if (n < A.V) {
+                        const uint16_t bits = __bfloat16_as_ushort(__float2bfloat16_rn(c0[e] + c1[e]));
+                        if (A.logits) A.logits[int64_t(g) * A.V + n] = bits;
+                        if (A.k > 0) insert_rank(top, rank_topk(bits, uint32_t(n)), A.k);
+                        best = max(best, rank_argmax(bits, uint32_t(n)));
                     }
+                }
             }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) c0[i] = c1[i] = 0.f;
         }
     }
-    // the CTA's lists: per row, the warps' lists merged by warp 0's lane m
-    if (lane < M) {
+    if (q < Q) {
+        // a wait gave up (the error word is set): wait, bounded, for this warp's copies still in flight
+        for (int r = q + 1; r < Q && r < q + S; ++r) mbar_wait(&bars[r % S], uint32_t(r / S) & 1u);
+    }
+    __syncthreads();  // every ring is idle: its memory now holds the pick's lists
+    uint64_t* lst = reinterpret_cast<uint64_t*>(smem);      // [warp * 4 + t][kLhMaxM][kTkK + 1]
+    uint64_t* fin = lst + kLhWarps * 4 * kLhMaxM * (kTkK + 1);  // [NT][kTkK]
+    if (g < A.M) {
+        uint64_t* l = lst + ((warp * 4 + t) * kLhMaxM + g) * (kTkK + 1);
 #pragma unroll
-        for (int j = 0; j < kTkK; ++j) lst[warp][lane][j] = top[j];
-        lst[warp][lane][kTkK] = best;
+        for (int j = 0; j < kTkK; ++j) l[j] = top[j];
+        l[kTkK] = best;
     }
     __syncthreads();
-    // the counter sits at a fixed offset, so calls of any grid size share a workspace safely
-    unsigned* counter = reinterpret_cast<unsigned*>(A.ws);
+    unsigned* counter = reinterpret_cast<unsigned*>(A.ws);  // fixed offset: calls of any grid share a workspace
     uint64_t* ws = A.ws + 32;
-    if (warp == 0 && lane < M) {
-        for (int w = 1; w < kLhWarps; ++w) {
-            for (int j = 0; j < A.k; ++j) insert_rank(top, lst[w][lane][j], A.k);
-            best = max(best, lst[w][lane][kTkK]);
-        }
-        uint64_t* mine = ws + (size_t(blockIdx.x) * kLhMaxM + lane) * (kTkK + 1);
+    if (threadIdx.x < A.M) {
+        const int m = threadIdx.x;
+        uint64_t t2[kTkK], b2 = 0;
 #pragma unroll
-        for (int j = 0; j < kTkK; ++j) __stcg(mine + j, top[j]);
-        __stcg(mine + kTkK, best);
+        for (int j = 0; j < kTkK; ++j) t2[j] = 0;
+        for (int r = 0; r < kLhWarps * 4; ++r) {
+            const uint64_t* l = lst + (r * kLhMaxM + m) * (kTkK + 1);
+            for (int j = 0; j < A.k; ++j) insert_rank(t2, l[j], A.k);
+            b2 = max(b2, l[kTkK]);
+        }
+        uint64_t* out = ws + (size_t(blockIdx.x) * kLhMaxM + m) * (kTkK + 1);
+#pragma unroll
+        for (int j = 0; j < kTkK; ++j) __stcg(out + j, t2[j]);
+        __stcg(out + kTkK, b2);
     }
     __syncthreads();
+    const int G = int(gridDim.x);
     if (threadIdx.x == 0) {
         __threadfence();
         last = atomicAdd(counter, 1u) == unsigned(G - 1);
@@ -194,12 +205,12 @@ __global__ void __launch_bounds__(kLhWarps * 32, CPS) lmhead_pick_kernel(const L
     if (!last) return;
     // the last CTA, per row: thread t merges the lists of CTAs t, t + 256, ..., then a pairwise merge tree in
     // shared memory (merge_lists) and one thread writes the indices
-    for (int m = 0; m < M; ++m) {
+    for (int m = 0; m < A.M; ++m) {
         uint64_t t2[kTkK], b2 = 0;
 #pragma unroll
         for (int j = 0; j < kTkK; ++j) t2[j] = 0;
-        for (int c = threadIdx.x; c < G; c += NT) {
-            const uint64_t* src = ws + (size_t(c) * kLhMaxM + m) * (kTkK + 1);
+        for (int cta = threadIdx.x; cta < G; cta += NT) {
+            const uint64_t* src = ws + (size_t(cta) * kLhMaxM + m) * (kTkK + 1);
             for (int j = 0; j < A.k; ++j) insert_rank(t2, __ldcg(src + j), A.k);
             b2 = max(b2, __ldcg(src + kTkK));
         }
@@ -232,35 +243,48 @@ __global__ void __launch_bounds__(kLhWarps * 32, CPS) lmhead_pick_kernel(const L
     if (threadIdx.x == 0) atomicExch(counter, 0u);  // reusable by the next launch
 }
 
-int lmhead_grid() { return sm_count() * kLhCtasPerSm; }
+int lmhead_grid() { return sm_count(); }
 
-template <int M, int NC>
+// the deepest ring (stages per warp) whose plan fits the shared memory, or 0
+int lmhead_stages(int M, int K) {
+    for (int S = 4; S >= 2; --S)
+        if (LhPlan(M, K, S).total <= kLhSmemLimit) return S;
+    return 0;
+}
+
+template <int S>
 static int launch_lh(const LmHeadArgs& A, cudaStream_t stream) {
+    auto kern = lmhead_pick_kernel<S>;
+    const size_t smem = LhPlan(A.M, A.K, S).total;
+    static std::mutex mu;
+    static size_t opt_in = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (smem > opt_in) {
+            CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+            opt_in = smem;
+        }
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(lmhead_grid());
     cfg.blockDim = dim3(kLhWarps * 32);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    CUDA_TRY(cudaLaunchKernelEx(&cfg, lmhead_pick_kernel<M, NC, kLhCtasPerSm>, A));
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, A));
     return MONO_OK;
 }
 
-// (measured at 8 rows: 4 columns per warp at 2 CTAs per SM, 460 us; 2 columns at 3 CTAs per SM, 599 us; 8 columns
-// at 1 CTA per SM, 575 us)
 int launch_lmhead(const LmHeadArgs& A, cudaStream_t stream) {
-    switch (A.M) {
-        case 1: return launch_lh<1, 1>(A, stream);
-        case 2: return launch_lh<2, 2>(A, stream);
-        case 3: return launch_lh<3, 2>(A, stream);
-        case 4: return launch_lh<4, 4>(A, stream);
-        case 5: return launch_lh<5, 4>(A, stream);
-        case 6: return launch_lh<6, 4>(A, stream);
-        case 7: return launch_lh<7, 4>(A, stream);
-        default: return launch_lh<8, 4>(A, stream);
+    switch (lmhead_stages(A.M, A.K)) {
+        case 4: return launch_lh<4>(A, stream);
+        case 3: return launch_lh<3>(A, stream);
+        case 2: return launch_lh<2>(A, stream);
+        default: return fail(MONO_EINVAL, "lm_head: x rows of K = %d do not fit next to the rings", A.K);
     }
 }
 
@@ -276,7 +300,8 @@ extern "C" int mono_lmhead_pick(const void* x, int64_t x_stride, const void* w, 
     MONO_CHECK(x && w && workspace, "null operand");
     MONO_CHECK(M >= 1 && M <= kLhMaxM, "1 <= M <= %d rows", kLhMaxM);
     MONO_CHECK(k >= 0 && k <= kTkK, "0 <= k <= %d", kTkK);
-    MONO_CHECK(K >= 256 && K % 256 == 0 && K <= (1 << 20), "K a multiple of 256 up to 2^20");
+    MONO_CHECK(K >= kLhChunk && K % kLhChunk == 0 && lmhead_stages(int(M), int(std::min<int64_t>(K, 1 << 20))) > 0,
+               "K a multiple of 512 whose M x rows fit in shared memory beside the rings (K <= 4096 at M = 8)");
     MONO_CHECK(V >= 1 && V < (int64_t(1) << 31) && V * K < (int64_t(1) << 40), "1 <= V < 2^31");
     MONO_CHECK(x_stride >= K && x_stride % 8 == 0 && aligned(x, 16) && aligned(w, 16),
                "x rows and w 16-byte aligned, x_stride a multiple of 8 elements");

@@ -312,13 +312,14 @@ MONO_API int mono_gemv_bf16(const void* x, int64_t x_stride, const void* w, int6
 /* bf16 lm_head with the pick fused: the verify's greedy logits + argmax (the reference's verify_logits then
  * lg.argmax, comfy_mono_decode_xpu/mtp_loop.py:325-327) and the draft pick (csrc/draft_lmhead.sycl:87-292: the
  * draft token, the top-n row and the children's verify tokens in one launch). For M <= 8 rows of x [M][x_stride]
- * against w [V][K]: logits = bf16(sum_k x[m][k] * w[n][k]) in a pinned order (lane l of 32 accumulates the 8-element
- * pieces l, l + 32, ... with fmaf in element order, then the xor butterfly 16, 8, 4, 2, 1), then per row
+ * against w [V][K]: logits = bf16(sum_k x[m][k] * w[n][k]) on the tensor cores (fp32 accumulation over a fixed
+ * partition of K into 8 slices, the slices summed in order: the same bits on every launch), then per row
  *   argmax[m]   the argmax by the rank (float order, NaN largest, -0 == +0, smallest index on ties)
  *   topk[m][j]  j < k <= 8, descending by the top-k rank (the reference's fast_topk tie order)
  *   logits      (optional, NULL: not written) bf16 [M][V]
  * and, with children (device int32, up to 8 slots of dst, -1 ends) and dst (device int64), M == 1: dst[children[0]]
- * = argmax, dst[children[j]] = topk[j] for 1 <= j < k (the draft token and its siblings' tokens). K % 256 == 0;
+ * = argmax, dst[children[j]] = topk[j] for 1 <= j < k (the draft token and its siblings' tokens). K % 256 == 0,
+ * K <= 8192;
  * workspace: mono_lmhead_workspace() bytes, zero-filled before first use (the kernel leaves it reusable); one call
  * at a time per workspace. */
 MONO_API size_t mono_lmhead_workspace(void);

@@ -5,11 +5,12 @@ strides, the parity-alternating GDN buffers, the ctl handoff from the accept to 
 
   bit-exact   layer_pre (RMSNorm -> quant -> W4A8 q|k|v or qkv|z), Q/K norm + RoPE + KV-cache rows, the a|b
               projection, the gate / quant -> o_proj / out_proj + residual, the fused MLP, the final norm, the
-              verify lm_head argmax, every draft's lm_head pick into the verify-token row, the accept walk (result
-              row, counters, ctl, next token, hidden row) and the KV slot moves of an off-chain path, the GDN conv
-              state after the replay
+              verify argmax and every draft's pick into the verify-token row (on the lm_head kernel's own logits),
+              the accept walk (result row, counters, ctl, next token, hidden row) and the KV slot moves of an
+              off-chain path, the GDN conv state after the replay
   tolerance   tree attention and the GDN core / recurrent state against fp64 (the bounds of
-              tests/test_attention_gpu.py and tests/test_gdn_gpu.py)
+              tests/test_attention_gpu.py and tests/test_gdn_gpu.py); the tensor-core lm_head logits against the exact
+              dot products (oracle/lmhead.py tolerance)
 
 The accepted path is steered on some steps (the verify tokens are rewritten before the accept), so the replay of an
 off-chain leaf, a full-chain accept and the KV moves run on the device and are checked like the natural steps."""
@@ -37,6 +38,17 @@ def _row_linear(x_bits, norm_bits, eps, srcs, residual=None):
     xn = ol.rmsnorm(x_bits, norm_bits, eps) if norm_bits is not None else x_bits
     q, s = ow.act_quant(xn)
     return xn, np.concatenate([_gptq(q, s, src, residual) for src in srcs], axis=1)
+
+
+def _kernel_pick(xf, lm_t, lm, k):
+    """The pick of the lm_head kernel's own logits for the normed rows xf (device), after checking those logits
+    against the exact dot products."""
+    from mono_b200 import _C
+    lg = bf16_bits(_C.lmhead_pick(xf, lm_t, k=0, logits=True)[2])
+    exact, abs_sum = olh.logits_exact(bf16_bits(xf), lm)
+    err = np.abs(bf16_bits_to_f32(lg).astype(np.float64) - exact)
+    assert (err <= olh.tolerance(exact, abs_sum)).all(), err.max()
+    return olh.pick_logits(lg, k)
 
 
 def _steer(model, path):
@@ -80,7 +92,7 @@ def test_decoder_steps_match_oracle_op_by_op(cuda):
         for name, i, T in events:
             if name == "draft":
                 # the pick of draft i: its children's verify tokens, from the GPU's normed hidden row
-                _, am, top = olh.pick(bf16_bits(T["xf"]), lm, cfg.tree[i])
+                am, top = _kernel_pick(T["xf"], model.lm_head, lm, cfg.tree[i])
                 d = T["drafts"].cpu().tolist()
                 kids = [c for c in tree["children"][i] if c >= 0]
                 assert d[kids[0]] == int(am[0]), (step, i)
@@ -152,7 +164,7 @@ def test_decoder_steps_match_oracle_op_by_op(cuda):
                 assert T["tokens"].cpu().tolist() == drafts_seen
                 xf_ref = ol.rmsnorm(bf16_bits(T["x"]), bf16_bits(model.final_norm), eps)
                 assert np.array_equal(bf16_bits(T["xf"]), xf_ref)
-                _, am, _ = olh.pick(xf_ref, lm, 0)
+                am, _ = _kernel_pick(T["xf"], model.lm_head, lm, 0)
                 assert T["toks"].view(-1).cpu().tolist() == am.tolist(), step
                 x_final = bf16_bits(T["x"])
             elif name == "accept_in":
