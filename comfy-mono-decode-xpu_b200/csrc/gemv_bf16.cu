@@ -2,7 +2,9 @@
 // one draft row, comfy_mono_decode_xpu/draft_head.py:198-210): out[m][n] = bf16(sum_k x[m][k] * w[n][k]) with
 // fp32 accumulation, for a few rows (M <= 8) of x against a bf16 weight [N][K] far larger than L2.
 //
-// HBM-bound: the algorithmic bytes are the weight (N * K * 2) plus M * (K + N) * 2. One warp per output column
+// HBM-bound: the algorithmic bytes are the weight (N * K * 2) plus M * (K + N) * 2. For K a multiple of 512 (all
+// of the draft head's projections) the call runs the lm_head's ring kernel without its pick (lmhead.cu: tensor-core
+// MMAs, kilobyte bulk copies). Otherwise, this file's kernel: one warp per output column
 // n: lane l reads the 16-byte pieces l, l + 32, ... of weight row n (each warp load is 512 contiguous bytes),
 // 4 pieces in flight per lane (measured faster than 8 at M = 1: more resident warps), read past L1 and marked evict-first in L2 (the weight is streamed once per
 // draft; the KV cache and activations keep L2). The x rows come through the read-only path (L1 hits after the
@@ -102,6 +104,10 @@ extern "C" int mono_gemv_bf16(const void* x, int64_t x_stride, const void* w, in
     auto* o = static_cast<uint16_t*>(out);
     const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const int k = int(K), n = int(N);
+    // K a multiple of 512 (every projection of the draft head): the tensor-core ring kernel of the lm_head, which
+    // keeps S kilobyte requests per warp in flight; other K: the warp-per-column kernel below
+    if (aligned(out, 16) && out_stride % 8 == 0 && bf16_rows_fit(int(M), k))
+        return launch_bf16_rows(xs, x_stride, ws, int(M), n, k, o, out_stride, s);
     switch (M) {
         case 1: gemv_bf16_launch<1>(xs, x_stride, ws, k, n, o, out_stride, s); break;
         case 2: gemv_bf16_launch<2>(xs, x_stride, ws, k, n, o, out_stride, s); break;

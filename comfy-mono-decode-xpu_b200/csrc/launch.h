@@ -156,6 +156,11 @@ struct TopkArgs {
     int64_t V;
     int rows, k, argmax_order, with_argmax;
 };
+// the lm_head's bf16 ring kernel without the pick (lmhead.cu): out[m][n] = bf16(x[m] . w[n]) on the tensor cores
+bool bf16_rows_fit(int M, int K);
+int launch_bf16_rows(const uint16_t* x, int64_t x_stride, const uint16_t* w, int M, int N, int K, uint16_t* out,
+                     int64_t out_stride, cudaStream_t stream);
+
 size_t topk_workspace_bytes(int64_t rows);
 int launch_topk(const TopkArgs& A, cudaStream_t stream);
 

@@ -52,7 +52,7 @@ struct LmHeadArgs {
     const int32_t* children;  // pick form: up to 8 slots of dst, -1 ends (row 0's tokens), or null
     int64_t* dst;             // pick form: the verify-token row
     uint64_t* ws;             // the arrival counter (first 256 bytes), then [G][kLhMaxM][kTkK + 1] CTA lists
-    int64_t x_stride;
+    int64_t x_stride, out_stride;  // out_stride: the logits' row stride (V for the pick)
     int K, V, M, k;
 };
 
@@ -70,7 +70,8 @@ struct LhPlan {
     }
 };
 
-template <int S>
+// PICK = false: the plain bf16 GEMV (the draft head's projections): logits = out [M][out_stride], no pick.
+template <int S, bool PICK>
 __global__ void __launch_bounds__(kLhWarps * 32, 1) lmhead_pick_kernel(const LmHeadArgs A) {
     constexpr int NT = kLhWarps * 32;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -153,9 +154,11 @@ __global__ void __launch_bounds__(kLhWarps * 32, 1) lmhead_pick_kernel(const LmH
                     const int n = n0 + 2 * t + e;
                     if (n < A.V) {
                         const uint16_t bits = __bfloat16_as_ushort(__float2bfloat16_rn(c0[e] + c1[e]));
-                        if (A.logits) A.logits[int64_t(g) * A.V + n] = bits;
-                        if (A.k > 0) insert_rank(top, rank_topk(bits, uint32_t(n)), A.k);
-                        best = max(best, rank_argmax(bits, uint32_t(n)));
+                        if (!PICK || A.logits) A.logits[int64_t(g) * A.out_stride + n] = bits;
+                        if constexpr (PICK) {
+                            if (A.k > 0) insert_rank(top, rank_topk(bits, uint32_t(n)), A.k);
+                            best = max(best, rank_argmax(bits, uint32_t(n)));
+                        }
                     }
                 }
             }
@@ -167,6 +170,7 @@ __global__ void __launch_bounds__(kLhWarps * 32, 1) lmhead_pick_kernel(const LmH
         // a wait gave up (the error word is set): wait, bounded, for this warp's copies still in flight
         for (int r = q + 1; r < Q && r < q + S; ++r) mbar_wait(&bars[r % S], uint32_t(r / S) & 1u);
     }
+    if constexpr (!PICK) return;
     __syncthreads();  // every ring is idle: its memory now holds the pick's lists
     uint64_t* lst = reinterpret_cast<uint64_t*>(smem);      // [warp * 4 + t][kLhMaxM][kTkK + 1]
     uint64_t* fin = lst + kLhWarps * 4 * kLhMaxM * (kTkK + 1);  // [NT][kTkK]
@@ -252,9 +256,9 @@ int lmhead_stages(int M, int K) {
     return 0;
 }
 
-template <int S>
+template <int S, bool PICK>
 static int launch_lh(const LmHeadArgs& A, cudaStream_t stream) {
-    auto kern = lmhead_pick_kernel<S>;
+    auto kern = lmhead_pick_kernel<S, PICK>;
     const size_t smem = LhPlan(A.M, A.K, S).total;
     static std::mutex mu;
     static size_t opt_in = 0;
@@ -279,13 +283,32 @@ static int launch_lh(const LmHeadArgs& A, cudaStream_t stream) {
     return MONO_OK;
 }
 
-int launch_lmhead(const LmHeadArgs& A, cudaStream_t stream) {
+template <bool PICK>
+static int launch_lmhead_t(const LmHeadArgs& A, cudaStream_t stream) {
     switch (lmhead_stages(A.M, A.K)) {
-        case 4: return launch_lh<4>(A, stream);
-        case 3: return launch_lh<3>(A, stream);
-        case 2: return launch_lh<2>(A, stream);
+        case 4: return launch_lh<4, PICK>(A, stream);
+        case 3: return launch_lh<3, PICK>(A, stream);
+        case 2: return launch_lh<2, PICK>(A, stream);
         default: return fail(MONO_EINVAL, "lm_head: x rows of K = %d do not fit next to the rings", A.K);
     }
+}
+
+int launch_lmhead(const LmHeadArgs& A, cudaStream_t stream) { return launch_lmhead_t<true>(A, stream); }
+
+bool bf16_rows_fit(int M, int K) { return K >= kLhChunk && K % kLhChunk == 0 && M <= kLhMaxM && lmhead_stages(M, K) > 0; }
+
+int launch_bf16_rows(const uint16_t* x, int64_t x_stride, const uint16_t* w, int M, int N, int K, uint16_t* out,
+                     int64_t out_stride, cudaStream_t stream) {
+    LmHeadArgs A{};
+    A.x = x;
+    A.w = w;
+    A.logits = out;
+    A.x_stride = x_stride;
+    A.out_stride = out_stride;
+    A.K = K;
+    A.V = N;
+    A.M = M;
+    return launch_lmhead_t<false>(A, stream);
 }
 
 }  // namespace mono
@@ -320,6 +343,7 @@ extern "C" int mono_lmhead_pick(const void* x, int64_t x_stride, const void* w, 
     A.dst = dst;
     A.ws = static_cast<uint64_t*>(workspace);
     A.x_stride = x_stride;
+    A.out_stride = V;
     A.K = int(K);
     A.V = int(V);
     A.M = int(M);
