@@ -13,8 +13,8 @@
 // x[t-1] w[2], .. from 0), out = bf16(y / (1 + exp(-y))), over the conv state (3 newest inputs, oldest
 // first) and the replayed then the verify rows. Threads < (n + M) * HV make the gates:
 // decay = exp(g_decay * softplus(a + dt_bias)) (softplus(v) = v above 20), beta = bf16(sigmoid(b)).
-// Kernel 2 (one CTA per value head, 512 threads = 4 row groups x 128 value columns; thread (rg, col) keeps
-// state rows rg * 32 .. rg * 32 + 31 of column col in registers): L2 norms of q and k of the key head
+// Kernel 2 (per value head 4 row groups x 128 value columns, spread over a cluster of 4 CTAs below; thread
+// (rg, col) keeps state rows rg * 32 .. rg * 32 + 31 of column col in registers): L2 norms of q and k of the key head
 // (qi = 1 / max(sqrt(sum), 1e-12), q <- (q * scale) * qi, k <- k * ki), then per row in order
 //   S <- S * decay;  mem = S^T k;  delta = (v - mem) * beta;  S <- S + k delta^T;  o = S^T q
 // (fma chains over each row group's 32 rows, the 4 group partials summed in order), raw = bf16(o); the
@@ -23,80 +23,76 @@
 #include <cmath>
 #include <mutex>
 
+#include <cooperative_groups.h>
+
 #include "gdn.cuh"
 
 namespace mono {
 
-__device__ uint16_t g_gdn_silu[65536];
+namespace cg = cooperative_groups;
 
-__global__ void gdn_silu_lut_kernel() {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < 65536) g_gdn_silu[i] = f32_to_bf16_bits(gdn_silu_formula(bf16_bits_to_f32(uint16_t(i))));
-}
+constexpr int kConvThreads = 64;  // 128 CTAs over the 8192 channels of the 9B model: one per SM, not 32
 
-int ensure_gdn_silu_lut(cudaStream_t stream) {
-    static std::mutex mu;
-    static bool done[64] = {};
-    int dev = 0;
-    CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64) return fail(MONO_EINVAL, "device index");
-    std::lock_guard<std::mutex> lock(mu);
-    if (done[dev]) return MONO_OK;
-    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-    CUDA_TRY(cudaStreamIsCapturing(stream, &cs));
-    if (cs != cudaStreamCaptureStatusNone)
-        return fail(MONO_EINVAL, "the first GDN launch on a device must not be inside a graph capture");
-    gdn_silu_lut_kernel<<<256, 256, 0, stream>>>();
-    CUDA_TRY(cudaGetLastError());
-    CUDA_TRY(cudaStreamSynchronize(stream));
-    done[dev] = true;
-    return MONO_OK;
-}
-
-__global__ void __launch_bounds__(256) gdn_conv_kernel(const GdnArgs A) {
+__global__ void __launch_bounds__(kConvThreads) gdn_conv_kernel(const GdnArgs A) {
     gdn_conv_item(A, blockIdx.x * blockDim.x + threadIdx.x);
 }
 
-__global__ void __launch_bounds__(kRG * kDH) gdn_delta_kernel(const GdnArgs A) {
+// Kernel 2 runs as a cluster of 4 CTAs per value head (128 CTAs at 32 heads): CTA c of the cluster keeps value
+// columns 32c .. 32c + 31, thread (row group = warp, lane) column 32c + lane, state rows rg * 32 .. rg * 32 + 31 -
+// the partition and every sum order of a one-CTA head, so the bits are the same. The gated RMSNorm of a row needs
+// all 128 columns: after a cluster barrier each CTA reads the others' raw rows from their shared memory.
+constexpr int kDcCols = 32, kDcCtas = kDH / kDcCols;
+static_assert(kRG == 4 && kDcCols == 32, "one warp per row group, one lane per column");
+
+__global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols) gdn_delta_kernel(const GdnArgs A) {
     __shared__ __align__(16) float qn[kGdnMaxAll][kDH];
     __shared__ __align__(16) float kn[kGdnMaxAll][kDH];
-    __shared__ float part[2][kRG][kDH];
-    __shared__ float raw[kGdnMaxRows][kDH];
+    __shared__ float part[2][kRG][kDcCols];
+    __shared__ float raw[kGdnMaxRows][kDcCols];
     __shared__ float sums[2 * kGdnMaxAll];
-    __shared__ float vsm[kGdnMaxAll][kDH];  // v of every row (the recurrence reads no global memory)
-    __shared__ float gsm[kGdnMaxAll][2];    // decay, beta of every row
-    const int h = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int rg = tid / kDH, col = tid % kDH;
+    __shared__ float nsum[kGdnMaxRows];
+    __shared__ float vsm[kGdnMaxAll][kDcCols];  // v of the CTA's columns, every row
+    __shared__ float gsm[kGdnMaxAll][2];        // decay, beta of every row
+    __shared__ int cs[kGdnCtlWords];
+    gdn_ctl_stage(A, cs);
+    __syncthreads();
+    cg::cluster_group cluster = cg::this_cluster();
+    const int cr = int(cluster.block_rank());
+    const int h = int(blockIdx.x) / kDcCtas, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int rg = warp, col = cr * kDcCols + lane;
     const int kh = h / (A.HV / A.HK), KD = A.HK * kDH, M = A.M;
-    const int n = gdn_pending(A), R = n + M;
-    // sums of squares of q and k of the key head per row: (row, q or k) pairs over the 16 warps
-    for (int pr = warp; pr < 2 * R; pr += 16) {
+    const int n = gdn_pending_s(A, cs), R = n + M;
+    // sums of squares of q and k of the key head per row: (row, q or k) pairs over the 4 warps
+    for (int pr = warp; pr < 2 * R; pr += kRG) {
         const int t = pr >> 1, which = pr & 1;
         const float s = gdn_sumsq128(A.conv_out + size_t(t) * A.C + which * KD + kh * kDH, lane);
         if (lane == 0) sums[pr] = s;
     }
+    float st[kRPG];
+    float* S = A.state + (size_t(h) * kDH + rg * kRPG) * kDH + col;
+#pragma unroll
+    for (int r = 0; r < kRPG; ++r) st[r] = S[size_t(r) * kDH];
     __syncthreads();
     for (int e = tid; e < R * kDH; e += blockDim.x) {
         const int t = e / kDH, d = e % kDH;
         const float qi = gdn_l2_inv(sums[2 * t]), ki = gdn_l2_inv(sums[2 * t + 1]);
         qn[t][d] = (bf16_bits_to_f32(A.conv_out[size_t(t) * A.C + kh * kDH + d]) * A.qscale) * qi;
         kn[t][d] = bf16_bits_to_f32(A.conv_out[size_t(t) * A.C + KD + kh * kDH + d]) * ki;
-        vsm[t][d] = bf16_bits_to_f32(A.conv_out[size_t(t) * A.C + 2 * KD + h * kDH + d]);
+    }
+    for (int e = tid; e < R * kDcCols; e += blockDim.x) {
+        const int t = e / kDcCols, c = e % kDcCols;
+        vsm[t][c] = bf16_bits_to_f32(A.conv_out[size_t(t) * A.C + 2 * KD + h * kDH + cr * kDcCols + c]);
     }
     if (tid < 2 * R) gsm[tid >> 1][tid & 1] = A.gates[((tid >> 1) * A.HV + h) * 2 + (tid & 1)];
-    for (int e = tid; e < M * kDH; e += blockDim.x) raw[e / kDH][e % kDH] = 0.f;  // rows no entry names
-    float st[kRPG];
-    float* S = A.state + (size_t(h) * kDH + rg * kRPG) * kDH + col;
-#pragma unroll
-    for (int r = 0; r < kRPG; ++r) st[r] = S[size_t(r) * kDH];
+    for (int e = tid; e < M * kDcCols; e += blockDim.x) raw[e / kDcCols][e % kDcCols] = 0.f;  // rows no entry names
     __syncthreads();
     // the entries: the replayed rows (committing), then the verify program (gdn_entry)
-    const int E = n + gdn_verify_entries(A);
+    const int E = n + gdn_verify_entries_s(A, cs);
     for (int e = 0; e < E; ++e) {
-        const GdnEntry en = gdn_entry(A, n, e);
+        const GdnEntry en = gdn_entry_s(A, cs, n, e);
         const int t = en.row;
         const float decay = gsm[t][0], beta = gsm[t][1];
-        const float v = vsm[t][col];
+        const float v = vsm[t][lane];
         // the row group's 32 k and q values as 16-byte shared loads (a warp's lanes share the row group: broadcast)
         float kr[kRPG], qr[kRPG];
 #pragma unroll
@@ -118,9 +114,9 @@ __global__ void __launch_bounds__(kRG * kDH) gdn_delta_kernel(const GdnArgs A) {
 #pragma unroll
             for (int r = 0; r < kRPG; ++r) mem = fmaf(st[r] * decay, kr[r], mem);
         }
-        part[0][rg][col] = mem;
+        part[0][rg][lane] = mem;
         __syncthreads();
-        const float kv = part[0][0][col] + part[0][1][col] + part[0][2][col] + part[0][3][col];
+        const float kv = part[0][0][lane] + part[0][1][lane] + part[0][2][lane] + part[0][3][lane];
         const float delta = (v - kv) * beta;
         float o = 0.f;
         if (en.commit) {
@@ -133,9 +129,10 @@ __global__ void __launch_bounds__(kRG * kDH) gdn_delta_kernel(const GdnArgs A) {
 #pragma unroll
             for (int r = 0; r < kRPG; ++r) o = fmaf(fmaf(kr[r], delta, st[r] * decay), qr[r], o);
         }
-        part[1][rg][col] = o;
+        part[1][rg][lane] = o;
         __syncthreads();
-        if (rg == 0 && en.out >= 0) raw[en.out][col] = bf16_round(part[1][0][col] + part[1][1][col] + part[1][2][col] + part[1][3][col]);
+        if (rg == 0 && en.out >= 0)
+            raw[en.out][lane] = bf16_round(part[1][0][lane] + part[1][1][lane] + part[1][2][lane] + part[1][3][lane]);
         if (A.ctl != nullptr && e == n - 1)  // the committed state after the replay
 #pragma unroll
             for (int r = 0; r < kRPG; ++r) S[size_t(r) * kDH] = st[r];
@@ -143,22 +140,27 @@ __global__ void __launch_bounds__(kRG * kDH) gdn_delta_kernel(const GdnArgs A) {
     if (A.ctl == nullptr)
 #pragma unroll
         for (int r = 0; r < kRPG; ++r) S[size_t(r) * kDH] = st[r];
-    __syncthreads();
-    // gated RMSNorm of every output row: warp w < M sums row w's squares (order of gdn_sumsq128)
-    if (warp < M) {
+    cluster.sync();  // every CTA's raw rows are written (a cluster barrier orders its shared-memory writes)
+    // gated RMSNorm of every output row: row t's squares in gdn_sumsq128's order (lane l: columns l, l + 32, l + 64,
+    // l + 96 in order, i.e. CTA 0 .. 3's column l, then the xor butterfly)
+    for (int t = warp; t < M; t += kRG) {
         float s = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) s = fmaf(raw[warp][lane + 32 * j], raw[warp][lane + 32 * j], s);
+        for (int j = 0; j < kDcCtas; ++j) {
+            const float* rj = cluster.map_shared_rank(&raw[0][0], j);
+            const float v = rj[t * kDcCols + lane];
+            s = fmaf(v, v, s);
+        }
 #pragma unroll
         for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0) sums[warp] = s;
+        if (lane == 0) nsum[t] = s;
     }
-    __syncthreads();
-    for (int e = tid; e < M * kDH; e += blockDim.x) {
-        const int t = e / kDH, d = e % kDH;
+    cluster.sync();  // no CTA leaves while another reads its raw rows; nsum is visible to the CTA
+    for (int e = tid; e < M * kDcCols; e += blockDim.x) {
+        const int t = e / kDcCols, c = e % kDcCols, d = cr * kDcCols + c;
         const float z = bf16_bits_to_f32(A.z[size_t(t) * A.z_stride + h * kDH + d]);
         A.core[size_t(t) * A.HV * kDH + h * kDH + d] =
-            gdn_core(raw[t][d], bf16_bits_to_f32(A.gnorm_w[d]), gdn_norm_inv(sums[t], A.gnorm_eps), z);
+            gdn_core(raw[t][c], bf16_bits_to_f32(A.gnorm_w[d]), gdn_norm_inv(nsum[t], A.gnorm_eps), z);
     }
 }
 
@@ -171,9 +173,26 @@ __global__ void __launch_bounds__(256) gdn_ab_kernel(const uint16_t* x, int64_t 
     const int cl = warp >> 2, q = warp & 3, n = blockIdx.x * 2 + cl;
     uint4 wv[4];
     if (n < N) gdn_ab_load_w(w, K, n, q, lane, wv);  // in flight while the rows are copied
-    for (int i = threadIdx.x; i < M * per; i += blockDim.x) {
-        const int m = i / per, c = i - m * per;
-        reinterpret_cast<uint4*>(xs + size_t(m) * K)[c] = __ldcg(reinterpret_cast<const uint4*>(x + size_t(m) * x_stride) + c);
+    // the rows in batches of 16 pieces per thread, every load of a batch issued before its stores (one L2 round
+    // trip per batch instead of one per piece)
+    for (int base = 0; base < M * per; base += 16 * 256) {
+        uint4 v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int i = base + j * 256 + int(threadIdx.x);
+            if (i < M * per) {
+                const int m = i / per, c = i - m * per;
+                v[j] = __ldcg(reinterpret_cast<const uint4*>(x + size_t(m) * x_stride) + c);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int i = base + j * 256 + int(threadIdx.x);
+            if (i < M * per) {
+                const int m = i / per, c = i - m * per;
+                reinterpret_cast<uint4*>(xs + size_t(m) * K)[c] = v[j];
+            }
+        }
     }
     __syncthreads();
     if (n < N) gdn_ab_quarter(xs, wv, K, M, q, lane, &qs[cl][q][0]);
@@ -208,16 +227,14 @@ size_t gdn_workspace_bytes(int M, int C, int HV) {
 }
 
 int launch_gdn_step(GdnArgs A, void* ws, cudaStream_t stream) {
-    const int rc = ensure_gdn_silu_lut(stream);
-    if (rc != MONO_OK) return rc;
     const size_t rows = size_t(A.M) + kGdnMaxRows;
     A.conv_out = static_cast<uint16_t*>(ws);
     A.gates = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + (rows * A.C * 2 + 255) / 256 * 256);
     const int rmax = int(rows);
     const int nthreads = A.C > rmax * A.HV ? A.C : rmax * A.HV;
-    gdn_conv_kernel<<<(nthreads + 255) / 256, 256, 0, stream>>>(A);
+    gdn_conv_kernel<<<(nthreads + kConvThreads - 1) / kConvThreads, kConvThreads, 0, stream>>>(A);
     CUDA_TRY(cudaGetLastError());
-    gdn_delta_kernel<<<A.HV, kRG * kDH, 0, stream>>>(A);
+    gdn_delta_kernel<<<A.HV * kDcCtas, kRG * kDcCols, 0, stream>>>(A);
     CUDA_TRY(cudaGetLastError());
     return MONO_OK;
 }

@@ -9,11 +9,11 @@ namespace mono {
 
 constexpr int kDH = 128, kRG = 4, kRPG = kDH / kRG, kGdnMaxRows = 8, kGdnMaxAll = 2 * kGdnMaxRows;
 
-// bf16(y / (1 + exp(-y))) of every bf16 pattern y (fp32 arithmetic): the conv and gated-norm SiLU as one load
-// each, the same bits as evaluating the formula per value. Built once per device (ensure_gdn_silu_lut).
-extern __device__ uint16_t g_gdn_silu[65536];
+// The conv and gated-norm SiLU: bf16(y / (1 + exp(-y))) of a bf16 value y, fp32 arithmetic, evaluated in place
+// (a table lookup would put a dependent global load behind every output).
 __device__ __forceinline__ float gdn_silu_formula(float y) { return y / (1.f + expf(-y)); }
-__device__ __forceinline__ float gdn_silu(float y_bf16) { return bf16_bits_to_f32(g_gdn_silu[f32_to_bf16_bits(y_bf16)]); }
+__device__ __forceinline__ uint16_t gdn_silu_bits(float y_bf16) { return f32_to_bf16_bits(gdn_silu_formula(y_bf16)); }
+__device__ __forceinline__ float gdn_silu(float y_bf16) { return bf16_bits_to_f32(gdn_silu_bits(y_bf16)); }
 
 // ctl (deferred form) = [pending, parity, accepted slots[8], parents[8], program[8]] (csrc/mono_gdn.sycl:38-40).
 // parent(t) of verify row t: a row before it, or -1 (the root's parent; anything else reads as -1). Without ctl (the
@@ -45,6 +45,34 @@ __device__ __forceinline__ GdnEntry gdn_entry(const GdnArgs& A, int n, int e) {
     if (e < n) return GdnEntry{e, -1, true};
     if (A.ctl == nullptr) return GdnEntry{e, e, true};
     const int p = __ldcg(A.ctl + 2 + 2 * kGdnMaxRows + (e - n));
+    return GdnEntry{n + (p & 15), p & 15, (p & 32) != 0};
+}
+
+// The same accessors over a shared-memory copy of the ctl words (gdn_ctl_stage, then a barrier): for kernels that
+// walk the entries one after another, so that no entry waits for a global load.
+constexpr int kGdnCtlWords = 2 + 3 * kGdnMaxRows;
+__device__ __forceinline__ void gdn_ctl_stage(const GdnArgs& A, int* cs) {
+    if (A.ctl != nullptr && threadIdx.x < kGdnCtlWords) cs[threadIdx.x] = __ldcg(A.ctl + threadIdx.x);
+}
+__device__ __forceinline__ int gdn_pending_s(const GdnArgs& A, const int* cs) {
+    if (A.ctl == nullptr) return 0;
+    const int n = cs[0];
+    return n < 0 ? 0 : (n > kGdnMaxRows ? kGdnMaxRows : n);
+}
+__device__ __forceinline__ int gdn_verify_entries_s(const GdnArgs& A, const int* cs) {
+    if (A.ctl == nullptr) return A.M;
+    int e = 0;
+    while (e < kGdnMaxRows) {
+        const int p = cs[2 + 2 * kGdnMaxRows + e];
+        if (p < 0 || (p & 15) >= A.M) break;
+        ++e;
+    }
+    return e;
+}
+__device__ __forceinline__ GdnEntry gdn_entry_s(const GdnArgs& A, const int* cs, int n, int e) {
+    if (e < n) return GdnEntry{e, -1, true};
+    if (A.ctl == nullptr) return GdnEntry{e, e, true};
+    const int p = cs[2 + 2 * kGdnMaxRows + (e - n)];
     return GdnEntry{n + (p & 15), p & 15, (p & 32) != 0};
 }
 
@@ -127,7 +155,7 @@ __device__ __forceinline__ void gdn_conv_item(const GdnArgs& A, int i) {
 #pragma unroll
             for (int d = 0; d < 4; ++d) sum = fmaf(hist[3 + t - d], w[3 - d], sum);
             const float y = bf16_round(sum);
-            A.conv_out[size_t(t) * A.C + i] = g_gdn_silu[f32_to_bf16_bits(y)];
+            A.conv_out[size_t(t) * A.C + i] = gdn_silu_bits(y);
         }
     }
     // the committed window after the replay: the three newest of (conv state, replayed inputs), oldest first
@@ -160,7 +188,7 @@ __device__ __forceinline__ void gdn_conv_item(const GdnArgs& A, int i) {
             sum = fmaf(v, w[3 - d], sum);
         }
         const float y = bf16_round(sum);
-        A.conv_out[size_t(n + t) * A.C + i] = g_gdn_silu[f32_to_bf16_bits(y)];
+        A.conv_out[size_t(n + t) * A.C + i] = gdn_silu_bits(y);
     }
     // the new conv state: the committed window (deferred form), or the three newest of (conv state, all M rows)
     // (committing form, n = 0: sequence position M + r, oldest first)

@@ -141,8 +141,6 @@ int fill_gdn_args(GdnArgs& A, const void* qkv, const void* z, const void* a, con
                   const void* prev_b, void* save_qkv, void* save_a, void* save_b, int64_t qkv_stride,
                   int64_t z_stride, int64_t ab_stride);
 int launch_gdn_step(GdnArgs A, void* ws, cudaStream_t stream);
-// Builds the GDN SiLU table of the current device once (synchronously; not inside a graph capture).
-int ensure_gdn_silu_lut(cudaStream_t stream);
 // a | b projection (gdn.cuh gdn_ab_column): out[m][n] for n < N, one warp per column
 int launch_gdn_ab(const uint16_t* x, int64_t x_stride, const uint16_t* w, int K, int M, int N, uint16_t* out,
                   int64_t out_stride, cudaStream_t stream);

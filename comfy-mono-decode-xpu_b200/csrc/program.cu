@@ -249,7 +249,10 @@ static __device__ __noinline__ void prog_gdn_delta(const GdnArgs& A, float* scra
     const int gc = c0 + cl;
     const bool active = gc < total;
     const int h0 = c0 / kDH, h1 = ((c0 + CPC < total ? c0 + CPC : total) - 1) / kDH, nhl = h1 - h0 + 1;
-    const int n = gdn_pending(A), R = n + A.M, KD = A.HK * kDH, grp = A.HV / A.HK;
+    __shared__ int cs[kGdnCtlWords];  // the ctl words, read once (the entry walk below reads them many times)
+    gdn_ctl_stage(A, cs);
+    consumer_sync<CW>();
+    const int n = gdn_pending_s(A, cs), R = n + A.M, KD = A.HK * kDH, grp = A.HV / A.HK;
     float* qn = scratch;                         // [2][kGdnMaxAll][kDH]
     float* kn = qn + 2 * kGdnMaxAll * kDH;       // [2][kGdnMaxAll][kDH]
     float* part = kn + 2 * kGdnMaxAll * kDH;     // [2][kRG][CPC]
@@ -296,9 +299,9 @@ static __device__ __noinline__ void prog_gdn_delta(const GdnArgs& A, float* scra
     float* p1 = part + kRG * CPC;
     if (active && rg == 0)  // rows no entry names read as zero (the entries below overwrite the others)
         for (int m = 0; m < A.M; ++m) A.core[size_t(m) * total + gc] = 0;
-    const int E = n + gdn_verify_entries(A);
+    const int E = n + gdn_verify_entries_s(A, cs);
     for (int e = 0; e < E; ++e) {
-        const GdnEntry en = gdn_entry(A, n, e);
+        const GdnEntry en = gdn_entry_s(A, cs, n, e);
         const int t = en.row;
         float mem = 0.f, decay = 1.f, beta = 0.f, v = 0.f;
         if (active) {
@@ -544,12 +547,6 @@ int launch_program(const Op* ops_host, const Op* ops_dev, int nops, int M, unsig
     MlpShape Z;
     const int c = program_shape(ops_host, nops, M, Z);
     MONO_CHECK(c >= 0, "program: not planned (mono_program_plan)");
-    for (int i = 0; i < nops; ++i)
-        if (ops_host[i].kind == OP_GDN_CONV || ops_host[i].kind == OP_GDN_DELTA || ops_host[i].kind == OP_ROWS) {
-            const int rc = ensure_gdn_silu_lut(stream);
-            if (rc != MONO_OK) return rc;
-            break;
-        }
     static_assert(sizeof(ProgParam) < 32000, "kernel parameter space");
     ProgParam G;
     std::memset(&G, 0, sizeof(G));
