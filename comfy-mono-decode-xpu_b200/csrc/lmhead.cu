@@ -27,7 +27,7 @@ namespace mono {
 constexpr int kLhWarps = 8, kLhMaxM = 8, kLhRows = 8, kLhChunk = 512;
 constexpr int kLhRowPitch = kLhChunk * 2 + 16;   // bytes per staged weight row (16-byte skew: conflict-free ldmatrix)
 constexpr int kLhStage = kLhRows * kLhRowPitch;  // one ring stage: 8 rows x 512 k
-constexpr size_t kLhSmemLimit = 227 * 1024 - 256;  // dynamic bytes: the opt-in maximum less the static ones
+constexpr size_t kLhSmemLimit = 227 * 1024 - 8 * 1024;  // dynamic bytes: the opt-in maximum less the static ones
 
 __device__ __forceinline__ void lh_mma(float (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
     // rows 8..15 of A are zero (a1 = a3 = 0): only rows 0..7, the x rows, carry data
@@ -54,6 +54,7 @@ struct LmHeadArgs {
     uint64_t* ws;             // the arrival counter (first 256 bytes), then [G][kLhMaxM][kTkK + 1] CTA lists
     int64_t x_stride, out_stride;  // out_stride: the logits' row stride (V for the pick)
     int K, V, M, k;
+    int ks;  // K slices per tile (1, 2, 4 or 8; lmhead_split)
 };
 
 size_t lmhead_workspace_bytes(int grid) { return size_t(grid) * kLhMaxM * (kTkK + 1) * 8 + 256; }
@@ -75,6 +76,7 @@ template <int S, bool PICK>
 __global__ void __launch_bounds__(kLhWarps * 32, 1) lmhead_pick_kernel(const LmHeadArgs A) {
     constexpr int NT = kLhWarps * 32;
     extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ float2 part[2][kLhWarps][32];  // the K slices' sums of a round (ks > 1), double-buffered
     __shared__ uint64_t finb[kLhWarps];
     __shared__ int last;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -90,15 +92,20 @@ __global__ void __launch_bounds__(kLhWarps * 32, 1) lmhead_pick_kernel(const LmH
     __syncwarp();
     pdl_launch_dependents();
     // this warp's tiles of 8 vocabulary rows: wg, wg + NW, ...; chunk q = (tile q / CPT, k chunk q % CPT)
-    const int CPT = A.K / kLhChunk;
+    // K split: warp w takes slice w % ks of tile w / ks of the CTA's round (8 / ks tiles a round); ks = 1 when the
+    // tiles outnumber the warps enough for an even load (lmhead_split)
+    const int ks = A.ks, TPR = kLhWarps / ks, CPT = A.K / kLhChunk, CPU = CPT / ks;
+    const int lt = warp / ks, sl = warp % ks;
     const int tiles = (A.V + kLhRows - 1) / kLhRows;
-    const int wg = int(blockIdx.x) * kLhWarps + warp, NW = int(gridDim.x) * kLhWarps;
-    const int mine = wg < tiles ? (tiles - 1 - wg) / NW + 1 : 0;
-    const int Q = mine * CPT;
+    const int G = int(gridDim.x), b = int(blockIdx.x), stride = G * TPR;
+    const int first = b * TPR + lt;  // this warp's tile in round 0
+    const int Rc = b * TPR < tiles ? (tiles - b * TPR + stride - 1) / stride : 0;  // the CTA's rounds
+    const int Rw = first < tiles ? (tiles - first + stride - 1) / stride : 0;      // rounds with a tile for this warp
+    const int Q = Rw * CPU;
     const uint64_t pol = l2_evict_first_policy();
     auto issue = [&](int q) {  // lane r < 8 copies row r of chunk q (1 KB) into stage q % S
-        const int tile = wg + (q / CPT) * NW, c = q - (q / CPT) * CPT;
-        const int n0 = tile * kLhRows, rows = min(kLhRows, A.V - n0);
+        const int r = q / CPU, c = sl * CPU + (q - r * CPU);
+        const int n0 = (first + r * stride) * kLhRows, rows = min(kLhRows, A.V - n0);
         uint64_t* bar = &bars[q % S];
         if (lane == 0) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the stage's earlier reads first
@@ -128,47 +135,62 @@ __global__ void __launch_bounds__(kLhWarps * 32, 1) lmhead_pick_kernel(const LmH
     // ldmatrix row addresses: W rows lane & 7 at k + 8 (lane >> 3); x rows likewise (past M: the zero row)
     const int lr = lane & 7, lk = 8 * (lane >> 3);
     const uint16_t* xrow = lr < A.M ? xs + size_t(lr) * pitch + lk : nullptr;
-    float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
     int q = 0;
-    for (; q < Q; ++q) {
-        if (!mbar_wait(&bars[q % S], uint32_t(q / S) & 1u)) break;
-        const int c = q % CPT;
-        const uint8_t* st = ring + (q % S) * kLhStage + lr * kLhRowPitch + lk * 2;
-        const int kx = c * kLhChunk;
+    bool bad = false;
+    for (int r = 0; r < Rc; ++r) {
+        float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+        if (r < Rw && !bad) {
+            for (int cc = 0; cc < CPU; ++cc, ++q) {
+                if (!mbar_wait(&bars[q % S], uint32_t(q / S) & 1u)) {
+                    bad = true;
+                    break;
+                }
+                const uint8_t* st = ring + (q % S) * kLhStage + lr * kLhRowPitch + lk * 2;
+                const int kx = (sl * CPU + cc) * kLhChunk;
 #pragma unroll 4
-        for (int kk = 0; kk < kLhChunk; kk += 32) {
-            uint32_t b[4], a[4];
-            lh_ldsm_x4(b, st + kk * 2);
-            lh_ldsm_x4(a, xrow ? xrow + kx + kk : zero16);
-            lh_mma(c0, a[0], a[1], b[0], b[1]);
-            lh_mma(c1, a[2], a[3], b[2], b[3]);
+                for (int kk = 0; kk < kLhChunk; kk += 32) {
+                    uint32_t bw[4], a[4];
+                    lh_ldsm_x4(bw, st + kk * 2);
+                    lh_ldsm_x4(a, xrow ? xrow + kx + kk : zero16);
+                    lh_mma(c0, a[0], a[1], bw[0], bw[1]);
+                    lh_mma(c1, a[2], a[3], bw[2], bw[3]);
+                }
+                __syncwarp();
+                if (q + S < Q) issue(q + S);
+            }
         }
-        __syncwarp();
-        if (q + S < Q) issue(q + S);
-        if (c == CPT - 1) {
-            // the tile's logits: token g (< M) at columns n0 + 2t, n0 + 2t + 1 (the two k-step chains summed in order)
-            const int n0 = (wg + (q / CPT) * NW) * kLhRows;
-            if (g < A.M) {
+        // the slice's sums (the two k-step chains added in order), then the ks slices of the tile in slice order
+        float v0 = c0[0] + c1[0], v1 = c0[1] + c1[1];
+        if (ks > 1) {
+            part[r & 1][warp][lane] = make_float2(v0, v1);
+            __syncthreads();  // (the other buffer is read before the next round's barrier: no second one needed)
+            if (sl == 0)
+                for (int j = 1; j < ks; ++j) {
+                    const float2 o = part[r & 1][warp + j][lane];
+                    v0 += o.x;
+                    v1 += o.y;
+                }
+        }
+        if (sl == 0 && r < Rw && g < A.M) {
+            // the tile's outputs: row g (< M) at columns n0 + 2t, n0 + 2t + 1
+            const int n0 = (first + r * stride) * kLhRows;
 #pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int n = n0 + 2 * t + e;
-                    if (n < A.V) {
-                        const uint16_t bits = __bfloat16_as_ushort(__float2bfloat16_rn(c0[e] + c1[e]));
-                        if (!PICK || A.logits) A.logits[int64_t(g) * A.out_stride + n] = bits;
-                        if constexpr (PICK) {
-                            if (A.k > 0) insert_rank(top, rank_topk(bits, uint32_t(n)), A.k);
-                            best = max(best, rank_argmax(bits, uint32_t(n)));
-                        }
+            for (int e = 0; e < 2; ++e) {
+                const int n = n0 + 2 * t + e;
+                if (n < A.V) {
+                    const uint16_t bits = __bfloat16_as_ushort(__float2bfloat16_rn(e ? v1 : v0));
+                    if (!PICK || A.logits) A.logits[int64_t(g) * A.out_stride + n] = bits;
+                    if constexpr (PICK) {
+                        if (A.k > 0) insert_rank(top, rank_topk(bits, uint32_t(n)), A.k);
+                        best = max(best, rank_argmax(bits, uint32_t(n)));
                     }
                 }
             }
-#pragma unroll
-            for (int i = 0; i < 4; ++i) c0[i] = c1[i] = 0.f;
         }
     }
-    if (q < Q) {
+    if (bad) {
         // a wait gave up (the error word is set): wait, bounded, for this warp's copies still in flight
-        for (int r = q + 1; r < Q && r < q + S; ++r) mbar_wait(&bars[r % S], uint32_t(r / S) & 1u);
+        for (int r2 = q + 1; r2 < Q && r2 < q + S; ++r2) mbar_wait(&bars[r2 % S], uint32_t(r2 / S) & 1u);
     }
     if constexpr (!PICK) return;
     __syncthreads();  // every ring is idle: its memory now holds the pick's lists
@@ -199,7 +221,6 @@ __global__ void __launch_bounds__(kLhWarps * 32, 1) lmhead_pick_kernel(const LmH
         __stcg(out + kTkK, b2);
     }
     __syncthreads();
-    const int G = int(gridDim.x);
     if (threadIdx.x == 0) {
         __threadfence();
         last = atomicAdd(counter, 1u) == unsigned(G - 1);
@@ -283,8 +304,29 @@ static int launch_lh(const LmHeadArgs& A, cudaStream_t stream) {
     return MONO_OK;
 }
 
+// K slices per tile: the fewest (1, 2, 4, 8 dividing the K chunks) whose rounds keep the warps busy within 2 % of
+// the best split; the matrices of the draft head have fewer 8-row tiles than the grid has warps, the lm_head many
+int lmhead_split(int V, int K) {
+    const int64_t tiles = (int64_t(V) + kLhRows - 1) / kLhRows, cpt = K / kLhChunk, G = sm_count();
+    int best = 1;
+    double best_eff = 0.0;
+    for (int ks = 1; ks <= kLhWarps; ks *= 2) {
+        if (cpt % ks) break;
+        const int64_t per_round = G * (kLhWarps / ks), rounds = (tiles + per_round - 1) / per_round;
+        const double eff = double(tiles) / double(rounds * per_round);
+        if (eff > best_eff + 0.02) {
+            best_eff = eff;
+            best = ks;
+        }
+    }
+    return best;
+}
+
 template <bool PICK>
-static int launch_lmhead_t(const LmHeadArgs& A, cudaStream_t stream) {
+static int launch_lmhead_t(LmHeadArgs A, cudaStream_t stream) {
+    // the pick over a vocabulary has tiles enough for every warp: no split (a split's per-round barrier measured
+    // slower there: 235 against 197 us)
+    A.ks = PICK ? 1 : lmhead_split(A.V, A.K);
     switch (lmhead_stages(A.M, A.K)) {
         case 4: return launch_lh<4, PICK>(A, stream);
         case 3: return launch_lh<3, PICK>(A, stream);
