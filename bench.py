@@ -319,6 +319,33 @@ def mlp_bytes(M, H, I):
     return 2 * w(I, H) + w(H, I) + H * 2 + M * H * 2 * 2
 
 
+MLP_PHASES = ("start", "dependency wait", "P1 rows + barrier + staging", "P2 gate/up consumed", "P2 epilogue",
+              "P2 barrier", "P3 re-quantization + barrier + staging", "P4 down consumed", "P4 epilogue")
+
+
+def mlp_phase_trace(launch, dev):
+    """One launch with the phase trace on (include/mono_b200.h mono_trace_enable): per phase boundary, the median
+    and the last CTA's time in us after the first CTA started."""
+    import numpy as np
+    import torch
+
+    from mono_b200 import _lib
+    nbytes = _lib.load().mono_trace_bytes()
+    buf = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize(dev)
+    _lib.call("mono_trace_enable", buf.data_ptr(), nbytes)
+    try:
+        launch()
+        torch.cuda.synchronize(dev)
+    finally:
+        _lib.call("mono_trace_enable", None, 0)
+    t = buf.view(torch.int64).view(1024, 16)[:, :len(MLP_PHASES)].cpu().numpy().astype(np.float64)
+    t = t[t[:, 0] > 0]
+    rel = (t - t[:, 0].min()) / 1000.0
+    return {name: {"median": round(float(np.median(rel[:, p])), 2), "last": round(float(rel[:, p].max()), 2)}
+            for p, name in enumerate(MLP_PHASES)}
+
+
 def run_mlp(args):
     """Config 1: the fused MLP block (RMSNorm -> gate/up -> SiLU*up -> requant -> down -> residual), M rows,
     hidden 4096, intermediate 12288; 4 weight copies (312 MB) cycled so every block streams from HBM."""
@@ -403,6 +430,8 @@ def run_mlp(args):
         f1.record(stream)
     stream.synchronize()
     e2e = world * n_e2e * b / (f0.elapsed_time(f1) * 1e-3) / 1e9
+    trace = mlp_phase_trace(lambda: _C.mlp_gptq(xd, nwd, 1e-6, *ws[0], silu_lut=lut, out=outs[0]), dev) \
+        if args.trace else None
     if rank == 0:
         print(json.dumps({
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -411,7 +440,8 @@ def run_mlp(args):
             "data": "synthetic (seeded, BASELINE configs[1] distributions)",
             "config": {"workload": f"fused W4A8 MLP block 4096->12288->4096, M={M} rows (configs[1])",
                        "blocks_per_step": per_step, "weight_copies": copies,
-                       "l2": "inputs larger than L2 (4 weight copies = 312 MB cycled)", "parity_gate": bool(ok)},
+                       "l2": "inputs larger than L2 (4 weight copies = 312 MB cycled)", "parity_gate": bool(ok),
+                       **({"phase_trace_us": trace} if trace else {})},
             "roofline": {"bound": "hbm", "achieved": round(b / (us * 1e-6) / 1e9, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(b / (us * 1e-6) / 1e9 / hbm, 4), "peak_source": src,
                          **traffic_fields("mlp_kernel_m8"), "kernel": "mlp_kernel<1,2>",
@@ -574,6 +604,18 @@ def run_decode(args):
     model = Qwen35W4A8(cfg, dev, prompt_len=prompt, gen_tokens=max(512, args.steps * 8 + 64), seed=0x5EED + 4 + rank,
                        fused=args.programs, prefetch=args.prefetch, draft_gemv=not args.cublas_draft)
     stream = torch.cuda.Stream(dev)
+    if args.profile_step:
+        # for ncu --profile-from-start off: warm steps, then one eager step between profiler start / stop
+        for _ in range(max(args.warmup, 3)):
+            model.step()
+        torch.cuda.synchronize(dev)
+        torch.cuda.profiler.start()
+        model.step()
+        torch.cuda.synchronize(dev)
+        torch.cuda.profiler.stop()
+        if rank == 0:
+            print(json.dumps({"profile_step": "one decode step profiled", "launches": model.own_launches_per_step()}))
+        return
     with Clocks(local) as clk:
         ms, toks, graphs = _decode_measure(model, stream, args.steps, args.warmup, world, dev)
     step_ms = ms / args.steps
@@ -823,6 +865,9 @@ def main():
     ap.add_argument("--rows", type=int, default=8, help="activation rows (tree-verify rows)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-second-prompt", action="store_true", help="decode: skip the prompt-4096 measurement")
+    ap.add_argument("--trace", action="store_true", help="mlp: add the fused kernel's phase trace to config")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="decode: run one eager step between cudaProfilerStart / Stop (for ncu --profile-from-start off)")
     ap.add_argument("--programs", action="store_true",
                     help="decode: run the verify body as layer programs (one persistent launch per run of layers) "
                          "instead of one launch per fused op")
