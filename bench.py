@@ -454,6 +454,85 @@ def run_mlp(args):
         dist.destroy_process_group()
 
 
+def run_lmhead(args):
+    """The bf16 lm_head pick alone (mono_lmhead_pick: the verify's greedy argmax at --rows rows, or a draft's top-2
+    pick at one row): 151,936 x 4096 bf16 weights (1.24 GB > L2) read once per call; the pick is checked against
+    the oracle on the kernel's own logits before timing."""
+    import numpy as np
+    import torch
+
+    from mono_b200 import _C
+    from oracle import lmhead as olh
+
+    V, K, M, per_step = 151936, 4096, args.rows, 8
+    k = 2 if M == 1 else 0
+    rank, world, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    g = torch.Generator(device=dev).manual_seed(0x5EED + 9 + rank)
+    w = (torch.randn(V, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    am, tk, lg = _C.lmhead_pick(x, w, k=k, logits=True)
+    lg_bits = lg.cpu().view(torch.int16).numpy().view(np.uint16)
+    am_ref, top_ref = olh.pick_logits(lg_bits, k)
+    ok = bool(np.array_equal(am.cpu().numpy(), am_ref) and (k == 0 or np.array_equal(tk.cpu().numpy(), top_ref)))
+    stream = torch.cuda.Stream(dev)
+
+    def step():
+        for _ in range(per_step):
+            _C.lmhead_pick(x, w, k=k)
+
+    with torch.cuda.stream(stream):
+        step()
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(stream)
+        stream.synchronize()
+    ms = e0.elapsed_time(e1)
+    b = V * K * 2 + M * K * 2
+    us = ms * 1e3 / (args.steps * per_step)
+    hbm, src = peaks()
+    # e2e: host rows in, the picked indices back, per call through the public op
+    hx = x.cpu().pin_memory()
+    ha = torch.empty(M, dtype=torch.int64).pin_memory()
+    n_e2e = 8
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        f0.record(stream)
+        for _ in range(n_e2e):
+            a2 = _C.lmhead_pick(hx.to(dev, non_blocking=True), w, k=k)[0]
+            ha.copy_(a2, non_blocking=True)
+        f1.record(stream)
+    stream.synchronize()
+    e2e_us = f0.elapsed_time(f1) * 1e3 / n_e2e
+    if rank == 0:
+        gbs = round(b / (us * 1e-6) / 1e9, 1)
+        print(json.dumps({
+            "metric": "lm_head pick GB/s (bf16 151936 x 4096, fused argmax / top-k)", "value": gbs, "unit": "GB/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 -> fp32 accumulate",
+            "data": "synthetic (seeded N(0, 0.02) weights, N(0, 1) rows)",
+            "config": {"workload": f"bf16 lm_head 151936 x 4096 + pick, M = {M} rows, k = {k}", "calls_per_step": per_step,
+                       "l2": "inputs larger than L2 (1.24 GB of weights)", "parity_gate": ok},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": round(gbs / hbm, 4),
+                         "peak_source": src, **traffic_fields("lmhead_pick_kernel_m8" if M > 1 else "lmhead_pick_kernel_m1"),
+                         "kernel": "lmhead_pick_kernel", "us_per_launch": round(us, 3), "algorithmic_bytes_per_launch": b},
+            "e2e": {"value": round(b / (e2e_us * 1e-6) / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": per_step * M * K * 2,
+                    "d2h_bytes_per_step": per_step * M * 8},
+            "gpu_launches": args.steps * per_step, "clocks": clk.summary()}))
+
+
 def run_topk_rows(args):
     """The verify sampling's top-k filter (the reference's topk_rows, csrc/topk_rows.sycl): exact top-64 of 8 fp32
     rows of 248,320 logits per call (the reference's "8 x 248k"); 32 input copies (254 MB) cycled so every call
@@ -860,7 +939,7 @@ def main():
     ap.add_argument("--steps", type=int, default=None, help="default: 200 (decode), 2000 (gemv, mlp)")
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["gemv", "mlp", "decode", "topk_rows"])
+    ap.add_argument("--workload", default="decode", choices=["gemv", "mlp", "decode", "topk_rows", "lmhead"])
     ap.add_argument("--prompt", type=int, default=1024, help="decode: committed prompt length (KV prefix)")
     ap.add_argument("--rows", type=int, default=8, help="activation rows (tree-verify rows)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
@@ -887,6 +966,8 @@ def main():
         run_decode(args)
     elif args.workload == "topk_rows":
         run_topk_rows(args)
+    elif args.workload == "lmhead":
+        run_lmhead(args)
     else:
         run_ours(args)
 
