@@ -62,28 +62,55 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
     const int rg = warp, col = cr * kDcCols + lane;
     const int kh = h / (A.HV / A.HK), KD = A.HK * kDH, M = A.M;
     const int n = gdn_pending_s(A, cs), R = n + M;
-    // sums of squares of q and k of the key head per row: (row, q or k) pairs over the 4 warps
-    for (int pr = warp; pr < 2 * R; pr += kRG) {
-        const int t = pr >> 1, which = pr & 1;
-        const float s = gdn_sumsq128(A.conv_out + size_t(t) * A.C + which * KD + kh * kDH, lane);
-        if (lane == 0) sums[pr] = s;
+    // The rows' q, k (key head kh, element tid) and v (this CTA's 32 columns) with every load issued before the
+    // first store: one L2 round trip, not one per row.
+    static_assert(kRG * kDcCols == kDH, "one thread per q / k element");
+    float qr[kGdnMaxAll], kr0[kGdnMaxAll], vr[kGdnMaxAll / kRG];
+#pragma unroll
+    for (int t = 0; t < kGdnMaxAll; ++t)
+        if (t < R) {
+            qr[t] = bf16_bits_to_f32(__ldcg(A.conv_out + size_t(t) * A.C + kh * kDH + tid));
+            kr0[t] = bf16_bits_to_f32(__ldcg(A.conv_out + size_t(t) * A.C + KD + kh * kDH + tid));
+        }
+#pragma unroll
+    for (int j = 0; j < kGdnMaxAll / kRG; ++j) {
+        const int t = warp + kRG * j;  // v rows of this warp: warp, warp + 4, ...
+        if (t < R) vr[j] = bf16_bits_to_f32(__ldcg(A.conv_out + size_t(t) * A.C + 2 * KD + h * kDH + cr * kDcCols + lane));
     }
+    const float g0 = tid < 2 * R ? __ldcg(A.gates + ((tid >> 1) * A.HV + h) * 2 + (tid & 1)) : 0.f;
     float st[kRPG];
     float* S = A.state + (size_t(h) * kDH + rg * kRPG) * kDH + col;
 #pragma unroll
     for (int r = 0; r < kRPG; ++r) st[r] = S[size_t(r) * kDH];
+#pragma unroll
+    for (int t = 0; t < kGdnMaxAll; ++t)
+        if (t < R) {
+            qn[t][tid] = qr[t];
+            kn[t][tid] = kr0[t];
+        }
+#pragma unroll
+    for (int j = 0; j < kGdnMaxAll / kRG; ++j)
+        if (warp + kRG * j < R) vsm[warp + kRG * j][lane] = vr[j];
+    if (tid < 2 * R) gsm[tid >> 1][tid & 1] = g0;
     __syncthreads();
-    for (int e = tid; e < R * kDH; e += blockDim.x) {
-        const int t = e / kDH, d = e % kDH;
-        const float qi = gdn_l2_inv(sums[2 * t]), ki = gdn_l2_inv(sums[2 * t + 1]);
-        qn[t][d] = (bf16_bits_to_f32(A.conv_out[size_t(t) * A.C + kh * kDH + d]) * A.qscale) * qi;
-        kn[t][d] = bf16_bits_to_f32(A.conv_out[size_t(t) * A.C + KD + kh * kDH + d]) * ki;
+    // sums of squares of q and k per row in gdn_sumsq128's order (lane l: elements l, l + 32, l + 64, l + 96, then
+    // the xor butterfly), (row, q or k) pairs over the 4 warps, read back from shared memory
+    for (int pr = warp; pr < 2 * R; pr += kRG) {
+        const float* src = (pr & 1) ? &kn[pr >> 1][0] : &qn[pr >> 1][0];
+        float sq = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sq = fmaf(src[lane + 32 * j], src[lane + 32 * j], sq);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        if (lane == 0) sums[pr] = sq;
     }
-    for (int e = tid; e < R * kDcCols; e += blockDim.x) {
-        const int t = e / kDcCols, c = e % kDcCols;
-        vsm[t][c] = bf16_bits_to_f32(A.conv_out[size_t(t) * A.C + 2 * KD + h * kDH + cr * kDcCols + c]);
-    }
-    if (tid < 2 * R) gsm[tid >> 1][tid & 1] = A.gates[((tid >> 1) * A.HV + h) * 2 + (tid & 1)];
+    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < kGdnMaxAll; ++t)
+        if (t < R) {
+            qn[t][tid] = (qr[t] * A.qscale) * gdn_l2_inv(sums[2 * t]);
+            kn[t][tid] = kr0[t] * gdn_l2_inv(sums[2 * t + 1]);
+        }
     for (int e = tid; e < M * kDcCols; e += blockDim.x) raw[e / kDcCols][e % kDcCols] = 0.f;  // rows no entry names
     __syncthreads();
     // the entries: the replayed rows (committing), then the verify program (gdn_entry)

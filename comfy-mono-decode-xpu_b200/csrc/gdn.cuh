@@ -105,43 +105,75 @@ __device__ __forceinline__ float pick(const float (&a)[N], int i) {
 // newest committed inputs (the replayed rows in the deferred form, all rows in the committing form). All
 // activations are read through L2 (they may have been written by this launch).
 __device__ __forceinline__ void gdn_conv_item(const GdnArgs& A, int i) {
-    const int n = gdn_pending(A), R = n + A.M;
-    uint16_t sa = 0, sb = 0;
+    // Loads in two round trips: the ctl words (pending count, slots, parents), then every input this item reads;
+    // no store before the last load (a load after a store the compiler cannot prove disjoint waits for it).
+    int n = 0, slot[kGdnMaxRows], par[kGdnMaxRows];
+    if (A.ctl != nullptr) {
+        int raw_n = __ldcg(A.ctl), raw_s[kGdnMaxRows], raw_p[kGdnMaxRows];
+#pragma unroll
+        for (int t = 0; t < kGdnMaxRows; ++t) {
+            raw_s[t] = __ldcg(A.ctl + 2 + t);
+            raw_p[t] = __ldcg(A.ctl + 2 + kGdnMaxRows + t);
+        }
+        n = raw_n < 0 ? 0 : (raw_n > kGdnMaxRows ? kGdnMaxRows : raw_n);
+#pragma unroll
+        for (int t = 0; t < kGdnMaxRows; ++t) {
+            slot[t] = raw_s[t] < 0 ? 0 : (raw_s[t] >= kGdnMaxRows ? kGdnMaxRows - 1 : raw_s[t]);
+            par[t] = t < A.M && raw_p[t] >= 0 && raw_p[t] < t ? raw_p[t] : -1;  // gdn_parent
+        }
+    } else {
+#pragma unroll
+        for (int t = 0; t < kGdnMaxRows; ++t) {
+            slot[t] = 0;
+            par[t] = t < A.M ? t - 1 : -1;
+        }
+    }
+    const int R = n + A.M;
     const bool saving = A.save_a != nullptr && i < A.M * A.HV;
+    const bool gating = i < R * A.HV;
+    const bool conv = i < A.C;
+    uint16_t sa = 0, sb = 0, ab = 0, bb = 0;
     if (saving) {
         const int t = i / A.HV, h = i % A.HV;
         sa = __ldcg(A.a + size_t(t) * A.ab_stride + h);
         sb = __ldcg(A.b + size_t(t) * A.ab_stride + h);
     }
-    if (i < R * A.HV) {
+    float dtb = 0.f, gdec = 0.f;
+    if (gating) {
         const int t = i / A.HV, h = i % A.HV;
-        const uint16_t ab = t < n ? __ldcg(A.prev_a + size_t(gdn_slot(A, t)) * A.HV + h) : __ldcg(A.a + size_t(t - n) * A.ab_stride + h);
-        const uint16_t bb = t < n ? __ldcg(A.prev_b + size_t(gdn_slot(A, t)) * A.HV + h) : __ldcg(A.b + size_t(t - n) * A.ab_stride + h);
-        const float av = bf16_bits_to_f32(ab) + A.dt_bias[h];
+        int st = 0;
+#pragma unroll
+        for (int u = 0; u < kGdnMaxRows; ++u)
+            if (u == t) st = slot[u];
+        ab = t < n ? __ldcg(A.prev_a + size_t(st) * A.HV + h) : __ldcg(A.a + size_t(t - n) * A.ab_stride + h);
+        bb = t < n ? __ldcg(A.prev_b + size_t(st) * A.HV + h) : __ldcg(A.b + size_t(t - n) * A.ab_stride + h);
+        dtb = A.dt_bias[h];
+        gdec = A.g_decay[h];
+    }
+    uint16_t rp[kGdnMaxRows], rv[kGdnMaxRows];  // raw inputs of the replayed rows / of the verify rows
+    float w[4], hist[3 + kGdnMaxRows], vr[kGdnMaxRows];
+    if (conv) {
+#pragma unroll
+        for (int t = 0; t < kGdnMaxRows; ++t) {
+            rp[t] = t < n ? __ldcg(A.prev_qkv + size_t(slot[t]) * A.C + i) : uint16_t(0);
+            rv[t] = t < A.M ? __ldcg(A.qkv + size_t(t) * A.qkv_stride + i) : uint16_t(0);
+        }
+#pragma unroll
+        for (int d = 0; d < 4; ++d) w[d] = bf16_bits_to_f32(A.conv_w[size_t(i) * 4 + d]);
+#pragma unroll
+        for (int r = 0; r < 3; ++r) hist[r] = bf16_bits_to_f32(A.conv_state[size_t(i) * 3 + r]);
+    }
+    if (gating) {
+        const float av = bf16_bits_to_f32(ab) + dtb;
         const float sp = av > 20.f ? av : logf(1.f + expf(av));
-        A.gates[i * 2] = expf(A.g_decay[h] * sp);
+        A.gates[i * 2] = expf(gdec * sp);
         A.gates[i * 2 + 1] = bf16_round(1.f / (1.f + expf(-bf16_bits_to_f32(bb))));
     }
     if (saving) {
         A.save_a[i] = sa;
         A.save_b[i] = sb;
     }
-    if (i >= A.C) return;
-    // every load first (the stores below may alias nothing the compiler can prove, so loads after a store
-    // would wait for it)
-    uint16_t rp[kGdnMaxRows], rv[kGdnMaxRows];  // raw inputs of the replayed rows / of the verify rows
-    float w[4], hist[3 + kGdnMaxRows], vr[kGdnMaxRows];
-    int par[kGdnMaxRows];
-#pragma unroll
-    for (int t = 0; t < kGdnMaxRows; ++t) {
-        rp[t] = t < n ? __ldcg(A.prev_qkv + size_t(gdn_slot(A, t)) * A.C + i) : uint16_t(0);
-        rv[t] = t < A.M ? __ldcg(A.qkv + size_t(t) * A.qkv_stride + i) : uint16_t(0);
-        par[t] = t < A.M ? gdn_parent(A, t) : -1;
-    }
-#pragma unroll
-    for (int d = 0; d < 4; ++d) w[d] = bf16_bits_to_f32(A.conv_w[size_t(i) * 4 + d]);
-#pragma unroll
-    for (int r = 0; r < 3; ++r) hist[r] = bf16_bits_to_f32(A.conv_state[size_t(i) * 3 + r]);
+    if (!conv) return;
     if (A.save_qkv != nullptr)
 #pragma unroll
         for (int t = 0; t < kGdnMaxRows; ++t)
