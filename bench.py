@@ -661,6 +661,89 @@ def _decode_measure(model, stream, steps, warmup, world, dev):
     return ms, toks, graphs
 
 
+def run_decode_tp(args):
+    """The decode step of ONE stream over `--gpus` ranks in tensor parallel (mono_b200.tp: column / row sharding,
+    an all-reduce of the [8, 4096] bf16 residual after every row-sharded projection, the vocabulary-sharded
+    lm_head with the merged pick). Reports the single stream's tok/s (strong scaling) and the measured latency of
+    one all-reduce of that size (a CUDA graph of 64)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from mono_b200 import mtp_loop
+    from mono_b200 import tp as tpm
+    from mono_b200.decoder import Qwen35Config
+
+    rank, world, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    cfg = Qwen35Config()
+    model = tpm.make_decoder(cfg, dev, dist.group.WORLD, args.prompt, gen_tokens=max(512, args.steps * 8 + 64))
+    stream = torch.cuda.Stream(dev)
+    with Clocks(local) as clk:
+        ms, toks, graphs = _decode_measure(model, stream, args.steps, args.warmup, world, dev)
+    toks //= world  # one stream: every rank counts the same tokens
+    del graphs
+    model.release_graphs()
+    # one all-reduce of the residual's size, 64 in a graph
+    buf = torch.zeros(8, cfg.hidden, dtype=torch.bfloat16, device=dev)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            dist.all_reduce(buf)
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for _ in range(64):
+            dist.all_reduce(buf)
+    g.replay()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(10):
+            g.replay()
+        e1.record(stream)
+    stream.synchronize()
+    ar_us, _ = reduce_time_and_count(e0.elapsed_time(e1) * 1e3 / 640, 0, dev, world)
+    del g
+    # e2e: the plugin's greedy loop, every rank in step (the same committed tokens on every rank)
+    mtp_loop.generate_device(model, 16)
+    torch.cuda.synchronize()
+    dist.barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    committed = mtp_loop.generate_device(model, args.steps)
+    f1.record()
+    torch.cuda.synchronize()
+    e2e_ms, _ = reduce_time_and_count(f0.elapsed_time(f1), 0, dev, world)
+    model.release_graphs()
+    step_bytes = model.step_bytes()
+    hbm, src = peaks()
+    step_ms = ms / args.steps
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": round(toks / (ms * 1e-3), 2), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (random-init Qwen3.5-9B-shaped W4A8 weights, random tokens, seeded)",
+            "config": {"workload": "Qwen3.5-9B-shaped W4A8 MTP decode (configs[4]), ONE stream in tensor parallel",
+                       "parallelism": f"tp{world}", "all_reduces_per_step": model.tp_reduces_per_step(),
+                       "all_reduce_us": round(ar_us, 2), "all_reduce_bytes": 8 * cfg.hidden * 2,
+                       "tokens_per_step": round(toks / args.steps, 3),
+                       "per_gpu_bytes_per_step": step_bytes},
+            "step_roofline": {"achieved": round(step_bytes / (step_ms * 1e-3) / 1e9, 1), "peak": hbm, "unit": "GB/s",
+                              "frac": round(step_bytes / (step_ms * 1e-3) / 1e9 / hbm, 4), "peak_source": src,
+                              "what": "one rank's shard per step"},
+            "e2e": {"value": round(len(committed) / (e2e_ms * 1e-3), 2), "unit": "tok/s",
+                    "path": "mono_b200.mtp_loop.generate_device on the sharded decoder"},
+            "gpu_launches": args.steps * model.own_launches_per_step(), "clocks": clk.summary()}), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def run_decode(args):
     """Config 4: the synthetic Qwen3.5-9B-shaped W4A8 decoder with the device MTP loop (the 8-node tree4s1m8 draft
     tree of depth 4 from the bf16 MTP head and bf16 lm_head, 8 verify rows, greedy accept), one stream per GPU.
@@ -945,6 +1028,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-second-prompt", action="store_true", help="decode: skip the prompt-4096 measurement")
     ap.add_argument("--trace", action="store_true", help="mlp: add the fused kernel's phase trace to config")
+    ap.add_argument("--tp", action="store_true",
+                    help="decode: one stream in tensor parallel over the --gpus ranks (mono_b200.tp) instead of replicas")
     ap.add_argument("--profile-step", action="store_true",
                     help="decode: run one eager step between cudaProfilerStart / Stop (for ncu --profile-from-start off)")
     ap.add_argument("--programs", action="store_true",
@@ -962,6 +1047,8 @@ def main():
         run_reference(args)
     elif args.workload == "mlp":
         run_mlp(args)
+    elif args.workload == "decode" and args.tp:
+        run_decode_tp(args)
     elif args.workload == "decode":
         run_decode(args)
     elif args.workload == "topk_rows":

@@ -53,6 +53,7 @@ struct LmHeadArgs {
     int64_t* dst;             // pick form: the verify-token row
     uint64_t* ws;             // the arrival counter (first 256 bytes), then [G][kLhMaxM][kTkK + 1] CTA lists
     int64_t x_stride, out_stride;  // out_stride: the logits' row stride (V for the pick)
+    int64_t index_base;            // the pick's index of row 0 of w (a vocabulary shard's offset; 0 otherwise)
     int K, V, M, k;
     int ks;  // K slices per tile (1, 2, 4 or 8; lmhead_split)
 };
@@ -181,8 +182,9 @@ __global__ void __launch_bounds__(kLhWarps * 32, 1) lmhead_pick_kernel(const LmH
                     const uint16_t bits = __bfloat16_as_ushort(__float2bfloat16_rn(e ? v1 : v0));
                     if (!PICK || A.logits) A.logits[int64_t(g) * A.out_stride + n] = bits;
                     if constexpr (PICK) {
-                        if (A.k > 0) insert_rank(top, rank_topk(bits, uint32_t(n)), A.k);
-                        best = max(best, rank_argmax(bits, uint32_t(n)));
+                        const uint32_t gi = uint32_t(A.index_base + n);  // ranked by the global index
+                        if (A.k > 0) insert_rank(top, rank_topk(bits, gi), A.k);
+                        best = max(best, rank_argmax(bits, gi));
                     }
                 }
             }
@@ -360,14 +362,16 @@ using namespace mono;
 extern "C" size_t mono_lmhead_workspace(void) { return lmhead_workspace_bytes(lmhead_grid()); }
 
 extern "C" int mono_lmhead_pick(const void* x, int64_t x_stride, const void* w, int64_t M, int64_t V, int64_t K, int64_t k,
-                                void* logits, int64_t* argmax, int64_t* topk, const int32_t* children, int64_t* dst,
-                                void* workspace, size_t workspace_bytes, mono_stream_t stream) {
+                                int64_t index_base, void* logits, int64_t* argmax, int64_t* topk,
+                                const int32_t* children, int64_t* dst, void* workspace, size_t workspace_bytes,
+                                mono_stream_t stream) {
     MONO_CHECK(x && w && workspace, "null operand");
     MONO_CHECK(M >= 1 && M <= kLhMaxM, "1 <= M <= %d rows", kLhMaxM);
     MONO_CHECK(k >= 0 && k <= kTkK, "0 <= k <= %d", kTkK);
     MONO_CHECK(K >= kLhChunk && K % kLhChunk == 0 && lmhead_stages(int(M), int(std::min<int64_t>(K, 1 << 20))) > 0,
                "K a multiple of 512 whose M x rows fit in shared memory beside the rings (K <= 4096 at M = 8)");
     MONO_CHECK(V >= 1 && V < (int64_t(1) << 31) && V * K < (int64_t(1) << 40), "1 <= V < 2^31");
+    MONO_CHECK(index_base >= 0 && index_base + V < (int64_t(1) << 31), "0 <= index_base, index_base + V < 2^31");
     MONO_CHECK(x_stride >= K && x_stride % 8 == 0 && aligned(x, 16) && aligned(w, 16),
                "x rows and w 16-byte aligned, x_stride a multiple of 8 elements");
     MONO_CHECK(argmax || (topk && k > 0) || logits || children, "no output requested");
@@ -386,6 +390,7 @@ extern "C" int mono_lmhead_pick(const void* x, int64_t x_stride, const void* w, 
     A.ws = static_cast<uint64_t*>(workspace);
     A.x_stride = x_stride;
     A.out_stride = V;
+    A.index_base = index_base;
     A.K = int(K);
     A.V = int(V);
     A.M = int(M);

@@ -661,11 +661,12 @@ def layer_gdn(x, norm_in, eps_in, qkv_w, z_w, wab, conv_w, conv_state, dt_bias, 
 _lmhead_ws = {}
 
 
-def lmhead_pick(x, w, k=0, logits=False, argmax_out=None, topk_out=None, children=None, dst=None):
+def lmhead_pick(x, w, k=0, logits=False, argmax_out=None, topk_out=None, children=None, dst=None, index_base=0):
     """bf16 lm_head of M <= 8 rows with the greedy / draft pick fused (include/mono_b200.h mono_lmhead_pick):
     x bf16 [M, K] (rows 16-byte aligned), w bf16 [V, K]. Returns (argmax int64 [M], top-k int64 [M, k] or None,
     logits bf16 [M, V] or None). With children (int32 device tensor of up to 8 slots, -1 ends) and dst (int64 device
-    row), also writes the draft pick into dst (M must be 1)."""
+    row), also writes the draft pick into dst (M must be 1). index_base: the vocabulary index of w's row 0 (a
+    tensor-parallel shard): ranks and returned indices are global."""
     _cuda(x, w)
     _check(x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1 and
            w.is_contiguous() and w.dim() == 2 and w.size(1) == x.size(1), "x bf16 [M, K], w bf16 [V, K]")
@@ -679,8 +680,8 @@ def lmhead_pick(x, w, k=0, logits=False, argmax_out=None, topk_out=None, childre
     need = _lib.load().mono_lmhead_workspace()
     ws = _workspace(_lmhead_ws, (x.device,), need, x.device)
     with torch.cuda.device(x.device):
-        _lib.call("mono_lmhead_pick", _p(x), x.stride(0), _p(w), M, V, K, k, _p(lg), _p(am), _p(tk), _p(children),
-                  _p(dst), _p(ws), need, _stream(x.device))
+        _lib.call("mono_lmhead_pick", _p(x), x.stride(0), _p(w), M, V, K, k, int(index_base), _p(lg), _p(am), _p(tk),
+                  _p(children), _p(dst), _p(ws), need, _stream(x.device))
     return am, tk, lg
 
 

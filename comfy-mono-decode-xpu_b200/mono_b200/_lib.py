@@ -56,7 +56,7 @@ SIGNATURES = {
                                    P, P, P, P, P, I64, I64, I64, P, SZ, P]),
     "mono_gemv_bf16": (I, [P, I64, P, I64, I64, I64, P, I64, P]),
     "mono_lmhead_workspace": (SZ, []),
-    "mono_lmhead_pick": (I, [P, I64, P, I64, I64, I64, I64, P, P, P, P, P, P, SZ, P]),
+    "mono_lmhead_pick": (I, [P, I64, P, I64, I64, I64, I64, I64, P, P, P, P, P, P, SZ, P]),
     "mono_topk_rows_workspace": (SZ, [I64, I64]),
     "mono_topk_rows": (I, [P, I, I64, I64, I64, P, P, P, SZ, P]),
     "mono_program_op_bytes": (SZ, []),

@@ -212,6 +212,19 @@ class Qwen35W4A8:
         self.fused, self.prefetch, self.draft_gemv = fused, prefetch, draft_gemv
         self.programs = self._build_programs() if fused else None
 
+    # ---- hooks of the tensor-parallel variant (mono_b200.tp): identities on one GPU --------------------------
+    def _residual(self, r):
+        """The residual a row-sharded projection adds: every rank but 0 adds none (None / False)."""
+        return r
+
+    def _reduce(self, t):
+        """The sum of a row-sharded projection's partial outputs over the ranks (in place)."""
+        return t
+
+    def _pick(self, xf, k, argmax_out=None, children=None, dst=None, node=0):
+        """The lm_head pick of the normed rows xf: the verify's argmax (argmax_out), or a draft's pick into dst."""
+        _C.lmhead_pick(xf, self.lm_head, k=k, argmax_out=argmax_out, children=children, dst=dst)
+
     def _t(self, name, layer, **tensors):
         if self.trace is not None:
             self.trace(name, layer, {k: v.clone() for k, v in tensors.items()})
@@ -231,8 +244,10 @@ class Qwen35W4A8:
                                   self.apos, c.eps, c.eps, c.rotary_dim)
         y = _C.attn_dpas(q, L["kc"], L["vc"], self.aseq, k, v.transpose(1, 2), self.mask[:M])
         x1 = _C.rowlin_gptq(y[0], _C.ROWLIN_GATE, [(L["o"], c.hidden)], gate=pre[:, hd:nq], gate_head_stride=2 * hd,
-                            lut=self.sig_lut, residual=x)
-        out = _C.mlp_gptq(x1, L["ln2"], c.eps, L["gate"], L["up"], L["down"], silu_lut=self.silu_lut, I=c.inter)
+                            lut=self.sig_lut, residual=self._residual(x))
+        x1 = self._reduce(x1)
+        out = self._reduce(_C.mlp_gptq(x1, L["ln2"], c.eps, L["gate"], L["up"], L["down"], silu_lut=self.silu_lut,
+                                       I=c.inter, residual=self._residual(True)))
         self._t("attn", i, x=x, pre=pre, q=q, k=k, kc=L["kc"], vc=L["vc"], y=y, x1=x1, out=out, freqs=freqs,
                 apos=self.apos, aseq=self.aseq)
         return out
@@ -250,8 +265,9 @@ class Qwen35W4A8:
         core = _C.gdn_step_deferred(pre[:, :Ck], pre[:, Ck:], ab[:, :HV], ab[:, HV:], L["conv_w"], L["conv_state"],
                                     L["dt_bias"], L["g_decay"],
                                     L["state"], L["gnorm"], c.eps, D ** -0.5, c.gdn_k_heads, self.ctl, prev, save)
-        x1 = _C.rowlin_gptq(core, _C.ROWLIN_QUANT, [(L["out"], c.hidden)], residual=x)
-        out = _C.mlp_gptq(x1, L["ln2"], c.eps, L["gate"], L["up"], L["down"], silu_lut=self.silu_lut, I=c.inter)
+        x1 = self._reduce(_C.rowlin_gptq(core, _C.ROWLIN_QUANT, [(L["out"], c.hidden)], residual=self._residual(x)))
+        out = self._reduce(_C.mlp_gptq(x1, L["ln2"], c.eps, L["gate"], L["up"], L["down"], silu_lut=self.silu_lut,
+                                       I=c.inter, residual=self._residual(True)))
         self._t("gdn", i, x=x, pre=pre, xn=xn, ab=ab, core=core, x1=x1, out=out, state=L["state"],
                 conv_state=L["conv_state"])
         return out
@@ -352,7 +368,7 @@ class Qwen35W4A8:
                 x = self._attention(L, x, freqs, i) if c.is_attn(i) else self._gdn(L, x, i)
         # final norm, then the bf16 lm_head with the greedy argmax fused (no logits written)
         xf = _C.rmsnorm_add(x, self.final_norm, c.eps)
-        _C.lmhead_pick(xf, self.lm_head, k=0, argmax_out=self.toks.view(-1))
+        self._pick(xf, 0, argmax_out=self.toks.view(-1))
         self._t("verify", -1, tokens=tokens, x=x, xf=xf, toks=self.toks)
         return self.toks, x
 
@@ -383,11 +399,11 @@ class Qwen35W4A8:
                                    self.mpos, c.eps, c.eps, c.rotary_dim)
         y = _C.attn_dpas(q, m["kc"], m["vc"], self.mseq, kk, v.transpose(1, 2), self.no_mask)
         yg = _C.lut_mul(y[0], qkv[:, hd:nq], self.sig_lut, b_head_stride=2 * hd)
-        xn, x = _C.rmsnorm_add(x, m["ln2"], c.eps, add=self._linear(yg, m["o"]))
+        xn, x = _C.rmsnorm_add(x, m["ln2"], c.eps, add=self._reduce(self._linear(yg, m["o"])))
         gu = self._linear(xn, m["gate_up"])
         h = _C.lut_mul(gu[:, c.inter:], gu[:, :c.inter], self.silu_lut)
-        xf, x = _C.rmsnorm_add(x, m["norm"], c.eps, add=self._linear(h, m["down"]))
-        _C.lmhead_pick(xf, self.lm_head, k=c.tree[k], children=self.children[8 * k:8 * k + 8], dst=self.drafts)
+        xf, x = _C.rmsnorm_add(x, m["norm"], c.eps, add=self._reduce(self._linear(h, m["down"])))
+        self._pick(xf, c.tree[k], children=self.children[8 * k:8 * k + 8], dst=self.drafts, node=k)
         self._t("draft", k, xf=xf, drafts=self.drafts)
         return x.view(1, 1, -1)
 

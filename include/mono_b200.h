@@ -318,14 +318,16 @@ MONO_API int mono_gemv_bf16(const void* x, int64_t x_stride, const void* w, int6
  *   topk[m][j]  j < k <= 8, descending by the top-k rank (the reference's fast_topk tie order)
  *   logits      (optional, NULL: not written) bf16 [M][V]
  * and, with children (device int32, up to 8 slots of dst, -1 ends) and dst (device int64), M == 1: dst[children[0]]
- * = argmax, dst[children[j]] = topk[j] for 1 <= j < k (the draft token and its siblings' tokens). K % 256 == 0,
- * K <= 8192;
+ * = argmax, dst[children[j]] = topk[j] for 1 <= j < k (the draft token and its siblings' tokens). index_base: the
+ * vocabulary index of w's row 0 (a tensor-parallel shard; 0 otherwise): ranks and written indices are
+ * index_base + row, so the shards' candidates merge into the whole vocabulary's pick. K % 512 == 0, M x rows of
+ * K fitting in shared memory next to the rings (K <= 4096 at M = 8);
  * workspace: mono_lmhead_workspace() bytes, zero-filled before first use (the kernel leaves it reusable); one call
  * at a time per workspace. */
 MONO_API size_t mono_lmhead_workspace(void);
 MONO_API int mono_lmhead_pick(const void* x, int64_t x_stride, const void* w, int64_t M, int64_t V, int64_t K, int64_t k,
-                              void* logits, int64_t* argmax, int64_t* topk, const int32_t* children, int64_t* dst,
-                              void* workspace, size_t workspace_bytes, mono_stream_t stream);
+                              int64_t index_base, void* logits, int64_t* argmax, int64_t* topk, const int32_t* children,
+                              int64_t* dst, void* workspace, size_t workspace_bytes, mono_stream_t stream);
 
 /* Exact top-k of a few long rows, k <= 64 (the reference's topk_rows, csrc/topk_rows.sycl:2-17: the verify
  * sampling's torch.topk(logits.float(), k)): per row the k largest by the radix key of the fp32 value (sign-flipped
