@@ -687,28 +687,33 @@ def run_decode_tp(args):
     toks //= world  # one stream: every rank counts the same tokens
     del graphs
     model.release_graphs()
-    # one all-reduce of the residual's size, 64 in a graph
+    # one all-reduce of the residual's size (the decoder's own, then NCCL's), 64 in a graph
     buf = torch.zeros(8, cfg.hidden, dtype=torch.bfloat16, device=dev)
-    with torch.cuda.stream(stream):
-        for _ in range(3):
-            dist.all_reduce(buf)
-    stream.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=stream):
-        for _ in range(64):
-            dist.all_reduce(buf)
-    g.replay()
-    torch.cuda.synchronize()
-    dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        e0.record(stream)
-        for _ in range(10):
-            g.replay()
-        e1.record(stream)
-    stream.synchronize()
-    ar_us, _ = reduce_time_and_count(e0.elapsed_time(e1) * 1e3 / 640, 0, dev, world)
-    del g
+
+    def per_call_us(fn):
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                fn(buf)
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for _ in range(64):
+                fn(buf)
+        g.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(10):
+                g.replay()
+            e1.record(stream)
+        stream.synchronize()
+        del g
+        return reduce_time_and_count(e0.elapsed_time(e1) * 1e3 / 640, 0, dev, world)[0]
+
+    ar_us = per_call_us(model._reduce)
+    nccl_us = per_call_us(lambda t: dist.all_reduce(t))
     # e2e: the plugin's greedy loop, every rank in step (the same committed tokens on every rank)
     mtp_loop.generate_device(model, 16)
     torch.cuda.synchronize()
@@ -723,6 +728,10 @@ def run_decode_tp(args):
     step_bytes = model.step_bytes()
     hbm, src = peaks()
     step_ms = ms / args.steps
+    ar_mode = "one-shot peer kernel (mono_allreduce2_bf16)" if model.peer_sum is not None else "NCCL"
+    torch.cuda.synchronize()
+    dist.barrier()
+    model.close()
     if rank == 0:
         print(json.dumps({
             "metric": METRIC, "value": round(toks / (ms * 1e-3), 2), "unit": "tok/s", "n_gpus": world,
@@ -731,7 +740,9 @@ def run_decode_tp(args):
             "data": "synthetic (random-init Qwen3.5-9B-shaped W4A8 weights, random tokens, seeded)",
             "config": {"workload": "Qwen3.5-9B-shaped W4A8 MTP decode (configs[4]), ONE stream in tensor parallel",
                        "parallelism": f"tp{world}", "all_reduces_per_step": model.tp_reduces_per_step(),
-                       "all_reduce_us": round(ar_us, 2), "all_reduce_bytes": 8 * cfg.hidden * 2,
+                       "all_reduce": ar_mode,
+                       "all_reduce_us": round(ar_us, 2), "nccl_all_reduce_us": round(nccl_us, 2),
+                       "all_reduce_bytes": 8 * cfg.hidden * 2,
                        "tokens_per_step": round(toks / args.steps, 3),
                        "per_gpu_bytes_per_step": step_bytes},
             "step_roofline": {"achieved": round(step_bytes / (step_ms * 1e-3) / 1e9, 1), "peak": hbm, "unit": "GB/s",

@@ -18,6 +18,7 @@ enum DeviceError : int {
     DEV_FLAG_TIMEOUT = 3,   // a flag wait (peer / producer) ran past its iteration limit
     DEV_BAD_POSITION = 4,   // a KV-cache position outside [0, capacity): the write was skipped
     DEV_BAD_TREE = 5,       // a children table entry not after its parent or not below rows: the accept walk stopped
+    DEV_PEER_TIMEOUT = 6,   // a wait for the peer GPU's arrival (two-GPU all-reduce) gave up
 };
 extern __device__ int g_device_error;
 

@@ -724,3 +724,46 @@ def topk_rows(x, k, index_order=False):
         _lib.call("mono_topk_rows", _p(x), flags, R, N, int(k), _p(values), _p(indices), _p(ws), nbytes,
                   _stream(x.device))
     return values, indices
+
+
+class PeerSum:
+    """The two-GPU one-shot all-reduce of bf16 rows (include/mono_b200.h mono_allreduce2_bf16) between this rank and
+    its peer: an area of this rank's memory (receive buffers + arrival counters) is mapped by the peer through CUDA
+    IPC. `exchange(handle: bytes) -> [handle of rank 0, handle of rank 1]` passes the handles (e.g. through
+    torch.distributed.all_gather_object); `peer` is the other rank's index. Calls sum in place; both ranks must make
+    the same calls in the same order."""
+
+    def __init__(self, device, cap, exchange, peer):
+        import ctypes
+        lib = _lib.load()
+        self.device, self.cap = torch.device(device), int(cap)
+        nbytes = lib.mono_allreduce2_area_bytes(self.cap)
+        area = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _lib.call("mono_p2p_area_alloc", nbytes, ctypes.byref(area))
+            self.area = area.value
+            h = (ctypes.c_char * 64)()
+            _lib.call("mono_ipc_handle", self.area, h, 64)
+            handles = exchange(bytes(h))
+            ph = (ctypes.c_char * 64).from_buffer_copy(handles[peer])
+            pp = ctypes.c_void_p()
+            _lib.call("mono_ipc_open", ph, 64, ctypes.byref(pp))
+            self.peer = pp.value
+        self.calls = torch.zeros(16, dtype=torch.int32, device=self.device)
+
+    def __call__(self, t):
+        _check(t.is_cuda and t.dtype == torch.bfloat16 and t.is_contiguous() and t.numel() <= self.cap,
+               "bf16 contiguous rows within the area's capacity")
+        with torch.cuda.device(t.device):
+            _lib.call("mono_allreduce2_bf16", _p(t), _p(t), t.numel(), self.area, self.peer, self.cap, _p(self.calls),
+                      _stream(t.device))
+        return t
+
+    def close(self):
+        with torch.cuda.device(self.device):
+            if self.peer:
+                _lib.call("mono_ipc_close", self.peer)
+                self.peer = None
+            if self.area:
+                _lib.call("mono_p2p_area_free", self.area)
+                self.area = None

@@ -57,6 +57,13 @@ SIGNATURES = {
     "mono_gemv_bf16": (I, [P, I64, P, I64, I64, I64, P, I64, P]),
     "mono_lmhead_workspace": (SZ, []),
     "mono_lmhead_pick": (I, [P, I64, P, I64, I64, I64, I64, I64, P, P, P, P, P, P, SZ, P]),
+    "mono_allreduce2_area_bytes": (SZ, [I64]),
+    "mono_p2p_area_alloc": (I, [SZ, P]),
+    "mono_p2p_area_free": (I, [P]),
+    "mono_ipc_handle": (I, [P, P, SZ]),
+    "mono_ipc_open": (I, [P, SZ, P]),
+    "mono_ipc_close": (I, [P]),
+    "mono_allreduce2_bf16": (I, [P, P, I64, P, P, I64, P, P]),
     "mono_topk_rows_workspace": (SZ, [I64, I64]),
     "mono_topk_rows": (I, [P, I, I64, I64, I64, P, P, P, SZ, P]),
     "mono_program_op_bytes": (SZ, []),

@@ -16,12 +16,16 @@ Sharding of the Qwen3.5 decode step over `world` ranks (one process per GPU, tor
     merged pick equals the pick over the whole vocabulary exactly (merge_pick)
   replicated: the embedding, the norms, the accept walk and its bookkeeping (every rank walks the same tokens)
 
-Numerics of the row-sharded projections: rank 0 adds the residual, every rank rounds its partial to bf16, the
-all-reduce sums the partials; the fused MLP quantizes h with the amax of its own I / W columns (a finer grid than
+The all-reduce: on two GPUs a one-shot kernel over NVLink peer memory (mono_allreduce2_bf16: each rank stores its
+partial into the peer's buffer, raises the peer's counter, waits for its own, sums; MONO_DECODE_XPU_TP_P2P = "0"
+uses NCCL instead). Numerics of the row-sharded projections: rank 0 adds the residual, every rank rounds its
+partial to bf16, the all-reduce sums the partials (fp32 sum of the two bf16 values, rounded once); the fused MLP quantizes h with the amax of its own I / W columns (a finer grid than
 the one-GPU model's). Against the one-GPU model the sharded outputs agree within a stated tolerance
 (tests/test_tp.py), not bit for bit; the vocabulary merge is exact.
 """
 from __future__ import annotations
+
+import os
 
 import torch
 
@@ -138,6 +142,19 @@ def make_decoder(cfg, device, group, prompt_len, gen_tokens=512, seed=0x5EED + 4
             v0, v1 = split_range(cfg.vocab, self.tp_rank, self.tp_world)
             self.lm_head = self.lm_head[v0:v1].contiguous()
             self.vocab_base = v0
+            # the residual sums: the one-shot peer kernel on two GPUs (MONO_DECODE_XPU_TP_P2P, "0": NCCL)
+            self.peer_sum = None
+            if self.tp_world == 2 and os.environ.get("MONO_DECODE_XPU_TP_P2P", "1") == "1":
+                def exchange(h):
+                    out = [None] * self.tp_world
+                    dist.all_gather_object(out, h, group=self.tp_group)
+                    return out
+                self.peer_sum = _C().PeerSum(device, 8 * cfg.hidden, exchange, 1 - self.tp_rank)
+
+        def close(self):
+            if self.peer_sum is not None:
+                self.peer_sum.close()
+                self.peer_sum = None
 
         def tp_reduces_per_step(self):
             """All-reduces of a step: two per layer, two per draft's MTP block."""
@@ -149,6 +166,8 @@ def make_decoder(cfg, device, group, prompt_len, gen_tokens=512, seed=0x5EED + 4
             return False if r is True else None
 
         def _reduce(self, t):
+            if self.peer_sum is not None:
+                return self.peer_sum(t)
             dist.all_reduce(t, group=self.tp_group)
             return t
 

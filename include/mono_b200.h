@@ -329,6 +329,24 @@ MONO_API int mono_lmhead_pick(const void* x, int64_t x_stride, const void* w, in
                               int64_t index_base, void* logits, int64_t* argmax, int64_t* topk, const int32_t* children,
                               int64_t* dst, void* workspace, size_t workspace_bytes, mono_stream_t stream);
 
+/* ---- two-GPU one-shot all-reduce (the tensor-parallel variant's residual sum) ------------------------------
+ * Each rank allocates an area of mono_allreduce2_area_bytes(cap) bytes with mono_p2p_area_alloc (its own
+ * cudaMalloc, zeroed: an IPC handle names a whole allocation), passes its handle (mono_ipc_handle, 64 bytes) to
+ * the peer, and maps the peer's (mono_ipc_open). mono_allreduce2_bf16 then sums the n bf16 values of `in` on both
+ * ranks into `out` (may be `in`): the chunk of CTA b is stored into the peer's area over NVLink, a release-add
+ * raises the peer's counter b, the CTA waits (acquire, bounded: 1 s, device error 6) for its own counter b, and
+ * writes bf16(float(in) + float(received)) — the same bits on both ranks. my_calls: a zeroed device int32 [16]
+ * of this rank (the call count per CTA: the kernel takes no host scalar and replays in CUDA graphs). Both ranks
+ * must make the same calls in the same order. n % 8 == 0, n <= cap. Plain peer stores and loads only. */
+MONO_API size_t mono_allreduce2_area_bytes(int64_t cap);
+MONO_API int mono_p2p_area_alloc(size_t bytes, void** ptr_out);
+MONO_API int mono_p2p_area_free(void* ptr);
+MONO_API int mono_ipc_handle(void* ptr, void* handle_out, size_t handle_bytes);
+MONO_API int mono_ipc_open(const void* handle, size_t handle_bytes, void** ptr_out);
+MONO_API int mono_ipc_close(void* ptr);
+MONO_API int mono_allreduce2_bf16(const void* in, void* out, int64_t n, void* my_area, void* peer_area, int64_t cap,
+                                  unsigned* my_calls, mono_stream_t stream);
+
 /* Exact top-k of a few long rows, k <= 64 (the reference's topk_rows, csrc/topk_rows.sycl:2-17: the verify
  * sampling's torch.topk(logits.float(), k)): per row the k largest by the radix key of the fp32 value (sign-flipped
  * bits: -0 below +0; rows holding NaN are not torch's order), sorted descending. Equal values come out in one of two
