@@ -774,8 +774,17 @@ def run_decode(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     cfg = Qwen35Config()
     prompt = args.prompt
-    model = Qwen35W4A8(cfg, dev, prompt_len=prompt, gen_tokens=max(512, args.steps * 8 + 64), seed=0x5EED + 4 + rank,
-                       fused=args.programs, prefetch=args.prefetch, draft_gemv=not args.cublas_draft)
+    B = args.streams
+
+    def make_model(plen):
+        if B > 1:  # batched streams: one weight stream a step for all of them (mono_b200.streams)
+            from mono_b200.streams import Qwen35W4A8Streams
+            return Qwen35W4A8Streams(cfg, dev, prompt_len=plen, streams=B, gen_tokens=max(512, args.steps * 8 + 64),
+                                     seed=0x5EED + 4 + rank, draft_gemv=not args.cublas_draft)
+        return Qwen35W4A8(cfg, dev, prompt_len=plen, gen_tokens=max(512, args.steps * 8 + 64), seed=0x5EED + 4 + rank,
+                          fused=args.programs, prefetch=args.prefetch, draft_gemv=not args.cublas_draft)
+
+    model = make_model(prompt)
     stream = torch.cuda.Stream(dev)
     if args.profile_step:
         # for ncu --profile-from-start off: warm steps, then one eager step between profiler start / stop
@@ -802,27 +811,30 @@ def run_decode(args):
     # timed region: the prompt's token ids copied host -> device (pinned) and seeding the loop (the prefill itself is
     # left to stock, as in the reference), and the committed tokens read back.
     from mono_b200 import mtp_loop
-    prompt_ids = torch.randint(0, cfg.vocab, (prompt,), generator=torch.Generator().manual_seed(rank)).pin_memory()
-    dev_ids = torch.empty(prompt, dtype=torch.int64, device=dev)
+    prompt_ids = torch.randint(0, cfg.vocab, (B, prompt), generator=torch.Generator().manual_seed(rank)).pin_memory()
+    dev_ids = torch.empty(B, prompt, dtype=torch.int64, device=dev)
+    gen = (lambda n: mtp_loop.generate_device(model, n)) if B == 1 else \
+        (lambda n: mtp_loop.generate_device_streams(model, n))
     with torch.cuda.stream(stream):
-        mtp_loop.generate_device(model, 16)  # captures the loop's graphs (outside the timing)
+        gen(16)  # captures the loop's graphs (outside the timing)
     stream.synchronize()
     n_new = max(64, args.steps)
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         f0.record(stream)
         dev_ids.copy_(prompt_ids, non_blocking=True)
-        model.next_tok.view(-1).copy_(dev_ids[-1:])
-        committed = mtp_loop.generate_device(model, n_new)
+        model.next_tok.view(-1).copy_(dev_ids[:, -1])
+        committed = gen(n_new)
         f1.record(stream)
     stream.synchronize()
-    e2e_steps = -(-n_new // 8) * 8  # whole rings of 8 steps (about one token per step)
-    e2e_ms, e2e_toks = reduce_time_and_count(f0.elapsed_time(f1), len(committed), dev, world)
+    n_committed = len(committed) if B == 1 else sum(len(c) for c in committed)
+    e2e_steps = -(-n_new // 8) * 8  # whole rings of 8 steps (about one token per step and stream)
+    e2e_ms, e2e_toks = reduce_time_and_count(f0.elapsed_time(f1), n_committed, dev, world)
     model.release_graphs()
     # the dominant kernel alone (the fused MLP block): a graph of its launches over the layers' weights at the
     # step's 8 verify rows, averaged per launch with CUDA events
     import mono_b200._C as C_
-    R = model.tree["rows"]
+    R = model.tree["rows"] * B  # the verify rows of all streams
     xs = torch.randn(R, cfg.hidden, device=dev).to(torch.bfloat16)
     outs = torch.empty_like(xs)
     with torch.cuda.stream(stream):
@@ -851,8 +863,7 @@ def run_decode(args):
     if prompt != 4096 and not args.no_second_prompt:
         del model
         torch.cuda.empty_cache()
-        m2 = Qwen35W4A8(cfg, dev, prompt_len=4096, gen_tokens=max(512, args.steps * 8 + 64), seed=0x5EED + 4 + rank,
-                        fused=args.programs, prefetch=args.prefetch, draft_gemv=not args.cublas_draft)
+        m2 = make_model(4096)
         steps2 = max(10, args.steps // 2)
         ms2, toks2, g2 = _decode_measure(m2, stream, steps2, args.warmup, world, dev)
         del g2
@@ -868,7 +879,9 @@ def run_decode(args):
             "data": "synthetic (random-init Qwen3.5-9B-shaped W4A8 weights, random tokens, seeded)",
             "config": {"workload": f"Qwen3.5-9B-shaped W4A8 MTP decode (configs[4]): 8-node tree4s1m8 draft tree of "
                                    f"depth 4 (bf16 MTP head, bf16 lm_head), 8 verify rows, greedy accept, prompt {prompt}, "
-                                   "1 stream per GPU",
+                                   + ("1 stream per GPU" if B == 1 else
+                                      f"{B} streams per GPU batched in one step ({R} verify rows)"),
+                       "streams_per_gpu": B,
                        "layers": cfg.layers, "steps_per_s": round(args.steps / (ms * 1e-3), 2),
                        "tokens_per_step": round(toks / (args.steps * world), 3),
                        "tokens_per_step_note": "random-init weights: the drafts rarely match the verify (about one "
@@ -879,10 +892,11 @@ def run_decode(args):
                        "draft_projections": "cuBLAS (F.linear)" if args.cublas_draft else "mono_gemv_bf16",
                        "lm_head": "mono_lmhead_pick (bf16 GEMV with the argmax / top-2 pick fused), verify and drafts",
                        "prompt_4096": p4096,
-                       "parallelism": f"independent streams x{world}"},
+                       "parallelism": f"independent streams x{world * B} ({B} per GPU)"},
             "roofline": {"bound": "hbm", "achieved": round(mlp_b / (mlp_us * 1e-6) / 1e9, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(mlp_b / (mlp_us * 1e-6) / 1e9 / hbm, 4), "peak_source": src,
-                         **traffic_fields("mlp_kernel_m8"),
+                         **(traffic_fields("mlp_kernel_m8") if R == 8 else
+                            {"traffic": None, "traffic_source": f"no ncu capture at M = {R} committed"}),
                          "kernel": f"mlp_kernel (fused MLP block, the step's dominant W4A8 kernel), M = {R} verify rows",
                          "us_per_launch": round(mlp_us, 3), "algorithmic_bytes_per_launch": mlp_b},
             "step_roofline": {"achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
@@ -890,10 +904,11 @@ def run_decode(args):
                               "what": "whole step: W4 body + bf16 lm_head (verify and 4 drafts) + bf16 MTP block x 4 + "
                                       "GDN states + KV"},
             "e2e": {"value": round(e2e_toks / (e2e_ms * 1e-3), 2), "unit": "tok/s",
-                    "h2d_bytes_per_step": round(prompt * 8 / e2e_steps, 1), "d2h_bytes_per_step": 32 * 8,
-                    "path": "mono_b200.mtp_loop.generate_device (the _generate_mtp install point's greedy loop)",
-                    "copies": f"h2d: the prompt's {prompt} token ids (pinned) once per generate; d2h: a 256-byte "
-                              "result row per step, read in rings of 8"},
+                    "h2d_bytes_per_step": round(B * prompt * 8 / e2e_steps, 1), "d2h_bytes_per_step": B * 32 * 8,
+                    "path": ("mono_b200.mtp_loop.generate_device (the _generate_mtp install point's greedy loop)"
+                             if B == 1 else "mono_b200.mtp_loop.generate_device_streams (every stream's greedy loop)"),
+                    "copies": f"h2d: the {B} prompts' {prompt} token ids (pinned) once per generate; d2h: a "
+                              f"{B * 256}-byte block of result rows per step, read in rings of 8"},
             "gpu_launches": args.steps * model.own_launches_per_step(), "clocks": clk.summary()}
         if cpu is not None:
             line["cpu_baseline"] = cpu
@@ -1036,6 +1051,8 @@ def main():
     ap.add_argument("--workload", default="decode", choices=["gemv", "mlp", "decode", "topk_rows", "lmhead"])
     ap.add_argument("--prompt", type=int, default=1024, help="decode: committed prompt length (KV prefix)")
     ap.add_argument("--rows", type=int, default=8, help="activation rows (tree-verify rows)")
+    ap.add_argument("--streams", type=int, default=1,
+                    help="decode: independent streams per GPU batched in one step (2: 16 verify rows)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-second-prompt", action="store_true", help="decode: skip the prompt-4096 measurement")
     ap.add_argument("--trace", action="store_true", help="mlp: add the fused kernel's phase trace to config")

@@ -3,6 +3,7 @@
 #include <mutex>
 #include <string>
 
+#include "gdn.cuh"
 #include "launch.h"
 
 namespace mono {
@@ -91,6 +92,8 @@ int fill_gdn_args(GdnArgs& A, const void* qkv, const void* z, const void* a, con
     A.C = int(C);
     A.HK = int(HK);
     A.HV = int(HV);
+    A.streams = 1;
+    A.ctl_stride = 0;
     const size_t rows = size_t(M) + 8;
     A.conv_out = static_cast<uint16_t*>(workspace);
     A.gates = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + (rows * C * 2 + 255) / 256 * 256);
@@ -280,9 +283,20 @@ int mono_qk_norm_rope_kv(const void* rawq, int64_t q_row_stride, int64_t q_head_
                          const float* freqs, void* key_cache, void* value_cache, int64_t cap, const int64_t* position,
                          int64_t S, int64_t Hq, int64_t Hk, float epsq, float epsk, int64_t rd, void* out_q,
                          void* out_k, mono_stream_t stream) {
+    return mono_qk_norm_rope_kv_streams(rawq, q_row_stride, q_head_stride, rawk, k_row_stride, v, v_row_stride, wq, wk,
+                                        freqs, key_cache, value_cache, cap, position, S, 1, Hq, Hk, epsq, epsk, rd,
+                                        out_q, out_k, stream);
+}
+
+int mono_qk_norm_rope_kv_streams(const void* rawq, int64_t q_row_stride, int64_t q_head_stride, const void* rawk,
+                                 int64_t k_row_stride, const void* v, int64_t v_row_stride, const void* wq,
+                                 const void* wk, const float* freqs, void* key_cache, void* value_cache, int64_t cap,
+                                 const int64_t* position, int64_t S, int64_t streams, int64_t Hq, int64_t Hk,
+                                 float epsq, float epsk, int64_t rd, void* out_q, void* out_k, mono_stream_t stream) {
     MONO_CHECK(rawq && rawk && v && wq && wk && freqs && key_cache && value_cache && position && out_q && out_k,
                "null operand");
-    MONO_CHECK(S >= 1 && S <= 8, "1 <= S <= 8 decode rows (got %lld)", (long long)S);
+    MONO_CHECK(streams >= 1 && streams <= 8 && S % streams == 0 && S / streams >= 1 && S / streams <= 8,
+               "1 <= streams <= 8 of 1 <= S / streams <= 8 decode rows each (S = %lld)", (long long)S);
     MONO_CHECK(Hq >= 1 && Hk >= 1 && Hq <= 1024 && Hk <= 1024, "head counts");
     MONO_CHECK(rd >= 2 && rd <= 256 && rd % 2 == 0, "even rotary dimension in [2, 256] (got %lld)", (long long)rd);
     MONO_CHECK(cap >= 1 && epsq > 0.f && epsk > 0.f, "positive capacity and eps");
@@ -316,24 +330,37 @@ int mono_qk_norm_rope_kv(const void* rawq, int64_t q_row_stride, int64_t q_head_
     A.rd = int(rd);
     A.epsq = epsq;
     A.epsk = epsk;
+    A.streams = int(streams);
     return launch_qk_norm_rope_kv(A, reinterpret_cast<cudaStream_t>(stream));
 }
 
-size_t mono_tree_attention_workspace(int64_t Hk, int64_t cap) {
-    if (Hk < 1 || cap < 1) return 0;
-    return attn_workspace_bytes(int(Hk), int(cap), sm_count());
+size_t mono_tree_attention_workspace(int64_t Hk, int64_t cap) { return mono_tree_attention_streams_workspace(Hk, 1, cap); }
+
+size_t mono_tree_attention_streams_workspace(int64_t Hk, int64_t streams, int64_t cap) {
+    if (Hk < 1 || cap < 1 || streams < 1 || streams > 8) return 0;
+    return attn_workspace_bytes(int(Hk * streams), int(streams), int(cap), sm_count());
 }
 
 int mono_tree_attention(const void* q, const void* key_cache, const void* value_cache, const int32_t* seqlen,
                         const void* xk, const void* xv, const int32_t* mask, int64_t H, int64_t Hk, int64_t S,
                         int64_t cap, void* out, void* workspace, size_t workspace_bytes, mono_stream_t stream) {
+    return mono_tree_attention_streams(q, key_cache, value_cache, seqlen, xk, xv, mask, H, Hk, S, 1, cap, out,
+                                       workspace, workspace_bytes, stream);
+}
+
+int mono_tree_attention_streams(const void* q, const void* key_cache, const void* value_cache, const int32_t* seqlen,
+                                const void* xk, const void* xv, const int32_t* mask, int64_t H, int64_t Hk, int64_t S,
+                                int64_t streams, int64_t cap, void* out, void* workspace, size_t workspace_bytes,
+                                mono_stream_t stream) {
     MONO_CHECK(q && key_cache && value_cache && seqlen && out && workspace, "null operand");
+    MONO_CHECK(streams >= 1 && streams <= 8, "1 <= streams <= 8");
     MONO_CHECK(S >= 1 && S <= 8 && Hk >= 1 && H % Hk == 0 && (H / Hk) * S <= 32,
                "1..8 rows, H a multiple of Hk, (H / Hk) * S <= 32 query rows per kv head");
     MONO_CHECK(mask != nullptr || S == 1, "a tree mask for S > 1 rows (S = 1 without a mask: the draft row)");
     MONO_CHECK(mask == nullptr || (xk && xv), "tree rows need xk / xv");
     MONO_CHECK(cap >= 1 && cap <= (int64_t(1) << 30), "cache capacity");
-    MONO_CHECK(workspace_bytes >= mono_tree_attention_workspace(Hk, cap), "workspace too small (mono_tree_attention_workspace)");
+    MONO_CHECK(workspace_bytes >= mono_tree_attention_streams_workspace(Hk, streams, cap),
+               "workspace too small (mono_tree_attention_streams_workspace)");
     const void* ptrs[] = {q, key_cache, value_cache, out, workspace};
     for (const void* ptr : ptrs) MONO_CHECK(aligned(ptr, 16), "16-byte aligned operands");
     AttnArgs A{};
@@ -345,16 +372,22 @@ int mono_tree_attention(const void* q, const void* key_cache, const void* value_
     A.xv = static_cast<const uint16_t*>(xv);
     A.mask = mask;
     A.out = static_cast<uint16_t*>(out);
-    A.H = int(H);
-    A.Hk = int(Hk);
+    A.H = int(H * streams);
+    A.Hk = int(Hk * streams);
     A.S = int(S);
     A.cap = int(cap);
+    A.streams = int(streams);
     return launch_tree_attention(A, workspace, reinterpret_cast<cudaStream_t>(stream));
 }
 
 size_t mono_gdn_step_workspace(int64_t M, int64_t C, int64_t HV) {
     if (M < 1 || C < 1 || HV < 1) return 0;
-    return gdn_workspace_bytes(int(M), int(C), int(HV));
+    return gdn_workspace_bytes(int(M), int(C), int(HV), 1);
+}
+
+size_t mono_gdn_step_streams_workspace(int64_t M, int64_t C, int64_t HV, int64_t streams) {
+    if (M < 1 || C < 1 || HV < 1 || streams < 1 || streams > 8) return 0;
+    return gdn_workspace_bytes(int(M), int(C), int(HV), int(streams));
 }
 
 static int gdn_step_impl(const void* qkv, const void* z, const void* a, const void* b, const void* conv_w,
@@ -362,12 +395,19 @@ static int gdn_step_impl(const void* qkv, const void* z, const void* a, const vo
                          float gnorm_eps, float qscale, int64_t M, int64_t HK, int64_t HV, void* core, void* workspace,
                          size_t workspace_bytes, const int32_t* ctl, const void* prev_qkv, const void* prev_a,
                          const void* prev_b, void* save_qkv, void* save_a, void* save_b, int64_t qkv_stride,
-                         int64_t z_stride, int64_t ab_stride, mono_stream_t stream) {
+                         int64_t z_stride, int64_t ab_stride, mono_stream_t stream, int64_t streams = 1,
+                         int64_t ctl_stride = 0) {
+    MONO_CHECK(streams >= 1 && streams <= 8, "1 <= streams <= 8");
+    MONO_CHECK(streams == 1 || ctl == nullptr || ctl_stride >= kGdnCtlWords, "ctl rows of %d words", kGdnCtlWords);
+    MONO_CHECK(workspace_bytes >= mono_gdn_step_streams_workspace(M, (2 * HK + HV) * 128, HV, streams),
+               "workspace too small (mono_gdn_step_streams_workspace)");
     GdnArgs A;
     const int rc = fill_gdn_args(A, qkv, z, a, b, conv_w, conv_state, dt_bias, g_decay, state, gnorm_w, gnorm_eps, qscale,
                                  M, HK, HV, core, workspace, workspace_bytes, ctl, prev_qkv, prev_a, prev_b, save_qkv,
                                  save_a, save_b, qkv_stride, z_stride, ab_stride);
     if (rc != MONO_OK) return rc;
+    A.streams = int(streams);
+    A.ctl_stride = int(ctl_stride);
     return launch_gdn_step(A, workspace, reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -391,6 +431,20 @@ int mono_gdn_step_deferred(const void* qkv, const void* z, const void* a, const 
     return gdn_step_impl(qkv, z, a, b, conv_w, conv_state, dt_bias, g_decay, state, gnorm_w, gnorm_eps, qscale, M, HK,
                          HV, core, workspace, workspace_bytes, ctl, prev_qkv, prev_a, prev_b, save_qkv, save_a, save_b,
                          qkv_stride, z_stride, ab_stride, stream);
+}
+
+int mono_gdn_step_deferred_streams(const void* qkv, const void* z, const void* a, const void* b, const void* conv_w,
+                                   void* conv_state, const float* dt_bias, const float* g_decay, float* state,
+                                   const void* gnorm_w, float gnorm_eps, float qscale, int64_t M, int64_t HK,
+                                   int64_t HV, int64_t streams, void* core, const int32_t* ctl, int64_t ctl_stride,
+                                   const void* prev_qkv, const void* prev_a, const void* prev_b, void* save_qkv,
+                                   void* save_a, void* save_b, int64_t qkv_stride, int64_t z_stride, int64_t ab_stride,
+                                   void* workspace, size_t workspace_bytes, mono_stream_t stream) {
+    MONO_CHECK(ctl && prev_qkv && prev_a && prev_b && save_qkv && save_a && save_b, "deferred form: ctl, prev and save buffers");
+    MONO_CHECK(prev_qkv != save_qkv && prev_a != save_a && prev_b != save_b, "save buffers must not alias the replayed ones");
+    return gdn_step_impl(qkv, z, a, b, conv_w, conv_state, dt_bias, g_decay, state, gnorm_w, gnorm_eps, qscale, M, HK,
+                         HV, core, workspace, workspace_bytes, ctl, prev_qkv, prev_a, prev_b, save_qkv, save_a, save_b,
+                         qkv_stride, z_stride, ab_stride, stream, streams, ctl_stride);
 }
 
 size_t mono_topk_workspace(int64_t rows) { return rows < 1 ? 0 : topk_workspace_bytes(rows); }

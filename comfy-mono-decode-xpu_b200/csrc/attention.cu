@@ -9,20 +9,30 @@
 // (positions outside [0, cap) are skipped and recorded in the device error word).
 //
 // Tree attention (the role of csrc/attn_dpas.sycl:269-342): q rows of one kv head (groups x S <= 32) attend
-// the committed prefix [0, L) of the bf16 cache plus the tree rows their mask admits.
-//   Kernel 1, CTA = (kv head, context chunk): 64-token tiles of K and V staged in shared memory, S = Q K^T and
-//   O += P V on the tensor cores (mma.sync m16n8k16 bf16, fp32 accumulation; P rounded to bf16 for P V), an
-//   online softmax per row; the chunk's unnormalized O, running max and sum go to the workspace.
-//   Kernel 2, CTA = (q head, row): merge of the active chunks and of the admitted tree rows (fp32 scores over
-//   the head dimension), one bf16 rounding of the output.
+// the committed prefix [0, L) of the bf16 cache plus the tree rows their mask admits. One launch:
+//   CTA = (kv head, context chunk), chunks in clusters of 8 CTAs: 64-token tiles of K and V staged in shared
+//   memory, S = Q K^T and O += P V on the tensor cores (mma.sync m16n8k16 bf16, fp32 accumulation; P rounded to
+//   bf16 for P V), an online softmax per row; the chunk's unnormalized O, running max and sum stay in the CTA's
+//   shared memory.
+//   Cluster merge: after a cluster barrier, warp w of cluster rank j merges row 4 j + w over the 8 chunks of
+//   the cluster, reading the peers' shared memory (rank order; fp32).
+//   Cross-cluster merge (only when the context spans more than one cluster): each cluster writes its merged
+//   rows to the workspace; per (kv head, rank) the last arriving CTA merges the clusters in cluster order.
+//   The merged row then takes the admitted tree rows (fp32 scores over the head dimension) and is rounded
+//   once to bf16.
 // Chunks follow the actual length L read on the device: per = max(ceil(L / chunks), 64) tokens rounded up to
-// the tile, active = ceil(L / per); CTAs past the last active chunk exit.
+// the tile, active = ceil(L / per); clusters past the last active chunk exit at once, inactive chunks of a
+// live cluster contribute an empty partial.
+#include <cooperative_groups.h>
+
 #include <cmath>
 #include <mutex>
 
 #include "launch.h"
 
 namespace mono {
+
+namespace cg = cooperative_groups;
 
 constexpr int kHD = 256;
 
@@ -33,13 +43,15 @@ __global__ void __launch_bounds__(32) qk_norm_rope_kv_kernel(const NormRopeArgs 
     __shared__ __align__(16) uint16_t nrm[kHD];
     const int lane = threadIdx.x;
     const int s = blockIdx.x / (A.Hq + 2 * A.Hk), h = blockIdx.x % (A.Hq + 2 * A.Hk);
+    // batched streams: rows [b R, (b + 1) R) are stream b's, its caches are kv heads [b Hk, (b + 1) Hk)
+    const int R = A.S / A.streams, b = s / R, sr = s % R;
     const int64_t p = A.pos[s];
     const bool pos_ok = p >= 0 && p < A.cap;
     if (!pos_ok && lane == 0) set_device_error(DEV_BAD_POSITION);
     if (h >= A.Hq + A.Hk) {  // v: cache write only
         const int hv = h - A.Hq - A.Hk;
         if (pos_ok)
-            reinterpret_cast<uint4*>(A.vc + (size_t(hv) * A.cap + p) * kHD)[lane] =
+            reinterpret_cast<uint4*>(A.vc + (size_t(b * A.Hk + hv) * A.cap + p) * kHD)[lane] =
                 reinterpret_cast<const uint4*>(A.v + size_t(s) * A.vs + size_t(hv) * kHD)[lane];
         return;
     }
@@ -86,10 +98,10 @@ __global__ void __launch_bounds__(32) qk_norm_rope_kv_kernel(const NormRopeArgs 
     }
     const uint4 out = make_uint4(ou[0], ou[1], ou[2], ou[3]);
     if (isq) {
-        reinterpret_cast<uint4*>(A.oq + (size_t(hh) * A.S + s) * kHD)[lane] = out;
+        reinterpret_cast<uint4*>(A.oq + (size_t(b * A.Hq + hh) * R + sr) * kHD)[lane] = out;
     } else {
-        reinterpret_cast<uint4*>(A.ok + (size_t(hh) * A.S + s) * kHD)[lane] = out;
-        if (pos_ok) reinterpret_cast<uint4*>(A.kc + (size_t(hh) * A.cap + p) * kHD)[lane] = out;
+        reinterpret_cast<uint4*>(A.ok + (size_t(b * A.Hk + hh) * R + sr) * kHD)[lane] = out;
+        if (pos_ok) reinterpret_cast<uint4*>(A.kc + (size_t(b * A.Hk + hh) * A.cap + p) * kHD)[lane] = out;
     }
 }
 
@@ -106,7 +118,39 @@ constexpr int kAttRows = 32;              // q rows per kv head (groups x S), pa
 constexpr int kQPitch = kHD + 8;          // bf16 elements per staged row (16-byte skew: conflict-free ldmatrix)
 constexpr int kPPitch = kAttTile + 8;
 constexpr int kAttThreads = 128;
+constexpr int kAttCluster = 8;            // chunk CTAs per cluster; 4 warps x 8 CTAs = the 32 rows
+constexpr int kOPitch = kHD + 8;          // fp32 elements per row of a CTA's partial O in shared memory
 
+__device__ __forceinline__ void cluster_arrive_release() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+// the shared::cluster address of p (this CTA's shared memory) in cluster CTA `rank`, and loads from it
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, int rank) {
+    uint32_t a;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
+    return a;
+}
+__device__ __forceinline__ float4 ld_cluster_v4(uint32_t a) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ float2 ld_cluster_v2(uint32_t a) {
+    float2 v;
+    asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
 
 __device__ __forceinline__ void attn_chunking(int L, int chunks, int& per, int& active) {
     per = (L + chunks - 1) / chunks;
@@ -134,7 +178,65 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], 
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-__global__ void __launch_bounds__(kAttThreads) attn_partial_kernel(const AttnArgs A) {
+__device__ __forceinline__ void unpack8(const uint4 v, float (&f)[8]) {
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        f[2 * j] = __uint_as_float(u[j] << 16);
+        f[2 * j + 1] = __uint_as_float(u[j] & 0xFFFF0000u);
+    }
+}
+
+// One warp finishes row r of kv head kh (q head kh * groups + r / S, tree row r % S); lane l holds dims
+// [8 l, 8 l + 8) of the merged prefix (acc unnormalized, running max M, sum). The admitted tree rows follow in
+// row order (score = q . xk / 16 over the head dimension: lane sums in dim order, xor butterfly 16 .. 1), then
+// out = bf16(acc / sum).
+__device__ __forceinline__ void attn_finish_row(const AttnArgs& A, int kh, int r, int lane, float (&acc)[8], float M,
+                                                float sum) {
+    const int groups = A.H / A.Hk, h = kh * groups + r / A.S, s = r % A.S;
+    if (A.mask != nullptr) {
+        const int mk = A.mask[s];
+        float qf[8];
+        unpack8(reinterpret_cast<const uint4*>(A.q + (size_t(h) * A.S + s) * kHD)[lane], qf);
+        uint4 kx[8], vx[8];
+#pragma unroll
+        for (int tr = 0; tr < 8; ++tr)
+            if (tr < A.S) {  // every tree row, not only the admitted ones: no wait on the mask word
+                kx[tr] = reinterpret_cast<const uint4*>(A.xk + (size_t(kh) * A.S + tr) * kHD)[lane];
+                vx[tr] = reinterpret_cast<const uint4*>(A.xv + (size_t(kh) * A.S + tr) * kHD)[lane];
+            }
+#pragma unroll
+        for (int tr = 0; tr < 8; ++tr) {
+            if (!(tr < A.S && ((mk >> tr) & 1))) continue;
+            float kf[8], vf[8];
+            unpack8(kx[tr], kf);
+            unpack8(vx[tr], vf);
+            float v = 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v += qf[j] * kf[j];
+#pragma unroll
+            for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            const float sc = v * 0.0625f;
+            const float M2 = fmaxf(M, sc);
+            const float fp = M == -INFINITY ? 0.f : expf(M - M2), ft = expf(sc - M2);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] = acc[j] * fp + ft * vf[j];
+            sum = sum * fp + ft;
+            M = M2;
+        }
+    }
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float lo = sum > 0.f ? acc[2 * j] / sum : 0.f, hi = sum > 0.f ? acc[2 * j + 1] / sum : 0.f;
+        o[j] = uint32_t(f32_to_bf16_bits(lo)) | (uint32_t(f32_to_bf16_bits(hi)) << 16);
+    }
+    const int Hs = A.H / A.streams, b = h / Hs;  // stream b's output rows [b S, (b + 1) S) of Hs heads
+    reinterpret_cast<uint4*>(A.out + ((size_t(b) * A.S + s) * Hs + h % Hs) * kHD)[lane] =
+        make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+__global__ void __cluster_dims__(kAttCluster, 1, 1) __launch_bounds__(kAttThreads) attn_kernel(const AttnArgs A) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint16_t* Qs = reinterpret_cast<uint16_t*>(smem);               // [32][kQPitch]
     uint16_t* Ks = Qs + kAttRows * kQPitch;                         // [64][kQPitch]
@@ -143,21 +245,34 @@ __global__ void __launch_bounds__(kAttThreads) attn_partial_kernel(const AttnArg
     float* red = reinterpret_cast<float*>(Ps + kAttRows * kPPitch);  // [4 warps][32 rows]
     const int chunk = blockIdx.x, kh = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
-    const int L = clamp_len(A.seqlen[0], A.cap);
+    const int L = clamp_len(A.seqlen[kh / (A.Hk / A.streams)], A.cap);
     int per, active;
     attn_chunking(L, A.chunks, per, active);
-    if (chunk >= active) return;
+    const int parts = active > 0 ? active : 1;  // L = 0: cluster 0 still writes the tree rows' outputs
+    const int live = (parts + kAttCluster - 1) / kAttCluster, cg0 = chunk / kAttCluster;
+    if (cg0 >= live) return;  // the whole cluster: no chunk of it has work
     const int groups = A.H / A.Hk, R = groups * A.S;
     const int t0 = chunk * per, t1 = (t0 + per < L) ? t0 + per : L;
-    // Q rows r = gi * S + s of q head kh * groups + gi; rows >= R are zero
-    for (int i = tid; i < kAttRows * (kHD / 8); i += kAttThreads) {
-        const int r = i / (kHD / 8), c = i % (kHD / 8);
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (r < R) {
-            const int gi = r / A.S, s = r % A.S;
-            v = reinterpret_cast<const uint4*>(A.q + (size_t(kh * groups + gi) * A.S + s) * kHD)[c];
+    {  // the rows a merging warp finishes (q row, tree rows' k and v: 128-byte lines) into L2 ahead of use
+        const int r = (chunk % kAttCluster) * 4 + warp;
+        if (r < R && A.mask != nullptr) {
+            const int h = kh * groups + r / A.S, s = r % A.S;
+            const int lines = 4 * (1 + 2 * A.S);
+            for (int i = lane; i < lines; i += 32) {
+                const int row = i >> 2, part = (i & 3) * 64;
+                const uint16_t* base = row == 0 ? A.q + (size_t(h) * A.S + s) * kHD
+                                     : (row <= A.S ? A.xk : A.xv) + (size_t(kh) * A.S + (row - 1) % A.S) * kHD;
+                prefetch_l2(base + part);
+            }
         }
-        reinterpret_cast<uint4*>(Qs + r * kQPitch)[c] = v;
+    }
+    // Q rows r = gi * S + s of q head kh * groups + gi, rows >= R zero (the copies join the first tile's group)
+    for (int i = tid; chunk < active && i < kAttRows * (kHD / 8); i += kAttThreads) {
+        const int r = i / (kHD / 8), c = i % (kHD / 8);
+        if (r < R)
+            cp_async16(Qs + r * kQPitch + c * 8, A.q + (size_t(kh * groups + r / A.S) * A.S + r % A.S) * kHD + c * 8);
+        else
+            reinterpret_cast<uint4*>(Qs + r * kQPitch)[c] = make_uint4(0, 0, 0, 0);
     }
     float O[2][8][4];
 #pragma unroll
@@ -305,96 +420,160 @@ __global__ void __launch_bounds__(kAttThreads) attn_partial_kernel(const AttnArg
             lrun[rr] = lrun[rr] * scale_old[rr] + sum;
         }
     }
-    // the chunk's unnormalized O, max and sum
-    const size_t unit = size_t(kh) * A.chunks + chunk;
-    float* po = A.part + unit * kAttRows * kHD;
+    // the chunk's unnormalized O, max and sum into this CTA's shared memory, over the K / V tiles (every warp
+    // is past its last P V read)
+    float* Op = reinterpret_cast<float*>(Ks);  // [32][kOPitch]
+    float* Ml = Op + kAttRows * kOPitch;       // [32][2]
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
             const int col = warp * 64 + nt * 8 + 2 * t;
-            *reinterpret_cast<float2*>(po + (mt * 16 + g) * kHD + col) = make_float2(O[mt][nt][0], O[mt][nt][1]);
-            *reinterpret_cast<float2*>(po + (mt * 16 + 8 + g) * kHD + col) = make_float2(O[mt][nt][2], O[mt][nt][3]);
+            *reinterpret_cast<float2*>(Op + (mt * 16 + g) * kOPitch + col) = make_float2(O[mt][nt][0], O[mt][nt][1]);
+            *reinterpret_cast<float2*>(Op + (mt * 16 + 8 + g) * kOPitch + col) = make_float2(O[mt][nt][2], O[mt][nt][3]);
         }
     if (warp == 0 && t == 0)
 #pragma unroll
         for (int rr = 0; rr < 4; ++rr) {
             const int row = (rr >> 1) * 16 + (rr & 1) * 8 + g;
-            A.ml[(unit * kAttRows + row) * 2] = mrun[rr];
-            A.ml[(unit * kAttRows + row) * 2 + 1] = lrun[rr];
+            Ml[row * 2] = mrun[rr];
+            Ml[row * 2 + 1] = lrun[rr];
         }
-}
-
-// CTA = (q head h, row s), thread = head dim d.
-__global__ void __launch_bounds__(kHD) attn_merge_kernel(const AttnArgs A) {
-    __shared__ float red[kHD / 32];
-    const int d = threadIdx.x, h = blockIdx.x / A.S, s = blockIdx.x % A.S;
-    const int groups = A.H / A.Hk, kh = h / groups, r = (h % groups) * A.S + s;
-    const int L = clamp_len(A.seqlen[0], A.cap);
-    int per, active;
-    attn_chunking(L, A.chunks, per, active);
-    float M = -INFINITY;
-    for (int c = 0; c < active; ++c) M = fmaxf(M, A.ml[((size_t(kh) * A.chunks + c) * kAttRows + r) * 2]);
-    float acc = 0.f, sum = 0.f;
-    for (int c = 0; c < active; ++c) {
-        const size_t u = (size_t(kh) * A.chunks + c) * kAttRows + r;
-        const float w = expf(A.ml[u * 2] - M);
-        sum += A.ml[u * 2 + 1] * w;
-        acc += A.part[u * kHD + d] * w;
-    }
-    if (A.mask != nullptr) {
-        const int mk = A.mask[s];
-        const float qd = bf16_bits_to_f32(A.q[(size_t(h) * A.S + s) * kHD + d]);
-        for (int tr = 0; tr < A.S; ++tr) {
-            if (!((mk >> tr) & 1)) continue;
-            float v = qd * bf16_bits_to_f32(A.xk[(size_t(kh) * A.S + tr) * kHD + d]);
+    cluster_arrive_release();
+    cluster_wait_acquire();  // every chunk's partial of the cluster is written
+    // cluster merge: warp w of cluster rank j takes row r = 4 j + w; lane l dims [8 l, 8 l + 8)
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = int(cluster.block_rank()), r = rank * 4 + warp;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float M = -INFINITY, sum = 0.f;
+    if (r < R) {
+        float mc[kAttCluster], lc[kAttCluster];
+        float4 oc[kAttCluster][2];
 #pragma unroll
-            for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            __syncthreads();
-            if ((d & 31) == 0) red[d >> 5] = v;
-            __syncthreads();
-            float sc = 0.f;
+        for (int c = 0; c < kAttCluster; ++c) {
+            const float2 ml2 = ld_cluster_v2(cluster_addr(Ml + r * 2, c));
+            const uint32_t oa = cluster_addr(Op + r * kOPitch + 8 * lane, c);
+            mc[c] = ml2.x;
+            lc[c] = ml2.y;
+            oc[c][0] = ld_cluster_v4(oa);
+            oc[c][1] = ld_cluster_v4(oa + 16);
+        }
 #pragma unroll
-            for (int w = 0; w < kHD / 32; ++w) sc += red[w];
-            sc *= 0.0625f;
-            const float M2 = fmaxf(M, sc);
-            const float fp = M == -INFINITY ? 0.f : expf(M - M2), ft = expf(sc - M2);
-            acc = acc * fp + ft * bf16_bits_to_f32(A.xv[(size_t(kh) * A.S + tr) * kHD + d]);
-            sum = sum * fp + ft;
-            M = M2;
+        for (int c = 0; c < kAttCluster; ++c) M = fmaxf(M, mc[c]);
+#pragma unroll
+        for (int c = 0; c < kAttCluster; ++c) {
+            const float w = mc[c] == -INFINITY ? 0.f : expf(mc[c] - M);
+            sum += lc[c] * w;
+            const float o8[8] = {oc[c][0].x, oc[c][0].y, oc[c][0].z, oc[c][0].w,
+                                 oc[c][1].x, oc[c][1].y, oc[c][1].z, oc[c][1].w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] += o8[j] * w;
         }
     }
-    A.out[(size_t(s) * A.H + h) * kHD + d] = f32_to_bf16_bits(sum > 0.f ? acc / sum : 0.f);
+    cluster_arrive_release();  // this CTA is done with the peers' shared memory
+    if (live == 1) {
+        if (r < R) attn_finish_row(A, kh, r, lane, acc, M, sum);
+    } else {
+        // cross-cluster merge: clusters write their merged rows; per (kv head, rank) the last arriving CTA merges
+        // the live clusters in cluster order
+        __shared__ int last;
+        const size_t G = size_t(A.chunks / kAttCluster);
+        if (r < R) {
+            const size_t u = (size_t(kh) * G + cg0) * kAttRows + r;
+            float4* gp = reinterpret_cast<float4*>(A.part + u * kHD) + 2 * lane;
+            gp[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            gp[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+            if (lane == 0) {
+                A.ml[u * 2] = M;
+                A.ml[u * 2 + 1] = sum;
+            }
+        }
+        __syncthreads();
+        if (tid == 0) {
+            // acq_rel: releases the CTA's rows (ordered before by the barrier) and, for the last arrival, acquires
+            // every other cluster's
+            unsigned* cnt = A.count + kh * kAttCluster + rank;
+            const unsigned prev = atom_add_acq_rel_gpu(cnt, 1u);
+            last = prev == unsigned(live - 1);
+            if (last) *cnt = 0u;  // every live cluster has arrived: zero for the next launch
+        }
+        __syncthreads();
+        if (last && r < R) {
+            // lane c holds cluster c's (max, sum) (live <= 32 clusters: attn_chunks); the rows
+            // are loaded four clusters at a time, merged in cluster order
+            const size_t u0 = size_t(kh) * G * kAttRows + r;
+            float mc = -INFINITY, lc = 0.f;
+            if (lane < live) {
+                mc = __ldcg(A.ml + (u0 + size_t(lane) * kAttRows) * 2);
+                lc = __ldcg(A.ml + (u0 + size_t(lane) * kAttRows) * 2 + 1);
+            }
+            M = mc;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+            const float wl = mc == -INFINITY ? 0.f : expf(mc - M);
+            sum = 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+            for (int c0 = 0; c0 < live; c0 += 4) {
+                float4 a[4], b[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    if (c0 + q < live) {
+                        const float4* gp = reinterpret_cast<const float4*>(A.part + (u0 + size_t(c0 + q) * kAttRows) * kHD) + 2 * lane;
+                        a[q] = __ldcg(gp);
+                        b[q] = __ldcg(gp + 1);
+                    }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float w = __shfl_sync(0xffffffffu, wl, (c0 + q) & 31);
+                    const float l = __shfl_sync(0xffffffffu, lc, (c0 + q) & 31);
+                    if (c0 + q >= live) continue;
+                    sum += l * w;
+                    const float o8[8] = {a[q].x, a[q].y, a[q].z, a[q].w, b[q].x, b[q].y, b[q].z, b[q].w};
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) acc[j] += o8[j] * w;
+                }
+            }
+            attn_finish_row(A, kh, r, lane, acc, M, sum);
+        }
+    }
+    cluster_wait_acquire();  // the peers are done with this CTA's shared memory
 }
 
 size_t attn_smem_bytes() {
     return size_t(kAttRows + 2 * kAttTile) * kQPitch * 2 + size_t(kAttRows) * kPPitch * 2 + 4 * 32 * 4;
 }
+static_assert(size_t(kAttRows) * kOPitch * 4 + kAttRows * 2 * 4 <= size_t(2 * kAttTile) * kQPitch * 2,
+              "the partial O fits over the K / V tiles");
 int attn_chunks(int Hk, int cap, int sms) {
-    // about two CTAs per SM at the longest context the cache holds, at least one tile per chunk
+    // about two CTAs per SM at the longest context the cache holds, at least one tile per chunk, whole clusters
     int chunks = (2 * sms + Hk - 1) / Hk;
     const int tiles = (cap + kAttTile - 1) / kAttTile;
-    return chunks < tiles ? chunks : (tiles > 0 ? tiles : 1);
+    if (tiles < chunks) chunks = tiles > 0 ? tiles : 1;
+    if (chunks > 32 * kAttCluster) chunks = 32 * kAttCluster;  // the cross-cluster merge holds one cluster per lane
+    return (chunks + kAttCluster - 1) / kAttCluster * kAttCluster;
 }
-size_t attn_workspace_bytes(int Hk, int cap, int sms) {
-    const size_t chunks = attn_chunks(Hk, cap, sms);
-    return size_t(Hk) * chunks * kAttRows * (kHD + 2) * 4;
+// chunks follow one stream's kv heads: a batched stream is split exactly as it would be alone
+size_t attn_workspace_bytes(int Hk, int streams, int cap, int sms) {
+    const size_t clusters = attn_chunks(Hk / streams, cap, sms) / kAttCluster;
+    return size_t(Hk) * clusters * kAttRows * (kHD + 2) * 4 + size_t(Hk) * kAttCluster * 4;
 }
 
 int launch_tree_attention(AttnArgs A, void* ws, cudaStream_t stream) {
-    A.chunks = attn_chunks(A.Hk, A.cap, sm_count());
+    A.chunks = attn_chunks(A.Hk / A.streams, A.cap, sm_count());
+    const size_t G = size_t(A.chunks / kAttCluster);
     A.part = static_cast<float*>(ws);
-    A.ml = A.part + size_t(A.Hk) * A.chunks * kAttRows * kHD;
+    A.ml = A.part + size_t(A.Hk) * G * kAttRows * kHD;
+    A.count = reinterpret_cast<unsigned*>(A.ml + size_t(A.Hk) * G * kAttRows * 2);
+    MONO_CHECK(G <= 32, "at most 32 clusters of context chunks per kv head (got %d)", int(G));
     const size_t smem = attn_smem_bytes();
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(once, [&] {
-        attr_err = cudaFuncSetAttribute(attn_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        attr_err = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     });
     CUDA_TRY(attr_err);
-    attn_partial_kernel<<<dim3(A.chunks, A.Hk), kAttThreads, smem, stream>>>(A);
-    CUDA_TRY(cudaGetLastError());
-    attn_merge_kernel<<<A.H * A.S, kHD, 0, stream>>>(A);
+    attn_kernel<<<dim3(A.chunks, A.Hk), kAttThreads, smem, stream>>>(A);
     CUDA_TRY(cudaGetLastError());
     return MONO_OK;
 }

@@ -42,6 +42,13 @@ __device__ __forceinline__ void trace_stamp(int phase) {
     if (tr != nullptr && threadIdx.x == 0 && blockIdx.x < kTraceCtas && phase < kTracePhases)
         tr[blockIdx.x * kTracePhases + phase] = globaltimer();
 }
+// the same for a two-dimensional grid: slot = blockIdx.y * gridDim.x + blockIdx.x
+__device__ __forceinline__ void trace_stamp_2d(int phase) {
+    unsigned long long* tr = g_trace;
+    const unsigned slot = blockIdx.y * gridDim.x + blockIdx.x;
+    if (tr != nullptr && threadIdx.x == 0 && slot < kTraceCtas && phase < kTracePhases)
+        tr[slot * kTracePhases + phase] = globaltimer();
+}
 
 // ---- shared-memory addresses ---------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

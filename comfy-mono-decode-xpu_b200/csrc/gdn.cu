@@ -33,7 +33,32 @@ namespace cg = cooperative_groups;
 
 constexpr int kConvThreads = 64;  // 128 CTAs over the 8192 channels of the 9B model: one per SM, not 32
 
-__global__ void __launch_bounds__(kConvThreads) gdn_conv_kernel(const GdnArgs A) {
+// Stream b's view of a batched call's operands (the layout of GdnArgs::streams).
+__device__ __forceinline__ GdnArgs gdn_stream(const GdnArgs& A0, int b) {
+    GdnArgs A = A0;
+    const size_t rows = size_t(b) * A.M, wrows = size_t(b) * (A.M + kGdnMaxRows);
+    A.qkv += rows * A.qkv_stride;
+    A.z += rows * A.z_stride;
+    A.a += rows * A.ab_stride;
+    A.b += rows * A.ab_stride;
+    A.core += rows * A.HV * kDH;
+    A.conv_state += size_t(b) * A.C * 3;
+    A.state += size_t(b) * A.HV * kDH * kDH;
+    A.conv_out += wrows * A.C;
+    A.gates += wrows * A.HV * 2;
+    // (null pointers stay null: the offsets are zero for stream 0, and batched calls are deferred ones)
+    A.ctl += size_t(b) * A.ctl_stride;
+    A.prev_qkv += size_t(b) * kGdnMaxRows * A.C;
+    A.prev_a += size_t(b) * kGdnMaxRows * A.HV;
+    A.prev_b += size_t(b) * kGdnMaxRows * A.HV;
+    A.save_qkv += size_t(b) * kGdnMaxRows * A.C;
+    A.save_a += size_t(b) * kGdnMaxRows * A.HV;
+    A.save_b += size_t(b) * kGdnMaxRows * A.HV;
+    return A;
+}
+
+__global__ void __launch_bounds__(kConvThreads) gdn_conv_kernel(const GdnArgs A0) {
+    const GdnArgs A = gdn_stream(A0, blockIdx.y);
     gdn_conv_item(A, blockIdx.x * blockDim.x + threadIdx.x);
 }
 
@@ -44,7 +69,8 @@ __global__ void __launch_bounds__(kConvThreads) gdn_conv_kernel(const GdnArgs A)
 constexpr int kDcCols = 32, kDcCtas = kDH / kDcCols;
 static_assert(kRG == 4 && kDcCols == 32, "one warp per row group, one lane per column");
 
-__global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols) gdn_delta_kernel(const GdnArgs A) {
+__global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols) gdn_delta_kernel(const GdnArgs A0) {
+    const GdnArgs A = gdn_stream(A0, blockIdx.y);
     __shared__ __align__(16) float qn[kGdnMaxAll][kDH];
     __shared__ __align__(16) float kn[kGdnMaxAll][kDH];
     __shared__ float part[2][kRG][kDcCols];
@@ -247,21 +273,21 @@ int launch_gdn_ab(const uint16_t* x, int64_t x_stride, const uint16_t* w, int K,
     return MONO_OK;
 }
 
-size_t gdn_workspace_bytes(int M, int C, int HV) {
-    // conv outputs and gates of up to 8 replayed rows + the M verify rows
-    const size_t rows = size_t(M) + kGdnMaxRows;
+size_t gdn_workspace_bytes(int M, int C, int HV, int streams) {
+    // per stream: conv outputs and gates of up to 8 replayed rows + the M verify rows
+    const size_t rows = (size_t(M) + kGdnMaxRows) * streams;
     return (rows * C * 2 + 255) / 256 * 256 + rows * HV * 2 * 4;
 }
 
 int launch_gdn_step(GdnArgs A, void* ws, cudaStream_t stream) {
     const size_t rows = size_t(A.M) + kGdnMaxRows;
     A.conv_out = static_cast<uint16_t*>(ws);
-    A.gates = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + (rows * A.C * 2 + 255) / 256 * 256);
+    A.gates = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + (rows * A.streams * A.C * 2 + 255) / 256 * 256);
     const int rmax = int(rows);
     const int nthreads = A.C > rmax * A.HV ? A.C : rmax * A.HV;
-    gdn_conv_kernel<<<(nthreads + kConvThreads - 1) / kConvThreads, kConvThreads, 0, stream>>>(A);
+    gdn_conv_kernel<<<dim3((nthreads + kConvThreads - 1) / kConvThreads, A.streams), kConvThreads, 0, stream>>>(A);
     CUDA_TRY(cudaGetLastError());
-    gdn_delta_kernel<<<A.HV * kDcCtas, kRG * kDcCols, 0, stream>>>(A);
+    gdn_delta_kernel<<<dim3(A.HV * kDcCtas, A.streams), kRG * kDcCols, 0, stream>>>(A);
     CUDA_TRY(cudaGetLastError());
     return MONO_OK;
 }

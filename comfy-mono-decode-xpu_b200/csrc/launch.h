@@ -81,10 +81,11 @@ struct NormRopeArgs {
     uint16_t* kc;        // [Hk][cap][256]
     uint16_t* vc;
     const int64_t* pos;
-    uint16_t* oq;  // [Hq][S][256]
-    uint16_t* ok;  // [Hk][S][256]
+    uint16_t* oq;  // [streams][Hq][S / streams][256]
+    uint16_t* ok;  // [streams][Hk][S / streams][256]
     int64_t qs, qh, ks, vs, cap;
     int S, Hq, Hk, rd;
+    int streams;   // batched streams: S / streams rows each, caches [streams][Hk][cap][256]
     float epsq, epsk;
 };
 int launch_qk_norm_rope_kv(const NormRopeArgs& A, cudaStream_t stream);
@@ -97,12 +98,14 @@ struct AttnArgs {
     const uint16_t* xk;   // [Hk][S][256]
     const uint16_t* xv;
     const int32_t* mask;  // [S] or null
-    uint16_t* out;        // [S][H * 256]
-    float* part;          // [Hk][chunks][32][256]
-    float* ml;            // [Hk][chunks][32][2]
-    int H, Hk, S, cap, chunks;
+    uint16_t* out;        // [streams][S][H / streams * 256]
+    float* part;          // workspace: [Hk][chunks / 8][32][256] merged rows of each cluster
+    float* ml;            // [Hk][chunks / 8][32][2]
+    unsigned* count;      // [Hk][8] arrivals per (kv head, cluster rank); zero between launches
+    int H, Hk, S, cap, chunks;  // H, Hk: all streams' heads (stream b: q heads [b H / streams, ...), its kv heads)
+    int streams;                // seqlen[b]: stream b's committed length
 };
-size_t attn_workspace_bytes(int Hk, int cap, int sms);
+size_t attn_workspace_bytes(int Hk, int streams, int cap, int sms);
 int launch_tree_attention(AttnArgs A, void* ws, cudaStream_t stream);
 
 struct GdnArgs {
@@ -131,8 +134,12 @@ struct GdnArgs {
     uint16_t* save_b;
     int64_t qkv_stride, z_stride, ab_stride;  // row strides (elements) of qkv, z, a / b
     int M, C, HK, HV;
+    // batched streams (grid y): stream b's rows are [b M, (b + 1) M) of qkv / z / a / b / core; its conv state,
+    // recurrent state, ctl (ctl_stride words apart), replay / save buffers and workspace rows are the b-th of
+    // `streams` consecutive copies (gdn_stream)
+    int streams, ctl_stride;
 };
-size_t gdn_workspace_bytes(int M, int C, int HV);
+size_t gdn_workspace_bytes(int M, int C, int HV, int streams);
 // Validates the GDN step's operands and fills A (workspace: gdn_workspace_bytes; conv_out and gates in it).
 int fill_gdn_args(GdnArgs& A, const void* qkv, const void* z, const void* a, const void* b, const void* conv_w,
                   void* conv_state, const float* dt_bias, const float* g_decay, float* state, const void* gnorm_w,

@@ -1,5 +1,5 @@
 // bf16 lm_head with the greedy / draft pick fused (the role of the reference's verify logits + argmax, and of its
-// draft pick, csrc/draft_lmhead.sycl:87-292): for M <= 8 rows of x [M][K] against W [V][K] (bf16, far larger than
+// draft pick, csrc/draft_lmhead.sycl:87-292): for M <= 16 rows of x [M][K] against W [V][K] (bf16, far larger than
 // L2), logits = bf16(x W^T) on the tensor cores, and per row the argmax (argmax rank: smallest index on ties) and
 // the top-k (k <= 8, top-k rank), without writing the logits (optional).
 //
@@ -7,12 +7,12 @@
 // b * 8 + j, + G * 8, ... For each tile it streams the rows in chunks of 512 k: lanes 0..7 each copy one row's 1 KB
 // (a bulk copy, evict-first, completion on the stage's mbarrier) into the warp's own ring of S stages (rows 16-byte
 // skewed: conflict-free ldmatrix), so every request is a contiguous kilobyte and the ring keeps S chunks per warp
-// in flight. The MMA is m16n8k16 with A = the x rows (rows 8..15 zero) and B = the 8 weight rows, both read with
+// in flight. The MMA is m16n8k16 with A = the x rows (rows past M zero) and B = the 8 weight rows, both read with
 // ldmatrix; two accumulators take alternate k-steps of the tile and are added at its end (one fixed partition and
 // order: the same bits on every launch), then rounded once to bf16.
 //
-// Pick: thread (g, t) of a warp holds row g's logits at columns 2t, 2t + 1 of each tile and keeps that row's running
-// top-k list and argmax in registers; at the end the CTA merges its 32 lists per row and writes them to the
+// Pick: thread (g, t) of a warp holds rows g and g + 8's logits at columns 2t, 2t + 1 of each tile and keeps those
+// rows' running top-k lists and argmaxes in registers; at the end the CTA merges its 32 lists per row and writes them to the
 // workspace; the last CTA to finish (an arrival counter) merges the CTAs' lists - ranks are distinct, so the merge
 // order does not matter - and writes the indices. The pick form then scatters the draft's tokens into the verify-token row: dst[children[0]] =
 // argmax, dst[children[j]] = top-k[j] (j >= 1), the reference's draft pick (csrc/draft_lmhead.sycl:4-17).
@@ -24,18 +24,19 @@
 
 namespace mono {
 
-constexpr int kLhWarps = 8, kLhMaxM = 8, kLhRows = 8, kLhChunk = 512;
+constexpr int kLhWarps = 8, kLhMaxM = 16, kLhRows = 8, kLhChunk = 512;
 constexpr int kLhRowPitch = kLhChunk * 2 + 16;   // bytes per staged weight row (16-byte skew: conflict-free ldmatrix)
 constexpr int kLhStage = kLhRows * kLhRowPitch;  // one ring stage: 8 rows x 512 k
 constexpr size_t kLhSmemLimit = 227 * 1024 - 8 * 1024;  // dynamic bytes: the opt-in maximum less the static ones
 
-__device__ __forceinline__ void lh_mma(float (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
-    // rows 8..15 of A are zero (a1 = a3 = 0): only rows 0..7, the x rows, carry data
+// A rows 0..7 (a0, a2) and 8..15 (a1, a3: zero registers when M <= 8) are x rows
+__device__ __forceinline__ void lh_mma(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
         "{%0, %1, %2, %3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 __device__ __forceinline__ void lh_ldsm_x4(uint32_t (&r)[4], const void* p) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -49,8 +50,9 @@ struct LmHeadArgs {
     uint16_t* logits;         // [M][V] bf16 or null
     int64_t* argmax;          // [M] or null
     int64_t* topk;            // [M][k] or null (k = 0: none)
-    const int32_t* children;  // pick form: up to 8 slots of dst, -1 ends (row 0's tokens), or null
-    int64_t* dst;             // pick form: the verify-token row
+    const int32_t* children;  // pick form: up to 8 slots of a dst row, -1 ends, or null
+    int64_t* dst;             // pick form: the verify-token rows, row m's at dst + m * dst_stride
+    int64_t dst_stride;
     uint64_t* ws;             // the arrival counter (first 256 bytes), then [G][kLhMaxM][kTkK + 1] CTA lists
     int64_t x_stride, out_stride;  // out_stride: the logits' row stride (V for the pick)
     int64_t index_base;            // the pick's index of row 0 of w (a vocabulary shard's offset; 0 otherwise)
@@ -130,12 +132,15 @@ __global__ void __launch_bounds__(kLhWarps * 32, 1) lmhead_pick_kernel(const LmH
         if (threadIdx.x == 0) *reinterpret_cast<uint4*>(const_cast<uint16_t*>(zero16)) = make_uint4(0, 0, 0, 0);
     }
     __syncthreads();
-    uint64_t top[kTkK], best = 0;
+    uint64_t top[2][kTkK], best[2] = {0, 0};  // rows g and g + 8
 #pragma unroll
-    for (int j = 0; j < kTkK; ++j) top[j] = 0;
-    // ldmatrix row addresses: W rows lane & 7 at k + 8 (lane >> 3); x rows likewise (past M: the zero row)
+    for (int j = 0; j < kTkK; ++j) top[0][j] = top[1][j] = 0;
+    // ldmatrix row addresses: W rows lane & 7 at k + 8 (lane >> 3); x rows likewise, and rows 8 + (lane & 7) when
+    // M > 8 (past M: the zero row)
     const int lr = lane & 7, lk = 8 * (lane >> 3);
     const uint16_t* xrow = lr < A.M ? xs + size_t(lr) * pitch + lk : nullptr;
+    const uint16_t* xrow2 = 8 + lr < A.M ? xs + size_t(8 + lr) * pitch + lk : nullptr;
+    const bool hi = A.M > 8;
     int q = 0;
     bool bad = false;
     for (int r = 0; r < Rc; ++r) {
@@ -150,18 +155,20 @@ __global__ void __launch_bounds__(kLhWarps * 32, 1) lmhead_pick_kernel(const LmH
                 const int kx = (sl * CPU + cc) * kLhChunk;
 #pragma unroll 4
                 for (int kk = 0; kk < kLhChunk; kk += 32) {
-                    uint32_t bw[4], a[4];
+                    uint32_t bw[4], a[4], a8[4] = {0u, 0u, 0u, 0u};
                     lh_ldsm_x4(bw, st + kk * 2);
                     lh_ldsm_x4(a, xrow ? xrow + kx + kk : zero16);
-                    lh_mma(c0, a[0], a[1], bw[0], bw[1]);
-                    lh_mma(c1, a[2], a[3], bw[2], bw[3]);
+                    if (hi) lh_ldsm_x4(a8, xrow2 ? xrow2 + kx + kk : zero16);
+                    lh_mma(c0, a[0], a8[0], a[1], a8[1], bw[0], bw[1]);
+                    lh_mma(c1, a[2], a8[2], a[3], a8[3], bw[2], bw[3]);
                 }
                 __syncwarp();
                 if (q + S < Q) issue(q + S);
             }
         }
         // the slice's sums (the two k-step chains added in order), then the ks slices of the tile in slice order
-        float v0 = c0[0] + c1[0], v1 = c0[1] + c1[1];
+        // (ks > 1 only for M <= 8: rows g + 8 are empty there)
+        float v0 = c0[0] + c1[0], v1 = c0[1] + c1[1], v2 = c0[2] + c1[2], v3 = c0[3] + c1[3];
         if (ks > 1) {
             part[r & 1][warp][lane] = make_float2(v0, v1);
             __syncthreads();  // (the other buffer is read before the next round's barrier: no second one needed)
@@ -173,18 +180,24 @@ __global__ void __launch_bounds__(kLhWarps * 32, 1) lmhead_pick_kernel(const LmH
                 }
         }
         if (sl == 0 && r < Rw && g < A.M) {
-            // the tile's outputs: row g (< M) at columns n0 + 2t, n0 + 2t + 1
+            // the tile's outputs: rows g and g + 8 (< M) at columns n0 + 2t, n0 + 2t + 1
             const int n0 = (first + r * stride) * kLhRows;
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const int n = n0 + 2 * t + e;
-                if (n < A.V) {
-                    const uint16_t bits = __bfloat16_as_ushort(__float2bfloat16_rn(e ? v1 : v0));
-                    if (!PICK || A.logits) A.logits[int64_t(g) * A.out_stride + n] = bits;
-                    if constexpr (PICK) {
-                        const uint32_t gi = uint32_t(A.index_base + n);  // ranked by the global index
-                        if (A.k > 0) insert_rank(top, rank_topk(bits, gi), A.k);
-                        best = max(best, rank_argmax(bits, gi));
+            for (int h = 0; h < 2; ++h) {
+                const int row = g + 8 * h;
+                if (h == 1 && row >= A.M) break;
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int n = n0 + 2 * t + e;
+                    if (n < A.V) {
+                        const float v = h ? (e ? v3 : v2) : (e ? v1 : v0);
+                        const uint16_t bits = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+                        if (!PICK || A.logits) A.logits[int64_t(row) * A.out_stride + n] = bits;
+                        if constexpr (PICK) {
+                            const uint32_t gi = uint32_t(A.index_base + n);  // ranked by the global index
+                            if (A.k > 0) insert_rank(top[h], rank_topk(bits, gi), A.k);
+                            best[h] = max(best[h], rank_argmax(bits, gi));
+                        }
                     }
                 }
             }
@@ -198,12 +211,14 @@ __global__ void __launch_bounds__(kLhWarps * 32, 1) lmhead_pick_kernel(const LmH
     __syncthreads();  // every ring is idle: its memory now holds the pick's lists
     uint64_t* lst = reinterpret_cast<uint64_t*>(smem);      // [warp * 4 + t][kLhMaxM][kTkK + 1]
     uint64_t* fin = lst + kLhWarps * 4 * kLhMaxM * (kTkK + 1);  // [NT][kTkK]
-    if (g < A.M) {
-        uint64_t* l = lst + ((warp * 4 + t) * kLhMaxM + g) * (kTkK + 1);
 #pragma unroll
-        for (int j = 0; j < kTkK; ++j) l[j] = top[j];
-        l[kTkK] = best;
-    }
+    for (int h = 0; h < 2; ++h)
+        if (g + 8 * h < A.M) {
+            uint64_t* l = lst + ((warp * 4 + t) * kLhMaxM + g + 8 * h) * (kTkK + 1);
+#pragma unroll
+            for (int j = 0; j < kTkK; ++j) l[j] = top[h][j];
+            l[kTkK] = best[h];
+        }
     __syncthreads();
     unsigned* counter = reinterpret_cast<unsigned*>(A.ws);  // fixed offset: calls of any grid share a workspace
     uint64_t* ws = A.ws + 32;
@@ -258,11 +273,11 @@ __global__ void __launch_bounds__(kLhWarps * 32, 1) lmhead_pick_kernel(const LmH
             if (A.argmax) A.argmax[m] = am;
             if (A.topk)
                 for (int j = 0; j < A.k; ++j) A.topk[m * A.k + j] = int64_t(topk_index(fin[j]));
-            if (m == 0 && A.children != nullptr)
+            if (A.children != nullptr)
                 for (int j = 0; j < 8; ++j) {
                     const int c = A.children[j];
                     if (c < 0) break;
-                    A.dst[c] = (j == 0 || j >= A.k) ? am : int64_t(topk_index(fin[j]));
+                    A.dst[m * A.dst_stride + c] = (j == 0 || j >= A.k) ? am : int64_t(topk_index(fin[j]));
                 }
         }
         __syncthreads();
@@ -274,7 +289,7 @@ int lmhead_grid() { return sm_count(); }
 
 // the deepest ring (stages per warp) whose plan fits the shared memory, or 0
 int lmhead_stages(int M, int K) {
-    for (int S = 4; S >= 2; --S)
+    for (int S = 4; S >= 1; --S)
         if (LhPlan(M, K, S).total <= kLhSmemLimit) return S;
     return 0;
 }
@@ -328,11 +343,12 @@ template <bool PICK>
 static int launch_lmhead_t(LmHeadArgs A, cudaStream_t stream) {
     // the pick over a vocabulary has tiles enough for every warp: no split (a split's per-round barrier measured
     // slower there: 235 against 197 us)
-    A.ks = PICK ? 1 : lmhead_split(A.V, A.K);
+    A.ks = (PICK || A.M > 8) ? 1 : lmhead_split(A.V, A.K);
     switch (lmhead_stages(A.M, A.K)) {
         case 4: return launch_lh<4, PICK>(A, stream);
         case 3: return launch_lh<3, PICK>(A, stream);
         case 2: return launch_lh<2, PICK>(A, stream);
+        case 1: return launch_lh<1, PICK>(A, stream);
         default: return fail(MONO_EINVAL, "lm_head: x rows of K = %d do not fit next to the rings", A.K);
     }
 }
@@ -363,20 +379,20 @@ extern "C" size_t mono_lmhead_workspace(void) { return lmhead_workspace_bytes(lm
 
 extern "C" int mono_lmhead_pick(const void* x, int64_t x_stride, const void* w, int64_t M, int64_t V, int64_t K, int64_t k,
                                 int64_t index_base, void* logits, int64_t* argmax, int64_t* topk,
-                                const int32_t* children, int64_t* dst, void* workspace, size_t workspace_bytes,
-                                mono_stream_t stream) {
+                                const int32_t* children, int64_t* dst, int64_t dst_stride, void* workspace,
+                                size_t workspace_bytes, mono_stream_t stream) {
     MONO_CHECK(x && w && workspace, "null operand");
     MONO_CHECK(M >= 1 && M <= kLhMaxM, "1 <= M <= %d rows", kLhMaxM);
     MONO_CHECK(k >= 0 && k <= kTkK, "0 <= k <= %d", kTkK);
     MONO_CHECK(K >= kLhChunk && K % kLhChunk == 0 && lmhead_stages(int(M), int(std::min<int64_t>(K, 1 << 20))) > 0,
-               "K a multiple of 512 whose M x rows fit in shared memory beside the rings (K <= 4096 at M = 8)");
+               "K a multiple of 512 whose M x rows fit in shared memory beside the rings (K <= 4096 at M = 16)");
     MONO_CHECK(V >= 1 && V < (int64_t(1) << 31) && V * K < (int64_t(1) << 40), "1 <= V < 2^31");
     MONO_CHECK(index_base >= 0 && index_base + V < (int64_t(1) << 31), "0 <= index_base, index_base + V < 2^31");
     MONO_CHECK(x_stride >= K && x_stride % 8 == 0 && aligned(x, 16) && aligned(w, 16),
                "x rows and w 16-byte aligned, x_stride a multiple of 8 elements");
     MONO_CHECK(argmax || (topk && k > 0) || logits || children, "no output requested");
     MONO_CHECK(k == 0 || topk || children, "top-k wanted but no top-k output");
-    MONO_CHECK(!children || (dst && M == 1), "the pick form takes one row and a destination");
+    MONO_CHECK(!children || (dst && (M == 1 || dst_stride >= 8)), "the pick form: a destination, rows 8 slots apart");
     MONO_CHECK(aligned(workspace, 256) && workspace_bytes >= lmhead_workspace_bytes(lmhead_grid()),
                "workspace: mono_lmhead_workspace() bytes, 256-byte aligned, zero-filled before its first use");
     LmHeadArgs A{};
@@ -387,6 +403,7 @@ extern "C" int mono_lmhead_pick(const void* x, int64_t x_stride, const void* w, 
     A.topk = topk;
     A.children = children;
     A.dst = dst;
+    A.dst_stride = dst_stride;
     A.ws = static_cast<uint64_t*>(workspace);
     A.x_stride = x_stride;
     A.out_stride = V;

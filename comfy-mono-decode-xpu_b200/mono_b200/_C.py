@@ -262,46 +262,61 @@ def mlp_gptq(x, norm_w, eps, gate, up, down, silu_lut=None, residual=True, out=N
     return out
 
 
-def qk_norm_rope_kv(rawq, rawk, vn, weightq, weightk, freqs, key, value, position, epsq, epsk, rd):
+def qk_norm_rope_kv(rawq, rawk, vn, weightq, weightk, freqs, key, value, position, epsq, epsk, rd, streams=1):
     """Q/K head RMSNorm + partial RoPE + K/V cache write (the reference's _C.qk_norm_rope_kv,
     csrc/rope_kv.sycl:120-245). rawq bf16 [1, S, Hq, 256] (the query half of gated heads: head stride 512, or
     dense), rawk / vn bf16 [1, S, Hk, 256] (dense heads), weights bf16 [256], freqs fp32 [S, rd/2, 2, 2], key /
     value caches bf16 [1, Hk, cap, 256] (written in place at position[s]), position int64 [>= S].
-    Returns (q [1, Hq, S, 256], k [1, Hk, S, 256])."""
+    Returns (q [1, Hq, S, 256], k [1, Hk, S, 256]).
+    streams > 1 (batched decode streams, include/mono_b200.h mono_qk_norm_rope_kv_streams): the S rows are
+    `streams` groups of S / streams, the caches [1, streams * Hk, cap, 256] (stream b: heads [b Hk, (b + 1) Hk));
+    returns q [1, streams * Hq, S / streams, 256] and k [1, streams * Hk, S / streams, 256]."""
     _cuda(rawq, rawk, vn, weightq, weightk, freqs, key, value, position)
     _check(rawq.dtype == torch.bfloat16 and rawq.dim() == 4 and rawq.size(0) == 1 and rawq.size(3) == 256
            and rawq.stride(3) == 1, "Q: bf16 [1, S, Hq, 256]")
     S, Hq, Hk = rawq.size(1), rawq.size(2), rawk.size(2)
+    _check(streams >= 1 and S % streams == 0, "rows in equal groups per stream")
+    R = S // streams
     _check(rawk.dim() == 4 and rawk.shape == vn.shape and rawk.size(1) == S and rawk.stride(3) == 1 and
            rawk.stride(2) == 256 and vn.stride(3) == 1 and vn.stride(2) == 256, "K/V: bf16 [1, S, Hk, 256], dense heads")
     _check(all(t.dtype == torch.bfloat16 for t in (rawk, vn, key, value, weightq, weightk)), "bf16 K/V, caches, weights")
     _check(key.is_contiguous() and value.is_contiguous() and key.shape == value.shape and key.dim() == 4 and
-           key.size(1) == Hk and key.size(3) == 256, "K/V cache: bf16 [1, Hk, cap, 256]")
+           key.size(1) == streams * Hk and key.size(3) == 256, "K/V cache: bf16 [1, streams * Hk, cap, 256]")
     _check(freqs.dtype == torch.float32 and freqs.is_contiguous() and freqs.numel() == S * (rd // 2) * 4,
            "frequencies: fp32 [S, rd/2, 2, 2]")
     _check(position.dtype == torch.int64 and position.is_contiguous() and position.numel() >= S, "int64 positions")
     _check(weightq.is_contiguous() and weightk.is_contiguous(), "contiguous norm weights")
-    q = torch.empty((1, Hq, S, 256), dtype=torch.bfloat16, device=rawq.device)
-    k = torch.empty((1, Hk, S, 256), dtype=torch.bfloat16, device=rawq.device)
+    q = torch.empty((1, streams * Hq, R, 256), dtype=torch.bfloat16, device=rawq.device)
+    k = torch.empty((1, streams * Hk, R, 256), dtype=torch.bfloat16, device=rawq.device)
     with torch.cuda.device(rawq.device):
-        _lib.call("mono_qk_norm_rope_kv", _p(rawq), rawq.stride(1), rawq.stride(2), _p(rawk), rawk.stride(1), _p(vn),
-                  vn.stride(1), _p(weightq), _p(weightk), _p(freqs), _p(key), _p(value), key.size(2), _p(position), S, Hq,
-                  Hk, float(epsq), float(epsk), int(rd), _p(q), _p(k), _stream(rawq.device))
+        if streams == 1:
+            _lib.call("mono_qk_norm_rope_kv", _p(rawq), rawq.stride(1), rawq.stride(2), _p(rawk), rawk.stride(1),
+                      _p(vn), vn.stride(1), _p(weightq), _p(weightk), _p(freqs), _p(key), _p(value), key.size(2),
+                      _p(position), S, Hq, Hk, float(epsq), float(epsk), int(rd), _p(q), _p(k), _stream(rawq.device))
+        else:
+            _lib.call("mono_qk_norm_rope_kv_streams", _p(rawq), rawq.stride(1), rawq.stride(2), _p(rawk),
+                      rawk.stride(1), _p(vn), vn.stride(1), _p(weightq), _p(weightk), _p(freqs), _p(key), _p(value),
+                      key.size(2), _p(position), S, streams, Hq, Hk, float(epsq), float(epsk), int(rd), _p(q), _p(k),
+                      _stream(rawq.device))
     return q, k
 
 
 _attn_ws = {}
 
 
-def attn_dpas(q, key, value, seqlen, xk, xv, mask, chunks_hint=0, out=None):
+def attn_dpas(q, key, value, seqlen, xk, xv, mask, chunks_hint=0, out=None, streams=1):
     """Tree decode attention (the reference's _C.attn_dpas, csrc/attn_dpas.sycl:269-342). q bf16 [1, H, S, 256];
     key / value bf16 [1, Hk, cap, 256]; seqlen int32 [1] on the device (L, no host sync); xk / xv bf16
     [1, Hk, S, 256]; mask int32 [S] (an empty tensor: the single draft row over the prefix only).
     Returns bf16 [1, S, H * 256] (into `out` when given). chunks_hint is accepted for the reference's signature and
-    unused."""
+    unused. streams > 1 (batched decode streams, include/mono_b200.h mono_tree_attention_streams): q, the caches,
+    xk and xv hold `streams` groups of heads (stream b: q heads [b H, (b + 1) H), kv heads [b Hk, (b + 1) Hk)),
+    seqlen int32 [streams], one mask for all; returns bf16 [1, streams * S, H * 256] (stream b's rows [b S, ...))."""
     _cuda(q, key, value, seqlen, xk, xv)
     _check(q.dtype == torch.bfloat16 and q.dim() == 4 and q.size(0) == 1 and q.size(3) == 256, "q bf16 [1, H, S, 256]")
-    H, S, Hk, cap = q.size(1), q.size(2), key.size(1), key.size(2)
+    _check(streams >= 1 and q.size(1) % streams == 0 and key.size(1) % streams == 0, "heads in equal groups per stream")
+    H, S, Hk, cap = q.size(1) // streams, q.size(2), key.size(1) // streams, key.size(2)
+    _check(seqlen.numel() >= streams, "one length per stream")
     _check(key.is_contiguous() and value.is_contiguous() and key.shape == value.shape and key.size(3) == 256,
            "cache bf16 [1, Hk, cap, 256]")
     _check(seqlen.dtype == torch.int32 and mask.dtype == torch.int32, "int32 seqlen / mask")
@@ -309,14 +324,15 @@ def attn_dpas(q, key, value, seqlen, xk, xv, mask, chunks_hint=0, out=None):
     _check(mask.numel() == S if tree else S == 1, "mask [S] (or empty with one row)")
     q = q.contiguous()
     xk, xv = xk.contiguous(), xv.contiguous()
-    nbytes = _lib.load().mono_tree_attention_workspace(Hk, cap)
-    ws = _workspace(_attn_ws, (q.device, Hk, cap), nbytes, q.device)
+    nbytes = _lib.load().mono_tree_attention_streams_workspace(Hk, streams, cap)
+    ws = _workspace(_attn_ws, (q.device, Hk, streams, cap), nbytes, q.device)
     if out is None:
-        out = torch.empty((1, S, H * 256), dtype=torch.bfloat16, device=q.device)
-    _check(out.dtype == torch.bfloat16 and out.is_contiguous() and out.numel() == S * H * 256, "out bf16 [1, S, H * 256]")
+        out = torch.empty((1, streams * S, H * 256), dtype=torch.bfloat16, device=q.device)
+    _check(out.dtype == torch.bfloat16 and out.is_contiguous() and out.numel() == streams * S * H * 256,
+           "out bf16 [1, streams * S, H * 256]")
     with torch.cuda.device(q.device):
-        _lib.call("mono_tree_attention", _p(q), _p(key), _p(value), _p(seqlen), _p(xk), _p(xv),
-                  _p(mask) if tree else None, H, Hk, S, cap, _p(out), _p(ws), nbytes, _stream(q.device))
+        _lib.call("mono_tree_attention_streams", _p(q), _p(key), _p(value), _p(seqlen), _p(xk), _p(xv),
+                  _p(mask) if tree else None, H, Hk, S, streams, cap, _p(out), _p(ws), nbytes, _stream(q.device))
     return out
 
 
@@ -451,30 +467,49 @@ def rowlin_gptq(x, mode, weights, norm_w=None, eps=1e-6, gate=None, gate_head_st
 
 
 def gdn_step_deferred(qkv, z, a, b, conv_w, conv_state, dt_bias, g_decay, state, gnorm_w, gnorm_eps, qscale, hk, ctl,
-                      prev, save):
+                      prev, save, streams=1):
     """The deferred GDN step of the device MTP loop (include/mono_b200.h mono_gdn_step_deferred): replays the
     ctl[0] accepted rows of the previous step from prev = (qkv [8, C], a [8, HV], b [8, HV]), persists, then runs
     this step's rows as a chain without persisting and saves their inputs to save (same shapes, not aliasing
-    prev). Returns core bf16 [M, HV * 128]."""
+    prev). Returns core bf16 [M, HV * 128].
+    streams > 1 (batched decode streams, mono_gdn_step_deferred_streams): the rows are `streams` groups of
+    M / streams; conv_state [streams, C, 3], state [streams, HV, 128, 128], ctl int32 [streams, 26], prev / save
+    [streams, 8, ...]: each stream's slice is its one-stream call's."""
     _cuda(qkv, z, a, b, conv_w, conv_state, dt_bias, g_decay, state, gnorm_w, ctl, *prev, *save)
-    M, C = qkv.shape
+    MT, C = qkv.shape
     HV = a.shape[1]
-    _check(C == (2 * hk + HV) * 128 and z.shape == (M, HV * 128) and b.shape == a.shape, "GDN shapes")
-    _check(ctl.dtype == torch.int32 and ctl.numel() >= 10, "ctl int32 [26]")
+    _check(streams >= 1 and MT % streams == 0, "rows in equal groups per stream")
+    if streams == 1 and prev[0].dim() == 3:  # one stream's slice of the batched layout
+        prev, save = tuple(t[0] for t in prev), tuple(t[0] for t in save)
+    M = MT // streams
+    _check(C == (2 * hk + HV) * 128 and z.shape == (MT, HV * 128) and b.shape == a.shape, "GDN shapes")
+    _check(ctl.dtype == torch.int32 and ctl.is_contiguous() and ctl.numel() >= 26 * streams - 16, "ctl int32 [26]")
+    if streams > 1:
+        _check(ctl.dim() == 2 and ctl.size(0) == streams and conv_state.shape == (streams, C, 3) and
+               state.shape == (streams, HV, 128, 128) and prev[0].shape == (streams, 8, C) and
+               prev[1].shape == (streams, 8, HV) and save[0].shape == (streams, 8, C), "per-stream state shapes")
+    else:
+        _check(prev[0].shape == (8, C) and prev[1].shape == (8, HV) and save[0].shape == (8, C), "saved rows [8, ...]")
     for t in (qkv, z, a, b):  # column slices of wider rows are fine
         _check(t.dtype == torch.bfloat16 and t.stride(1) == 1, "bf16 rows with unit column stride")
     _check(a.stride(0) == b.stride(0), "a and b share a row stride")
     for t in (conv_w, conv_state, gnorm_w, *prev, *save):
         _check(t.dtype == torch.bfloat16 and t.is_contiguous(), "bf16 contiguous operands")
-    _check(prev[0].shape == (8, C) and prev[1].shape == (8, HV) and save[0].shape == (8, C), "saved rows [8, ...]")
-    nbytes = _lib.load().mono_gdn_step_workspace(M, C, HV)
-    ws = _workspace(_gdn_ws, (qkv.device, M, C, HV), nbytes, qkv.device)
-    core = torch.empty((M, HV * 128), dtype=torch.bfloat16, device=qkv.device)
+    nbytes = _lib.load().mono_gdn_step_streams_workspace(M, C, HV, streams)
+    ws = _workspace(_gdn_ws, (qkv.device, M, C, HV, streams), nbytes, qkv.device)
+    core = torch.empty((MT, HV * 128), dtype=torch.bfloat16, device=qkv.device)
     with torch.cuda.device(qkv.device):
-        _lib.call("mono_gdn_step_deferred", _p(qkv), _p(z), _p(a), _p(b), _p(conv_w), _p(conv_state), _p(dt_bias),
-                  _p(g_decay), _p(state), _p(gnorm_w), float(gnorm_eps), float(qscale), M, hk, HV, _p(core), _p(ctl),
-                  _p(prev[0]), _p(prev[1]), _p(prev[2]), _p(save[0]), _p(save[1]), _p(save[2]), qkv.stride(0),
-                  z.stride(0), a.stride(0), _p(ws), nbytes, _stream(qkv.device))
+        if streams == 1:
+            _lib.call("mono_gdn_step_deferred", _p(qkv), _p(z), _p(a), _p(b), _p(conv_w), _p(conv_state), _p(dt_bias),
+                      _p(g_decay), _p(state), _p(gnorm_w), float(gnorm_eps), float(qscale), M, hk, HV, _p(core),
+                      _p(ctl), _p(prev[0]), _p(prev[1]), _p(prev[2]), _p(save[0]), _p(save[1]), _p(save[2]),
+                      qkv.stride(0), z.stride(0), a.stride(0), _p(ws), nbytes, _stream(qkv.device))
+        else:
+            _lib.call("mono_gdn_step_deferred_streams", _p(qkv), _p(z), _p(a), _p(b), _p(conv_w), _p(conv_state),
+                      _p(dt_bias), _p(g_decay), _p(state), _p(gnorm_w), float(gnorm_eps), float(qscale), M, hk, HV,
+                      streams, _p(core), _p(ctl), ctl.stride(0), _p(prev[0]), _p(prev[1]), _p(prev[2]), _p(save[0]),
+                      _p(save[1]), _p(save[2]), qkv.stride(0), z.stride(0), a.stride(0), _p(ws), nbytes,
+                      _stream(qkv.device))
     return core
 
 
@@ -665,8 +700,9 @@ def lmhead_pick(x, w, k=0, logits=False, argmax_out=None, topk_out=None, childre
     """bf16 lm_head of M <= 8 rows with the greedy / draft pick fused (include/mono_b200.h mono_lmhead_pick):
     x bf16 [M, K] (rows 16-byte aligned), w bf16 [V, K]. Returns (argmax int64 [M], top-k int64 [M, k] or None,
     logits bf16 [M, V] or None). With children (int32 device tensor of up to 8 slots, -1 ends) and dst (int64 device
-    row), also writes the draft pick into dst (M must be 1). index_base: the vocabulary index of w's row 0 (a
-    tensor-parallel shard): ranks and returned indices are global."""
+    tensor: one row, or [M, >= 8] with unit column stride, one row per x row), also writes each row's draft pick
+    into its dst row. index_base: the vocabulary index of w's row 0 (a tensor-parallel shard): ranks and returned
+    indices are global."""
     _cuda(x, w)
     _check(x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1 and
            w.is_contiguous() and w.dim() == 2 and w.size(1) == x.size(1), "x bf16 [M, K], w bf16 [V, K]")
@@ -677,11 +713,18 @@ def lmhead_pick(x, w, k=0, logits=False, argmax_out=None, topk_out=None, childre
     if k > 0 and children is None:
         tk = topk_out if topk_out is not None else torch.empty(M, k, dtype=torch.int64, device=x.device)
     lg = torch.empty(M, V, dtype=torch.bfloat16, device=x.device) if logits else None
+    dst_stride = 0
+    if children is not None:
+        _check(dst is not None and dst.dtype == torch.int64, "the pick form needs an int64 dst")
+        if M > 1:
+            _check(dst.dim() == 2 and dst.size(0) == M and dst.size(1) >= 8 and dst.stride(1) == 1,
+                   "dst [M, >= 8] rows for M > 1")
+            dst_stride = dst.stride(0)
     need = _lib.load().mono_lmhead_workspace()
     ws = _workspace(_lmhead_ws, (x.device,), need, x.device)
     with torch.cuda.device(x.device):
         _lib.call("mono_lmhead_pick", _p(x), x.stride(0), _p(w), M, V, K, k, int(index_base), _p(lg), _p(am), _p(tk),
-                  _p(children), _p(dst), _p(ws), need, _stream(x.device))
+                  _p(children), _p(dst), dst_stride, _p(ws), need, _stream(x.device))
     return am, tk, lg
 
 

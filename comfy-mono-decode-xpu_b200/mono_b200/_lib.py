@@ -39,7 +39,14 @@ SIGNATURES = {
     "mono_mlp_gptq": (I, [P, P, ctypes.c_float, P, P, P, P, I64, I64, I64, I, P, P, SZ, P]),
     "mono_qk_norm_rope_kv": (I, [P, I64, I64, P, I64, P, I64, P, P, P, P, P, I64, P, I64, I64, I64, ctypes.c_float,
                                  ctypes.c_float, I64, P, P, P]),
+    "mono_qk_norm_rope_kv_streams": (I, [P, I64, I64, P, I64, P, I64, P, P, P, P, P, I64, P, I64, I64, I64, I64,
+                                         ctypes.c_float, ctypes.c_float, I64, P, P, P]),
     "mono_tree_attention_workspace": (SZ, [I64, I64]),
+    "mono_tree_attention_streams_workspace": (SZ, [I64, I64, I64]),
+    "mono_tree_attention_streams": (I, [P, P, P, P, P, P, P, I64, I64, I64, I64, I64, P, P, SZ, P]),
+    "mono_gdn_step_streams_workspace": (SZ, [I64, I64, I64, I64]),
+    "mono_gdn_step_deferred_streams": (I, [P, P, P, P, P, P, P, P, P, P, ctypes.c_float, ctypes.c_float, I64, I64, I64,
+                                           I64, P, P, I64, P, P, P, P, P, P, I64, I64, I64, P, SZ, P]),
     "mono_tree_attention": (I, [P, P, P, P, P, P, P, I64, I64, I64, I64, P, P, SZ, P]),
     "mono_gdn_step_workspace": (SZ, [I64, I64, I64]),
     "mono_rowlin_gptq_workspace": (SZ, [I64]),
@@ -56,7 +63,7 @@ SIGNATURES = {
                                    P, P, P, P, P, I64, I64, I64, P, SZ, P]),
     "mono_gemv_bf16": (I, [P, I64, P, I64, I64, I64, P, I64, P]),
     "mono_lmhead_workspace": (SZ, []),
-    "mono_lmhead_pick": (I, [P, I64, P, I64, I64, I64, I64, I64, P, P, P, P, P, P, SZ, P]),
+    "mono_lmhead_pick": (I, [P, I64, P, I64, I64, I64, I64, I64, P, P, P, P, P, I64, P, SZ, P]),
     "mono_allreduce2_area_bytes": (SZ, [I64]),
     "mono_p2p_area_alloc": (I, [SZ, P]),
     "mono_p2p_area_free": (I, [P]),

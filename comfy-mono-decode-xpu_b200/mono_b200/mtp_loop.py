@@ -68,6 +68,27 @@ def generate_device(decoder, max_new_tokens, stop_tokens=(), sync_every=8):
     return out
 
 
+def generate_device_streams(decoder, max_new_tokens, sync_every=8):
+    """generate_device for a batch of streams (mono_b200.streams.Qwen35W4A8Streams): each step's result rows [B, 32]
+    go to a device ring read back every `sync_every` steps; runs until every stream has max_new_tokens. Returns the
+    committed tokens of each stream."""
+    step = getattr(decoder, "step_graphed", None) or decoder.step
+    B = decoder.streams
+    out = [[] for _ in range(B)]
+    ring = None
+    while min(len(o) for o in out) < max_new_tokens:
+        for i in range(sync_every):
+            r = step()
+            if ring is None:
+                ring = torch.empty((sync_every,) + tuple(r.shape), dtype=r.dtype, device=r.device)
+            ring[i].copy_(r)
+        for rows in ring.cpu().tolist():
+            for b, r in enumerate(rows):
+                if len(out[b]) < max_new_tokens:
+                    out[b].extend(r[1:1 + r[0]][:max_new_tokens - len(out[b])])
+    return out
+
+
 def install(q35=None, llama=None):
     if MODE == "0":
         return False

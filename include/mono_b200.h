@@ -190,6 +190,16 @@ MONO_API int mono_qk_norm_rope_kv(const void* rawq, int64_t q_row_stride, int64_
                                   const void* wk, const float* freqs, void* key_cache, void* value_cache, int64_t cap,
                                   const int64_t* position, int64_t S, int64_t Hq, int64_t Hk, float epsq, float epsk,
                                   int64_t rd, void* out_q, void* out_k, mono_stream_t stream);
+/* The same for `streams` batched decode streams (1 <= streams <= 8) sharing one launch: rows [b R, (b + 1) R) of
+ * the S = streams x R rows (R <= 8) are stream b's; its caches are heads [b Hk, (b + 1) Hk) of key/value caches
+ * bf16 [streams][Hk][cap][256]; out_q bf16 [streams][Hq][R][256], out_k bf16 [streams][Hk][R][256]. Each row's
+ * result is the one-stream call's (streams = 1 is mono_qk_norm_rope_kv). */
+MONO_API int mono_qk_norm_rope_kv_streams(const void* rawq, int64_t q_row_stride, int64_t q_head_stride,
+                                          const void* rawk, int64_t k_row_stride, const void* v, int64_t v_row_stride,
+                                          const void* wq, const void* wk, const float* freqs, void* key_cache,
+                                          void* value_cache, int64_t cap, const int64_t* position, int64_t S,
+                                          int64_t streams, int64_t Hq, int64_t Hk, float epsq, float epsk, int64_t rd,
+                                          void* out_q, void* out_k, mono_stream_t stream);
 
 /* Tree decode attention (the role of the reference's attn_dpas, csrc/attn_dpas.sycl:269-342): every query row
  * (q head h, row s) attends the committed prefix [0, L) of the cache of kv head h / (H / Hk) and the tree
@@ -197,13 +207,23 @@ MONO_API int mono_qk_norm_rope_kv(const void* rawq, int64_t q_row_stride, int64_
  * for P V, fp32 accumulation, bf16 output. L = clamp(seqlen[0], 0, cap) is read on the device (no host sync).
  * q bf16 [H][S][256]; caches bf16 [Hk][cap][256]; xk, xv bf16 [Hk][S][256]; mask int32 [S] (NULL with S = 1:
  * the MTP draft row, prefix only); out bf16 [S][H * 256]. (H / Hk) * S <= 32, 1 <= S <= 8. workspace:
- * mono_tree_attention_workspace(Hk, cap) bytes (no initial contents needed); one call at a time per
- * workspace. Not bit-exact with any other implementation: results are within the tolerance of an fp64
+ * mono_tree_attention_workspace(Hk, cap) bytes, zero-filled before its first use (the call leaves its arrival
+ * counters at zero again); one call at a time per workspace. Not bit-exact with any other implementation: results are within the tolerance of an fp64
  * reference stated by the tests. */
 MONO_API size_t mono_tree_attention_workspace(int64_t Hk, int64_t cap);
 MONO_API int mono_tree_attention(const void* q, const void* key_cache, const void* value_cache, const int32_t* seqlen,
                                  const void* xk, const void* xv, const int32_t* mask, int64_t H, int64_t Hk, int64_t S,
                                  int64_t cap, void* out, void* workspace, size_t workspace_bytes, mono_stream_t stream);
+/* The same for `streams` batched decode streams (1 <= streams <= 8) with one tree shape (mask int32 [S], shared):
+ * q bf16 [streams][H][S][256]; caches bf16 [streams][Hk][cap][256]; seqlen int32 [streams] (stream b's committed
+ * length); xk, xv bf16 [streams][Hk][S][256]; out bf16 [streams][S][H * 256]. Every stream's context is split as
+ * it would be alone, so each stream's output equals its one-stream call's. Workspace:
+ * mono_tree_attention_streams_workspace(Hk, streams, cap) bytes, zero-filled before first use. */
+MONO_API size_t mono_tree_attention_streams_workspace(int64_t Hk, int64_t streams, int64_t cap);
+MONO_API int mono_tree_attention_streams(const void* q, const void* key_cache, const void* value_cache,
+                                         const int32_t* seqlen, const void* xk, const void* xv, const int32_t* mask,
+                                         int64_t H, int64_t Hk, int64_t S, int64_t streams, int64_t cap, void* out,
+                                         void* workspace, size_t workspace_bytes, mono_stream_t stream);
 
 /* ---- Gated-DeltaNet ----------------------------------------------------------------------------------- */
 
@@ -244,6 +264,21 @@ MONO_API int mono_gdn_step_deferred(const void* qkv, const void* z, const void* 
                                     const void* prev_a, const void* prev_b, void* save_qkv, void* save_a, void* save_b,
                                     int64_t qkv_stride, int64_t z_stride, int64_t ab_stride, void* workspace,
                                     size_t workspace_bytes, mono_stream_t stream);
+/* The deferred form for `streams` batched decode streams (1 <= streams <= 8) in one launch pair: M rows per stream;
+ * qkv, z, a, b, core hold the streams' rows one after another (stream b's rows [b M, (b + 1) M), the row strides
+ * as above); conv_state bf16 [streams][C][3], state fp32 [streams][HV][128][128], ctl int32 [streams][ctl_stride
+ * >= 26], prev / save buffers [streams][8][C] and [streams][8][HV]; conv_w, dt_bias, g_decay, gnorm_w shared.
+ * Each stream's results are its one-stream call's. Workspace: mono_gdn_step_streams_workspace(M, C, HV, streams)
+ * bytes. */
+MONO_API size_t mono_gdn_step_streams_workspace(int64_t M, int64_t C, int64_t HV, int64_t streams);
+MONO_API int mono_gdn_step_deferred_streams(const void* qkv, const void* z, const void* a, const void* b,
+                                           const void* conv_w, void* conv_state, const float* dt_bias,
+                                           const float* g_decay, float* state, const void* gnorm_w, float gnorm_eps,
+                                           float qscale, int64_t M, int64_t HK, int64_t HV, int64_t streams, void* core,
+                                           const int32_t* ctl, int64_t ctl_stride, const void* prev_qkv,
+                                           const void* prev_a, const void* prev_b, void* save_qkv, void* save_a,
+                                           void* save_b, int64_t qkv_stride, int64_t z_stride, int64_t ab_stride,
+                                           void* workspace, size_t workspace_bytes, mono_stream_t stream);
 
 /* ---- small row kernels of the bf16 parts of the step (MTP draft head, final norm) ------------------------- */
 
@@ -311,23 +346,25 @@ MONO_API int mono_gemv_bf16(const void* x, int64_t x_stride, const void* w, int6
 
 /* bf16 lm_head with the pick fused: the verify's greedy logits + argmax (the reference's verify_logits then
  * lg.argmax, comfy_mono_decode_xpu/mtp_loop.py:325-327) and the draft pick (csrc/draft_lmhead.sycl:87-292: the
- * draft token, the top-n row and the children's verify tokens in one launch). For M <= 8 rows of x [M][x_stride]
+ * draft token, the top-n row and the children's verify tokens in one launch). For M <= 16 rows of x [M][x_stride]
  * against w [V][K]: logits = bf16(sum_k x[m][k] * w[n][k]) on the tensor cores (fp32 accumulation over a fixed
  * partition of K into 8 slices, the slices summed in order: the same bits on every launch), then per row
  *   argmax[m]   the argmax by the rank (float order, NaN largest, -0 == +0, smallest index on ties)
  *   topk[m][j]  j < k <= 8, descending by the top-k rank (the reference's fast_topk tie order)
  *   logits      (optional, NULL: not written) bf16 [M][V]
- * and, with children (device int32, up to 8 slots of dst, -1 ends) and dst (device int64), M == 1: dst[children[0]]
- * = argmax, dst[children[j]] = topk[j] for 1 <= j < k (the draft token and its siblings' tokens). index_base: the
+ * and, with children (device int32, up to 8 slots of a dst row, -1 ends) and dst (device int64), for every row m:
+ * d = dst + m * dst_stride (dst_stride >= 8 when M > 1), d[children[0]] = argmax, d[children[j]] = topk[j] for
+ * 1 <= j < k (a draft token and its siblings' tokens; one row per batched stream). index_base: the
  * vocabulary index of w's row 0 (a tensor-parallel shard; 0 otherwise): ranks and written indices are
  * index_base + row, so the shards' candidates merge into the whole vocabulary's pick. K % 512 == 0, M x rows of
- * K fitting in shared memory next to the rings (K <= 4096 at M = 8);
+ * K fitting in shared memory next to the rings (K <= 4096 at M = 16);
  * workspace: mono_lmhead_workspace() bytes, zero-filled before first use (the kernel leaves it reusable); one call
  * at a time per workspace. */
 MONO_API size_t mono_lmhead_workspace(void);
 MONO_API int mono_lmhead_pick(const void* x, int64_t x_stride, const void* w, int64_t M, int64_t V, int64_t K, int64_t k,
                               int64_t index_base, void* logits, int64_t* argmax, int64_t* topk, const int32_t* children,
-                              int64_t* dst, void* workspace, size_t workspace_bytes, mono_stream_t stream);
+                              int64_t* dst, int64_t dst_stride, void* workspace, size_t workspace_bytes,
+                              mono_stream_t stream);
 
 /* ---- two-GPU one-shot all-reduce (the tensor-parallel variant's residual sum) ------------------------------
  * Each rank allocates an area of mono_allreduce2_area_bytes(cap) bytes with mono_p2p_area_alloc (its own

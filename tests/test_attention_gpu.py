@@ -112,3 +112,37 @@ def test_tree_attention_within_tolerance_of_fp64(cuda, L, cap, parents):
     assert np.isfinite(o).all()
     assert (err <= 8e-3 + 2 ** -7 * np.abs(ref)).all(), (err.max(), (err - 2 ** -7 * np.abs(ref)).max())
     assert err.mean() <= 1e-3, err.mean()
+
+
+@pytest.mark.parametrize("S,lens", [(8, (1030, 517)), (1, (1000, 64)), (8, (0, 300))])
+def test_batched_streams_equal_one_stream_calls(cuda, S, lens):
+    """qk_norm_rope_kv and tree attention over two batched streams (mono_*_streams: stacked heads, one length per
+    stream) give exactly each stream's one-stream results, caches included."""
+    from mono_b200 import _C
+    H, HK, D, cap, B = 16, 4, 256, 1152, 2
+    g = torch.Generator().manual_seed(S + lens[0])
+    qg = torch.randn(1, B * S, H, 512, generator=g).bfloat16().to(cuda)
+    rk = torch.randn(1, B * S, HK, D, generator=g).bfloat16().to(cuda)
+    v = torch.randn(1, B * S, HK, D, generator=g).bfloat16().to(cuda)
+    wq = (1 + torch.randn(D, generator=g) * .3).bfloat16().to(cuda)
+    wk = (1 + torch.randn(D, generator=g) * .3).bfloat16().to(cuda)
+    f = torch.randn(B * S, 32, 2, 2, generator=g).to(cuda)
+    kc = torch.randn(1, B * HK, cap, D, generator=g).bfloat16().to(cuda)
+    vc = torch.randn(1, B * HK, cap, D, generator=g).bfloat16().to(cuda)
+    pos = torch.cat([torch.arange(S) + lens[b] for b in range(B)]).to(cuda)
+    mask = torch.tensor(oa.tree_mask([-1, 0, 1, 2, 3, 0, 5, 1][:S]) if S > 1 else [], dtype=torch.int32).to(cuda)
+    seq = torch.tensor(lens, dtype=torch.int32).to(cuda)
+    kc1, vc1 = kc.clone(), vc.clone()
+    q, k = _C.qk_norm_rope_kv(qg[..., :D], rk, v, wq, wk, f, kc, vc, pos, 1e-6, 1e-6, 64, streams=B)
+    xv = v.view(B, S, HK, D).permute(0, 2, 1, 3).reshape(1, B * HK, S, D)
+    out = _C.attn_dpas(q, kc, vc, seq, k, xv, mask, streams=B)
+    for b in range(B):
+        rows = slice(b * S, (b + 1) * S)
+        heads = slice(b * HK, (b + 1) * HK)
+        kcb, vcb = kc1[:, heads].contiguous(), vc1[:, heads].contiguous()
+        qb, kb = _C.qk_norm_rope_kv(qg[:, rows, :, :D], rk[:, rows], v[:, rows], wq, wk, f[rows].contiguous(), kcb, vcb,
+                                    pos[rows].contiguous(), 1e-6, 1e-6, 64)
+        assert torch.equal(qb[0], q[0, b * H:(b + 1) * H]) and torch.equal(kb[0], k[0, heads])
+        assert torch.equal(kcb, kc[:, heads]) and torch.equal(vcb, vc[:, heads])
+        ob = _C.attn_dpas(qb, kcb, vcb, seq[b:b + 1], kb, v[:, rows].transpose(1, 2), mask)
+        assert torch.equal(ob[0], out[0, rows]), b

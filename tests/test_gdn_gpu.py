@@ -143,3 +143,44 @@ def test_gdn_deferred_tree_verify_then_replay_off_chain(cuda, path):
     assert np.abs(o2 - ref2).mean() <= 2e-3 * np.abs(ref2).mean()
     assert np.array_equal(bf16_bits(cs), hist2)
     assert (np.abs(st.cpu().numpy() - state2) <= 1e-4 * (1 + np.abs(state2))).all()
+
+
+def test_deferred_streams_equal_one_stream_calls(cuda):
+    """mono_gdn_step_deferred_streams: two streams in one launch pair give exactly the two one-stream calls'
+    outputs, states, conv states and saved rows (different replay counts per stream)."""
+    from mono_b200 import _C
+    HK, HV, M, B = 4, 8, 8, 2
+    C = (2 * HK + HV) * 128
+    g = torch.Generator().manual_seed(5)
+    r = lambda *s, sc=1.0: (torch.randn(*s, generator=g) * sc)  # noqa: E731
+    qkv = r(B * M, C).bfloat16().to(cuda)
+    z = r(B * M, HV * 128).bfloat16().to(cuda)
+    ab = r(B * M, 2 * HV).bfloat16().to(cuda)
+    conv_w = r(C, 4, sc=0.5).bfloat16().to(cuda)
+    conv = r(B, C, 3).bfloat16().to(cuda)
+    dt = r(HV, sc=0.1).to(cuda)
+    gd = -r(HV).abs().to(cuda)
+    state = r(B, HV, 128, 128, sc=0.1).to(cuda)
+    gw = (1 + r(128, sc=0.1)).bfloat16().to(cuda)
+    prev = (r(B, 8, C).bfloat16().to(cuda), r(B, 8, HV).bfloat16().to(cuda), r(B, 8, HV).bfloat16().to(cuda))
+    save = tuple(torch.zeros_like(t) for t in prev)
+    ctl = torch.zeros(B, 26, dtype=torch.int32)
+    prog = og.tree_program(TREE8_PARENTS, 8)
+    for b, path in enumerate(([0, 1, 6], [0])):  # accepted paths of the previous step, replayed first
+        ctl[b, 0] = len(path)
+        ctl[b, 2:10] = torch.tensor(path + list(range(len(path), 8)), dtype=torch.int32)
+        ctl[b, 10:26] = torch.tensor(TREE8_PARENTS + prog, dtype=torch.int32)
+    ctl = ctl.to(cuda)
+    ones = [dict(conv=conv[b].clone(), state=state[b].clone(), save=tuple(torch.zeros_like(t[b]) for t in prev))
+            for b in range(B)]
+    core = _C.gdn_step_deferred(qkv, z, ab[:, :HV], ab[:, HV:], conv_w, conv, dt, gd, state, gw, 1e-6, 128 ** -0.5, HK,
+                                ctl, prev, save, streams=B)
+    for b in range(B):
+        rows = slice(b * M, (b + 1) * M)
+        o = ones[b]
+        cb = _C.gdn_step_deferred(qkv[rows], z[rows], ab[rows, :HV], ab[rows, HV:], conv_w, o["conv"], dt, gd,
+                                  o["state"], gw, 1e-6, 128 ** -0.5, HK, ctl[b], tuple(t[b] for t in prev), o["save"])
+        assert torch.equal(cb, core[rows]), b
+        assert torch.equal(o["state"], state[b]) and torch.equal(o["conv"], conv[b])
+        for q in range(3):
+            assert torch.equal(o["save"][q], save[q][b])
