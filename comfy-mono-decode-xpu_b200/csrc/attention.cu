@@ -41,6 +41,7 @@ constexpr int kHD = 256;
 
 __global__ void __launch_bounds__(32) qk_norm_rope_kv_kernel(const NormRopeArgs A) {
     __shared__ __align__(16) uint16_t nrm[kHD];
+    pdl_launch_dependents();  // an ordinary launch (its inputs are complete): the attention may launch at once
     const int lane = threadIdx.x;
     const int s = blockIdx.x / (A.Hq + 2 * A.Hk), h = blockIdx.x % (A.Hq + 2 * A.Hk);
     // batched streams: rows [b R, (b + 1) R) are stream b's, its caches are kv heads [b Hk, (b + 1) Hk)
@@ -253,6 +254,28 @@ __global__ void __cluster_dims__(kAttCluster, 1, 1) __launch_bounds__(kAttThread
     if (cg0 >= live) return;  // the whole cluster: no chunk of it has work
     const int groups = A.H / A.Hk, R = groups * A.S;
     const int t0 = chunk * per, t1 = (t0 + per < L) ? t0 + per : L;
+    const uint16_t* kbase = A.kc + size_t(kh) * A.cap * kHD;
+    const uint16_t* vbase = A.vc + size_t(kh) * A.cap * kHD;
+    // Before the dependency wait (a launch with programmatic dependency on the Q / K norm + KV write): the chunk's
+    // first K / V tile when the preceding kernel cannot have written it. That kernel writes this call's rows at
+    // their positions: past the prefix with a tree mask, the prefix's last S tokens for the draft row.
+    const int fresh = A.mask != nullptr ? L : L - A.S;
+    const bool early = chunk < active && t0 < t1 && t0 + ((t1 - t0) < kAttTile ? (t1 - t0) : kAttTile) <= fresh;
+    auto load_tile = [&](int tt, int nvalid) {
+        for (int i = tid; i < kAttTile * (kHD / 8); i += kAttThreads) {
+            const int r = i / (kHD / 8), c = i % (kHD / 8);
+            if (r < nvalid) {
+                cp_async16(Ks + r * kQPitch + c * 8, kbase + size_t(tt + r) * kHD + c * 8);
+                cp_async16(Vs + r * kQPitch + c * 8, vbase + size_t(tt + r) * kHD + c * 8);
+            } else {
+                reinterpret_cast<uint4*>(Ks + r * kQPitch)[c] = make_uint4(0, 0, 0, 0);
+                reinterpret_cast<uint4*>(Vs + r * kQPitch)[c] = make_uint4(0, 0, 0, 0);
+            }
+        }
+    };
+    if (early) load_tile(t0, (t1 - t0) < kAttTile ? (t1 - t0) : kAttTile);
+    pdl_wait();
+    pdl_launch_dependents();  // after the wait: a dependent's early loads never see this kernel's inputs change
     {  // the rows a merging warp finishes (q row, tree rows' k and v: 128-byte lines) into L2 ahead of use
         const int r = (chunk % kAttCluster) * 4 + warp;
         if (r < R && A.mask != nullptr) {
@@ -283,21 +306,10 @@ __global__ void __cluster_dims__(kAttCluster, 1, 1) __launch_bounds__(kAttThread
             for (int i = 0; i < 4; ++i) O[mt][nt][i] = 0.f;
     // running max / sum of the rows this thread's fragments touch: rows g, g + 8 (m-tile 0), g + 16, g + 24
     float mrun[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY}, lrun[4] = {0.f, 0.f, 0.f, 0.f};
-    const uint16_t* kbase = A.kc + size_t(kh) * A.cap * kHD;
-    const uint16_t* vbase = A.vc + size_t(kh) * A.cap * kHD;
     for (int tt = t0; tt < t1; tt += kAttTile) {
         const int nvalid = (t1 - tt) < kAttTile ? (t1 - tt) : kAttTile;
         __syncthreads();  // the previous tile's K / V / P reads are done
-        for (int i = tid; i < kAttTile * (kHD / 8); i += kAttThreads) {
-            const int r = i / (kHD / 8), c = i % (kHD / 8);
-            if (r < nvalid) {
-                cp_async16(Ks + r * kQPitch + c * 8, kbase + size_t(tt + r) * kHD + c * 8);
-                cp_async16(Vs + r * kQPitch + c * 8, vbase + size_t(tt + r) * kHD + c * 8);
-            } else {
-                reinterpret_cast<uint4*>(Ks + r * kQPitch)[c] = make_uint4(0, 0, 0, 0);
-                reinterpret_cast<uint4*>(Vs + r * kQPitch)[c] = make_uint4(0, 0, 0, 0);
-            }
-        }
+        if (!(early && tt == t0)) load_tile(tt, nvalid);
         cp_async_commit();
         cp_async_wait<0>();
         __syncthreads();
@@ -573,8 +585,18 @@ int launch_tree_attention(AttnArgs A, void* ws, cudaStream_t stream) {
         attr_err = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     });
     CUDA_TRY(attr_err);
-    attn_kernel<<<dim3(A.chunks, A.Hk), kAttThreads, smem, stream>>>(A);
-    CUDA_TRY(cudaGetLastError());
+    // programmatic dependency on the preceding kernel (the Q / K norm + KV write): griddepcontrol.wait inside
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(A.chunks, A.Hk);
+    cfg.blockDim = dim3(kAttThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, attn_kernel, A));
     return MONO_OK;
 }
 

@@ -59,7 +59,7 @@ __device__ __forceinline__ GdnArgs gdn_stream(const GdnArgs& A0, int b) {
 
 __global__ void __launch_bounds__(kConvThreads) gdn_conv_kernel(const GdnArgs A0) {
     const GdnArgs A = gdn_stream(A0, blockIdx.y);
-    gdn_conv_item(A, blockIdx.x * blockDim.x + threadIdx.x);
+    gdn_conv_item<true>(A, blockIdx.x * blockDim.x + threadIdx.x);
 }
 
 // Kernel 2 runs as a cluster of 4 CTAs per value head (128 CTAs at 32 heads): CTA c of the cluster keeps value
@@ -88,8 +88,15 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
     const int rg = warp, col = cr * kDcCols + lane;
     const int kh = h / (A.HV / A.HK), KD = A.HK * kDH, M = A.M;
     const int n = gdn_pending_s(A, cs), R = n + M;
-    // The rows' q, k (key head kh, element tid) and v (this CTA's 32 columns) with every load issued before the
-    // first store: one L2 round trip, not one per row.
+    // The recurrent state (written by this kernel's previous launch for the layer) before the dependency wait;
+    // then the rows' q, k (key head kh, element tid) and v (this CTA's 32 columns) with every load issued before
+    // the first store: one L2 round trip, not one per row.
+    float st[kRPG];
+    float* S = A.state + (size_t(h) * kDH + rg * kRPG) * kDH + col;
+#pragma unroll
+    for (int r = 0; r < kRPG; ++r) st[r] = S[size_t(r) * kDH];
+    pdl_wait();
+    pdl_launch_dependents();
     static_assert(kRG * kDcCols == kDH, "one thread per q / k element");
     float qr[kGdnMaxAll], kr0[kGdnMaxAll], vr[kGdnMaxAll / kRG];
 #pragma unroll
@@ -104,10 +111,6 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
         if (t < R) vr[j] = bf16_bits_to_f32(__ldcg(A.conv_out + size_t(t) * A.C + 2 * KD + h * kDH + cr * kDcCols + lane));
     }
     const float g0 = tid < 2 * R ? __ldcg(A.gates + ((tid >> 1) * A.HV + h) * 2 + (tid & 1)) : 0.f;
-    float st[kRPG];
-    float* S = A.state + (size_t(h) * kDH + rg * kRPG) * kDH + col;
-#pragma unroll
-    for (int r = 0; r < kRPG; ++r) st[r] = S[size_t(r) * kDH];
 #pragma unroll
     for (int t = 0; t < kGdnMaxAll; ++t)
         if (t < R) {
@@ -218,6 +221,7 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
 }
 
 // a | b projection: the CTA copies the M rows into shared memory; its 8 warps take the 4 quarters of 2 columns.
+// Launched with a programmatic dependency: the weights load before griddepcontrol.wait, the rows after it.
 __global__ void __launch_bounds__(256) gdn_ab_kernel(const uint16_t* x, int64_t x_stride, const uint16_t* w, int K,
                                                       int M, int N, uint16_t* out, int64_t out_stride) {
     extern __shared__ __align__(16) uint16_t xs[];
@@ -226,6 +230,8 @@ __global__ void __launch_bounds__(256) gdn_ab_kernel(const uint16_t* x, int64_t 
     const int cl = warp >> 2, q = warp & 3, n = blockIdx.x * 2 + cl;
     uint4 wv[4];
     if (n < N) gdn_ab_load_w(w, K, n, q, lane, wv);  // in flight while the rows are copied
+    pdl_wait();
+    pdl_launch_dependents();  // after the wait: a dependent's early loads never see this kernel's inputs change
     // the rows in batches of 16 pieces per thread, every load of a batch issued before its stores (one L2 round
     // trip per batch instead of one per piece)
     for (int base = 0; base < M * per; base += 16 * 256) {
@@ -268,8 +274,17 @@ int launch_gdn_ab(const uint16_t* x, int64_t x_stride, const uint16_t* w, int K,
             opt_in = smem;
         }
     }
-    gdn_ab_kernel<<<(N + 1) / 2, 256, smem, stream>>>(x, x_stride, w, K, M, N, out, out_stride);
-    CUDA_TRY(cudaGetLastError());
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((N + 1) / 2);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, gdn_ab_kernel, x, x_stride, w, K, M, N, out, out_stride));
     return MONO_OK;
 }
 
@@ -285,9 +300,21 @@ int launch_gdn_step(GdnArgs A, void* ws, cudaStream_t stream) {
     A.gates = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + (rows * A.streams * A.C * 2 + 255) / 256 * 256);
     const int rmax = int(rows);
     const int nthreads = A.C > rmax * A.HV ? A.C : rmax * A.HV;
-    gdn_conv_kernel<<<dim3((nthreads + kConvThreads - 1) / kConvThreads, A.streams), kConvThreads, 0, stream>>>(A);
-    CUDA_TRY(cudaGetLastError());
-    gdn_delta_kernel<<<dim3(A.HV * kDcCtas, A.streams), kRG * kDcCols, 0, stream>>>(A);
+    // both with a programmatic dependency on their predecessor (griddepcontrol.wait inside, after the loads that
+    // no recent kernel writes)
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((nthreads + kConvThreads - 1) / kConvThreads, A.streams);
+    cfg.blockDim = dim3(kConvThreads);
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, gdn_conv_kernel, A));
+    cfg.gridDim = dim3(A.HV * kDcCtas, A.streams);
+    cfg.blockDim = dim3(kRG * kDcCols);
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, gdn_delta_kernel, A));
     CUDA_TRY(cudaGetLastError());
     return MONO_OK;
 }

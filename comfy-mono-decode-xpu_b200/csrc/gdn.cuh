@@ -104,6 +104,10 @@ __device__ __forceinline__ float pick(const float (&a)[N], int i) {
 // conv state after the replay), newest first (csrc/mono_gdn.sycl:313-375). The conv state becomes the three
 // newest committed inputs (the replayed rows in the deferred form, all rows in the committing form). All
 // activations are read through L2 (they may have been written by this launch).
+// PDL (a launch with programmatic dependency): the inputs no recent kernel writes (ctl words, the replay rows
+// saved by the previous step, conv weights and state, gate parameters) are loaded before griddepcontrol.wait,
+// this step's rows (qkv, a, b) after it.
+template <bool PDL = false>
 __device__ __forceinline__ void gdn_conv_item(const GdnArgs& A, int i) {
     // Loads in two round trips: the ctl words (pending count, slots, parents), then every input this item reads;
     // no store before the last load (a load after a store the compiler cannot prove disjoint waits for it).
@@ -133,36 +137,45 @@ __device__ __forceinline__ void gdn_conv_item(const GdnArgs& A, int i) {
     const bool gating = i < R * A.HV;
     const bool conv = i < A.C;
     uint16_t sa = 0, sb = 0, ab = 0, bb = 0;
-    if (saving) {
-        const int t = i / A.HV, h = i % A.HV;
-        sa = __ldcg(A.a + size_t(t) * A.ab_stride + h);
-        sb = __ldcg(A.b + size_t(t) * A.ab_stride + h);
-    }
     float dtb = 0.f, gdec = 0.f;
+    const int gt = i / A.HV, gh = i % A.HV;  // gating / saving: row gt, value head gh
     if (gating) {
-        const int t = i / A.HV, h = i % A.HV;
         int st = 0;
 #pragma unroll
         for (int u = 0; u < kGdnMaxRows; ++u)
-            if (u == t) st = slot[u];
-        ab = t < n ? __ldcg(A.prev_a + size_t(st) * A.HV + h) : __ldcg(A.a + size_t(t - n) * A.ab_stride + h);
-        bb = t < n ? __ldcg(A.prev_b + size_t(st) * A.HV + h) : __ldcg(A.b + size_t(t - n) * A.ab_stride + h);
-        dtb = A.dt_bias[h];
-        gdec = A.g_decay[h];
+            if (u == gt) st = slot[u];
+        if (gt < n) {
+            ab = __ldcg(A.prev_a + size_t(st) * A.HV + gh);
+            bb = __ldcg(A.prev_b + size_t(st) * A.HV + gh);
+        }
+        dtb = A.dt_bias[gh];
+        gdec = A.g_decay[gh];
     }
     uint16_t rp[kGdnMaxRows], rv[kGdnMaxRows];  // raw inputs of the replayed rows / of the verify rows
     float w[4], hist[3 + kGdnMaxRows], vr[kGdnMaxRows];
     if (conv) {
 #pragma unroll
-        for (int t = 0; t < kGdnMaxRows; ++t) {
-            rp[t] = t < n ? __ldcg(A.prev_qkv + size_t(slot[t]) * A.C + i) : uint16_t(0);
-            rv[t] = t < A.M ? __ldcg(A.qkv + size_t(t) * A.qkv_stride + i) : uint16_t(0);
-        }
+        for (int t = 0; t < kGdnMaxRows; ++t) rp[t] = t < n ? __ldcg(A.prev_qkv + size_t(slot[t]) * A.C + i) : uint16_t(0);
 #pragma unroll
         for (int d = 0; d < 4; ++d) w[d] = bf16_bits_to_f32(A.conv_w[size_t(i) * 4 + d]);
 #pragma unroll
         for (int r = 0; r < 3; ++r) hist[r] = bf16_bits_to_f32(A.conv_state[size_t(i) * 3 + r]);
     }
+    if constexpr (PDL) {
+        pdl_wait();  // this step's rows: written by the preceding kernels
+        pdl_launch_dependents();  // after the wait: a dependent's early reads never see this kernel's inputs change
+    }
+    if (saving) {
+        sa = __ldcg(A.a + size_t(gt) * A.ab_stride + gh);
+        sb = __ldcg(A.b + size_t(gt) * A.ab_stride + gh);
+    }
+    if (gating && gt >= n) {
+        ab = __ldcg(A.a + size_t(gt - n) * A.ab_stride + gh);
+        bb = __ldcg(A.b + size_t(gt - n) * A.ab_stride + gh);
+    }
+    if (conv)
+#pragma unroll
+        for (int t = 0; t < kGdnMaxRows; ++t) rv[t] = t < A.M ? __ldcg(A.qkv + size_t(t) * A.qkv_stride + i) : uint16_t(0);
     if (gating) {
         const float av = bf16_bits_to_f32(ab) + dtb;
         const float sp = av > 20.f ? av : logf(1.f + expf(av));

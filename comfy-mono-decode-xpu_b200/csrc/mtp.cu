@@ -17,6 +17,7 @@ constexpr int kSlots = 8, kRanks = 7;
 __global__ void __launch_bounds__(256) mtp_prep_draft_kernel(const int64_t* st, int64_t k, const float* ftab, int64_t n,
                                                              int64_t cap, float* freqs, int64_t* mpos, int np,
                                                              int32_t* mseq) {
+    pdl_launch_dependents();  // an ordinary launch: its inputs are complete; the next kernel may start
     const int t = threadIdx.x;
     const int64_t p = st[0] + k, m = st[1] + k;
     const int64_t row = p < cap ? (p < 0 ? 0 : p) : cap - 1;
@@ -29,6 +30,7 @@ __global__ void __launch_bounds__(64) mtp_prep_verify_kernel(const int64_t* st, 
                                                              int64_t* vpos, const int64_t* tree_pos, int rows,
                                                              int32_t* ctl, const int32_t* tree_ctl, int parity,
                                                              int64_t rope_offset) {
+    pdl_launch_dependents();  // an ordinary launch: its inputs are complete; the next kernel may start
     const int t = threadIdx.x;
     const int64_t pos = st[0];
     if (t < np) apos[t] = pos + t;

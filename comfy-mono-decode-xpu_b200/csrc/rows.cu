@@ -14,6 +14,7 @@ __global__ void __launch_bounds__(256) rmsnorm_add_kernel(const uint16_t* __rest
                                                           const uint16_t* __restrict__ w, float eps, int H, int64_t x_stride,
                                                           int64_t add_stride, int64_t out_stride, uint16_t* __restrict__ out,
                                                           uint16_t* __restrict__ sum_out) {
+    pdl_launch_dependents();  // an ordinary launch: its inputs are complete; the next kernel may start
     __shared__ float red[8];
     const int m = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5, P = H >> 3;
     const uint16_t* xr = x + size_t(m) * x_stride;
@@ -61,6 +62,7 @@ __global__ void __launch_bounds__(256) lut_mul_kernel(const uint16_t* __restrict
                                                       const uint16_t* __restrict__ b, int64_t b_stride,
                                                       int64_t b_head_stride, const uint16_t* __restrict__ lut, int K,
                                                       uint16_t* __restrict__ out, int64_t out_stride) {
+    pdl_launch_dependents();  // an ordinary launch: its inputs are complete; the next kernel may start
     const int m = blockIdx.y;
     const int c0 = (blockIdx.x * 256 + threadIdx.x) * 8;
     if (c0 >= K) return;

@@ -208,7 +208,9 @@ MONO_API int mono_qk_norm_rope_kv_streams(const void* rawq, int64_t q_row_stride
  * q bf16 [H][S][256]; caches bf16 [Hk][cap][256]; xk, xv bf16 [Hk][S][256]; mask int32 [S] (NULL with S = 1:
  * the MTP draft row, prefix only); out bf16 [S][H * 256]. (H / Hk) * S <= 32, 1 <= S <= 8. workspace:
  * mono_tree_attention_workspace(Hk, cap) bytes, zero-filled before its first use (the call leaves its arrival
- * counters at zero again); one call at a time per workspace. Not bit-exact with any other implementation: results are within the tolerance of an fp64
+ * counters at zero again); one call at a time per workspace. Launch order: the kernel carries a programmatic
+ * dependency on the preceding kernel and may load K / V tiles of the prefix before waiting for it: the prefix
+ * [0, L) (with a mask; [0, L - S) without) must not be written by the two kernels launched just before the call. Not bit-exact with any other implementation: results are within the tolerance of an fp64
  * reference stated by the tests. */
 MONO_API size_t mono_tree_attention_workspace(int64_t Hk, int64_t cap);
 MONO_API int mono_tree_attention(const void* q, const void* key_cache, const void* value_cache, const int32_t* seqlen,
@@ -241,6 +243,9 @@ MONO_API int mono_tree_attention_streams(const void* q, const void* key_cache, c
  * fp32 arithmetic; results within the tolerance of an fp64 reference stated by the tests. workspace:
  * mono_gdn_step_workspace(M, C, HV) bytes (256-byte aligned). */
 MONO_API size_t mono_gdn_step_workspace(int64_t M, int64_t C, int64_t HV);  /* covers both forms */
+/* Launch order: the step's two kernels carry a programmatic dependency on the preceding kernel (they may start
+ * while it runs and wait for it before reading qkv, z, a, b): the ctl words, the replay / save buffers and the
+ * conv and recurrent states must not be written by the two kernels launched just before the call. */
 MONO_API int mono_gdn_step(const void* qkv, const void* z, const void* a, const void* b, const void* conv_w,
                            void* conv_state, const float* dt_bias, const float* g_decay, float* state,
                            const void* gnorm_w, float gnorm_eps, float qscale, int64_t M, int64_t HK, int64_t HV,
