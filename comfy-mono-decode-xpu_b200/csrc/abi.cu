@@ -232,7 +232,7 @@ int mono_mlp_gptq(const void* x, const void* norm_w, float eps, const void* gate
                   int64_t M, int64_t H, int64_t I, int residual, void* out, void* workspace, size_t workspace_bytes,
                   mono_stream_t stream) {
     MONO_CHECK(x && gate_q && up_q && down_q && silu_lut && out && workspace, "null operand");
-    MONO_CHECK(M >= 1 && M <= 16, "1 <= M <= 16 (got %lld)", (long long)M);
+    MONO_CHECK(M >= 1 && M <= kStreamMaxRows, "1 <= M <= %d (got %lld)", kStreamMaxRows, (long long)M);
     MONO_CHECK(H >= kChunkK && H % kChunkK == 0 && H <= 4096, "H must be a multiple of 1024 up to 4096");
     MONO_CHECK(I >= kChunkK && I % kChunkK == 0 && I <= kChunkK * kMaxChunks, "I must be a multiple of 1024 up to 16384");
     MONO_CHECK(workspace_bytes >= mlp_workspace_bytes(int(H), int(I)), "workspace too small (%zu < %zu)", workspace_bytes,
@@ -250,12 +250,13 @@ int mono_mlp_gptq(const void* x, const void* norm_w, float eps, const void* gate
     A.H = int(H);
     A.I = int(I);
     A.residual = residual != 0;
+    const size_t R = kStreamMaxRows;
     A.q1 = reinterpret_cast<int8_t*>(w);
-    w += al(16 * size_t(H));
+    w += al(R * size_t(H));
     A.h = reinterpret_cast<uint16_t*>(w);
-    w += al(16 * size_t(I) * 2);
+    w += al(R * size_t(I) * 2);
     A.q2 = reinterpret_cast<int8_t*>(w);
-    w += al(16 * size_t(I));
+    w += al(R * size_t(I));
     A.s1 = reinterpret_cast<float*>(w + 256);
     A.amax2 = reinterpret_cast<unsigned*>(w + 512);
     A.bar = reinterpret_cast<unsigned*>(w + 768);
@@ -483,7 +484,7 @@ int mono_rowlin_gptq(const void* x, int mode, const void* norm_w, float eps, con
                                        gate_row_stride % 8 == 0 && aligned(gate, 16)),
                "gate mode: gate (16-byte aligned, strides multiples of 8 elements) and lut");
     MONO_CHECK(nm >= 1 && nm <= 3, "1 to 3 matrices");
-    MONO_CHECK(M >= 1 && M <= 16, "1 <= M <= 16 (got %lld)", (long long)M);
+    MONO_CHECK(M >= 1 && M <= kStreamMaxRows, "1 <= M <= %d (got %lld)", kStreamMaxRows, (long long)M);
     MONO_CHECK(K >= kChunkK && K % kChunkK == 0 && K <= 4096, "K a multiple of 1024 up to 4096 (got %lld)", (long long)K);
     MONO_CHECK(workspace_bytes >= rowlin_workspace_bytes(int(K)) && aligned(workspace, 256), "workspace (mono_rowlin_gptq_workspace)");
     MONO_CHECK(aligned(x, 16) && aligned(out, 16) && (!xn_out || aligned(xn_out, 16)), "16-byte aligned rows");
@@ -514,7 +515,7 @@ int mono_rowlin_gptq(const void* x, int mode, const void* norm_w, float eps, con
     A.out = static_cast<uint16_t*>(out);
     A.xn_out = static_cast<uint16_t*>(xn_out);
     A.q = reinterpret_cast<int8_t*>(w);
-    const size_t qb = (16 * size_t(K) + 255) / 256 * 256;
+    const size_t qb = (size_t(kStreamMaxRows) * K + 255) / 256 * 256;
     A.s = reinterpret_cast<float*>(w + qb);
     A.bar = reinterpret_cast<unsigned*>(w + qb + 256);
     A.mode = mode;

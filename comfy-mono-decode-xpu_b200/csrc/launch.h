@@ -8,6 +8,9 @@ namespace mono {
 // Shared bytes after the staged rows for the fused quantization: 16 row scales + 8 reduction floats per
 // warp-group.
 constexpr int kQuantExtra = 256;
+// Rows of the fused MLP and the row linear (the verify rows of up to 4 batched decode streams); their
+// workspaces hold this many rows.
+constexpr int kStreamMaxRows = 32;
 
 struct LinearEpi {
     const uint16_t* xb;      // bf16 activations [M][K]: quantized per token inside the kernel (xs unused), or null
@@ -29,17 +32,18 @@ struct MlpArgs {
     int H, I, residual, max_items;
     // workspace
     int8_t* q1;       // [M][H]
-    float* s1;        // [16]
+    float* s1;        // [kStreamMaxRows]
     uint16_t* h;      // [M][I]
-    unsigned* amax2;  // [16] (float bits of non-negative values; zero between launches)
+    unsigned* amax2;  // [kStreamMaxRows] (float bits of non-negative values; zero between launches)
     int8_t* q2;       // [M][I] (only when the down phase's activations are not staged in shared memory)
     unsigned* bar;    // [2] grid barrier words (zero between launches)
 };
 // Shared-memory shape of a cooperative stream kernel: ring stages, partial bytes, staged-activation bytes.
 struct MlpShape {
     int S;
-    int part_bytes;  // partials of the larger phase
+    int part_bytes;  // partials of the larger phase's batch
     int x_bytes;     // staged activations of the larger staged phase
+    int tb0, tb1;    // tiles per batch of phase 0 and 1 (the partials of a batch fit part_bytes)
 };
 int launch_mlp(Program& P, MlpArgs& A, cudaStream_t stream);
 
@@ -54,8 +58,8 @@ struct RowLinArgs {
     const uint16_t* residual;  // [M][N] or null
     uint16_t* out;             // [M][N]
     uint16_t* xn_out;          // NORM: normalized rows [M][K], or null
-    int8_t* q;                 // workspace [16][K]
-    float* s;                  // workspace [16]
+    int8_t* q;                 // workspace [kStreamMaxRows][K]
+    float* s;                  // workspace [kStreamMaxRows]
     unsigned* bar;             // workspace [2], zero between launches
     int mode, N;
 };

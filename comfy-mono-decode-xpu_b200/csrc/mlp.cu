@@ -37,8 +37,8 @@ template <int MT, int CW, int PW>
 __global__ void __launch_bounds__((CW + PW) * 32, 1) mlp_kernel(const Program P, const MlpArgs A, const MlpShape Z) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float red[64];
-    __shared__ float s1s[16], s2s[16];
-    __shared__ unsigned rowmax[16];
+    __shared__ float s1s[kStreamMaxRows], s2s[kStreamMaxRows];
+    __shared__ unsigned rowmax[kStreamMaxRows];
     __shared__ int flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int M = P.M, S = Z.S;
@@ -74,23 +74,27 @@ __global__ void __launch_bounds__((CW + PW) * 32, 1) mlp_kernel(const Program P,
     for (int m = int(blockIdx.x); m < M; m += int(gridDim.x))
         norm_quant_row_cta<NT, kConsumerBar>(A.x + size_t(m) * A.H, A.norm_w, A.eps, A.H, nullptr, A.q1 + size_t(m) * A.H,
                                              A.s1 + m, red);
-    if (threadIdx.x < 16) rowmax[threadIdx.x] = 0u;
+    if (threadIdx.x < kStreamMaxRows) rowmax[threadIdx.x] = 0u;
     ok = grid_barrier_named<kConsumerBar, NT>(A.bar, epoch, &flag) && ok;
     if (threadIdx.x < M) s1s[threadIdx.x] = __ldcg(A.s1 + threadIdx.x);
     stage_x_consumers<CW>(A.q1, M, A.H, true, xsm);
     trace_stamp(2);
 
-    // ---- P2: gate / up, h = silu(g) * u, row maxima of |h| ----
+    // ---- P2: gate / up, h = silu(g) * u, row maxima of |h| (tiles in batches of Z.tb0: the partials of a batch
+    // fit the shared buffer; one batch unless the rows are many) ----
     {
         const PhaseDesc& ph = P.ph[0];
         const XSrc xs{xsm, A.H + 16, true, true};
-        const int C = phase_chunks(ph), ntl = cta_tiles(ph);
-        ok = consume_phase<FMT_GPTQ, LAYOUT_TILED, MT, CW>(P, 0, xs, ring, full, empty, S, part, warp, lane) && ok;
+        const int C = phase_chunks(ph), ntl = cta_tiles(ph), TB = Z.tb0;
+        for (int k0 = 0; k0 < ntl && ok; k0 += TB) {
+        const int kb = ntl - k0 < TB ? ntl - k0 : TB;
+        ok = consume_phase<FMT_GPTQ, LAYOUT_TILED, MT, CW>(P, 0, xs, ring, full, empty, S, part, warp, lane, k0 * 2 * C,
+                                                           kb * 2 * C) && ok;
         ok = consumer_sync_and<CW>(ok);
-        trace_stamp(3);
-        for (int e = threadIdx.x; e < ntl * M * 16 && ok; e += NT) {
+        if (k0 + kb >= ntl) trace_stamp(3);
+        for (int e = threadIdx.x; e < kb * M * 16 && ok; e += NT) {
             const int k = e / (M * 16), r = e - k * (M * 16), m = r >> 4, nl = r & 15;
-            const int n = cta_tile(ph, k) * 16 + nl;
+            const int n = cta_tile(ph, k0 + k) * 16 + nl;
             const uint32_t* pk = part + size_t(k) * 2 * C * MT * 128;
             const float s = s1s[m];
             const float tg = __uint_as_float(tile_total<FMT_GPTQ, MT>(pk, C, 0, m, nl));
@@ -101,7 +105,8 @@ __global__ void __launch_bounds__((CW + PW) * 32, 1) mlp_kernel(const Program P,
             A.h[size_t(m) * A.I + n] = hb;
             atomicMax(&rowmax[m], __float_as_uint(fabsf(bf16_bits_to_f32(hb))));
         }
-        consumer_sync<CW>();
+        consumer_sync<CW>();  // the batch's partials are read before the next batch writes them
+        }
         if (threadIdx.x < M) atomicMax(A.amax2 + threadIdx.x, rowmax[threadIdx.x]);
     }
     trace_stamp(4);
@@ -133,21 +138,26 @@ __global__ void __launch_bounds__((CW + PW) * 32, 1) mlp_kernel(const Program P,
     }
     trace_stamp(6);
 
-    // ---- P4: down (+ residual) ----
+    // ---- P4: down (+ residual), tiles in batches of Z.tb1 ----
     {
         const PhaseDesc& ph = P.ph[1];
-        const int C = phase_chunks(ph), ntl = cta_tiles(ph);
-        ok = consume_phase<FMT_GPTQ, LAYOUT_TILED, MT, CW>(P, 1, xs1, ring, full, empty, S, part, warp, lane) && ok;
-        ok = consumer_sync_and<CW>(ok);
-        trace_stamp(7);
-        for (int e = threadIdx.x; e < ntl * M * 16 && ok; e += NT) {
-            const int k = e / (M * 16), r = e - k * (M * 16), m = r >> 4, nl = r & 15;
-            const int n = cta_tile(ph, k) * 16 + nl;
-            const float tot = __uint_as_float(tile_total<FMT_GPTQ, MT>(part + size_t(k) * C * MT * 128, C, 0, m, nl));
-            uint16_t rr = f32_to_bf16_bits(__fmul_rn(tot, s2s[m]));
-            const size_t o = size_t(m) * A.H + n;
-            if (A.residual) rr = f32_to_bf16_bits(__fadd_rn(bf16_bits_to_f32(A.x[o]), bf16_bits_to_f32(rr)));
-            A.out[o] = rr;
+        const int C = phase_chunks(ph), ntl = cta_tiles(ph), TB = Z.tb1;
+        for (int k0 = 0; k0 < ntl && ok; k0 += TB) {
+            const int kb = ntl - k0 < TB ? ntl - k0 : TB;
+            ok = consume_phase<FMT_GPTQ, LAYOUT_TILED, MT, CW>(P, 1, xs1, ring, full, empty, S, part, warp, lane, k0 * C,
+                                                               kb * C) && ok;
+            ok = consumer_sync_and<CW>(ok);
+            if (k0 + kb >= ntl) trace_stamp(7);
+            for (int e = threadIdx.x; e < kb * M * 16 && ok; e += NT) {
+                const int k = e / (M * 16), r = e - k * (M * 16), m = r >> 4, nl = r & 15;
+                const int n = cta_tile(ph, k0 + k) * 16 + nl;
+                const float tot = __uint_as_float(tile_total<FMT_GPTQ, MT>(part + size_t(k) * C * MT * 128, C, 0, m, nl));
+                uint16_t rr = f32_to_bf16_bits(__fmul_rn(tot, s2s[m]));
+                const size_t o = size_t(m) * A.H + n;
+                if (A.residual) rr = f32_to_bf16_bits(__fadd_rn(bf16_bits_to_f32(A.x[o]), bf16_bits_to_f32(rr)));
+                A.out[o] = rr;
+            }
+            consumer_sync<CW>();
         }
     }
     trace_stamp(8);
@@ -156,7 +166,7 @@ __global__ void __launch_bounds__((CW + PW) * 32, 1) mlp_kernel(const Program P,
     if (threadIdx.x == 0) {
         __threadfence();
         if (atomicAdd(A.bar + 1, 1u) == gridDim.x - 1) {
-            for (int m = 0; m < 16; ++m) atomicExch(A.amax2 + m, 0u);
+            for (int m = 0; m < kStreamMaxRows; ++m) atomicExch(A.amax2 + m, 0u);
             atomicExch(A.bar, 0u);
             atomicExch(A.bar + 1, 0u);
         }
@@ -164,9 +174,10 @@ __global__ void __launch_bounds__((CW + PW) * 32, 1) mlp_kernel(const Program P,
 }
 
 size_t mlp_workspace_bytes(int H, int I) {
-    // q1, h, q2 (16 rows each), s1, amax2, barrier words; every piece 256-byte aligned
+    // q1, h, q2 (kStreamMaxRows rows each), s1, amax2, barrier words; every piece 256-byte aligned
     auto al = [](size_t b) { return (b + 255) / 256 * 256; };
-    return al(16 * size_t(H)) + al(16 * size_t(I) * 2) + al(16 * size_t(I)) + 4 * 256;
+    const size_t R = kStreamMaxRows;
+    return al(R * size_t(H)) + al(R * size_t(I) * 2) + al(R * size_t(I)) + 4 * 256;
 }
 
 template <int MT, int CW, int PW>
@@ -201,43 +212,58 @@ static int launch_mlp_t(const Program& P, const MlpArgs& A, const MlpShape& Z, s
 }
 
 
+// Stream configuration c of kStreamConfig (consumer and producer warps; the ring depth is the plan's).
+template <int MT>
+static int dispatch_mlp(int c, Program& P, MlpArgs& A, const MlpShape& Z, size_t smem, cudaStream_t stream) {
+    switch (c) {
+        case 0: return launch_mlp_t<MT, 10, 2>(P, A, Z, smem, stream);
+        case 2: return launch_mlp_t<MT, 12, 4>(P, A, Z, smem, stream);
+        default: return launch_mlp_t<MT, 8, 4>(P, A, Z, smem, stream);  // configs 1 and 3
+    }
+}
+
 int launch_mlp(Program& P, MlpArgs& A, cudaStream_t stream) {
     const int M = P.M, G = sm_count();
-    const bool two = M > 8;
-    const int MT = two ? 2 : 1;
-    // partials: the larger phase's items of one CTA
-    size_t part = 0;
-    for (int i = 0; i < P.nph; ++i) {
-        const int nt = phase_tiles(P.ph[i]), per_cta = (nt + G - 1) / G;
-        part = std::max(part, size_t(per_cta) * (P.ph[i].paired ? 2 : 1) * phase_chunks(P.ph[i]) * MT * 128 * 4);
+    const int MT = M > 16 ? 4 : (M > 8 ? 2 : 1);
+    // partials per tile (items x MT 8-row tiles x 128 words) and the CTA's tiles of each phase
+    int per_cta[2];
+    size_t tile_bytes[2];
+    for (int i = 0; i < 2; ++i) {
+        const int nt = phase_tiles(P.ph[i]);
+        per_cta[i] = (nt + G - 1) / G;
+        tile_bytes[i] = size_t(P.ph[i].paired ? 2 : 1) * phase_chunks(P.ph[i]) * MT * 128 * 4;
     }
     P.ph[0].rev = 0;
     P.ph[1].rev = 1;
     A.max_items = 0;
-    // the first phase's block is always staged (P1 writes it); the down phase's when it fits next to the ring
+    // the first phase's block is always staged (P1 writes it); the down phase's when it fits next to the ring.
+    // Pass 0: every tile's partials at once (one batch per phase); pass 1 (many rows): tiles in batches.
     P.ph[0].xsmem = 1;
-    for (int staged = 1; staged >= 0; --staged) {
-        P.ph[1].xsmem = staged;
-        size_t xb = size_t(M) * (P.ph[0].K + 16);
-        if (staged) xb = std::max(xb, size_t(M) * (P.ph[1].K + 16));
-        for (int c = 0; c < kStreamConfigs; ++c) {
-            const StreamConfig sc = kStreamConfig[c];
-            const StreamPlan plan(stage_bytes<FMT_GPTQ>(), sc.S, part, xb, 0);
-            if (plan.total > kStreamSmemLimit) continue;
-            const MlpShape Z{sc.S, int(part), int(xb)};
-#define MONO_MLP(MTV, CWV, PWV) return launch_mlp_t<MTV, CWV, PWV>(P, A, Z, plan.total, stream)
-            if (!two) {
-                if (c == 0) MONO_MLP(1, 10, 2);
-                if (c == 1) MONO_MLP(1, 8, 4);
-                MONO_MLP(1, 12, 4);
-            } else {
-                if (c == 0) MONO_MLP(2, 10, 2);
-                if (c == 1) MONO_MLP(2, 8, 4);
-                MONO_MLP(2, 12, 4);
+    for (int pass = 0; pass < 2; ++pass)
+        for (int staged = 1; staged >= 0; --staged) {
+            P.ph[1].xsmem = staged;
+            size_t xb = size_t(M) * (P.ph[0].K + 16);
+            if (staged) xb = std::max(xb, size_t(M) * (P.ph[1].K + 16));
+            for (int c = 0; c < kStreamConfigs; ++c) {
+                const StreamConfig sc = kStreamConfig[c];
+                int tb0 = per_cta[0], tb1 = per_cta[1];
+                if (pass == 1) {
+                    const StreamPlan bare(stage_bytes<FMT_GPTQ>(), sc.S, 0, xb, 0);
+                    if (bare.total >= kStreamSmemLimit) continue;
+                    const size_t budget = (kStreamSmemLimit - bare.total) / 128 * 128;
+                    tb0 = std::min<int>(tb0, int(budget / tile_bytes[0]));
+                    tb1 = std::min<int>(tb1, int(budget / tile_bytes[1]));
+                    if (tb0 < 1 || tb1 < 1) continue;
+                }
+                const size_t part = std::max(size_t(tb0) * tile_bytes[0], size_t(tb1) * tile_bytes[1]);
+                const StreamPlan plan(stage_bytes<FMT_GPTQ>(), sc.S, part, xb, 0);
+                if (plan.total > kStreamSmemLimit) continue;
+                const MlpShape Z{sc.S, int(part), int(xb), tb0, tb1};
+                if (MT == 1) return dispatch_mlp<1>(c, P, A, Z, plan.total, stream);
+                if (MT == 2) return dispatch_mlp<2>(c, P, A, Z, plan.total, stream);
+                return dispatch_mlp<4>(c, P, A, Z, plan.total, stream);
             }
-#undef MONO_MLP
         }
-    }
     return fail(MONO_EINVAL, "mlp: no shared-memory plan fits (M=%d)", M);
 }
 

@@ -566,11 +566,11 @@ int launch_program(const Op* ops_host, const Op* ops_dev, int nops, int M, unsig
 #define MONO_PG(MTV, CWV, PWV) return launch_program_t<MTV, CWV, PWV>(G, Z, plan.total, stream)
     if (!two) {
         if (c == 0) MONO_PG(1, 10, 2);
-        if (c == 1) MONO_PG(1, 8, 4);
+        if (c == 1 || c == 3) MONO_PG(1, 8, 4);
         MONO_PG(1, 12, 4);
     } else {
         if (c == 0) MONO_PG(2, 10, 2);
-        if (c == 1) MONO_PG(2, 8, 4);
+        if (c == 1 || c == 3) MONO_PG(2, 8, 4);
         MONO_PG(2, 12, 4);
     }
 #undef MONO_PG

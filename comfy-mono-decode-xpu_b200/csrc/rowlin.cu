@@ -9,6 +9,7 @@
 //   P2 all   out[m][n] = bf16(total[m][n] * s[m]) (+ residual: bf16(residual + that)) for the up to three
 //            matrices of the phase, outputs concatenated along n (row stride = the sum of their rows)
 // The producer warps stream the weights from the start, across the row phase and the grid barrier.
+#include <algorithm>
 #include <mutex>
 
 #include "launch.h"
@@ -73,23 +74,29 @@ __global__ void __launch_bounds__((CW + PW) * 32, 1) rowlin_kernel(const Program
         xs = XSrc{xsm, K + 16, true, true};
     }
     trace_stamp(3);
-    const int C = phase_chunks(ph), ntl = cta_tiles(ph);
-    ok = consume_phase<FMT_GPTQ, LAYOUT_TILED, MT, CW>(P, 0, xs, ring, full, empty, S, part, warp, lane) && ok;
-    ok = consumer_sync_and<CW>(ok);
-    for (int e = threadIdx.x; e < ntl * M * 16 && ok; e += NT) {
-        const int k = e / (M * 16), r = e - k * (M * 16), m = r >> 4, nl = r & 15;
-        const int n = (int(blockIdx.x) + k * int(gridDim.x)) * 16 + nl;  // concatenated output column
-        const float tot = __uint_as_float(tile_total<FMT_GPTQ, MT>(part + size_t(k) * C * MT * 128, C, 0, m, nl));
-        uint16_t rr = f32_to_bf16_bits(__fmul_rn(tot, __ldcg(A.s + m)));
-        const size_t o = size_t(m) * A.N + n;
-        if (A.residual) rr = f32_to_bf16_bits(__fadd_rn(bf16_bits_to_f32(A.residual[o]), bf16_bits_to_f32(rr)));
-        A.out[o] = rr;
+    // tiles in batches of Z.tb0 (the partials of a batch fit the shared buffer; one batch unless the rows are many)
+    const int C = phase_chunks(ph), ntl = cta_tiles(ph), TB = Z.tb0;
+    for (int k0 = 0; k0 < ntl && ok; k0 += TB) {
+        const int kb = ntl - k0 < TB ? ntl - k0 : TB;
+        ok = consume_phase<FMT_GPTQ, LAYOUT_TILED, MT, CW>(P, 0, xs, ring, full, empty, S, part, warp, lane, k0 * C,
+                                                           kb * C) && ok;
+        ok = consumer_sync_and<CW>(ok);
+        for (int e = threadIdx.x; e < kb * M * 16 && ok; e += NT) {
+            const int k = e / (M * 16), r = e - k * (M * 16), m = r >> 4, nl = r & 15;
+            const int n = (int(blockIdx.x) + (k0 + k) * int(gridDim.x)) * 16 + nl;  // concatenated output column
+            const float tot = __uint_as_float(tile_total<FMT_GPTQ, MT>(part + size_t(k) * C * MT * 128, C, 0, m, nl));
+            uint16_t rr = f32_to_bf16_bits(__fmul_rn(tot, __ldcg(A.s + m)));
+            const size_t o = size_t(m) * A.N + n;
+            if (A.residual) rr = f32_to_bf16_bits(__fadd_rn(bf16_bits_to_f32(A.residual[o]), bf16_bits_to_f32(rr)));
+            A.out[o] = rr;
+        }
+        consumer_sync<CW>();  // the batch's partials are read before the next batch writes them
     }
     trace_stamp(4);
     grid_exit_named<kConsumerBar, NT>(A.bar);
 }
 
-size_t rowlin_workspace_bytes(int K) { return (16 * size_t(K) + 255) / 256 * 256 + 3 * 256; }
+size_t rowlin_workspace_bytes(int K) { return (size_t(kStreamMaxRows) * K + 255) / 256 * 256 + 3 * 256; }
 
 template <int MT, int CW, int PW>
 static int launch_rowlin_t(const Program& P, const RowLinArgs& A, const MlpShape& Z, size_t smem, cudaStream_t stream) {
@@ -124,32 +131,44 @@ static int launch_rowlin_t(const Program& P, const RowLinArgs& A, const MlpShape
     return MONO_OK;
 }
 
+template <int MT>
+static int dispatch_rowlin(int c, const Program& P, const RowLinArgs& A, const MlpShape& Z, size_t smem,
+                           cudaStream_t stream) {
+    switch (c) {
+        case 0: return launch_rowlin_t<MT, 10, 2>(P, A, Z, smem, stream);
+        case 2: return launch_rowlin_t<MT, 12, 4>(P, A, Z, smem, stream);
+        default: return launch_rowlin_t<MT, 8, 4>(P, A, Z, smem, stream);  // configs 1 and 3
+    }
+}
+
 int launch_rowlin(Program& P, RowLinArgs& A, cudaStream_t stream) {
     const int M = P.M, G = sm_count();
-    const int MT = M > 8 ? 2 : 1;
+    const int MT = M > 16 ? 4 : (M > 8 ? 2 : 1);
     const int nt = phase_tiles(P.ph[0]), grid = nt < G ? nt : G, per_cta = (nt + grid - 1) / grid;
-    const size_t part = size_t(per_cta) * phase_chunks(P.ph[0]) * MT * 128 * 4;
-    for (int staged = 1; staged >= 0; --staged) {
-        P.ph[0].xsmem = staged;
-        const size_t xb = staged ? size_t(M) * (P.ph[0].K + 16) : 0;
-        for (int c = 0; c < kStreamConfigs; ++c) {
-            const StreamConfig sc = kStreamConfig[c];
-            const StreamPlan plan(stage_bytes<FMT_GPTQ>(), sc.S, part, xb, 0);
-            if (plan.total > kStreamSmemLimit) continue;
-            const MlpShape Z{sc.S, int(part), int(xb)};
-#define MONO_RL(MTV, CWV, PWV) return launch_rowlin_t<MTV, CWV, PWV>(P, A, Z, plan.total, stream)
-            if (MT == 1) {
-                if (c == 0) MONO_RL(1, 10, 2);
-                if (c == 1) MONO_RL(1, 8, 4);
-                MONO_RL(1, 12, 4);
-            } else {
-                if (c == 0) MONO_RL(2, 10, 2);
-                if (c == 1) MONO_RL(2, 8, 4);
-                MONO_RL(2, 12, 4);
+    const size_t tile_bytes = size_t(phase_chunks(P.ph[0])) * MT * 128 * 4;
+    // pass 0: every tile's partials at once; pass 1 (many rows): tiles in batches
+    for (int pass = 0; pass < 2; ++pass)
+        for (int staged = 1; staged >= 0; --staged) {
+            P.ph[0].xsmem = staged;
+            const size_t xb = staged ? size_t(M) * (P.ph[0].K + 16) : 0;
+            for (int c = 0; c < kStreamConfigs; ++c) {
+                const StreamConfig sc = kStreamConfig[c];
+                int tb = per_cta;
+                if (pass == 1) {
+                    const StreamPlan bare(stage_bytes<FMT_GPTQ>(), sc.S, 0, xb, 0);
+                    if (bare.total >= kStreamSmemLimit) continue;
+                    tb = std::min<int>(tb, int((kStreamSmemLimit - bare.total) / 128 * 128 / tile_bytes));
+                    if (tb < 1) continue;
+                }
+                const size_t part = size_t(tb) * tile_bytes;
+                const StreamPlan plan(stage_bytes<FMT_GPTQ>(), sc.S, part, xb, 0);
+                if (plan.total > kStreamSmemLimit) continue;
+                const MlpShape Z{sc.S, int(part), int(xb), tb, 0};
+                if (MT == 1) return dispatch_rowlin<1>(c, P, A, Z, plan.total, stream);
+                if (MT == 2) return dispatch_rowlin<2>(c, P, A, Z, plan.total, stream);
+                return dispatch_rowlin<4>(c, P, A, Z, plan.total, stream);
             }
-#undef MONO_RL
         }
-    }
     return fail(MONO_EINVAL, "rowlin: no shared-memory plan fits (M=%d K=%d)", M, P.ph[0].K);
 }
 

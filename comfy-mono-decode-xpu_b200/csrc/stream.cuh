@@ -35,8 +35,9 @@ constexpr int kConsumerBar = 15;  // named barrier of the consumer warps
 struct StreamConfig {
     int CW, PW, S;
 };
-constexpr int kStreamConfigs = 3;
-constexpr StreamConfig kStreamConfig[kStreamConfigs] = {{10, 2, 20}, {8, 4, 16}, {12, 4, 12}};
+// The last, shallow ring leaves room for 32 staged activation rows (4 batched decode streams).
+constexpr int kStreamConfigs = 4;
+constexpr StreamConfig kStreamConfig[kStreamConfigs] = {{10, 2, 20}, {8, 4, 16}, {12, 4, 12}, {8, 4, 8}};
 constexpr size_t kStreamSmemLimit = 227 * 1024 - 512;  // dynamic bytes, leaving room for the static ones
 
 // Barrier of the CW consumer warps (the producer warp is warp CW, the last one).

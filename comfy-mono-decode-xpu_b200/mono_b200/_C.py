@@ -697,7 +697,7 @@ _lmhead_ws = {}
 
 
 def lmhead_pick(x, w, k=0, logits=False, argmax_out=None, topk_out=None, children=None, dst=None, index_base=0):
-    """bf16 lm_head of M <= 8 rows with the greedy / draft pick fused (include/mono_b200.h mono_lmhead_pick):
+    """bf16 lm_head of M <= 16 rows with the greedy / draft pick fused (include/mono_b200.h mono_lmhead_pick):
     x bf16 [M, K] (rows 16-byte aligned), w bf16 [V, K]. Returns (argmax int64 [M], top-k int64 [M, k] or None,
     logits bf16 [M, V] or None). With children (int32 device tensor of up to 8 slots, -1 ends) and dst (int64 device
     tensor: one row, or [M, >= 8] with unit column stride, one row per x row), also writes each row's draft pick

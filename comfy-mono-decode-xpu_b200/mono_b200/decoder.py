@@ -419,8 +419,9 @@ class Qwen35W4A8:
         toks, x = self.verify(self.drafts)
         if steer is not None:
             steer(toks)
-        self._t("accept_in", -1, toks=toks, drafts=self.drafts, st=self.st, ctl=self.ctl,
-                kv=torch.stack([t for L in self.layers if "kc" in L for t in (L["kc"], L["vc"])]))
+        if self.trace is not None:  # (the stacked caches are a 50 MB copy: only when a test traces the step)
+            self._t("accept_in", -1, toks=toks, drafts=self.drafts, st=self.st, ctl=self.ctl,
+                    kv=torch.stack([t for L in self.layers if "kc" in L for t in (L["kc"], L["vc"])]))
         _C.mtp_accept(self.st, toks, self.drafts.view(1, -1), None, self.children, self.tree["rows"], c.depth, x,
                       self.next_tok, self.hidden, self.ctl, self.kv_ptrs, c.kv_heads, self.cap, c.head_dim,
                       self.result)

@@ -1,6 +1,6 @@
 """Independent decode streams batched on one GPU: every weight byte is read once per step for all of them.
 
-B streams (B x 8 verify rows <= 16: B <= 2 with the 8-row tree) share one model's weights and run one step
+B streams (B x 8 verify rows <= 32: B <= 4 with the 8-row tree) share one model's weights and run one step
 together. Their state is stacked:
 
   attention KV caches [1, B * Hk, cap, 256]      stream b: kv heads [b Hk, (b + 1) Hk)
@@ -15,7 +15,8 @@ and every row-wise kernel takes the B x 8 verify rows (B draft rows) as one batc
   tree attention                    mono_tree_attention_streams (stream b's q heads over its kv heads, its length)
   GDN conv + delta                  mono_gdn_step_deferred_streams (grid y = stream)
   draft head projections            mono_gemv_bf16 at M = B
-  lm_head picks                     mono_lmhead_pick at M = 8 B (verify) and M = B (each draft, dst row per stream)
+  lm_head picks                     mono_lmhead_pick at M = B (each draft, dst row per stream) and for the verify
+                                    in launches of up to 16 rows (one lm_head read per 2 streams)
   MTP prep / accept                 one launch per stream (a few microseconds each)
 
 Each stream's arithmetic is exactly its one-stream step's (row-wise kernels; attention chunks a stream's context as
@@ -29,7 +30,9 @@ import torch
 from . import _C
 from .decoder import Qwen35W4A8, _bf
 
-MAX_ROWS = 16  # verify rows of one batched step: the W4A8 engine's and the lm_head pick's row limit
+MAX_ROWS = 32  # verify rows of one batched step: the fused MLP's and the row linear's row limit
+PICK_ROWS = 16  # rows of one lm_head pick launch
+AB_ROWS = 16    # rows of one GDN a | b projection launch
 
 
 def _state_of(m):
@@ -163,7 +166,9 @@ class Qwen35W4A8Streams(Qwen35W4A8):
         xn = torch.empty_like(x)
         pre = _C.rowlin_gptq(x, _C.ROWLIN_NORM, [(L["qkv"], Ck), (L["z"], HV * D)], norm_w=L["ln1"], eps=c.eps,
                              xn_out=xn)
-        ab = _C.gdn_ab(xn, L["wab"])
+        ab = torch.empty(x.shape[0], 2 * HV, dtype=torch.bfloat16, device=x.device)
+        for r0 in range(0, x.shape[0], AB_ROWS):  # the a | b projection stages its rows: 16 a launch
+            _C.gdn_ab(xn[r0:r0 + AB_ROWS], L["wab"], out=ab[r0:r0 + AB_ROWS])
         prev, save = L["saved"][self.parity], L["saved"][1 - self.parity]
         core = _C.gdn_step_deferred(pre[:, :Ck], pre[:, Ck:], ab[:, :HV], ab[:, HV:], L["conv_w"], L["conv_state"],
                                     L["dt_bias"], L["g_decay"], L["state"], L["gnorm"], c.eps, D ** -0.5,
@@ -186,7 +191,9 @@ class Qwen35W4A8Streams(Qwen35W4A8):
         for i, L in enumerate(self.layers):
             x = self._attention(L, x, freqs, i) if c.is_attn(i) else self._gdn(L, x, i)
         xf = _C.rmsnorm_add(x, self.final_norm, c.eps)
-        self._pick(xf, 0, argmax_out=self.toks.view(-1))
+        toks = self.toks.view(-1)
+        for r0 in range(0, xf.shape[0], PICK_ROWS):
+            self._pick(xf[r0:r0 + PICK_ROWS], 0, argmax_out=toks[r0:r0 + PICK_ROWS])
         self._t("verify", -1, tokens=tokens, x=x, xf=xf, toks=self.toks)
         return self.toks, x
 
@@ -245,9 +252,10 @@ class Qwen35W4A8Streams(Qwen35W4A8):
         c, B = self.cfg, self.streams
         n_attn = sum(1 for i in range(c.layers) if c.is_attn(i))
         n_gdn = c.layers - n_attn
-        body = c.layers * 3 + n_gdn * 3 + n_attn * 2
+        body = c.layers * 3 + n_gdn * (2 + -(-B * self.tree["rows"] // AB_ROWS)) + n_attn * 2
         draft = c.depth * (B + 2 + 1 + 1 + 2 + 3 + 1 + (5 if self.draft_gemv else 0))
-        return body + draft + B + 1 + 1 + B  # prep_verify per stream, final norm, lm_head pick, accept per stream
+        picks = -(-B * self.tree["rows"] // PICK_ROWS)
+        return body + draft + B + 1 + picks + B  # prep_verify per stream, final norm, lm_head picks, accepts
 
     def step_bytes(self) -> int:
         """Algorithmic HBM bytes of one batched step: the weights once, every stream's GDN states and KV prefix."""
@@ -257,7 +265,8 @@ class Qwen35W4A8Streams(Qwen35W4A8):
         small = sum(L[k].numel() * L[k].element_size() for L in self.layers for k in ("wab", "conv_w") if k in L)
         state = sum(L["state"].numel() * 4 * 2 for L in self.layers if "state" in L)  # all streams' states
         lm = self.lm_head.numel() * 2
+        picks = -(-B * self.tree["rows"] // PICK_ROWS)  # verify lm_head reads
         mtp = sum(t.numel() * t.element_size() for k, t in self.mtp.items() if k not in ("kc", "vc"))
         kv = int(self.st[:, 0].sum().item()) * c.kv_heads * c.head_dim * 2 * 2 * sum(1 for L in self.layers
                                                                                       if "kc" in L)
-        return body + small + state + lm * (1 + c.depth) + mtp * c.depth + kv
+        return body + small + state + lm * (picks + c.depth) + mtp * c.depth + kv

@@ -1,4 +1,4 @@
-"""2-way tensor parallelism of one decode stream (SURVEY 8(e) P2; the reference has no distributed path).
+"""2-way tensor parallelism of one decode stream (the reference has no distributed path).
 
 Sharding of the Qwen3.5 decode step over `world` ranks (one process per GPU, torch.distributed over NCCL):
 

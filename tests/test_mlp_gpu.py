@@ -27,7 +27,7 @@ def test_mlp_gptq_bit_exact(cuda, H, I):
     lut_np = bf16_bits(lut)
     g = torch.Generator().manual_seed(H + I)
     w = (1 + torch.randn(H, generator=g) * 0.02).to(torch.bfloat16)
-    for M in (1, 3, 8, 9, 16):
+    for M in (1, 3, 8, 9, 16, 24, 32):  # (17..32: four 8-row tiles, tiles in batches)
         x = torch.randn(M, H, generator=g).to(torch.bfloat16)
         ref = ol.mlp_gptq(bf16_bits(x), bf16_bits(w), 1e-6, *mats, lut_np)
         for _ in range(2):  # the second call reuses the workspace (barrier words reset by the kernel)

@@ -22,7 +22,7 @@ def _mats(shapes, K, seed, cuda):
     return host, dev
 
 
-@pytest.mark.parametrize("M", [1, 8, 9, 16])
+@pytest.mark.parametrize("M", [1, 8, 9, 16, 25, 32])
 def test_rowlin_norm_qkv_bit_exact(cuda, M):
     from mono_b200 import _C
     K = 4096
@@ -39,7 +39,7 @@ def test_rowlin_norm_qkv_bit_exact(cuda, M):
     assert np.array_equal(bf16_bits(xn_out), xn)
 
 
-@pytest.mark.parametrize("M", [1, 8])
+@pytest.mark.parametrize("M", [1, 8, 32])
 def test_rowlin_gate_oproj_residual_bit_exact(cuda, M):
     from mono_b200 import _C
     K = 4096

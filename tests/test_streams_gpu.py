@@ -36,15 +36,17 @@ def _perturb(m, seed, shift):
     m.st[1] -= shift
 
 
-@pytest.mark.parametrize("steered", [False, True])
-def test_two_streams_equal_two_models(cuda, steered):
+@pytest.mark.parametrize("B,steered", [(2, False), (2, True), (4, True)])
+def test_streams_equal_separate_models(cuda, B, steered):
+    """B = 4: 32 verify rows (the W4A8 kernels' four-tile path, tiles in batches; two lm_head pick launches)."""
     from mono_b200.decoder import Qwen35W4A8
     from mono_b200.streams import Qwen35W4A8Streams
     cfg = _cfg()
-    models = [Qwen35W4A8(cfg, cuda, prompt_len=96, gen_tokens=64) for _ in range(2)]
-    _perturb(models[1], 11, 29)
+    models = [Qwen35W4A8(cfg, cuda, prompt_len=96, gen_tokens=64) for _ in range(B)]
+    for b in range(1, B):
+        _perturb(models[b], 10 + b, 13 * b + 3)
     batch = Qwen35W4A8Streams.from_models(models)
-    assert batch.streams == 2
+    assert batch.streams == B
     for step in range(3):
         force = steered and step != 1
         rb = batch.step(steer=(lambda t: t[:, 0].copy_(batch.drafts[:, 1])) if force else None).clone()
@@ -52,7 +54,7 @@ def test_two_streams_equal_two_models(cuda, steered):
         for m in models:
             rs.append(m.step(steer=(lambda t, m=m: t[0, 0].copy_(m.drafts[1])) if force else None).clone())
         torch.cuda.synchronize()
-        for b in range(2):
+        for b in range(B):
             assert torch.equal(rb[b], rs[b]), (step, b, rb[b, :10].tolist(), rs[b][:10].tolist())
         if force:
             assert all(int(r[0]) >= 2 for r in rs)
