@@ -871,22 +871,25 @@ def run_decode(args):
         p4096 = {"tok_s": round(toks2 / (ms2 * 1e-3), 2), "ms_per_step": round(ms2 / steps2, 4), "steps": steps2,
                  "algorithmic_bytes_per_step": m2.step_bytes()}
         model = m2
-    # two streams batched in one step on this GPU (mono_b200.streams: 16 verify rows, one weight read per step)
-    batched = None
+    # 2 and 4 streams batched in one step on this GPU (mono_b200.streams: 16 / 32 verify rows, one weight read per
+    # step for all of them)
+    batched = {}
     if B == 1 and not args.no_batched:
         from mono_b200.streams import Qwen35W4A8Streams
-        del model
-        torch.cuda.empty_cache()
-        m3 = Qwen35W4A8Streams(cfg, dev, prompt_len=prompt, streams=2, gen_tokens=max(512, args.steps * 8 + 64),
-                               seed=0x5EED + 4 + rank, draft_gemv=not args.cublas_draft)
-        steps3 = max(10, args.steps // 2)
-        ms3, toks3, g3 = _decode_measure(m3, stream, steps3, args.warmup, world, dev)
-        del g3
-        batched = {"streams": 2, "tok_s": round(toks3 / (ms3 * 1e-3), 2), "ms_per_step": round(ms3 / steps3, 4),
-                   "steps": steps3, "tokens_per_step": round(toks3 / (steps3 * world), 3),
-                   "what": "aggregate committed tok/s of 2 independent streams on this GPU, stepped together "
-                           "(bench.py --streams 2 for the full line)"}
-        model = m3
+        for nb in (2, 4):
+            del model
+            torch.cuda.empty_cache()
+            m3 = Qwen35W4A8Streams(cfg, dev, prompt_len=prompt, streams=nb, gen_tokens=max(512, args.steps * 8 + 64),
+                                   seed=0x5EED + 4 + rank, draft_gemv=not args.cublas_draft)
+            steps3 = max(10, args.steps // 2)
+            ms3, toks3, g3 = _decode_measure(m3, stream, steps3, args.warmup, world, dev)
+            del g3
+            batched[nb] = {"streams": nb, "tok_s": round(toks3 / (ms3 * 1e-3), 2),
+                           "ms_per_step": round(ms3 / steps3, 4), "steps": steps3,
+                           "tokens_per_step": round(toks3 / (steps3 * world), 3),
+                           "what": f"aggregate committed tok/s of {nb} independent streams on this GPU, stepped "
+                                   f"together (bench.py --streams {nb} for the full line)"}
+            model = m3
     cpu = cpu_decode_baseline(args) if (rank == 0 and world == 1 and not args.no_cpu) else None
     if rank == 0:
         line = {
@@ -909,7 +912,7 @@ def run_decode(args):
                        "draft_projections": "cuBLAS (F.linear)" if args.cublas_draft else "mono_gemv_bf16",
                        "lm_head": "mono_lmhead_pick (bf16 GEMV with the argmax / top-2 pick fused), verify and drafts",
                        "prompt_4096": p4096,
-                       "streams_2": batched,
+                       "streams_2": batched.get(2), "streams_4": batched.get(4),
                        "parallelism": f"independent streams x{world * B} ({B} per GPU)"},
             "roofline": {"bound": "hbm", "achieved": round(mlp_b / (mlp_us * 1e-6) / 1e9, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(mlp_b / (mlp_us * 1e-6) / 1e9 / hbm, 4), "peak_source": src,
@@ -1069,9 +1072,9 @@ def main():
     ap.add_argument("--workload", default="decode", choices=["gemv", "mlp", "decode", "topk_rows", "lmhead"])
     ap.add_argument("--prompt", type=int, default=1024, help="decode: committed prompt length (KV prefix)")
     ap.add_argument("--rows", type=int, default=8, help="activation rows (tree-verify rows)")
-    ap.add_argument("--no-batched", action="store_true", help="decode: skip the 2-stream batched measurement")
+    ap.add_argument("--no-batched", action="store_true", help="decode: skip the 2- and 4-stream batched measurements")
     ap.add_argument("--streams", type=int, default=1,
-                    help="decode: independent streams per GPU batched in one step (2: 16 verify rows)")
+                    help="decode: independent streams per GPU batched in one step (up to 4: 32 verify rows)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-second-prompt", action="store_true", help="decode: skip the prompt-4096 measurement")
     ap.add_argument("--trace", action="store_true", help="mlp: add the fused kernel's phase trace to config")
