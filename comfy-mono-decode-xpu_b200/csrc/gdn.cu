@@ -220,12 +220,20 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
     }
 }
 
-// a | b projection: the CTA copies the M rows into shared memory; its 8 warps take the 4 quarters of 2 columns.
-// Launched with a programmatic dependency: the weights load before griddepcontrol.wait, the rows after it.
+// a | b projection: CTA (x, y) copies rows [16 y, 16 y + 16) of the M rows into shared memory; its 8 warps take
+// the 4 quarters of columns 2x, 2x + 1. Launched with a programmatic dependency: the weights load before
+// griddepcontrol.wait, the rows after it.
+constexpr int kAbRows = 16;
 __global__ void __launch_bounds__(256) gdn_ab_kernel(const uint16_t* x, int64_t x_stride, const uint16_t* w, int K,
                                                       int M, int N, uint16_t* out, int64_t out_stride) {
     extern __shared__ __align__(16) uint16_t xs[];
-    __shared__ float qs[2][4][16];
+    {  // this CTA's block of rows
+        const int r0 = int(blockIdx.y) * kAbRows;
+        x += size_t(r0) * x_stride;
+        out += size_t(r0) * out_stride;
+        M = M - r0 < kAbRows ? M - r0 : kAbRows;
+    }
+    __shared__ float qs[2][4][kAbRows];
     const int per = K >> 3, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int cl = warp >> 2, q = warp & 3, n = blockIdx.x * 2 + cl;
     uint4 wv[4];
@@ -258,13 +266,13 @@ __global__ void __launch_bounds__(256) gdn_ab_kernel(const uint16_t* x, int64_t 
     __syncthreads();
     if (threadIdx.x < 2 * M) {
         const int c = threadIdx.x / M, m = threadIdx.x % M, nn = blockIdx.x * 2 + c;
-        if (nn < N) out[size_t(m) * out_stride + nn] = gdn_ab_combine(&qs[c][0][0], 16, m);
+        if (nn < N) out[size_t(m) * out_stride + nn] = gdn_ab_combine(&qs[c][0][0], kAbRows, m);
     }
 }
 
 int launch_gdn_ab(const uint16_t* x, int64_t x_stride, const uint16_t* w, int K, int M, int N, uint16_t* out,
                   int64_t out_stride, cudaStream_t stream) {
-    const size_t smem = size_t(M) * K * 2;
+    const size_t smem = size_t(M < kAbRows ? M : kAbRows) * K * 2;
     static std::mutex mu;
     static size_t opt_in = 48 * 1024;
     {
@@ -278,7 +286,7 @@ int launch_gdn_ab(const uint16_t* x, int64_t x_stride, const uint16_t* w, int K,
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((N + 1) / 2);
+    cfg.gridDim = dim3((N + 1) / 2, (M + kAbRows - 1) / kAbRows);
     cfg.blockDim = dim3(256);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;

@@ -238,8 +238,8 @@ int mono_program_launch(const void* ops, const void* ops_device, int nops, int64
 int mono_gdn_ab(const void* x, int64_t x_stride, const void* w, int64_t K, int64_t M, int64_t N, void* out,
                 mono_stream_t stream) {
     MONO_CHECK(x && w && out, "null operand");
-    MONO_CHECK(M >= 1 && M <= 16 && N >= 1 && K % 1024 == 0 && K > 0 && K <= 4096 && x_stride >= K && x_stride % 8 == 0,
-               "1 <= M <= 16, K a multiple of 1024 up to 4096");
+    MONO_CHECK(M >= 1 && M <= 32 && N >= 1 && K % 1024 == 0 && K > 0 && K <= 4096 && x_stride >= K && x_stride % 8 == 0,
+               "1 <= M <= 32, K a multiple of 1024 up to 4096");
     MONO_CHECK(aligned(x, 16) && aligned(w, 16), "16-byte aligned rows");
     return launch_gdn_ab(static_cast<const uint16_t*>(x), x_stride, static_cast<const uint16_t*>(w), int(K), int(M), int(N),
                          static_cast<uint16_t*>(out), N, reinterpret_cast<cudaStream_t>(stream));

@@ -17,6 +17,7 @@ and every row-wise kernel takes the B x 8 verify rows (B draft rows) as one batc
   draft head projections            mono_gemv_bf16 at M = B
   lm_head picks                     mono_lmhead_pick at M = B (each draft, dst row per stream) and for the verify
                                     in launches of up to 16 rows (one lm_head read per 2 streams)
+  GDN a | b projection              mono_gdn_ab (blocks of 16 rows across the grid)
   MTP prep / accept                 one launch per stream (a few microseconds each)
 
 Each stream's arithmetic is exactly its one-stream step's (row-wise kernels; attention chunks a stream's context as
@@ -32,7 +33,6 @@ from .decoder import Qwen35W4A8, _bf
 
 MAX_ROWS = 32  # verify rows of one batched step: the fused MLP's and the row linear's row limit
 PICK_ROWS = 16  # rows of one lm_head pick launch
-AB_ROWS = 16    # rows of one GDN a | b projection launch
 
 
 def _state_of(m):
@@ -166,9 +166,7 @@ class Qwen35W4A8Streams(Qwen35W4A8):
         xn = torch.empty_like(x)
         pre = _C.rowlin_gptq(x, _C.ROWLIN_NORM, [(L["qkv"], Ck), (L["z"], HV * D)], norm_w=L["ln1"], eps=c.eps,
                              xn_out=xn)
-        ab = torch.empty(x.shape[0], 2 * HV, dtype=torch.bfloat16, device=x.device)
-        for r0 in range(0, x.shape[0], AB_ROWS):  # the a | b projection stages its rows: 16 a launch
-            _C.gdn_ab(xn[r0:r0 + AB_ROWS], L["wab"], out=ab[r0:r0 + AB_ROWS])
+        ab = _C.gdn_ab(xn, L["wab"])
         prev, save = L["saved"][self.parity], L["saved"][1 - self.parity]
         core = _C.gdn_step_deferred(pre[:, :Ck], pre[:, Ck:], ab[:, :HV], ab[:, HV:], L["conv_w"], L["conv_state"],
                                     L["dt_bias"], L["g_decay"], L["state"], L["gnorm"], c.eps, D ** -0.5,
@@ -252,7 +250,7 @@ class Qwen35W4A8Streams(Qwen35W4A8):
         c, B = self.cfg, self.streams
         n_attn = sum(1 for i in range(c.layers) if c.is_attn(i))
         n_gdn = c.layers - n_attn
-        body = c.layers * 3 + n_gdn * (2 + -(-B * self.tree["rows"] // AB_ROWS)) + n_attn * 2
+        body = c.layers * 3 + n_gdn * 3 + n_attn * 2
         draft = c.depth * (B + 2 + 1 + 1 + 2 + 3 + 1 + (5 if self.draft_gemv else 0))
         picks = -(-B * self.tree["rows"] // PICK_ROWS)
         return body + draft + B + 1 + picks + B  # prep_verify per stream, final norm, lm_head picks, accepts

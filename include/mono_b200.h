@@ -466,7 +466,7 @@ MONO_API int mono_program_launch(const void* ops, const void* ops_device, int no
  * 4 quarters; for quarter q, lane l of 32 sums its 8-element pieces l + 32 j (j ascending over the quarter's
  * 256-wide slices, elements in order) from +0, then the xor butterfly (16, 8, 4, 2, 1) gives Q_q; out =
  * bf16(((Q_0 + Q_1) + Q_2) + Q_3). x bf16 [M][K] (row stride x_stride), w bf16 [N][K], out bf16 [M][N];
- * K % 1024 == 0, K <= 4096, M <= 16. */
+ * K % 1024 == 0, K <= 4096, M <= 32. */
 MONO_API int mono_gdn_ab(const void* x, int64_t x_stride, const void* w, int64_t K, int64_t M, int64_t N, void* out,
                          mono_stream_t stream);
 
