@@ -14,7 +14,8 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("M,V,k,K", [(1, 30001, 2, 4096), (5, 16384, 0, 4096), (8, 12289, 8, 4096),
-                                     (3, 4099, 1, 4096), (8, 32768, 2, 2048), (2, 151936, 8, 4096)])
+                                     (3, 4099, 1, 4096), (8, 32768, 2, 2048), (2, 151936, 8, 4096),
+                                     (16, 20011, 2, 4096), (12, 8192, 8, 4096), (16, 4104, 0, 2048)])
 def test_lmhead_pick(cuda, M, V, k, K):
     from mono_b200 import _C
     g = torch.Generator().manual_seed(M * 7 + V)
