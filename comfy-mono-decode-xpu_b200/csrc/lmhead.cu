@@ -123,11 +123,27 @@ __global__ void __launch_bounds__(kLhWarps * 32, 1) lmhead_pick_kernel(const LmH
     for (int q = 0; q < S && q < Q; ++q) issue(q);
     pdl_wait();
     {
-        const int per_row = A.K >> 3;
-        for (int i = threadIdx.x; i < A.M * per_row; i += NT) {
-            const int m = i / per_row, c = i - m * per_row;
-            *reinterpret_cast<uint4*>(xs + size_t(m) * pitch + 8 * c) =
-                __ldg(reinterpret_cast<const uint4*>(A.x + m * A.x_stride) + c);
+        // the x rows in batches of 16 pieces per thread, every load of a batch issued before its stores (one L2
+        // round trip per batch, not one per piece)
+        const int per_row = A.K >> 3, total = A.M * per_row;
+        for (int base = threadIdx.x; base < total; base += 16 * NT) {
+            uint4 v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int i = base + j * NT;
+                if (i < total) {
+                    const int m = i / per_row, c = i - m * per_row;
+                    v[j] = __ldg(reinterpret_cast<const uint4*>(A.x + m * A.x_stride) + c);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int i = base + j * NT;
+                if (i < total) {
+                    const int m = i / per_row, c = i - m * per_row;
+                    *reinterpret_cast<uint4*>(xs + size_t(m) * pitch + 8 * c) = v[j];
+                }
+            }
         }
         if (threadIdx.x == 0) *reinterpret_cast<uint4*>(const_cast<uint16_t*>(zero16)) = make_uint4(0, 0, 0, 0);
     }
