@@ -97,6 +97,20 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
     for (int r = 0; r < kRPG; ++r) st[r] = S[size_t(r) * kDH];
     pdl_wait();
     pdl_launch_dependents();
+    // the gated norm's z and weight for this thread's output elements e = tid + 128 j (rows t = e / 32), loaded
+    // now: their latency hides behind the recurrence
+    constexpr int kZPer = kGdnMaxRows * kDcCols / (kRG * kDcCols);
+    float zv[kZPer], gw[kZPer];
+#pragma unroll
+    for (int j = 0; j < kZPer; ++j) {
+        const int e = tid + j * kRG * kDcCols;
+        zv[j] = gw[j] = 0.f;
+        if (e < M * kDcCols) {
+            const int t = e / kDcCols, d = cr * kDcCols + e % kDcCols;
+            zv[j] = bf16_bits_to_f32(__ldcg(A.z + size_t(t) * A.z_stride + h * kDH + d));
+            gw[j] = bf16_bits_to_f32(A.gnorm_w[d]);
+        }
+    }
     static_assert(kRG * kDcCols == kDH, "one thread per q / k element");
     float qr[kGdnMaxAll], kr0[kGdnMaxAll], vr[kGdnMaxAll / kRG];
 #pragma unroll
@@ -131,14 +145,14 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
         for (int j = 0; j < 4; ++j) sq = fmaf(src[lane + 32 * j], src[lane + 32 * j], sq);
 #pragma unroll
         for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-        if (lane == 0) sums[pr] = sq;
+        if (lane == 0) sums[pr] = gdn_l2_inv(sq);  // the row's inverse norm, once (not once per thread)
     }
     __syncthreads();
 #pragma unroll
     for (int t = 0; t < kGdnMaxAll; ++t)
         if (t < R) {
-            qn[t][tid] = (qr[t] * A.qscale) * gdn_l2_inv(sums[2 * t]);
-            kn[t][tid] = kr0[t] * gdn_l2_inv(sums[2 * t + 1]);
+            qn[t][tid] = (qr[t] * A.qscale) * sums[2 * t];
+            kn[t][tid] = kr0[t] * sums[2 * t + 1];
         }
     for (int e = tid; e < M * kDcCols; e += blockDim.x) raw[e / kDcCols][e % kDcCols] = 0.f;  // rows no entry names
     __syncthreads();
@@ -209,14 +223,15 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
         }
 #pragma unroll
         for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0) nsum[t] = s;
+        if (lane == 0) nsum[t] = gdn_norm_inv(s, A.gnorm_eps);  // the row's norm factor, once
     }
     cluster.sync();  // no CTA leaves while another reads its raw rows; nsum is visible to the CTA
-    for (int e = tid; e < M * kDcCols; e += blockDim.x) {
-        const int t = e / kDcCols, c = e % kDcCols, d = cr * kDcCols + c;
-        const float z = bf16_bits_to_f32(A.z[size_t(t) * A.z_stride + h * kDH + d]);
-        A.core[size_t(t) * A.HV * kDH + h * kDH + d] =
-            gdn_core(raw[t][c], bf16_bits_to_f32(A.gnorm_w[d]), gdn_norm_inv(nsum[t], A.gnorm_eps), z);
+    for (int j = 0; j < kZPer; ++j) {
+        const int e = tid + j * kRG * kDcCols;
+        if (e < M * kDcCols) {
+            const int t = e / kDcCols, c = e % kDcCols, d = cr * kDcCols + c;
+            A.core[size_t(t) * A.HV * kDH + h * kDH + d] = gdn_core(raw[t][c], gw[j], nsum[t], zv[j]);
+        }
     }
 }
 
