@@ -73,7 +73,9 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
     const GdnArgs A = gdn_stream(A0, blockIdx.y);
     __shared__ __align__(16) float qn[kGdnMaxAll][kDH];
     __shared__ __align__(16) float kn[kGdnMaxAll][kDH];
-    __shared__ float part[2][kRG][kDcCols];
+    __shared__ float part[2][kRG][kDcCols];           // the entries' S^T k partials, by entry parity
+    __shared__ float opart[kGdnMaxAll][kRG][kDcCols];  // every entry's output partials (summed after the entries)
+    __shared__ int eout[kGdnMaxAll];
     __shared__ float raw[kGdnMaxRows][kDcCols];
     __shared__ float sums[2 * kGdnMaxAll];
     __shared__ float nsum[kGdnMaxRows];
@@ -184,9 +186,10 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
 #pragma unroll
             for (int r = 0; r < kRPG; ++r) mem = fmaf(st[r] * decay, kr[r], mem);
         }
-        part[0][rg][lane] = mem;
+        float (&pe)[kRG][kDcCols] = part[e & 1];  // the other buffer is still being read by the previous entry
+        pe[rg][lane] = mem;
         __syncthreads();
-        const float kv = part[0][0][lane] + part[0][1][lane] + part[0][2][lane] + part[0][3][lane];
+        const float kv = pe[0][lane] + pe[1][lane] + pe[2][lane] + pe[3][lane];
         const float delta = (v - kv) * beta;
         float o = 0.f;
         if (en.commit) {
@@ -199,10 +202,8 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
 #pragma unroll
             for (int r = 0; r < kRPG; ++r) o = fmaf(fmaf(kr[r], delta, st[r] * decay), qr[r], o);
         }
-        part[1][rg][lane] = o;
-        __syncthreads();
-        if (rg == 0 && en.out >= 0)
-            raw[en.out][lane] = bf16_round(part[1][0][lane] + part[1][1][lane] + part[1][2][lane] + part[1][3][lane]);
+        opart[e][rg][lane] = o;
+        if (tid == 0) eout[e] = en.out;
         if (A.ctl != nullptr && e == n - 1)  // the committed state after the replay
 #pragma unroll
             for (int r = 0; r < kRPG; ++r) S[size_t(r) * kDH] = st[r];
@@ -210,6 +211,10 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
     if (A.ctl == nullptr)
 #pragma unroll
         for (int r = 0; r < kRPG; ++r) S[size_t(r) * kDH] = st[r];
+    __syncthreads();  // every entry's output partials are written
+    if (rg == 0)  // the entries' outputs in entry order (a later entry naming the same row wins, as it did in turn)
+        for (int e = 0; e < E; ++e)
+            if (eout[e] >= 0) raw[eout[e]][lane] = bf16_round(opart[e][0][lane] + opart[e][1][lane] + opart[e][2][lane] + opart[e][3][lane]);
     cluster.sync();  // every CTA's raw rows are written (a cluster barrier orders its shared-memory writes)
     // gated RMSNorm of every output row: row t's squares in gdn_sumsq128's order (lane l: columns l, l + 32, l + 64,
     // l + 96 in order, i.e. CTA 0 .. 3's column l, then the xor butterfly)
