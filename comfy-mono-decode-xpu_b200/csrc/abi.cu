@@ -345,20 +345,24 @@ size_t mono_tree_attention_streams_workspace(int64_t Hk, int64_t streams, int64_
 int mono_tree_attention(const void* q, const void* key_cache, const void* value_cache, const int32_t* seqlen,
                         const void* xk, const void* xv, const int32_t* mask, int64_t H, int64_t Hk, int64_t S,
                         int64_t cap, void* out, void* workspace, size_t workspace_bytes, mono_stream_t stream) {
-    return mono_tree_attention_streams(q, key_cache, value_cache, seqlen, xk, xv, mask, H, Hk, S, 1, cap, out,
-                                       workspace, workspace_bytes, stream);
+    return mono_tree_attention_streams(q, key_cache, value_cache, seqlen, xk, xv, mask, H, Hk, S, 1, cap, Hk * S * 256,
+                                       S * 256, 256, out, workspace, workspace_bytes, stream);
 }
 
 int mono_tree_attention_streams(const void* q, const void* key_cache, const void* value_cache, const int32_t* seqlen,
                                 const void* xk, const void* xv, const int32_t* mask, int64_t H, int64_t Hk, int64_t S,
-                                int64_t streams, int64_t cap, void* out, void* workspace, size_t workspace_bytes,
+                                int64_t streams, int64_t cap, int64_t xv_stream_stride, int64_t xv_head_stride,
+                                int64_t xv_row_stride, void* out, void* workspace, size_t workspace_bytes,
                                 mono_stream_t stream) {
     MONO_CHECK(q && key_cache && value_cache && seqlen && out && workspace, "null operand");
     MONO_CHECK(streams >= 1 && streams <= 8, "1 <= streams <= 8");
+    MONO_CHECK(xv_stream_stride >= 0 && xv_head_stride >= 0 && xv_row_stride >= 0 && xv_stream_stride % 8 == 0 &&
+                   xv_head_stride % 8 == 0 && xv_row_stride % 8 == 0,
+               "tree value strides: non-negative multiples of 8 elements");
     MONO_CHECK(S >= 1 && S <= 8 && Hk >= 1 && H % Hk == 0 && (H / Hk) * S <= 32,
                "1..8 rows, H a multiple of Hk, (H / Hk) * S <= 32 query rows per kv head");
     MONO_CHECK(mask != nullptr || S == 1, "a tree mask for S > 1 rows (S = 1 without a mask: the draft row)");
-    MONO_CHECK(mask == nullptr || (xk && xv), "tree rows need xk / xv");
+    MONO_CHECK(mask == nullptr || (xk && xv && aligned(xk, 16) && aligned(xv, 16)), "tree rows need 16-byte aligned xk / xv");
     MONO_CHECK(cap >= 1 && cap <= (int64_t(1) << 30), "cache capacity");
     MONO_CHECK(workspace_bytes >= mono_tree_attention_streams_workspace(Hk, streams, cap),
                "workspace too small (mono_tree_attention_streams_workspace)");
@@ -372,6 +376,9 @@ int mono_tree_attention_streams(const void* q, const void* key_cache, const void
     A.xk = static_cast<const uint16_t*>(xk);
     A.xv = static_cast<const uint16_t*>(xv);
     A.mask = mask;
+    A.xv_bs = xv_stream_stride;
+    A.xv_hs = xv_head_stride;
+    A.xv_rs = xv_row_stride;
     A.out = static_cast<uint16_t*>(out);
     A.H = int(H * streams);
     A.Hk = int(Hk * streams);

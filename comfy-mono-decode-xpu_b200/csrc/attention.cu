@@ -188,6 +188,12 @@ __device__ __forceinline__ void unpack8(const uint4 v, float (&f)[8]) {
     }
 }
 
+// The tree value row t of kv head kh (of all streams' heads), as strided by the caller.
+__device__ __forceinline__ const uint16_t* attn_xv_row(const AttnArgs& A, int kh, int t) {
+    const int hs = A.Hk / A.streams;
+    return A.xv + size_t(kh / hs) * A.xv_bs + size_t(kh % hs) * A.xv_hs + size_t(t) * A.xv_rs;
+}
+
 // One warp finishes row r of kv head kh (q head kh * groups + r / S, tree row r % S); lane l holds dims
 // [8 l, 8 l + 8) of the merged prefix (acc unnormalized, running max M, sum). The admitted tree rows follow in
 // row order (score = q . xk / 16 over the head dimension: lane sums in dim order, xor butterfly 16 .. 1), then
@@ -204,7 +210,7 @@ __device__ __forceinline__ void attn_finish_row(const AttnArgs& A, int kh, int r
         for (int tr = 0; tr < 8; ++tr)
             if (tr < A.S) {  // every tree row, not only the admitted ones: no wait on the mask word
                 kx[tr] = reinterpret_cast<const uint4*>(A.xk + (size_t(kh) * A.S + tr) * kHD)[lane];
-                vx[tr] = reinterpret_cast<const uint4*>(A.xv + (size_t(kh) * A.S + tr) * kHD)[lane];
+                vx[tr] = reinterpret_cast<const uint4*>(attn_xv_row(A, kh, tr))[lane];
             }
 #pragma unroll
         for (int tr = 0; tr < 8; ++tr) {
@@ -283,8 +289,9 @@ __global__ void __cluster_dims__(kAttCluster, 1, 1) __launch_bounds__(kAttThread
             const int lines = 4 * (1 + 2 * A.S);
             for (int i = lane; i < lines; i += 32) {
                 const int row = i >> 2, part = (i & 3) * 64;
-                const uint16_t* base = row == 0 ? A.q + (size_t(h) * A.S + s) * kHD
-                                     : (row <= A.S ? A.xk : A.xv) + (size_t(kh) * A.S + (row - 1) % A.S) * kHD;
+                const uint16_t* base = row == 0      ? A.q + (size_t(h) * A.S + s) * kHD
+                                       : row <= A.S ? A.xk + (size_t(kh) * A.S + (row - 1)) * kHD
+                                                    : attn_xv_row(A, kh, row - 1 - A.S);
                 prefetch_l2(base + part);
             }
         }

@@ -100,7 +100,8 @@ struct AttnArgs {
     const uint16_t* vc;
     const int32_t* seqlen;
     const uint16_t* xk;   // [Hk][S][256]
-    const uint16_t* xv;
+    const uint16_t* xv;   // element (stream b, kv head k of the stream, row t) at b xv_bs + k xv_hs + t xv_rs
+    int64_t xv_bs, xv_hs, xv_rs;
     const int32_t* mask;  // [S] or null
     uint16_t* out;        // [streams][S][H / streams * 256]
     float* part;          // workspace: [Hk][chunks / 8][32][256] merged rows of each cluster

@@ -309,9 +309,11 @@ def attn_dpas(q, key, value, seqlen, xk, xv, mask, chunks_hint=0, out=None, stre
     key / value bf16 [1, Hk, cap, 256]; seqlen int32 [1] on the device (L, no host sync); xk / xv bf16
     [1, Hk, S, 256]; mask int32 [S] (an empty tensor: the single draft row over the prefix only).
     Returns bf16 [1, S, H * 256] (into `out` when given). chunks_hint is accepted for the reference's signature and
-    unused. streams > 1 (batched decode streams, include/mono_b200.h mono_tree_attention_streams): q, the caches,
-    xk and xv hold `streams` groups of heads (stream b: q heads [b H, (b + 1) H), kv heads [b Hk, (b + 1) Hk)),
-    seqlen int32 [streams], one mask for all; returns bf16 [1, streams * S, H * 256] (stream b's rows [b S, ...))."""
+    unused. xv may be any strided view with unit last stride (e.g. the projection's value columns transposed): the
+    kernel reads it in place. streams > 1 (batched decode streams, include/mono_b200.h mono_tree_attention_streams):
+    q, the caches and xk hold `streams` groups of heads (stream b: q heads [b H, (b + 1) H), kv heads
+    [b Hk, (b + 1) Hk)), xv is [streams, Hk, S, 256] (any strides, unit last), seqlen int32 [streams], one mask for
+    all; returns bf16 [1, streams * S, H * 256] (stream b's rows [b S, ...))."""
     _cuda(q, key, value, seqlen, xk, xv)
     _check(q.dtype == torch.bfloat16 and q.dim() == 4 and q.size(0) == 1 and q.size(3) == 256, "q bf16 [1, H, S, 256]")
     _check(streams >= 1 and q.size(1) % streams == 0 and key.size(1) % streams == 0, "heads in equal groups per stream")
@@ -323,7 +325,15 @@ def attn_dpas(q, key, value, seqlen, xk, xv, mask, chunks_hint=0, out=None, stre
     tree = mask.numel() > 0
     _check(mask.numel() == S if tree else S == 1, "mask [S] (or empty with one row)")
     q = q.contiguous()
-    xk, xv = xk.contiguous(), xv.contiguous()
+    xk = xk.contiguous()
+    if xv.dim() == 4 and xv.size(0) == 1 and xv.size(1) == streams * Hk and streams > 1:
+        xv = xv.view(streams, Hk, xv.size(2), xv.size(3)) if xv.is_contiguous() else xv.contiguous().view(
+            streams, Hk, xv.size(2), xv.size(3))
+    _check(xv.dim() == 4 and tuple(xv.shape[1:]) == (Hk, S, 256) and xv.size(0) in (1, streams) and xv.stride(3) == 1,
+           "xv bf16 [streams or 1, Hk, S, 256] with unit last stride")
+    if xv.stride(1) % 8 or xv.stride(2) % 8 or (streams > 1 and xv.stride(0) % 8) or xv.data_ptr() % 16:
+        xv = xv.contiguous()
+    xv_strides = (xv.stride(0) if streams > 1 else 0, xv.stride(1), xv.stride(2))
     nbytes = _lib.load().mono_tree_attention_streams_workspace(Hk, streams, cap)
     ws = _workspace(_attn_ws, (q.device, Hk, streams, cap), nbytes, q.device)
     if out is None:
@@ -332,7 +342,8 @@ def attn_dpas(q, key, value, seqlen, xk, xv, mask, chunks_hint=0, out=None, stre
            "out bf16 [1, streams * S, H * 256]")
     with torch.cuda.device(q.device):
         _lib.call("mono_tree_attention_streams", _p(q), _p(key), _p(value), _p(seqlen), _p(xk), _p(xv),
-                  _p(mask) if tree else None, H, Hk, S, streams, cap, _p(out), _p(ws), nbytes, _stream(q.device))
+                  _p(mask) if tree else None, H, Hk, S, streams, cap, *xv_strides, _p(out), _p(ws), nbytes,
+                  _stream(q.device))
     return out
 
 

@@ -43,7 +43,7 @@ SIGNATURES = {
                                          ctypes.c_float, ctypes.c_float, I64, P, P, P]),
     "mono_tree_attention_workspace": (SZ, [I64, I64]),
     "mono_tree_attention_streams_workspace": (SZ, [I64, I64, I64]),
-    "mono_tree_attention_streams": (I, [P, P, P, P, P, P, P, I64, I64, I64, I64, I64, P, P, SZ, P]),
+    "mono_tree_attention_streams": (I, [P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, I64, I64, P, P, SZ, P]),
     "mono_gdn_step_streams_workspace": (SZ, [I64, I64, I64, I64]),
     "mono_gdn_step_deferred_streams": (I, [P, P, P, P, P, P, P, P, P, P, ctypes.c_float, ctypes.c_float, I64, I64, I64,
                                            I64, P, P, I64, P, P, P, P, P, P, I64, I64, I64, P, SZ, P]),

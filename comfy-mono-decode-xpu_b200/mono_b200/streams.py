@@ -135,10 +135,11 @@ class Qwen35W4A8Streams(Qwen35W4A8):
 
     # ---- layers --------------------------------------------------------------------------------------------
     def _kv_rows(self, v):
-        """v rows [B R, Hk, 256] (stream-major) as the attention's tree keys / values [1, B Hk, R, 256]."""
+        """v rows [1, B R, Hk, 256] (stream-major, a view of the projection's rows) as the attention's tree values
+        [B, Hk, R, 256]: a strided view, read in place by the kernel."""
         B = self.streams
         M, Hk, hd = v.shape[1], v.shape[2], v.shape[3]
-        return v.reshape(B, M // B, Hk, hd).permute(0, 2, 1, 3).reshape(1, B * Hk, M // B, hd)
+        return v[0].view(B, M // B, Hk, hd).permute(0, 2, 1, 3)
 
     def _attention(self, L, x, freqs, i=-1):
         c, B = self.cfg, self.streams

@@ -218,14 +218,17 @@ MONO_API int mono_tree_attention(const void* q, const void* key_cache, const voi
                                  int64_t cap, void* out, void* workspace, size_t workspace_bytes, mono_stream_t stream);
 /* The same for `streams` batched decode streams (1 <= streams <= 8) with one tree shape (mask int32 [S], shared):
  * q bf16 [streams][H][S][256]; caches bf16 [streams][Hk][cap][256]; seqlen int32 [streams] (stream b's committed
- * length); xk, xv bf16 [streams][Hk][S][256]; out bf16 [streams][S][H * 256]. Every stream's context is split as
- * it would be alone, so each stream's output equals its one-stream call's. Workspace:
- * mono_tree_attention_streams_workspace(Hk, streams, cap) bytes, zero-filled before first use. */
+ * length); xk bf16 [streams][Hk][S][256]; xv: the tree value row t of stream b's kv head k at element offset
+ * b xv_stream_stride + k xv_head_stride + t xv_row_stride (multiples of 8; the projection rows in place, no
+ * copy); out bf16 [streams][S][H * 256]. Every stream's context is split as it would be alone, so each stream's
+ * output equals its one-stream call's. Workspace: mono_tree_attention_streams_workspace(Hk, streams, cap) bytes,
+ * zero-filled before first use. */
 MONO_API size_t mono_tree_attention_streams_workspace(int64_t Hk, int64_t streams, int64_t cap);
 MONO_API int mono_tree_attention_streams(const void* q, const void* key_cache, const void* value_cache,
                                          const int32_t* seqlen, const void* xk, const void* xv, const int32_t* mask,
-                                         int64_t H, int64_t Hk, int64_t S, int64_t streams, int64_t cap, void* out,
-                                         void* workspace, size_t workspace_bytes, mono_stream_t stream);
+                                         int64_t H, int64_t Hk, int64_t S, int64_t streams, int64_t cap,
+                                         int64_t xv_stream_stride, int64_t xv_head_stride, int64_t xv_row_stride,
+                                         void* out, void* workspace, size_t workspace_bytes, mono_stream_t stream);
 
 /* ---- Gated-DeltaNet ----------------------------------------------------------------------------------- */
 
