@@ -480,10 +480,11 @@ int mono_fast_topk(const void* x, int64_t rows, int64_t V, int64_t k, int argmax
 
 size_t mono_rowlin_gptq_workspace(int64_t K) { return K < 1 ? 0 : rowlin_workspace_bytes(int(K)); }
 
-int mono_rowlin_gptq(const void* x, int mode, const void* norm_w, float eps, const void* gate, int64_t gate_row_stride,
-                     int64_t gate_head_stride, const void* lut, const void* const* weights, const int64_t* rows, int nm,
-                     int64_t M, int64_t K, const void* residual, void* out, void* xn_out, void* workspace,
-                     size_t workspace_bytes, mono_stream_t stream) {
+static int rowlin_entry(const void* x, int mode, const void* norm_w, float eps, const void* gate, int64_t gate_row_stride,
+                        int64_t gate_head_stride, const void* lut, const void* const* weights, const int64_t* rows, int nm,
+                        int64_t M, int64_t K, const void* residual, void* out, void* xn_out, const void* ab_w,
+                        int64_t ab_n, void* ab_out, int64_t ab_stride, void* workspace, size_t workspace_bytes,
+                        mono_stream_t stream) {
     MONO_CHECK(x && weights && rows && out && workspace, "null operand");
     MONO_CHECK(mode == ROWLIN_NORM || mode == ROWLIN_GATE || mode == ROWLIN_QUANT, "mode 0 (norm), 1 (gate), 2 (quant)");
     MONO_CHECK(mode != ROWLIN_NORM || norm_w, "norm mode needs norm_w");
@@ -527,7 +528,33 @@ int mono_rowlin_gptq(const void* x, int mode, const void* norm_w, float eps, con
     A.bar = reinterpret_cast<unsigned*>(w + qb + 256);
     A.mode = mode;
     A.N = int(N);
+    if (ab_out) {
+        MONO_CHECK(mode == ROWLIN_NORM && xn_out, "a|b projection: norm mode with xn_out");
+        MONO_CHECK(ab_w && aligned(ab_w, 16) && ab_n >= 1 && ab_n <= 128 && ab_stride >= ab_n,
+                   "a|b: bf16 weights [ab_n][K] (16-byte aligned), 1 <= ab_n <= 128, ab_stride >= ab_n");
+        A.ab_w = static_cast<const uint16_t*>(ab_w);
+        A.ab_out = static_cast<uint16_t*>(ab_out);
+        A.ab_n = int(ab_n);
+        A.ab_stride = ab_stride;
+    }
     return launch_rowlin(P, A, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int mono_rowlin_gptq(const void* x, int mode, const void* norm_w, float eps, const void* gate, int64_t gate_row_stride,
+                     int64_t gate_head_stride, const void* lut, const void* const* weights, const int64_t* rows, int nm,
+                     int64_t M, int64_t K, const void* residual, void* out, void* xn_out, void* workspace,
+                     size_t workspace_bytes, mono_stream_t stream) {
+    return rowlin_entry(x, mode, norm_w, eps, gate, gate_row_stride, gate_head_stride, lut, weights, rows, nm, M, K,
+                        residual, out, xn_out, nullptr, 0, nullptr, 0, workspace, workspace_bytes, stream);
+}
+
+int mono_rowlin_norm_ab_gptq(const void* x, const void* norm_w, float eps, const void* const* weights,
+                             const int64_t* rows, int nm, int64_t M, int64_t K, void* out, void* xn_out,
+                             const void* ab_w, int64_t ab_n, void* ab_out, int64_t ab_stride, void* workspace,
+                             size_t workspace_bytes, mono_stream_t stream) {
+    MONO_CHECK(ab_out && xn_out, "null operand");
+    return rowlin_entry(x, ROWLIN_NORM, norm_w, eps, nullptr, 0, 0, nullptr, weights, rows, nm, M, K, nullptr, out,
+                        xn_out, ab_w, ab_n, ab_out, ab_stride, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

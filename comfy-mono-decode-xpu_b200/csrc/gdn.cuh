@@ -291,11 +291,12 @@ __device__ __forceinline__ void gdn_ab_load_w(const uint16_t* __restrict__ w, in
     for (int j = 0; j < 4; ++j)
         if (j < J4) wv[j] = __ldg(wr + 32 * j);
 }
+// Rows m0, m0 + mstep, .. < M of xs (row stride K); qsum[m] = the quarter sum of row m.
 __device__ __forceinline__ void gdn_ab_quarter(const uint16_t* __restrict__ xs, const uint4 (&wv)[4], int K, int M, int q,
-                                               int lane, float* qsum) {
+                                               int lane, float* qsum, int m0 = 0, int mstep = 1) {
     const int J4 = K >> 10;
 #pragma unroll 1
-    for (int m = 0; m < M; ++m) {
+    for (int m = m0; m < M; m += mstep) {
         const uint4* xr = reinterpret_cast<const uint4*>(xs + size_t(m) * K) + 32 * (q * J4) + lane;
         float acc = 0.f;
 #pragma unroll

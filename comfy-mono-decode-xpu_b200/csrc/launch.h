@@ -62,6 +62,12 @@ struct RowLinArgs {
     float* s;                  // workspace [kStreamMaxRows]
     unsigned* bar;             // workspace [2], zero between launches
     int mode, N;
+    // NORM with xn_out: the GDN a | b projection of the normalized rows (gdn.cuh gdn_ab_quarter order), column c
+    // by CTA gridDim.x - 1 - c after its GEMV tiles: ab_out[m * ab_stride + c] for c < ab_n (null: none)
+    const uint16_t* ab_w;  // [ab_n][K] bf16
+    uint16_t* ab_out;
+    int ab_n;
+    int64_t ab_stride;
 };
 size_t rowlin_workspace_bytes(int K);
 int launch_rowlin(Program& P, RowLinArgs& A, cudaStream_t stream);

@@ -31,8 +31,9 @@ namespace mono {
 // The last CTA to leave clears the row maxima for the next launch (every CTA has read them by then).
 // Measured alternatives (not kept): every CTA preparing all rows itself, or quantizing all of h itself, to drop
 // a barrier: the per-element work of M full rows on one SM outweighs a barrier (12 us against 6 us for P1 at
-// M = 5); and tiles split across CTAs for an even item count: the exchange of the cut tiles' partials costs
-// three L2 round trips per phase.
+// M = 5; every CTA quantizing all 8 x 12288 values of h while staging them, with 16 loads in flight per thread:
+// P3 28 us against 6 us, about 17 instructions per value, i.e. ~15k issue cycles per SM); and tiles split across
+// CTAs for an even item count: the exchange of the cut tiles' partials costs three L2 round trips per phase.
 template <int MT, int CW, int PW>
 __global__ void __launch_bounds__((CW + PW) * 32, 1) mlp_kernel(const Program P, const MlpArgs A, const MlpShape Z) {
     extern __shared__ __align__(128) uint8_t smem[];

@@ -13,6 +13,7 @@
 #include <mutex>
 
 #include "launch.h"
+#include "gdn.cuh"
 #include "grid.cuh"
 #include "rowops.cuh"
 #include "stream.cuh"
@@ -50,6 +51,11 @@ __global__ void __launch_bounds__((CW + PW) * 32, 1) rowlin_kernel(const Program
         return;
     }
     constexpr int NT = CW * 32;
+    const int ab_col = int(gridDim.x) - 1 - int(blockIdx.x);
+    const bool ab = A.ab_out != nullptr && ab_col < A.ab_n;
+    if (ab && threadIdx.x == 0)  // the a | b column's weights (constant) into L2 for the tail phase
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(A.ab_w + size_t(ab_col) * K), "r"(K * 2)
+                     : "memory");
     pdl_wait();
     unsigned epoch = 0;
     bool ok = true;
@@ -93,6 +99,37 @@ __global__ void __launch_bounds__((CW + PW) * 32, 1) rowlin_kernel(const Program
         consumer_sync<CW>();  // the batch's partials are read before the next batch writes them
     }
     trace_stamp(4);
+    if (ab && ok) {
+        // GDN a | b column ab_col on a CTA with the fewest GEMV tiles: warp w takes quarter w & 3 of the rows
+        // w / 4, w / 4 + RG, .. (gdn.cuh gdn_ab_quarter: the order of mono_gdn_ab); the normalized rows (written
+        // in P1, before the grid barrier) are copied in blocks into the ring, idle once every item is consumed.
+        constexpr int RG = CW / 4;
+        const int q = warp & 3, rg = warp >> 2, per = K >> 3;
+        const int R = int(plan.ring / (size_t(K) * 2));
+        float* abq = reinterpret_cast<float*>(part);  // [4][kStreamMaxRows]; the partials are summed already
+        uint16_t* xs = reinterpret_cast<uint16_t*>(ring);
+        uint4 wv[4];
+        if (rg < RG) gdn_ab_load_w(A.ab_w, K, ab_col, q, lane, wv);
+        for (int r0 = 0; r0 < M; r0 += R) {
+            const int rb = M - r0 < R ? M - r0 : R;
+            const uint4* src = reinterpret_cast<const uint4*>(A.xn_out + size_t(r0) * K);
+            for (int base = threadIdx.x; base < rb * per; base += 16 * NT) {
+                uint4 v[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (base + j * NT < rb * per) v[j] = __ldcg(src + base + j * NT);
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (base + j * NT < rb * per) reinterpret_cast<uint4*>(xs)[base + j * NT] = v[j];
+            }
+            consumer_sync<CW>();
+            if (rg < RG) gdn_ab_quarter(xs, wv, K, rb, q, lane, abq + q * kStreamMaxRows + r0, rg, RG);
+            consumer_sync<CW>();
+        }
+        if (int(threadIdx.x) < M)
+            A.ab_out[size_t(threadIdx.x) * A.ab_stride + ab_col] = gdn_ab_combine(abq, kStreamMaxRows, threadIdx.x);
+        trace_stamp(5);
+    }
     grid_exit_named<kConsumerBar, NT>(A.bar);
 }
 
@@ -115,6 +152,7 @@ static int launch_rowlin_t(const Program& P, const RowLinArgs& A, const MlpShape
     if (per_sm < 1) return fail(MONO_EINVAL, "rowlin: one CTA does not fit an SM (%zu B shared)", smem);
     const int tiles = phase_tiles(P.ph[0]);
     const int grid = tiles < sm_count() ? tiles : sm_count();
+    if (A.ab_out && A.ab_n > grid) return fail(MONO_EINVAL, "rowlin: %d a|b columns on %d CTAs", A.ab_n, grid);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3((CW + PW) * 32);

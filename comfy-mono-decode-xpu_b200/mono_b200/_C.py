@@ -447,11 +447,13 @@ _rowlin_ws = {}
 
 
 def rowlin_gptq(x, mode, weights, norm_w=None, eps=1e-6, gate=None, gate_head_stride=512, lut=None, residual=None,
-                out=None, xn_out=None):
+                out=None, xn_out=None, ab=None):
     """Row preparation (RMSNorm / sigmoid gate / plain) + per-token quant + GPTQ W4A8 linear of up to three TILED
     matrices in one launch (include/mono_b200.h mono_rowlin_gptq). weights: list of (tiled uint8 tensor, rows).
     gate: bf16 [M, ...] whose row m holds the gate of column c at (c / 256) * gate_head_stride + c % 256.
-    Returns out bf16 [M, sum rows]."""
+    ab = (w bf16 [N, K], out bf16 [M, N] with unit column stride): NORM mode with xn_out only; the same launch
+    also writes the GDN a | b projection of the normalized rows, gdn_ab(xn_out, w) bit for bit
+    (mono_rowlin_norm_ab_gptq). Returns out bf16 [M, sum rows]."""
     import ctypes
     _cuda(x)
     _check(x.dtype == torch.bfloat16 and x.dim() == 2 and x.is_contiguous(), "x bf16 [M, K] contiguous")
@@ -470,6 +472,21 @@ def rowlin_gptq(x, mode, weights, norm_w=None, eps=1e-6, gate=None, gate_head_st
     nbytes = _lib.load().mono_rowlin_gptq_workspace(K)
     ws = _workspace(_rowlin_ws, (x.device, K), nbytes, x.device)
     gate_row_stride = gate.stride(0) if gate is not None else 0
+    if ab is not None:
+        wab, ab_out = ab
+        _check(mode == ROWLIN_NORM and xn_out is not None and norm_w is not None and residual is None,
+               "a|b projection: norm mode with xn_out, no residual")
+        _check(xn_out.dtype == torch.bfloat16 and xn_out.is_contiguous() and xn_out.shape == x.shape, "xn_out [M, K]")
+        _check(wab.dtype == torch.bfloat16 and wab.is_contiguous() and wab.dim() == 2 and wab.shape[1] == K,
+               "a|b weights bf16 [N, K]")
+        _check(ab_out.dtype == torch.bfloat16 and ab_out.dim() == 2 and ab_out.shape == (M, wab.shape[0]) and
+               ab_out.stride(1) == 1, "a|b out bf16 [M, N]")
+        _cuda(wab, ab_out)
+        with torch.cuda.device(x.device):
+            _lib.call("mono_rowlin_norm_ab_gptq", _p(x), _p(norm_w), float(eps), ctypes.cast(ptrs, ctypes.c_void_p),
+                      ctypes.cast(rows, ctypes.c_void_p), len(weights), M, K, _p(out), _p(xn_out), _p(wab),
+                      int(wab.shape[0]), _p(ab_out), ab_out.stride(0), _p(ws), nbytes, _stream(x.device))
+        return out
     with torch.cuda.device(x.device):
         _lib.call("mono_rowlin_gptq", _p(x), int(mode), _p(norm_w), float(eps), _p(gate), gate_row_stride,
                   int(gate_head_stride), _p(lut), ctypes.cast(ptrs, ctypes.c_void_p), ctypes.cast(rows, ctypes.c_void_p),

@@ -17,8 +17,8 @@ comfy_mono_decode_xpu/mtp_loop.py:270-341):
            of an off-chain path, next token and hidden row (all on the device)
 
 Per layer: full attention = rowlin(norm -> q|k|v) -> qk_norm_rope_kv -> tree attention -> rowlin(gate -> o_proj +
-residual) -> fused MLP; GDN = rowlin(norm -> qkv|z, xn) -> a|b (mono_gdn_ab) -> deferred GDN step ->
-rowlin(quant -> out_proj + residual) -> fused MLP. The MTP head's five bf16 projections run on this build's bf16
+residual) -> fused MLP; GDN = rowlin(norm -> qkv|z, xn, + the a|b projection of xn on the launch's last CTAs:
+mono_rowlin_norm_ab_gptq) -> deferred GDN step -> rowlin(quant -> out_proj + residual) -> fused MLP. The MTP head's five bf16 projections run on this build's bf16
 GEMV (mono_gemv_bf16; cuBLAS through torch's F.linear with draft_gemv=False); its norms and gates are the row kernels
 (mono_rmsnorm_add, mono_lut_mul).
 """
@@ -258,9 +258,9 @@ class Qwen35W4A8:
         HV, D = c.gdn_v_heads, c.gdn_dim
         Ck = 2 * c.gdn_k_heads * D + HV * D
         xn = torch.empty_like(x)
+        ab = torch.empty((x.shape[0], L["wab"].shape[0]), dtype=torch.bfloat16, device=x.device)
         pre = _C.rowlin_gptq(x, _C.ROWLIN_NORM, [(L["qkv"], Ck), (L["z"], HV * D)], norm_w=L["ln1"], eps=c.eps,
-                             xn_out=xn)
-        ab = _C.gdn_ab(xn, L["wab"])
+                             xn_out=xn, ab=(L["wab"], ab))  # + the a | b projection of xn in the same launch
         prev, save = L["saved"][self.parity], L["saved"][1 - self.parity]
         core = _C.gdn_step_deferred(pre[:, :Ck], pre[:, Ck:], ab[:, :HV], ab[:, HV:], L["conv_w"], L["conv_state"],
                                     L["dt_bias"], L["g_decay"],
@@ -459,8 +459,8 @@ class Qwen35W4A8:
         n_gdn = c.layers - n_attn
         if self.fused:  # one layer program per run of layers between attention cores; rope + attention x2
             body = (n_attn + 1) + n_attn * 3
-        else:  # rowlin x2 + MLP; GDN a|b + conv + delta; rope + attention x2
-            body = c.layers * 3 + n_gdn * 3 + n_attn * 3
+        else:  # rowlin x2 (the GDN layers' first with the a|b projection) + MLP; GDN conv + delta; rope + attention x2
+            body = c.layers * 3 + n_gdn * 2 + n_attn * 3
         # per draft: prep, 2 norms, rope, attention x2, 2 luts, 3 norm(-add)s, lm_head pick (+ 5 projections)
         draft = c.depth * (1 + 2 + 1 + 2 + 2 + 3 + 1 + (5 if self.draft_gemv else 0))
         return body + draft + 1 + 1 + 1 + 1  # prep_verify, final norm, lm_head pick, accept

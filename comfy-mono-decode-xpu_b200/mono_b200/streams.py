@@ -17,7 +17,7 @@ and every row-wise kernel takes the B x 8 verify rows (B draft rows) as one batc
   draft head projections            mono_gemv_bf16 at M = B
   lm_head picks                     mono_lmhead_pick at M = B (each draft, dst row per stream) and for the verify
                                     in launches of up to 16 rows (one lm_head read per 2 streams)
-  GDN a | b projection              mono_gdn_ab (blocks of 16 rows across the grid)
+  GDN layer_pre + a | b projection  mono_rowlin_norm_ab_gptq at M = 8 B
   MTP prep / accept                 one launch per stream (a few microseconds each)
 
 Each stream's arithmetic is exactly its one-stream step's (row-wise kernels; attention chunks a stream's context as
@@ -165,9 +165,9 @@ class Qwen35W4A8Streams(Qwen35W4A8):
         HV, D = c.gdn_v_heads, c.gdn_dim
         Ck = 2 * c.gdn_k_heads * D + HV * D
         xn = torch.empty_like(x)
+        ab = torch.empty((x.shape[0], L["wab"].shape[0]), dtype=torch.bfloat16, device=x.device)
         pre = _C.rowlin_gptq(x, _C.ROWLIN_NORM, [(L["qkv"], Ck), (L["z"], HV * D)], norm_w=L["ln1"], eps=c.eps,
-                             xn_out=xn)
-        ab = _C.gdn_ab(xn, L["wab"])
+                             xn_out=xn, ab=(L["wab"], ab))  # + the a | b projection of xn in the same launch
         prev, save = L["saved"][self.parity], L["saved"][1 - self.parity]
         core = _C.gdn_step_deferred(pre[:, :Ck], pre[:, Ck:], ab[:, :HV], ab[:, HV:], L["conv_w"], L["conv_state"],
                                     L["dt_bias"], L["g_decay"], L["state"], L["gnorm"], c.eps, D ** -0.5,
@@ -251,7 +251,7 @@ class Qwen35W4A8Streams(Qwen35W4A8):
         c, B = self.cfg, self.streams
         n_attn = sum(1 for i in range(c.layers) if c.is_attn(i))
         n_gdn = c.layers - n_attn
-        body = c.layers * 3 + n_gdn * 3 + n_attn * 2
+        body = c.layers * 3 + n_gdn * 2 + n_attn * 2
         draft = c.depth * (B + 2 + 1 + 1 + 2 + 3 + 1 + (5 if self.draft_gemv else 0))
         picks = -(-B * self.tree["rows"] // PICK_ROWS)
         return body + draft + B + 1 + picks + B  # prep_verify per stream, final norm, lm_head picks, accepts

@@ -163,7 +163,7 @@ MONO_API int mono_mlp_gptq(const void* x, const void* norm_w, float eps, const v
  *   mode 2 (quant): q, s = act_quant(x)
  *   out[m][n] = bf16(GPTQ linear(q, s)) (+ residual: bf16(residual + that)) for nm (1..3) TILED weights of
  *   rows[i] outputs each, concatenated along n (out row stride = sum of rows).
- * x bf16 [M][K], 1 <= M <= 16, K a multiple of 1024 up to 4096. workspace: mono_rowlin_gptq_workspace(K) bytes,
+ * x bf16 [M][K], 1 <= M <= 32, K a multiple of 1024 up to 4096. workspace: mono_rowlin_gptq_workspace(K) bytes,
  * zero-filled before its first use (the kernel leaves it reusable); one call at a time per workspace. */
 MONO_API size_t mono_rowlin_gptq_workspace(int64_t K);
 MONO_API int mono_rowlin_gptq(const void* x, int mode, const void* norm_w, float eps, const void* gate,
@@ -171,6 +171,15 @@ MONO_API int mono_rowlin_gptq(const void* x, int mode, const void* norm_w, float
                               const void* const* weights, const int64_t* rows, int nm, int64_t M, int64_t K,
                               const void* residual, void* out, void* xn_out, void* workspace, size_t workspace_bytes,
                               mono_stream_t stream);
+/* The GDN layer's front in one launch: mono_rowlin_gptq in mode 0 (RMSNorm -> quant -> qkv | z, the normalized
+ * rows to xn_out [M][K], required) and the a | b projection of those rows, ab_out[m * ab_stride + n] =
+ * mono_gdn_ab(xn_out, ab_w)[m][n] bit for bit (ab_w bf16 [ab_n][K], 1 <= ab_n <= 128 and at most the launch's
+ * CTAs: min(output rows / 16, SMs)). It replaces mono_rowlin_gptq + mono_gdn_ab of the reference's GDN layer_pre
+ * (csrc/mono_layer.sycl:69-155 and the in_proj_a / in_proj_b linear, csrc/mono_gdn.sycl:10-11). */
+MONO_API int mono_rowlin_norm_ab_gptq(const void* x, const void* norm_w, float eps, const void* const* weights,
+                                      const int64_t* rows, int nm, int64_t M, int64_t K, void* out, void* xn_out,
+                                      const void* ab_w, int64_t ab_n, void* ab_out, int64_t ab_stride,
+                                      void* workspace, size_t workspace_bytes, mono_stream_t stream);
 
 /* ---- full-attention decode layer ------------------------------------------------------------------ */
 

@@ -39,6 +39,35 @@ def test_rowlin_norm_qkv_bit_exact(cuda, M):
     assert np.array_equal(bf16_bits(xn_out), xn)
 
 
+@pytest.mark.parametrize("M", [1, 5, 8, 16, 24, 32])
+def test_rowlin_norm_ab_bit_exact(cuda, M):
+    """The GDN layer_pre in one launch (mono_rowlin_norm_ab_gptq): qkv | z, the normalized rows and the a | b
+    projection of those rows (on the launch's last CTAs) equal the oracle and the separate mono_gdn_ab call."""
+    from mono_b200 import _C
+    from oracle import gdn as og
+    K, HV = 4096, 32
+    host, dev = _mats([8192, 4096], K, 0x5EED + 7, cuda)
+    g = torch.Generator().manual_seed(70 + M)
+    x = torch.randn(M, K, generator=g).bfloat16()
+    w = (1 + torch.randn(K, generator=g) * 0.02).bfloat16()
+    wab = (torch.randn(2 * HV, K, generator=g) * 0.02).bfloat16()
+    xn = ol.rmsnorm(bf16_bits(x), bf16_bits(w), 1e-6)
+    q, s = ow.act_quant(xn)
+    ref = np.concatenate([ow.gptq_linear(q, s, p, sc) for p, sc in host], axis=1)
+    xn_out = torch.empty(M, K, dtype=torch.bfloat16, device=cuda)
+    wide = torch.full((M, 2 * HV + 8), -1.0, dtype=torch.bfloat16, device=cuda)  # a row stride wider than N
+    ab = wide[:, 4:4 + 2 * HV]
+    out = _C.rowlin_gptq(x.to(cuda), _C.ROWLIN_NORM, dev, norm_w=w.to(cuda), eps=1e-6, xn_out=xn_out,
+                         ab=(wab.to(cuda), ab))
+    torch.cuda.synchronize()
+    assert np.array_equal(bf16_bits(out), ref)
+    assert np.array_equal(bf16_bits(xn_out), xn)
+    assert np.array_equal(bf16_bits(ab), og.ab_projection(xn, bf16_bits(wab)))
+    assert np.array_equal(bf16_bits(ab), bf16_bits(_C.gdn_ab(xn_out, wab.to(cuda))))
+    assert bool((wide[:, :4] == -1).all()) and bool((wide[:, 4 + 2 * HV:] == -1).all())  # nothing outside the view
+    assert _C.device_status() == 0
+
+
 @pytest.mark.parametrize("M", [1, 8, 32])
 def test_rowlin_gate_oproj_residual_bit_exact(cuda, M):
     from mono_b200 import _C
