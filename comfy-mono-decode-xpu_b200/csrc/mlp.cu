@@ -77,8 +77,7 @@ __global__ void __launch_bounds__((CW + PW) * 32, 1) mlp_kernel(const Program P,
                                              A.s1 + m, red);
     if (threadIdx.x < kStreamMaxRows) rowmax[threadIdx.x] = 0u;
     ok = grid_barrier_named<kConsumerBar, NT>(A.bar, epoch, &flag) && ok;
-    if (threadIdx.x < M) s1s[threadIdx.x] = __ldcg(A.s1 + threadIdx.x);
-    stage_x_consumers<CW>(A.q1, M, A.H, true, xsm);
+    stage_x_consumers<CW>(A.q1, M, A.H, true, xsm, A.s1, s1s);  // the rows and their scales in one round trip
     trace_stamp(2);
 
     // ---- P2: gate / up, h = silu(g) * u, row maxima of |h| (tiles in batches of Z.tb0: the partials of a batch

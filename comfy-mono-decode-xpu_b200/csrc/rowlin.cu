@@ -27,6 +27,7 @@ template <int MT, int CW, int PW>
 __global__ void __launch_bounds__((CW + PW) * 32, 1) rowlin_kernel(const Program P, const RowLinArgs A, const MlpShape Z) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float red[64];
+    __shared__ float ss[kStreamMaxRows];  // the row scales, staged with the rows
     __shared__ int flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int M = P.M, S = Z.S, K = P.ph[0].K;
@@ -57,6 +58,7 @@ __global__ void __launch_bounds__((CW + PW) * 32, 1) rowlin_kernel(const Program
         asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(A.ab_w + size_t(ab_col) * K), "r"(K * 2)
                      : "memory");
     pdl_wait();
+    trace_stamp(1);
     unsigned epoch = 0;
     bool ok = true;
     // row m on CTA m, all consumer threads (rowops.cuh: the pinned order of the warp-group forms)
@@ -70,16 +72,19 @@ __global__ void __launch_bounds__((CW + PW) * 32, 1) rowlin_kernel(const Program
                                                  A.xn_out ? A.xn_out + size_t(m) * K : nullptr, A.q + size_t(m) * K,
                                                  A.s + m, red);
     }
-    trace_stamp(1);
-    ok = grid_barrier_named<kConsumerBar, NT>(A.bar, epoch, &flag);
     trace_stamp(2);
+    ok = grid_barrier_named<kConsumerBar, NT>(A.bar, epoch, &flag);
+    trace_stamp(3);
     const PhaseDesc& ph = P.ph[0];
     XSrc xs{ph.x, K, false, true, true};  // written by this launch: L2 reads
     if (ph.xsmem) {
-        stage_x_consumers<CW>(ph.x, M, K, true, xsm);
+        stage_x_consumers<CW>(ph.x, M, K, true, xsm, A.s, ss);  // the rows and their scales in one round trip
         xs = XSrc{xsm, K + 16, true, true};
+    } else {
+        if (int(threadIdx.x) < M) ss[threadIdx.x] = __ldcg(A.s + threadIdx.x);
+        consumer_sync<CW>();
     }
-    trace_stamp(3);
+    trace_stamp(4);
     // tiles in batches of Z.tb0 (the partials of a batch fit the shared buffer; one batch unless the rows are many)
     const int C = phase_chunks(ph), ntl = cta_tiles(ph), TB = Z.tb0;
     for (int k0 = 0; k0 < ntl && ok; k0 += TB) {
@@ -91,14 +96,14 @@ __global__ void __launch_bounds__((CW + PW) * 32, 1) rowlin_kernel(const Program
             const int k = e / (M * 16), r = e - k * (M * 16), m = r >> 4, nl = r & 15;
             const int n = (int(blockIdx.x) + (k0 + k) * int(gridDim.x)) * 16 + nl;  // concatenated output column
             const float tot = __uint_as_float(tile_total<FMT_GPTQ, MT>(part + size_t(k) * C * MT * 128, C, 0, m, nl));
-            uint16_t rr = f32_to_bf16_bits(__fmul_rn(tot, __ldcg(A.s + m)));
+            uint16_t rr = f32_to_bf16_bits(__fmul_rn(tot, ss[m]));
             const size_t o = size_t(m) * A.N + n;
             if (A.residual) rr = f32_to_bf16_bits(__fadd_rn(bf16_bits_to_f32(A.residual[o]), bf16_bits_to_f32(rr)));
             A.out[o] = rr;
         }
         consumer_sync<CW>();  // the batch's partials are read before the next batch writes them
     }
-    trace_stamp(4);
+    trace_stamp(5);
     if (ab && ok) {
         // GDN a | b column ab_col on a CTA with the fewest GEMV tiles: warp w takes quarter w & 3 of the rows
         // w / 4, w / 4 + RG, .. (gdn.cuh gdn_ab_quarter: the order of mono_gdn_ab); the normalized rows (written
@@ -128,7 +133,7 @@ __global__ void __launch_bounds__((CW + PW) * 32, 1) rowlin_kernel(const Program
         }
         if (int(threadIdx.x) < M)
             A.ab_out[size_t(threadIdx.x) * A.ab_stride + ab_col] = gdn_ab_combine(abq, kStreamMaxRows, threadIdx.x);
-        trace_stamp(5);
+        trace_stamp(6);
     }
     grid_exit_named<kConsumerBar, NT>(A.bar);
 }

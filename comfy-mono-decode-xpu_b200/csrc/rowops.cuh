@@ -262,22 +262,29 @@ __device__ __forceinline__ void norm_quant_row_cta(const uint16_t* __restrict__ 
     constexpr int KP = RowPieces<NT>::kMax;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, np = H >> 3, J = H >> 10;
     float vals[KP][8];
-    uint4 wv[KP];
+    uint4 wv[KP], xv[KP];
+    // every load of the row in flight at once: the pieces of the sum of squares (threads t < 128: pieces
+    // t + 128 j, the pinned order), then the thread's own pieces and norm weights
+    uint4 sv[kRowMaxPieces];
+    if (w && tid < 128)
+#pragma unroll
+        for (int j = 0; j < kRowMaxPieces; ++j)
+            if (j < J) sv[j] = __ldcg(reinterpret_cast<const uint4*>(x) + tid + 128 * j);
 #pragma unroll
     for (int i = 0; i < KP; ++i)
         if (tid + NT * i < np) {
-            const uint4 v = __ldcg(reinterpret_cast<const uint4*>(x) + tid + NT * i);
+            xv[i] = __ldcg(reinterpret_cast<const uint4*>(x) + tid + NT * i);
             if (w) wv[i] = __ldg(reinterpret_cast<const uint4*>(w) + tid + NT * i);
-            const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+        }
+#pragma unroll
+    for (int i = 0; i < KP; ++i)
+        if (tid + NT * i < np) {
+            const uint32_t u[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
 #pragma unroll
             for (int e = 0; e < 8; ++e) vals[i][e] = __uint_as_float((e & 1) ? (u[e >> 1] & 0xFFFF0000u) : (u[e >> 1] << 16));
         }
     if (w) {
         if (tid < 128) {  // the pinned sum of squares: thread t over pieces t + 128 j
-            uint4 sv[kRowMaxPieces];
-#pragma unroll
-            for (int j = 0; j < kRowMaxPieces; ++j)
-                if (j < J) sv[j] = __ldcg(reinterpret_cast<const uint4*>(x) + tid + 128 * j);
             float p = 0.f;
 #pragma unroll
             for (int j = 0; j < kRowMaxPieces; ++j)

@@ -255,10 +255,15 @@ __device__ __forceinline__ bool consume_phase(const Program& P, int ph, const XS
 // Vector staging of an activation block x [M][K] (rows contiguous) by the consumer threads into shared
 // memory (pitch K + 16), permuted unless x is permuted already: batches of 8 pieces of 16 bytes per
 // thread, every load of a batch in flight before any store. Ends with a consumer barrier.
+// sc (optional): the M row scales, copied to sc_dst[M] in the same round trip as the first batch.
 template <int CW>
-__device__ __forceinline__ void stage_x_consumers(const int8_t* x, int M, int K, bool xperm, int8_t* xsm) {
+__device__ __forceinline__ void stage_x_consumers(const int8_t* x, int M, int K, bool xperm, int8_t* xsm,
+                                                  const float* sc = nullptr, float* sc_dst = nullptr) {
     const int T = CW * 32, words = K >> 4, total = M * words;
     const uint4* src = reinterpret_cast<const uint4*>(x);
+    const bool own_sc = sc != nullptr && int(threadIdx.x) < M;
+    float scv = 0.f;
+    if (own_sc) scv = __ldcg(sc + threadIdx.x);
     for (int base = threadIdx.x; base < total; base += 8 * T) {
         uint4 v[8];
 #pragma unroll
@@ -273,6 +278,7 @@ __device__ __forceinline__ void stage_x_consumers(const int8_t* x, int M, int K,
             }
         }
     }
+    if (own_sc) sc_dst[threadIdx.x] = scv;
     consumer_sync<CW>();
 }
 
