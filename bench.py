@@ -320,7 +320,8 @@ def mlp_bytes(M, H, I):
 
 
 MLP_PHASES = ("start", "dependency wait", "P1 rows + barrier + staging", "P2 gate/up consumed", "P2 epilogue",
-              "P2 barrier", "P3 re-quantization + barrier + staging", "P4 down consumed", "P4 epilogue")
+              "P2 barrier", "P3 re-quantization + barrier + staging", "P4 down consumed", "P4 epilogue",
+              "(P3) row maxima read", "(P3) pieces quantized", "(P3) barrier", "(P1) rows", "(P1) barrier")
 
 
 def mlp_phase_trace(launch, dev):

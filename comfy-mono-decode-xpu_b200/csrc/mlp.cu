@@ -76,7 +76,9 @@ __global__ void __launch_bounds__((CW + PW) * 32, 1) mlp_kernel(const Program P,
         norm_quant_row_cta<NT, kConsumerBar>(A.x + size_t(m) * A.H, A.norm_w, A.eps, A.H, nullptr, A.q1 + size_t(m) * A.H,
                                              A.s1 + m, red);
     if (threadIdx.x < kStreamMaxRows) rowmax[threadIdx.x] = 0u;
+    trace_stamp(12);
     ok = grid_barrier_named<kConsumerBar, NT>(A.bar, epoch, &flag) && ok;
+    trace_stamp(13);
     stage_x_consumers<CW>(A.q1, M, A.H, true, xsm, A.s1, s1s);  // the rows and their scales in one round trip
     trace_stamp(2);
 
@@ -115,24 +117,30 @@ __global__ void __launch_bounds__((CW + PW) * 32, 1) mlp_kernel(const Program P,
 
     // ---- P3: q2 = quant(h) ----
     XSrc xs1{A.q2, A.I, false, true, true};
-    if (threadIdx.x < M) s2s[threadIdx.x] = __fdiv_rn(__uint_as_float(__ldcg(A.amax2 + threadIdx.x)), 127.f);
-    consumer_sync<CW>();
     {
-        // 8-element pieces: one 16-byte load of h, one 8-byte store of permuted q2, spread over all CTAs
+        // 8-element pieces: one 16-byte load of h, one 8-byte store of permuted q2, spread over all CTAs; the
+        // thread's first piece is loaded before the row maxima, so both loads are in flight together
         const int ppr = A.I >> 3, pieces = M * ppr;
-        const int stride = int(gridDim.x) * NT;
-        for (int i = int(blockIdx.x) * NT + int(threadIdx.x); i < pieces; i += stride) {
+        const int stride = int(gridDim.x) * NT, i0 = int(blockIdx.x) * NT + int(threadIdx.x);
+        uint4 h0 = make_uint4(0, 0, 0, 0);
+        if (i0 < pieces) h0 = __ldcg(reinterpret_cast<const uint4*>(A.h) + i0);
+        if (threadIdx.x < M) s2s[threadIdx.x] = __fdiv_rn(__uint_as_float(__ldcg(A.amax2 + threadIdx.x)), 127.f);
+        consumer_sync<CW>();
+        trace_stamp(9);
+        for (int i = i0; i < pieces; i += stride) {
             const int m = i / ppr;
-            const uint4 hv = __ldcg(reinterpret_cast<const uint4*>(A.h) + i);
+            const uint4 hv = i == i0 ? h0 : __ldcg(reinterpret_cast<const uint4*>(A.h) + i);
             const uint32_t u[4] = {hv.x, hv.y, hv.z, hv.w};
             float v[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) v[e] = __uint_as_float((e & 1) ? (u[e >> 1] & 0xFFFF0000u) : (u[e >> 1] << 16));
             reinterpret_cast<uint2*>(A.q2)[i] = quant8_perm(v, s2s[m]);
         }
+        trace_stamp(10);
         ok = grid_barrier_named<kConsumerBar, NT>(A.bar, epoch, &flag) && ok;
+        trace_stamp(11);
         if (P.ph[1].xsmem) {
-            stage_x_consumers<CW>(A.q2, M, A.I, true, xsm);
+            stage_x_consumers<CW, 16>(A.q2, M, A.I, true, xsm);  // 16 loads in flight: one round trip at 8 rows
             xs1 = XSrc{xsm, A.I + 16, true, true};
         }
     }

@@ -253,10 +253,10 @@ __device__ __forceinline__ bool consume_phase(const Program& P, int ph, const XS
 }
 
 // Vector staging of an activation block x [M][K] (rows contiguous) by the consumer threads into shared
-// memory (pitch K + 16), permuted unless x is permuted already: batches of 8 pieces of 16 bytes per
+// memory (pitch K + 16), permuted unless x is permuted already: batches of NB (8 or 16) pieces of 16 bytes per
 // thread, every load of a batch in flight before any store. Ends with a consumer barrier.
 // sc (optional): the M row scales, copied to sc_dst[M] in the same round trip as the first batch.
-template <int CW>
+template <int CW, int NB = 8>
 __device__ __forceinline__ void stage_x_consumers(const int8_t* x, int M, int K, bool xperm, int8_t* xsm,
                                                   const float* sc = nullptr, float* sc_dst = nullptr) {
     const int T = CW * 32, words = K >> 4, total = M * words;
@@ -264,13 +264,14 @@ __device__ __forceinline__ void stage_x_consumers(const int8_t* x, int M, int K,
     const bool own_sc = sc != nullptr && int(threadIdx.x) < M;
     float scv = 0.f;
     if (own_sc) scv = __ldcg(sc + threadIdx.x);
-    for (int base = threadIdx.x; base < total; base += 8 * T) {
-        uint4 v[8];
+    // (every CTA walks the block in the same order: staggered start offsets per CTA measured slower)
+    for (int base = threadIdx.x; base < total; base += NB * T) {
+        uint4 v[NB];
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
+        for (int j = 0; j < NB; ++j)
             if (base + j * T < total) v[j] = __ldcg(src + base + j * T);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < NB; ++j) {
             const int i = base + j * T;
             if (i < total) {
                 const int m = i / words, c = i - m * words;
