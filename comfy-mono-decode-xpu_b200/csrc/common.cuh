@@ -19,6 +19,7 @@ enum DeviceError : int {
     DEV_BAD_POSITION = 4,   // a KV-cache position outside [0, capacity): the write was skipped
     DEV_BAD_TREE = 5,       // a children table entry not after its parent or not below rows: the accept walk stopped
     DEV_PEER_TIMEOUT = 6,   // a wait for the peer GPU's arrival (two-GPU all-reduce) gave up
+    DEV_BAD_TOKEN = 7,      // a token id outside [0, vocabulary): embedding row 0 was read instead
 };
 extern __device__ int g_device_error;
 

@@ -82,6 +82,7 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
     __shared__ float vsm[kGdnMaxAll][kDcCols];  // v of the CTA's columns, every row
     __shared__ float gsm[kGdnMaxAll][2];        // decay, beta of every row
     __shared__ int cs[kGdnCtlWords];
+    trace_stamp_2d(0);
     gdn_ctl_stage(A, cs);
     __syncthreads();
     cg::cluster_group cluster = cg::this_cluster();
@@ -99,6 +100,7 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
     for (int r = 0; r < kRPG; ++r) st[r] = S[size_t(r) * kDH];
     pdl_wait();
     pdl_launch_dependents();
+    trace_stamp_2d(1);
     // the gated norm's z and weight for this thread's output elements e = tid + 128 j (rows t = e / 32), loaded
     // now: their latency hides behind the recurrence
     constexpr int kZPer = kGdnMaxRows * kDcCols / (kRG * kDcCols);
@@ -138,6 +140,7 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
         if (warp + kRG * j < R) vsm[warp + kRG * j][lane] = vr[j];
     if (tid < 2 * R) gsm[tid >> 1][tid & 1] = g0;
     __syncthreads();
+    trace_stamp_2d(2);
     // sums of squares of q and k per row in gdn_sumsq128's order (lane l: elements l, l + 32, l + 64, l + 96, then
     // the xor butterfly), (row, q or k) pairs over the 4 warps, read back from shared memory
     for (int pr = warp; pr < 2 * R; pr += kRG) {
@@ -158,6 +161,7 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
         }
     for (int e = tid; e < M * kDcCols; e += blockDim.x) raw[e / kDcCols][e % kDcCols] = 0.f;  // rows no entry names
     __syncthreads();
+    trace_stamp_2d(3);
     // the entries: the replayed rows (committing), then the verify program (gdn_entry)
     const int E = n + gdn_verify_entries_s(A, cs);
     for (int e = 0; e < E; ++e) {
@@ -212,10 +216,12 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
 #pragma unroll
         for (int r = 0; r < kRPG; ++r) S[size_t(r) * kDH] = st[r];
     __syncthreads();  // every entry's output partials are written
+    trace_stamp_2d(4);
     if (rg == 0)  // the entries' outputs in entry order (a later entry naming the same row wins, as it did in turn)
         for (int e = 0; e < E; ++e)
             if (eout[e] >= 0) raw[eout[e]][lane] = bf16_round(opart[e][0][lane] + opart[e][1][lane] + opart[e][2][lane] + opart[e][3][lane]);
     cluster.sync();  // every CTA's raw rows are written (a cluster barrier orders its shared-memory writes)
+    trace_stamp_2d(5);
     // gated RMSNorm of every output row: row t's squares in gdn_sumsq128's order (lane l: columns l, l + 32, l + 64,
     // l + 96 in order, i.e. CTA 0 .. 3's column l, then the xor butterfly)
     for (int t = warp; t < M; t += kRG) {
@@ -231,6 +237,7 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
         if (lane == 0) nsum[t] = gdn_norm_inv(s, A.gnorm_eps);  // the row's norm factor, once
     }
     cluster.sync();  // no CTA leaves while another reads its raw rows; nsum is visible to the CTA
+    trace_stamp_2d(6);
     for (int j = 0; j < kZPer; ++j) {
         const int e = tid + j * kRG * kDcCols;
         if (e < M * kDcCols) {
@@ -238,6 +245,7 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
             A.core[size_t(t) * A.HV * kDH + h * kDH + d] = gdn_core(raw[t][c], gw[j], nsum[t], zv[j]);
         }
     }
+    trace_stamp_2d(7);
 }
 
 // a | b projection: CTA (x, y) copies rows [16 y, 16 y + 16) of the M rows into shared memory; its 8 warps take

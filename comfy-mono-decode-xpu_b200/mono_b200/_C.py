@@ -557,6 +557,28 @@ def rmsnorm_add(x, w, eps, add=None, out=None, sum_out=None):
     return (out, sum_out) if add is not None else out
 
 
+def draft_embed_norm_cat(embed, tokens, index, enorm_w, hidden, hnorm_w, eps, out=None):
+    """The MTP draft head's front (include/mono_b200.h mono_draft_embed_norm_cat): for each row b of hidden
+    [B, H], cat(RMSNorm(embed[tokens[b, index]]; enorm_w), RMSNorm(hidden[b]; hnorm_w)) -> bf16 [B, 2 H].
+    tokens: int64 [B, n] (or [n] for B = 1) on the device."""
+    _cuda(embed, tokens, enorm_w, hidden, hnorm_w)
+    B, H = hidden.shape
+    V = embed.shape[0]
+    _check(embed.dtype == torch.bfloat16 and embed.is_contiguous() and embed.shape[1] == H, "embed bf16 [V, H]")
+    _check(tokens.dtype == torch.int64 and tokens.stride(-1) == 1, "int64 token ids")
+    tok2 = tokens.view(1, -1) if tokens.dim() == 1 else tokens
+    _check(tok2.shape[0] == B and 0 <= index < tok2.shape[1], "tokens [B, n], index < n")
+    _check(hidden.dtype == torch.bfloat16 and hidden.stride(1) == 1, "hidden bf16 rows")
+    if out is None:
+        out = torch.empty((B, 2 * H), dtype=torch.bfloat16, device=hidden.device)
+    _check(out.dtype == torch.bfloat16 and out.shape == (B, 2 * H) and out.stride(1) == 1, "out bf16 [B, 2 H]")
+    with torch.cuda.device(hidden.device):
+        _lib.call("mono_draft_embed_norm_cat", _p(embed), V, H, _p(tok2), tok2.stride(0), int(index), _p(enorm_w),
+                  _p(hidden), hidden.stride(0), _p(hnorm_w), float(eps), B, _p(out), out.stride(0),
+                  _stream(hidden.device))
+    return out
+
+
 def lut_mul(a, b, lut, b_head_stride=256, out=None):
     """bf16(a * lut[b]) elementwise over rows [M, K]; b's column c at (c / 256) * b_head_stride + c % 256."""
     _cuda(a, b, lut)

@@ -385,10 +385,8 @@ class Qwen35W4A8:
         hd, H = c.head_dim, c.hidden
         _C.mtp_prep_draft(self.st, k, self.rope.view(1, 1, self.cap, -1, 2, 2), self.mfreq.view(1, 1, 1, -1, 2, 2),
                           self.mpos, self.mseq)
-        e = self.embed[self.drafts[k:k + 1]]
-        cat = torch.empty(1, 2 * H, dtype=torch.bfloat16, device=self.dev)
-        _C.rmsnorm_add(e, m["enorm"], c.eps, out=cat[:, :H])
-        _C.rmsnorm_add(hidden.view(1, -1), m["hnorm"], c.eps, out=cat[:, H:])
+        # cat(RMSNorm(embedding of node k's token), RMSNorm(hidden)): gather and both norms in one launch
+        cat = _C.draft_embed_norm_cat(self.embed, self.drafts, k, m["enorm"], hidden.view(1, -1), m["hnorm"], c.eps)
         x = self._linear(cat, m["fc"])
         qkv = self._linear(_C.rmsnorm_add(x, m["ln1"], c.eps), m["qkv"])
         nq = 2 * c.heads * hd
@@ -461,8 +459,8 @@ class Qwen35W4A8:
             body = (n_attn + 1) + n_attn * 3
         else:  # rowlin x2 (the GDN layers' first with the a|b projection) + MLP; GDN conv + delta; rope + attention x2
             body = c.layers * 3 + n_gdn * 2 + n_attn * 3
-        # per draft: prep, 2 norms, rope, attention x2, 2 luts, 3 norm(-add)s, lm_head pick (+ 5 projections)
-        draft = c.depth * (1 + 2 + 1 + 2 + 2 + 3 + 1 + (5 if self.draft_gemv else 0))
+        # per draft: prep, embedding + 2 norms, rope, attention x2, 2 luts, 3 norm(-add)s, lm_head pick (+ 5 projections)
+        draft = c.depth * (1 + 1 + 1 + 2 + 2 + 3 + 1 + (5 if self.draft_gemv else 0))
         return body + draft + 1 + 1 + 1 + 1  # prep_verify, final norm, lm_head pick, accept
 
     def step_bytes(self) -> int:

@@ -205,10 +205,7 @@ class Qwen35W4A8Streams(Qwen35W4A8):
         for b in range(B):
             _C.mtp_prep_draft(self.st[b], k, ftab, self.mfreq[b:b + 1].view(1, 1, 1, -1, 2, 2), self.mpos[b],
                               self.mseq[b:b + 1])
-        e = self.embed[self.drafts[:, k]]
-        cat = torch.empty(B, 2 * H, dtype=torch.bfloat16, device=self.dev)
-        _C.rmsnorm_add(e, m["enorm"], c.eps, out=cat[:, :H])
-        _C.rmsnorm_add(hidden.view(B, -1), m["hnorm"], c.eps, out=cat[:, H:])
+        cat = _C.draft_embed_norm_cat(self.embed, self.drafts, k, m["enorm"], hidden.view(B, -1), m["hnorm"], c.eps)
         x = self._linear(cat, m["fc"])
         qkv = self._linear(_C.rmsnorm_add(x, m["ln1"], c.eps), m["qkv"])
         nq = 2 * c.heads * hd
@@ -252,7 +249,7 @@ class Qwen35W4A8Streams(Qwen35W4A8):
         n_attn = sum(1 for i in range(c.layers) if c.is_attn(i))
         n_gdn = c.layers - n_attn
         body = c.layers * 3 + n_gdn * 2 + n_attn * 2
-        draft = c.depth * (B + 2 + 1 + 1 + 2 + 3 + 1 + (5 if self.draft_gemv else 0))
+        draft = c.depth * (B + 1 + 1 + 1 + 2 + 3 + 1 + (5 if self.draft_gemv else 0))
         picks = -(-B * self.tree["rows"] // PICK_ROWS)
         return body + draft + B + 1 + picks + B  # prep_verify per stream, final norm, lm_head picks, accepts
 

@@ -305,6 +305,16 @@ MONO_API int mono_gdn_step_deferred_streams(const void* qkv, const void* z, cons
 MONO_API int mono_rmsnorm_add(const void* x, int64_t x_stride, const void* add, int64_t add_stride, const void* w,
                               float eps, int64_t M, int64_t H, void* out, void* sum_out, int64_t out_stride,
                               mono_stream_t stream);
+/* The MTP draft head's front in one launch (the reference's draft_embed_norm_cat with a bf16 embedding,
+ * csrc/draft_fused.sycl:4-6): for each of B rows (one per decode stream), out[b][0, H) = RMSNorm(embed row of
+ * token tokens[b * tok_stride + index]; enorm_w) and out[b][H, 2 H) = RMSNorm(hidden[b]; hnorm_w), each with
+ * mono_rmsnorm_add's arithmetic (the same bits as the gather + two mono_rmsnorm_add calls). embed bf16 [V][H];
+ * tokens int64 on the device (a token outside [0, V) reads row 0 and sets device status 7); hidden bf16 rows
+ * (hidden_stride elements apart); out bf16 rows of 2 H (out_stride apart). */
+MONO_API int mono_draft_embed_norm_cat(const void* embed, int64_t V, int64_t H, const int64_t* tokens,
+                                       int64_t tok_stride, int64_t index, const void* enorm_w, const void* hidden,
+                                       int64_t hidden_stride, const void* hnorm_w, float eps, int64_t B, void* out,
+                                       int64_t out_stride, mono_stream_t stream);
 
 /* out[m][c] = bf16(a[m][c] * lut[b[m][(c / 256) * b_head_stride + c % 256]]) (lut: bf16 [65536], e.g. SiLU or
  * sigmoid of every bf16 pattern): SiLU(gate) * up, or attention * sigmoid(gate of gated heads). */

@@ -39,3 +39,30 @@ def test_lut_mul_matches_torch_exactly(cuda):
     out = _C.lut_mul(y, qg[:, 256:], sig, b_head_stride=512)
     ref = (y.float() * torch.sigmoid(qg.view(2, 16, 512)[..., 256:].reshape(2, -1)).float()).bfloat16()
     assert torch.equal(out, ref)
+
+
+@pytest.mark.parametrize("B", [1, 3])
+def test_draft_embed_norm_cat_equals_gather_and_two_norms(cuda, B):
+    """mono_draft_embed_norm_cat: the embedding rows of tokens[b, index] and the hidden rows, each RMS-normalized,
+    side by side; bit for bit the torch gather + two mono_rmsnorm_add calls. A token outside the vocabulary reads
+    row 0 and sets device status 7 (the kernel's own check; no out-of-bounds read)."""
+    from mono_b200 import _C
+    g = torch.Generator().manual_seed(90 + B)
+    V, H = 1000, 4096
+    embed = (torch.randn(V, H, generator=g) * 0.02).bfloat16().to(cuda)
+    hidden = torch.randn(B, H, generator=g).bfloat16().to(cuda)
+    ew = (1 + torch.randn(H, generator=g) * 0.1).bfloat16().to(cuda)
+    hw = (1 + torch.randn(H, generator=g) * 0.1).bfloat16().to(cuda)
+    tokens = torch.randint(0, V, (B, 9), generator=g).to(cuda)
+    for index in (0, 4, 8):
+        out = _C.draft_embed_norm_cat(embed, tokens, index, ew, hidden, hw, 1e-6)
+        ref_e = _C.rmsnorm_add(embed[tokens[:, index]], ew, 1e-6)
+        ref_h = _C.rmsnorm_add(hidden, hw, 1e-6)
+        assert torch.equal(out[:, :H], ref_e) and torch.equal(out[:, H:], ref_h), index
+    assert _C.device_status() == 0
+    bad = tokens.clone()
+    bad[0, 2] = V + 5
+    out = _C.draft_embed_norm_cat(embed, bad, 2, ew, hidden, hw, 1e-6)
+    assert torch.equal(out[0, :H], _C.rmsnorm_add(embed[:1], ew, 1e-6)[0])
+    assert _C.device_status() == 7
+    assert _C.device_status() == 0  # read and reset
