@@ -13,11 +13,11 @@
 // x[t-1] w[2], .. from 0), out = bf16(y / (1 + exp(-y))), over the conv state (3 newest inputs, oldest
 // first) and the replayed then the verify rows. Threads < (n + M) * HV make the gates:
 // decay = exp(g_decay * softplus(a + dt_bias)) (softplus(v) = v above 20), beta = bf16(sigmoid(b)).
-// Kernel 2 (per value head 4 row groups x 128 value columns, spread over a cluster of 4 CTAs below; thread
-// (rg, col) keeps state rows rg * 32 .. rg * 32 + 31 of column col in registers): L2 norms of q and k of the key head
+// Kernel 2 (per value head 8 row groups x 128 value columns, spread over a cluster of 4 CTAs below; thread
+// (rg, col) keeps state rows rg * 16 .. rg * 16 + 15 of column col in registers): L2 norms of q and k of the key head
 // (qi = 1 / max(sqrt(sum), 1e-12), q <- (q * scale) * qi, k <- k * ki), then per row in order
 //   S <- S * decay;  mem = S^T k;  delta = (v - mem) * beta;  S <- S + k delta^T;  o = S^T q
-// (fma chains over each row group's 32 rows, the 4 group partials summed in order), raw = bf16(o); the
+// (fma chains over each row group's 16 rows, the 8 group partials summed in order), raw = bf16(o); the
 // gated RMSNorm core = bf16(bf16(raw * w * rsqrt(mean(raw^2) + eps)) * bf16(silu(z))). fp32 throughout;
 // results are checked against an fp64 reference with a stated tolerance.
 #include <cmath>
@@ -63,11 +63,11 @@ __global__ void __launch_bounds__(kConvThreads) gdn_conv_kernel(const GdnArgs A0
 }
 
 // Kernel 2 runs as a cluster of 4 CTAs per value head (128 CTAs at 32 heads): CTA c of the cluster keeps value
-// columns 32c .. 32c + 31, thread (row group = warp, lane) column 32c + lane, state rows rg * 32 .. rg * 32 + 31 -
+// columns 32c .. 32c + 31, thread (row group = warp, lane) column 32c + lane, state rows rg * kRPG .. + kRPG - 1 -
 // the partition and every sum order of a one-CTA head, so the bits are the same. The gated RMSNorm of a row needs
 // all 128 columns: after a cluster barrier each CTA reads the others' raw rows from their shared memory.
 constexpr int kDcCols = 32, kDcCtas = kDH / kDcCols;
-static_assert(kRG == 4 && kDcCols == 32, "one warp per row group, one lane per column");
+static_assert(kRG == 8 && kDcCols == 32, "one warp per row group, one lane per column");
 
 __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols) gdn_delta_kernel(const GdnArgs A0) {
     const GdnArgs A = gdn_stream(A0, blockIdx.y);
@@ -115,26 +115,22 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
             gw[j] = bf16_bits_to_f32(A.gnorm_w[d]);
         }
     }
-    static_assert(kRG * kDcCols == kDH, "one thread per q / k element");
-    float qr[kGdnMaxAll], kr0[kGdnMaxAll], vr[kGdnMaxAll / kRG];
+    static_assert(kRG * kDcCols == 2 * kDH, "one thread per q or k element");
+    const int qe = tid & (kDH - 1);
+    const bool isk = tid >= kDH;  // threads [0, 128): q element qe of every row; [128, 256): k element qe
+    float qk[kGdnMaxAll], vr[kGdnMaxAll / kRG];
 #pragma unroll
     for (int t = 0; t < kGdnMaxAll; ++t)
-        if (t < R) {
-            qr[t] = bf16_bits_to_f32(__ldcg(A.conv_out + size_t(t) * A.C + kh * kDH + tid));
-            kr0[t] = bf16_bits_to_f32(__ldcg(A.conv_out + size_t(t) * A.C + KD + kh * kDH + tid));
-        }
+        if (t < R) qk[t] = bf16_bits_to_f32(__ldcg(A.conv_out + size_t(t) * A.C + (isk ? KD : 0) + kh * kDH + qe));
 #pragma unroll
     for (int j = 0; j < kGdnMaxAll / kRG; ++j) {
-        const int t = warp + kRG * j;  // v rows of this warp: warp, warp + 4, ...
+        const int t = warp + kRG * j;  // v rows of this warp: warp, warp + kRG, ...
         if (t < R) vr[j] = bf16_bits_to_f32(__ldcg(A.conv_out + size_t(t) * A.C + 2 * KD + h * kDH + cr * kDcCols + lane));
     }
     const float g0 = tid < 2 * R ? __ldcg(A.gates + ((tid >> 1) * A.HV + h) * 2 + (tid & 1)) : 0.f;
 #pragma unroll
     for (int t = 0; t < kGdnMaxAll; ++t)
-        if (t < R) {
-            qn[t][tid] = qr[t];
-            kn[t][tid] = kr0[t];
-        }
+        if (t < R) (isk ? kn : qn)[t][qe] = qk[t];
 #pragma unroll
     for (int j = 0; j < kGdnMaxAll / kRG; ++j)
         if (warp + kRG * j < R) vsm[warp + kRG * j][lane] = vr[j];
@@ -142,7 +138,7 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
     __syncthreads();
     trace_stamp_2d(2);
     // sums of squares of q and k per row in gdn_sumsq128's order (lane l: elements l, l + 32, l + 64, l + 96, then
-    // the xor butterfly), (row, q or k) pairs over the 4 warps, read back from shared memory
+    // the xor butterfly), (row, q or k) pairs over the warps, read back from shared memory
     for (int pr = warp; pr < 2 * R; pr += kRG) {
         const float* src = (pr & 1) ? &kn[pr >> 1][0] : &qn[pr >> 1][0];
         float sq = 0.f;
@@ -156,8 +152,10 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
 #pragma unroll
     for (int t = 0; t < kGdnMaxAll; ++t)
         if (t < R) {
-            qn[t][tid] = (qr[t] * A.qscale) * sums[2 * t];
-            kn[t][tid] = kr0[t] * sums[2 * t + 1];
+            if (isk)
+                kn[t][qe] = qk[t] * sums[2 * t + 1];
+            else
+                qn[t][qe] = (qk[t] * A.qscale) * sums[2 * t];
         }
     for (int e = tid; e < M * kDcCols; e += blockDim.x) raw[e / kDcCols][e % kDcCols] = 0.f;  // rows no entry names
     __syncthreads();
@@ -169,7 +167,7 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
         const int t = en.row;
         const float decay = gsm[t][0], beta = gsm[t][1];
         const float v = vsm[t][lane];
-        // the row group's 32 k and q values as 16-byte shared loads (a warp's lanes share the row group: broadcast)
+        // the row group's kRPG k and q values as 16-byte shared loads (a warp's lanes share the row group: broadcast)
         float kr[kRPG], qr[kRPG];
 #pragma unroll
         for (int r4 = 0; r4 < kRPG / 4; ++r4) {
@@ -193,7 +191,9 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
         float (&pe)[kRG][kDcCols] = part[e & 1];  // the other buffer is still being read by the previous entry
         pe[rg][lane] = mem;
         __syncthreads();
-        const float kv = pe[0][lane] + pe[1][lane] + pe[2][lane] + pe[3][lane];
+        float kv = pe[0][lane];  // the group partials in group order
+#pragma unroll
+        for (int j = 1; j < kRG; ++j) kv += pe[j][lane];
         const float delta = (v - kv) * beta;
         float o = 0.f;
         if (en.commit) {
@@ -219,7 +219,12 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
     trace_stamp_2d(4);
     if (rg == 0)  // the entries' outputs in entry order (a later entry naming the same row wins, as it did in turn)
         for (int e = 0; e < E; ++e)
-            if (eout[e] >= 0) raw[eout[e]][lane] = bf16_round(opart[e][0][lane] + opart[e][1][lane] + opart[e][2][lane] + opart[e][3][lane]);
+            if (eout[e] >= 0) {
+                float o = opart[e][0][lane];
+#pragma unroll
+                for (int j = 1; j < kRG; ++j) o += opart[e][j][lane];
+                raw[eout[e]][lane] = bf16_round(o);
+            }
     cluster.sync();  // every CTA's raw rows are written (a cluster barrier orders its shared-memory writes)
     trace_stamp_2d(5);
     // gated RMSNorm of every output row: row t's squares in gdn_sumsq128's order (lane l: columns l, l + 32, l + 64,

@@ -7,7 +7,9 @@
 
 namespace mono {
 
-constexpr int kDH = 128, kRG = 4, kRPG = kDH / kRG, kGdnMaxRows = 8, kGdnMaxAll = 2 * kGdnMaxRows;
+// kRG row groups of the 128 key rows (kRPG rows each): a delta-rule thread keeps kRPG state rows of one value column
+// in registers; S^T k and S^T q are fma chains over a group's rows, the kRG group partials summed in group order.
+constexpr int kDH = 128, kRG = 8, kRPG = kDH / kRG, kGdnMaxRows = 8, kGdnMaxAll = 2 * kGdnMaxRows;
 
 // The conv and gated-norm SiLU: bf16(y / (1 + exp(-y))) of a bf16 value y, fp32 arithmetic, evaluated in place
 // (a table lookup would put a dependent global load behind every output).

@@ -14,7 +14,7 @@
 //   OP_QUANT  q = quant(h) with the row maxima of the paired GEMV
 //   OP_AB     the bf16 a | b projection, one warp per output column on the last CTAs
 //   OP_GDN_*  the Gated-DeltaNet conv + gates (gdn_conv_item over the channels) and delta rule (value columns
-//             spread over the CTAs: CTA b holds columns [b CW 8, (b + 1) CW 8) as 4 row groups of 32 state rows)
+//             spread over the CTAs: CTA b holds columns [b CW 4, (b + 1) CW 4) as 8 row groups of 16 state rows)
 // Every activation that an earlier op of the launch wrote is read through L2 (ld.global.cg).
 #include <cstring>
 #include <mutex>
@@ -323,7 +323,9 @@ static __device__ __noinline__ void prog_gdn_delta(const GdnArgs& A, float* scra
         consumer_sync<CW>();
         float o = 0.f;
         if (active) {
-            const float kv = p0[cl] + p0[CPC + cl] + p0[2 * CPC + cl] + p0[3 * CPC + cl];
+            float kv = p0[cl];  // the group partials in group order (gdn_delta_kernel's)
+#pragma unroll
+            for (int j = 1; j < kRG; ++j) kv += p0[j * CPC + cl];
             const float delta = (v - kv) * beta;
             if (en.commit) {
 #pragma unroll
@@ -338,8 +340,12 @@ static __device__ __noinline__ void prog_gdn_delta(const GdnArgs& A, float* scra
         }
         p1[rg * CPC + cl] = o;
         consumer_sync<CW>();
-        if (active && rg == 0 && en.out >= 0)
-            A.core[size_t(en.out) * total + gc] = f32_to_bf16_bits(bf16_round(p1[cl] + p1[CPC + cl] + p1[2 * CPC + cl] + p1[3 * CPC + cl]));
+        if (active && rg == 0 && en.out >= 0) {
+            float os = p1[cl];
+#pragma unroll
+            for (int j = 1; j < kRG; ++j) os += p1[j * CPC + cl];
+            A.core[size_t(en.out) * total + gc] = f32_to_bf16_bits(bf16_round(os));
+        }
         if (active && A.ctl != nullptr && e == n - 1)
 #pragma unroll
             for (int r = 0; r < kRPG; ++r) Sp[size_t(r) * kDH] = st[r];
