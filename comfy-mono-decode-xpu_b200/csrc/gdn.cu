@@ -22,6 +22,7 @@
 // results are checked against an fp64 reference with a stated tolerance.
 #include <cmath>
 #include <mutex>
+#include <utility>
 
 #include <cooperative_groups.h>
 
@@ -241,7 +242,10 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
         for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
         if (lane == 0) nsum[t] = gdn_norm_inv(s, A.gnorm_eps);  // the row's norm factor, once
     }
-    cluster.sync();  // no CTA leaves while another reads its raw rows; nsum is visible to the CTA
+    // this CTA's reads of the others' raw rows are done: arrive now, wait only before leaving (no CTA may leave
+    // while another still reads its raw rows), so the stores below need not wait for the slowest reader
+    auto done_reading = cluster.barrier_arrive();
+    __syncthreads();  // nsum is visible to the CTA
     trace_stamp_2d(6);
     for (int j = 0; j < kZPer; ++j) {
         const int e = tid + j * kRG * kDcCols;
@@ -251,6 +255,7 @@ __global__ void __cluster_dims__(kDcCtas, 1, 1) __launch_bounds__(kRG * kDcCols)
         }
     }
     trace_stamp_2d(7);
+    cluster.barrier_wait(std::move(done_reading));
 }
 
 // a | b projection: CTA (x, y) copies rows [16 y, 16 y + 16) of the M rows into shared memory; its 8 warps take
