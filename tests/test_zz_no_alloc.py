@@ -57,3 +57,34 @@ def test_rot_quant_noalloc_rejects_shapes_beyond_its_scratch(cuda):
     assert lib.mono_rot_quant_noalloc(dummy, dummy, 17, 4096, dummy, dummy, None) == _lib.MONO_EINVAL
     assert b"fixed scratch" in lib.mono_last_error()
     assert lib.mono_rot_quant_noalloc(dummy, dummy, 8, 16384, dummy, dummy, None) == _lib.MONO_EINVAL
+
+
+def test_rot_quant_noalloc_in_a_cuda_graph(cuda):
+    """The use the header names: after one call in the context, the entry is captured in a CUDA graph (its memset
+    node and two kernels, nothing allocated) and replayed with new inputs written into the captured buffers; every
+    replay equals the workspace entry bit for bit."""
+    from mono_b200 import _lib
+    lib = _lib.load()
+    h = torch.from_numpy(ow.hadamard_256().view(np.int16)).view(torch.bfloat16).to(cuda)
+    g = torch.Generator().manual_seed(7)
+    M, K = 8, 4096
+    x = torch.zeros(M, K, dtype=torch.bfloat16, device=cuda)
+    q = torch.empty(M, K, dtype=torch.int8, device=cuda)
+    s = torch.empty(M, dtype=torch.float32, device=cuda)
+    _rot_quant_noalloc(lib, x, h)  # the first call in the context (outside any capture)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        rc = lib.mono_rot_quant_noalloc(x.data_ptr(), h.data_ptr(), M, K, q.data_ptr(), s.data_ptr(),
+                                        side.cuda_stream)
+    assert rc == 0, lib.mono_last_error()
+    for _ in range(2):
+        x.copy_((torch.randn(M, K, generator=g) * torch.exp(torch.randn(M, K, generator=g))).to(torch.bfloat16))
+        graph.replay()
+        torch.cuda.synchronize()
+        q_ref, s_ref = _rot_quant_with_workspace(lib, x, h)
+        torch.cuda.synchronize()
+        assert torch.equal(q, q_ref)
+        assert torch.equal(s.view(torch.int32), s_ref.view(torch.int32))
+    del graph
