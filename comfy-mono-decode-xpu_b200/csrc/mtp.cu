@@ -14,11 +14,18 @@ namespace mono {
 
 constexpr int kSlots = 8, kRanks = 7;
 
+// CTA b: stream b of a batch (st, freqs, mpos, mseq offset by b times their strides; one stream: strides 0)
 __global__ void __launch_bounds__(256) mtp_prep_draft_kernel(const int64_t* st, int64_t k, const float* ftab, int64_t n,
                                                              int64_t cap, float* freqs, int64_t* mpos, int np,
-                                                             int32_t* mseq) {
+                                                             int32_t* mseq, int64_t st_stride, int64_t freqs_stride,
+                                                             int64_t mpos_stride, int64_t mseq_stride) {
     pdl_launch_dependents();  // an ordinary launch: its inputs are complete; the next kernel may start
     const int t = threadIdx.x;
+    const int64_t b = blockIdx.x;
+    st += b * st_stride;
+    freqs += b * freqs_stride;
+    mpos += b * mpos_stride;
+    mseq += b * mseq_stride;
     const int64_t p = st[0] + k, m = st[1] + k;
     const int64_t row = p < cap ? (p < 0 ? 0 : p) : cap - 1;
     for (int64_t i = t; i < n; i += 256) freqs[i] = ftab[row * n + i];
@@ -179,7 +186,21 @@ int mono_mtp_prep_draft(const int64_t* st, int64_t k, const float* ftab, int64_t
     MONO_CHECK(st && ftab && freqs && mpos && mseq, "null operand");
     MONO_CHECK(row_elems >= 1 && cap >= 1 && np >= 0 && np <= 256 && k >= 0, "sizes");
     mtp_prep_draft_kernel<<<1, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(st, k, ftab, row_elems, cap, freqs, mpos,
-                                                                                  int(np), mseq);
+                                                                                  int(np), mseq, 0, 0, 0, 0);
+    CUDA_TRY(cudaGetLastError());
+    return MONO_OK;
+}
+
+int mono_mtp_prep_draft_streams(const int64_t* st, int64_t st_stride, int64_t k, const float* ftab, int64_t row_elems,
+                                int64_t cap, float* freqs, int64_t freqs_stride, int64_t* mpos, int64_t mpos_stride,
+                                int64_t np, int32_t* mseq, int64_t mseq_stride, int64_t streams, mono_stream_t stream) {
+    MONO_CHECK(st && ftab && freqs && mpos && mseq, "null operand");
+    MONO_CHECK(row_elems >= 1 && cap >= 1 && np >= 0 && np <= 256 && k >= 0, "sizes");
+    MONO_CHECK(streams >= 1 && streams <= 65535 && st_stride >= 2 && freqs_stride >= row_elems && mpos_stride >= np &&
+                   mseq_stride >= 1,
+               "1 <= streams; per-stream strides cover each stream's words");
+    mtp_prep_draft_kernel<<<unsigned(streams), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        st, k, ftab, row_elems, cap, freqs, mpos, int(np), mseq, st_stride, freqs_stride, mpos_stride, mseq_stride);
     CUDA_TRY(cudaGetLastError());
     return MONO_OK;
 }

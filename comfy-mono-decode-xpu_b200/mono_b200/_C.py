@@ -385,6 +385,24 @@ def mtp_prep_draft(st, k, ftab, freqs, mpos, mseq):
                   _stream(st.device))
 
 
+def mtp_prep_draft_streams(st, k, ftab, freqs, mpos, mseq):
+    """mtp_prep_draft for B batched streams in one launch (mono_mtp_prep_draft_streams): st int64 [B, W], freqs
+    float [B, ...] (row b: stream b's rope row), mpos int64 [B, np], mseq int32 [B]."""
+    _cuda(st, ftab, freqs, mpos, mseq)
+    _check(st.dtype == torch.int64 and mpos.dtype == torch.int64 and mseq.dtype == torch.int32, "int64 st / mpos, int32 mseq")
+    B = st.size(0)
+    _check(st.dim() == 2 and st.stride(1) == 1 and freqs.size(0) == B and freqs.is_contiguous() and
+           mpos.dim() == 2 and mpos.size(0) == B and mpos.stride(1) == 1 and mseq.numel() == B and mseq.dim() == 1,
+           "per-stream rows [B, ...]")
+    _check(ftab.dtype == torch.float32 and ftab.is_contiguous() and freqs.dtype == torch.float32, "float rope rows")
+    n = freqs[0].numel()
+    cap = ftab.numel() // n
+    _check(cap * n == ftab.numel(), "rope table rows of the row size")
+    with torch.cuda.device(st.device):
+        _lib.call("mono_mtp_prep_draft_streams", _p(st), st.stride(0), int(k), _p(ftab), n, cap, _p(freqs), n,
+                  _p(mpos), mpos.stride(0), mpos.size(1), _p(mseq), mseq.stride(0), B, _stream(st.device))
+
+
 def mtp_prep_verify(st, apos, aseq, vpos, tree_pos, ctl, tree_ctl, parity, rope_offset):
     """The reference's _C.mtp_prep_verify (csrc/mtp_loop.sycl:57-90)."""
     _cuda(st, apos, aseq, vpos, tree_pos, ctl, tree_ctl)

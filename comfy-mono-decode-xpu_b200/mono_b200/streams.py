@@ -18,7 +18,8 @@ and every row-wise kernel takes the B x 8 verify rows (B draft rows) as one batc
   lm_head picks                     mono_lmhead_pick at M = B (each draft, dst row per stream) and for the verify
                                     in launches of up to 16 rows (one lm_head read per 2 streams)
   GDN layer_pre + a | b projection  mono_rowlin_norm_ab_gptq at M = 8 B
-  MTP prep / accept                 one launch per stream (a few microseconds each)
+  MTP draft prep                    mono_mtp_prep_draft_streams (every stream in one launch)
+  MTP verify prep / accept          one launch per stream (a few microseconds each)
 
 Each stream's arithmetic is exactly its one-stream step's (row-wise kernels; attention chunks a stream's context as
 it would alone), so a batch of B streams commits the same tokens and states as B separate Qwen35W4A8 models:
@@ -201,10 +202,7 @@ class Qwen35W4A8Streams(Qwen35W4A8):
         in its verify-token row. Returns the MTP hidden rows [B, 1, H]."""
         c, m, B = self.cfg, self.mtp, self.streams
         hd, H = c.head_dim, c.hidden
-        ftab = self.rope.view(1, 1, self.cap, -1, 2, 2)
-        for b in range(B):
-            _C.mtp_prep_draft(self.st[b], k, ftab, self.mfreq[b:b + 1].view(1, 1, 1, -1, 2, 2), self.mpos[b],
-                              self.mseq[b:b + 1])
+        _C.mtp_prep_draft_streams(self.st, k, self.rope, self.mfreq, self.mpos, self.mseq)  # every stream, one launch
         cat = _C.draft_embed_norm_cat(self.embed, self.drafts, k, m["enorm"], hidden.view(B, -1), m["hnorm"], c.eps)
         x = self._linear(cat, m["fc"])
         qkv = self._linear(_C.rmsnorm_add(x, m["ln1"], c.eps), m["qkv"])
@@ -249,7 +247,7 @@ class Qwen35W4A8Streams(Qwen35W4A8):
         n_attn = sum(1 for i in range(c.layers) if c.is_attn(i))
         n_gdn = c.layers - n_attn
         body = c.layers * 3 + n_gdn * 2 + n_attn * 2
-        draft = c.depth * (B + 1 + 1 + 1 + 2 + 3 + 1 + (5 if self.draft_gemv else 0))
+        draft = c.depth * (1 + 1 + 1 + 1 + 2 + 3 + 1 + (5 if self.draft_gemv else 0))
         picks = -(-B * self.tree["rows"] // PICK_ROWS)
         return body + draft + B + 1 + picks + B  # prep_verify per stream, final norm, lm_head picks, accepts
 

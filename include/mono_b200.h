@@ -342,6 +342,12 @@ MONO_API int mono_fast_topk(const void* x, int64_t rows, int64_t V, int64_t k, i
  * (i < np), mseq = st[1] + k + 1 (reference: mtp_prep_draft). */
 MONO_API int mono_mtp_prep_draft(const int64_t* st, int64_t k, const float* ftab, int64_t row_elems, int64_t cap,
                                  float* freqs, int64_t* mpos, int64_t np, int32_t* mseq, mono_stream_t stream);
+/* The same for `streams` batched decode streams in one launch: stream b's st, freqs, mpos and mseq start b x their
+ * strides (elements) after the given pointers; each stream's words are its one-stream call's. */
+MONO_API int mono_mtp_prep_draft_streams(const int64_t* st, int64_t st_stride, int64_t k, const float* ftab,
+                                         int64_t row_elems, int64_t cap, float* freqs, int64_t freqs_stride,
+                                         int64_t* mpos, int64_t mpos_stride, int64_t np, int32_t* mseq,
+                                         int64_t mseq_stride, int64_t streams, mono_stream_t stream);
 
 /* apos[i] = st[0] + i (i < np <= 64), aseq = st[0], vpos[r] = tree_pos[r] + st[0] + rope_offset (r < rows <= 8),
  * ctl[1] = parity, ctl[10 .. 26) = tree_ctl[0 .. 16) (reference: mtp_prep_verify). */

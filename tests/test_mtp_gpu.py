@@ -137,3 +137,25 @@ def test_mtp_accept_malformed_children_table_stops_with_status(cuda):
     assert result[0].item() == 2  # rows 0 and 1, then the bad entry (back to 0) ends the walk
     assert _C.device_status() == 5
     assert _C.device_status() == 0  # (reset by the read)
+
+
+def test_prep_draft_streams_equals_one_stream_calls(cuda):
+    """mono_mtp_prep_draft_streams: one launch for B streams writes each stream's rope row, MTP KV positions and
+    length exactly as B one-stream calls do (different counters per stream, one past the table's end)."""
+    from mono_b200 import _C
+    B, cap, rd = 3, 64, 64
+    g = torch.Generator().manual_seed(4)
+    rope = torch.randn(cap, rd // 2, 2, 2, generator=g).to(cuda)
+    st = torch.tensor([[10, 7, 0, 0], [63, 40, 0, 0], [0, 0, 0, 0]], dtype=torch.int64, device=cuda)
+    for k in (0, 2):
+        freqs = torch.zeros(B, rd // 2, 2, 2, device=cuda)
+        mpos = torch.zeros(B, 1, dtype=torch.int64, device=cuda)
+        mseq = torch.zeros(B, dtype=torch.int32, device=cuda)
+        _C.mtp_prep_draft_streams(st, k, rope, freqs, mpos, mseq)
+        for b in range(B):
+            f1 = torch.zeros(1, 1, 1, rd // 2, 2, 2, device=cuda)
+            p1 = torch.zeros(1, dtype=torch.int64, device=cuda)
+            s1 = torch.zeros(1, dtype=torch.int32, device=cuda)
+            _C.mtp_prep_draft(st[b], k, rope.view(1, 1, cap, -1, 2, 2), f1, p1, s1)
+            assert torch.equal(freqs[b], f1.view(rd // 2, 2, 2)), (k, b)
+            assert torch.equal(mpos[b], p1) and torch.equal(mseq[b:b + 1], s1), (k, b)
