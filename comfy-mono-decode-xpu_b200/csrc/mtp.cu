@@ -33,12 +33,21 @@ __global__ void __launch_bounds__(256) mtp_prep_draft_kernel(const int64_t* st, 
     if (t == 0) mseq[0] = int32_t(m + 1);
 }
 
+// CTA b: stream b of a batch (st, apos, aseq, vpos, ctl offset by b times their strides; one stream: strides 0)
 __global__ void __launch_bounds__(64) mtp_prep_verify_kernel(const int64_t* st, int64_t* apos, int np, int32_t* aseq,
                                                              int64_t* vpos, const int64_t* tree_pos, int rows,
                                                              int32_t* ctl, const int32_t* tree_ctl, int parity,
-                                                             int64_t rope_offset) {
+                                                             int64_t rope_offset, int64_t st_stride,
+                                                             int64_t apos_stride, int64_t aseq_stride,
+                                                             int64_t vpos_stride, int64_t ctl_stride) {
     pdl_launch_dependents();  // an ordinary launch: its inputs are complete; the next kernel may start
     const int t = threadIdx.x;
+    const int64_t b = blockIdx.x;
+    st += b * st_stride;
+    apos += b * apos_stride;
+    aseq += b * aseq_stride;
+    vpos += b * vpos_stride;
+    ctl += b * ctl_stride;
     const int64_t pos = st[0];
     if (t < np) apos[t] = pos + t;
     if (t == 0) aseq[0] = int32_t(pos);
@@ -211,7 +220,24 @@ int mono_mtp_prep_verify(const int64_t* st, int64_t* apos, int64_t np, int32_t* 
     MONO_CHECK(st && apos && aseq && vpos && tree_pos && ctl && tree_ctl, "null operand");
     MONO_CHECK(rows >= 1 && rows <= kSlots && np >= 0 && np <= 64, "rows <= 8, positions <= 64");
     mtp_prep_verify_kernel<<<1, 64, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        st, apos, int(np), aseq, vpos, tree_pos, int(rows), ctl, tree_ctl, int(parity), rope_offset);
+        st, apos, int(np), aseq, vpos, tree_pos, int(rows), ctl, tree_ctl, int(parity), rope_offset, 0, 0, 0, 0, 0);
+    CUDA_TRY(cudaGetLastError());
+    return MONO_OK;
+}
+
+int mono_mtp_prep_verify_streams(const int64_t* st, int64_t st_stride, int64_t* apos, int64_t apos_stride, int64_t np,
+                                 int32_t* aseq, int64_t aseq_stride, int64_t* vpos, int64_t vpos_stride,
+                                 const int64_t* tree_pos, int64_t rows, int32_t* ctl, int64_t ctl_stride,
+                                 const int32_t* tree_ctl, int64_t parity, int64_t rope_offset, int64_t streams,
+                                 mono_stream_t stream) {
+    MONO_CHECK(st && apos && aseq && vpos && tree_pos && ctl && tree_ctl, "null operand");
+    MONO_CHECK(rows >= 1 && rows <= kSlots && np >= 0 && np <= 64, "rows <= 8, positions <= 64");
+    MONO_CHECK(streams >= 1 && streams <= 65535 && st_stride >= 2 && apos_stride >= np && aseq_stride >= 1 &&
+                   vpos_stride >= rows && ctl_stride >= 2 + 3 * kSlots,
+               "1 <= streams; per-stream strides cover each stream's words");
+    mtp_prep_verify_kernel<<<unsigned(streams), 64, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        st, apos, int(np), aseq, vpos, tree_pos, int(rows), ctl, tree_ctl, int(parity), rope_offset, st_stride,
+        apos_stride, aseq_stride, vpos_stride, ctl_stride);
     CUDA_TRY(cudaGetLastError());
     return MONO_OK;
 }

@@ -414,6 +414,23 @@ def mtp_prep_verify(st, apos, aseq, vpos, tree_pos, ctl, tree_ctl, parity, rope_
                   _p(ctl), _p(tree_ctl), int(parity), int(rope_offset), _stream(st.device))
 
 
+def mtp_prep_verify_streams(st, apos, aseq, vpos, tree_pos, ctl, tree_ctl, parity, rope_offset):
+    """mtp_prep_verify for B batched streams in one launch (mono_mtp_prep_verify_streams): st int64 [B, W], apos
+    int64 [B, np], aseq int32 [B], vpos int64 [B, rows], ctl int32 [B, 26]; tree_pos / tree_ctl shared."""
+    _cuda(st, apos, aseq, vpos, tree_pos, ctl, tree_ctl)
+    B = st.size(0)
+    _check(st.dtype == torch.int64 and st.dim() == 2 and st.stride(1) == 1, "st int64 [B, W]")
+    _check(apos.dim() == 2 and apos.size(0) == B and apos.stride(1) == 1 and aseq.dim() == 1 and aseq.numel() == B and
+           vpos.dim() == 2 and vpos.size(0) == B and vpos.stride(1) == 1 and ctl.dim() == 2 and ctl.size(0) == B and
+           ctl.size(1) == 26 and ctl.stride(1) == 1, "per-stream rows [B, ...]")
+    _check(ctl.dtype == torch.int32 and tree_ctl.dtype == torch.int32 and tree_ctl.numel() == 16, "ctl / tree program")
+    _check(tree_pos.numel() == vpos.size(1), "rows")
+    with torch.cuda.device(st.device):
+        _lib.call("mono_mtp_prep_verify_streams", _p(st), st.stride(0), _p(apos), apos.stride(0), apos.size(1),
+                  _p(aseq), aseq.stride(0), _p(vpos), vpos.stride(0), _p(tree_pos), vpos.size(1), _p(ctl),
+                  ctl.stride(0), _p(tree_ctl), int(parity), int(rope_offset), B, _stream(st.device))
+
+
 def mtp_accept(st, toks, vtok, cand, children, rows, depth, x, nt_buf, h_buf, ctl, kv_ptrs, kv_heads, kv_cap, head_dim,
                result):
     """The reference's _C.mtp_accept (csrc/mtp_loop.sycl:92-196): accept walk, result row, counters, ctl, next

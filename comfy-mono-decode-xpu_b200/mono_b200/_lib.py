@@ -52,6 +52,7 @@ SIGNATURES = {
     "mono_rowlin_gptq_workspace": (SZ, [I64]),
     "mono_draft_embed_norm_cat": (I, [P, I64, I64, P, I64, I64, P, P, I64, P, ctypes.c_float, I64, P, I64, P]),
     "mono_mtp_prep_draft_streams": (I, [P, I64, I64, P, I64, I64, P, I64, P, I64, I64, P, I64, I64, P]),
+    "mono_mtp_prep_verify_streams": (I, [P, I64, P, I64, I64, P, I64, P, I64, P, I64, P, I64, P, I64, I64, I64, P]),
     "mono_rowlin_gptq": (I, [P, I, P, ctypes.c_float, P, I64, I64, P, P, P, I, I64, I64, P, P, P, P, SZ, P]),
     "mono_rowlin_norm_ab_gptq": (I, [P, P, ctypes.c_float, P, P, I, I64, I64, P, P, P, I64, P, I64, P, SZ, P]),
     "mono_rmsnorm_add": (I, [P, I64, P, I64, P, ctypes.c_float, I64, I64, P, P, I64, P]),

@@ -18,8 +18,8 @@ and every row-wise kernel takes the B x 8 verify rows (B draft rows) as one batc
   lm_head picks                     mono_lmhead_pick at M = B (each draft, dst row per stream) and for the verify
                                     in launches of up to 16 rows (one lm_head read per 2 streams)
   GDN layer_pre + a | b projection  mono_rowlin_norm_ab_gptq at M = 8 B
-  MTP draft prep                    mono_mtp_prep_draft_streams (every stream in one launch)
-  MTP verify prep / accept          one launch per stream (a few microseconds each)
+  MTP draft / verify prep           mono_mtp_prep_draft_streams / mono_mtp_prep_verify_streams (one launch each)
+  MTP accept                        one launch per stream (a few microseconds each)
 
 Each stream's arithmetic is exactly its one-stream step's (row-wise kernels; attention chunks a stream's context as
 it would alone), so a batch of B streams commits the same tokens and states as B separate Qwen35W4A8 models:
@@ -183,9 +183,8 @@ class Qwen35W4A8Streams(Qwen35W4A8):
         """Every stream's tree rows ([B, R] tokens) through the body in one batch; returns (greedy tokens [B, R],
         final hidden rows [B R, H])."""
         c, B = self.cfg, self.streams
-        for b in range(B):
-            _C.mtp_prep_verify(self.st[b], self.apos[b], self.aseq[b:b + 1], self.vpos[b], self.tree_pos, self.ctl[b],
-                               self.tree_ctl, self.parity, 0)
+        _C.mtp_prep_verify_streams(self.st, self.apos, self.aseq, self.vpos, self.tree_pos, self.ctl, self.tree_ctl,
+                                   self.parity, 0)  # every stream, one launch
         freqs = self.rope[self.vpos.view(-1).clamp(max=self.cap - 1)]
         x = self.embed[tokens.view(-1)]
         for i, L in enumerate(self.layers):
@@ -249,7 +248,7 @@ class Qwen35W4A8Streams(Qwen35W4A8):
         body = c.layers * 3 + n_gdn * 2 + n_attn * 2
         draft = c.depth * (1 + 1 + 1 + 1 + 2 + 3 + 1 + (5 if self.draft_gemv else 0))
         picks = -(-B * self.tree["rows"] // PICK_ROWS)
-        return body + draft + B + 1 + picks + B  # prep_verify per stream, final norm, lm_head picks, accepts
+        return body + draft + 1 + 1 + picks + B  # prep_verify (all streams), final norm, lm_head picks, accepts
 
     def step_bytes(self) -> int:
         """Algorithmic HBM bytes of one batched step: the weights once, every stream's GDN states and KV prefix."""

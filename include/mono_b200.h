@@ -354,6 +354,14 @@ MONO_API int mono_mtp_prep_draft_streams(const int64_t* st, int64_t st_stride, i
 MONO_API int mono_mtp_prep_verify(const int64_t* st, int64_t* apos, int64_t np, int32_t* aseq, int64_t* vpos,
                                   const int64_t* tree_pos, int64_t rows, int32_t* ctl, const int32_t* tree_ctl,
                                   int64_t parity, int64_t rope_offset, mono_stream_t stream);
+/* The same for `streams` batched decode streams in one launch: stream b's st, apos, aseq, vpos and ctl start b x
+ * their strides (elements) after the given pointers (tree_pos and tree_ctl are shared); each stream's words are its
+ * one-stream call's. */
+MONO_API int mono_mtp_prep_verify_streams(const int64_t* st, int64_t st_stride, int64_t* apos, int64_t apos_stride,
+                                          int64_t np, int32_t* aseq, int64_t aseq_stride, int64_t* vpos,
+                                          int64_t vpos_stride, const int64_t* tree_pos, int64_t rows, int32_t* ctl,
+                                          int64_t ctl_stride, const int32_t* tree_ctl, int64_t parity,
+                                          int64_t rope_offset, int64_t streams, mono_stream_t stream);
 
 /* The accept step (reference: mtp_accept; host twin comfy_mono_decode_xpu/mtp_loop.py:117-136): from row 0,
  * continue along the first child c (children int32 [8][8], -1 ends a list) with drafts[c] == toks[current];

@@ -159,3 +159,22 @@ def test_prep_draft_streams_equals_one_stream_calls(cuda):
             _C.mtp_prep_draft(st[b], k, rope.view(1, 1, cap, -1, 2, 2), f1, p1, s1)
             assert torch.equal(freqs[b], f1.view(rd // 2, 2, 2)), (k, b)
             assert torch.equal(mpos[b], p1) and torch.equal(mseq[b:b + 1], s1), (k, b)
+
+
+def test_prep_verify_streams_equals_one_stream_calls(cuda):
+    """mono_mtp_prep_verify_streams: one launch for B streams writes each stream's attention positions / length,
+    verify RoPE positions and ctl words exactly as B one-stream calls do."""
+    from mono_b200 import _C
+    B, R = 3, 8
+    st = torch.tensor([[10, 7, 0, 0], [500, 40, 0, 0], [0, 0, 0, 0]], dtype=torch.int64, device=cuda)
+    tree_pos = torch.tensor([0, 1, 2, 3, 4, 3, 2, 1], dtype=torch.int64, device=cuda)
+    tree_ctl = torch.arange(16, dtype=torch.int32, device=cuda) - 3
+    outs = [torch.full((B, R), -9, dtype=torch.int64, device=cuda), torch.full((B,), -9, dtype=torch.int32, device=cuda),
+            torch.full((B, R), -9, dtype=torch.int64, device=cuda), torch.full((B, 26), -9, dtype=torch.int32, device=cuda)]
+    _C.mtp_prep_verify_streams(st, outs[0], outs[1], outs[2], tree_pos, outs[3], tree_ctl, 1, 5)
+    for b in range(B):
+        one = [torch.full((R,), -9, dtype=torch.int64, device=cuda), torch.full((1,), -9, dtype=torch.int32, device=cuda),
+               torch.full((R,), -9, dtype=torch.int64, device=cuda), torch.full((26,), -9, dtype=torch.int32, device=cuda)]
+        _C.mtp_prep_verify(st[b], one[0], one[1], one[2], tree_pos, one[3], tree_ctl, 1, 5)
+        assert torch.equal(outs[0][b], one[0]) and torch.equal(outs[1][b:b + 1], one[1]), b
+        assert torch.equal(outs[2][b], one[2]) and torch.equal(outs[3][b], one[3]), b
